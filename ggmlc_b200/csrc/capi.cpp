@@ -1,0 +1,369 @@
+// extern "C" boundary of libggmlc_b200.so (declarations in include/ggmlc_b200.h).  Every entry
+// point catches C++ exceptions and turns them into -1 + gb_last_error(), the C counterpart of
+// the std::runtime_error -> Python exception path of the reference bindings.
+#include "../../include/ggmlc_b200.h"
+
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <string>
+
+#include "executor.h"
+#include "graph.h"
+#include "kernels.h"
+#include "kutil.cuh"
+
+struct gb_graph {
+    std::shared_ptr<gb::Graph> g;
+    std::vector<uint32_t> tensor_ids;
+};
+
+struct gb_executor {
+    std::unique_ptr<gb::Executor> e;
+    std::string summary, mm_summary, ktimes;
+};
+
+namespace {
+thread_local std::string g_err;
+
+template <class F>
+int guard(F&& f) {
+    try {
+        f();
+        return 0;
+    } catch (const std::exception& ex) {
+        g_err = ex.what();
+    } catch (...) {
+        g_err = "unknown error";
+    }
+    return -1;
+}
+
+gb_graph* wrap(std::shared_ptr<gb::Graph> g) {
+    auto* h = new gb_graph();
+    h->g = std::move(g);
+    for (auto& [id, t] : h->g->tensors) h->tensor_ids.push_back(id);
+    return h;
+}
+
+const std::vector<uint32_t>& ids_of(const gb_graph* g, int which) {
+    switch (which) {
+        case 0: return g->g->inputs;
+        case 1: return g->g->outputs;
+        default: return g->g->parameters;
+    }
+}
+}  // namespace
+
+extern "C" {
+
+const char* gb_last_error(void) { return g_err.c_str(); }
+int gb_version(void) { return 100; }
+
+int gb_get_available_devices(char* buf, size_t cap) {
+    std::string s;
+    int rc = guard([&] {
+        for (auto& d : gb::Executor::available_devices()) s += (s.empty() ? "" : "\n") + d;
+    });
+    if (rc) return -1;
+    if (buf && cap) {
+        std::strncpy(buf, s.c_str(), cap - 1);
+        buf[cap - 1] = 0;
+    }
+    return (int)s.size() + 1;
+}
+
+int gb_loader_load_from_file(const char* path, gb_graph** out) {
+    return guard([&] { *out = wrap(gb::load_gguf_file(path)); });
+}
+int gb_loader_load_from_bytes(const void* data, size_t size, gb_graph** out) {
+    return guard([&] { *out = wrap(gb::load_gguf_bytes((const uint8_t*)data, size)); });
+}
+void gb_graph_free(gb_graph* g) { delete g; }
+
+const char* gb_graph_name(const gb_graph* g) { return g->g->name.c_str(); }
+int gb_graph_num_symbols(const gb_graph* g) { return (int)g->g->symbol_table.size(); }
+const char* gb_graph_symbol(const gb_graph* g, int i) {
+    if (i < 0 || i >= (int)g->g->symbol_table.size()) return nullptr;
+    return g->g->symbol_table[(size_t)i].c_str();
+}
+int gb_graph_num_ids(const gb_graph* g, int which) { return (int)ids_of(g, which).size(); }
+int gb_graph_id(const gb_graph* g, int which, int i, uint32_t* id) {
+    const auto& v = ids_of(g, which);
+    if (i < 0 || i >= (int)v.size()) {
+        g_err = "index out of range";
+        return -1;
+    }
+    *id = v[(size_t)i];
+    return 0;
+}
+int gb_graph_num_tensors(const gb_graph* g) { return (int)g->tensor_ids.size(); }
+int gb_graph_tensor_id(const gb_graph* g, int i, uint32_t* id) {
+    if (i < 0 || i >= (int)g->tensor_ids.size()) {
+        g_err = "index out of range";
+        return -1;
+    }
+    *id = g->tensor_ids[(size_t)i];
+    return 0;
+}
+int gb_graph_tensor_info(const gb_graph* g, uint32_t id, const char** name, int* type,
+                         int* storage, uint64_t* data_size) {
+    return guard([&] {
+        const gb::GTensor& t = g->g->t(id);
+        if (name) *name = t.name.c_str();
+        if (type) *type = t.type;
+        if (storage) *storage = t.storage;
+        if (data_size) *data_size = t.data_size;
+    });
+}
+int gb_graph_tensor_symbol_index(const gb_graph* g, uint32_t id, int axis) {
+    auto it = g->g->tensors.find(id);
+    if (it == g->g->tensors.end() || axis < 0 || axis > 3 || !it->second.ne[axis]) return -1;
+    return it->second.ne[axis]->symbol_index(g->g->symbol_table);
+}
+int gb_graph_num_ops(const gb_graph* g) { return (int)g->g->ops.size(); }
+int gb_graph_op_info(const gb_graph* g, int i, uint32_t* id, int* opcode, const char** name) {
+    if (i < 0 || i >= (int)g->g->ops.size()) {
+        g_err = "index out of range";
+        return -1;
+    }
+    const auto& op = g->g->ops[(size_t)i];
+    if (id) *id = op.id;
+    if (opcode) *opcode = op.opcode;
+    if (name) *name = op.name.c_str();
+    return 0;
+}
+const char* gb_graph_metadata_str(const gb_graph* g, const char* key) {
+    auto it = g->g->meta_str.find(key);
+    return it == g->g->meta_str.end() ? nullptr : it->second.c_str();
+}
+
+int gb_executor_create(const gb_graph* g, const char* device, gb_executor** out) {
+    return guard([&] {
+        auto* h = new gb_executor();
+        try {
+            h->e.reset(new gb::Executor(g->g, device ? device : "cuda"));
+        } catch (...) {
+            delete h;
+            throw;
+        }
+        *out = h;
+    });
+}
+void gb_executor_free(gb_executor* e) { delete e; }
+const char* gb_executor_device(const gb_executor* e) { return e->e->device().c_str(); }
+
+int gb_executor_prepare(gb_executor* e, const char* const* names, const int64_t* values, int n,
+                        int enable_arena_reuse) {
+    return guard([&] {
+        gb::SymEnv env;
+        for (int i = 0; i < n; ++i) env[names[i]] = values[i];
+        e->e->prepare(env, enable_arena_reuse != 0);
+    });
+}
+int gb_executor_set_input(gb_executor* e, uint32_t tid, const void* data, size_t bytes) {
+    return guard([&] { e->e->set_input(tid, data, bytes); });
+}
+int gb_executor_set_input_by_name(gb_executor* e, const char* name, const void* data,
+                                  size_t bytes) {
+    return guard([&] { e->e->set_input_by_name(name, data, bytes); });
+}
+int gb_executor_run(gb_executor* e, int) {
+    return guard([&] { e->e->run(); });
+}
+int gb_executor_synchronize(gb_executor* e) {
+    return guard([&] { e->e->synchronize(); });
+}
+int gb_executor_get_output(gb_executor* e, uint32_t tid, const void** data, size_t* bytes) {
+    return guard([&] { *data = e->e->get_output(tid, bytes); });
+}
+int gb_executor_get_tensor_shape(gb_executor* e, uint32_t tid, int64_t ne[4]) {
+    return guard([&] {
+        auto s = e->e->tensor_shape(tid);
+        for (int d = 0; d < 4; ++d) ne[d] = s[(size_t)d];
+    });
+}
+int gb_executor_get_tensor_size_bytes(gb_executor* e, uint32_t tid, size_t* bytes) {
+    return guard([&] { *bytes = e->e->tensor_size_bytes(tid); });
+}
+int gb_executor_set_state(gb_executor* e, uint32_t tid, const void* data, size_t bytes) {
+    return guard([&] { e->e->set_state(tid, data, bytes); });
+}
+int gb_executor_get_state(gb_executor* e, uint32_t tid, const void** data, size_t* bytes) {
+    return guard([&] { *data = e->e->get_state(tid, bytes); });
+}
+int gb_executor_reset_state(gb_executor* e) {
+    return guard([&] { e->e->reset_state(); });
+}
+int gb_executor_init_kv_cache(gb_executor* e, int64_t max_ctx) {
+    return guard([&] { e->e->init_kv_cache(max_ctx); });
+}
+int gb_executor_reset_kv_cache(gb_executor* e) {
+    return guard([&] { e->e->reset_kv_cache(); });
+}
+int gb_executor_has_kv_cache(const gb_executor* e) { return e->e->has_kv_cache() ? 1 : 0; }
+int gb_executor_set_logits_last_only(gb_executor* e, int enable) {
+    return guard([&] { e->e->set_logits_last_only(enable != 0); });
+}
+int gb_executor_logits_last_only(const gb_executor* e) { return e->e->logits_last_only() ? 1 : 0; }
+int gb_executor_set_enable_cuda_graph(gb_executor* e, int enable) {
+    return guard([&] { e->e->set_enable_cuda_graph(enable != 0); });
+}
+int gb_executor_is_cuda_graph_enabled(const gb_executor* e) {
+    return e->e->cuda_graph_enabled() ? 1 : 0;
+}
+int gb_executor_is_cuda_graph_captured(const gb_executor* e) {
+    return e->e->cuda_graph_captured() ? 1 : 0;
+}
+int gb_executor_set_enable_profile(gb_executor* e, int enable) {
+    return guard([&] { e->e->set_enable_profile(enable != 0); });
+}
+int gb_executor_reset_profile(gb_executor* e) {
+    return guard([&] { e->e->reset_profile(); });
+}
+int gb_executor_get_profile(gb_executor* e, double* prepare_ms, double* run_ms, int* n_prepare,
+                            int* n_run) {
+    return guard([&] {
+        auto p = e->e->profile();
+        if (prepare_ms) *prepare_ms = p.prepare_ms;
+        if (run_ms) *run_ms = p.run_ms;
+        if (n_prepare) *n_prepare = p.n_prepare;
+        if (n_run) *n_run = p.n_run;
+    });
+}
+const char* gb_executor_graph_summary(gb_executor* e) {
+    e->summary = e->e->graph_summary();
+    return e->summary.c_str();
+}
+const char* gb_executor_mul_mat_shape_summary(gb_executor* e) {
+    e->mm_summary = e->e->mul_mat_shape_summary();
+    return e->mm_summary.c_str();
+}
+int64_t gb_executor_launches_per_run(const gb_executor* e) { return e->e->launches_per_run(); }
+int gb_executor_set_kernel_timing(gb_executor* e, int enable) {
+    return guard([&] { e->e->set_kernel_timing(enable != 0); });
+}
+int gb_executor_reset_kernel_times(gb_executor* e) {
+    return guard([&] { e->e->reset_kernel_times(); });
+}
+const char* gb_executor_kernel_times(gb_executor* e) {
+    e->ktimes = e->e->kernel_times_json();
+    return e->ktimes.c_str();
+}
+void* gb_executor_stream(const gb_executor* e) { return (void*)e->e->stream(); }
+
+// ---- op level ----------------------------------------------------------------------------------
+
+int gb_repack_blocks(const void* gguf, int type, int64_t N, int64_t K, void* wq, void* wd,
+                     void* stream) {
+    return guard([&] {
+        gb::launch_repack_blocks((const uint8_t*)gguf, type, N, K, wq, (__half*)wd,
+                                 (cudaStream_t)stream);
+    });
+}
+int gb_quantize_q8_0(const float* x, int64_t x_stride, int64_t M, int64_t K, int8_t* xq,
+                     float* xd, void* stream) {
+    return guard([&] { gb::launch_quantize_q8_0(x, x_stride, M, K, xq, xd, (cudaStream_t)stream); });
+}
+int gb_mul_mat_q(int type, const void* wq, const void* wd, int64_t N, int64_t K,
+                 const int8_t* xq, const float* xd, int64_t M, float* y, const float* bias,
+                 const float* residual, void* stream) {
+    return guard([&] {
+        GB_CHECK(type == gb::T_Q8_0 || type == gb::T_Q4_0, "gb_mul_mat_q: type must be Q8_0 or Q4_0");
+        gb::QWeight w;
+        w.type = type;
+        w.N = N;
+        w.K = K;
+        w.qs = wq;
+        w.d = (const __half*)wd;
+        gb::MatmulEpilogue ep;
+        ep.bias = bias;
+        ep.residual = residual;
+        ep.res_stride = N;
+        gb::launch_matmul_q_exact(w, xq, xd, M, y, N, ep, (cudaStream_t)stream);
+    });
+}
+int gb_get_rows(int type, const void* wq, const void* wd, int64_t N, int64_t K,
+                const int32_t* ids, int64_t n, float* out, void* stream) {
+    return guard([&] {
+        gb::QWeight w;
+        w.type = type;
+        w.N = N;
+        w.K = K;
+        w.qs = wq;
+        w.d = (const __half*)wd;
+        gb::launch_get_rows(w, ids, n, out, K, (cudaStream_t)stream);
+    });
+}
+int gb_rms_norm(const float* x, int64_t M, int64_t D, float eps, const float* gamma, float* y,
+                int8_t* yq, float* yd, void* stream) {
+    return guard([&] {
+        gb::launch_rms_norm(x, D, M, D, eps, gamma, y, D, yq, yd, (cudaStream_t)stream);
+    });
+}
+int gb_swiglu(const float* x, int64_t M, int64_t F, float* y, int8_t* yq, float* yd,
+              void* stream) {
+    return guard([&] {
+        gb::launch_swiglu(x, 2 * F, M, F, false, y, F, yq, yd, (cudaStream_t)stream);
+    });
+}
+float gb_rope_table_fill(float* host_out, int64_t n_pos, int n_dims, float freq_base) {
+    const float ts = powf(freq_base, -2.0f / (float)n_dims);
+    const int half = n_dims / 2;
+    for (int64_t p = 0; p < n_pos; ++p) {
+        float theta = (float)p;
+        for (int i = 0; i < half; ++i) {
+            host_out[2 * (p * half + i)] = cosf(theta);
+            host_out[2 * (p * half + i) + 1] = sinf(theta);
+            theta *= ts;
+        }
+    }
+    return ts;
+}
+int gb_rope_neox(const float* x, int64_t hd, int64_t H, int64_t s, const int32_t* pos,
+                 int n_dims, float freq_base, const void* table, int64_t n_pos, float* y,
+                 void* stream) {
+    return guard([&] {
+        gb::TView xv, yv;
+        xv.data = (char*)x;
+        yv.data = (char*)y;
+        xv.type = yv.type = gb::T_F32;
+        xv.ne[0] = yv.ne[0] = hd;
+        xv.ne[1] = yv.ne[1] = H;
+        xv.ne[2] = yv.ne[2] = s;
+        xv.nb[0] = yv.nb[0] = 4;
+        xv.nb[1] = yv.nb[1] = 4 * hd;
+        xv.nb[2] = yv.nb[2] = 4 * hd * H;
+        xv.nb[3] = yv.nb[3] = 4 * hd * H * s;
+        gb::RopeTable rt;
+        rt.cs = (const float2*)table;
+        rt.n_pos = table ? n_pos : 0;
+        rt.n_dims = n_dims;
+        rt.theta_scale = powf(freq_base, -2.0f / (float)n_dims);
+        gb::launch_rope_neox(xv, pos, false, nullptr, rt, &yv, nullptr, (cudaStream_t)stream);
+    });
+}
+size_t gb_attention_workspace_bytes(int64_t s, int64_t Hq, int64_t hd, int64_t ctx) {
+    return gb::attn_workspace_bytes(s, Hq, hd, ctx);
+}
+int gb_attention(const float* q, const void* k, const void* v, int64_t hd, int64_t s,
+                 int64_t Hq, int64_t Hkv, int64_t ctx, int64_t kv_pos, float scale, float* o,
+                 void* work, void* stream) {
+    return guard([&] {
+        GB_CHECK(kv_pos >= 0 && kv_pos + s <= ctx, "gb_attention: kv_pos + s exceeds ctx");
+        gb::TView qv;
+        qv.data = (char*)q;
+        qv.type = gb::T_F32;
+        qv.ne[0] = hd;  // view [hd, s, Hq] over q[s][Hq][hd]
+        qv.ne[1] = s;
+        qv.ne[2] = Hq;
+        qv.nb[0] = 4;
+        qv.nb[1] = 4 * hd * Hq;
+        qv.nb[2] = 4 * hd;
+        qv.nb[3] = 4 * hd * Hq * s;
+        gb::launch_attention(qv, (const __half*)k, (const __half*)v, ctx, Hkv, nullptr, false,
+                             kv_pos, scale, o, work, ctx, (cudaStream_t)stream);
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,1132 @@
+// Graph lowering and execution (see executor.h).  Op semantics follow the reference executor
+// (runtime/src/executor.cpp: GET_ROWS :2034, ROPE :2053, FLASH_ATTN_EXT :2091-2354, MUL_MAT
+// :2362-2447, RESHAPE/PERMUTE/VIEW :2448-2560, custom ops 200-203 :2703-2757).
+#include "executor.h"
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <set>
+#include <sstream>
+
+#include "common.h"
+#include "kutil.cuh"
+
+namespace gb {
+
+namespace {
+
+constexpr int64_t kKvPad = 256;  // executor.h:181 kv_n_pad_
+
+int64_t pad_kv_len(int64_t n_kv, int64_t max_ctx) {
+    if (n_kv < 1) n_kv = 1;
+    int64_t padded = std::max(kKvPad, (n_kv + kKvPad - 1) / kKvPad * kKvPad);
+    return std::min(padded, max_ctx);
+}
+
+void set_contig(Val& v) {
+    const int64_t eb = v.type == T_F16 ? 2 : (v.type == T_I64 ? 8 : 4);
+    v.nb[0] = eb;
+    for (int d = 1; d < 4; ++d) v.nb[d] = v.nb[d - 1] * v.ne[d - 1];
+}
+
+int64_t nelem(const int64_t* ne) { return ne[0] * ne[1] * ne[2] * ne[3]; }
+
+double now_ms() {
+    return std::chrono::duration<double, std::milli>(
+               std::chrono::steady_clock::now().time_since_epoch())
+        .count();
+}
+
+}  // namespace
+
+bool Val::contiguous() const {
+    int64_t e = type == T_F16 ? 2 : (type == T_I64 ? 8 : 4);
+    if (nb[0] != e) return false;
+    int64_t s = e * ne[0];
+    for (int d = 1; d < 4; ++d) {
+        if (ne[d] > 1 && nb[d] != s) return false;
+        s *= ne[d];
+    }
+    return true;
+}
+
+TView Program::view(const Val& v) const {
+    TView t;
+    t.data = ptr(v.ref);
+    t.type = v.type;
+    for (int d = 0; d < 4; ++d) {
+        t.ne[d] = v.ne[d];
+        t.nb[d] = v.nb[d];
+    }
+    return t;
+}
+
+// ------------------------------------------------------------------------------ construction
+
+std::vector<std::string> Executor::available_devices() {
+    std::vector<std::string> out = {"cpu"};
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+    }
+    for (int i = 0; i < n; ++i) out.push_back("cuda:" + std::to_string(i));
+    if (n > 0) out.push_back("cuda");
+    return out;
+}
+
+Executor::Executor(std::shared_ptr<Graph> g, const std::string& device) : g_(std::move(g)) {
+    std::string d = device;
+    for (auto& c : d) c = (char)std::tolower((unsigned char)c);
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+    }
+    if (d == "auto") d = "cuda:0";
+    GB_CHECK(d.rfind("cuda", 0) == 0,
+             "device '" + device + "' is not served by the B200 engine (CUDA only; the CPU path "
+             "is the reference runtime)");
+    GB_CHECK(n > 0, "no CUDA device is visible");
+    dev_ = 0;
+    if (d.size() > 5 && d[4] == ':') dev_ = std::stoi(d.substr(5));
+    GB_CHECK(dev_ >= 0 && dev_ < n, "CUDA device index out of range: " + device);
+    device_ = "cuda:" + std::to_string(dev_);
+    GB_CUDA(cudaSetDevice(dev_));
+    GB_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+    GB_CUDA(cudaMallocHost(&h_step_, sizeof(StepParams)));
+    GB_CUDA(cudaMalloc(&d_step_, sizeof(StepParams)));
+    h_step_->pos = 0;
+    GB_CUDA(cudaMemcpy(d_step_, h_step_, sizeof(StepParams), cudaMemcpyHostToDevice));
+    upload_weights();
+}
+
+Executor::~Executor() {
+    cudaSetDevice(dev_);
+    if (stream_) cudaStreamSynchronize(stream_);
+    for (auto& [k, p] : programs_) free_program(*p);
+    for (void* p : weight_allocs_) cudaFree(p);
+    for (auto& [id, c] : kv_) {
+        cudaFree(c.k);
+        cudaFree(c.v);
+    }
+    for (auto& [id, p] : state_dev_) cudaFree(p);
+    for (auto& [k, t] : rope_tabs_) cudaFree(t.first);
+    for (cudaEvent_t ev : kevents_) cudaEventDestroy(ev);
+    if (h_step_) cudaFreeHost(h_step_);
+    if (d_step_) cudaFree(d_step_);
+    if (pinned_out_) cudaFreeHost(pinned_out_);
+    if (stream_) cudaStreamDestroy(stream_);
+}
+
+void Executor::free_program(Program& p) {
+    if (p.graph_exec) cudaGraphExecDestroy(p.graph_exec);
+    p.graph_exec = nullptr;
+    for (void* q : p.owned) cudaFree(q);
+    p.owned.clear();
+    if (p.arena) cudaFree(p.arena);
+    p.arena = nullptr;
+}
+
+// Upload every tensor with a GGUF payload: quantized matrices are repacked into the SoA layout
+// (aligned quants + fp16 scale rows), everything else is copied as is.
+void Executor::upload_weights() {
+    size_t staging_bytes = 0;
+    for (auto& [id, t] : g_->tensors)
+        if (t.data && is_quant(t.type)) staging_bytes = std::max<size_t>(staging_bytes, t.data_size);
+    uint8_t* staging = nullptr;
+    if (staging_bytes) GB_CUDA(cudaMalloc(&staging, staging_bytes));
+    for (auto& [id, t] : g_->tensors) {
+        if (!t.data || t.data_size == 0) continue;
+        if (is_quant(t.type)) {
+            const int64_t K = t.file_ne[0];
+            const int64_t N = t.file_ne[1] * t.file_ne[2] * t.file_ne[3];
+            QWeight w;
+            w.type = t.type;
+            w.N = N;
+            w.K = K;
+            const size_t qbytes = (size_t)(t.type == T_Q8_0 ? N * K : N * K / 2);
+            const size_t dbytes = (size_t)(N * (K / QK) * 2);
+            void* qs = nullptr;
+            void* dd = nullptr;
+            GB_CUDA(cudaMalloc(&qs, qbytes));
+            GB_CUDA(cudaMalloc(&dd, dbytes));
+            weight_allocs_.push_back(qs);
+            weight_allocs_.push_back(dd);
+            GB_CUDA(cudaMemcpyAsync(staging, t.data, t.data_size, cudaMemcpyHostToDevice, stream_));
+            launch_repack_blocks(staging, t.type, N, K, qs, (__half*)dd, stream_);
+            GB_CUDA(cudaStreamSynchronize(stream_));
+            w.qs = qs;
+            w.d = (const __half*)dd;
+            qweights_[id] = w;
+            weight_bytes_ += qbytes + dbytes;
+        } else {
+            void* p = nullptr;
+            GB_CUDA(cudaMalloc(&p, t.data_size));
+            weight_allocs_.push_back(p);
+            GB_CUDA(cudaMemcpy(p, t.data, t.data_size, cudaMemcpyHostToDevice));
+            consts_[id] = (char*)p;
+            weight_bytes_ += t.data_size;
+            if (t.type == T_F32 || t.type == T_F16) {
+                QWeight w;
+                w.type = t.type;
+                w.K = t.file_ne[0];
+                w.N = t.file_ne[1] * t.file_ne[2] * t.file_ne[3];
+                w.qs = p;
+                qweights_[id] = w;
+            }
+        }
+    }
+    if (staging) cudaFree(staging);
+}
+
+// ------------------------------------------------------------------------------ KV cache
+
+void Executor::init_kv_cache(int64_t max_ctx) {
+    if (kv_enabled_) return;
+    // enable rule of the reference (executor.cpp:505-539)
+    bool has_rope = false, has_pos_sym = false, has_pos_in = false, has_arange = false;
+    for (auto& op : g_->ops) has_rope |= op.opcode == OP_ROPE;
+    for (auto& s : g_->symbol_table) has_pos_sym |= s == "pos";
+    for (uint32_t id : g_->inputs) {
+        auto it = g_->tensors.find(id);
+        if (it != g_->tensors.end() &&
+            (it->second.name == "position_ids" || it->second.name.find("pos") != std::string::npos))
+            has_pos_in = true;
+    }
+    for (auto& [id, t] : g_->tensors)
+        if (t.name.find("arange") != std::string::npos && t.data) has_arange = true;
+    if (!has_rope && !has_pos_sym && !has_arange && !has_pos_in) return;
+    SymEnv env;
+    env["s"] = 1;
+    for (auto& s : g_->symbol_table) env[s] = 1;
+    bool any = false;
+    for (auto& op : g_->ops) {
+        if (op.opcode != OP_FLASH_ATTN_EXT) continue;
+        const GTensor& k = g_->t(op.inputs.at(1));
+        KVCache c;
+        c.hd = k.ne[0]->eval(env);
+        c.Hkv = k.ne[2]->eval(env);
+        c.batch = k.ne[3]->eval(env);
+        c.ctx = max_ctx;
+        const size_t bytes = (size_t)(c.hd * c.Hkv * c.batch * max_ctx) * 2;
+        GB_CUDA(cudaMalloc(&c.k, bytes));
+        GB_CUDA(cudaMalloc(&c.v, bytes));
+        GB_CUDA(cudaMemset(c.k, 0, bytes));
+        GB_CUDA(cudaMemset(c.v, 0, bytes));
+        kv_[op.id] = c;
+        any = true;
+    }
+    if (!any) return;
+    kv_max_ctx_ = max_ctx;
+    kv_enabled_ = true;
+}
+
+void Executor::reset_kv_cache() {
+    for (auto& [id, c] : kv_) {
+        const size_t bytes = (size_t)(c.hd * c.Hkv * c.batch * c.ctx) * 2;
+        GB_CUDA(cudaMemsetAsync(c.k, 0, bytes, stream_));
+        GB_CUDA(cudaMemsetAsync(c.v, 0, bytes, stream_));
+    }
+}
+
+// Host table of (cos, sin) for positions 0..n_pos-1, computed exactly as ggml_rope_cache_init
+// does on the CPU (ops.cpp:5910-5923): theta starts at the position, is multiplied by
+// theta_scale = powf(base, -2/n_dims) once per pair in fp32, and cosf/sinf come from libm.
+const float2* Executor::rope_table(int n_dims, float freq_base, float freq_scale, int64_t* n_pos,
+                                   float* theta_scale) {
+    const float ts = powf(freq_base, -2.0f / (float)n_dims);
+    *theta_scale = ts;
+    const int64_t np = std::max<int64_t>(4096, kv_max_ctx_);
+    char key[96];
+    snprintf(key, sizeof(key), "%d/%a/%a/%lld", n_dims, freq_base, freq_scale, (long long)np);
+    auto it = rope_tabs_.find(key);
+    if (it != rope_tabs_.end()) {
+        *n_pos = it->second.second.first;
+        return it->second.first;
+    }
+    const int half = n_dims / 2;
+    std::vector<float2> h((size_t)(np * half));
+    for (int64_t p = 0; p < np; ++p) {
+        float theta = (float)p;
+        for (int i = 0; i < half; ++i) {
+            const float th = freq_scale * theta;
+            h[(size_t)(p * half + i)] = make_float2(cosf(th), sinf(th));
+            theta *= ts;
+        }
+    }
+    float2* d = nullptr;
+    GB_CUDA(cudaMalloc(&d, h.size() * sizeof(float2)));
+    GB_CUDA(cudaMemcpy(d, h.data(), h.size() * sizeof(float2), cudaMemcpyHostToDevice));
+    rope_tabs_[key] = {d, {np, ts}};
+    *n_pos = np;
+    return d;
+}
+
+// ------------------------------------------------------------------------------ lowering
+
+std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
+    auto P = std::make_shared<Program>();
+    Program& pg = *P;
+    pg.env = env;
+    pg.kv = kv;
+    const Graph& G = *g_;
+    const int nops = (int)G.ops.size();
+
+    // concrete shapes
+    std::map<uint32_t, std::array<int64_t, 4>> shape;
+    for (auto& [id, t] : G.tensors) {
+        std::array<int64_t, 4> ne{1, 1, 1, 1};
+        for (int d = 0; d < 4; ++d) ne[d] = t.ne[d] ? t.ne[d]->eval(env) : 1;
+        shape[id] = ne;
+    }
+    // consumers (op indices) per tensor
+    std::map<uint32_t, std::vector<int>> consumers;
+    for (int i = 0; i < nops; ++i)
+        for (uint32_t in : G.ops[i].inputs) consumers[in].push_back(i);
+    std::set<uint32_t> outputs(G.outputs.begin(), G.outputs.end());
+    auto& vals = pg.vals;
+
+    // graph inputs: persistent device buffers sized for this program
+    for (uint32_t id : G.inputs) {
+        const GTensor& t = G.t(id);
+        Val v;
+        v.type = t.type;
+        for (int d = 0; d < 4; ++d) v.ne[d] = shape[id][d];
+        set_contig(v);
+        const size_t bytes = (size_t)(nelem(v.ne) * v.nb[0]);
+        char* p = nullptr;
+        GB_CUDA(cudaMalloc(&p, std::max<size_t>(bytes, 16)));
+        pg.owned.push_back(p);
+        pg.input_bufs[id] = p;
+        v.ref.fixed = p;
+        vals[id] = v;
+    }
+    // weights / constants
+    auto weight_val = [&](uint32_t id) -> Val {
+        const GTensor& t = G.t(id);
+        Val v;
+        v.type = t.type;
+        for (int d = 0; d < 4; ++d) v.ne[d] = shape[id][d];
+        auto qw = qweights_.find(id);
+        if (qw != qweights_.end() && is_quant(t.type)) {
+            v.w = &qw->second;
+            v.has_f = false;
+            return v;
+        }
+        auto c = consts_.find(id);
+        GB_CHECK(c != consts_.end(), "tensor '" + t.name + "' has no data");
+        if (qw != qweights_.end()) v.w = &qw->second;
+        set_contig(v);
+        v.ref.fixed = c->second;
+        // the arange constant is offset by pos when the KV cache is in use (executor.cpp:2854)
+        return v;
+    };
+    auto get = [&](uint32_t id) -> Val& {
+        auto it = vals.find(id);
+        if (it != vals.end()) return it->second;
+        const GTensor& t = G.t(id);
+        GB_CHECK(t.data != nullptr, "tensor '" + t.name + "' (id " + std::to_string(id) +
+                                        ") is used before it is produced");
+        vals[id] = weight_val(id);
+        return vals[id];
+    };
+
+    auto add = [&](const std::string& name, Launch fn, double bytes = 0.0) {
+        pg.launches.push_back(std::move(fn));
+        pg.launch_names.push_back(name);
+        pg.launch_bytes.push_back(bytes);
+    };
+    // algorithmic bytes of a quantized matmul: weight quants + scales once, Q8_0 activations,
+    // f32 outputs (and residual reads)
+    auto mm_bytes = [](const QWeight* w, int64_t M, bool residual) {
+        const double wb = w->type == T_Q8_0 ? (double)w->N * w->K * (34.0 / 32.0)
+                                            : (double)w->N * w->K * (18.0 / 32.0);
+        return wb + (double)M * w->K * (34.0 / 32.0) + (double)M * w->N * 4.0 * (residual ? 2 : 1);
+    };
+    auto alloc = [&](Val& v, int op) {
+        set_contig(v);
+        v.ref = BufRef{};
+        v.ref.buf = pg.new_buf(nelem(v.ne) * v.nb[0], op);
+    };
+    // Q8_0 rows for a value (rows of ne0); emits a quantize launch unless already present
+    auto ensure_q = [&](Val& x, int op) {
+        if (x.has_q) {
+            pg.use(x.q, op);
+            pg.use(x.qd, op);
+            return;
+        }
+        GB_CHECK(x.has_f && x.type == T_F32, "matmul input is not f32");
+        GB_CHECK(x.nb[0] == 4 && x.rows_uniform(), "matmul input rows are not uniform");
+        const int64_t M = x.nrows(), K = x.ne[0];
+        x.q.buf = pg.new_buf(M * K, op);
+        x.qd.buf = pg.new_buf(M * (K / QK) * 4, op);
+        x.has_q = true;
+        pg.use(x.ref, op);
+        const BufRef src = x.ref, qb = x.q, qdb = x.qd;
+        const int64_t stride = x.nb[1] / 4;
+        add("quantize_q8_0", [=](Program& p, cudaStream_t st) {
+            launch_quantize_q8_0((const float*)p.ptr(src), stride, M, K, (int8_t*)p.ptr(qb),
+                                 (float*)p.ptr(qdb), st);
+        });
+    };
+    auto cont = [&](Val x, int op) -> Val {
+        Val y;
+        y.type = x.type == T_F16 ? T_F16 : (x.type == T_I32 ? T_I32 : T_F32);
+        for (int d = 0; d < 4; ++d) y.ne[d] = x.ne[d];
+        alloc(y, op);
+        pg.use(x.ref, op);
+        const Val xs = x, ys = y;
+        add("cont", [=](Program& p, cudaStream_t st) { launch_copy(p.view(xs), p.view(ys), st); });
+        return y;
+    };
+    // which consumers need f32 / Q8_0 of tensor id
+    auto needs = [&](uint32_t id, bool& need_f, bool& need_q) {
+        need_f = outputs.count(id) != 0;
+        need_q = false;
+        for (int ci : consumers[id]) {
+            const GOp& c = G.ops[ci];
+            const bool qmm = c.opcode == OP_MUL_MAT && c.inputs.size() >= 2 && c.inputs[1] == id &&
+                             is_quant(G.t(c.inputs[0]).type) && c.inputs[0] != id;
+            if (qmm && !(logits_last_only_ && outputs.count(c.outputs[0]))) need_q = true;
+            else need_f = true;
+        }
+        if (!need_f && !need_q) need_f = true;
+    };
+
+    std::set<int> skip;  // ops folded into an earlier launch
+    for (int oi = 0; oi < nops; ++oi) {
+        if (skip.count(oi)) continue;
+        const GOp& op = G.ops[oi];
+        GB_CHECK(!op.outputs.empty(), "op without outputs");
+        const uint32_t out = op.outputs[0];
+        const auto& one = shape[out];
+        auto in = [&](size_t k) -> Val& { return get(op.inputs.at(k)); };
+        for (uint32_t iid : op.inputs) {
+            Val& iv = get(iid);
+            pg.use(iv.ref, oi);
+            if (iv.has_q) {
+                pg.use(iv.q, oi);
+                pg.use(iv.qd, oi);
+            }
+        }
+        Val o;
+        o.type = T_F32;
+        for (int d = 0; d < 4; ++d) o.ne[d] = one[d];
+
+        switch (op.opcode) {
+            case OP_GET_ROWS: {
+                Val& w = in(0);
+                Val ids = in(1);
+                GB_CHECK(w.w, "GET_ROWS table must be a weight tensor");
+                GB_CHECK(ids.type == T_I32, "GET_ROWS indices must be int32");
+                if (!ids.contiguous()) ids = cont(ids, oi);
+                const int64_t n = nelem(ids.ne);
+                alloc(o, oi);
+                const QWeight* qw = w.w;
+                const BufRef ir = ids.ref, orf = o.ref;
+                const int64_t K = qw->K;
+                add("get_rows", [=](Program& p, cudaStream_t st) {
+                    launch_get_rows(*qw, (const int32_t*)p.ptr(ir), n, (float*)p.ptr(orf), K, st);
+                });
+                break;
+            }
+            case OP_RMS_NORM_C:
+            case OP_RMS_NORM:
+            case OP_LAYER_NORM:
+            case OP_NORM: {
+                Val x = in(0);
+                if (!(x.nb[0] == 4 && x.rows_uniform())) x = cont(x, oi);
+                const float eps = (float)op.f("eps", 1e-5);
+                const float* gamma = nullptr;
+                const float* beta = nullptr;
+                if (op.inputs.size() > 1) gamma = (const float*)get(op.inputs[1]).ref.fixed;
+                if (op.inputs.size() > 2) beta = (const float*)get(op.inputs[2]).ref.fixed;
+                bool nf, nq;
+                needs(out, nf, nq);
+                const int64_t D = x.ne[0], M = x.nrows();
+                if (nf) alloc(o, oi);
+                else o.has_f = false;
+                if (nq) {
+                    o.q.buf = pg.new_buf(M * D, oi);
+                    o.qd.buf = pg.new_buf(M * (D / QK) * 4, oi);
+                    o.has_q = true;
+                }
+                const BufRef xr = x.ref, orf = o.ref, qr = o.q, qdr = o.qd;
+                const int64_t xs = x.nb[1] / 4;
+                const bool rms = op.opcode == OP_RMS_NORM_C || op.opcode == OP_RMS_NORM;
+                const bool hf = o.has_f, hq = o.has_q;
+                add(rms ? "rms_norm" : "layer_norm", [=](Program& p, cudaStream_t st) {
+                    float* y = hf ? (float*)p.ptr(orf) : nullptr;
+                    int8_t* yq = hq ? (int8_t*)p.ptr(qr) : nullptr;
+                    float* yd = hq ? (float*)p.ptr(qdr) : nullptr;
+                    if (rms)
+                        launch_rms_norm((const float*)p.ptr(xr), xs, M, D, eps, gamma, y, D, yq, yd, st);
+                    else
+                        launch_layer_norm((const float*)p.ptr(xr), xs, M, D, eps, gamma, beta, y, D,
+                                          yq, yd, st);
+                });
+                break;
+            }
+            case OP_MUL_MAT: {
+                Val& wv = in(0);
+                GB_CHECK(wv.w, "MUL_MAT: first operand must be a weight matrix");
+                const QWeight* qw = wv.w;
+                Val& xin = in(1);
+                const int64_t K = qw->K, N = qw->N;
+                GB_CHECK(xin.ne[0] == K, "MUL_MAT: inner dimensions differ (" +
+                                             std::to_string(xin.ne[0]) + " vs " +
+                                             std::to_string(K) + ")");
+                int64_t M = xin.nrows();
+                int64_t row0 = 0;
+                const bool last_only = logits_last_only_ && outputs.count(out) && M > 1;
+                if (last_only) {
+                    row0 = M - 1;
+                    o.ne[1] = 1;
+                    o.ne[2] = 1;
+                    o.ne[3] = 1;
+                }
+                const int64_t Mrun = last_only ? 1 : M;
+                // fused residual ADD: the only consumer is ADD(other, this) of equal shape
+                int add_op = -1;
+                const float* bias = nullptr;
+                if (op.inputs.size() > 2) bias = (const float*)get(op.inputs[2]).ref.fixed;
+                Val res;
+                if (!outputs.count(out) && consumers[out].size() == 1 && !last_only) {
+                    const int ci = consumers[out][0];
+                    const GOp& c = G.ops[ci];
+                    if (c.opcode == OP_ADD && c.inputs.size() == 2 && c.inputs[0] != c.inputs[1]) {
+                        const uint32_t other = c.inputs[0] == out ? c.inputs[1] : c.inputs[0];
+                        auto ov = vals.find(other);
+                        if (ov != vals.end() && ov->second.has_f && ov->second.type == T_F32 &&
+                            ov->second.contiguous() && nelem(ov->second.ne) == N * M &&
+                            ov->second.ne[0] == N) {
+                            add_op = ci;
+                            res = ov->second;
+                        }
+                    }
+                }
+                Val y = o;
+                const uint32_t out_id = add_op >= 0 ? G.ops[add_op].outputs[0] : out;
+                if (add_op >= 0)
+                    for (int d = 0; d < 4; ++d) y.ne[d] = shape[out_id][d];
+                alloc(y, oi);
+                MatmulEpilogue ep;
+                ep.bias = bias;
+                BufRef rref;
+                if (add_op >= 0) {
+                    rref = res.ref;
+                    pg.use(res.ref, add_op);
+                    ep.res_stride = N;
+                }
+                const BufRef yr = y.ref;
+                const int64_t ystride = N;
+                if (is_quant(qw->type)) {
+                    if (last_only) {
+                        // quantize only the last row (the CPU path quantizes the gathered row)
+                        GB_CHECK(xin.has_f, "last-token matmul needs f32 input");
+                        Val xl = xin;
+                        xl.ref.off += row0 * xin.nb[1];
+                        xl.ne[1] = 1;
+                        xl.ne[2] = 1;
+                        xl.ne[3] = 1;
+                        xl.has_q = false;
+                        ensure_q(xl, oi);
+                        const BufRef qb = xl.q, qdb = xl.qd;
+                        add("matmul_q", [=](Program& p, cudaStream_t st) {
+                            MatmulEpilogue e = ep;
+                            launch_matmul_q_exact(*qw, (const int8_t*)p.ptr(qb),
+                                                  (const float*)p.ptr(qdb), 1, (float*)p.ptr(yr),
+                                                  ystride, e, st);
+                        }, mm_bytes(qw, 1, false));
+                    } else {
+                        ensure_q(xin, oi);
+                        const BufRef qb = xin.q, qdb = xin.qd;
+                        add("matmul_q", [=](Program& p, cudaStream_t st) {
+                            MatmulEpilogue e = ep;
+                            if (rref.fixed || rref.buf >= 0) e.residual = (const float*)p.ptr(rref);
+                            launch_matmul_q_exact(*qw, (const int8_t*)p.ptr(qb),
+                                                  (const float*)p.ptr(qdb), Mrun, (float*)p.ptr(yr),
+                                                  ystride, e, st);
+                        }, mm_bytes(qw, Mrun, add_op >= 0));
+                    }
+                } else {
+                    Val x = xin;
+                    if (!(x.nb[0] == 4 && x.rows_uniform())) x = cont(x, oi);
+                    const BufRef xr = x.ref;
+                    const int64_t xs = x.nb[1] / 4;
+                    const int64_t off = row0 * x.nb[1];
+                    add("matmul_f", [=](Program& p, cudaStream_t st) {
+                        MatmulEpilogue e = ep;
+                        if (rref.fixed || rref.buf >= 0) e.residual = (const float*)p.ptr(rref);
+                        launch_matmul_f(*qw, (const float*)(p.ptr(xr) + off), xs, Mrun,
+                                        (float*)p.ptr(yr), ystride, e, st);
+                    });
+                }
+                if (add_op >= 0) {
+                    vals[out_id] = y;
+                    skip.insert(add_op);
+                    continue;
+                }
+                vals[out] = y;
+                continue;
+            }
+            case OP_VIEW: {
+                Val x = in(0);
+                if (!x.contiguous() && x.ref.buf >= 0 && false) x = cont(x, oi);
+                const int g = (int)op.i("ggml_dim", 0);
+                const int64_t start = op.i("start", 0), step = op.i("step", 1),
+                              mult = op.i("offset_mult", 1);
+                o = x;
+                o.has_q = false;
+                o.w = nullptr;
+                for (int d = 0; d < 4; ++d) o.ne[d] = one[d];
+                o.ref.off += start * mult * x.nb[g];
+                if (g >= 1) o.nb[g] = x.nb[g] * step;
+                if (g == 0) GB_CHECK(step == 1, "VIEW with a step along dim 0 is not supported");
+                if (outputs.count(out) && !o.contiguous()) o = cont(o, oi);
+                break;
+            }
+            case OP_RESHAPE: {
+                Val x = in(0);
+                o = x;
+                o.has_q = false;
+                o.w = nullptr;
+                for (int d = 0; d < 4; ++d) o.ne[d] = one[d];
+                GB_CHECK(nelem(o.ne) == nelem(x.ne), "RESHAPE: element count mismatch");
+                if (x.contiguous()) {
+                    set_contig(o);
+                    if (x.has_q && x.ne[0] == o.ne[0]) {
+                        o.has_q = true;
+                        o.q = x.q;
+                        o.qd = x.qd;
+                    }
+                    o.has_f = x.has_f;
+                    if (!o.has_f) {  // only Q8_0 rows exist: keep them
+                        o.ref = x.ref;
+                    }
+                } else if (x.nb[0] == 4 && x.ne[0] == one[0] * one[1] && x.ne[1] == one[2] &&
+                           x.ne[2] == 1 && x.ne[3] == 1 && one[3] == 1) {
+                    // strided split of a fused-QKV slice (executor.cpp:80-113)
+                    o.nb[0] = x.nb[0];
+                    o.nb[1] = x.nb[0] * one[0];
+                    o.nb[2] = x.nb[1];
+                    o.nb[3] = x.nb[1] * one[2];
+                } else {
+                    Val c = cont(x, oi);
+                    o = c;
+                    for (int d = 0; d < 4; ++d) o.ne[d] = one[d];
+                    set_contig(o);
+                }
+                break;
+            }
+            case OP_PERMUTE:
+            case OP_TRANSPOSE: {
+                Val x = in(0);
+                int ax[4] = {1, 0, 2, 3};
+                if (op.opcode == OP_PERMUTE) {
+                    ax[0] = (int)op.i("axis0", 1);
+                    ax[1] = (int)op.i("axis1", 0);
+                    ax[2] = (int)op.i("axis2", 2);
+                    ax[3] = (int)op.i("axis3", 3);
+                }
+                o = x;
+                o.has_q = false;
+                o.w = nullptr;
+                for (int d = 0; d < 4; ++d) {
+                    o.ne[ax[d]] = x.ne[d];
+                    o.nb[ax[d]] = x.nb[d];
+                }
+                if (outputs.count(out)) o = cont(o, oi);
+                break;
+            }
+            case OP_CONT:
+            case OP_CPY: {
+                o = cont(in(0), oi);
+                for (int d = 0; d < 4; ++d) o.ne[d] = one[d];
+                set_contig(o);
+                break;
+            }
+            case OP_ROPE: {
+                Val x = in(0);
+                const int mode = (int)op.i("mode", 2);
+                GB_CHECK(mode == 2, "ROPE: only NEOX mode (2) is supported");
+                GB_CHECK(op.inputs.size() < 3, "ROPE: frequency factors are not supported");
+                GB_CHECK(op.f("ext_factor", 0.0) == 0.0, "ROPE: YaRN ext_factor is not supported");
+                const int n_dims = (int)op.i("n_dims", x.ne[0]);
+                const float fb = (float)op.f("freq_base", 10000.0);
+                const float fs = (float)op.f("freq_scale", 1.0);
+                const uint32_t pid = op.inputs.at(1);
+                Val pv = get(pid);
+                GB_CHECK(pv.type == T_I32, "ROPE positions must be int32");
+                if (!pv.contiguous()) pv = cont(pv, oi);
+                const GTensor& pt = G.t(pid);
+                const bool arange = pt.data && pt.name.find("arange") != std::string::npos;
+                const bool use_step = arange && env.count("pos");
+                // an identity arange (0, 1, 2, ...) is replaced by base + i on the device, so
+                // positions past the stored constant's length stay valid
+                bool identity = false;
+                if (arange && pt.type == T_I32) {
+                    identity = true;
+                    const int32_t* a = (const int32_t*)pt.data;
+                    for (uint64_t i = 0; i < pt.data_size / 4; ++i)
+                        if (a[i] != (int32_t)i) { identity = false; break; }
+                }
+                const int64_t npos = nelem(pv.ne);
+                bool permuted = false;
+                if (x.ne[2] != npos && x.ne[1] == npos) {  // [hd, s, H] input (executor.cpp:2076)
+                    permuted = true;
+                    std::swap(x.ne[1], x.ne[2]);
+                    std::swap(x.nb[1], x.nb[2]);
+                }
+                Val y;
+                y.type = T_F32;
+                for (int d = 0; d < 4; ++d) y.ne[d] = x.ne[d];
+                alloc(y, oi);
+                int64_t tab_n = 0;
+                float ts = 1.0f;
+                const float2* tab = rope_table(n_dims, fb, fs, &tab_n, &ts);
+                RopeTable rt;
+                rt.cs = tab;
+                rt.n_pos = tab_n;
+                rt.n_dims = n_dims;
+                rt.theta_scale = ts;
+                const Val xs = x, ys = y;
+                const BufRef pr = pv.ref;
+                const bool ident = identity;
+                const StepParams* dstep = d_step_;
+                add("rope", [=](Program& p, cudaStream_t st) {
+                    TView yv = p.view(ys);
+                    launch_rope_neox(p.view(xs), ident ? nullptr : (const int32_t*)p.ptr(pr),
+                                     use_step, dstep, rt, &yv, nullptr, st);
+                });
+                o = y;
+                if (permuted) {
+                    std::swap(o.ne[1], o.ne[2]);
+                    std::swap(o.nb[1], o.nb[2]);
+                }
+                break;
+            }
+            case OP_FLASH_ATTN_EXT: {
+                Val q = in(0), k = in(1);
+                Val v = op.inputs.size() > 2 ? in(2) : in(1);
+                GB_CHECK(op.inputs.size() <= 3, "FLASH_ATTN_EXT with an explicit mask is not supported");
+                const int64_t hd = q.ne[0], s = q.ne[1], Hq = q.ne[2];
+                const int64_t Hkv = k.ne[2];
+                GB_CHECK(q.ne[3] == 1 && k.ne[3] == 1, "batched attention (ne3 > 1) is not supported");
+                float scale = 1.0f / sqrtf((float)hd);
+                if (op.has("scale")) scale = (float)op.f("scale", scale);
+                const bool causal = op.i("is_causal", 0) != 0;
+                const bool fused_t = op.i("fused_transpose", 0) != 0;
+                const bool use_cache = kv && kv_.count(op.id);
+                // K/V destination: the persistent cache, or a per-call f16 scratch
+                __half* kc;
+                __half* vc;
+                int64_t ctx;
+                BufRef kref, vref;
+                if (use_cache) {
+                    const KVCache& c = kv_.at(op.id);
+                    GB_CHECK(c.hd == hd && c.Hkv == Hkv, "KV cache shape mismatch");
+                    kc = c.k;
+                    vc = c.v;
+                    ctx = c.ctx;
+                    kref.fixed = (char*)kc;
+                    vref.fixed = (char*)vc;
+                } else {
+                    ctx = k.ne[1];
+                    kref.buf = pg.new_buf(Hkv * ctx * hd * 2, oi);
+                    vref.buf = pg.new_buf(Hkv * ctx * hd * 2, oi);
+                    kc = vc = nullptr;
+                }
+                // k/v arrive as [hd, s, Hkv]; the cache writer walks [hd, Hkv, s]
+                auto heads_then_rows = [](Val t) {
+                    std::swap(t.ne[1], t.ne[2]);
+                    std::swap(t.nb[1], t.nb[2]);
+                    return t;
+                };
+                GB_CHECK(k.ne[1] == s && v.ne[1] == s && v.ne[2] == Hkv,
+                         "FLASH_ATTN_EXT: K/V rows must match the query rows");
+                const Val ks = heads_then_rows(k), vs = heads_then_rows(v), qs = q;
+                const StepParams* dstep = use_cache ? d_step_ : nullptr;
+                add("kv_write", [=](Program& p, cudaStream_t st) {
+                    KVDst kd{(__half*)p.ptr(kref), ctx};
+                    KVDst vd{(__half*)p.ptr(vref), ctx};
+                    launch_kv_write(p.view(ks), dstep, kd, st);
+                    launch_kv_write(p.view(vs), dstep, vd, st);
+                });
+                Val y;
+                y.type = T_F32;
+                y.ne[0] = hd;
+                y.ne[1] = Hq;
+                y.ne[2] = s;
+                y.ne[3] = 1;
+                alloc(y, oi);
+                const int64_t max_kv = use_cache ? pad_kv_len(kv_max_ctx_, kv_max_ctx_) : s;
+                const size_t wbytes = attn_workspace_bytes(s, Hq, hd, max_kv);
+                BufRef wref;
+                if (wbytes) wref.buf = pg.new_buf((int64_t)wbytes, oi);
+                const BufRef yr = y.ref;
+                const bool step_on = use_cache;
+                add("attention", [=](Program& p, cudaStream_t st) {
+                    launch_attention(p.view(qs), (const __half*)p.ptr(kref), (const __half*)p.ptr(vref),
+                                     ctx, Hkv, dstep, step_on, 0, scale, (float*)p.ptr(yr),
+                                     wbytes ? p.ptr(wref) : nullptr, max_kv, st);
+                });
+                (void)causal;
+                o = y;
+                if (!fused_t) {
+                    std::swap(o.ne[1], o.ne[2]);
+                    std::swap(o.nb[1], o.nb[2]);
+                }
+                for (int d = 0; d < 4; ++d)
+                    GB_CHECK(o.ne[d] == one[d], "FLASH_ATTN_EXT output shape mismatch");
+                break;
+            }
+            case OP_ADD:
+            case OP_MUL: {
+                Val a = in(0), b = in(1);
+                alloc(o, oi);
+                const Val as = a, bs = b, os = o;
+                const int bop = op.opcode == OP_ADD ? 0 : 1;
+                add(bop ? "mul" : "add",
+                    [=](Program& p, cudaStream_t st) { launch_binary(p.view(as), p.view(bs), p.view(os), bop, st); });
+                break;
+            }
+            case OP_SWIGLU:
+            case OP_GLU: {
+                GB_CHECK(op.inputs.size() == 1, "split SWIGLU (gate, up) is not supported");
+                Val x = in(0);
+                if (!(x.nb[0] == 4 && x.rows_uniform())) x = cont(x, oi);
+                const int64_t F = x.ne[0] / 2, M = x.nrows();
+                const bool swapped = op.i("swapped", 0) != 0;
+                bool nf, nq;
+                needs(out, nf, nq);
+                if (nf) alloc(o, oi);
+                else o.has_f = false;
+                if (nq) {
+                    o.q.buf = pg.new_buf(M * F, oi);
+                    o.qd.buf = pg.new_buf(M * (F / QK) * 4, oi);
+                    o.has_q = true;
+                }
+                const BufRef xr = x.ref, orf = o.ref, qr = o.q, qdr = o.qd;
+                const int64_t xs = x.nb[1] / 4;
+                const bool hf = o.has_f, hq = o.has_q;
+                add("swiglu", [=](Program& p, cudaStream_t st) {
+                    launch_swiglu((const float*)p.ptr(xr), xs, M, F, swapped,
+                                  hf ? (float*)p.ptr(orf) : nullptr, F,
+                                  hq ? (int8_t*)p.ptr(qr) : nullptr, hq ? (float*)p.ptr(qdr) : nullptr,
+                                  st);
+                });
+                break;
+            }
+            case OP_BIAS_GELU: {
+                Val x = in(0);
+                if (!(x.nb[0] == 4 && x.rows_uniform())) x = cont(x, oi);
+                const float* bias = op.inputs.size() > 1 ? (const float*)get(op.inputs[1]).ref.fixed : nullptr;
+                const int64_t F = x.ne[0], M = x.nrows();
+                bool nf, nq;
+                needs(out, nf, nq);
+                if (nf) alloc(o, oi);
+                else o.has_f = false;
+                if (nq) {
+                    o.q.buf = pg.new_buf(M * F, oi);
+                    o.qd.buf = pg.new_buf(M * (F / QK) * 4, oi);
+                    o.has_q = true;
+                }
+                const BufRef xr = x.ref, orf = o.ref, qr = o.q, qdr = o.qd;
+                const int64_t xs = x.nb[1] / 4;
+                const bool hf = o.has_f, hq = o.has_q;
+                add("bias_gelu", [=](Program& p, cudaStream_t st) {
+                    launch_bias_gelu((const float*)p.ptr(xr), xs, bias, M, F,
+                                     hf ? (float*)p.ptr(orf) : nullptr, F,
+                                     hq ? (int8_t*)p.ptr(qr) : nullptr,
+                                     hq ? (float*)p.ptr(qdr) : nullptr, st);
+                });
+                break;
+            }
+            default:
+                GB_CHECK(false, "opcode " + std::to_string(op.opcode) + " ('" + op.name +
+                                    "') is not supported by the B200 engine");
+        }
+        vals[out] = o;
+    }
+
+    // outputs stay live to the end
+    for (uint32_t id : G.outputs) {
+        auto it = vals.find(id);
+        GB_CHECK(it != vals.end(), "graph output was not produced");
+        GB_CHECK(it->second.has_f && it->second.contiguous(), "graph output is not contiguous");
+        pg.use(it->second.ref, nops + 1);
+    }
+
+    // assign arena offsets: greedy placement of buffers by size over their live ranges
+    const int nb = (int)pg.buf_size.size();
+    std::vector<int> order(nb);
+    for (int i = 0; i < nb; ++i) order[i] = i;
+    std::sort(order.begin(), order.end(), [&](int a, int b) { return pg.buf_size[a] > pg.buf_size[b]; });
+    pg.buf_off.assign(nb, 0);
+    std::vector<int> placed;
+    int64_t total = 0;
+    for (int b : order) {
+        std::vector<std::pair<int64_t, int64_t>> busy;
+        for (int o2 : placed)
+            if (!(pg.buf_last[o2] < pg.buf_first[b] || pg.buf_last[b] < pg.buf_first[o2]))
+                busy.push_back({pg.buf_off[o2], pg.buf_off[o2] + pg.buf_size[o2]});
+        std::sort(busy.begin(), busy.end());
+        int64_t off = 0;
+        for (auto& r : busy) {
+            if (off + pg.buf_size[b] <= r.first) break;
+            off = std::max(off, r.second);
+        }
+        pg.buf_off[b] = off;
+        total = std::max(total, off + pg.buf_size[b]);
+        placed.push_back(b);
+    }
+    pg.arena_bytes = (size_t)total;
+    if (total) GB_CUDA(cudaMalloc(&pg.arena, (size_t)total));
+    return P;
+}
+
+// ------------------------------------------------------------------------------ execution
+
+void Executor::prepare(const SymEnv& env_in, bool /*arena_reuse*/) {
+    const double t0 = profile_on_ ? now_ms() : 0;
+    GB_CUDA(cudaSetDevice(dev_));
+    SymEnv env = env_in;
+    const bool kv = kv_enabled_ && env.count("pos");
+    int64_t pos = kv ? env.at("pos") : 0;
+    // the program key: every symbol except pos (kernels read pos from StepParams)
+    std::string key = kv ? "kv" : "plain";
+    if (logits_last_only_) key += "/last";
+    SymEnv shape_env;
+    for (auto& [k, v] : env)
+        if (k != "pos") shape_env[k] = v;
+    std::vector<std::pair<std::string, int64_t>> items(shape_env.begin(), shape_env.end());
+    std::sort(items.begin(), items.end());
+    for (auto& [k, v] : items) key += "/" + k + "=" + std::to_string(v);
+    if (kv) {
+        int64_t s = env.count("s") ? env.at("s") : 1;
+        GB_CHECK(pos >= 0 && pos + s <= kv_max_ctx_,
+                 "KV cache overflow: pos " + std::to_string(pos) + " + s " + std::to_string(s) +
+                     " > max_ctx " + std::to_string(kv_max_ctx_));
+    }
+    auto it = programs_.find(key);
+    if (it == programs_.end()) {
+        SymEnv benv = shape_env;
+        if (kv) benv["pos"] = pos;
+        auto p = build(benv, kv);
+        p->key = key;
+        p->s = env.count("s") ? env.at("s") : 0;
+        p->decode = kv && p->s == 1;
+        programs_[key] = p;
+        active_ = p;
+    } else {
+        active_ = it->second;
+    }
+    h_step_->pos = pos;
+    if (profile_on_) {
+        profile_.prepare_ms += now_ms() - t0;
+        profile_.n_prepare++;
+    }
+}
+
+void Executor::set_input(uint32_t tid, const void* data, size_t bytes) {
+    GB_CHECK(active_, "set_input before prepare");
+    auto it = active_->input_bufs.find(tid);
+    GB_CHECK(it != active_->input_bufs.end(), "tensor " + std::to_string(tid) + " is not a graph input");
+    const Val& v = active_->vals.at(tid);
+    const size_t need = (size_t)(nelem(v.ne) * v.nb[0]);
+    GB_CHECK(bytes == need, "set_input size mismatch for tensor " + std::to_string(tid) + ": got " +
+                                std::to_string(bytes) + " bytes, expected " + std::to_string(need));
+    GB_CUDA(cudaMemcpyAsync(it->second, data, bytes, cudaMemcpyHostToDevice, stream_));
+}
+
+void Executor::set_input_by_name(const std::string& name, const void* data, size_t bytes) {
+    for (uint32_t id : g_->inputs)
+        if (g_->t(id).name == name) return set_input(id, data, bytes);
+    GB_CHECK(false, "no graph input named '" + name + "'");
+}
+
+void Executor::run() {
+    GB_CHECK(active_, "run before prepare");
+    const double t0 = profile_on_ ? now_ms() : 0;
+    Program& p = *active_;
+    GB_CUDA(cudaMemcpyAsync(d_step_, h_step_, sizeof(StepParams), cudaMemcpyHostToDevice, stream_));
+    if (ktiming_) {
+        const size_t n = p.launches.size();
+        while (kevents_.size() < n + 1) {
+            cudaEvent_t ev;
+            GB_CUDA(cudaEventCreate(&ev));
+            kevents_.push_back(ev);
+        }
+        GB_CUDA(cudaEventRecord(kevents_[0], stream_));
+        for (size_t i = 0; i < n; ++i) {
+            p.launches[i](p, stream_);
+            GB_CUDA(cudaEventRecord(kevents_[i + 1], stream_));
+        }
+        GB_CUDA(cudaStreamSynchronize(stream_));
+        for (size_t i = 0; i < n; ++i) {
+            float ms = 0;
+            GB_CUDA(cudaEventElapsedTime(&ms, kevents_[i], kevents_[i + 1]));
+            KTime& k = ktimes_[p.launch_names[i]];
+            k.ms += ms;
+            k.n += 1;
+            k.bytes += p.launch_bytes[i];
+        }
+    } else if (cuda_graph_ && p.decode) {
+        if (!p.graph_exec) {
+            cudaGraph_t graph;
+            GB_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+            try {
+                for (auto& l : p.launches) l(p, stream_);
+            } catch (...) {
+                cudaStreamEndCapture(stream_, &graph);
+                throw;
+            }
+            GB_CUDA(cudaStreamEndCapture(stream_, &graph));
+            GB_CUDA(cudaGraphInstantiate(&p.graph_exec, graph, 0));
+            cudaGraphDestroy(graph);
+        }
+        GB_CUDA(cudaGraphLaunch(p.graph_exec, stream_));
+    } else {
+        for (auto& l : p.launches) l(p, stream_);
+    }
+    if (profile_on_) {
+        GB_CUDA(cudaStreamSynchronize(stream_));
+        profile_.run_ms += now_ms() - t0;
+        profile_.n_run++;
+    }
+}
+
+void Executor::synchronize() { GB_CUDA(cudaStreamSynchronize(stream_)); }
+
+bool Executor::cuda_graph_captured() const {
+    for (auto& [k, p] : programs_)
+        if (p->graph_exec) return true;
+    return false;
+}
+
+const void* Executor::get_output(uint32_t tid, size_t* bytes) {
+    GB_CHECK(active_, "get_output before prepare");
+    auto it = active_->vals.find(tid);
+    GB_CHECK(it != active_->vals.end(), "unknown output tensor " + std::to_string(tid));
+    const Val& v = it->second;
+    GB_CHECK(v.has_f && v.contiguous(), "output tensor is not contiguous");
+    const size_t n = (size_t)(nelem(v.ne) * v.nb[0]);
+    if (pinned_out_bytes_ < n) {
+        if (pinned_out_) cudaFreeHost(pinned_out_);
+        GB_CUDA(cudaMallocHost(&pinned_out_, n));
+        pinned_out_bytes_ = n;
+    }
+    GB_CUDA(cudaMemcpyAsync(pinned_out_, active_->ptr(v.ref), n, cudaMemcpyDeviceToHost, stream_));
+    GB_CUDA(cudaStreamSynchronize(stream_));
+    auto& host = out_host_[tid];
+    host.resize(n);
+    std::memcpy(host.data(), pinned_out_, n);
+    *bytes = n;
+    return host.data();
+}
+
+std::array<int64_t, 4> Executor::tensor_shape(uint32_t tid) const {
+    if (active_) {
+        auto it = active_->vals.find(tid);
+        if (it != active_->vals.end())
+            return {it->second.ne[0], it->second.ne[1], it->second.ne[2], it->second.ne[3]};
+    }
+    const GTensor& t = g_->t(tid);
+    SymEnv env = active_ ? active_->env : SymEnv{};
+    std::array<int64_t, 4> ne{1, 1, 1, 1};
+    for (int d = 0; d < 4; ++d) {
+        try {
+            ne[d] = t.ne[d]->eval(env);
+        } catch (...) {
+            ne[d] = t.file_ne[d];
+        }
+    }
+    return ne;
+}
+
+size_t Executor::tensor_size_bytes(uint32_t tid) const {
+    auto ne = tensor_shape(tid);
+    const GTensor& t = g_->t(tid);
+    return (size_t)(row_bytes(t.type, ne[0]) * ne[1] * ne[2] * ne[3]);
+}
+
+void Executor::set_state(uint32_t tid, const void* data, size_t bytes) {
+    auto& p = state_dev_[tid];
+    if (!p) GB_CUDA(cudaMalloc(&p, bytes));
+    GB_CUDA(cudaMemcpy(p, data, bytes, cudaMemcpyHostToDevice));
+}
+
+const void* Executor::get_state(uint32_t tid, size_t* bytes) {
+    auto it = state_dev_.find(tid);
+    GB_CHECK(it != state_dev_.end(), "no state tensor " + std::to_string(tid));
+    size_t n = tensor_size_bytes(tid);
+    auto& host = out_host_[tid];
+    host.resize(n);
+    GB_CUDA(cudaMemcpy(host.data(), it->second, n, cudaMemcpyDeviceToHost));
+    *bytes = n;
+    return host.data();
+}
+
+void Executor::reset_state() {
+    for (auto& [id, p] : state_dev_) GB_CUDA(cudaMemset(p, 0, tensor_size_bytes(id)));
+}
+
+int64_t Executor::launches_per_run() const {
+    return active_ ? (int64_t)active_->launches.size() : 0;
+}
+
+std::string Executor::graph_summary() const {
+    std::map<std::string, int> hist;
+    if (active_)
+        for (auto& n : active_->launch_names) hist[n]++;
+    std::ostringstream os;
+    os << "{\"engine\":\"ggmlc_b200\",\"launch_steps\":" << (active_ ? active_->launches.size() : 0)
+       << ",\"arena_bytes\":" << (active_ ? active_->arena_bytes : 0) << ",\"steps\":{";
+    bool first = true;
+    for (auto& [k, v] : hist) {
+        os << (first ? "" : ",") << "\"" << k << "\":" << v;
+        first = false;
+    }
+    os << "}}";
+    return os.str();
+}
+
+std::string Executor::kernel_times_json() const {
+    std::ostringstream os;
+    os.precision(9);
+    os << "{";
+    bool first = true;
+    for (auto& [k, v] : ktimes_) {
+        os << (first ? "" : ",") << "\"" << k << "\":[" << v.ms << "," << v.n << "," << v.bytes
+           << "]";
+        first = false;
+    }
+    os << "}";
+    return os.str();
+}
+
+std::string Executor::mul_mat_shape_summary() const {
+    std::map<std::string, int> hist;
+    for (auto& op : g_->ops) {
+        if (op.opcode != OP_MUL_MAT) continue;
+        const GTensor& w = g_->t(op.inputs[0]);
+        std::ostringstream k;
+        k << "type" << w.type << ":" << w.file_ne[0] << "x" << w.file_ne[1];
+        hist[k.str()]++;
+    }
+    std::ostringstream os;
+    os << "{\"mul_mat\":{";
+    bool first = true;
+    for (auto& [k, v] : hist) {
+        os << (first ? "" : ",") << "\"" << k << "\":" << v;
+        first = false;
+    }
+    os << "}}";
+    return os.str();
+}
+
+}  // namespace gb

@@ -1,0 +1,184 @@
+// ModelExecutor for the B200 engine: the CUDA replacement of runtime/src/executor.cpp behind
+// the same interface (runtime/include/ggmlc/executor.h:25-287).
+//
+// prepare(env) lowers the graph for one shape into a Program: a list of kernel launches over
+// an activation arena, with the fusions this engine applies (norm/SwiGLU/GELU emit the Q8_0
+// rows their matmul consumes; matmul epilogues add bias and the residual ADD).  Programs are
+// cached per shape; the KV position is not part of the key — kernels read it from a device
+// StepParams, so a decode Program (and its CUDA graph) is replayed for every token.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <array>
+#include <functional>
+#include <map>
+#include <memory>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "common.h"
+#include "graph.h"
+#include "kernels.h"
+
+namespace gb {
+
+struct BufRef {
+    int buf = -1;           // arena buffer id (or -1)
+    char* fixed = nullptr;  // persistent device memory (weights, KV cache, inputs)
+    int64_t off = 0;
+};
+
+struct Val {
+    BufRef ref;
+    int type = T_F32;
+    int64_t ne[4] = {1, 1, 1, 1};
+    int64_t nb[4] = {0, 0, 0, 0};
+    bool has_f = true;       // f32/f16/i32 data present at ref
+    BufRef q, qd;            // Q8_0 rows (int8 quants, fp32 scales) when materialized
+    bool has_q = false;
+    const QWeight* w = nullptr;  // quantized weight
+    bool contiguous() const;
+    int64_t nrows() const { return ne[1] * ne[2] * ne[3]; }
+    bool rows_uniform() const { return nb[2] == nb[1] * ne[1] && nb[3] == nb[2] * ne[2]; }
+};
+
+struct Program;
+using Launch = std::function<void(Program&, cudaStream_t)>;
+
+struct Program {
+    std::string key;
+    SymEnv env;
+    bool kv = false;
+    bool decode = false;
+    std::vector<int64_t> buf_size, buf_first, buf_last, buf_off;
+    char* arena = nullptr;
+    size_t arena_bytes = 0;
+    std::vector<Launch> launches;
+    std::vector<std::string> launch_names;
+    std::vector<double> launch_bytes;  // algorithmic HBM bytes of each launch (0 if untracked)
+    std::map<uint32_t, Val> vals;
+    std::map<uint32_t, char*> input_bufs;  // graph inputs (device, persistent per program)
+    std::vector<void*> owned;              // device allocations to free
+    cudaGraphExec_t graph_exec = nullptr;
+    int64_t s = 0;
+
+    char* ptr(const BufRef& r) const {
+        if (r.fixed) return r.fixed + r.off;
+        if (r.buf < 0) return nullptr;
+        return arena + buf_off[r.buf] + r.off;
+    }
+    int new_buf(int64_t bytes, int first) {
+        buf_size.push_back((bytes + 255) / 256 * 256);
+        buf_first.push_back(first);
+        buf_last.push_back(first);
+        return (int)buf_size.size() - 1;
+    }
+    void use(const BufRef& r, int op) {
+        if (!r.fixed && r.buf >= 0 && op > buf_last[r.buf]) buf_last[r.buf] = op;
+    }
+    TView view(const Val& v) const;
+};
+
+struct KVCache {
+    __half* k = nullptr;
+    __half* v = nullptr;
+    int64_t hd = 0, Hkv = 0, batch = 1, ctx = 0;
+};
+
+class Executor {
+public:
+    Executor(std::shared_ptr<Graph> g, const std::string& device);
+    ~Executor();
+
+    static std::vector<std::string> available_devices();
+    const std::string& device() const { return device_; }
+
+    void prepare(const SymEnv& env, bool arena_reuse);
+    void set_input(uint32_t tid, const void* data, size_t bytes);
+    void set_input_by_name(const std::string& name, const void* data, size_t bytes);
+    void run();
+    void synchronize();
+    const void* get_output(uint32_t tid, size_t* bytes);
+    std::array<int64_t, 4> tensor_shape(uint32_t tid) const;
+    size_t tensor_size_bytes(uint32_t tid) const;
+
+    // persistent STATE tensors (executor.cpp:3063-3136); kept on the device
+    void set_state(uint32_t tid, const void* data, size_t bytes);
+    const void* get_state(uint32_t tid, size_t* bytes);
+    void reset_state();
+
+    void init_kv_cache(int64_t max_ctx);
+    void reset_kv_cache();
+    bool has_kv_cache() const { return kv_enabled_; }
+    int64_t kv_max_ctx() const { return kv_max_ctx_; }
+
+    void set_logits_last_only(bool on) { logits_last_only_ = on; }
+    bool logits_last_only() const { return logits_last_only_; }
+    void set_enable_cuda_graph(bool on) { cuda_graph_ = on; }
+    bool cuda_graph_enabled() const { return cuda_graph_; }
+    bool cuda_graph_captured() const;
+
+    struct Profile {
+        double prepare_ms = 0, run_ms = 0;
+        int n_prepare = 0, n_run = 0;
+    };
+    void set_enable_profile(bool on) { profile_on_ = on; }
+    void reset_profile() { profile_ = Profile(); }
+    Profile profile() const { return profile_; }
+    std::string graph_summary() const;
+    std::string mul_mat_shape_summary() const;
+    // Per-launch device timing: while on, run() skips graph replay, brackets every launch with
+    // CUDA events and accumulates {name: [ms, launches, algorithmic bytes]}.
+    void set_kernel_timing(bool on) { ktiming_ = on; }
+    void reset_kernel_times() { ktimes_.clear(); }
+    std::string kernel_times_json() const;
+
+    cudaStream_t stream() const { return stream_; }
+    const Graph& graph() const { return *g_; }
+    // number of kernel launches of the active program (per run)
+    int64_t launches_per_run() const;
+    size_t weight_bytes() const { return weight_bytes_; }
+
+private:
+    void upload_weights();
+    std::shared_ptr<Program> build(const SymEnv& env, bool kv);
+    const float2* rope_table(int n_dims, float freq_base, float freq_scale, int64_t* n_pos,
+                             float* theta_scale);
+    void free_program(Program& p);
+
+    std::shared_ptr<Graph> g_;
+    std::string device_;
+    int dev_ = 0;
+    cudaStream_t stream_ = nullptr;
+    std::map<uint32_t, QWeight> qweights_;
+    std::map<uint32_t, char*> consts_;  // f32/i32/f16 params and constants on device
+    std::vector<void*> weight_allocs_;
+    size_t weight_bytes_ = 0;
+    std::map<uint32_t, KVCache> kv_;    // per FLASH_ATTN_EXT op id
+    bool kv_enabled_ = false;
+    int64_t kv_max_ctx_ = 0;
+    bool logits_last_only_ = false;
+    bool cuda_graph_ = false;
+    bool profile_on_ = false;
+    Profile profile_;
+    StepParams* h_step_ = nullptr;  // pinned
+    StepParams* d_step_ = nullptr;
+    std::map<std::string, std::shared_ptr<Program>> programs_;
+    std::shared_ptr<Program> active_;
+    std::map<uint32_t, std::vector<uint8_t>> out_host_;
+    std::map<uint32_t, char*> state_dev_;
+    std::map<std::string, std::pair<float2*, std::pair<int64_t, float>>> rope_tabs_;
+    void* pinned_out_ = nullptr;
+    size_t pinned_out_bytes_ = 0;
+    bool ktiming_ = false;
+    struct KTime {
+        double ms = 0, bytes = 0;
+        int64_t n = 0;
+    };
+    std::map<std::string, KTime> ktimes_;
+    std::vector<cudaEvent_t> kevents_;
+};
+
+}  // namespace gb

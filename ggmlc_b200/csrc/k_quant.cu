@@ -1,0 +1,102 @@
+// Quantization-side kernels: Q8_0 activation quantization, GGUF block repack, GET_ROWS.
+#include <cuda_fp16.h>
+
+#include "common.h"
+#include "kernels.h"
+#include "kutil.cuh"
+
+namespace gb {
+
+// One warp per 32-element block; lane j owns element j.  Reproduces quantize_row_q8_0 of the
+// x86 AVX2 build (ggml-cpu/arch/x86/quants.c:302-392) bit for bit: amax = max|x|,
+// d = fp16(amax / 127), id = amax ? 127 / amax : 0, q = round-half-even(x * id).
+__global__ void k_quantize_q8_0(const float* __restrict__ x, int64_t x_stride, int64_t M,
+                                int64_t K, int8_t* __restrict__ xq, float* __restrict__ xd) {
+    const int64_t nb = K / QK;
+    const int64_t blk = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+    if (blk >= M * nb) return;
+    const int lane = threadIdx.x & 31;
+    const int64_t m = blk / nb, b = blk % nb;
+    const float v = x[m * x_stride + b * QK + lane];
+    float d16, q;
+    q8_block(v, lane, d16, q);
+    xq[m * K + b * QK + lane] = (int8_t)__float2int_rn(q);
+    if (lane == 0) xd[m * nb + b] = d16;
+}
+
+void launch_quantize_q8_0(const float* x, int64_t x_stride, int64_t M, int64_t K, int8_t* xq,
+                          float* xd, cudaStream_t st) {
+    GB_CHECK(K % QK == 0, "quantize: K must be a multiple of 32");
+    const int64_t blocks = M * (K / QK);
+    if (blocks == 0) return;
+    const int warps = 8;
+    k_quantize_q8_0<<<(unsigned)((blocks + warps - 1) / warps), warps * 32, 0, st>>>(
+        x, x_stride, M, K, xq, xd);
+    GB_CUDA(cudaGetLastError());
+}
+
+// GGUF rows of 34-byte (Q8_0) / 18-byte (Q4_0) blocks -> aligned quants + fp16 scale array.
+// One thread per block; the source is 2-byte aligned, so it is read in 16-bit words.
+__global__ void k_repack(const uint8_t* __restrict__ src, int type, int64_t nblocks,
+                         uint8_t* __restrict__ qs, __half* __restrict__ d) {
+    const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= nblocks) return;
+    const int bb = type == T_Q8_0 ? 34 : 18;
+    const int nq = bb - 2;
+    const uint16_t* s = (const uint16_t*)(src + b * bb);
+    d[b] = __ushort_as_half(s[0]);
+    uint16_t* o = (uint16_t*)(qs + b * nq);
+    for (int j = 0; j < nq / 2; ++j) o[j] = s[1 + j];
+}
+
+void launch_repack_blocks(const uint8_t* gguf, int type, int64_t N, int64_t K, void* qs,
+                          __half* d, cudaStream_t st) {
+    GB_CHECK(type == T_Q8_0 || type == T_Q4_0, "repack: not a block type");
+    const int64_t nblocks = N * (K / QK);
+    if (!nblocks) return;
+    k_repack<<<(unsigned)((nblocks + 255) / 256), 256, 0, st>>>(gguf, type, nblocks,
+                                                                 (uint8_t*)qs, d);
+    GB_CUDA(cudaGetLastError());
+}
+
+// GET_ROWS with dequantization: y = q * d (one rounded fp32 product, as dequantize_row_q8_0 /
+// _q4_0 in ggml-quants.c:459-477, :553-567).
+__global__ void k_get_rows(QWeight w, const int32_t* __restrict__ ids, int64_t n,
+                           float* __restrict__ out, int64_t out_stride) {
+    const int64_t r = blockIdx.y;
+    if (r >= n) return;
+    const int64_t K = w.K;
+    int64_t row = ids[r];
+    const bool ok = row >= 0 && row < w.N;
+    for (int64_t k = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; k < K;
+         k += (int64_t)gridDim.x * blockDim.x) {
+        float v = 0.0f;
+        if (ok) {
+            if (w.type == T_Q8_0) {
+                const int8_t* q = (const int8_t*)w.qs + row * K;
+                v = __fmul_rn((float)q[k], __half2float(w.d[row * (K / QK) + k / QK]));
+            } else if (w.type == T_Q4_0) {
+                const uint8_t* q = (const uint8_t*)w.qs + row * (K / 2);
+                const int64_t b = k / QK, j = k % QK;
+                const uint8_t byte = q[b * 16 + (j & 15)];
+                const int nib = j < 16 ? (byte & 0x0F) : (byte >> 4);
+                v = __fmul_rn((float)(nib - 8), __half2float(w.d[row * (K / QK) + b]));
+            } else if (w.type == T_F16) {
+                v = __half2float(((const __half*)w.qs)[row * K + k]);
+            } else {
+                v = ((const float*)w.qs)[row * K + k];
+            }
+        }
+        out[r * out_stride + k] = v;
+    }
+}
+
+void launch_get_rows(const QWeight& w, const int32_t* ids, int64_t n, float* out,
+                     int64_t out_stride, cudaStream_t st) {
+    if (!n) return;
+    dim3 grid((unsigned)((w.K + 255) / 256), (unsigned)n);
+    k_get_rows<<<grid, 256, 0, st>>>(w, ids, n, out, out_stride);
+    GB_CUDA(cudaGetLastError());
+}
+
+}  // namespace gb

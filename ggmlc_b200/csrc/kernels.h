@@ -1,0 +1,118 @@
+// Host-side declarations of the engine's CUDA kernels (launchers).  Every launcher takes the
+// stream explicitly; none allocates memory.  Layout conventions (all device memory):
+//   quantized weight  W[N][K]: qs = N rows of K int8 (Q8_0) or K/2 packed nibbles (Q4_0, GGUF
+//                     order inside each 16-byte block), d = N rows of K/32 fp16 block scales;
+//   Q8_0 activations  X[M][K]: xq = M rows of K int8, xd = M rows of K/32 fp32 scales (the fp16
+//                     scale widened, exactly as the CPU reads it).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace gb {
+
+// Per-step values read by kernels inside captured graphs (decode replays change only these).
+struct StepParams {
+    int64_t pos;  // first position of this call's tokens in the KV cache
+};
+
+struct QWeight {
+    int type = 0;               // T_Q8_0 or T_Q4_0 (or T_F32 / T_F16 for float weights)
+    int64_t N = 0, K = 0;       // rows, columns
+    const void* qs = nullptr;   // quants (or float data for T_F32 / T_F16)
+    const __half* d = nullptr;  // block scales (quantized types)
+};
+
+// ---- quantization ----------------------------------------------------------------------------
+// Q8_0 activation quantization with the x86 AVX2 CPU semantics (amax/127 -> fp16 scale,
+// q = rint(x * 127/amax)).  x rows are `x_stride` floats apart.
+void launch_quantize_q8_0(const float* x, int64_t x_stride, int64_t M, int64_t K, int8_t* xq,
+                          float* xd, cudaStream_t st);
+
+// Repack a GGUF block tensor (N rows of K elements, 34/18-byte blocks) into the SoA layout.
+void launch_repack_blocks(const uint8_t* gguf, int type, int64_t N, int64_t K, void* qs,
+                          __half* d, cudaStream_t st);
+
+// GET_ROWS: rows ids[i] of a quantized / f16 / f32 table [V][K] dequantized to f32 out[i][K].
+void launch_get_rows(const QWeight& w, const int32_t* ids, int64_t n, float* out,
+                     int64_t out_stride, cudaStream_t st);
+
+// ---- matmul -----------------------------------------------------------------------------------
+// Y[m][n] = sum_k X[m][k] W[n][k] (+ bias[n]) (+ residual[m][n]) for Q8_0/Q4_0 W and Q8_0 X.
+// Bit-exact with the reference x86 CPU kernels: 8 fp32 lane accumulators per output, lane i
+// holding the int32 dot of elements 4i..4i+3 of each block, fma(d_w*d_x, lane, acc) block by
+// block, lanes reduced ((a0+a4)+(a2+a6))+((a1+a5)+(a3+a7)).
+struct MatmulEpilogue {
+    const float* bias = nullptr;      // [N] or null
+    const float* residual = nullptr;  // [M][res_stride] or null
+    int64_t res_stride = 0;
+};
+void launch_matmul_q_exact(const QWeight& w, const int8_t* xq, const float* xd, int64_t M,
+                           float* y, int64_t y_stride, const MatmulEpilogue& ep,
+                           cudaStream_t st);
+// Float-weight matmul (F32/F16 W, f32 X), used for non-quantized linears.
+void launch_matmul_f(const QWeight& w, const float* x, int64_t x_stride, int64_t M, float* y,
+                     int64_t y_stride, const MatmulEpilogue& ep, cudaStream_t st);
+
+// ---- norms / activations --------------------------------------------------------------------
+// RMSNorm (fp32 squares summed in double, scale = 1/sqrtf(mean+eps)), optional gamma; writes f32
+// rows (y) and/or Q8_0 rows (yq, yd).
+void launch_rms_norm(const float* x, int64_t x_stride, int64_t M, int64_t D, float eps,
+                     const float* gamma, float* y, int64_t y_stride, int8_t* yq, float* yd,
+                     cudaStream_t st);
+// LayerNorm (NORM op semantics of the x86 CPU build), optional gamma / beta.
+void launch_layer_norm(const float* x, int64_t x_stride, int64_t M, int64_t D, float eps,
+                       const float* gamma, const float* beta, float* y, int64_t y_stride,
+                       int8_t* yq, float* yd, cudaStream_t st);
+// SwiGLU over rows [gate(F) ; up(F)] (x row stride x_stride) -> F outputs, f32 and/or Q8_0.
+void launch_swiglu(const float* x, int64_t x_stride, int64_t M, int64_t F, bool swapped,
+                   float* y, int64_t y_stride, int8_t* yq, float* yd, cudaStream_t st);
+// bias + tanh-GELU (fast_gelu_f32 of the reference's CPU custom op), f32 and/or Q8_0.
+void launch_bias_gelu(const float* x, int64_t x_stride, const float* bias, int64_t M, int64_t F,
+                      float* y, int64_t y_stride, int8_t* yq, float* yd, cudaStream_t st);
+
+// ---- generic strided tensors ------------------------------------------------------------------
+struct TView {
+    char* data = nullptr;
+    int type = 0;
+    int64_t ne[4] = {1, 1, 1, 1};
+    int64_t nb[4] = {0, 0, 0, 0};  // byte strides
+};
+// dst = a (op) b with ggml broadcasting of b over a; op: 0 add, 1 mul.  f32 only.
+void launch_binary(const TView& a, const TView& b, const TView& dst, int op, cudaStream_t st);
+// dst = src (any strides, f32/f16/i32 with conversion to dst type).
+void launch_copy(const TView& src, const TView& dst, cudaStream_t st);
+
+// ---- RoPE / KV cache / attention ---------------------------------------------------------------
+// NEOX RoPE.  x: f32 view [hd, H, s] (ne0 contiguous); positions = pos_src[pos_off + i] where
+// pos_off = step->pos when use_step_pos else 0.  cos/sin come from `table` (n_pos x n_dims/2
+// pairs computed on the host with the CPU's theta recurrence) when the position is inside it.
+// Output either f32 view y, or (kv != null) f16 rows into a KV cache at row step->pos + i.
+struct RopeTable {
+    const float2* cs = nullptr;  // [n_pos][n_dims/2] (cos, sin)
+    int64_t n_pos = 0;
+    int n_dims = 0;
+    float theta_scale = 1.0f;
+};
+struct KVDst {
+    __half* base = nullptr;  // [H][ctx][hd]
+    int64_t ctx = 0;         // rows per head
+};
+void launch_rope_neox(const TView& x, const int32_t* pos_src, bool use_step_pos,
+                      const StepParams* step, const RopeTable& tab, const TView* y,
+                      const KVDst* kv, cudaStream_t st);
+// Write s rows of a f32 view [hd, H, s] into a f16 KV cache at rows step->pos + i.
+void launch_kv_write(const TView& src, const StepParams* step, const KVDst& kv, cudaStream_t st);
+
+// Attention of q (f32 view [hd, s, Hq]) over KV caches [Hkv][ctx][hd] f16, causal at absolute
+// positions: query i sees cache rows 0 .. kv_base + i where kv_base = step->pos (use_step) or 0.
+// Output o: f32 [s][Hq][hd] contiguous (the FLASH_ATTN_EXT permuted result) .  Q is rounded to
+// fp16 like the CPU kernel.  work: scratch of attn_workspace_bytes().
+size_t attn_workspace_bytes(int64_t s, int64_t Hq, int64_t hd, int64_t max_kv);
+void launch_attention(const TView& q, const __half* kc, const __half* vc, int64_t ctx,
+                      int64_t Hkv, const StepParams* step, bool use_step, int64_t kv_off,
+                      float scale, float* o, void* work, int64_t max_kv, cudaStream_t st);
+
+}  // namespace gb

@@ -1,0 +1,165 @@
+/*
+ * ggmlc_b200 — C ABI of the B200 execution engine for ggmlc-compiled GGUF decoder graphs.
+ *
+ * This is the drop-in boundary that replaces the reference's nanobind module `ggmlc._runtime`
+ * (runtime/bindings/python_bindings.cpp:22-295) for the CUDA hot path.  Each entry point names
+ * the binding it replaces.  Plain C types only: opaque handles, pointers and sizes.
+ *
+ * Conventions: functions return 0 on success and -1 on error; gb_last_error() then holds the
+ * message (thread-local).  Strings returned by the library stay valid until the owning handle
+ * is freed or the same call is made again.  Host buffers passed in are only read during the
+ * call.  Device pointers (the op-level section) must be CUDA device memory of the current
+ * device; `stream` is a cudaStream_t (NULL = legacy default stream).
+ */
+#ifndef GGMLC_B200_H
+#define GGMLC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct gb_graph gb_graph;       /* ggmlc::SerializedModelGraph */
+typedef struct gb_executor gb_executor; /* ggmlc::ModelExecutor */
+
+/* Last error message of this thread ("" if none). */
+const char* gb_last_error(void);
+/* ABI version (major * 10000 + minor * 100 + patch). */
+int gb_version(void);
+
+/* get_available_devices() — python_bindings.cpp:133: "cpu", "cuda:0".., "cuda".  Writes a
+ * '\n'-separated list into buf (capacity cap); returns the needed length or -1. */
+int gb_get_available_devices(char* buf, size_t cap);
+
+/* ---- ModelLoader (python_bindings.cpp:108-130; loader.cpp:257-443) ------------------------ */
+int gb_loader_load_from_file(const char* path, gb_graph** out);
+int gb_loader_load_from_bytes(const void* data, size_t size, gb_graph** out);
+void gb_graph_free(gb_graph* g);
+
+/* SerializedModelGraph fields (python_bindings.cpp:71-106) */
+const char* gb_graph_name(const gb_graph* g);
+int gb_graph_num_symbols(const gb_graph* g);
+const char* gb_graph_symbol(const gb_graph* g, int i);
+/* which: 0 inputs, 1 outputs, 2 parameters */
+int gb_graph_num_ids(const gb_graph* g, int which);
+int gb_graph_id(const gb_graph* g, int which, int i, uint32_t* id);
+int gb_graph_num_tensors(const gb_graph* g);
+int gb_graph_tensor_id(const gb_graph* g, int i, uint32_t* id);
+/* SerializedTensor(id, name, data_size, storage, type) — python_bindings.cpp:71-92 */
+int gb_graph_tensor_info(const gb_graph* g, uint32_t id, const char** name, int* type,
+                         int* storage, uint64_t* data_size);
+/* SerializedTensor.symbol_index(axis): symbol-table index of dim `axis`, or -1 */
+int gb_graph_tensor_symbol_index(const gb_graph* g, uint32_t id, int axis);
+int gb_graph_num_ops(const gb_graph* g);
+int gb_graph_op_info(const gb_graph* g, int i, uint32_t* id, int* opcode, const char** name);
+/* metadata string (e.g. "general.name"); NULL when absent */
+const char* gb_graph_metadata_str(const gb_graph* g, const char* key);
+
+/* ---- ModelExecutor (python_bindings.cpp:136-217; executor.h:25-287) ----------------------- */
+/* device: "cuda", "cuda:N" or "auto".  "cpu" is refused: this engine has no CPU fallback. */
+int gb_executor_create(const gb_graph* g, const char* device, gb_executor** out);
+void gb_executor_free(gb_executor* e);
+const char* gb_executor_device(const gb_executor* e);
+/* prepare(symbols, enable_arena_reuse) — executor.cpp:1453 */
+int gb_executor_prepare(gb_executor* e, const char* const* names, const int64_t* values, int n,
+                        int enable_arena_reuse);
+/* set_input_by_id / set_input_by_name — executor.cpp:2928-2944 (host -> device copy) */
+int gb_executor_set_input(gb_executor* e, uint32_t tid, const void* data, size_t bytes);
+int gb_executor_set_input_by_name(gb_executor* e, const char* name, const void* data,
+                                  size_t bytes);
+/* run(n_threads) — executor.cpp:2984 (n_threads is accepted and ignored on the GPU) */
+int gb_executor_run(gb_executor* e, int n_threads);
+int gb_executor_synchronize(gb_executor* e);
+/* get_output_bytes — executor.cpp:3138-3157: device -> host copy; *data is owned by the
+ * executor and valid until the next call for the same tensor */
+int gb_executor_get_output(gb_executor* e, uint32_t tid, const void** data, size_t* bytes);
+int gb_executor_get_tensor_shape(gb_executor* e, uint32_t tid, int64_t ne[4]);
+int gb_executor_get_tensor_size_bytes(gb_executor* e, uint32_t tid, size_t* bytes);
+/* set_state_by_id / get_state_bytes / reset_state — executor.cpp:3063-3136 */
+int gb_executor_set_state(gb_executor* e, uint32_t tid, const void* data, size_t bytes);
+int gb_executor_get_state(gb_executor* e, uint32_t tid, const void** data, size_t* bytes);
+int gb_executor_reset_state(gb_executor* e);
+/* init_kv_cache / reset_kv_cache / has_kv_cache — executor.cpp:498-632 */
+int gb_executor_init_kv_cache(gb_executor* e, int64_t max_ctx);
+int gb_executor_reset_kv_cache(gb_executor* e);
+int gb_executor_has_kv_cache(const gb_executor* e);
+/* set_logits_last_only / logits_last_only — executor.cpp:2398-2410 */
+int gb_executor_set_logits_last_only(gb_executor* e, int enable);
+int gb_executor_logits_last_only(const gb_executor* e);
+/* set_enable_cuda_graph / is_cuda_graph_enabled / is_cuda_graph_captured — cuda_graph.cu */
+int gb_executor_set_enable_cuda_graph(gb_executor* e, int enable);
+int gb_executor_is_cuda_graph_enabled(const gb_executor* e);
+int gb_executor_is_cuda_graph_captured(const gb_executor* e);
+/* set_enable_profile / reset_profile / get_profile — executor.h:103-116 */
+int gb_executor_set_enable_profile(gb_executor* e, int enable);
+int gb_executor_reset_profile(gb_executor* e);
+int gb_executor_get_profile(gb_executor* e, double* prepare_ms, double* run_ms, int* n_prepare,
+                            int* n_run);
+/* runtime_graph_summary / runtime_mul_mat_shape_summary — executor.cpp:3211-3459 (JSON) */
+const char* gb_executor_graph_summary(gb_executor* e);
+const char* gb_executor_mul_mat_shape_summary(gb_executor* e);
+/* kernel launches per run() of the prepared program (engine telemetry, no reference twin) */
+int64_t gb_executor_launches_per_run(const gb_executor* e);
+/* per-launch device timing for roofline accounting (engine telemetry; the reference's nearest
+ * twin is ExecutorProfile, executor.h:103-116): while enabled, run() brackets each launch with
+ * CUDA events; gb_executor_kernel_times returns JSON {name: [ms, launches, algorithmic bytes]} */
+int gb_executor_set_kernel_timing(gb_executor* e, int enable);
+int gb_executor_reset_kernel_times(gb_executor* e);
+const char* gb_executor_kernel_times(gb_executor* e);
+/* the executor's CUDA stream (cudaStream_t), for callers that order their own work after it */
+void* gb_executor_stream(const gb_executor* e);
+
+/* ---- op-level entry points (device pointers) ------------------------------------------------
+ * The kernels behind the executor, exposed for operator tests and the operator sweep.  They
+ * replace the CUDA ops of ggml-cuda the reference dispatches on this path.  Layouts:
+ *   Q8_0/Q4_0 weight W[N][K] in GGUF block rows: `wq` int8 [N][K] (Q8_0) or packed nibbles
+ *   [N][K/2] (Q4_0, GGUF order inside each 16-byte block) and `wd` fp16 bits [N][K/32];
+ *   Q8_0 activations X[M][K]: `xq` int8 [M][K], `xd` fp32 [M][K/32]. */
+
+/* GGUF block rows (34-byte Q8_0 / 18-byte Q4_0 blocks) -> wq, wd.  gguf is device memory.
+ * Replaces the weight upload of ggml_backend_tensor_set (executor.cpp:414-429). */
+int gb_repack_blocks(const void* gguf, int type, int64_t N, int64_t K, void* wq, void* wd,
+                     void* stream);
+/* Activation quantization, quantize_row_q8_0 (ggml-cpu/arch/x86/quants.c:302-392 semantics;
+ * the ggml-cuda twin is quantize_q8_1, quantize.cu:54-99).  x rows x_stride floats apart. */
+int gb_quantize_q8_0(const float* x, int64_t x_stride, int64_t M, int64_t K, int8_t* xq,
+                     float* xd, void* stream);
+/* MUL_MAT Y[M][N] = X W^T (+bias[N]) (+residual[M][N]) — ggml_cuda_mul_mat
+ * (ggml-cuda.cu:1812-1866: mul_mat_vec_q mmvq.cu:508 for M <= 8, mul_mat_q mmq.cuh:948
+ * above).  Decode rows (M <= 8) are bit-exact with the x86 CPU kernels. */
+int gb_mul_mat_q(int type, const void* wq, const void* wd, int64_t N, int64_t K,
+                 const int8_t* xq, const float* xd, int64_t M, float* y, const float* bias,
+                 const float* residual, void* stream);
+/* GET_ROWS with dequantization — k_get_rows (getrows.cu:6, get_rows_cuda_q :160) */
+int gb_get_rows(int type, const void* wq, const void* wd, int64_t N, int64_t K,
+                const int32_t* ids, int64_t n, float* out, void* stream);
+/* RMS_NORM (+gamma), optional fused Q8_0 output — rms_norm_f32 (norm.cu:77-156) */
+int gb_rms_norm(const float* x, int64_t M, int64_t D, float eps, const float* gamma, float* y,
+                int8_t* yq, float* yd, void* stream);
+/* SWIGLU over [gate(F) ; up(F)] rows, optional fused Q8_0 output — unary.cu:263-337 */
+int gb_swiglu(const float* x, int64_t M, int64_t F, float* y, int8_t* yq, float* yd,
+              void* stream);
+/* Host helper: fill (cos, sin) pairs [n_pos][n_dims/2] exactly as the CPU RoPE cache does
+ * (ggml-cpu/ops.cpp:5910-5923: fp32 theta recurrence, libm cosf/sinf).  Returns theta_scale. */
+float gb_rope_table_fill(float* host_out, int64_t n_pos, int n_dims, float freq_base);
+/* NEOX RoPE of x[s][H][hd] (f32) at positions pos[s] -> y — rope_neox (rope.cu:116-183).
+ * table: device copy of gb_rope_table_fill output for n_pos positions, or NULL (cos/sin are
+ * then evaluated on the device). */
+int gb_rope_neox(const float* x, int64_t hd, int64_t H, int64_t s, const int32_t* pos,
+                 int n_dims, float freq_base, const void* table, int64_t n_pos, float* y,
+                 void* stream);
+/* Attention of q[s][Hq][hd] (f32) over f16 caches k, v [Hkv][ctx][hd]; query i sees cache
+ * rows 0..kv_pos+i; output o[s][Hq][hd] — flash_attn_ext_vec / _f16 (fattn-vec.cuh:21,
+ * fattn-mma-f16.cuh:1705).  work: gb_attention_workspace_bytes() of device scratch. */
+size_t gb_attention_workspace_bytes(int64_t s, int64_t Hq, int64_t hd, int64_t ctx);
+int gb_attention(const float* q, const void* k, const void* v, int64_t hd, int64_t s,
+                 int64_t Hq, int64_t Hkv, int64_t ctx, int64_t kv_pos, float scale, float* o,
+                 void* work, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GGMLC_B200_H */
