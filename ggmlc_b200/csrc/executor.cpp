@@ -532,6 +532,8 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         xl.ne[1] = 1;
                         xl.ne[2] = 1;
                         xl.ne[3] = 1;
+                        xl.nb[2] = xl.nb[1];
+                        xl.nb[3] = xl.nb[1];
                         xl.has_q = false;
                         ensure_q(xl, oi);
                         const BufRef qb = xl.q, qdb = xl.qd;

@@ -116,8 +116,9 @@ def test_get_rows_bit_exact(G, wtype):
     w = G.random_blocks(rng, wtype, V, K)
     wq, wd = G.upload_weight(wtype, w, V, K)
     ids = rng.integers(0, V, 37).astype(np.int32)
+    ids_d = G.dev(ids)
     out = torch.empty((37, K), dtype=torch.float32, device="cuda")
-    G.check(G.lib().gb_get_rows(wtype, G.ptr(wq), G.ptr(wd), V, K, G.ptr(G.dev(ids)), 37,
+    G.check(G.lib().gb_get_rows(wtype, G.ptr(wq), G.ptr(wd), V, K, G.ptr(ids_d), 37,
                                 G.ptr(out), None))
     ref = np.empty((37, K), np.float32)
     O.lib().oracle_get_rows(wtype, O._p(np.ascontiguousarray(w)), K, O._p(ids), 37, O._p(ref))
@@ -136,7 +137,8 @@ def test_rms_norm_bit_exact(G, D):
         yq = torch.empty((M, D), dtype=torch.int8, device="cuda")
         yd = torch.empty((M, D // 32), dtype=torch.float32, device="cuda")
         gd = None if gamma is None else G.dev(gamma)
-        G.check(G.lib().gb_rms_norm(G.ptr(G.dev(x)), M, D, 1e-5, G.ptr(gd), G.ptr(y), G.ptr(yq),
+        xd_ = G.dev(x)
+        G.check(G.lib().gb_rms_norm(G.ptr(xd_), M, D, 1e-5, G.ptr(gd), G.ptr(y), G.ptr(yq),
                                     G.ptr(yd), None))
         ref = O.rms_norm(x, 1e-5, gamma)
         assert np.array_equal(y.cpu().numpy(), ref)
@@ -152,7 +154,8 @@ def test_swiglu_bit_exact(G, F):
     x = (rng.standard_normal((M, 2 * F)) * 4).astype(np.float32)
     x[0, :8] = [-120.0, -90.0, 88.0, 100.0, -1e-8, 0.0, 30.0, -30.0]  # exp special paths
     y = torch.empty((M, F), dtype=torch.float32, device="cuda")
-    G.check(G.lib().gb_swiglu(G.ptr(G.dev(x)), M, F, G.ptr(y), None, None, None))
+    x_d = G.dev(x)
+    G.check(G.lib().gb_swiglu(G.ptr(x_d), M, F, G.ptr(y), None, None, None))
     assert np.array_equal(y.cpu().numpy(), O.swiglu(x))
 
 
@@ -167,8 +170,9 @@ def test_rope_bit_exact(G, base):
     tab = np.empty((n_pos, hd // 2, 2), np.float32)
     G.lib().gb_rope_table_fill(tab.ctypes.data, n_pos, hd, base)
     y = torch.empty((s, H, hd), dtype=torch.float32, device="cuda")
-    G.check(G.lib().gb_rope_neox(G.ptr(G.dev(x)), hd, H, s, G.ptr(G.dev(pos)), hd, base,
-                                 G.ptr(G.dev(tab)), n_pos, G.ptr(y), None))
+    x_d, pos_d, tab_d = G.dev(x), G.dev(pos), G.dev(tab)  # keep device buffers alive
+    G.check(G.lib().gb_rope_neox(G.ptr(x_d), hd, H, s, G.ptr(pos_d), hd, base, G.ptr(tab_d),
+                                 n_pos, G.ptr(y), None))
     ref = O.rope_neox(x, pos, hd, np.float32(base))
     assert np.array_equal(y.cpu().numpy(), ref)
 
@@ -186,8 +190,8 @@ def test_attention_close(G, s, kv_pos, Hq, Hkv, hd):
     wb = G.lib().gb_attention_workspace_bytes(s, Hq, hd, ctx)
     work = torch.empty(max(int(wb), 16), dtype=torch.uint8, device="cuda")
     o = torch.empty((s, Hq, hd), dtype=torch.float32, device="cuda")
-    G.check(G.lib().gb_attention(G.ptr(G.dev(q)), G.ptr(G.dev(k.view(np.uint16))),
-                                 G.ptr(G.dev(v.view(np.uint16))), hd, s, Hq, Hkv, ctx, kv_pos,
+    q_d, k_d, v_d = G.dev(q), G.dev(k.view(np.uint16)), G.dev(v.view(np.uint16))
+    G.check(G.lib().gb_attention(G.ptr(q_d), G.ptr(k_d), G.ptr(v_d), hd, s, Hq, Hkv, ctx, kv_pos,
                                  scale, G.ptr(o), G.ptr(work), None))
     n_kv = kv_pos + s
     mask = O.causal_mask_f16(kv_pos, s, n_kv)
