@@ -147,8 +147,9 @@ void Executor::upload_weights() {
             w.type = t.type;
             w.N = N;
             w.K = K;
-            const size_t qbytes = (size_t)(t.type == T_Q8_0 ? N * K : N * K / 2);
-            const size_t dbytes = (size_t)(N * (K / QK) * 2);
+            GB_CHECK(K % QK == 0, "tensor '" + t.name + "': row length is not a multiple of 32");
+            const size_t qbytes = (size_t)(N * qrow_bytes(t.type, K));
+            const size_t dbytes = (size_t)(N * nb_padded(K) * 2);
             void* qs = nullptr;
             void* dd = nullptr;
             GB_CUDA(cudaMalloc(&qs, qbytes));
@@ -411,6 +412,8 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                 pg.use(iv.q, oi);
                 pg.use(iv.qd, oi);
             }
+            if (iv.virt_rms) pg.use(iv.rms_x, oi);
+            if (iv.virt_rope) pg.use(iv.rsrc, oi);
         }
         Val o;
         o.type = T_F32;
@@ -447,6 +450,18 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                 bool nf, nq;
                 needs(out, nf, nq);
                 const int64_t D = x.ne[0], M = x.nrows();
+                const bool rms_op = op.opcode == OP_RMS_NORM_C || op.opcode == OP_RMS_NORM;
+                if (rms_op && !nf && nq && M <= 8 && gemv_fused_fits(D, (int)M)) {
+                    // decode: every consumer is a quantized GEMV that normalizes in its prologue
+                    o.has_f = false;
+                    o.virt_rms = true;
+                    o.rms_x = x.ref;
+                    o.rms_stride = x.nb[1] / 4;
+                    o.rms_eps = eps;
+                    o.rms_gamma = gamma;
+                    o.ne[0] = D;
+                    break;
+                }
                 if (nf) alloc(o, oi);
                 else o.has_f = false;
                 if (nq) {
@@ -507,6 +522,125 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                             res = ov->second;
                         }
                     }
+                }
+                // decode GEMV (M <= 8): RMSNorm prologue / SwiGLU epilogue fused into one launch
+                const bool dec = is_quant(qw->type) && !last_only && Mrun <= 8 &&
+                                 gemv_fused_fits(K, (int)Mrun);
+                GB_CHECK(!xin.virt_rms || dec, "internal: unfused RMSNorm without a decode GEMV");
+                int swi_op = -1;
+                if (dec && !bias && add_op < 0 && !outputs.count(out) && consumers[out].size() == 1) {
+                    const int ci = consumers[out][0];
+                    const GOp& c = G.ops[ci];
+                    if ((c.opcode == OP_SWIGLU || c.opcode == OP_GLU) && c.inputs.size() == 1 &&
+                        c.i("swapped", 0) == 0 && N % 64 == 0 && xin.nrows() == Mrun)
+                        swi_op = ci;
+                }
+                if (dec) {
+                    GemvArgs ga;
+                    ga.w = *qw;
+                    ga.M = (int)Mrun;
+                    BufRef xr, qb, qdb;
+                    int64_t xs = 0;
+                    const float* gamma = nullptr;
+                    float eps = 0.0f;
+                    if (xin.virt_rms) {
+                        xr = xin.rms_x;
+                        xs = xin.rms_stride;
+                        gamma = xin.rms_gamma;
+                        eps = xin.rms_eps;
+                        pg.use(xr, oi);
+                    } else {
+                        ensure_q(xin, oi);
+                        qb = xin.q;
+                        qdb = xin.qd;
+                    }
+                    const bool virt = xin.virt_rms;
+                    const double bytes = mm_bytes(qw, Mrun, add_op >= 0);
+                    if (swi_op >= 0) {
+                        const uint32_t sout = G.ops[swi_op].outputs[0];
+                        Val h;
+                        h.type = T_F32;
+                        for (int d = 0; d < 4; ++d) h.ne[d] = shape[sout][d];
+                        const int64_t F = N / 2;
+                        GB_CHECK(h.ne[0] == F, "SwiGLU output width mismatch");
+                        bool nf, nq;
+                        needs(sout, nf, nq);
+                        if (nf) alloc(h, oi);
+                        else h.has_f = false;
+                        if (nq) {
+                            h.q.buf = pg.new_buf(Mrun * F, oi);
+                            h.qd.buf = pg.new_buf(Mrun * (F / QK) * 4, oi);
+                            h.has_q = true;
+                        }
+                        const BufRef hr = h.ref, hq = h.q, hqd = h.qd;
+                        const bool hf = h.has_f, hhq = h.has_q;
+                        add("matmul_q", [=](Program& p, cudaStream_t st) {
+                            GemvArgs a = ga;
+                            if (virt) {
+                                a.xf = (const float*)p.ptr(xr);
+                                a.xf_stride = xs;
+                                a.eps = eps;
+                                a.gamma = gamma;
+                            } else {
+                                a.xq = (const int8_t*)p.ptr(qb);
+                                a.xd = (const float*)p.ptr(qdb);
+                            }
+                            a.swiglu = true;
+                            a.F = F;
+                            if (hf) {
+                                a.y = (float*)p.ptr(hr);
+                                a.y_stride = F;
+                            }
+                            if (hhq) {
+                                a.yq = (int8_t*)p.ptr(hq);
+                                a.yd = (float*)p.ptr(hqd);
+                            }
+                            launch_gemv_fused(a, st);
+                        }, bytes);
+                        vals[sout] = h;
+                        skip.insert(swi_op);
+                        vals[out] = Val();  // never materialized
+                        vals[out].has_f = false;
+                        continue;
+                    }
+                    Val y = o;
+                    const uint32_t out_id = add_op >= 0 ? G.ops[add_op].outputs[0] : out;
+                    if (add_op >= 0)
+                        for (int d = 0; d < 4; ++d) y.ne[d] = shape[out_id][d];
+                    alloc(y, oi);
+                    BufRef rref;
+                    if (add_op >= 0) {
+                        rref = res.ref;
+                        pg.use(res.ref, add_op);
+                    }
+                    const BufRef yr = y.ref;
+                    add("matmul_q", [=](Program& p, cudaStream_t st) {
+                        GemvArgs a = ga;
+                        if (virt) {
+                            a.xf = (const float*)p.ptr(xr);
+                            a.xf_stride = xs;
+                            a.eps = eps;
+                            a.gamma = gamma;
+                        } else {
+                            a.xq = (const int8_t*)p.ptr(qb);
+                            a.xd = (const float*)p.ptr(qdb);
+                        }
+                        a.y = (float*)p.ptr(yr);
+                        a.y_stride = N;
+                        a.bias = bias;
+                        if (rref.fixed || rref.buf >= 0) {
+                            a.residual = (const float*)p.ptr(rref);
+                            a.res_stride = N;
+                        }
+                        launch_gemv_fused(a, st);
+                    }, bytes);
+                    if (add_op >= 0) {
+                        vals[out_id] = y;
+                        skip.insert(add_op);
+                    } else {
+                        vals[out] = y;
+                    }
+                    continue;
                 }
                 Val y = o;
                 const uint32_t out_id = add_op >= 0 ? G.ops[add_op].outputs[0] : out;
@@ -600,7 +734,9 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                 GB_CHECK(nelem(o.ne) == nelem(x.ne), "RESHAPE: element count mismatch");
                 if (x.contiguous()) {
                     set_contig(o);
-                    if (x.has_q && x.ne[0] == o.ne[0]) {
+                    // Q8_0 rows are 32-element blocks of the contiguous data: any reshape that
+                    // keeps rows a multiple of 32 reuses them
+                    if (x.has_q && x.ne[0] % QK == 0 && o.ne[0] % QK == 0) {
                         o.has_q = true;
                         o.q = x.q;
                         o.qd = x.qd;
@@ -633,6 +769,12 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                     ax[1] = (int)op.i("axis1", 0);
                     ax[2] = (int)op.i("axis2", 2);
                     ax[3] = (int)op.i("axis3", 3);
+                }
+                if (x.virt_rope) {  // only (0,2,1,3) permutes reach here (see OP_ROPE)
+                    o = x;
+                    o.rope_perm = !x.rope_perm;
+                    for (int d = 0; d < 4; ++d) o.ne[d] = one[d];
+                    break;
                 }
                 o = x;
                 o.has_q = false;
@@ -683,10 +825,6 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                     std::swap(x.ne[1], x.ne[2]);
                     std::swap(x.nb[1], x.nb[2]);
                 }
-                Val y;
-                y.type = T_F32;
-                for (int d = 0; d < 4; ++d) y.ne[d] = x.ne[d];
-                alloc(y, oi);
                 int64_t tab_n = 0;
                 float ts = 1.0f;
                 const float2* tab = rope_table(n_dims, fb, fs, &tab_n, &ts);
@@ -695,6 +833,45 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                 rt.n_pos = tab_n;
                 rt.n_dims = n_dims;
                 rt.theta_scale = ts;
+                // Leave the rotation to the attention kernels when every consumer is a
+                // (0,2,1,3) PERMUTE feeding FLASH_ATTN_EXT as q or k, the source rows are
+                // head-contiguous and the positions are the identity arange.
+                bool virt = identity && !permuted && x.nb[0] == 4 && x.nb[1] == x.ne[0] * 4 &&
+                            x.type == T_F32 && !outputs.count(out) && !consumers[out].empty();
+                for (int ci : consumers[out]) {
+                    const GOp& c = G.ops[ci];
+                    const bool perm = c.opcode == OP_PERMUTE && c.i("axis0", 1) == 0 &&
+                                      c.i("axis1", 0) == 2 && c.i("axis2", 2) == 1 &&
+                                      c.i("axis3", 3) == 3;
+                    if (!perm || outputs.count(c.outputs[0])) {
+                        virt = false;
+                        break;
+                    }
+                    for (int cj : consumers[c.outputs[0]]) {
+                        const GOp& f = G.ops[cj];
+                        if (f.opcode != OP_FLASH_ATTN_EXT || f.inputs.size() < 2 ||
+                            (f.inputs[0] != c.outputs[0] && f.inputs[1] != c.outputs[0]))
+                            virt = false;
+                    }
+                }
+                if (virt) {
+                    o = Val();
+                    o.has_f = false;
+                    o.virt_rope = true;
+                    o.rsrc = x.ref;
+                    for (int d = 0; d < 4; ++d) {
+                        o.rsrc_ne[d] = x.ne[d];
+                        o.rsrc_nb[d] = x.nb[d];
+                        o.ne[d] = one[d];
+                    }
+                    o.rtab = rt;
+                    o.r_use_step = use_step;
+                    break;
+                }
+                Val y;
+                y.type = T_F32;
+                for (int d = 0; d < 4; ++d) y.ne[d] = x.ne[d];
+                alloc(y, oi);
                 const Val xs = x, ys = y;
                 const BufRef pr = pv.ref;
                 const bool ident = identity;
@@ -750,8 +927,197 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                 };
                 GB_CHECK(k.ne[1] == s && v.ne[1] == s && v.ne[2] == Hkv,
                          "FLASH_ATTN_EXT: K/V rows must match the query rows");
-                const Val ks = heads_then_rows(k), vs = heads_then_rows(v), qs = q;
+                // with the KV cache the reference always applies the causal window mask
+                // (executor.cpp:2143-2157); without it only is_causal graphs are served
+                GB_CHECK(use_cache || causal || s == 1,
+                         "non-causal FLASH_ATTN_EXT over several query rows is not supported");
                 const StepParams* dstep = use_cache ? d_step_ : nullptr;
+                // ---- fused path: q, k, v are heads of one projection row buffer ----------------
+                struct Src {
+                    BufRef ref;
+                    int64_t head_nb = 0, row_nb = 0;
+                    bool rot = false;
+                    bool ok = false;
+                };
+                auto src_of = [&](const Val& t) {
+                    Src r;
+                    if (t.virt_rope) {
+                        r.ok = t.rope_perm && t.rsrc_nb[0] == 4;
+                        r.ref = t.rsrc;
+                        r.head_nb = t.rsrc_nb[1];
+                        r.row_nb = t.rsrc_nb[2];
+                        r.rot = true;
+                    } else {
+                        r.ok = t.has_f && t.type == T_F32 && t.nb[0] == 4;
+                        r.ref = t.ref;
+                        r.head_nb = t.nb[2];
+                        r.row_nb = t.nb[1];
+                    }
+                    return r;
+                };
+                const Src sq = src_of(q), sk = src_of(k), sv = src_of(v);
+                bool fuse = sq.ok && sk.ok && sv.ok && !sv.rot && sq.rot == sk.rot &&
+                            sq.ref.buf == sk.ref.buf && sk.ref.buf == sv.ref.buf &&
+                            sq.ref.fixed == sk.ref.fixed && sk.ref.fixed == sv.ref.fixed &&
+                            sq.head_nb == hd * 4 && sk.head_nb == hd * 4 && sv.head_nb == hd * 4 &&
+                            sq.row_nb == sk.row_nb && sk.row_nb == sv.row_nb && hd % 32 == 0;
+                if (fuse && sq.rot)
+                    fuse = q.rtab.cs == k.rtab.cs && q.rtab.n_dims == k.rtab.n_dims &&
+                           q.r_use_step == use_cache && k.r_use_step == use_cache;
+                if (fuse) {
+                    BufRef base = sq.ref;
+                    base.off = 0;
+                    const int64_t q_off = sq.ref.off / 4, k_off = sk.ref.off / 4, v_off = sv.ref.off / 4;
+                    const int64_t row_f = sq.row_nb / 4;
+                    RopeTable rt;
+                    if (sq.rot) rt = q.rtab;  // else n_dims 0: no rotation
+                    Val y;
+                    y.type = T_F32;
+                    y.ne[0] = hd;
+                    y.ne[1] = Hq;
+                    y.ne[2] = s;
+                    y.ne[3] = 1;
+                    if (use_cache && s == 1) {
+                        // which outputs the consumer chain needs (through a RESHAPE)
+                        uint32_t look = out;
+                        if (!outputs.count(out) && consumers[out].size() == 1 &&
+                            G.ops[consumers[out][0]].opcode == OP_RESHAPE && fused_t)
+                            look = G.ops[consumers[out][0]].outputs[0];
+                        bool nf, nq;
+                        needs(look, nf, nq);
+                        if (look == out) nf = true;
+                        if (nf) alloc(y, oi);
+                        else {
+                            set_contig(y);
+                            y.has_f = false;
+                        }
+                        if (nq) {
+                            y.q.buf = pg.new_buf(Hq * hd, oi);
+                            y.qd.buf = pg.new_buf(Hq * hd / QK * 4, oi);
+                            y.has_q = true;
+                        }
+                        AttnDecArgs da;
+                        da.q_off = q_off;
+                        da.k_off = k_off;
+                        da.v_off = v_off;
+                        da.Hq = (int)Hq;
+                        da.Hkv = (int)Hkv;
+                        da.hd = (int)hd;
+                        da.tab = rt;
+                        da.step = d_step_;
+                        da.kc = kc;
+                        da.vc = vc;
+                        da.ctx = ctx;
+                        da.scale = scale;
+                        da.max_kv = kv_max_ctx_;
+                        da.splits = attn_decode_splits(Hkv, kv_max_ctx_);
+                        BufRef wref;
+                        wref.buf = pg.new_buf((int64_t)attn_decode_workspace(Hq, hd, da.splits), oi);
+                        const BufRef yr = y.ref, yq = y.q, yqd = y.qd;
+                        const bool hf = y.has_f, hq = y.has_q;
+                        const double kvb = (double)Hkv * hd * 2 * 2;  // K+V bytes per position
+                        add("attention", [=](Program& p, cudaStream_t st) {
+                            AttnDecArgs a = da;
+                            a.qkv = (const float*)p.ptr(base);
+                            a.part = (float*)p.ptr(wref);
+                            if (hf) a.o = (float*)p.ptr(yr);
+                            if (hq) {
+                                a.oq = (int8_t*)p.ptr(yq);
+                                a.od = (float*)p.ptr(yqd);
+                            }
+                            launch_attn_decode(a, st);
+                        }, kvb);
+                        (void)row_f;
+                    } else {
+                        // RoPE + KV write in one launch, then attention over the cache
+                        Val qt;
+                        qt.type = T_F32;
+                        qt.ne[0] = hd;
+                        qt.ne[1] = Hq;
+                        qt.ne[2] = s;
+                        alloc(qt, oi);  // [s][Hq][hd]
+                        QkvRopeArgs ra;
+                        ra.qkv_stride = row_f;
+                        ra.q_off = q_off;
+                        ra.k_off = k_off;
+                        ra.v_off = v_off;
+                        ra.Hq = (int)Hq;
+                        ra.Hkv = (int)Hkv;
+                        ra.hd = (int)hd;
+                        ra.s = s;
+                        ra.tab = rt;
+                        ra.step = dstep;
+                        ra.ctx = ctx;
+                        const BufRef qtr = qt.ref;
+                        add("rope_kv", [=](Program& p, cudaStream_t st) {
+                            QkvRopeArgs a = ra;
+                            a.qkv = (const float*)p.ptr(base);
+                            a.q_out = (float*)p.ptr(qtr);
+                            a.kc = (__half*)p.ptr(kref);
+                            a.vc = (__half*)p.ptr(vref);
+                            launch_rope_qkv(a, st);
+                        });
+                        Val qv = qt;  // view [hd, s, Hq] of the [s][Hq][hd] buffer
+                        qv.ne[1] = s;
+                        qv.ne[2] = Hq;
+                        qv.nb[1] = Hq * hd * 4;
+                        qv.nb[2] = hd * 4;
+                        alloc(y, oi);
+                        const int64_t max_kv = use_cache ? kv_max_ctx_ : s;
+                        const size_t wbytes = attn_workspace_bytes(s, Hq, hd, max_kv);
+                        BufRef wref;
+                        if (wbytes) wref.buf = pg.new_buf((int64_t)wbytes, oi);
+                        const BufRef yr = y.ref;
+                        const bool step_on = use_cache;
+                        pg.use(qt.ref, oi);
+                        add("attention", [=](Program& p, cudaStream_t st) {
+                            launch_attention(p.view(qv), (const __half*)p.ptr(kref),
+                                             (const __half*)p.ptr(vref), ctx, Hkv, dstep, step_on, 0,
+                                             scale, (float*)p.ptr(yr),
+                                             wbytes ? p.ptr(wref) : nullptr, max_kv, st);
+                        });
+                    }
+                    o = y;
+                    if (!fused_t) {
+                        std::swap(o.ne[1], o.ne[2]);
+                        std::swap(o.nb[1], o.nb[2]);
+                        o.has_q = false;
+                    }
+                    for (int d = 0; d < 4; ++d)
+                        GB_CHECK(o.ne[d] == one[d], "FLASH_ATTN_EXT output shape mismatch");
+                    break;
+                }
+                // ---- generic path ----------------------------------------------------------------
+                auto materialize = [&](Val& t) {  // emit a deferred RoPE into its own buffer
+                    if (!t.virt_rope) return;
+                    Val xs;
+                    xs.ref = t.rsrc;
+                    xs.type = T_F32;
+                    for (int d = 0; d < 4; ++d) {
+                        xs.ne[d] = t.rsrc_ne[d];
+                        xs.nb[d] = t.rsrc_nb[d];
+                    }
+                    Val y;
+                    y.type = T_F32;
+                    for (int d = 0; d < 4; ++d) y.ne[d] = xs.ne[d];
+                    alloc(y, oi);
+                    const RopeTable rt = t.rtab;
+                    const bool us = t.r_use_step;
+                    const StepParams* ds = d_step_;
+                    add("rope", [=](Program& p, cudaStream_t st) {
+                        TView yv = p.view(y);
+                        launch_rope_neox(p.view(xs), nullptr, us, ds, rt, &yv, nullptr, st);
+                    });
+                    const bool perm = t.rope_perm;
+                    t = y;
+                    if (perm) {
+                        std::swap(t.ne[1], t.ne[2]);
+                        std::swap(t.nb[1], t.nb[2]);
+                    }
+                };
+                materialize(q);
+                materialize(k);
+                const Val ks = heads_then_rows(k), vs = heads_then_rows(v), qs = q;
                 add("kv_write", [=](Program& p, cudaStream_t st) {
                     KVDst kd{(__half*)p.ptr(kref), ctx};
                     KVDst vd{(__half*)p.ptr(vref), ctx};
@@ -765,7 +1131,7 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                 y.ne[2] = s;
                 y.ne[3] = 1;
                 alloc(y, oi);
-                const int64_t max_kv = use_cache ? pad_kv_len(kv_max_ctx_, kv_max_ctx_) : s;
+                const int64_t max_kv = use_cache ? kv_max_ctx_ : s;
                 const size_t wbytes = attn_workspace_bytes(s, Hq, hd, max_kv);
                 BufRef wref;
                 if (wbytes) wref.buf = pg.new_buf((int64_t)wbytes, oi);

@@ -39,6 +39,22 @@ struct Val {
     BufRef q, qd;            // Q8_0 rows (int8 quants, fp32 scales) when materialized
     bool has_q = false;
     const QWeight* w = nullptr;  // quantized weight
+    // RMSNorm output left unmaterialized: the consuming decode GEMV normalizes rms_x itself
+    bool virt_rms = false;
+    BufRef rms_x;
+    int64_t rms_stride = 0;
+    float rms_eps = 0.0f;
+    const float* rms_gamma = nullptr;
+    // RoPE output left unmaterialized: the attention lowering rotates q/k inside its kernels.
+    // rsrc_* describe the un-rotated [hd, H, s] source view; rope_perm tracks a (0,2,1,3)
+    // permute applied after the rotation.
+    bool virt_rope = false;
+    bool rope_perm = false;
+    BufRef rsrc;
+    int64_t rsrc_ne[4] = {1, 1, 1, 1};
+    int64_t rsrc_nb[4] = {0, 0, 0, 0};
+    RopeTable rtab;
+    bool r_use_step = false;
     bool contiguous() const;
     int64_t nrows() const { return ne[1] * ne[2] * ne[3]; }
     bool rows_uniform() const { return nb[2] == nb[1] * ne[1] && nb[3] == nb[2] * ne[2]; }

@@ -1,17 +1,11 @@
-// Quantized MUL_MAT kernels.
+// Quantized MUL_MAT kernels over the group weight layout (kernels.h).
 //
-// gemv_exact (M <= 8, the decode path): one 8-lane group per output row.  Lane i owns fp32
-// accumulator i and, block after block, adds fma(d_w*d_x, dp4a(w[4i..4i+3], x[4i..4i+3]), acc).
-// That is the exact arithmetic order of the reference's x86 kernels (ggml_vec_dot_q{8,4}_0_q8_0,
-// arch/x86/quants.c:1308-1342 and :701, and llamafile tinyBLAS_Q0_AVX sgemm.cpp:1353), so the
-// fp32 outputs are bit-identical to the CPU's for identical inputs.  Weight quants stream from
-// HBM as 32-bit words (a 32-byte Q8_0 block / 16-byte Q4_0 block per 8 lanes), the Q8_0
-// activations sit in shared memory.
+// M <= 8 (the decode path) goes to the bit-exact GEMV in k_gemv.cu.
 //
-// gemm_block (M > 8, prefill): int8 tensor-core tiles (mma m16n8k32, one instruction per 32-K
-// block) give the exact int32 block dot; the per-block scale product d_w*d_x is applied in fp32
-// right after each block.  Integer block sums are exact, the fp32 summation order differs from
-// the CPU's lane order.
+// gemm_block (M > 8, prefill): int8 tensor-core tiles (mma m16n8k32, one instruction per
+// 32-K block) give the exact int32 block dot; the block scale product is applied in fp32 right
+// after each block.  Integer block sums are exact; the fp32 summation order differs from the
+// CPU's lane order (within 1e-5 relative in tests/test_ops_gpu.py).
 #include <cuda_fp16.h>
 
 #include "common.h"
@@ -22,81 +16,9 @@ namespace gb {
 
 namespace {
 
-__device__ __forceinline__ int load_w_word(const uint8_t* __restrict__ row, int wtype, int64_t b,
-                                           int i) {
-    if (wtype == T_Q8_0) {
-        return __ldg((const int*)(row + b * 32 + 4 * i));
-    }
-    const unsigned w = (unsigned)__ldg((const int*)(row + b * 16 + 4 * (i & 3)));
-    const unsigned v = (w >> (4 * (i >> 2))) & 0x0F0F0F0Fu;
-    return (int)__vsub4(v, 0x08080808u);
-}
-
-template <int WT, int MAXM>
-__global__ void __launch_bounds__(128) k_gemv_exact(const uint8_t* __restrict__ qs,
-                                                    const __half* __restrict__ dw,
-                                                    int64_t N, int64_t K,
-                                                    const int8_t* __restrict__ xq,
-                                                    const float* __restrict__ xd, int M,
-                                                    float* __restrict__ y, int64_t y_stride,
-                                                    MatmulEpilogue ep) {
-    extern __shared__ __align__(16) uint8_t smem[];
-    const int64_t nb = K / QK;
-    int8_t* sx = (int8_t*)smem;
-    float* sxd = (float*)(smem + (size_t)MAXM * K);
-    // stage Q8_0 activations (M rows) in shared memory
-    {
-        const int64_t nw = (int64_t)M * K / 4;
-        for (int64_t t = threadIdx.x; t < nw; t += blockDim.x)
-            ((int*)sx)[t] = ((const int*)xq)[t];
-        for (int64_t t = threadIdx.x; t < (int64_t)M * nb; t += blockDim.x) sxd[t] = xd[t];
-    }
-    __syncthreads();
-    const int lane = threadIdx.x & 31;
-    const int i = lane & 7;
-    const int grp = lane >> 3;
-    const int warps = blockDim.x / 32;
-    const int64_t row_bytes = WT == T_Q8_0 ? K : K / 2;
-    const unsigned gmask = 0xFFu << (grp * 8);
-    for (int64_t base = ((int64_t)blockIdx.x * warps + threadIdx.x / 32) * 4; base < N;
-         base += (int64_t)gridDim.x * warps * 4) {
-        const int64_t n = base + grp;
-        const bool valid = n < N;
-        const int64_t nr = valid ? n : N - 1;
-        const uint8_t* wrow = qs + nr * row_bytes;
-        const __half* drow = dw + nr * nb;
-        float acc[MAXM];
-#pragma unroll
-        for (int m = 0; m < MAXM; ++m) acc[m] = 0.0f;
-#pragma unroll 4
-        for (int64_t b = 0; b < nb; ++b) {
-            const int wv = load_w_word(wrow, WT, b, i);
-            const float dwb = __half2float(drow[b]);
-#pragma unroll
-            for (int m = 0; m < MAXM; ++m) {
-                if (m < M) {
-                    const int xv = *(const int*)(sx + (int64_t)m * K + b * 32 + 4 * i);
-                    const int p = __dp4a(wv, xv, 0);
-                    const float s = __fmul_rn(dwb, sxd[(int64_t)m * nb + b]);
-                    acc[m] = __fmaf_rn(s, (float)p, acc[m]);
-                }
-            }
-        }
-#pragma unroll
-        for (int m = 0; m < MAXM; ++m) {
-            if (m < M) {
-                // ((a0+a4)+(a2+a6)) + ((a1+a5)+(a3+a7))  (hsum_float_8)
-                float t = __fadd_rn(acc[m], __shfl_down_sync(gmask, acc[m], 4, 8));
-                float u = __fadd_rn(t, __shfl_down_sync(gmask, t, 2, 8));
-                float r = __fadd_rn(u, __shfl_down_sync(gmask, u, 1, 8));
-                if (i == 0 && valid) {
-                    if (ep.bias) r = __fadd_rn(r, ep.bias[n]);
-                    if (ep.residual) r = __fadd_rn(ep.residual[(int64_t)m * ep.res_stride + n], r);
-                    y[(int64_t)m * y_stride + n] = r;
-                }
-            }
-        }
-    }
+// exact int -> float for |p| < 2^22 with one integer add and one fp32 add
+__device__ __forceinline__ float i2f_exact(int p) {
+    return __fsub_rn(__int_as_float(0x4B400000 + p), 12582912.0f);
 }
 
 // ---- block GEMM on int8 tensor cores (prefill) ----------------------------------------------
@@ -121,8 +43,8 @@ __global__ void __launch_bounds__(128) k_gemm_block(const uint8_t* __restrict__ 
     const int g = lane >> 2, tg = lane & 3;
     const int64_t m0 = (int64_t)blockIdx.y * 64 + (warp >> 1) * 32;
     const int64_t n0 = (int64_t)blockIdx.x * 64 + (warp & 1) * 32;
-    const int64_t nb = K / QK;
-    const int64_t wrow_bytes = WT == T_Q8_0 ? K : K / 2;
+    const int64_t nb = K / QK, nbp = nb_padded(K);
+    const int64_t wrow_bytes = qrow_bytes(WT, K);
     float acc[2][4][4];
 #pragma unroll
     for (int a = 0; a < 2; ++a)
@@ -130,7 +52,6 @@ __global__ void __launch_bounds__(128) k_gemm_block(const uint8_t* __restrict__ 
         for (int b = 0; b < 4; ++b)
 #pragma unroll
             for (int c = 0; c < 4; ++c) acc[a][b][c] = 0.0f;
-    // clamp rows for loads; stores are masked
     int64_t arow[2][2];
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt) {
@@ -158,18 +79,18 @@ __global__ void __launch_bounds__(128) k_gemm_block(const uint8_t* __restrict__ 
         for (int nt = 0; nt < 4; ++nt) {
             const uint8_t* wr = qs + brow[nt] * wrow_bytes;
             if (WT == T_Q8_0) {
-                bf[nt][0] = __ldg((const int*)(wr + kb * 32 + 4 * tg));
-                bf[nt][1] = __ldg((const int*)(wr + kb * 32 + 16 + 4 * tg));
+                const uint2 v = __ldg((const uint2*)(wr + q8_word_off(kb, tg)));
+                bf[nt][0] = (int)v.x;  // word tg: k = 4tg..4tg+3
+                bf[nt][1] = (int)v.y;  // word tg+4: k = 16+4tg..
             } else {
-                const unsigned w = (unsigned)__ldg((const int*)(wr + kb * 16 + 4 * tg));
+                const unsigned w = (unsigned)__ldg((const int*)(wr + q4_word_off(kb, tg)));
                 bf[nt][0] = (int)__vsub4(w & 0x0F0F0F0Fu, 0x08080808u);
                 bf[nt][1] = (int)__vsub4((w >> 4) & 0x0F0F0F0Fu, 0x08080808u);
             }
-            // scales of the two output columns this thread holds (n = n0+nt*8+2tg, +1)
             const int64_t c0 = min(n0 + nt * 8 + 2 * tg, N - 1);
             const int64_t c1 = min(n0 + nt * 8 + 2 * tg + 1, N - 1);
-            dwv[nt][0] = __half2float(dw[c0 * nb + kb]);
-            dwv[nt][1] = __half2float(dw[c1 * nb + kb]);
+            dwv[nt][0] = __half2float(dw[c0 * nbp + kb]);
+            dwv[nt][1] = __half2float(dw[c1 * nbp + kb]);
         }
         float dxv[2][2];
 #pragma unroll
@@ -183,10 +104,10 @@ __global__ void __launch_bounds__(128) k_gemm_block(const uint8_t* __restrict__ 
             for (int nt = 0; nt < 4; ++nt) {
                 int c[4] = {0, 0, 0, 0};
                 mma_s8(c, af[mt], bf[nt]);
-                acc[mt][nt][0] = __fmaf_rn(__fmul_rn(dwv[nt][0], dxv[mt][0]), (float)c[0], acc[mt][nt][0]);
-                acc[mt][nt][1] = __fmaf_rn(__fmul_rn(dwv[nt][1], dxv[mt][0]), (float)c[1], acc[mt][nt][1]);
-                acc[mt][nt][2] = __fmaf_rn(__fmul_rn(dwv[nt][0], dxv[mt][1]), (float)c[2], acc[mt][nt][2]);
-                acc[mt][nt][3] = __fmaf_rn(__fmul_rn(dwv[nt][1], dxv[mt][1]), (float)c[3], acc[mt][nt][3]);
+                acc[mt][nt][0] = __fmaf_rn(__fmul_rn(dwv[nt][0], dxv[mt][0]), i2f_exact(c[0]), acc[mt][nt][0]);
+                acc[mt][nt][1] = __fmaf_rn(__fmul_rn(dwv[nt][1], dxv[mt][0]), i2f_exact(c[1]), acc[mt][nt][1]);
+                acc[mt][nt][2] = __fmaf_rn(__fmul_rn(dwv[nt][0], dxv[mt][1]), i2f_exact(c[2]), acc[mt][nt][2]);
+                acc[mt][nt][3] = __fmaf_rn(__fmul_rn(dwv[nt][1], dxv[mt][1]), i2f_exact(c[3]), acc[mt][nt][3]);
             }
     }
 #pragma unroll
@@ -227,26 +148,6 @@ __global__ void k_matmul_f(QWeight w, const float* __restrict__ x, int64_t x_str
     }
 }
 
-template <int WT, int MAXM>
-void gemv_launch(const QWeight& w, const int8_t* xq, const float* xd, int64_t M, float* y,
-                 int64_t y_stride, const MatmulEpilogue& ep, cudaStream_t st) {
-    const size_t smem = (size_t)MAXM * w.K + (size_t)MAXM * (w.K / QK) * 4;
-    static bool configured = false;
-    if (!configured) {
-        GB_CUDA(cudaFuncSetAttribute(k_gemv_exact<WT, MAXM>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
-        configured = true;
-    }
-    GB_CHECK(smem <= 200 * 1024, "gemv: activation rows do not fit in shared memory");
-    const int threads = 128;
-    const int64_t tasks = (w.N + 3) / 4;  // 4 rows per warp
-    int64_t blocks = (tasks + threads / 32 - 1) / (threads / 32);
-    if (blocks > 148 * 16) blocks = 148 * 16;
-    k_gemv_exact<WT, MAXM><<<(unsigned)blocks, threads, smem, st>>>(
-        (const uint8_t*)w.qs, w.d, w.N, w.K, xq, xd, (int)M, y, y_stride, ep);
-    GB_CUDA(cudaGetLastError());
-}
-
 }  // namespace
 
 void launch_matmul_q_exact(const QWeight& w, const int8_t* xq, const float* xd, int64_t M,
@@ -254,22 +155,23 @@ void launch_matmul_q_exact(const QWeight& w, const int8_t* xq, const float* xd, 
                            cudaStream_t st) {
     GB_CHECK(w.K % QK == 0, "matmul: K must be a multiple of 32");
     if (M == 0 || w.N == 0) return;
-    if (M <= 8) {
-        const bool q8 = w.type == T_Q8_0;
-        if (M == 1) {
-            if (q8) gemv_launch<T_Q8_0, 1>(w, xq, xd, M, y, y_stride, ep, st);
-            else gemv_launch<T_Q4_0, 1>(w, xq, xd, M, y, y_stride, ep, st);
-        } else if (M <= 4) {
-            if (q8) gemv_launch<T_Q8_0, 4>(w, xq, xd, M, y, y_stride, ep, st);
-            else gemv_launch<T_Q4_0, 4>(w, xq, xd, M, y, y_stride, ep, st);
-        } else {
-            if (q8) gemv_launch<T_Q8_0, 8>(w, xq, xd, M, y, y_stride, ep, st);
-            else gemv_launch<T_Q4_0, 8>(w, xq, xd, M, y, y_stride, ep, st);
-        }
+    const bool q8 = w.type == T_Q8_0;
+    if (M <= 8 && gemv_fused_fits(w.K, (int)M)) {
+        GemvArgs a;
+        a.w = w;
+        a.M = (int)M;
+        a.xq = xq;
+        a.xd = xd;
+        a.y = y;
+        a.y_stride = y_stride;
+        a.bias = ep.bias;
+        a.residual = ep.residual;
+        a.res_stride = ep.res_stride;
+        launch_gemv_fused(a, st);
         return;
     }
     dim3 grid((unsigned)((w.N + 63) / 64), (unsigned)((M + 63) / 64));
-    if (w.type == T_Q8_0)
+    if (q8)
         k_gemm_block<T_Q8_0><<<grid, 128, 0, st>>>((const uint8_t*)w.qs, w.d, w.N, w.K, xq, xd,
                                                    M, y, y_stride, ep);
     else

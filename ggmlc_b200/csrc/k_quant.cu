@@ -35,27 +35,35 @@ void launch_quantize_q8_0(const float* x, int64_t x_stride, int64_t M, int64_t K
     GB_CUDA(cudaGetLastError());
 }
 
-// GGUF rows of 34-byte (Q8_0) / 18-byte (Q4_0) blocks -> aligned quants + fp16 scale array.
-// One thread per block; the source is 2-byte aligned, so it is read in 16-bit words.
-__global__ void k_repack(const uint8_t* __restrict__ src, int type, int64_t nblocks,
-                         uint8_t* __restrict__ qs, __half* __restrict__ d) {
-    const int64_t b = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (b >= nblocks) return;
+// GGUF rows of 34-byte (Q8_0) / 18-byte (Q4_0) blocks -> group layout (kernels.h) + fp16 scale
+// rows.  One thread per block; the source is 2-byte aligned, so it is read in 16-bit halves.
+__global__ void k_repack(const uint8_t* __restrict__ src, int type, int64_t N, int64_t nb,
+                         int64_t nbp, uint8_t* __restrict__ qs, __half* __restrict__ d) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= N * nb) return;
+    const int64_t row = i / nb, b = i % nb;
     const int bb = type == T_Q8_0 ? 34 : 18;
-    const int nq = bb - 2;
-    const uint16_t* s = (const uint16_t*)(src + b * bb);
-    d[b] = __ushort_as_half(s[0]);
-    uint16_t* o = (uint16_t*)(qs + b * nq);
-    for (int j = 0; j < nq / 2; ++j) o[j] = s[1 + j];
+    const uint16_t* s = (const uint16_t*)(src + i * bb);
+    d[row * nbp + b] = __ushort_as_half(s[0]);
+    const int nwords = type == T_Q8_0 ? 8 : 4;
+    uint8_t* rowp = qs + row * nbp * (type == T_Q8_0 ? 32 : 16);
+    for (int w = 0; w < nwords; ++w) {
+        const uint32_t v = (uint32_t)s[1 + 2 * w] | ((uint32_t)s[2 + 2 * w] << 16);
+        const int64_t off = type == T_Q8_0 ? q8_word_off(b, w) : q4_word_off(b, w);
+        *(uint32_t*)(rowp + off) = v;
+    }
 }
 
 void launch_repack_blocks(const uint8_t* gguf, int type, int64_t N, int64_t K, void* qs,
                           __half* d, cudaStream_t st) {
     GB_CHECK(type == T_Q8_0 || type == T_Q4_0, "repack: not a block type");
-    const int64_t nblocks = N * (K / QK);
-    if (!nblocks) return;
-    k_repack<<<(unsigned)((nblocks + 255) / 256), 256, 0, st>>>(gguf, type, nblocks,
-                                                                 (uint8_t*)qs, d);
+    GB_CHECK(K % QK == 0, "repack: K must be a multiple of 32");
+    const int64_t nb = K / QK, nbp = nb_padded(K);
+    if (!N || !nb) return;
+    GB_CUDA(cudaMemsetAsync(qs, 0, (size_t)(N * qrow_bytes(type, K)), st));
+    GB_CUDA(cudaMemsetAsync(d, 0, (size_t)(N * nbp * 2), st));
+    const int64_t n = N * nb;
+    k_repack<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(gguf, type, N, nb, nbp, (uint8_t*)qs, d);
     GB_CUDA(cudaGetLastError());
 }
 
@@ -72,15 +80,17 @@ __global__ void k_get_rows(QWeight w, const int32_t* __restrict__ ids, int64_t n
          k += (int64_t)gridDim.x * blockDim.x) {
         float v = 0.0f;
         if (ok) {
+            const int64_t b = k / QK, e = k % QK, nbp = nb_padded(K);
             if (w.type == T_Q8_0) {
-                const int8_t* q = (const int8_t*)w.qs + row * K;
-                v = __fmul_rn((float)q[k], __half2float(w.d[row * (K / QK) + k / QK]));
+                const uint8_t* q = (const uint8_t*)w.qs + row * qrow_bytes(T_Q8_0, K);
+                const int8_t qv = (int8_t)q[q8_word_off(b, (int)(e >> 2)) + (e & 3)];
+                v = __fmul_rn((float)qv, __half2float(w.d[row * nbp + b]));
             } else if (w.type == T_Q4_0) {
-                const uint8_t* q = (const uint8_t*)w.qs + row * (K / 2);
-                const int64_t b = k / QK, j = k % QK;
-                const uint8_t byte = q[b * 16 + (j & 15)];
-                const int nib = j < 16 ? (byte & 0x0F) : (byte >> 4);
-                v = __fmul_rn((float)(nib - 8), __half2float(w.d[row * (K / QK) + b]));
+                const uint8_t* q = (const uint8_t*)w.qs + row * qrow_bytes(T_Q4_0, K);
+                const int64_t j = e & 15;
+                const uint8_t byte = q[q4_word_off(b, (int)(j >> 2)) + (j & 3)];
+                const int nib = e < 16 ? (byte & 0x0F) : (byte >> 4);
+                v = __fmul_rn((float)(nib - 8), __half2float(w.d[row * nbp + b]));
             } else if (w.type == T_F16) {
                 v = __half2float(((const __half*)w.qs)[row * K + k]);
             } else {

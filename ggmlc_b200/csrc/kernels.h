@@ -1,9 +1,26 @@
 // Host-side declarations of the engine's CUDA kernels (launchers).  Every launcher takes the
 // stream explicitly; none allocates memory.  Layout conventions (all device memory):
-//   quantized weight  W[N][K]: qs = N rows of K int8 (Q8_0) or K/2 packed nibbles (Q4_0, GGUF
-//                     order inside each 16-byte block), d = N rows of K/32 fp16 block scales;
+//   quantized weight  W[N][K] ("group layout"): each row holds nbp = roundup(K/32, 4) blocks in
+//                     groups of 4 blocks.  A block's quants are read as 32-bit words: Q8_0 has 8
+//                     words (word w = elements 4w..4w+3), Q4_0 has 4 (word w = GGUF bytes
+//                     4w..4w+3: low nibbles elements 4w.., high nibbles elements 16+4w..).
+//                     Q8_0 group g (128 B): [t 0..3][block j 0..3][word t, word t+4];
+//                     Q4_0 group g (64 B):  [t 0..3][block j 0..3][word t].
+//                     Thread t of a row's quad therefore reads its words of 4 blocks in one or
+//                     two 16-byte loads.  d = N rows of nbp fp16 block scales (padding blocks 0).
 //   Q8_0 activations  X[M][K]: xq = M rows of K int8, xd = M rows of K/32 fp32 scales (the fp16
 //                     scale widened, exactly as the CPU reads it).
+__host__ __device__ inline int64_t nb_padded(int64_t K) { return ((K / 32) + 3) / 4 * 4; }
+// byte offset, inside a weight row, of 32-bit word w of block b
+__host__ __device__ inline int64_t q8_word_off(int64_t b, int w) {
+    return (b >> 2) * 128 + (w & 3) * 32 + (b & 3) * 8 + (w >> 2) * 4;
+}
+__host__ __device__ inline int64_t q4_word_off(int64_t b, int w) {
+    return (b >> 2) * 64 + w * 16 + (b & 3) * 4;
+}
+__host__ __device__ inline int64_t qrow_bytes(int type, int64_t K) {  // bytes of a group-layout row
+    return nb_padded(K) * (type == 8 ? 32 : 16);
+}
 #pragma once
 
 #include <cuda_fp16.h>
@@ -31,7 +48,8 @@ struct QWeight {
 void launch_quantize_q8_0(const float* x, int64_t x_stride, int64_t M, int64_t K, int8_t* xq,
                           float* xd, cudaStream_t st);
 
-// Repack a GGUF block tensor (N rows of K elements, 34/18-byte blocks) into the SoA layout.
+// Repack a GGUF block tensor (N rows of K elements, 34/18-byte blocks) into the group layout.
+// qs must hold N * qrow_bytes(type, K) bytes and d N * nb_padded(K) halves; padding is zeroed.
 void launch_repack_blocks(const uint8_t* gguf, int type, int64_t N, int64_t K, void* qs,
                           __half* d, cudaStream_t st);
 
@@ -52,6 +70,34 @@ struct MatmulEpilogue {
 void launch_matmul_q_exact(const QWeight& w, const int8_t* xq, const float* xd, int64_t M,
                            float* y, int64_t y_stride, const MatmulEpilogue& ep,
                            cudaStream_t st);
+// Decode GEMV with fused prologue / epilogue (M <= 8, bit-exact like launch_matmul_q_exact).
+//   input : Q8_0 rows (xq, xd), or f32 rows xf normalized in the prologue — RMSNorm with eps
+//           and optional gamma, exactly as launch_rms_norm — and quantized to Q8_0 in shared
+//           memory (the standalone norm and quantize launches disappear);
+//   output: f32 rows y (+bias, +residual), or SwiGLU of row pairs (gate n, up n+F) emitted as
+//           Q8_0 rows (yq, yd) and/or f32 rows (y) of length F — exactly launch_swiglu.
+struct GemvArgs {
+    QWeight w;
+    int M = 1;
+    const int8_t* xq = nullptr;  // input mode 0
+    const float* xd = nullptr;
+    const float* xf = nullptr;   // input mode 1 (RMSNorm prologue)
+    int64_t xf_stride = 0;
+    float eps = 0.0f;
+    const float* gamma = nullptr;
+    bool swiglu = false;         // output mode
+    int64_t F = 0;               // SwiGLU half width (w.N == 2F)
+    float* y = nullptr;
+    int64_t y_stride = 0;
+    const float* bias = nullptr;
+    const float* residual = nullptr;
+    int64_t res_stride = 0;
+    int8_t* yq = nullptr;
+    float* yd = nullptr;
+};
+void launch_gemv_fused(const GemvArgs& a, cudaStream_t st);
+bool gemv_fused_fits(int64_t K, int M);
+
 // Float-weight matmul (F32/F16 W, f32 X), used for non-quantized linears.
 void launch_matmul_f(const QWeight& w, const float* x, int64_t x_stride, int64_t M, float* y,
                      int64_t y_stride, const MatmulEpilogue& ep, cudaStream_t st);
@@ -105,6 +151,50 @@ void launch_rope_neox(const TView& x, const int32_t* pos_src, bool use_step_pos,
                       const KVDst* kv, cudaStream_t st);
 // Write s rows of a f32 view [hd, H, s] into a f16 KV cache at rows step->pos + i.
 void launch_kv_write(const TView& src, const StepParams* step, const KVDst& kv, cudaStream_t st);
+
+// Fused RoPE + KV write straight from the QKV projection output (rows of qkv_stride floats,
+// q/k/v heads at float offsets q_off/k_off/v_off): rotated q -> q_out [s][Hq][hd] f32, rotated k
+// and v -> cache rows base+t, base = step->pos (if step) + pos_off.  tab.n_dims == 0 disables
+// the rotation (models without RoPE).
+struct QkvRopeArgs {
+    const float* qkv = nullptr;
+    int64_t qkv_stride = 0, q_off = 0, k_off = 0, v_off = 0;
+    int Hq = 0, Hkv = 0, hd = 0;
+    int64_t s = 0;
+    RopeTable tab;
+    const StepParams* step = nullptr;
+    int64_t pos_off = 0;
+    float* q_out = nullptr;
+    __half* kc = nullptr;
+    __half* vc = nullptr;
+    int64_t ctx = 0;
+};
+void launch_rope_qkv(const QkvRopeArgs& a, cudaStream_t st);
+
+// Decode attention (one new token) fused with its RoPE and KV write: split-KV over the cache
+// (splits CTAs per KV head) and a combine that writes o (f32 [Hq][hd]) and/or the Q8_0 rows of
+// the output projection's input (oq [Hq*hd], od [Hq*hd/32]).  part: attn_decode_workspace().
+struct AttnDecArgs {
+    const float* qkv = nullptr;
+    int64_t q_off = 0, k_off = 0, v_off = 0;
+    int Hq = 0, Hkv = 0, hd = 0;
+    RopeTable tab;
+    const StepParams* step = nullptr;
+    int64_t pos_off = 0;
+    __half* kc = nullptr;
+    __half* vc = nullptr;
+    int64_t ctx = 0;
+    float scale = 1.0f;
+    int splits = 1;
+    int64_t max_kv = 0;
+    float* part = nullptr;
+    float* o = nullptr;
+    int8_t* oq = nullptr;
+    float* od = nullptr;
+};
+int attn_decode_splits(int64_t Hkv, int64_t max_kv);
+size_t attn_decode_workspace(int64_t Hq, int64_t hd, int splits);
+void launch_attn_decode(const AttnDecArgs& a, cudaStream_t st);
 
 // Attention of q (f32 view [hd, s, Hq]) over KV caches [Hkv][ctx][hd] f16, causal at absolute
 // positions: query i sees cache rows 0 .. kv_base + i where kv_base = step->pos (use_step) or 0.

@@ -114,12 +114,14 @@ void* gb_executor_stream(const gb_executor* e);
 /* ---- op-level entry points (device pointers) ------------------------------------------------
  * The kernels behind the executor, exposed for operator tests and the operator sweep.  They
  * replace the CUDA ops of ggml-cuda the reference dispatches on this path.  Layouts:
- *   Q8_0/Q4_0 weight W[N][K] in GGUF block rows: `wq` int8 [N][K] (Q8_0) or packed nibbles
- *   [N][K/2] (Q4_0, GGUF order inside each 16-byte block) and `wd` fp16 bits [N][K/32];
+ *   Q8_0/Q4_0 weight W[N][K] in the engine's group layout written by gb_repack_blocks: `wq`
+ *   N rows of nbp*32 (Q8_0) or nbp*16 (Q4_0) bytes, nbp = K/32 rounded up to a multiple of 4,
+ *   and `wd` fp16 bits [N][nbp];
  *   Q8_0 activations X[M][K]: `xq` int8 [M][K], `xd` fp32 [M][K/32]. */
 
-/* GGUF block rows (34-byte Q8_0 / 18-byte Q4_0 blocks) -> wq, wd.  gguf is device memory.
- * Replaces the weight upload of ggml_backend_tensor_set (executor.cpp:414-429). */
+/* GGUF block rows (34-byte Q8_0 / 18-byte Q4_0 blocks) -> wq, wd (group layout, padding
+ * zeroed).  gguf is device memory.  Replaces the weight upload of ggml_backend_tensor_set
+ * (executor.cpp:414-429). */
 int gb_repack_blocks(const void* gguf, int type, int64_t N, int64_t K, void* wq, void* wd,
                      void* stream);
 /* Activation quantization, quantize_row_q8_0 (ggml-cpu/arch/x86/quants.c:302-392 semantics;

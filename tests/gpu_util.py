@@ -69,8 +69,9 @@ def upload_weight(wtype: int, blocks: np.ndarray, N: int, K: int):
     """GGUF block bytes -> (wq, wd) device tensors through gb_repack_blocks."""
     torch = torch_dev()
     src = dev(blocks.reshape(-1))
-    wq = torch.empty(N * K if wtype == O.Q8_0 else N * K // 2, dtype=torch.uint8, device="cuda")
-    wd = torch.empty(N * (K // 32), dtype=torch.float16, device="cuda")
+    nbp = (K // 32 + 3) // 4 * 4  # blocks per row padded to groups of 4 (group layout)
+    wq = torch.empty(N * nbp * (32 if wtype == O.Q8_0 else 16), dtype=torch.uint8, device="cuda")
+    wd = torch.empty(N * nbp, dtype=torch.float16, device="cuda")
     check(lib().gb_repack_blocks(ptr(src), wtype, N, K, ptr(wq), ptr(wd), None))
     torch.cuda.synchronize()
     return wq, wd
