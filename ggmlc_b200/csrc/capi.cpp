@@ -254,18 +254,16 @@ void* gb_executor_stream(const gb_executor* e) { return (void*)e->e->stream(); }
 
 // ---- op level ----------------------------------------------------------------------------------
 
-int gb_repack_blocks(const void* gguf, int type, int64_t N, int64_t K, void* wq, void* wd,
-                     void* stream) {
+int gb_repack_blocks(const void* gguf, int type, int64_t N, int64_t K, void* wq, void* stream) {
     return guard([&] {
-        gb::launch_repack_blocks((const uint8_t*)gguf, type, N, K, wq, (__half*)wd,
-                                 (cudaStream_t)stream);
+        gb::launch_repack_blocks((const uint8_t*)gguf, type, N, K, wq, (cudaStream_t)stream);
     });
 }
 int gb_quantize_q8_0(const float* x, int64_t x_stride, int64_t M, int64_t K, int8_t* xq,
                      float* xd, void* stream) {
     return guard([&] { gb::launch_quantize_q8_0(x, x_stride, M, K, xq, xd, (cudaStream_t)stream); });
 }
-int gb_mul_mat_q(int type, const void* wq, const void* wd, int64_t N, int64_t K,
+int gb_mul_mat_q(int type, const void* wq, int64_t N, int64_t K,
                  const int8_t* xq, const float* xd, int64_t M, float* y, const float* bias,
                  const float* residual, void* stream) {
     return guard([&] {
@@ -275,7 +273,6 @@ int gb_mul_mat_q(int type, const void* wq, const void* wd, int64_t N, int64_t K,
         w.N = N;
         w.K = K;
         w.qs = wq;
-        w.d = (const __half*)wd;
         gb::MatmulEpilogue ep;
         ep.bias = bias;
         ep.residual = residual;
@@ -283,7 +280,73 @@ int gb_mul_mat_q(int type, const void* wq, const void* wd, int64_t N, int64_t K,
         gb::launch_matmul_q_exact(w, xq, xd, M, y, N, ep, (cudaStream_t)stream);
     });
 }
-int gb_get_rows(int type, const void* wq, const void* wd, int64_t N, int64_t K,
+int gb_gemv(int type, const void* wq, int64_t N, int64_t K, int64_t M,
+            const int8_t* xq, const float* xd, const float* xf, float eps, const float* gamma,
+            int swiglu, float* y, int8_t* yq, float* yd, const float* bias,
+            const float* residual, void* stream) {
+    return guard([&] {
+        GB_CHECK(type == gb::T_Q8_0 || type == gb::T_Q4_0, "gb_gemv: type must be Q8_0 or Q4_0");
+        gb::GemvArgs a;
+        a.w.type = type;
+        a.w.N = N;
+        a.w.K = K;
+        a.w.qs = wq;
+        a.M = (int)M;
+        a.xq = xq;
+        a.xd = xd;
+        a.xf = xf;
+        a.xf_stride = K;
+        a.eps = eps;
+        a.gamma = gamma;
+        a.swiglu = swiglu != 0;
+        a.F = N / 2;
+        a.y = y;
+        a.y_stride = swiglu ? N / 2 : N;
+        a.yq = yq;
+        a.yd = yd;
+        a.bias = bias;
+        a.residual = residual;
+        a.res_stride = N;
+        gb::launch_gemv_fused(a, (cudaStream_t)stream);
+    });
+}
+size_t gb_attn_decode_workspace_bytes(int64_t Hq, int64_t Hkv, int64_t hd, int64_t ctx) {
+    return gb::attn_decode_workspace(Hq, hd, gb::attn_decode_splits(Hkv, ctx));
+}
+int gb_attn_decode(const float* qkv, int64_t Hq, int64_t Hkv, int64_t hd, void* k, void* v,
+                   int64_t ctx, int64_t kv_pos, int n_dims, float freq_base, const void* table,
+                   int64_t n_pos, float scale, float* o, int8_t* oq, float* od, void* work,
+                   void* stream) {
+    return guard([&] {
+        GB_CHECK(kv_pos >= 0 && kv_pos < ctx, "gb_attn_decode: kv_pos outside the cache");
+        gb::AttnDecArgs a;
+        a.qkv = qkv;
+        a.q_off = 0;
+        a.k_off = Hq * hd;
+        a.v_off = (Hq + Hkv) * hd;
+        a.Hq = (int)Hq;
+        a.Hkv = (int)Hkv;
+        a.hd = (int)hd;
+        a.tab.cs = (const float2*)table;
+        a.tab.n_pos = table ? n_pos : 0;
+        a.tab.n_dims = n_dims;
+        a.tab.theta_scale = n_dims ? powf(freq_base, -2.0f / (float)n_dims) : 1.0f;
+        a.step = nullptr;
+        a.pos_off = kv_pos;
+        a.kc = (__half*)k;
+        a.vc = (__half*)v;
+        a.ctx = ctx;
+        a.scale = scale;
+        a.max_kv = ctx;
+        a.splits = gb::attn_decode_splits(Hkv, ctx);
+        a.part = (float*)work;
+        a.o = o;
+        a.oq = oq;
+        a.od = od;
+        gb::launch_attn_decode(a, (cudaStream_t)stream);
+    });
+}
+int gb_get_rows(int type, const void* wq, int64_t N, int64_t K,
                 const int32_t* ids, int64_t n, float* out, void* stream) {
     return guard([&] {
         gb::QWeight w;
@@ -291,7 +354,6 @@ int gb_get_rows(int type, const void* wq, const void* wd, int64_t N, int64_t K,
         w.N = N;
         w.K = K;
         w.qs = wq;
-        w.d = (const __half*)wd;
         gb::launch_get_rows(w, ids, n, out, K, (cudaStream_t)stream);
     });
 }

@@ -100,6 +100,7 @@ Executor::Executor(std::shared_ptr<Graph> g, const std::string& device) : g_(std
     GB_CUDA(cudaMalloc(&d_step_, sizeof(StepParams)));
     h_step_->pos = 0;
     GB_CUDA(cudaMemcpy(d_step_, h_step_, sizeof(StepParams), cudaMemcpyHostToDevice));
+    gemv_prepare_device(dev_);
     upload_weights();
 }
 
@@ -149,20 +150,15 @@ void Executor::upload_weights() {
             w.K = K;
             GB_CHECK(K % QK == 0, "tensor '" + t.name + "': row length is not a multiple of 32");
             const size_t qbytes = (size_t)(N * qrow_bytes(t.type, K));
-            const size_t dbytes = (size_t)(N * nb_padded(K) * 2);
             void* qs = nullptr;
-            void* dd = nullptr;
             GB_CUDA(cudaMalloc(&qs, qbytes));
-            GB_CUDA(cudaMalloc(&dd, dbytes));
             weight_allocs_.push_back(qs);
-            weight_allocs_.push_back(dd);
             GB_CUDA(cudaMemcpyAsync(staging, t.data, t.data_size, cudaMemcpyHostToDevice, stream_));
-            launch_repack_blocks(staging, t.type, N, K, qs, (__half*)dd, stream_);
+            launch_repack_blocks(staging, t.type, N, K, qs, stream_);
             GB_CUDA(cudaStreamSynchronize(stream_));
             w.qs = qs;
-            w.d = (const __half*)dd;
             qweights_[id] = w;
-            weight_bytes_ += qbytes + dbytes;
+            weight_bytes_ += qbytes;
         } else {
             void* p = nullptr;
             GB_CUDA(cudaMalloc(&p, t.data_size));
@@ -955,7 +951,8 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                     }
                     return r;
                 };
-                const Src sq = src_of(q), sk = src_of(k), sv = src_of(v);
+                Src sq = src_of(q), sk = src_of(k), sv = src_of(v);
+                if (s == 1) sq.row_nb = sk.row_nb = sv.row_nb = 0;  // one row: stride unused
                 bool fuse = sq.ok && sk.ok && sv.ok && !sv.rot && sq.rot == sk.rot &&
                             sq.ref.buf == sk.ref.buf && sk.ref.buf == sv.ref.buf &&
                             sq.ref.fixed == sk.ref.fixed && sk.ref.fixed == sv.ref.fixed &&
@@ -1368,7 +1365,11 @@ void Executor::run() {
     }
 }
 
-void Executor::synchronize() { GB_CUDA(cudaStreamSynchronize(stream_)); }
+void Executor::synchronize() {
+    GB_CUDA(cudaStreamSynchronize(stream_));
+    const int code = gemv_error_code(dev_);
+    GB_CHECK(code == 0, "GEMV pipeline wait timed out (code " + std::to_string(code) + ")");
+}
 
 bool Executor::cuda_graph_captured() const {
     for (auto& [k, p] : programs_)
@@ -1389,7 +1390,7 @@ const void* Executor::get_output(uint32_t tid, size_t* bytes) {
         pinned_out_bytes_ = n;
     }
     GB_CUDA(cudaMemcpyAsync(pinned_out_, active_->ptr(v.ref), n, cudaMemcpyDeviceToHost, stream_));
-    GB_CUDA(cudaStreamSynchronize(stream_));
+    synchronize();
     auto& host = out_host_[tid];
     host.resize(n);
     std::memcpy(host.data(), pinned_out_, n);

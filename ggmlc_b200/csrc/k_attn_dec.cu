@@ -5,11 +5,13 @@
 //   ROPE x2 + SET_ROWS x2, executor.cpp:2132-2184, in one launch).
 // k_attn_decode (s == 1): split-KV flash decoding.  grid = (splits, Hkv); each CTA rotates the q
 //   heads of its GQA group itself, the CTA whose range holds the new position also rotates the
-//   new k and writes k, v into the cache, then the CTA scores its positions (one warp per
-//   position, lanes across head_dim), runs the softmax over its range and accumulates V.
-//   Partials (m, l, acc) go to a workspace.
-// k_attn_combine: merges the splits of each head and writes the head's output as f32 and/or as
-//   Q8_0 blocks for the output projection (head_dim % 32 == 0, so blocks never straddle heads).
+//   new k and writes k, v into the cache, then the CTA walks its positions in chunks of 64: the
+//   chunk's K and V rows are staged in shared memory with cp.async (one memory round trip per
+//   chunk), scores come from one warp per position (lanes across head_dim), and an online
+//   softmax rescales the per-thread V accumulators.  Partials (m, l, acc) go to a workspace.
+// k_attn_combine: merges the splits of each head (all splits read in parallel) and writes the
+//   head's output as f32 and/or as Q8_0 blocks for the output projection (head_dim % 32 == 0,
+//   so blocks never straddle heads).
 //
 // RoPE arithmetic is the reference's (ops.cpp:5910-5923, 5998-6015) with the host cos/sin table;
 // attention accumulates in fp32 (the CPU rounds its V accumulator to fp16 per position).
@@ -74,17 +76,27 @@ __global__ void k_rope_qkv(QkvRopeArgs a) {
     }
 }
 
-constexpr int kDecWarps = 4;
+constexpr int kDecThreads = 128;
 constexpr int kMaxRk = 8;     // q heads per KV head handled by one CTA
-constexpr int kMaxSpan = 512; // positions per split staged in shared memory
+constexpr int kChunk = 64;    // positions staged per round trip
+constexpr int kMaxOut = kMaxRk * 256 / kDecThreads;  // V outputs per thread
 
-__global__ void __launch_bounds__(kDecWarps * 32) k_attn_decode(AttnDecArgs a) {
-    __shared__ float sq[kMaxRk * 256];          // rotated q (fp16-rounded) for the group
-    __shared__ float ss[kMaxRk * kMaxSpan];     // scores / probabilities
-    __shared__ float sred[kDecWarps * kMaxRk];
-    __shared__ float sacc[kDecWarps * kMaxRk * 256 / 4];  // reused per 64-dim slab
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                     (unsigned)__cvta_generic_to_shared(dst)),
+                 "l"(src)
+                 : "memory");
+}
+
+__global__ void __launch_bounds__(kDecThreads) k_attn_decode(AttnDecArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
     const int hd = a.hd;
     const int rk = a.Hq / a.Hkv;
+    __half* sk = (__half*)smem;                      // [kChunk][hd]
+    __half* sv = sk + kChunk * hd;                   // [kChunk][hd]
+    float* sq = (float*)(sv + kChunk * hd);          // [rk][hd] rotated q (fp16-rounded)
+    float* ss = sq + rk * hd;                        // [rk][kChunk] scores / probabilities
+    float* sstat = ss + rk * kChunk;                 // [rk][3] running max, sum, correction
     const int hk = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t pos = (a.step ? a.step->pos : 0) + a.pos_off;  // position of the new token
@@ -93,125 +105,152 @@ __global__ void __launch_bounds__(kDecWarps * 32) k_attn_decode(AttnDecArgs a) {
     const int64_t c0 = (int64_t)blockIdx.x * per;
     const int64_t c1 = min(c0 + per, nkv);
     const float* row = a.qkv;
-    // q heads of this group, rotated at pos and rounded to fp16 (q_to_vec_dot)
-    for (int e = threadIdx.x; e < rk * hd; e += blockDim.x) {
-        const int h = e / hd, d = e % hd;
-        const float* src = row + a.q_off + (int64_t)(hk * rk + h) * hd;
-        sq[h * hd + d] = __half2float(__float2half_rn(rope_elem(src, d, hd, a.tab, pos)));
-    }
-    // the split holding the new position writes its k, v rows into the cache
-    if (c0 <= pos && pos < c1) {
+    const __half* kbase = a.kc + ((int64_t)hk * a.ctx) * hd;
+    const __half* vbase = a.vc + ((int64_t)hk * a.ctx) * hd;
+    const int vec = hd / 8;  // 16-byte pieces per row
+    // the split holding the new position writes its k, v rows into the cache first
+    const bool owns_new = c0 <= pos && pos < c1;
+    if (owns_new) {
         for (int d = threadIdx.x; d < hd; d += blockDim.x) {
             const float* ks = row + a.k_off + (int64_t)hk * hd;
             a.kc[((int64_t)hk * a.ctx + pos) * hd + d] = __float2half_rn(rope_elem(ks, d, hd, a.tab, pos));
             a.vc[((int64_t)hk * a.ctx + pos) * hd + d] = __float2half_rn(row[a.v_off + (int64_t)hk * hd + d]);
         }
+        __syncthreads();  // the new row is read back below
+    }
+    // first chunk in flight while q is rotated
+    auto stage = [&](int64_t cs, int rows) {
+        for (int e = threadIdx.x; e < rows * vec * 2; e += blockDim.x) {
+            const int r = e / (vec * 2), piece = e % (vec * 2);
+            const int kv = piece >= vec;
+            const int pc = piece - kv * vec;
+            const __half* src = (kv ? vbase : kbase) + (cs + r) * hd + pc * 8;
+            __half* dst = (kv ? sv : sk) + r * hd + pc * 8;
+            cp_async16(dst, src);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    if (c0 < c1) stage(c0, (int)min((int64_t)kChunk, c1 - c0));
+    for (int e = threadIdx.x; e < rk * hd; e += blockDim.x) {
+        const int h = e / hd, d = e % hd;
+        const float* src = row + a.q_off + (int64_t)(hk * rk + h) * hd;
+        sq[h * hd + d] = __half2float(__float2half_rn(rope_elem(src, d, hd, a.tab, pos)));
+    }
+    for (int h = threadIdx.x; h < rk; h += blockDim.x) {
+        sstat[h * 3 + 0] = -INFINITY;
+        sstat[h * 3 + 1] = 0.0f;
+        sstat[h * 3 + 2] = 1.0f;
+    }
+    float acc[kMaxOut];
+#pragma unroll
+    for (int k = 0; k < kMaxOut; ++k) acc[k] = 0.0f;
+    const int per_lane = hd / 32;
+    for (int64_t cs = c0; cs < c1; cs += kChunk) {
+        const int rows = (int)min((int64_t)kChunk, c1 - cs);
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        __syncthreads();
+        // scores: one warp per position, lanes across head_dim
+        for (int r = warp; r < rows; r += kDecThreads / 32) {
+            float kv[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                if (j < per_lane) kv[j] = __half2float(sk[r * hd + lane * per_lane + j]);
+            for (int h = 0; h < rk; ++h) {
+                float dot = 0.0f;
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    if (j < per_lane) dot = __fmaf_rn(kv[j], sq[h * hd + lane * per_lane + j], dot);
+                dot = warp_sum(dot);
+                if (lane == 0) ss[h * kChunk + r] = __fmul_rn(dot, a.scale);
+            }
+        }
+        __syncthreads();
+        // online softmax statistics per head (one warp per head)
+        for (int h = warp; h < rk; h += kDecThreads / 32) {
+            float mx = -INFINITY;
+            for (int r = lane; r < rows; r += 32) mx = fmaxf(mx, ss[h * kChunk + r]);
+            mx = warp_max(mx);
+            const float mold = sstat[h * 3 + 0];
+            const float mnew = fmaxf(mold, mx);
+            float l = 0.0f;
+            for (int r = lane; r < rows; r += 32) {
+                const float p = expf(ss[h * kChunk + r] - mnew);
+                ss[h * kChunk + r] = p;
+                l += p;
+            }
+            l = warp_sum(l);
+            if (lane == 0) {
+                const float corr = expf(mold - mnew);
+                sstat[h * 3 + 0] = mnew;
+                sstat[h * 3 + 1] = sstat[h * 3 + 1] * corr + l;
+                sstat[h * 3 + 2] = corr;
+            }
+        }
+        __syncthreads();
+        // V accumulation: thread owns outputs e = tid + k*128 of the group's [rk][hd]
+#pragma unroll
+        for (int k = 0; k < kMaxOut; ++k) {
+            const int e = threadIdx.x + k * kDecThreads;
+            if (e < rk * hd) {
+                const int h = e / hd, d = e % hd;
+                float v = acc[k] * sstat[h * 3 + 2];
+                for (int r = 0; r < rows; ++r)
+                    v = __fmaf_rn(ss[h * kChunk + r], __half2float(sv[r * hd + d]), v);
+                acc[k] = v;
+            }
+        }
+        __syncthreads();  // chunk buffers are free again
+        if (cs + kChunk < c1) stage(cs + kChunk, (int)min((int64_t)kChunk, c1 - cs - kChunk));
     }
     __syncthreads();
     float* part = a.part + ((int64_t)blockIdx.x * a.Hq + (int64_t)hk * rk) * (hd + 2);
-    if (c0 >= c1) {
-        for (int e = threadIdx.x; e < rk * (hd + 2); e += blockDim.x) {
-            const int h = e / (hd + 2), k = e % (hd + 2);
-            part[h * (hd + 2) + k] = k == 0 ? -INFINITY : 0.0f;
-        }
-        return;
+    for (int h = threadIdx.x; h < rk; h += blockDim.x) {
+        part[h * (hd + 2) + 0] = c0 < c1 ? sstat[h * 3 + 0] : -INFINITY;
+        part[h * (hd + 2) + 1] = c0 < c1 ? sstat[h * 3 + 1] : 0.0f;
     }
-    const int64_t span = c1 - c0;
-    const __half* kbase = a.kc + ((int64_t)hk * a.ctx) * hd;
-    const __half* vbase = a.vc + ((int64_t)hk * a.ctx) * hd;
-    const int per_lane = hd / 32;  // 2 (hd 64) or 4 (hd 128) or 8 (hd 256)
-    // pass 1: scores, one warp per position
-    for (int64_t c = c0 + warp; c < c1; c += kDecWarps) {
-        float kv[8];
-        const __half* kr = kbase + c * hd + lane * per_lane;
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-            if (j < per_lane) kv[j] = __half2float(kr[j]);
-        for (int h = 0; h < rk; ++h) {
-            float dot = 0.0f;
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-                if (j < per_lane) dot = __fmaf_rn(kv[j], sq[h * hd + lane * per_lane + j], dot);
-            dot = warp_sum(dot);
-            if (lane == 0) ss[h * kMaxSpan + (c - c0)] = __fmul_rn(dot, a.scale);
-        }
-    }
-    __syncthreads();
-    // softmax statistics per head over this split (warp h handles head h, strided)
-    for (int h = warp; h < rk; h += kDecWarps) {
-        float mx = -INFINITY;
-        for (int64_t c = lane; c < span; c += 32) mx = fmaxf(mx, ss[h * kMaxSpan + c]);
-        mx = warp_max(mx);
-        float l = 0.0f;
-        for (int64_t c = lane; c < span; c += 32) {
-            const float p = expf(ss[h * kMaxSpan + c] - mx);
-            ss[h * kMaxSpan + c] = p;
-            l += p;
-        }
-        l = warp_sum(l);
-        if (lane == 0) {
-            part[h * (hd + 2) + 0] = mx;
-            part[h * (hd + 2) + 1] = l;
-        }
-    }
-    __syncthreads();
-    // pass 2: V accumulation, one warp per position, lanes across head_dim
-    float acc[kMaxRk][8];
-#pragma unroll
-    for (int h = 0; h < kMaxRk; ++h)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[h][j] = 0.0f;
-    for (int64_t c = c0 + warp; c < c1; c += kDecWarps) {
-        float vv[8];
-        const __half* vr = vbase + c * hd + lane * per_lane;
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-            if (j < per_lane) vv[j] = __half2float(vr[j]);
-#pragma unroll
-        for (int h = 0; h < kMaxRk; ++h) {
-            if (h < rk) {
-                const float p = ss[h * kMaxSpan + (c - c0)];
-#pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    if (j < per_lane) acc[h][j] = __fmaf_rn(p, vv[j], acc[h][j]);
-            }
-        }
-    }
-    // reduce across warps through shared memory, one head at a time
-    for (int h = 0; h < rk; ++h) {
-        __syncthreads();
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-            if (j < per_lane) sacc[warp * hd + lane * per_lane + j] = acc[h][j];
-        __syncthreads();
-        for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-            float v = 0.0f;
-            for (int w = 0; w < kDecWarps; ++w) v += sacc[w * hd + d];
-            part[h * (hd + 2) + 2 + d] = v;
-        }
+    for (int k = 0; k < kMaxOut; ++k) {
+        const int e = threadIdx.x + k * kDecThreads;
+        if (e < rk * hd) part[(e / hd) * (hd + 2) + 2 + e % hd] = acc[k];
     }
 }
 
 __global__ void k_attn_combine(AttnDecArgs a) {
+    __shared__ float sw[256];
+    __shared__ float sL;
     const int h = blockIdx.x;  // q head
     const int hd = a.hd;
     const int S = a.splits;
-    float M = -INFINITY;
-    for (int sp = 0; sp < S; ++sp) M = fmaxf(M, a.part[((int64_t)sp * a.Hq + h) * (hd + 2)]);
-    float L = 0.0f;
-    for (int sp = 0; sp < S; ++sp) {
-        const float* pr = a.part + ((int64_t)sp * a.Hq + h) * (hd + 2);
-        if (pr[0] != -INFINITY) L += pr[1] * expf(pr[0] - M);
+    const float* base = a.part + (int64_t)h * (hd + 2);
+    const int64_t sstride = (int64_t)a.Hq * (hd + 2);
+    if (threadIdx.x < 32) {
+        float M = -INFINITY;
+        for (int sp = threadIdx.x; sp < S; sp += 32) M = fmaxf(M, base[sp * sstride]);
+        M = warp_max(M);
+        float L = 0.0f;
+        for (int sp = threadIdx.x; sp < S; sp += 32) {
+            const float m = base[sp * sstride];
+            const float w = m == -INFINITY ? 0.0f : expf(m - M);
+            sw[sp] = w;
+            L += base[sp * sstride + 1] * w;
+        }
+        L = warp_sum(L);
+        if (threadIdx.x == 0) sL = L;
     }
-    const float inv = L == 0.0f ? 0.0f : 1.0f / L;
+    __syncthreads();
+    const float inv = sL == 0.0f ? 0.0f : 1.0f / sL;
     const int lane = threadIdx.x & 31;
     for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-        float v = 0.0f;
-        for (int sp = 0; sp < S; ++sp) {
-            const float* pr = a.part + ((int64_t)sp * a.Hq + h) * (hd + 2);
-            if (pr[0] != -INFINITY) v += pr[2 + d] * expf(pr[0] - M);
+        float v0 = 0.0f, v1 = 0.0f, v2 = 0.0f, v3 = 0.0f;
+        int sp = 0;
+        for (; sp + 4 <= S; sp += 4) {
+            v0 += base[(sp + 0) * sstride + 2 + d] * sw[sp + 0];
+            v1 += base[(sp + 1) * sstride + 2 + d] * sw[sp + 1];
+            v2 += base[(sp + 2) * sstride + 2 + d] * sw[sp + 2];
+            v3 += base[(sp + 3) * sstride + 2 + d] * sw[sp + 3];
         }
-        v *= inv;
+        for (; sp < S; ++sp) v0 += base[sp * sstride + 2 + d] * sw[sp];
+        const float v = ((v0 + v1) + (v2 + v3)) * inv;
         if (a.o) a.o[(int64_t)h * hd + d] = v;
         if (a.oq) {  // blockDim.x == hd: warp w owns elements 32w..32w+31 of the head
             float d16, q;
@@ -220,6 +259,10 @@ __global__ void k_attn_combine(AttnDecArgs a) {
             if (lane == 0) a.od[((int64_t)h * hd + d) / 32] = d16;
         }
     }
+}
+
+size_t dec_smem(int hd, int rk) {
+    return (size_t)kChunk * hd * 2 * 2 + (size_t)rk * hd * 4 + (size_t)rk * kChunk * 4 + rk * 12;
 }
 
 }  // namespace
@@ -235,10 +278,9 @@ void launch_rope_qkv(const QkvRopeArgs& a, cudaStream_t st) {
 }
 
 int attn_decode_splits(int64_t Hkv, int64_t max_kv) {
-    // about two CTAs per SM, and at most kMaxSpan positions per split
+    // about two CTAs per SM; each split then walks max_kv / splits positions
     int64_t s = (296 + Hkv - 1) / Hkv;
-    const int64_t need = (max_kv + kMaxSpan - 1) / kMaxSpan;
-    if (s < need) s = need;
+    if (s > max_kv) s = max_kv;
     if (s > 256) s = 256;
     return (int)(s < 1 ? 1 : s);
 }
@@ -250,10 +292,18 @@ size_t attn_decode_workspace(int64_t Hq, int64_t hd, int splits) {
 void launch_attn_decode(const AttnDecArgs& a, cudaStream_t st) {
     GB_CHECK(a.hd % 32 == 0 && a.hd <= 256, "attn_decode: head_dim must be a multiple of 32, <= 256");
     GB_CHECK(a.Hq % a.Hkv == 0 && a.Hq / a.Hkv <= kMaxRk, "attn_decode: GQA group too large");
-    GB_CHECK(a.splits >= 1 && a.splits * (int64_t)kMaxSpan >= a.max_kv,
-             "attn_decode: too few splits for the context");
+    GB_CHECK(a.splits >= 1 && a.splits <= 256, "attn_decode: bad split count");
+    const size_t smem = dec_smem(a.hd, a.Hq / a.Hkv);
+    int dev = 0;
+    GB_CUDA(cudaGetDevice(&dev));
+    static unsigned configured = 0;
+    if (!(configured & (1u << (dev & 31)))) {
+        GB_CUDA(cudaFuncSetAttribute(k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     100 * 1024));
+        configured |= 1u << (dev & 31);
+    }
     dim3 grid((unsigned)a.splits, (unsigned)a.Hkv);
-    k_attn_decode<<<grid, kDecWarps * 32, 0, st>>>(a);
+    k_attn_decode<<<grid, kDecThreads, smem, st>>>(a);
     GB_CUDA(cudaGetLastError());
     k_attn_combine<<<(unsigned)a.Hq, (unsigned)a.hd, 0, st>>>(a);
     GB_CUDA(cudaGetLastError());

@@ -34,7 +34,7 @@ __device__ __forceinline__ void mma_s8(int (&c)[4], const int (&a)[4], const int
 
 template <int WT>
 __global__ void __launch_bounds__(128) k_gemm_block(const uint8_t* __restrict__ qs,
-                                                    const __half* __restrict__ dw, int64_t N,
+                                                    int64_t N,
                                                     int64_t K, const int8_t* __restrict__ xq,
                                                     const float* __restrict__ xd, int64_t M,
                                                     float* __restrict__ y, int64_t y_stride,
@@ -43,7 +43,7 @@ __global__ void __launch_bounds__(128) k_gemm_block(const uint8_t* __restrict__ 
     const int g = lane >> 2, tg = lane & 3;
     const int64_t m0 = (int64_t)blockIdx.y * 64 + (warp >> 1) * 32;
     const int64_t n0 = (int64_t)blockIdx.x * 64 + (warp & 1) * 32;
-    const int64_t nb = K / QK, nbp = nb_padded(K);
+    const int64_t nb = K / QK;
     const int64_t wrow_bytes = qrow_bytes(WT, K);
     float acc[2][4][4];
 #pragma unroll
@@ -79,18 +79,18 @@ __global__ void __launch_bounds__(128) k_gemm_block(const uint8_t* __restrict__ 
         for (int nt = 0; nt < 4; ++nt) {
             const uint8_t* wr = qs + brow[nt] * wrow_bytes;
             if (WT == T_Q8_0) {
-                const uint2 v = __ldg((const uint2*)(wr + q8_word_off(kb, tg)));
+                const uint2 v = __ldg((const uint2*)(wr + w_word_off(T_Q8_0, kb, tg)));
                 bf[nt][0] = (int)v.x;  // word tg: k = 4tg..4tg+3
                 bf[nt][1] = (int)v.y;  // word tg+4: k = 16+4tg..
             } else {
-                const unsigned w = (unsigned)__ldg((const int*)(wr + q4_word_off(kb, tg)));
+                const unsigned w = (unsigned)__ldg((const int*)(wr + w_word_off(T_Q4_0, kb, tg)));
                 bf[nt][0] = (int)__vsub4(w & 0x0F0F0F0Fu, 0x08080808u);
                 bf[nt][1] = (int)__vsub4((w >> 4) & 0x0F0F0F0Fu, 0x08080808u);
             }
             const int64_t c0 = min(n0 + nt * 8 + 2 * tg, N - 1);
             const int64_t c1 = min(n0 + nt * 8 + 2 * tg + 1, N - 1);
-            dwv[nt][0] = __half2float(dw[c0 * nbp + kb]);
-            dwv[nt][1] = __half2float(dw[c1 * nbp + kb]);
+            dwv[nt][0] = __half2float(*(const __half*)(qs + c0 * wrow_bytes + w_scale_off(WT, kb)));
+            dwv[nt][1] = __half2float(*(const __half*)(qs + c1 * wrow_bytes + w_scale_off(WT, kb)));
         }
         float dxv[2][2];
 #pragma unroll
@@ -172,10 +172,10 @@ void launch_matmul_q_exact(const QWeight& w, const int8_t* xq, const float* xd, 
     }
     dim3 grid((unsigned)((w.N + 63) / 64), (unsigned)((M + 63) / 64));
     if (q8)
-        k_gemm_block<T_Q8_0><<<grid, 128, 0, st>>>((const uint8_t*)w.qs, w.d, w.N, w.K, xq, xd,
+        k_gemm_block<T_Q8_0><<<grid, 128, 0, st>>>((const uint8_t*)w.qs, w.N, w.K, xq, xd,
                                                    M, y, y_stride, ep);
     else
-        k_gemm_block<T_Q4_0><<<grid, 128, 0, st>>>((const uint8_t*)w.qs, w.d, w.N, w.K, xq, xd,
+        k_gemm_block<T_Q4_0><<<grid, 128, 0, st>>>((const uint8_t*)w.qs, w.N, w.K, xq, xd,
                                                    M, y, y_stride, ep);
     GB_CUDA(cudaGetLastError());
 }

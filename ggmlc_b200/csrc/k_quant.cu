@@ -35,35 +35,34 @@ void launch_quantize_q8_0(const float* x, int64_t x_stride, int64_t M, int64_t K
     GB_CUDA(cudaGetLastError());
 }
 
-// GGUF rows of 34-byte (Q8_0) / 18-byte (Q4_0) blocks -> group layout (kernels.h) + fp16 scale
-// rows.  One thread per block; the source is 2-byte aligned, so it is read in 16-bit halves.
+// GGUF rows of 34-byte (Q8_0) / 18-byte (Q4_0) blocks -> super-group layout (kernels.h).  One
+// thread per block; the source is 2-byte aligned, so it is read in 16-bit halves.
 __global__ void k_repack(const uint8_t* __restrict__ src, int type, int64_t N, int64_t nb,
-                         int64_t nbp, uint8_t* __restrict__ qs, __half* __restrict__ d) {
+                         int64_t row_bytes, uint8_t* __restrict__ qs) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= N * nb) return;
     const int64_t row = i / nb, b = i % nb;
     const int bb = type == T_Q8_0 ? 34 : 18;
     const uint16_t* s = (const uint16_t*)(src + i * bb);
-    d[row * nbp + b] = __ushort_as_half(s[0]);
+    uint8_t* rowp = qs + row * row_bytes;
+    *(uint16_t*)(rowp + w_scale_off(type, b)) = s[0];
     const int nwords = type == T_Q8_0 ? 8 : 4;
-    uint8_t* rowp = qs + row * nbp * (type == T_Q8_0 ? 32 : 16);
     for (int w = 0; w < nwords; ++w) {
         const uint32_t v = (uint32_t)s[1 + 2 * w] | ((uint32_t)s[2 + 2 * w] << 16);
-        const int64_t off = type == T_Q8_0 ? q8_word_off(b, w) : q4_word_off(b, w);
-        *(uint32_t*)(rowp + off) = v;
+        *(uint32_t*)(rowp + w_word_off(type, b, w)) = v;
     }
 }
 
 void launch_repack_blocks(const uint8_t* gguf, int type, int64_t N, int64_t K, void* qs,
-                          __half* d, cudaStream_t st) {
+                          cudaStream_t st) {
     GB_CHECK(type == T_Q8_0 || type == T_Q4_0, "repack: not a block type");
     GB_CHECK(K % QK == 0, "repack: K must be a multiple of 32");
-    const int64_t nb = K / QK, nbp = nb_padded(K);
+    const int64_t nb = K / QK;
     if (!N || !nb) return;
-    GB_CUDA(cudaMemsetAsync(qs, 0, (size_t)(N * qrow_bytes(type, K)), st));
-    GB_CUDA(cudaMemsetAsync(d, 0, (size_t)(N * nbp * 2), st));
+    const int64_t rb = qrow_bytes(type, K);
+    GB_CUDA(cudaMemsetAsync(qs, 0, (size_t)(N * rb), st));
     const int64_t n = N * nb;
-    k_repack<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(gguf, type, N, nb, nbp, (uint8_t*)qs, d);
+    k_repack<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(gguf, type, N, nb, rb, (uint8_t*)qs);
     GB_CUDA(cudaGetLastError());
 }
 
@@ -80,17 +79,19 @@ __global__ void k_get_rows(QWeight w, const int32_t* __restrict__ ids, int64_t n
          k += (int64_t)gridDim.x * blockDim.x) {
         float v = 0.0f;
         if (ok) {
-            const int64_t b = k / QK, e = k % QK, nbp = nb_padded(K);
-            if (w.type == T_Q8_0) {
-                const uint8_t* q = (const uint8_t*)w.qs + row * qrow_bytes(T_Q8_0, K);
-                const int8_t qv = (int8_t)q[q8_word_off(b, (int)(e >> 2)) + (e & 3)];
-                v = __fmul_rn((float)qv, __half2float(w.d[row * nbp + b]));
-            } else if (w.type == T_Q4_0) {
-                const uint8_t* q = (const uint8_t*)w.qs + row * qrow_bytes(T_Q4_0, K);
-                const int64_t j = e & 15;
-                const uint8_t byte = q[q4_word_off(b, (int)(j >> 2)) + (j & 3)];
-                const int nib = e < 16 ? (byte & 0x0F) : (byte >> 4);
-                v = __fmul_rn((float)(nib - 8), __half2float(w.d[row * nbp + b]));
+            const int64_t b = k / QK, e = k % QK;
+            const uint8_t* q = (const uint8_t*)w.qs + row * qrow_bytes(w.type, K);
+            if (w.type == T_Q8_0 || w.type == T_Q4_0) {
+                const float d = __half2float(*(const __half*)(q + w_scale_off(w.type, b)));
+                if (w.type == T_Q8_0) {
+                    const int8_t qv = (int8_t)q[w_word_off(T_Q8_0, b, (int)(e >> 2)) + (e & 3)];
+                    v = __fmul_rn((float)qv, d);
+                } else {
+                    const int64_t j = e & 15;
+                    const uint8_t byte = q[w_word_off(T_Q4_0, b, (int)(j >> 2)) + (j & 3)];
+                    const int nib = e < 16 ? (byte & 0x0F) : (byte >> 4);
+                    v = __fmul_rn((float)(nib - 8), d);
+                }
             } else if (w.type == T_F16) {
                 v = __half2float(((const __half*)w.qs)[row * K + k]);
             } else {

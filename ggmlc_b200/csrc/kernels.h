@@ -1,25 +1,34 @@
 // Host-side declarations of the engine's CUDA kernels (launchers).  Every launcher takes the
 // stream explicitly; none allocates memory.  Layout conventions (all device memory):
-//   quantized weight  W[N][K] ("group layout"): each row holds nbp = roundup(K/32, 4) blocks in
-//                     groups of 4 blocks.  A block's quants are read as 32-bit words: Q8_0 has 8
-//                     words (word w = elements 4w..4w+3), Q4_0 has 4 (word w = GGUF bytes
-//                     4w..4w+3: low nibbles elements 4w.., high nibbles elements 16+4w..).
-//                     Q8_0 group g (128 B): [t 0..3][block j 0..3][word t, word t+4];
-//                     Q4_0 group g (64 B):  [t 0..3][block j 0..3][word t].
-//                     Thread t of a row's quad therefore reads its words of 4 blocks in one or
-//                     two 16-byte loads.  d = N rows of nbp fp16 block scales (padding blocks 0).
+//   quantized weight  W[N][K] ("super-group layout"): a row is one contiguous stream of
+//                     super-groups (SG) of 8 blocks, each SG = the quants of two groups of 4
+//                     blocks followed by the 8 fp16 block scales (16 B): Q8_0 SG = 2x128 + 16 =
+//                     272 B, Q4_0 SG = 2x64 + 16 = 144 B.  A block's quants are read as 32-bit
+//                     words: Q8_0 has 8 (word w = elements 4w..4w+3), Q4_0 has 4 (word w = GGUF
+//                     bytes 4w..4w+3: low nibbles elements 4w.., high nibbles 16+4w..).
+//                     Q8_0 group (128 B): [t 0..3][block j 0..3][word t, word t+4];
+//                     Q4_0 group (64 B):  [t 0..3][block j 0..3][word t] —
+//                     thread t of a row's quad reads its words of 4 blocks in 16-byte loads.
+//                     Padding blocks (K/32 rounded up to 8) are zero.
 //   Q8_0 activations  X[M][K]: xq = M rows of K int8, xd = M rows of K/32 fp32 scales (the fp16
 //                     scale widened, exactly as the CPU reads it).
-__host__ __device__ inline int64_t nb_padded(int64_t K) { return ((K / 32) + 3) / 4 * 4; }
-// byte offset, inside a weight row, of 32-bit word w of block b
-__host__ __device__ inline int64_t q8_word_off(int64_t b, int w) {
+__host__ __device__ inline int64_t n_sg(int64_t K) { return ((K / 32) + 7) / 8; }
+__host__ __device__ inline int64_t sg_bytes(int type) { return type == 8 ? 272 : 144; }
+__host__ __device__ inline int64_t qrow_bytes(int type, int64_t K) { return n_sg(K) * sg_bytes(type); }
+// byte offset, inside a weight row, of 32-bit word w of block b / of block b's fp16 scale
+__host__ __device__ inline int64_t w_word_off(int type, int64_t b, int w) {
+    const int64_t sg = b >> 3, bb = b & 7;
+    if (type == 8)
+        return sg * 272 + (bb >> 2) * 128 + (w & 3) * 32 + (bb & 3) * 8 + (w >> 2) * 4;
+    return sg * 144 + (bb >> 2) * 64 + w * 16 + (bb & 3) * 4;
+}
+__host__ __device__ inline int64_t w_scale_off(int type, int64_t b) {
+    return (b >> 3) * sg_bytes(type) + (type == 8 ? 256 : 128) + (b & 7) * 2;
+}
+// activation staging (shared memory): Q8_0 words in 4-block groups, same order as a Q8_0
+// weight group: [group][t 0..3][block j][word t, word t+4]
+__host__ __device__ inline int64_t x_word_off(int64_t b, int w) {
     return (b >> 2) * 128 + (w & 3) * 32 + (b & 3) * 8 + (w >> 2) * 4;
-}
-__host__ __device__ inline int64_t q4_word_off(int64_t b, int w) {
-    return (b >> 2) * 64 + w * 16 + (b & 3) * 4;
-}
-__host__ __device__ inline int64_t qrow_bytes(int type, int64_t K) {  // bytes of a group-layout row
-    return nb_padded(K) * (type == 8 ? 32 : 16);
 }
 #pragma once
 
@@ -38,8 +47,7 @@ struct StepParams {
 struct QWeight {
     int type = 0;               // T_Q8_0 or T_Q4_0 (or T_F32 / T_F16 for float weights)
     int64_t N = 0, K = 0;       // rows, columns
-    const void* qs = nullptr;   // quants (or float data for T_F32 / T_F16)
-    const __half* d = nullptr;  // block scales (quantized types)
+    const void* qs = nullptr;   // super-group rows (or float data for T_F32 / T_F16)
 };
 
 // ---- quantization ----------------------------------------------------------------------------
@@ -48,10 +56,10 @@ struct QWeight {
 void launch_quantize_q8_0(const float* x, int64_t x_stride, int64_t M, int64_t K, int8_t* xq,
                           float* xd, cudaStream_t st);
 
-// Repack a GGUF block tensor (N rows of K elements, 34/18-byte blocks) into the group layout.
-// qs must hold N * qrow_bytes(type, K) bytes and d N * nb_padded(K) halves; padding is zeroed.
+// Repack a GGUF block tensor (N rows of K elements, 34/18-byte blocks) into the super-group
+// layout.  qs must hold N * qrow_bytes(type, K) bytes; padding is zeroed.
 void launch_repack_blocks(const uint8_t* gguf, int type, int64_t N, int64_t K, void* qs,
-                          __half* d, cudaStream_t st);
+                          cudaStream_t st);
 
 // GET_ROWS: rows ids[i] of a quantized / f16 / f32 table [V][K] dequantized to f32 out[i][K].
 void launch_get_rows(const QWeight& w, const int32_t* ids, int64_t n, float* out,
@@ -97,6 +105,11 @@ struct GemvArgs {
 };
 void launch_gemv_fused(const GemvArgs& a, cudaStream_t st);
 bool gemv_fused_fits(int64_t K, int M);
+// The GEMV's pipeline waits are bounded; a timeout is recorded in a per-device error word
+// (1: producer, 2: consumer) instead of hanging.  gemv_prepare_device allocates that word
+// (call before graph capture); gemv_error_code reads it (0 = none).
+void gemv_prepare_device(int dev);
+int gemv_error_code(int dev);
 
 // Float-weight matmul (F32/F16 W, f32 X), used for non-quantized linears.
 void launch_matmul_f(const QWeight& w, const float* x, int64_t x_stride, int64_t M, float* y,

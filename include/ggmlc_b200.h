@@ -114,16 +114,15 @@ void* gb_executor_stream(const gb_executor* e);
 /* ---- op-level entry points (device pointers) ------------------------------------------------
  * The kernels behind the executor, exposed for operator tests and the operator sweep.  They
  * replace the CUDA ops of ggml-cuda the reference dispatches on this path.  Layouts:
- *   Q8_0/Q4_0 weight W[N][K] in the engine's group layout written by gb_repack_blocks: `wq`
- *   N rows of nbp*32 (Q8_0) or nbp*16 (Q4_0) bytes, nbp = K/32 rounded up to a multiple of 4,
- *   and `wd` fp16 bits [N][nbp];
+ *   Q8_0/Q4_0 weight W[N][K] in the engine's super-group layout written by gb_repack_blocks:
+ *   `wq` = N rows of ceil(K/256) super-groups of 8 blocks (quants + the 8 fp16 scales inline),
+ *   272 bytes (Q8_0) or 144 bytes (Q4_0) each;
  *   Q8_0 activations X[M][K]: `xq` int8 [M][K], `xd` fp32 [M][K/32]. */
 
-/* GGUF block rows (34-byte Q8_0 / 18-byte Q4_0 blocks) -> wq, wd (group layout, padding
+/* GGUF block rows (34-byte Q8_0 / 18-byte Q4_0 blocks) -> wq (super-group layout, padding
  * zeroed).  gguf is device memory.  Replaces the weight upload of ggml_backend_tensor_set
  * (executor.cpp:414-429). */
-int gb_repack_blocks(const void* gguf, int type, int64_t N, int64_t K, void* wq, void* wd,
-                     void* stream);
+int gb_repack_blocks(const void* gguf, int type, int64_t N, int64_t K, void* wq, void* stream);
 /* Activation quantization, quantize_row_q8_0 (ggml-cpu/arch/x86/quants.c:302-392 semantics;
  * the ggml-cuda twin is quantize_q8_1, quantize.cu:54-99).  x rows x_stride floats apart. */
 int gb_quantize_q8_0(const float* x, int64_t x_stride, int64_t M, int64_t K, int8_t* xq,
@@ -131,11 +130,31 @@ int gb_quantize_q8_0(const float* x, int64_t x_stride, int64_t M, int64_t K, int
 /* MUL_MAT Y[M][N] = X W^T (+bias[N]) (+residual[M][N]) — ggml_cuda_mul_mat
  * (ggml-cuda.cu:1812-1866: mul_mat_vec_q mmvq.cu:508 for M <= 8, mul_mat_q mmq.cuh:948
  * above).  Decode rows (M <= 8) are bit-exact with the x86 CPU kernels. */
-int gb_mul_mat_q(int type, const void* wq, const void* wd, int64_t N, int64_t K,
+int gb_mul_mat_q(int type, const void* wq, int64_t N, int64_t K,
                  const int8_t* xq, const float* xd, int64_t M, float* y, const float* bias,
                  const float* residual, void* stream);
+/* Decode GEMV (M <= 8) with fused prologue / epilogue, bit-exact like gb_mul_mat_q.  Input:
+ * Q8_0 rows (xq, xd) or, when xf != NULL, f32 rows [M][K] put through RMS_NORM(eps) (* gamma)
+ * and Q8_0 quantization first.  Output: y [M][N] (+bias, +residual); or with swiglu != 0 the
+ * SwiGLU of row pairs (n, n+N/2) as f32 y [M][N/2] and/or Q8_0 yq [M][N/2], yd [M][N/64].
+ * Replaces the ggml-cuda sequence rms_norm_f32 -> quantize_q8_1 -> mul_mat_vec_q ->
+ * unary_gated_op_kernel (norm.cu:77, quantize.cu:54, mmvq.cu:508, unary.cu:263). */
+int gb_gemv(int type, const void* wq, int64_t N, int64_t K, int64_t M,
+            const int8_t* xq, const float* xd, const float* xf, float eps, const float* gamma,
+            int swiglu, float* y, int8_t* yq, float* yd, const float* bias,
+            const float* residual, void* stream);
+/* Decode attention for one new token, fused with its RoPE and KV-cache write: qkv is the f32
+ * projection row [(Hq + 2 Hkv) * hd] (q heads, then k, then v); the new k (rotated) and v rows go
+ * to cache row kv_pos; o [Hq][hd] f32 and/or oq/od Q8_0.  table / n_pos / n_dims as
+ * gb_rope_neox (n_dims 0: no rotation).  work: gb_attn_decode_workspace_bytes().  Replaces
+ * rope_neox + k_set_rows + flash_attn_ext_vec (rope.cu:116, set-rows.cu:114, fattn-vec.cuh:21). */
+size_t gb_attn_decode_workspace_bytes(int64_t Hq, int64_t Hkv, int64_t hd, int64_t ctx);
+int gb_attn_decode(const float* qkv, int64_t Hq, int64_t Hkv, int64_t hd, void* k, void* v,
+                   int64_t ctx, int64_t kv_pos, int n_dims, float freq_base, const void* table,
+                   int64_t n_pos, float scale, float* o, int8_t* oq, float* od, void* work,
+                   void* stream);
 /* GET_ROWS with dequantization — k_get_rows (getrows.cu:6, get_rows_cuda_q :160) */
-int gb_get_rows(int type, const void* wq, const void* wd, int64_t N, int64_t K,
+int gb_get_rows(int type, const void* wq, int64_t N, int64_t K,
                 const int32_t* ids, int64_t n, float* out, void* stream);
 /* RMS_NORM (+gamma), optional fused Q8_0 output — rms_norm_f32 (norm.cu:77-156) */
 int gb_rms_norm(const float* x, int64_t M, int64_t D, float eps, const float* gamma, float* y,

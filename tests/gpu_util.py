@@ -30,10 +30,10 @@ def lib():
 
     L = _runtime.lib()
     P, I, I64, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
-    L.gb_repack_blocks.argtypes = [P, I, I64, I64, P, P, P]
+    L.gb_repack_blocks.argtypes = [P, I, I64, I64, P, P]
     L.gb_quantize_q8_0.argtypes = [P, I64, I64, I64, P, P, P]
-    L.gb_mul_mat_q.argtypes = [I, P, P, I64, I64, P, P, I64, P, P, P, P]
-    L.gb_get_rows.argtypes = [I, P, P, I64, I64, P, I64, P, P]
+    L.gb_mul_mat_q.argtypes = [I, P, I64, I64, P, P, I64, P, P, P, P]
+    L.gb_get_rows.argtypes = [I, P, I64, I64, P, I64, P, P]
     L.gb_rms_norm.argtypes = [P, I64, I64, F, P, P, P, P, P]
     L.gb_swiglu.argtypes = [P, I64, I64, P, P, P, P]
     L.gb_rope_table_fill.argtypes = [P, I64, I, F]
@@ -66,15 +66,14 @@ def random_blocks(rng, wtype: int, N: int, K: int, scale: float = 0.01) -> np.nd
 
 
 def upload_weight(wtype: int, blocks: np.ndarray, N: int, K: int):
-    """GGUF block bytes -> (wq, wd) device tensors through gb_repack_blocks."""
+    """GGUF block bytes -> device weight in the super-group layout (gb_repack_blocks)."""
     torch = torch_dev()
     src = dev(blocks.reshape(-1))
-    nbp = (K // 32 + 3) // 4 * 4  # blocks per row padded to groups of 4 (group layout)
-    wq = torch.empty(N * nbp * (32 if wtype == O.Q8_0 else 16), dtype=torch.uint8, device="cuda")
-    wd = torch.empty(N * nbp, dtype=torch.float16, device="cuda")
-    check(lib().gb_repack_blocks(ptr(src), wtype, N, K, ptr(wq), ptr(wd), None))
+    nsg = (K // 32 + 7) // 8  # super-groups of 8 blocks per row, scales inline
+    wq = torch.empty(N * nsg * (272 if wtype == O.Q8_0 else 144), dtype=torch.uint8, device="cuda")
+    check(lib().gb_repack_blocks(ptr(src), wtype, N, K, ptr(wq), None))
     torch.cuda.synchronize()
-    return wq, wd
+    return wq, None
 
 
 def quantize(x_dev, M: int, K: int):
@@ -89,7 +88,17 @@ def mul_mat(wtype, wq, wd, N, K, x_dev, M, bias=None, residual=None):
     torch = torch_dev()
     xq, xd = quantize(x_dev, M, K)
     y = torch.empty((M, N), dtype=torch.float32, device="cuda")
-    check(lib().gb_mul_mat_q(wtype, ptr(wq), ptr(wd), N, K, ptr(xq), ptr(xd), M, ptr(y),
+    check(lib().gb_mul_mat_q(wtype, ptr(wq), N, K, ptr(xq), ptr(xd), M, ptr(y),
                              ptr(bias), ptr(residual), None))
     torch.cuda.synchronize()
     return y.cpu().numpy()
+
+
+def lib_fused():
+    L = lib()
+    P, I, I64, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
+    L.gb_gemv.argtypes = [I, P, I64, I64, I64, P, P, P, F, P, I, P, P, P, P, P, P]
+    L.gb_attn_decode_workspace_bytes.argtypes = [I64, I64, I64, I64]
+    L.gb_attn_decode_workspace_bytes.restype = ctypes.c_size_t
+    L.gb_attn_decode.argtypes = [P, I64, I64, I64, P, P, I64, I64, I, F, P, I64, F, P, P, P, P, P]
+    return L

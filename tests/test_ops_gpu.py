@@ -118,7 +118,7 @@ def test_get_rows_bit_exact(G, wtype):
     ids = rng.integers(0, V, 37).astype(np.int32)
     ids_d = G.dev(ids)
     out = torch.empty((37, K), dtype=torch.float32, device="cuda")
-    G.check(G.lib().gb_get_rows(wtype, G.ptr(wq), G.ptr(wd), V, K, G.ptr(ids_d), 37,
+    G.check(G.lib().gb_get_rows(wtype, G.ptr(wq), V, K, G.ptr(ids_d), 37,
                                 G.ptr(out), None))
     ref = np.empty((37, K), np.float32)
     O.lib().oracle_get_rows(wtype, O._p(np.ascontiguousarray(w)), K, O._p(ids), 37, O._p(ref))
@@ -222,3 +222,94 @@ def test_attention_close(G, s, kv_pos, Hq, Hkv, hd):
     err_cpu = np.max(np.abs(cpu - exact))
     assert err_gpu <= 1e-5 * np.max(np.abs(exact))
     assert err_gpu <= err_cpu + 1e-6
+
+
+@pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_0])
+@pytest.mark.parametrize("M,K", [(1, 576), (1, 4096), (3, 1024)])
+@pytest.mark.parametrize("with_gamma", [False, True])
+def test_gemv_rms_prologue_bit_exact(G, wtype, M, K, with_gamma):
+    """RMSNorm (+gamma) and Q8_0 quantization fused into the GEMV prologue."""
+    torch = G.torch_dev()
+    rng = np.random.default_rng(K + M)
+    N = 96
+    w = G.random_blocks(rng, wtype, N, K)
+    wq, wd = G.upload_weight(wtype, w, N, K)
+    x = (rng.standard_normal((M, K)) * 2).astype(np.float32)
+    gamma = rng.standard_normal(K).astype(np.float32) if with_gamma else None
+    x_d = G.dev(x)
+    g_d = G.dev(gamma) if with_gamma else None
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    G.check(G.lib_fused().gb_gemv(wtype, G.ptr(wq), N, K, M, None, None, G.ptr(x_d),
+                                  1e-5, G.ptr(g_d), 0, G.ptr(y), None, None, None, None, None))
+    ref = O.mul_mat(wtype, w, N, K, O.rms_norm(x, 1e-5, gamma))
+    assert np.array_equal(y.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_0])
+@pytest.mark.parametrize("M", [1, 2, 7])
+def test_gemv_swiglu_epilogue_bit_exact(G, wtype, M):
+    """gate_up GEMV with SwiGLU and Q8_0 quantization of the result fused in the epilogue."""
+    torch = G.torch_dev()
+    rng = np.random.default_rng(M)
+    F, K = 160, 512
+    N = 2 * F
+    w = G.random_blocks(rng, wtype, N, K, scale=0.05)
+    wq, wd = G.upload_weight(wtype, w, N, K)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    xq, xd = G.quantize(G.dev(x), M, K)
+    y = torch.empty((M, F), dtype=torch.float32, device="cuda")
+    yq = torch.empty((M, F), dtype=torch.int8, device="cuda")
+    yd = torch.empty((M, F // 32), dtype=torch.float32, device="cuda")
+    G.check(G.lib_fused().gb_gemv(wtype, G.ptr(wq), N, K, M, G.ptr(xq), G.ptr(xd),
+                                  None, 0.0, None, 1, G.ptr(y), G.ptr(yq), G.ptr(yd), None, None,
+                                  None))
+    h = O.swiglu(O.mul_mat(wtype, w, N, K, x))
+    assert np.array_equal(y.cpu().numpy(), h)
+    hq = O.quantize_q8_0(h).reshape(M, F // 32, 34)
+    assert np.array_equal(yq.cpu().numpy(), hq[:, :, 2:].reshape(M, F).view(np.int8))
+    assert np.array_equal(yd.cpu().numpy(),
+                          hq[:, :, :2].copy().view(np.float16).reshape(M, F // 32).astype(np.float32))
+
+
+@pytest.mark.parametrize("Hq,Hkv,hd,kv_pos", [(4, 2, 64, 0), (9, 3, 64, 300), (32, 8, 128, 700)])
+def test_attn_decode_fused(G, Hq, Hkv, hd, kv_pos):
+    """Decode attention fused with RoPE and the KV write: cache row kv_pos holds fp16(rope(k)) and
+    fp16(v) bit-exactly, the output matches exact fp64 attention over the rotated q."""
+    torch = G.torch_dev()
+    rng = np.random.default_rng(Hq + kv_pos)
+    ctx = 1024
+    base = 500000.0
+    qkv = rng.standard_normal((Hq + 2 * Hkv) * hd).astype(np.float32)
+    k = rng.standard_normal((Hkv, ctx, hd)).astype(np.float16)
+    v = rng.standard_normal((Hkv, ctx, hd)).astype(np.float16)
+    n_pos = 4096
+    tab = np.empty((n_pos, hd // 2, 2), np.float32)
+    L = G.lib_fused()
+    G.lib().gb_rope_table_fill(tab.ctypes.data, n_pos, hd, base)
+    scale = float(np.float32(1.0) / np.sqrt(np.float32(hd)))
+    wb = L.gb_attn_decode_workspace_bytes(Hq, Hkv, hd, ctx)
+    work = torch.empty(int(wb), dtype=torch.uint8, device="cuda")
+    q_d, k_d, v_d, t_d = G.dev(qkv), G.dev(k.view(np.uint16)), G.dev(v.view(np.uint16)), G.dev(tab)
+    o = torch.empty((Hq, hd), dtype=torch.float32, device="cuda")
+    oq = torch.empty(Hq * hd, dtype=torch.int8, device="cuda")
+    od = torch.empty(Hq * hd // 32, dtype=torch.float32, device="cuda")
+    G.check(L.gb_attn_decode(G.ptr(q_d), Hq, Hkv, hd, G.ptr(k_d), G.ptr(v_d), ctx, kv_pos, hd,
+                             base, G.ptr(t_d), n_pos, scale, G.ptr(o), G.ptr(oq), G.ptr(od),
+                             G.ptr(work), None))
+    pos = np.array([kv_pos], np.int32)
+    qr = O.rope_neox(qkv[: Hq * hd].reshape(1, Hq, hd), pos, hd, np.float32(base))[0]
+    kr = O.rope_neox(qkv[Hq * hd:(Hq + Hkv) * hd].reshape(1, Hkv, hd), pos, hd, np.float32(base))[0]
+    vn = qkv[(Hq + Hkv) * hd:].reshape(Hkv, hd)
+    kc = k_d.cpu().numpy().view(np.float16)
+    vc = v_d.cpu().numpy().view(np.float16)
+    assert np.array_equal(kc[:, kv_pos], kr.astype(np.float16))
+    assert np.array_equal(vc[:, kv_pos], vn.astype(np.float16))
+    k2 = k.copy()
+    v2 = v.copy()
+    k2[:, kv_pos] = kr.astype(np.float16)
+    v2[:, kv_pos] = vn.astype(np.float16)
+    exact = _attention_exact(qr.reshape(1, Hq, hd), k2, v2, kv_pos, scale)[0]
+    got = o.cpu().numpy()
+    assert np.max(np.abs(got - exact)) <= 1e-5 * np.max(np.abs(exact))
+    ref_q = O.quantize_q8_0(got.reshape(1, -1)).reshape(-1, 34)
+    assert np.array_equal(oq.cpu().numpy(), ref_q[:, 2:].reshape(-1).view(np.int8))
