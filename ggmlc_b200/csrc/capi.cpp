@@ -346,6 +346,43 @@ int gb_attn_decode(const float* qkv, int64_t Hq, int64_t Hkv, int64_t hd, void* 
         gb::launch_attn_decode(a, (cudaStream_t)stream);
     });
 }
+size_t gb_attn_decode_noalloc_max_bytes(void) { return gb::kAttnDecStaticWorkBytes; }
+int gb_attn_decode_noalloc(const float* qkv, int64_t Hq, int64_t Hkv, int64_t hd, void* k,
+                           void* v, int64_t ctx, int64_t kv_pos, int n_dims, float freq_base,
+                           const void* table, int64_t n_pos, float scale, float* o, int8_t* oq,
+                           float* od, void* stream) {
+    return guard([&] {
+        GB_CHECK(Hq > 0 && Hkv > 0 && hd > 0, "gb_attn_decode_noalloc: head counts must be positive");
+        GB_CHECK(kv_pos >= 0 && kv_pos < ctx, "gb_attn_decode_noalloc: kv_pos outside the cache");
+        const int splits = gb::attn_decode_splits(Hkv, ctx);
+        float* work = gb::attn_decode_static_work(gb::attn_decode_workspace(Hq, hd, splits));
+        gb::AttnDecArgs a;
+        a.qkv = qkv;
+        a.q_off = 0;
+        a.k_off = Hq * hd;
+        a.v_off = (Hq + Hkv) * hd;
+        a.Hq = (int)Hq;
+        a.Hkv = (int)Hkv;
+        a.hd = (int)hd;
+        a.tab.cs = (const float2*)table;
+        a.tab.n_pos = table ? n_pos : 0;
+        a.tab.n_dims = n_dims;
+        a.tab.theta_scale = n_dims ? powf(freq_base, -2.0f / (float)n_dims) : 1.0f;
+        a.step = nullptr;
+        a.pos_off = kv_pos;
+        a.kc = (__half*)k;
+        a.vc = (__half*)v;
+        a.ctx = ctx;
+        a.scale = scale;
+        a.max_kv = ctx;
+        a.splits = splits;
+        a.part = work;
+        a.o = o;
+        a.oq = oq;
+        a.od = od;
+        gb::launch_attn_decode(a, (cudaStream_t)stream);
+    });
+}
 int gb_get_rows(int type, const void* wq, int64_t N, int64_t K,
                 const int32_t* ids, int64_t n, float* out, void* stream) {
     return guard([&] {

@@ -17,6 +17,9 @@
 // attention accumulates in fp32 (the CPU rounds its V accumulator to fp16 per position).
 #include <cuda_fp16.h>
 
+#include <mutex>
+#include <string>
+
 #include "common.h"
 #include "kernels.h"
 #include "kutil.cuh"
@@ -307,6 +310,35 @@ void launch_attn_decode(const AttnDecArgs& a, cudaStream_t st) {
     GB_CUDA(cudaGetLastError());
     k_attn_combine<<<(unsigned)a.Hq, (unsigned)a.hd, 0, st>>>(a);
     GB_CUDA(cudaGetLastError());
+}
+
+}  // namespace gb
+
+// Fixed scratch for gb_attn_decode_noalloc: the split partials of one decode-attention call.
+// Every partial the combine reads is written by k_attn_decode earlier on the same stream, so the
+// array needs no initial contents.  One array per device, shared by every call on that device.
+namespace gb {
+namespace {
+__device__ __align__(256) float g_dec_static_work[kAttnDecStaticWorkBytes / sizeof(float)];
+}  // namespace
+
+float* attn_decode_static_work(size_t need) {
+    GB_CHECK(need <= kAttnDecStaticWorkBytes,
+             "attn_decode: needs " + std::to_string(need) + " bytes of split scratch, more than the " +
+                 std::to_string(kAttnDecStaticWorkBytes) + "-byte static array");
+    int dev = 0;
+    GB_CUDA(cudaGetDevice(&dev));
+    GB_CHECK(dev >= 0 && dev < 64, "attn_decode: device ordinal out of range");
+    static std::mutex mu;
+    static void* addr[64] = {};
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev]) {
+        void* p = nullptr;
+        GB_CUDA(cudaGetSymbolAddress(&p, g_dec_static_work));
+        GB_CHECK(p != nullptr, "attn_decode: static scratch has no device address");
+        addr[dev] = p;
+    }
+    return (float*)addr[dev];
 }
 
 }  // namespace gb

@@ -208,6 +208,11 @@ struct AttnDecArgs {
 int attn_decode_splits(int64_t Hkv, int64_t max_kv);
 size_t attn_decode_workspace(int64_t Hq, int64_t hd, int splits);
 void launch_attn_decode(const AttnDecArgs& a, cudaStream_t st);
+// Size of the per-device static split scratch behind gb_attn_decode_noalloc.
+constexpr size_t kAttnDecStaticWorkBytes = size_t(4) << 20;
+// Device address of that scratch on the current device (looked up once per device); throws when
+// need exceeds kAttnDecStaticWorkBytes.
+float* attn_decode_static_work(size_t need);
 
 // Attention of q (f32 view [hd, s, Hq]) over KV caches [Hkv][ctx][hd] f16, causal at absolute
 // positions: query i sees cache rows 0 .. kv_base + i where kv_base = step->pos (use_step) or 0.

@@ -153,6 +153,21 @@ int gb_attn_decode(const float* qkv, int64_t Hq, int64_t Hkv, int64_t hd, void* 
                    int64_t ctx, int64_t kv_pos, int n_dims, float freq_base, const void* table,
                    int64_t n_pos, float scale, float* o, int8_t* oq, float* od, void* work,
                    void* stream);
+/* gb_attn_decode without the work argument, for callers that cannot allocate device memory.
+ * No counterpart in the reference (which sizes this scratch from its own CUDA memory pool).
+ * Allocates nothing: the split scratch is one fixed 4 MiB device array per device
+ * (gb_attn_decode_noalloc_max_bytes()), holding gb_attn_decode_workspace_bytes(Hq, Hkv, hd, ctx)
+ * bytes; larger shapes are rejected with an error before anything runs.  Its contents need no
+ * initial value (every partial is written before it is read).  The first call on a device looks
+ * up the array's address with that device current (setup): make it before any stream capture on
+ * that device.  All calls on one device share the array, so two calls whose kernels can overlap
+ * (different streams without ordering, or different host threads) race on it; order them on one
+ * stream.  Same results as gb_attn_decode. */
+size_t gb_attn_decode_noalloc_max_bytes(void);
+int gb_attn_decode_noalloc(const float* qkv, int64_t Hq, int64_t Hkv, int64_t hd, void* k,
+                           void* v, int64_t ctx, int64_t kv_pos, int n_dims, float freq_base,
+                           const void* table, int64_t n_pos, float scale, float* o, int8_t* oq,
+                           float* od, void* stream);
 /* GET_ROWS with dequantization — k_get_rows (getrows.cu:6, get_rows_cuda_q :160) */
 int gb_get_rows(int type, const void* wq, int64_t N, int64_t K,
                 const int32_t* ids, int64_t n, float* out, void* stream);
