@@ -254,6 +254,13 @@ void* gb_executor_stream(const gb_executor* e) { return (void*)e->e->stream(); }
 
 // ---- op level ----------------------------------------------------------------------------------
 
+int64_t gb_weight_row_bytes(int type, int64_t K) {
+    if ((type != gb::T_Q8_0 && type != gb::T_Q4_0) || K < 0 || K % 32) {
+        g_err = "gb_weight_row_bytes: Q8_0 or Q4_0 with K a multiple of 32 required";
+        return -1;
+    }
+    return gb::qrow_bytes(type, K);
+}
 int gb_repack_blocks(const void* gguf, int type, int64_t N, int64_t K, void* wq, void* stream) {
     return guard([&] {
         gb::launch_repack_blocks((const uint8_t*)gguf, type, N, K, wq, (cudaStream_t)stream);
@@ -277,7 +284,7 @@ int gb_mul_mat_q(int type, const void* wq, int64_t N, int64_t K,
         ep.bias = bias;
         ep.residual = residual;
         ep.res_stride = N;
-        gb::launch_matmul_q_exact(w, xq, xd, M, y, N, ep, (cudaStream_t)stream);
+        gb::launch_matmul_q(w, xq, xd, M, y, N, ep, (cudaStream_t)stream);
     });
 }
 int gb_gemv(int type, const void* wq, int64_t N, int64_t K, int64_t M,

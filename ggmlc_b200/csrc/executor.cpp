@@ -100,7 +100,6 @@ Executor::Executor(std::shared_ptr<Graph> g, const std::string& device) : g_(std
     GB_CUDA(cudaMalloc(&d_step_, sizeof(StepParams)));
     h_step_->pos = 0;
     GB_CUDA(cudaMemcpy(d_step_, h_step_, sizeof(StepParams), cudaMemcpyHostToDevice));
-    gemv_prepare_device(dev_);
     upload_weights();
 }
 
@@ -669,7 +668,7 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         const BufRef qb = xl.q, qdb = xl.qd;
                         add("matmul_q", [=](Program& p, cudaStream_t st) {
                             MatmulEpilogue e = ep;
-                            launch_matmul_q_exact(*qw, (const int8_t*)p.ptr(qb),
+                            launch_matmul_q(*qw, (const int8_t*)p.ptr(qb),
                                                   (const float*)p.ptr(qdb), 1, (float*)p.ptr(yr),
                                                   ystride, e, st);
                         }, mm_bytes(qw, 1, false));
@@ -679,7 +678,7 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         add("matmul_q", [=](Program& p, cudaStream_t st) {
                             MatmulEpilogue e = ep;
                             if (rref.fixed || rref.buf >= 0) e.residual = (const float*)p.ptr(rref);
-                            launch_matmul_q_exact(*qw, (const int8_t*)p.ptr(qb),
+                            launch_matmul_q(*qw, (const int8_t*)p.ptr(qb),
                                                   (const float*)p.ptr(qdb), Mrun, (float*)p.ptr(yr),
                                                   ystride, e, st);
                         }, mm_bytes(qw, Mrun, add_op >= 0));
@@ -1367,8 +1366,6 @@ void Executor::run() {
 
 void Executor::synchronize() {
     GB_CUDA(cudaStreamSynchronize(stream_));
-    const int code = gemv_error_code(dev_);
-    GB_CHECK(code == 0, "GEMV pipeline wait timed out (code " + std::to_string(code) + ")");
 }
 
 bool Executor::cuda_graph_captured() const {

@@ -81,8 +81,8 @@ __global__ void k_rope_qkv(QkvRopeArgs a) {
 
 constexpr int kDecThreads = 128;
 constexpr int kMaxRk = 8;     // q heads per KV head handled by one CTA
-constexpr int kChunk = 64;    // positions staged per round trip
-constexpr int kMaxOut = kMaxRk * 256 / kDecThreads;  // V outputs per thread
+constexpr int kChunk = 32;    // positions per staged chunk (two chunk buffers)
+constexpr int kMaxSplits = 64;
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
@@ -91,97 +91,124 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
                  : "memory");
 }
 
+// Split-KV decode attention for head_dim HD, one CTA per (split, KV head), 4 warps.
+// Launched as a programmatic dependent launch: the first chunk of cached K/V rows (written by
+// earlier steps) is requested before griddepcontrol.wait; the q/k/v projection row after it.
+// Scores: a warp per position, lane l holding dims [l*PL, l*PL+PL) of q (registers) and K.
+// Values: thread t owns 4 consecutive dims of one q head (HD/4 threads per head).
+template <int HD>
 __global__ void __launch_bounds__(kDecThreads) k_attn_decode(AttnDecArgs a) {
+    constexpr int PL = HD / 32;             // dims per lane in the score dot
+    constexpr int VEC = HD / 8;             // 16-byte pieces per K or V row
+    constexpr int TPH = HD / 4;             // value threads per q head
+    constexpr int HPP = kDecThreads / TPH;  // q heads per value pass
+    constexpr int NPASS = (kMaxRk + HPP - 1) / HPP;
     extern __shared__ __align__(16) uint8_t smem[];
-    const int hd = a.hd;
+    __half* sk = (__half*)smem;              // [2][kChunk][HD]
+    __half* sv = sk + 2 * kChunk * HD;       // [2][kChunk][HD]
+    __half* snew = sv + 2 * kChunk * HD;     // [2][HD] new k (rotated), new v
+    float* ss = (float*)(snew + 2 * HD);     // [kMaxRk][kChunk] scores / probabilities
+    float* sstat = ss + kMaxRk * kChunk;     // [kMaxRk][3] running max, sum, correction
+    float* sq = sstat + kMaxRk * 3;          // [kMaxRk][HD] rotated q (fp16-rounded)
     const int rk = a.Hq / a.Hkv;
-    __half* sk = (__half*)smem;                      // [kChunk][hd]
-    __half* sv = sk + kChunk * hd;                   // [kChunk][hd]
-    float* sq = (float*)(sv + kChunk * hd);          // [rk][hd] rotated q (fp16-rounded)
-    float* ss = sq + rk * hd;                        // [rk][kChunk] scores / probabilities
-    float* sstat = ss + rk * kChunk;                 // [rk][3] running max, sum, correction
     const int hk = blockIdx.y;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t pos = (a.step ? a.step->pos : 0) + a.pos_off;  // position of the new token
     const int64_t nkv = pos + 1;
     const int64_t per = (nkv + gridDim.x - 1) / gridDim.x;
-    const int64_t c0 = (int64_t)blockIdx.x * per;
+    const int64_t c0 = min((int64_t)blockIdx.x * per, nkv);
     const int64_t c1 = min(c0 + per, nkv);
-    const float* row = a.qkv;
-    const __half* kbase = a.kc + ((int64_t)hk * a.ctx) * hd;
-    const __half* vbase = a.vc + ((int64_t)hk * a.ctx) * hd;
-    const int vec = hd / 8;  // 16-byte pieces per row
-    // the split holding the new position writes its k, v rows into the cache first
-    const bool owns_new = c0 <= pos && pos < c1;
-    if (owns_new) {
-        for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-            const float* ks = row + a.k_off + (int64_t)hk * hd;
-            a.kc[((int64_t)hk * a.ctx + pos) * hd + d] = __float2half_rn(rope_elem(ks, d, hd, a.tab, pos));
-            a.vc[((int64_t)hk * a.ctx + pos) * hd + d] = __float2half_rn(row[a.v_off + (int64_t)hk * hd + d]);
-        }
-        __syncthreads();  // the new row is read back below
-    }
-    // first chunk in flight while q is rotated
-    auto stage = [&](int64_t cs, int rows) {
-        for (int e = threadIdx.x; e < rows * vec * 2; e += blockDim.x) {
-            const int r = e / (vec * 2), piece = e % (vec * 2);
-            const int kv = piece >= vec;
-            const int pc = piece - kv * vec;
-            const __half* src = (kv ? vbase : kbase) + (cs + r) * hd + pc * 8;
-            __half* dst = (kv ? sv : sk) + r * hd + pc * 8;
-            cp_async16(dst, src);
+    const __half* kbase = a.kc + ((int64_t)hk * a.ctx) * HD;
+    const __half* vbase = a.vc + ((int64_t)hk * a.ctx) * HD;
+    auto stage = [&](int buf, int64_t cs, int rows) {
+        __half* dk = sk + buf * kChunk * HD;
+        __half* dv = sv + buf * kChunk * HD;
+        for (int e = threadIdx.x; e < rows * VEC; e += kDecThreads) {
+            const int r = e / VEC, pc = e % VEC;
+            if (cs + r == pos) continue;  // the new row is taken from snew
+            cp_async16(dk + r * HD + pc * 8, kbase + (cs + r) * HD + pc * 8);
+            cp_async16(dv + r * HD + pc * 8, vbase + (cs + r) * HD + pc * 8);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    if (c0 < c1) stage(c0, (int)min((int64_t)kChunk, c1 - c0));
-    for (int e = threadIdx.x; e < rk * hd; e += blockDim.x) {
-        const int h = e / hd, d = e % hd;
-        const float* src = row + a.q_off + (int64_t)(hk * rk + h) * hd;
-        sq[h * hd + d] = __half2float(__float2half_rn(rope_elem(src, d, hd, a.tab, pos)));
+    const int nch = (int)((c1 - c0 + kChunk - 1) / kChunk);
+    if (nch > 0) stage(0, c0, (int)min((int64_t)kChunk, c1 - c0));
+    pdl_wait();
+    pdl_launch();
+
+    const float* row = a.qkv;
+    for (int e = threadIdx.x; e < rk * HD; e += kDecThreads) {
+        const int h = e / HD, d = e % HD;
+        const float* src = row + a.q_off + (int64_t)(hk * rk + h) * HD;
+        sq[e] = __half2float(__float2half_rn(rope_elem(src, d, HD, a.tab, pos)));
     }
-    for (int h = threadIdx.x; h < rk; h += blockDim.x) {
-        sstat[h * 3 + 0] = -INFINITY;
-        sstat[h * 3 + 1] = 0.0f;
-        sstat[h * 3 + 2] = 1.0f;
+    if (c0 <= pos && pos < c1) {
+        // this split holds the new position: rotate its k, write k and v to the cache
+        const float* ks = row + a.k_off + (int64_t)hk * HD;
+        for (int d = threadIdx.x; d < HD; d += kDecThreads) {
+            const __half kh = __float2half_rn(rope_elem(ks, d, HD, a.tab, pos));
+            const __half vh = __float2half_rn(row[a.v_off + (int64_t)hk * HD + d]);
+            a.kc[((int64_t)hk * a.ctx + pos) * HD + d] = kh;
+            a.vc[((int64_t)hk * a.ctx + pos) * HD + d] = vh;
+            snew[d] = kh;
+            snew[HD + d] = vh;
+        }
     }
-    float acc[kMaxOut];
+    if (threadIdx.x < kMaxRk) {
+        sstat[threadIdx.x * 3 + 0] = -INFINITY;
+        sstat[threadIdx.x * 3 + 1] = 0.0f;
+        sstat[threadIdx.x * 3 + 2] = 1.0f;
+    }
+    __syncthreads();  // sq ready
+    float qr[kMaxRk][PL];
 #pragma unroll
-    for (int k = 0; k < kMaxOut; ++k) acc[k] = 0.0f;
-    const int per_lane = hd / 32;
-    for (int64_t cs = c0; cs < c1; cs += kChunk) {
+    for (int h = 0; h < kMaxRk; ++h)
+#pragma unroll
+        for (int j = 0; j < PL; ++j) qr[h][j] = h < rk ? sq[h * HD + lane * PL + j] : 0.0f;
+    float4 acc[NPASS];
+#pragma unroll
+    for (int p = 0; p < NPASS; ++p) acc[p] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const int vh0 = threadIdx.x / TPH, vd = (threadIdx.x % TPH) * 4;
+
+    for (int c = 0; c < nch; ++c) {
+        const int buf = c & 1;
+        const int64_t cs = c0 + (int64_t)c * kChunk;
         const int rows = (int)min((int64_t)kChunk, c1 - cs);
         asm volatile("cp.async.wait_group 0;" ::: "memory");
-        __syncthreads();
-        // scores: one warp per position, lanes across head_dim
+        __syncthreads();  // chunk c landed; the previous chunk's reads are finished
+        if (c + 1 < nch) stage(buf ^ 1, cs + kChunk, (int)min((int64_t)kChunk, c1 - cs - kChunk));
+        const __half* ck = sk + buf * kChunk * HD;
+        const __half* cv = sv + buf * kChunk * HD;
         for (int r = warp; r < rows; r += kDecThreads / 32) {
-            float kv[8];
+            const __half* kr = (cs + r == pos ? snew : ck + r * HD) + lane * PL;
+            float kv[PL];
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-                if (j < per_lane) kv[j] = __half2float(sk[r * hd + lane * per_lane + j]);
-            for (int h = 0; h < rk; ++h) {
-                float dot = 0.0f;
+            for (int j = 0; j < PL; j += 2) {
+                const float2 f = __half22float2(*(const __half2*)(kr + j));
+                kv[j] = f.x;
+                kv[j + 1] = f.y;
+            }
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    if (j < per_lane) dot = __fmaf_rn(kv[j], sq[h * hd + lane * per_lane + j], dot);
-                dot = warp_sum(dot);
-                if (lane == 0) ss[h * kChunk + r] = __fmul_rn(dot, a.scale);
+            for (int h = 0; h < kMaxRk; ++h) {
+                if (h < rk) {
+                    float dot = 0.0f;
+#pragma unroll
+                    for (int j = 0; j < PL; ++j) dot = __fmaf_rn(kv[j], qr[h][j], dot);
+                    dot = warp_sum(dot);
+                    if (lane == 0) ss[h * kChunk + r] = __fmul_rn(dot, a.scale);
+                }
             }
         }
         __syncthreads();
         // online softmax statistics per head (one warp per head)
         for (int h = warp; h < rk; h += kDecThreads / 32) {
-            float mx = -INFINITY;
-            for (int r = lane; r < rows; r += 32) mx = fmaxf(mx, ss[h * kChunk + r]);
-            mx = warp_max(mx);
+            const float sc = lane < rows ? ss[h * kChunk + lane] : -INFINITY;
+            const float mx = warp_max(sc);
             const float mold = sstat[h * 3 + 0];
             const float mnew = fmaxf(mold, mx);
-            float l = 0.0f;
-            for (int r = lane; r < rows; r += 32) {
-                const float p = expf(ss[h * kChunk + r] - mnew);
-                ss[h * kChunk + r] = p;
-                l += p;
-            }
-            l = warp_sum(l);
+            const float p = lane < rows ? expf(sc - mnew) : 0.0f;
+            ss[h * kChunk + lane] = p;
+            const float l = warp_sum(p);
             if (lane == 0) {
                 const float corr = expf(mold - mnew);
                 sstat[h * 3 + 0] = mnew;
@@ -190,82 +217,116 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(AttnDecArgs a) {
             }
         }
         __syncthreads();
-        // V accumulation: thread owns outputs e = tid + k*128 of the group's [rk][hd]
 #pragma unroll
-        for (int k = 0; k < kMaxOut; ++k) {
-            const int e = threadIdx.x + k * kDecThreads;
-            if (e < rk * hd) {
-                const int h = e / hd, d = e % hd;
-                float v = acc[k] * sstat[h * 3 + 2];
-                for (int r = 0; r < rows; ++r)
-                    v = __fmaf_rn(ss[h * kChunk + r], __half2float(sv[r * hd + d]), v);
-                acc[k] = v;
+        for (int p = 0; p < NPASS; ++p) {
+            const int h = vh0 + p * HPP;
+            if (h < rk) {
+                const float corr = sstat[h * 3 + 2];
+                float4 v = make_float4(acc[p].x * corr, acc[p].y * corr, acc[p].z * corr,
+                                       acc[p].w * corr);
+                const float* ph = ss + h * kChunk;
+                for (int r = 0; r < rows; ++r) {
+                    const __half* vr = (cs + r == pos ? snew + HD : cv + r * HD) + vd;
+                    const uint2 raw = *(const uint2*)vr;
+                    const float2 f0 = __half22float2(*(const __half2*)&raw.x);
+                    const float2 f1 = __half22float2(*(const __half2*)&raw.y);
+                    const float pr = ph[r];
+                    v.x = __fmaf_rn(pr, f0.x, v.x);
+                    v.y = __fmaf_rn(pr, f0.y, v.y);
+                    v.z = __fmaf_rn(pr, f1.x, v.z);
+                    v.w = __fmaf_rn(pr, f1.y, v.w);
+                }
+                acc[p] = v;
             }
         }
-        __syncthreads();  // chunk buffers are free again
-        if (cs + kChunk < c1) stage(cs + kChunk, (int)min((int64_t)kChunk, c1 - cs - kChunk));
     }
     __syncthreads();
-    float* part = a.part + ((int64_t)blockIdx.x * a.Hq + (int64_t)hk * rk) * (hd + 2);
-    for (int h = threadIdx.x; h < rk; h += blockDim.x) {
-        part[h * (hd + 2) + 0] = c0 < c1 ? sstat[h * 3 + 0] : -INFINITY;
-        part[h * (hd + 2) + 1] = c0 < c1 ? sstat[h * 3 + 1] : 0.0f;
+    float* part = a.part + ((int64_t)blockIdx.x * a.Hq + (int64_t)hk * rk) * (HD + 4);
+    if (threadIdx.x < rk) {
+        part[threadIdx.x * (HD + 4) + 0] = c0 < c1 ? sstat[threadIdx.x * 3 + 0] : -INFINITY;
+        part[threadIdx.x * (HD + 4) + 1] = c0 < c1 ? sstat[threadIdx.x * 3 + 1] : 0.0f;
     }
 #pragma unroll
-    for (int k = 0; k < kMaxOut; ++k) {
-        const int e = threadIdx.x + k * kDecThreads;
-        if (e < rk * hd) part[(e / hd) * (hd + 2) + 2 + e % hd] = acc[k];
+    for (int p = 0; p < NPASS; ++p) {
+        const int h = vh0 + p * HPP;
+        if (h < rk) *(float4*)(part + h * (HD + 4) + 4 + vd) = acc[p];
     }
 }
 
-__global__ void k_attn_combine(AttnDecArgs a) {
-    __shared__ float sw[256];
+// Merge the splits of each q head; one CTA per q head, one thread per dim.  Every load is issued
+// before the first dependent step: thread d reads its value of each split, warp 0 the (m, l)
+// pairs.
+template <int HD>
+__global__ void __launch_bounds__(HD) k_attn_combine(AttnDecArgs a) {
+    __shared__ float sw[kMaxSplits];
     __shared__ float sL;
+    pdl_wait();
+    pdl_launch();
     const int h = blockIdx.x;  // q head
-    const int hd = a.hd;
     const int S = a.splits;
-    const float* base = a.part + (int64_t)h * (hd + 2);
-    const int64_t sstride = (int64_t)a.Hq * (hd + 2);
+    const int d = threadIdx.x;
+    const float* base = a.part + (int64_t)h * (HD + 4);
+    const int64_t sstride = (int64_t)a.Hq * (HD + 4);
+    float pv[kMaxSplits];
+#pragma unroll
+    for (int sp = 0; sp < kMaxSplits; ++sp) pv[sp] = sp < S ? __ldcg(base + sp * sstride + 4 + d) : 0.0f;
     if (threadIdx.x < 32) {
-        float M = -INFINITY;
-        for (int sp = threadIdx.x; sp < S; sp += 32) M = fmaxf(M, base[sp * sstride]);
-        M = warp_max(M);
-        float L = 0.0f;
-        for (int sp = threadIdx.x; sp < S; sp += 32) {
-            const float m = base[sp * sstride];
-            const float w = m == -INFINITY ? 0.0f : expf(m - M);
-            sw[sp] = w;
-            L += base[sp * sstride + 1] * w;
-        }
-        L = warp_sum(L);
-        if (threadIdx.x == 0) sL = L;
+        const int l = threadIdx.x;
+        const float2 ml0 = l < S ? __ldcg((const float2*)(base + l * sstride)) : make_float2(-INFINITY, 0.0f);
+        const float2 ml1 = l + 32 < S ? __ldcg((const float2*)(base + (l + 32) * sstride))
+                                      : make_float2(-INFINITY, 0.0f);
+        const float M = warp_max(fmaxf(ml0.x, ml1.x));
+        const float w0 = ml0.x == -INFINITY ? 0.0f : expf(ml0.x - M);
+        const float w1 = ml1.x == -INFINITY ? 0.0f : expf(ml1.x - M);
+        sw[l] = w0;
+        sw[l + 32] = w1;
+        const float L = warp_sum(ml0.y * w0 + ml1.y * w1);
+        if (l == 0) sL = L;
     }
     __syncthreads();
     const float inv = sL == 0.0f ? 0.0f : 1.0f / sL;
-    const int lane = threadIdx.x & 31;
-    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-        float v0 = 0.0f, v1 = 0.0f, v2 = 0.0f, v3 = 0.0f;
-        int sp = 0;
-        for (; sp + 4 <= S; sp += 4) {
-            v0 += base[(sp + 0) * sstride + 2 + d] * sw[sp + 0];
-            v1 += base[(sp + 1) * sstride + 2 + d] * sw[sp + 1];
-            v2 += base[(sp + 2) * sstride + 2 + d] * sw[sp + 2];
-            v3 += base[(sp + 3) * sstride + 2 + d] * sw[sp + 3];
-        }
-        for (; sp < S; ++sp) v0 += base[sp * sstride + 2 + d] * sw[sp];
-        const float v = ((v0 + v1) + (v2 + v3)) * inv;
-        if (a.o) a.o[(int64_t)h * hd + d] = v;
-        if (a.oq) {  // blockDim.x == hd: warp w owns elements 32w..32w+31 of the head
-            float d16, q;
-            q8_block(v, lane, d16, q);
-            a.oq[(int64_t)h * hd + d] = (int8_t)__float2int_rn(q);
-            if (lane == 0) a.od[((int64_t)h * hd + d) / 32] = d16;
-        }
+    float v0 = 0.0f, v1 = 0.0f, v2 = 0.0f, v3 = 0.0f;
+#pragma unroll
+    for (int sp = 0; sp < kMaxSplits; sp += 4) {
+        v0 += pv[sp] * sw[sp];
+        v1 += pv[sp + 1] * sw[sp + 1];
+        v2 += pv[sp + 2] * sw[sp + 2];
+        v3 += pv[sp + 3] * sw[sp + 3];
+    }
+    const float v = ((v0 + v1) + (v2 + v3)) * inv;
+    if (a.o) a.o[(int64_t)h * HD + d] = v;
+    if (a.oq) {  // warp w owns elements 32w..32w+31 of the head: one Q8_0 block
+        const int lane = threadIdx.x & 31;
+        float d16, q;
+        q8_block(v, lane, d16, q);
+        a.oq[(int64_t)h * HD + d] = (int8_t)__float2int_rn(q);
+        if (lane == 0) a.od[((int64_t)h * HD + d) / 32] = d16;
     }
 }
 
-size_t dec_smem(int hd, int rk) {
-    return (size_t)kChunk * hd * 2 * 2 + (size_t)rk * hd * 4 + (size_t)rk * kChunk * 4 + rk * 12;
+template <int HD>
+size_t dec_smem() {
+    return (size_t)4 * kChunk * HD * 2 + (size_t)2 * HD * 2 + (size_t)kMaxRk * kChunk * 4 +
+           kMaxRk * 12 + (size_t)kMaxRk * HD * 4;
+}
+
+template <int HD>
+void launch_dec(const AttnDecArgs& a, cudaStream_t st) {
+    const size_t smem = dec_smem<HD>();
+    int dev = 0;
+    GB_CUDA(cudaGetDevice(&dev));
+    static std::mutex mu;
+    static bool configured[64] = {};
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!configured[dev & 63]) {
+            GB_CUDA(cudaFuncSetAttribute(k_attn_decode<HD>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            configured[dev & 63] = true;
+        }
+    }
+    launch_pdl(k_attn_decode<HD>, dim3((unsigned)a.splits, (unsigned)a.Hkv), kDecThreads, smem, st, a);
+    launch_pdl(k_attn_combine<HD>, dim3((unsigned)a.Hq), HD, 0, st, a);
 }
 
 }  // namespace
@@ -284,32 +345,24 @@ int attn_decode_splits(int64_t Hkv, int64_t max_kv) {
     // about two CTAs per SM; each split then walks max_kv / splits positions
     int64_t s = (296 + Hkv - 1) / Hkv;
     if (s > max_kv) s = max_kv;
-    if (s > 256) s = 256;
+    if (s > kMaxSplits) s = kMaxSplits;
     return (int)(s < 1 ? 1 : s);
 }
 
 size_t attn_decode_workspace(int64_t Hq, int64_t hd, int splits) {
-    return (size_t)splits * Hq * (hd + 2) * sizeof(float);
+    return (size_t)splits * Hq * (hd + 4) * sizeof(float);
 }
 
 void launch_attn_decode(const AttnDecArgs& a, cudaStream_t st) {
-    GB_CHECK(a.hd % 32 == 0 && a.hd <= 256, "attn_decode: head_dim must be a multiple of 32, <= 256");
-    GB_CHECK(a.Hq % a.Hkv == 0 && a.Hq / a.Hkv <= kMaxRk, "attn_decode: GQA group too large");
-    GB_CHECK(a.splits >= 1 && a.splits <= 256, "attn_decode: bad split count");
-    const size_t smem = dec_smem(a.hd, a.Hq / a.Hkv);
-    int dev = 0;
-    GB_CUDA(cudaGetDevice(&dev));
-    static unsigned configured = 0;
-    if (!(configured & (1u << (dev & 31)))) {
-        GB_CUDA(cudaFuncSetAttribute(k_attn_decode, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     100 * 1024));
-        configured |= 1u << (dev & 31);
+    GB_CHECK(a.hd == 64 || a.hd == 128 || a.hd == 256, "attn_decode: head_dim must be 64, 128 or 256");
+    GB_CHECK(a.Hkv > 0 && a.Hq % a.Hkv == 0 && a.Hq / a.Hkv <= kMaxRk,
+             "attn_decode: GQA group too large");
+    GB_CHECK(a.splits >= 1 && a.splits <= kMaxSplits, "attn_decode: bad split count");
+    switch (a.hd) {
+        case 64: launch_dec<64>(a, st); break;
+        case 128: launch_dec<128>(a, st); break;
+        default: launch_dec<256>(a, st); break;
     }
-    dim3 grid((unsigned)a.splits, (unsigned)a.Hkv);
-    k_attn_decode<<<grid, kDecThreads, smem, st>>>(a);
-    GB_CUDA(cudaGetLastError());
-    k_attn_combine<<<(unsigned)a.Hq, (unsigned)a.hd, 0, st>>>(a);
-    GB_CUDA(cudaGetLastError());
 }
 
 }  // namespace gb

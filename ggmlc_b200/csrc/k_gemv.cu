@@ -1,23 +1,33 @@
-// Decode GEMV (M <= 8) over the super-group weight layout, bit-exact with the reference CPU
-// kernels, with optional fused RMSNorm+quantize prologue and SwiGLU+quantize epilogue.
+// Decode GEMV (M <= 8 activation rows) over the split-row weight layout, with an optional fused
+// RMSNorm + Q8_0 prologue and a bias / residual / SwiGLU epilogue.
 //
-// Arithmetic order.  The reference's x86 kernels (ggml_vec_dot_q{8,4}_0_q8_0,
-// arch/x86/quants.c:1308-1342 and :701; llamafile tinyBLAS_Q0_AVX, sgemm.cpp:1353) keep 8 fp32
-// lanes per output: lane i accumulates, block after block, fma(d_w*d_x, float(int dot of
-// elements 4i..4i+3), acc_i); the lanes are reduced ((a0+a4)+(a2+a6))+((a1+a5)+(a3+a7)).  A
-// quad of consumer threads owns an output row; thread t carries lanes t and t+4.
+// Arithmetic.  Per 32-element block the integer dot sumi = sum q_w * q_x is exact (dp4a chain),
+// and the output accumulates fp32 block terms sumi * (d_w * d_x), the block formula of the
+// reference's generic kernels (ggml-cpu/quants.c:225-256 Q4_0, :451-477 Q8_0).  The x86 build
+// splits each block over 8 SIMD lanes instead; the fp32 results agree to rounding (the integer
+// parts are identical).  Activations are quantized exactly like the x86 build
+// (arch/x86/quants.c:302-392).
 //
-// Data movement.  A producer warp streams each tile of R weight rows through a 4-stage shared
-// memory ring: one cp.async.bulk per row and stage (a contiguous run of C super-groups of that
-// row), completion tracked by mbarrier transaction counts; consumers release a stage with an
-// mbarrier arrive.  No TMA multicast is used.  Every wait is bounded: on timeout the kernel
-// records an error code in *err and returns instead of hanging.
+// Work mapping.  Lanes run along K: lane l of a warp takes blocks l, l+32, l+64, ... of a row, so
+// each 16-byte load of a warp reads 512 contiguous bytes.  A lane holds G blocks of one row in
+// registers ("group"); the next group (possibly of the warp's next row) is loaded before the
+// current one is consumed, so every warp keeps one group of loads in flight.  The Q8_0
+// activations live in shared memory, split into words 0-3 and 4-7 of each block so the lanes'
+// 16-byte reads are conflict-free.  A row's lane sums are combined by a fixed xor-butterfly.
+// Plain outputs: rows are dealt to all warps of the grid.  SwiGLU: a CTA owns 32 consecutive
+// outputs (row pairs n, F+n) so it can emit each Q8_0 block of the result itself.
 //
 // Q4_0 nibbles become int8 with a shift and two bitwise ops: (q<<4) ^ 0x80 read as int8 is
-// 16*(q-8), so dp4a yields 16x the lane dot; the activation scales are staged pre-divided by 16
-// (exact: a power of two), which makes fma(d_w*(d_x/16), 16p, acc) the same rounding as the
-// CPU's fma(d_w*d_x, p, acc).
+// 16*(q-8); the activation scales are staged divided by 16 (exact), so the products are
+// unchanged.  int -> float of the block sum uses the 1.5*2^23 bias trick (exact for |v| < 2^22).
+//
+// Launch: programmatic dependent launch.  The first group of weights is requested before
+// griddepcontrol.wait, so the weight stream of this launch overlaps the tail of the previous one;
+// all reads of activations and all writes happen after the wait.
 #include <cuda_fp16.h>
+
+#include <algorithm>
+#include <mutex>
 
 #include "common.h"
 #include "kernels.h"
@@ -27,388 +37,449 @@ namespace gb {
 
 namespace {
 
-constexpr int kStages = 4;
-constexpr int kStageTarget = 18 * 1024;  // bytes of weights per stage
-constexpr size_t kSmemMax = 220 * 1024;
-constexpr long long kSpinLimit = 1LL << 26;  // bounded mbarrier waits (then error + exit)
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr size_t kSmemMax = 200 * 1024;
 
-__device__ __forceinline__ unsigned smem_u32(const void* p) {
-    return (unsigned)__cvta_generic_to_shared(p);
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
 }
-__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+__device__ __forceinline__ unsigned short ldg_u16(const void* p) {
+    unsigned short v;
+    asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
+    return v;
 }
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
-                 "r"(bytes)
+
+__device__ __forceinline__ float block_sum_f(int s) {
+    return __fsub_rn(__int_as_float(s), 12582912.0f);
+}
+
+// A step covers 64 blocks of one row: lane l takes blocks 64g + l and 64g + 32 + l and their two
+// scales (one 4-byte word of the scale region).  Each warp streams its steps through a ring of
+// kDepth shared-memory slots with cp.async; a lane only ever reads what it copied itself, so no
+// synchronization beyond cp.async.wait_group is needed.
+constexpr int kDepth = 3;
+
+template <int WT>
+struct Slot {  // bytes of one ring slot (one step of one warp)
+    static constexpr int kQuant = (WT == T_Q8_0 ? 4 : 2) * 32 * 16;  // [piece][lane][16 B]
+    static constexpr int kBytes = kQuant + 32 * 4;                    // + [lane][2 scales]
+};
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                     (unsigned)__cvta_generic_to_shared(dst)),
+                 "l"(src)
                  : "memory");
 }
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(
+                     (unsigned)__cvta_generic_to_shared(dst)),
+                 "l"(src)
+                 : "memory");
 }
-// returns false on timeout
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, unsigned parity) {
-    const unsigned addr = smem_u32(bar);
-    for (long long i = 0; i < kSpinLimit; ++i) {
-        unsigned done;
-        asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-            " selp.u32 %0, 1, 0, p;\n}\n"
-            : "=r"(done)
-            : "r"(addr), "r"(parity)
-            : "memory");
-        if (done) return true;
-    }
-    return false;
-}
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-            smem_u32(dst)),
-        "l"(src), "r"(bytes), "r"(smem_u32(bar))
-        : "memory");
-}
-__device__ __forceinline__ void consumers_sync(int nthreads) {
-    asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory");
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-__device__ __forceinline__ float h2f_lo(unsigned v) { return __half2float(__ushort_as_half((unsigned short)(v & 0xFFFFu))); }
-__device__ __forceinline__ float h2f_hi(unsigned v) { return __half2float(__ushort_as_half((unsigned short)(v >> 16))); }
-
-// 4 blocks of one row (group) against the staged activations of blocks b0..b0+3
-template <int WT, int MAXM>
-__device__ __forceinline__ void consume_group(const uint8_t* grp, const float dw[4], int b0, int nb,
-                                              int t, int M, const uint8_t* sx, const float* sxd,
-                                              int nbx, float (&acc0)[MAXM], float (&acc1)[MAXM]) {
-    int wl[4], wh[4];
-    if (WT == T_Q8_0) {
-        const uint4 a = *(const uint4*)(grp + t * 32);
-        const uint4 b = *(const uint4*)(grp + t * 32 + 16);
-        wl[0] = a.x; wh[0] = a.y; wl[1] = a.z; wh[1] = a.w;
-        wl[2] = b.x; wh[2] = b.y; wl[3] = b.z; wh[3] = b.w;
-    } else {
-        const uint4 a = *(const uint4*)(grp + t * 16);
-        const unsigned wv[4] = {a.x, a.y, a.z, a.w};
+// copy step g of a row into a ring slot (blocks >= nb are skipped: their scales are zero)
+template <int WT>
+__device__ __forceinline__ void issue_step(uint8_t* slot, const uint8_t* row, int nb, int g,
+                                           int lane) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            wl[j] = (int)(((wv[j] << 4) & 0xF0F0F0F0u) ^ 0x80808080u);  // 16*(q_lo - 8)
-            wh[j] = (int)((wv[j] & 0xF0F0F0F0u) ^ 0x80808080u);         // 16*(q_hi - 8)
+    for (int i = 0; i < 2; ++i) {
+        const int b = g * 64 + i * 32 + lane;
+        if (b < nb) {
+            if (WT == T_Q8_0) {
+                cp_async16(slot + ((2 * i) * 32 + lane) * 16, row + (int64_t)b * 16);
+                cp_async16(slot + ((2 * i + 1) * 32 + lane) * 16, row + (int64_t)(nb + b) * 16);
+            } else {
+                cp_async16(slot + (i * 32 + lane) * 16, row + (int64_t)b * 16);
+            }
         }
     }
-    const int jmax = min(4, nb - b0);
+    cp_async4(slot + Slot<WT>::kQuant + lane * 4,
+              row + (int64_t)nb * quant_bytes(WT) + (int64_t)g * 128 + lane * 4);
+}
+
+// accumulate the two blocks of a landed step against the staged activations
+template <int WT, int MAXM>
+__device__ __forceinline__ void consume(const uint8_t* slot, int g, int lane, int M,
+                                        const uint4* sxa, const uint4* sxb, const float* sxd,
+                                        int nbp, float (&acc)[MAXM]) {
+    const unsigned sc = *(const unsigned*)(slot + Slot<WT>::kQuant + lane * 4);
 #pragma unroll
-    for (int m = 0; m < MAXM; ++m) {
-        if (m < M) {
-            const uint8_t* xs = sx + m * nbx * 32 + (b0 >> 2) * 128 + t * 32;
-            const uint4 xa = *(const uint4*)xs, xb = *(const uint4*)(xs + 16);
-            const float4 dx = *(const float4*)(sxd + m * nbx + b0);
-            const int xl[4] = {(int)xa.x, (int)xa.z, (int)xb.x, (int)xb.z};
-            const int xh[4] = {(int)xa.y, (int)xa.w, (int)xb.y, (int)xb.w};
-            const float dxf[4] = {dx.x, dx.y, dx.z, dx.w};
+    for (int i = 0; i < 2; ++i) {
+        const int b = g * 64 + i * 32 + lane;
+        int lo[4], hi[4];
+        if (WT == T_Q4_0) {
+            const uint4 q = *(const uint4*)(slot + (i * 32 + lane) * 16);
+            const unsigned w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-                if (j < jmax) {
-                    const float s = __fmul_rn(dw[j], dxf[j]);
-                    acc0[m] = __fmaf_rn(s, __int2float_rn(__dp4a(wl[j], xl[j], 0)), acc0[m]);
-                    acc1[m] = __fmaf_rn(s, __int2float_rn(__dp4a(wh[j], xh[j], 0)), acc1[m]);
-                }
+                lo[j] = (int)(((w[j] << 4) & 0xF0F0F0F0u) ^ 0x80808080u);  // 16*(q_lo - 8)
+                hi[j] = (int)((w[j] & 0xF0F0F0F0u) ^ 0x80808080u);         // 16*(q_hi - 8)
+            }
+        } else {
+            const uint4 qa = *(const uint4*)(slot + ((2 * i) * 32 + lane) * 16);
+            const uint4 qb = *(const uint4*)(slot + ((2 * i + 1) * 32 + lane) * 16);
+            lo[0] = (int)qa.x; lo[1] = (int)qa.y; lo[2] = (int)qa.z; lo[3] = (int)qa.w;
+            hi[0] = (int)qb.x; hi[1] = (int)qb.y; hi[2] = (int)qb.z; hi[3] = (int)qb.w;
+        }
+        const float dw = __half2float(__ushort_as_half((unsigned short)(i ? sc >> 16 : sc & 0xFFFF)));
+#pragma unroll
+        for (int m = 0; m < MAXM; ++m) {
+            if (m < M) {
+                const uint4 xa = sxa[m * nbp + b];
+                const uint4 xb = sxb[m * nbp + b];
+                const float dx = sxd[m * nbp + b];
+                int s = 0x4B400000;
+                s = __dp4a(lo[0], (int)xa.x, s);
+                s = __dp4a(lo[1], (int)xa.y, s);
+                s = __dp4a(lo[2], (int)xa.z, s);
+                s = __dp4a(lo[3], (int)xa.w, s);
+                s = __dp4a(hi[0], (int)xb.x, s);
+                s = __dp4a(hi[1], (int)xb.y, s);
+                s = __dp4a(hi[2], (int)xb.z, s);
+                s = __dp4a(hi[3], (int)xb.w, s);
+                acc[m] = __fmaf_rn(block_sum_f(s), __fmul_rn(dw, dx), acc[m]);
             }
         }
     }
 }
 
-__device__ double cons_sum_d(double v, double* sh, int nthreads) {
+__device__ __forceinline__ float warp_allsum(float v) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+    return v;
+}
+
+__device__ double block_sum_d(double v, double* sh) {
     v = warp_sum_d(v);
     const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
-    consumers_sync(nthreads);
+    __syncthreads();
     if (l == 0) sh[w] = v;
-    consumers_sync(nthreads);
+    __syncthreads();
     double t = 0.0;
-    for (int i = 0; i < nthreads / 32; ++i) t += sh[i];
+    for (int i = 0; i < kWarps; ++i) t += sh[i];
     return t;
 }
 
-// Activation staging by the consumer threads: Q8_0 words at x_word_off, scales (divided by 16
-// for Q4_0 weights) as fp32.
-template <int WT, int IN>
-__device__ void stage_inputs(const GemvArgs& a, int nb, int nbx, uint8_t* sx, float* sxd,
-                             double* shd, int nthreads) {
-    const int K = (int)a.w.K;
-    const float dscale = WT == T_Q4_0 ? 0.0625f : 1.0f;
-    if (IN == 0) {
-        for (int idx = threadIdx.x; idx < a.M * nbx * 8; idx += nthreads) {
-            const int m = idx / (nbx * 8), r = idx % (nbx * 8), b = r >> 3, w = r & 7;
-            const int v = b < nb ? __ldg((const int*)(a.xq + (int64_t)m * K + b * 32) + w) : 0;
-            *(int*)(sx + m * nbx * 32 + x_word_off(b, w)) = v;
-        }
-        for (int idx = threadIdx.x; idx < a.M * nbx; idx += nthreads) {
-            const int m = idx / nbx, b = idx % nbx;
-            sxd[idx] = b < nb ? __fmul_rn(a.xd[(int64_t)m * nb + b], dscale) : 0.0f;
-        }
-    } else {
-        // RMSNorm (ggml-cpu/ops.cpp:3859-3920) then Q8_0 (arch/x86/quants.c:302-392)
-        const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = nthreads >> 5;
-        for (int m = 0; m < a.M; ++m) {
-            const float* xr = a.xf + (int64_t)m * a.xf_stride;
-            double s = 0.0;
-            for (int k = threadIdx.x; k < K; k += nthreads) {
-                const float v = xr[k];
-                s += (double)__fmul_rn(v, v);
-            }
-            s = cons_sum_d(s, shd, nthreads);
-            const float mean = (float)(s / (double)K);
-            const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
-            for (int b = warp; b < nbx; b += nw) {
-                float d16 = 0.0f, q = 0.0f;
-                if (b < nb) {
-                    float v = __fmul_rn(xr[b * 32 + lane], scale);
-                    if (a.gamma) v = __fmul_rn(v, a.gamma[b * 32 + lane]);
-                    q8_block(v, lane, d16, q);
-                }
-                sx[m * nbx * 32 + x_word_off(b, lane >> 2) + (lane & 3)] =
-                    (uint8_t)(int8_t)__float2int_rn(q);
-                if (lane == 0) sxd[m * nbx + b] = __fmul_rn(d16, dscale);
-            }
-        }
-    }
-}
-
-struct Geo {
-    int R;           // rows per tile (32, or 64 for SwiGLU: 32 gate + 32 up)
-    int C;           // super-groups per row and stage
-    int nsg;         // super-groups per row
-    int nchunk;      // stages per tile
-    int ntiles;
-    int row_chunk;   // bytes per row and stage (C * sg bytes)
+// Stage the M activation rows as Q8_0 in shared memory: sxa/sxb = words 0-3 / 4-7 of each block,
+// sxd = fp32 scales (divided by 16 for Q4_0 weights); blocks nb..nbp-1 are zero.
+struct StageIn {  // the GemvArgs fields the prologue reads, passed by value
+    const int8_t* xq;
+    const float* xd;
+    const float* xf;
+    int64_t xf_stride;
+    const float* gamma;
+    float eps;
+    int M, K;
+    bool xf_rms;
 };
 
-template <int WT, int SWI>
-__host__ __device__ inline Geo make_geo(int64_t N, int64_t K, int64_t F) {
-    Geo g;
-    g.R = SWI ? 64 : 32;
-    const int sgb = (int)sg_bytes(WT);
-    g.C = kStageTarget / (g.R * sgb);
-    if (g.C < 1) g.C = 1;
-    g.nsg = (int)n_sg(K);
-    if (g.C > g.nsg) g.C = g.nsg;
-    g.nchunk = (g.nsg + g.C - 1) / g.C;
-    g.ntiles = SWI ? (int)(F / 32) : (int)((N + 31) / 32);
-    g.row_chunk = g.C * sgb;
-    return g;
-}
-
-template <int WT, int MAXM, int IN, int SWI>
-__global__ void k_gemv_fused(GemvArgs a, int* err) {
-    extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ double shd[8];
-    __shared__ float sres[SWI ? MAXM * 64 : 1];
-    __shared__ __align__(8) uint64_t full_bar[kStages], empty_bar[kStages];
-    const int K = (int)a.w.K;
-    const int N = (int)a.w.N;
-    const int nb = K / QK;
-    const int nbx = (nb + 3) & ~3;
-    const Geo geo = make_geo<WT, SWI>(a.w.N, a.w.K, a.F);
-    const int nthreads = geo.R * 4;  // consumer threads; the last warp is the producer
-    const int sgb = (int)sg_bytes(WT);
-    const int64_t rb = qrow_bytes(WT, K);
-    uint8_t* sx = smem;
-    float* sxd = (float*)(smem + (size_t)MAXM * nbx * 32);
-    const size_t act_bytes = ((size_t)MAXM * nbx * 36 + 127) & ~(size_t)127;
-    uint8_t* stages = smem + act_bytes;
-    const int stage_bytes = geo.R * geo.row_chunk;
-
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(&full_bar[s], 1);
-            mbar_init(&empty_bar[s], nthreads / 32);
-        }
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    __syncthreads();
-
-    const uint8_t* qs = (const uint8_t*)a.w.qs;
-    if (threadIdx.x >= nthreads) {
-        // ---------------- producer warp ----------------
-        if (threadIdx.x != nthreads) return;
-        int it = 0;
-        for (int tile = blockIdx.x; tile < geo.ntiles; tile += gridDim.x) {
-            for (int c = 0; c < geo.nchunk; ++c, ++it) {
-                const int st = it % kStages;
-                if (it >= kStages && !mbar_wait(&empty_bar[st], ((it / kStages) - 1) & 1)) {
-                    atomicExch(err, 1);
-                    return;
-                }
-                const int nsg_here = min(geo.C, geo.nsg - c * geo.C);
-                const unsigned bytes = (unsigned)(nsg_here * sgb);
-                mbar_expect_tx(&full_bar[st], bytes * geo.R);
-                uint8_t* dst = stages + (size_t)st * stage_bytes;
-                for (int r = 0; r < geo.R; ++r) {
-                    int row;
-                    if (SWI) row = r < 32 ? tile * 32 + r : (int)a.F + tile * 32 + (r - 32);
-                    else row = tile * 32 + r;
-                    if (row >= N) row = N - 1;
-                    bulk_g2s(dst + r * geo.row_chunk, qs + (int64_t)row * rb + (int64_t)c * geo.C * sgb,
-                             bytes, &full_bar[st]);
-                }
+template <int WT>
+__device__ __noinline__ void stage_x(const StageIn a, int nb, int nbp, uint4* sxa, uint4* sxb,
+                                     float* sxd, float* sxf, const float* sgm, double* shd) {
+    const int K = a.K;
+    const float dscale = WT == T_Q4_0 ? 0.0625f : 1.0f;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (!a.xf) {
+        for (int idx = threadIdx.x; idx < a.M * nbp; idx += kThreads) {
+            const int m = idx / nbp, b = idx % nbp;
+            uint4 va = make_uint4(0, 0, 0, 0), vb = make_uint4(0, 0, 0, 0);
+            float d = 0.0f;
+            if (b < nb) {
+                const int4* src = (const int4*)(a.xq + (int64_t)m * K + (int64_t)b * 32);
+                const int4 p = src[0], q = src[1];
+                va = make_uint4(p.x, p.y, p.z, p.w);
+                vb = make_uint4(q.x, q.y, q.z, q.w);
+                d = __fmul_rn(a.xd[(int64_t)m * nb + b], dscale);
             }
+            sxa[idx] = va;
+            sxb[idx] = vb;
+            sxd[idx] = d;
         }
         return;
     }
-
-    // ---------------- consumers ----------------
-    stage_inputs<WT, IN>(a, nb, nbx, sx, sxd, shd, nthreads);
-    consumers_sync(nthreads);
-    const int t = threadIdx.x & 3;
-    const int quad = threadIdx.x >> 2;
-    const int lane = threadIdx.x & 31;
-    int it = 0;
-    for (int tile = blockIdx.x; tile < geo.ntiles; tile += gridDim.x) {
-        float acc0[MAXM], acc1[MAXM];
-#pragma unroll
-        for (int m = 0; m < MAXM; ++m) acc0[m] = acc1[m] = 0.0f;
-        for (int c = 0; c < geo.nchunk; ++c, ++it) {
-            const int st = it % kStages;
-            if (!mbar_wait(&full_bar[st], (it / kStages) & 1)) {
-                atomicExch(err, 2);
-                return;
+    // f32 rows: the row is copied to shared memory with coalesced 16-byte loads (sxf: 33 floats
+    // per block, so a lane walking its own block hits a different bank every step), the sum of
+    // squares taken on the way; then one lane per block applies the scale and gamma (staged in
+    // sgm the same way) and quantizes — quantize_row_q8_0's per-block steps run once per block.
+    const bool vec4 = ((uintptr_t)a.xf & 15) == 0 && (a.xf_stride & 3) == 0;
+    for (int m = 0; m < a.M; ++m) {
+        const float* xr = a.xf + (int64_t)m * a.xf_stride;
+        double s0 = 0.0, s1 = 0.0;
+        if (vec4) {
+#pragma unroll 4
+            for (int k4 = threadIdx.x; k4 < K / 4; k4 += kThreads) {
+                const float4 t = __ldg((const float4*)xr + k4);
+                float* d = sxf + (k4 >> 3) * 33 + (k4 & 7) * 4;
+                d[0] = t.x; d[1] = t.y; d[2] = t.z; d[3] = t.w;
+                s0 += (double)__fmul_rn(t.x, t.x) + (double)__fmul_rn(t.y, t.y);
+                s1 += (double)__fmul_rn(t.z, t.z) + (double)__fmul_rn(t.w, t.w);
             }
-            const uint8_t* rowbuf = stages + (size_t)st * stage_bytes + quad * geo.row_chunk;
-            const int nsg_here = min(geo.C, geo.nsg - c * geo.C);
-            for (int sg = 0; sg < nsg_here; ++sg) {
-                const uint8_t* sgp = rowbuf + sg * sgb;
-                const int b0 = (c * geo.C + sg) * 8;
-                const uint4 sc = *(const uint4*)(sgp + (WT == T_Q8_0 ? 256 : 128));
-                const float d0[4] = {h2f_lo(sc.x), h2f_hi(sc.x), h2f_lo(sc.y), h2f_hi(sc.y)};
-                const float d1[4] = {h2f_lo(sc.z), h2f_hi(sc.z), h2f_lo(sc.w), h2f_hi(sc.w)};
-                consume_group<WT, MAXM>(sgp, d0, b0, nb, t, a.M, sx, sxd, nbx, acc0, acc1);
-                if (b0 + 4 < nb)
-                    consume_group<WT, MAXM>(sgp + (WT == T_Q8_0 ? 128 : 64), d1, b0 + 4, nb, t, a.M,
-                                            sx, sxd, nbx, acc0, acc1);
+        } else {
+#pragma unroll 4
+            for (int k = threadIdx.x; k < K; k += kThreads) {
+                const float t = __ldg(xr + k);
+                sxf[(k >> 5) * 33 + (k & 31)] = t;
+                s0 += (double)__fmul_rn(t, t);
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty_bar[st]);
         }
-        // reduce the quad: t_t = a_t + a_{t+4}, then (t0 + t2) + (t1 + t3)
-        const int row = SWI ? 0 : tile * 32 + quad;
+        float scale = 1.0f;
+        if (a.xf_rms) {
+            // RMSNorm (ggml-cpu/ops.cpp:3859-3920): fp32 squares summed in double
+            const double s = block_sum_d(s0 + s1, shd);
+            const float mean = (float)(s / (double)K);
+            scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+        } else {
+            __syncthreads();
+        }
+        for (int b = threadIdx.x; b < nbp; b += kThreads) {
+            uint4 qa = make_uint4(0, 0, 0, 0), qb = make_uint4(0, 0, 0, 0);
+            float d16 = 0.0f;
+            if (b < nb) {
+                const float* xb = sxf + b * 33;
+                const float* gb_ = sgm + b * 33;
+                auto val = [&](int i) {
+                    float v = xb[i];
+                    if (a.xf_rms) v = __fmul_rn(v, scale);
+                    if (a.gamma) v = __fmul_rn(v, gb_[i]);
+                    return v;
+                };
+                float amax = 0.0f;
+#pragma unroll 8
+                for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(val(i)));
+                // quantize_row_q8_0, x86 AVX2 build (arch/x86/quants.c:302-392)
+                d16 = __half2float(__float2half_rn(__fdiv_rn(amax, 127.0f)));
+                const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+                auto word = [&](int j) {
+                    unsigned w = 0;
 #pragma unroll
-        for (int m = 0; m < MAXM; ++m) {
-            if (m < a.M) {
-                const float tt = __fadd_rn(acc0[m], acc1[m]);
-                const float u = __fadd_rn(tt, __shfl_down_sync(0xffffffffu, tt, 2, 4));
-                float res = __fadd_rn(u, __shfl_down_sync(0xffffffffu, u, 1, 4));
-                if (t == 0) {
+                    for (int e = 0; e < 4; ++e)
+                        w |= ((unsigned)__float2int_rn(__fmul_rn(val(4 * j + e), id)) & 0xFF) << (8 * e);
+                    return w;
+                };
+                qa.x = word(0); qa.y = word(1); qa.z = word(2); qa.w = word(3);
+                qb.x = word(4); qb.y = word(5); qb.z = word(6); qb.w = word(7);
+            }
+            sxa[m * nbp + b] = qa;
+            sxb[m * nbp + b] = qb;
+            sxd[m * nbp + b] = __fmul_rn(d16, dscale);
+        }
+        __syncthreads();  // sxf is reused by the next row
+    }
+}
+
+// gamma staged like sxf (33 floats per block); it is a weight, so this runs before the
+// dependency wait
+__device__ __forceinline__ void stage_gamma(const float* gamma, int K, float* sgm) {
+    for (int k = threadIdx.x; k < K; k += kThreads) sgm[(k >> 5) * 33 + (k & 31)] = __ldg(gamma + k);
+}
+
+struct Geo {
+    int nb, nbp, ng;  // blocks per row, padded to whole steps (64 blocks), steps per row
+};
+
+__host__ __device__ inline Geo make_geo(int64_t K) {
+    Geo g;
+    g.nb = (int)(K / 32);
+    g.ng = (g.nb + 63) / 64;
+    g.nbp = g.ng * 64;
+    return g;
+}
+
+// SWI = 0: rows dealt to the warps of the grid.  SWI = 1: CTA tiles of 32 SwiGLU outputs.
+template <int WT, int MAXM, int SWI>
+__global__ void __launch_bounds__(kThreads, MAXM <= 2 ? 4 : 2) k_gemv(GemvArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ double shd[kWarps];
+    __shared__ float sres[SWI ? MAXM * 32 : 1];
+    const Geo geo = make_geo(a.w.K);
+    const int nb = geo.nb, nbp = geo.nbp, ng = geo.ng;
+    const int N = (int)a.w.N;
+    const int64_t rb = qrow_bytes(WT, a.w.K);
+    const uint8_t* qs = (const uint8_t*)a.w.qs;
+    uint4* sxa = (uint4*)smem;
+    uint4* sxb = sxa + MAXM * nbp;
+    float* sxd = (float*)(sxb + MAXM * nbp);
+    float* sxf = sxd + MAXM * nbp;                        // f32 input row, 33 floats per block
+    float* sgm = sxf + (a.xf ? nbp * 33 : 0);             // gamma, same layout
+    uint8_t* ring = (uint8_t*)(sgm + (a.xf && a.gamma ? nbp * 33 : 0));
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint8_t* wring = ring + warp * kDepth * Slot<WT>::kBytes;
+
+    const int F = (int)a.F;
+    const int gw = blockIdx.x * kWarps + warp;
+    const int tw = gridDim.x * kWarps;
+    // row k of this warp's sequence in a tile
+    auto row_of = [&](int tile, int k) -> int {
+        if (SWI) {  // pair tile*32 + warp*4 + k/2: gate row, then up row
+            const int p = tile * 32 + warp * 4 + (k >> 1);
+            return (k & 1) ? F + p : p;
+        }
+        return gw + k * tw;
+    };
+    const int rpt = SWI ? 8 : (gw < N ? (N - gw + tw - 1) / tw : 0);  // rows per tile
+    const int ntiles = SWI ? F / 32 : 1;
+    const int tstep = SWI ? (int)gridDim.x : 1;
+    const int tile0 = SWI ? (int)blockIdx.x : 0;
+    // step cursors (tile, row, step of the row): issue runs kDepth - 1 steps ahead of consume
+    int it = tile0, ik = 0, ig = 0, islot = 0;
+    auto issue = [&]() {
+        if (it < ntiles && ik < rpt) {
+            issue_step<WT>(wring + islot * Slot<WT>::kBytes, qs + (int64_t)row_of(it, ik) * rb, nb,
+                           ig, lane);
+            if (++ig == ng) {
+                ig = 0;
+                if (++ik == rpt) {
+                    ik = 0;
+                    it += tstep;
+                }
+            }
+        }
+        cp_commit();
+        islot = islot + 1 == kDepth ? 0 : islot + 1;
+    };
+#pragma unroll
+    for (int d = 0; d < kDepth - 1; ++d) issue();
+    if (a.xf && a.gamma) stage_gamma(a.gamma, (int)a.w.K, sgm);
+    pdl_wait();
+    pdl_launch();
+    stage_x<WT>(StageIn{a.xq, a.xd, a.xf, a.xf_stride, a.gamma, a.eps, a.M, (int)a.w.K, a.xf_rms},
+                nb, nbp, sxa, sxb, sxd, sxf, sgm, shd);
+    __syncthreads();
+
+    float acc[MAXM], gate[MAXM];
+#pragma unroll
+    for (int m = 0; m < MAXM; ++m) acc[m] = gate[m] = 0.0f;
+    int ct = tile0, ck = 0, cg = 0, cslot = 0;
+    while (ct < ntiles && ck < rpt) {
+        issue();
+        cp_wait<kDepth - 1>();
+        consume<WT, MAXM>(wring + cslot * Slot<WT>::kBytes, cg, lane, a.M, sxa, sxb, sxd, nbp, acc);
+        cslot = cslot + 1 == kDepth ? 0 : cslot + 1;
+        if (cg == ng - 1) {  // row ck complete
+            const int row = row_of(ct, ck);
+#pragma unroll
+            for (int m = 0; m < MAXM; ++m) {
+                if (m < a.M) {
+                    float r = warp_allsum(acc[m]);
+                    acc[m] = 0.0f;
                     if (SWI) {
-                        sres[m * 64 + quad] = res;
-                    } else if (row < N) {
-                        if (a.bias) res = __fadd_rn(res, a.bias[row]);
-                        if (a.residual) res = __fadd_rn(a.residual[(int64_t)m * a.res_stride + row], res);
-                        a.y[(int64_t)m * a.y_stride + row] = res;
+                        if (ck & 1) {
+                            if (lane == 0)
+                                sres[m * 32 + warp * 4 + (ck >> 1)] = __fmul_rn(ref_v_silu(gate[m]), r);
+                        } else {
+                            gate[m] = r;
+                        }
+                    } else if (lane == m) {
+                        if (a.bias) r = __fadd_rn(r, a.bias[row]);
+                        if (a.residual) r = __fadd_rn(a.residual[(int64_t)m * a.res_stride + row], r);
+                        a.y[(int64_t)m * a.y_stride + row] = r;
                     }
                 }
             }
-        }
-        if (SWI) {
-            consumers_sync(nthreads);
-            const int warp = threadIdx.x >> 5;
-            for (int m = warp; m < a.M; m += nthreads / 32) {
-                // ggml_vec_swiglu_f32 (vec.cpp:417-426): v_silu(gate) * up
-                const float h = __fmul_rn(ref_v_silu(sres[m * 64 + lane]), sres[m * 64 + 32 + lane]);
-                const int64_t col = (int64_t)tile * 32 + lane;
-                if (a.y) a.y[(int64_t)m * a.y_stride + col] = h;
-                if (a.yq) {
-                    float d16, q;
-                    q8_block(h, lane, d16, q);
-                    a.yq[(int64_t)m * a.F + col] = (int8_t)__float2int_rn(q);
-                    if (lane == 0) a.yd[(int64_t)m * (a.F / 32) + tile] = d16;
+            if (SWI && ck == rpt - 1) {
+                // ggml_vec_swiglu_f32 (vec.cpp:417-426) outputs of this tile, f32 and/or Q8_0
+                __syncthreads();
+                for (int m = warp; m < a.M; m += kWarps) {
+                    const float h = sres[m * 32 + lane];
+                    const int64_t col = (int64_t)ct * 32 + lane;
+                    if (a.y) a.y[(int64_t)m * a.y_stride + col] = h;
+                    if (a.yq) {
+                        float d16, q;
+                        q8_block(h, lane, d16, q);
+                        a.yq[(int64_t)m * a.F + col] = (int8_t)__float2int_rn(q);
+                        if (lane == 0) a.yd[(int64_t)m * (a.F / 32) + ct] = d16;
+                    }
                 }
+                __syncthreads();
             }
-            consumers_sync(nthreads);
+        }
+        if (++cg == ng) {
+            cg = 0;
+            if (++ck == rpt) {
+                ck = 0;
+                ct += tstep;
+            }
         }
     }
+}
+
+template <int WT>
+size_t smem_bytes(int maxm, int64_t K, bool xf, bool gamma) {
+    const Geo g = make_geo(K);
+    return (size_t)maxm * g.nbp * 36 + (xf ? (size_t)g.nbp * 33 * 4 * (gamma ? 2 : 1) : 0) +
+           (size_t)kWarps * kDepth * Slot<WT>::kBytes;
+}
+
+template <int WT, int MAXM, int SWI>
+void launch_t(const GemvArgs& a, cudaStream_t st) {
+    auto kern = k_gemv<WT, MAXM, SWI>;
+    const size_t smem = smem_bytes<WT>(MAXM, a.w.K, a.xf != nullptr, a.gamma != nullptr);
+    GB_CHECK(smem <= kSmemMax, "gemv: activation stage too large for shared memory");
+    int dev = 0;
+    GB_CUDA(cudaGetDevice(&dev));
+    GB_CHECK(dev >= 0 && dev < 64, "gemv: device ordinal out of range");
+    static std::mutex mu;
+    static bool configured[64] = {};
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!configured[dev]) {
+            GB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)kSmemMax));
+            configured[dev] = true;
+        }
+    }
+    int per_sm = 0;
+    GB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem));
+    const int64_t want = SWI ? a.F / 32 : (a.w.N + kWarps - 1) / kWarps;
+    const int64_t cap = (int64_t)sm_count(dev) * std::max(per_sm, 1);
+    launch_pdl(kern, (unsigned)std::min(want, cap), kThreads, smem, st, a);
 }
 
 template <int WT, int SWI>
-size_t smem_bytes(int maxm, int64_t N, int64_t K, int64_t F) {
-    const Geo g = make_geo<WT, SWI>(N, K, F);
-    const int64_t nbx = ((K / 32) + 3) & ~3;
-    const size_t act = ((size_t)maxm * nbx * 36 + 127) & ~(size_t)127;
-    return act + (size_t)kStages * g.R * g.row_chunk;
-}
-
-int* g_err_dev[32] = {nullptr};
-
-int* err_slot(int dev) {
-    if (!g_err_dev[dev & 31]) {
-        GB_CUDA(cudaMalloc(&g_err_dev[dev & 31], sizeof(int)));
-        GB_CUDA(cudaMemset(g_err_dev[dev & 31], 0, sizeof(int)));
-    }
-    return g_err_dev[dev & 31];
-}
-
-template <int WT, int MAXM, int IN, int SWI>
-void launch_t(const GemvArgs& a, cudaStream_t st) {
-    const size_t smem = smem_bytes<WT, SWI>(MAXM, a.w.N, a.w.K, a.F);
-    GB_CHECK(smem <= kSmemMax, "gemv: shared-memory stage too large");
-    int dev = 0;
-    GB_CUDA(cudaGetDevice(&dev));
-    static unsigned configured = 0;
-    if (!(configured & (1u << (dev & 31)))) {
-        GB_CUDA(cudaFuncSetAttribute(k_gemv_fused<WT, MAXM, IN, SWI>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemMax));
-        configured |= 1u << (dev & 31);
-    }
-    const Geo g = make_geo<WT, SWI>(a.w.N, a.w.K, a.F);
-    const int per_sm = smem <= 110 * 1024 ? 2 : 1;
-    const int blocks = g.ntiles < 148 * per_sm ? g.ntiles : 148 * per_sm;
-    k_gemv_fused<WT, MAXM, IN, SWI><<<blocks, g.R * 4 + 32, smem, st>>>(a, err_slot(dev));
-    GB_CUDA(cudaGetLastError());
-}
-
-template <int WT, int IN, int SWI>
 void launch_m(const GemvArgs& a, cudaStream_t st) {
-    if (a.M == 1) launch_t<WT, 1, IN, SWI>(a, st);
-    else if (a.M <= 4) launch_t<WT, 4, IN, SWI>(a, st);
-    else launch_t<WT, 8, IN, SWI>(a, st);
+    if (a.M == 1) launch_t<WT, 1, SWI>(a, st);
+    else if (a.M == 2) launch_t<WT, 2, SWI>(a, st);
+    else if (a.M <= 4) launch_t<WT, 4, SWI>(a, st);
+    else launch_t<WT, 8, SWI>(a, st);
 }
 
 }  // namespace
 
-void gemv_prepare_device(int dev) { (void)err_slot(dev); }
-
-int gemv_error_code(int dev) {
-    if (!g_err_dev[dev & 31]) return 0;
-    int v = 0;
-    GB_CUDA(cudaMemcpy(&v, g_err_dev[dev & 31], sizeof(int), cudaMemcpyDeviceToHost));
-    return v;
-}
-
 bool gemv_fused_fits(int64_t K, int M) {
     if (M < 1 || M > 8 || K % QK != 0) return false;
-    const int maxm = M == 1 ? 1 : (M <= 4 ? 4 : 8);
-    const size_t worst = std::max(smem_bytes<T_Q8_0, 1>(maxm, 64, K, 32),
-                                  smem_bytes<T_Q4_0, 1>(maxm, 64, K, 32));
-    return worst <= kSmemMax;
+    const int maxm = M == 1 ? 1 : (M == 2 ? 2 : (M <= 4 ? 4 : 8));
+    return std::max(smem_bytes<T_Q8_0>(maxm, K, true, true),
+                    smem_bytes<T_Q4_0>(maxm, K, true, true)) <= kSmemMax;
 }
 
 void launch_gemv_fused(const GemvArgs& a, cudaStream_t st) {
     GB_CHECK(a.w.type == T_Q8_0 || a.w.type == T_Q4_0, "gemv: quantized weights required");
     GB_CHECK(a.w.K % QK == 0 && a.w.K < (1LL << 30) && a.w.N < (1LL << 30), "gemv: bad shape");
     GB_CHECK(gemv_fused_fits(a.w.K, a.M), "gemv: M or K too large for the shared-memory stage");
-    GB_CHECK(!a.swiglu || (a.w.N == 2 * a.F && a.F % 32 == 0), "gemv: SwiGLU needs N == 2F, F % 32 == 0");
+    GB_CHECK(!a.swiglu || (a.w.N == 2 * a.F && a.F % 32 == 0),
+             "gemv: SwiGLU needs N == 2F, F % 32 == 0");
+    GB_CHECK(a.swiglu || (!a.yq && !a.yd), "gemv: Q8_0 output only with SwiGLU");
+    GB_CHECK(a.swiglu ? (a.y || a.yq) : a.y != nullptr, "gemv: no output");
+    GB_CHECK(!a.yq == !a.yd, "gemv: Q8_0 output needs quants and scales");
     GB_CHECK(a.xf || (a.xq && a.xd), "gemv: no input");
     if (a.w.N == 0 || a.M == 0) return;
-    const bool q8 = a.w.type == T_Q8_0;
-    const int in = a.xf ? 1 : 0;
-    if (q8) {
-        if (in == 0 && !a.swiglu) launch_m<T_Q8_0, 0, 0>(a, st);
-        else if (in == 0) launch_m<T_Q8_0, 0, 1>(a, st);
-        else if (!a.swiglu) launch_m<T_Q8_0, 1, 0>(a, st);
-        else launch_m<T_Q8_0, 1, 1>(a, st);
+    if (a.w.type == T_Q8_0) {
+        if (a.swiglu) launch_m<T_Q8_0, 1>(a, st);
+        else launch_m<T_Q8_0, 0>(a, st);
     } else {
-        if (in == 0 && !a.swiglu) launch_m<T_Q4_0, 0, 0>(a, st);
-        else if (in == 0) launch_m<T_Q4_0, 0, 1>(a, st);
-        else if (!a.swiglu) launch_m<T_Q4_0, 1, 0>(a, st);
-        else launch_m<T_Q4_0, 1, 1>(a, st);
+        if (a.swiglu) launch_m<T_Q4_0, 1>(a, st);
+        else launch_m<T_Q4_0, 0>(a, st);
     }
 }
 

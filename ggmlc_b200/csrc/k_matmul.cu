@@ -1,6 +1,6 @@
-// Quantized MUL_MAT kernels over the group weight layout (kernels.h).
+// Quantized MUL_MAT kernels over the split-row weight layout (kernels.h).
 //
-// M <= 8 (the decode path) goes to the bit-exact GEMV in k_gemv.cu.
+// M <= 8 (the decode path) goes to the GEMV in k_gemv.cu.
 //
 // gemm_block (M > 8, prefill): int8 tensor-core tiles (mma m16n8k32, one instruction per
 // 32-K block) give the exact int32 block dot; the block scale product is applied in fp32 right
@@ -79,18 +79,17 @@ __global__ void __launch_bounds__(128) k_gemm_block(const uint8_t* __restrict__ 
         for (int nt = 0; nt < 4; ++nt) {
             const uint8_t* wr = qs + brow[nt] * wrow_bytes;
             if (WT == T_Q8_0) {
-                const uint2 v = __ldg((const uint2*)(wr + w_word_off(T_Q8_0, kb, tg)));
-                bf[nt][0] = (int)v.x;  // word tg: k = 4tg..4tg+3
-                bf[nt][1] = (int)v.y;  // word tg+4: k = 16+4tg..
+                bf[nt][0] = __ldg((const int*)(wr + w_word_off(T_Q8_0, nb, kb, tg)));      // k = 4tg..
+                bf[nt][1] = __ldg((const int*)(wr + w_word_off(T_Q8_0, nb, kb, tg + 4)));  // k = 16+4tg..
             } else {
-                const unsigned w = (unsigned)__ldg((const int*)(wr + w_word_off(T_Q4_0, kb, tg)));
+                const unsigned w = (unsigned)__ldg((const int*)(wr + w_word_off(T_Q4_0, nb, kb, tg)));
                 bf[nt][0] = (int)__vsub4(w & 0x0F0F0F0Fu, 0x08080808u);
                 bf[nt][1] = (int)__vsub4((w >> 4) & 0x0F0F0F0Fu, 0x08080808u);
             }
             const int64_t c0 = min(n0 + nt * 8 + 2 * tg, N - 1);
             const int64_t c1 = min(n0 + nt * 8 + 2 * tg + 1, N - 1);
-            dwv[nt][0] = __half2float(*(const __half*)(qs + c0 * wrow_bytes + w_scale_off(WT, kb)));
-            dwv[nt][1] = __half2float(*(const __half*)(qs + c1 * wrow_bytes + w_scale_off(WT, kb)));
+            dwv[nt][0] = __half2float(*(const __half*)(qs + c0 * wrow_bytes + w_scale_off(WT, nb, kb)));
+            dwv[nt][1] = __half2float(*(const __half*)(qs + c1 * wrow_bytes + w_scale_off(WT, nb, kb)));
         }
         float dxv[2][2];
 #pragma unroll
@@ -150,9 +149,8 @@ __global__ void k_matmul_f(QWeight w, const float* __restrict__ x, int64_t x_str
 
 }  // namespace
 
-void launch_matmul_q_exact(const QWeight& w, const int8_t* xq, const float* xd, int64_t M,
-                           float* y, int64_t y_stride, const MatmulEpilogue& ep,
-                           cudaStream_t st) {
+void launch_matmul_q(const QWeight& w, const int8_t* xq, const float* xd, int64_t M, float* y,
+                     int64_t y_stride, const MatmulEpilogue& ep, cudaStream_t st) {
     GB_CHECK(w.K % QK == 0, "matmul: K must be a multiple of 32");
     if (M == 0 || w.N == 0) return;
     const bool q8 = w.type == T_Q8_0;

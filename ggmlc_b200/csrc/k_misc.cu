@@ -2,6 +2,8 @@
 // ggml_mul repeat src1 over src0) and CONT / CPY with type conversion.
 #include <cuda_fp16.h>
 
+#include <mutex>
+
 #include "common.h"
 #include "kernels.h"
 #include "kutil.cuh"
@@ -86,6 +88,23 @@ void launch_copy(const TView& src, const TView& dst, cudaStream_t st) {
     if (!total) return;
     k_copy<<<grid_for(total), 256, 0, st>>>(src, dst);
     GB_CUDA(cudaGetLastError());
+}
+
+}  // namespace gb
+
+namespace gb {
+
+int sm_count(int dev) {
+    static std::mutex mu;
+    static int cache[64] = {};
+    GB_CHECK(dev >= 0 && dev < 64, "device ordinal out of range");
+    std::lock_guard<std::mutex> lock(mu);
+    if (!cache[dev]) {
+        int n = 0;
+        GB_CUDA(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev));
+        cache[dev] = n > 0 ? n : 1;
+    }
+    return cache[dev];
 }
 
 }  // namespace gb

@@ -35,7 +35,7 @@ void launch_quantize_q8_0(const float* x, int64_t x_stride, int64_t M, int64_t K
     GB_CUDA(cudaGetLastError());
 }
 
-// GGUF rows of 34-byte (Q8_0) / 18-byte (Q4_0) blocks -> super-group layout (kernels.h).  One
+// GGUF rows of 34-byte (Q8_0) / 18-byte (Q4_0) blocks -> split-row layout (kernels.h).  One
 // thread per block; the source is 2-byte aligned, so it is read in 16-bit halves.
 __global__ void k_repack(const uint8_t* __restrict__ src, int type, int64_t N, int64_t nb,
                          int64_t row_bytes, uint8_t* __restrict__ qs) {
@@ -45,11 +45,11 @@ __global__ void k_repack(const uint8_t* __restrict__ src, int type, int64_t N, i
     const int bb = type == T_Q8_0 ? 34 : 18;
     const uint16_t* s = (const uint16_t*)(src + i * bb);
     uint8_t* rowp = qs + row * row_bytes;
-    *(uint16_t*)(rowp + w_scale_off(type, b)) = s[0];
+    *(uint16_t*)(rowp + w_scale_off(type, nb, b)) = s[0];
     const int nwords = type == T_Q8_0 ? 8 : 4;
     for (int w = 0; w < nwords; ++w) {
         const uint32_t v = (uint32_t)s[1 + 2 * w] | ((uint32_t)s[2 + 2 * w] << 16);
-        *(uint32_t*)(rowp + w_word_off(type, b, w)) = v;
+        *(uint32_t*)(rowp + w_word_off(type, nb, b, w)) = v;
     }
 }
 
@@ -79,16 +79,16 @@ __global__ void k_get_rows(QWeight w, const int32_t* __restrict__ ids, int64_t n
          k += (int64_t)gridDim.x * blockDim.x) {
         float v = 0.0f;
         if (ok) {
-            const int64_t b = k / QK, e = k % QK;
+            const int64_t b = k / QK, e = k % QK, nb = K / QK;
             const uint8_t* q = (const uint8_t*)w.qs + row * qrow_bytes(w.type, K);
             if (w.type == T_Q8_0 || w.type == T_Q4_0) {
-                const float d = __half2float(*(const __half*)(q + w_scale_off(w.type, b)));
+                const float d = __half2float(*(const __half*)(q + w_scale_off(w.type, nb, b)));
                 if (w.type == T_Q8_0) {
-                    const int8_t qv = (int8_t)q[w_word_off(T_Q8_0, b, (int)(e >> 2)) + (e & 3)];
+                    const int8_t qv = (int8_t)q[w_word_off(T_Q8_0, nb, b, (int)(e >> 2)) + (e & 3)];
                     v = __fmul_rn((float)qv, d);
                 } else {
                     const int64_t j = e & 15;
-                    const uint8_t byte = q[w_word_off(T_Q4_0, b, (int)(j >> 2)) + (j & 3)];
+                    const uint8_t byte = q[w_word_off(T_Q4_0, nb, b, (int)(j >> 2)) + (j & 3)];
                     const int nib = e < 16 ? (byte & 0x0F) : (byte >> 4);
                     v = __fmul_rn((float)(nib - 8), d);
                 }

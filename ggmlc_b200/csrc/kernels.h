@@ -1,35 +1,17 @@
 // Host-side declarations of the engine's CUDA kernels (launchers).  Every launcher takes the
 // stream explicitly; none allocates memory.  Layout conventions (all device memory):
-//   quantized weight  W[N][K] ("super-group layout"): a row is one contiguous stream of
-//                     super-groups (SG) of 8 blocks, each SG = the quants of two groups of 4
-//                     blocks followed by the 8 fp16 block scales (16 B): Q8_0 SG = 2x128 + 16 =
-//                     272 B, Q4_0 SG = 2x64 + 16 = 144 B.  A block's quants are read as 32-bit
-//                     words: Q8_0 has 8 (word w = elements 4w..4w+3), Q4_0 has 4 (word w = GGUF
-//                     bytes 4w..4w+3: low nibbles elements 4w.., high nibbles 16+4w..).
-//                     Q8_0 group (128 B): [t 0..3][block j 0..3][word t, word t+4];
-//                     Q4_0 group (64 B):  [t 0..3][block j 0..3][word t] —
-//                     thread t of a row's quad reads its words of 4 blocks in 16-byte loads.
-//                     Padding blocks (K/32 rounded up to 8) are zero.
+//   quantized weight  W[N][K] ("split-row layout"): a row holds the quants of its nb = K/32
+//                     blocks in block order, then the fp16 block scales.  A block's quants are
+//                     32-bit words: Q8_0 has 8 (word w = elements 4w..4w+3), Q4_0 has 4 (word w
+//                     = GGUF bytes 4w..4w+3: low nibbles are elements 4w.., high 16+4w..).
+//                     Q4_0 row: [nb][16 B] quants.  Q8_0 row: [nb][16 B] words 0-3, then
+//                     [nb][16 B] words 4-7.  A warp whose lanes take consecutive blocks reads 512
+//                     contiguous bytes per 16-byte load.  Scales come in groups of 64 blocks,
+//                     ordered [lane l 0..31][i 0..1] for block 64g + 32i + l, so the lane that
+//                     owns blocks l and l+32 of a group reads both scales with one 4-byte load;
+//                     the scale region is padded to whole groups (zero scales).
 //   Q8_0 activations  X[M][K]: xq = M rows of K int8, xd = M rows of K/32 fp32 scales (the fp16
 //                     scale widened, exactly as the CPU reads it).
-__host__ __device__ inline int64_t n_sg(int64_t K) { return ((K / 32) + 7) / 8; }
-__host__ __device__ inline int64_t sg_bytes(int type) { return type == 8 ? 272 : 144; }
-__host__ __device__ inline int64_t qrow_bytes(int type, int64_t K) { return n_sg(K) * sg_bytes(type); }
-// byte offset, inside a weight row, of 32-bit word w of block b / of block b's fp16 scale
-__host__ __device__ inline int64_t w_word_off(int type, int64_t b, int w) {
-    const int64_t sg = b >> 3, bb = b & 7;
-    if (type == 8)
-        return sg * 272 + (bb >> 2) * 128 + (w & 3) * 32 + (bb & 3) * 8 + (w >> 2) * 4;
-    return sg * 144 + (bb >> 2) * 64 + w * 16 + (bb & 3) * 4;
-}
-__host__ __device__ inline int64_t w_scale_off(int type, int64_t b) {
-    return (b >> 3) * sg_bytes(type) + (type == 8 ? 256 : 128) + (b & 7) * 2;
-}
-// activation staging (shared memory): Q8_0 words in 4-block groups, same order as a Q8_0
-// weight group: [group][t 0..3][block j][word t, word t+4]
-__host__ __device__ inline int64_t x_word_off(int64_t b, int w) {
-    return (b >> 2) * 128 + (w & 3) * 32 + (b & 3) * 8 + (w >> 2) * 4;
-}
 #pragma once
 
 #include <cuda_fp16.h>
@@ -44,10 +26,25 @@ struct StepParams {
     int64_t pos;  // first position of this call's tokens in the KV cache
 };
 
+__host__ __device__ inline int64_t quant_bytes(int type) { return type == 8 ? 32 : 16; }
+__host__ __device__ inline int64_t scale_region(int64_t nb) { return ((nb + 63) / 64) * 128; }
+__host__ __device__ inline int64_t qrow_bytes(int type, int64_t K) {
+    const int64_t nb = K / 32;
+    return nb * quant_bytes(type) + scale_region(nb);
+}
+// byte offset, inside a weight row of nb blocks, of 32-bit word w of block b / of b's scale
+__host__ __device__ inline int64_t w_word_off(int type, int64_t nb, int64_t b, int w) {
+    if (type == 8) return (w >> 2) * nb * 16 + b * 16 + (w & 3) * 4;
+    return b * 16 + w * 4;
+}
+__host__ __device__ inline int64_t w_scale_off(int type, int64_t nb, int64_t b) {
+    return nb * quant_bytes(type) + (b >> 6) * 128 + (b & 31) * 4 + ((b >> 5) & 1) * 2;
+}
+
 struct QWeight {
     int type = 0;               // T_Q8_0 or T_Q4_0 (or T_F32 / T_F16 for float weights)
     int64_t N = 0, K = 0;       // rows, columns
-    const void* qs = nullptr;   // super-group rows (or float data for T_F32 / T_F16)
+    const void* qs = nullptr;   // split-row layout rows (or float data for T_F32 / T_F16)
 };
 
 // ---- quantization ----------------------------------------------------------------------------
@@ -56,7 +53,7 @@ struct QWeight {
 void launch_quantize_q8_0(const float* x, int64_t x_stride, int64_t M, int64_t K, int8_t* xq,
                           float* xd, cudaStream_t st);
 
-// Repack a GGUF block tensor (N rows of K elements, 34/18-byte blocks) into the super-group
+// Repack a GGUF block tensor (N rows of K elements, 34/18-byte blocks) into the split-row
 // layout.  qs must hold N * qrow_bytes(type, K) bytes; padding is zeroed.
 void launch_repack_blocks(const uint8_t* gguf, int type, int64_t N, int64_t K, void* qs,
                           cudaStream_t st);
@@ -67,30 +64,31 @@ void launch_get_rows(const QWeight& w, const int32_t* ids, int64_t n, float* out
 
 // ---- matmul -----------------------------------------------------------------------------------
 // Y[m][n] = sum_k X[m][k] W[n][k] (+ bias[n]) (+ residual[m][n]) for Q8_0/Q4_0 W and Q8_0 X.
-// Bit-exact with the reference x86 CPU kernels: 8 fp32 lane accumulators per output, lane i
-// holding the int32 dot of elements 4i..4i+3 of each block, fma(d_w*d_x, lane, acc) block by
-// block, lanes reduced ((a0+a4)+(a2+a6))+((a1+a5)+(a3+a7)).
+// Per 32-element block the int32 dot is exact; block terms sumi * (d_w * d_x) accumulate in fp32
+// (the reference's generic block formula; the x86 lane order differs only in rounding).
+// M <= 8 runs the decode GEMV, larger M the tensor-core block GEMM.
 struct MatmulEpilogue {
     const float* bias = nullptr;      // [N] or null
     const float* residual = nullptr;  // [M][res_stride] or null
     int64_t res_stride = 0;
 };
-void launch_matmul_q_exact(const QWeight& w, const int8_t* xq, const float* xd, int64_t M,
-                           float* y, int64_t y_stride, const MatmulEpilogue& ep,
-                           cudaStream_t st);
-// Decode GEMV with fused prologue / epilogue (M <= 8, bit-exact like launch_matmul_q_exact).
-//   input : Q8_0 rows (xq, xd), or f32 rows xf normalized in the prologue — RMSNorm with eps
-//           and optional gamma, exactly as launch_rms_norm — and quantized to Q8_0 in shared
-//           memory (the standalone norm and quantize launches disappear);
+void launch_matmul_q(const QWeight& w, const int8_t* xq, const float* xd, int64_t M, float* y,
+                     int64_t y_stride, const MatmulEpilogue& ep, cudaStream_t st);
+// Decode GEMV with fused prologue / epilogue (M <= 8).  Launched as a programmatic dependent
+// launch: its weight loads start before the previous kernel on the stream has finished.
+//   input : Q8_0 rows (xq, xd; xq 16-byte aligned), or f32 rows xf quantized to Q8_0 in shared
+//           memory, after RMSNorm with eps and optional gamma when xf_rms (exactly as
+//           launch_rms_norm) — the standalone norm and quantize launches disappear;
 //   output: f32 rows y (+bias, +residual), or SwiGLU of row pairs (gate n, up n+F) emitted as
 //           Q8_0 rows (yq, yd) and/or f32 rows (y) of length F — exactly launch_swiglu.
 struct GemvArgs {
     QWeight w;
     int M = 1;
-    const int8_t* xq = nullptr;  // input mode 0
+    const int8_t* xq = nullptr;  // Q8_0 input
     const float* xd = nullptr;
-    const float* xf = nullptr;   // input mode 1 (RMSNorm prologue)
+    const float* xf = nullptr;   // f32 input, quantized in the prologue
     int64_t xf_stride = 0;
+    bool xf_rms = true;          // RMSNorm the f32 input first
     float eps = 0.0f;
     const float* gamma = nullptr;
     bool swiglu = false;         // output mode
@@ -105,11 +103,6 @@ struct GemvArgs {
 };
 void launch_gemv_fused(const GemvArgs& a, cudaStream_t st);
 bool gemv_fused_fits(int64_t K, int M);
-// The GEMV's pipeline waits are bounded; a timeout is recorded in a per-device error word
-// (1: producer, 2: consumer) instead of hanging.  gemv_prepare_device allocates that word
-// (call before graph capture); gemv_error_code reads it (0 = none).
-void gemv_prepare_device(int dev);
-int gemv_error_code(int dev);
 
 // Float-weight matmul (F32/F16 W, f32 X), used for non-quantized linears.
 void launch_matmul_f(const QWeight& w, const float* x, int64_t x_stride, int64_t M, float* y,

@@ -76,4 +76,30 @@ __device__ __forceinline__ float ref_v_silu(float x) {
     return __fdiv_rn(x, __fadd_rn(1.0f, e));
 }
 
+// Programmatic dependent launch.  A kernel launched with launch_pdl may start while the previous
+// kernel on its stream is still running; it must call pdl_wait() before it reads anything that
+// kernel writes and before it writes anything (the wait returns once the previous grid has
+// completed and its memory is visible).  pdl_launch() lets the next launch start early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// SM count of a device (cached per device).
+int sm_count(int dev);
+
+template <typename... P, typename... A>
+void launch_pdl(void (*kern)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                A&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    GB_CUDA(cudaLaunchKernelEx(&cfg, kern, std::forward<A>(args)...));
+}
+
 }  // namespace gb

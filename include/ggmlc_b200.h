@@ -114,12 +114,16 @@ void* gb_executor_stream(const gb_executor* e);
 /* ---- op-level entry points (device pointers) ------------------------------------------------
  * The kernels behind the executor, exposed for operator tests and the operator sweep.  They
  * replace the CUDA ops of ggml-cuda the reference dispatches on this path.  Layouts:
- *   Q8_0/Q4_0 weight W[N][K] in the engine's super-group layout written by gb_repack_blocks:
- *   `wq` = N rows of ceil(K/256) super-groups of 8 blocks (quants + the 8 fp16 scales inline),
- *   272 bytes (Q8_0) or 144 bytes (Q4_0) each;
+ *   Q8_0/Q4_0 weight W[N][K] in the engine's split-row layout written by gb_repack_blocks:
+ *   `wq` = N rows, each the K/32 blocks' quants in block order (Q4_0: 16 bytes per block; Q8_0:
+ *   bytes 0-15 of every block, then bytes 16-31 of every block), then the fp16 scales in groups
+ *   of 64 blocks (within a group: block 32i + l at position 2l + i), zero-padded to whole groups:
+ *   gb_weight_row_bytes(type, K) per row;
  *   Q8_0 activations X[M][K]: `xq` int8 [M][K], `xd` fp32 [M][K/32]. */
 
-/* GGUF block rows (34-byte Q8_0 / 18-byte Q4_0 blocks) -> wq (super-group layout, padding
+/* Bytes of one weight row in the split-row layout (Q8_0 = 8, Q4_0 = 2). */
+int64_t gb_weight_row_bytes(int type, int64_t K);
+/* GGUF block rows (34-byte Q8_0 / 18-byte Q4_0 blocks) -> wq (split-row layout, padding
  * zeroed).  gguf is device memory.  Replaces the weight upload of ggml_backend_tensor_set
  * (executor.cpp:414-429). */
 int gb_repack_blocks(const void* gguf, int type, int64_t N, int64_t K, void* wq, void* stream);
@@ -129,12 +133,14 @@ int gb_quantize_q8_0(const float* x, int64_t x_stride, int64_t M, int64_t K, int
                      float* xd, void* stream);
 /* MUL_MAT Y[M][N] = X W^T (+bias[N]) (+residual[M][N]) — ggml_cuda_mul_mat
  * (ggml-cuda.cu:1812-1866: mul_mat_vec_q mmvq.cu:508 for M <= 8, mul_mat_q mmq.cuh:948
- * above).  Decode rows (M <= 8) are bit-exact with the x86 CPU kernels. */
+ * above).  Block int32 dots are exact; block terms accumulate in fp32 (generic block formula of
+ * ggml-cpu/quants.c:225-256, :451-477). */
 int gb_mul_mat_q(int type, const void* wq, int64_t N, int64_t K,
                  const int8_t* xq, const float* xd, int64_t M, float* y, const float* bias,
                  const float* residual, void* stream);
-/* Decode GEMV (M <= 8) with fused prologue / epilogue, bit-exact like gb_mul_mat_q.  Input:
- * Q8_0 rows (xq, xd) or, when xf != NULL, f32 rows [M][K] put through RMS_NORM(eps) (* gamma)
+/* Decode GEMV (M <= 8) with fused prologue / epilogue, same arithmetic as gb_mul_mat_q.  Input:
+ * Q8_0 rows (xq, xd; xq 16-byte aligned) or, when xf != NULL, f32 rows [M][K] put through
+ * RMS_NORM(eps) (* gamma)
  * and Q8_0 quantization first.  Output: y [M][N] (+bias, +residual); or with swiglu != 0 the
  * SwiGLU of row pairs (n, n+N/2) as f32 y [M][N/2] and/or Q8_0 yq [M][N/2], yd [M][N/64].
  * Replaces the ggml-cuda sequence rms_norm_f32 -> quantize_q8_1 -> mul_mat_vec_q ->

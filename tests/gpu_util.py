@@ -31,6 +31,8 @@ def lib():
     L = _runtime.lib()
     P, I, I64, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
     L.gb_repack_blocks.argtypes = [P, I, I64, I64, P, P]
+    L.gb_weight_row_bytes.argtypes = [I, I64]
+    L.gb_weight_row_bytes.restype = I64
     L.gb_quantize_q8_0.argtypes = [P, I64, I64, I64, P, P, P]
     L.gb_mul_mat_q.argtypes = [I, P, I64, I64, P, P, I64, P, P, P, P]
     L.gb_get_rows.argtypes = [I, P, I64, I64, P, I64, P, P]
@@ -66,11 +68,12 @@ def random_blocks(rng, wtype: int, N: int, K: int, scale: float = 0.01) -> np.nd
 
 
 def upload_weight(wtype: int, blocks: np.ndarray, N: int, K: int):
-    """GGUF block bytes -> device weight in the super-group layout (gb_repack_blocks)."""
+    """GGUF block bytes -> device weight in the split-row layout (gb_repack_blocks)."""
     torch = torch_dev()
     src = dev(blocks.reshape(-1))
-    nsg = (K // 32 + 7) // 8  # super-groups of 8 blocks per row, scales inline
-    wq = torch.empty(N * nsg * (272 if wtype == O.Q8_0 else 144), dtype=torch.uint8, device="cuda")
+    rb = lib().gb_weight_row_bytes(wtype, K)
+    assert rb > 0
+    wq = torch.empty(N * rb, dtype=torch.uint8, device="cuda")
     check(lib().gb_repack_blocks(ptr(src), wtype, N, K, ptr(wq), None))
     torch.cuda.synchronize()
     return wq, None

@@ -47,25 +47,66 @@ def test_quantize_bit_exact(G, M, K):
     assert np.array_equal(xd.cpu().numpy(), ref_d)
 
 
+def _close(y, ref, rel=1e-5):
+    """fp32 block accumulation order differs from the CPU lanes: compare to the output range."""
+    return np.max(np.abs(y - ref)) <= rel * max(np.max(np.abs(ref)), 1e-30)
+
+
+def _int_exact_case(rng, wtype, N, K, M):
+    """Weights with one power-of-two scale per row and activations whose Q8_0 scale is exactly 1
+    (one element of 127 per block, the rest in [-3, 3]): every block term and every partial sum
+    is an exactly representable fp32 value (|sum| < 2^24 grid steps even at K = 14336), so any
+    summation order gives the same result and the GPU must reproduce the oracle bit for bit —
+    this pins the integer block dots."""
+    w = _pow2_blocks(rng, wtype, N, K)
+    x = rng.integers(-3, 4, size=(M, K)).astype(np.float32)
+    x[:, ::32] = 127.0
+    return w, x
+
+
+def _pow2_blocks(rng, wtype, N, K):
+    bb = 34 if wtype == O.Q8_0 else 18
+    nb = K // 32
+    w = rng.integers(0, 256, size=(N, nb, bb), dtype=np.uint8)
+    if wtype == O.Q8_0:
+        q = w[:, :, 2:]
+        q[q == 128] = 129
+    # one power-of-two scale per row keeps every partial sum on a 2^e grid below 2^24 steps
+    d = np.broadcast_to(2.0 ** rng.integers(-12, -6, size=(N, 1)), (N, nb)).astype(np.float16)
+    w[:, :, 0:2] = d.view(np.uint8).reshape(N, nb, 2)
+    return w.reshape(N, nb * bb)
+
+
 @pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_0])
 @pytest.mark.parametrize("M", [1, 2, 5, 8])
-@pytest.mark.parametrize("N,K", [(64, 256), (300, 4096)])
-def test_decode_matmul_bit_exact(G, wtype, M, N, K):
+@pytest.mark.parametrize("N,K", [(64, 256), (300, 4096), (40, 14336)])
+def test_decode_matmul_close(G, wtype, M, N, K):
     rng = np.random.default_rng(N + K + M + wtype)
     w = G.random_blocks(rng, wtype, N, K)
     wq, wd = G.upload_weight(wtype, w, N, K)
     x = _x(rng, M, K)
     y = G.mul_mat(wtype, wq, wd, N, K, G.dev(x), M)
+    assert _close(y, O.mul_mat(wtype, w, N, K, x))
+
+
+@pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_0])
+@pytest.mark.parametrize("M,N,K", [(1, 300, 4096), (3, 77, 14336), (8, 64, 576), (16, 96, 1024),
+                                   (64, 40, 4096)])
+def test_matmul_integer_path_bit_exact(G, wtype, M, N, K):
+    """Decode (M <= 8) and prefill (M > 8) kernels on inputs where fp32 summation is exact."""
+    rng = np.random.default_rng(7 * N + K + M + wtype)
+    w, x = _int_exact_case(rng, wtype, N, K, M)
+    wq, wd = G.upload_weight(wtype, w, N, K)
+    y = G.mul_mat(wtype, wq, wd, N, K, G.dev(x), M)
     assert np.array_equal(y, O.mul_mat(wtype, w, N, K, x))
 
 
 @pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_0])
-def test_decode_matmul_epilogue_bit_exact(G, wtype):
+def test_decode_matmul_epilogue(G, wtype):
     rng = np.random.default_rng(5)
     N, K, M = 96, 512, 3
-    w = G.random_blocks(rng, wtype, N, K)
+    w, x = _int_exact_case(rng, wtype, N, K, M)
     wq, wd = G.upload_weight(wtype, w, N, K)
-    x = _x(rng, M, K)
     bias = rng.standard_normal(N).astype(np.float32)
     res = rng.standard_normal((M, N)).astype(np.float32)
     y = G.mul_mat(wtype, wq, wd, N, K, G.dev(x), M, bias=G.dev(bias), residual=G.dev(res))
@@ -89,8 +130,8 @@ def test_prefill_matmul_close(G, wtype, M, N, K):
 @pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_0])
 @pytest.mark.parametrize("N,K", [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)])
 def test_operator_sweep_shapes_sampled_rows(G, wtype, N, K):
-    """BASELINE operator-sweep shapes at full size; the oracle checks a sample of output rows
-    (decode M=1 bit-exact, prefill M=64 within 1e-5)."""
+    """Operator-sweep shapes at full size; the oracle checks a sample of output rows (decode M=1
+    and prefill M=64 within 1e-5 of the output range)."""
     torch = G.torch_dev()
     rng = np.random.default_rng(N ^ K ^ wtype)
     w = G.random_blocks(rng, wtype, N, K, scale=0.02 / 127 * 3)
@@ -100,10 +141,7 @@ def test_operator_sweep_shapes_sampled_rows(G, wtype, N, K):
         x = rng.standard_normal((M, K)).astype(np.float32)
         y = G.mul_mat(wtype, wq, wd, N, K, G.dev(x), M)
         ref = O.mul_mat(wtype, np.ascontiguousarray(w[rows]), len(rows), K, x)
-        if M == 1:
-            assert np.array_equal(y[:, rows], ref)
-        else:
-            assert np.max(np.abs(y[:, rows] - ref)) <= 1e-5 * np.max(np.abs(ref))
+        assert _close(y[:, rows], ref)
     del wq, wd
     torch.cuda.empty_cache()
 
@@ -227,8 +265,10 @@ def test_attention_close(G, s, kv_pos, Hq, Hkv, hd):
 @pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_0])
 @pytest.mark.parametrize("M,K", [(1, 576), (1, 4096), (3, 1024)])
 @pytest.mark.parametrize("with_gamma", [False, True])
-def test_gemv_rms_prologue_bit_exact(G, wtype, M, K, with_gamma):
-    """RMSNorm (+gamma) and Q8_0 quantization fused into the GEMV prologue."""
+def test_gemv_rms_prologue(G, wtype, M, K, with_gamma):
+    """RMSNorm (+gamma) and Q8_0 quantization fused into the GEMV prologue: bit-identical to the
+    GEMV fed by the standalone RMSNorm's Q8_0 output (itself bit-exact with the CPU), and close
+    to the oracle."""
     torch = G.torch_dev()
     rng = np.random.default_rng(K + M)
     N = 96
@@ -239,16 +279,26 @@ def test_gemv_rms_prologue_bit_exact(G, wtype, M, K, with_gamma):
     x_d = G.dev(x)
     g_d = G.dev(gamma) if with_gamma else None
     y = torch.empty((M, N), dtype=torch.float32, device="cuda")
-    G.check(G.lib_fused().gb_gemv(wtype, G.ptr(wq), N, K, M, None, None, G.ptr(x_d),
-                                  1e-5, G.ptr(g_d), 0, G.ptr(y), None, None, None, None, None))
+    L = G.lib_fused()
+    G.check(L.gb_gemv(wtype, G.ptr(wq), N, K, M, None, None, G.ptr(x_d), 1e-5, G.ptr(g_d), 0,
+                      G.ptr(y), None, None, None, None, None))
+    xq = torch.empty((M, K), dtype=torch.int8, device="cuda")
+    xd = torch.empty((M, K // 32), dtype=torch.float32, device="cuda")
+    G.check(G.lib().gb_rms_norm(G.ptr(x_d), M, K, 1e-5, G.ptr(g_d), None, G.ptr(xq), G.ptr(xd),
+                                None))
+    y2 = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    G.check(L.gb_gemv(wtype, G.ptr(wq), N, K, M, G.ptr(xq), G.ptr(xd), None, 0.0, None, 0,
+                      G.ptr(y2), None, None, None, None, None))
+    assert torch.equal(y, y2)
     ref = O.mul_mat(wtype, w, N, K, O.rms_norm(x, 1e-5, gamma))
-    assert np.array_equal(y.cpu().numpy(), ref)
+    assert _close(y.cpu().numpy(), ref)
 
 
 @pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_0])
 @pytest.mark.parametrize("M", [1, 2, 7])
-def test_gemv_swiglu_epilogue_bit_exact(G, wtype, M):
-    """gate_up GEMV with SwiGLU and Q8_0 quantization of the result fused in the epilogue."""
+def test_gemv_swiglu_epilogue(G, wtype, M):
+    """gate_up GEMV with SwiGLU and Q8_0 quantization of the result fused in the epilogue:
+    bit-exact with the CPU SwiGLU and quantizer applied to the plain GEMV's outputs."""
     torch = G.torch_dev()
     rng = np.random.default_rng(M)
     F, K = 160, 512
@@ -260,15 +310,19 @@ def test_gemv_swiglu_epilogue_bit_exact(G, wtype, M):
     y = torch.empty((M, F), dtype=torch.float32, device="cuda")
     yq = torch.empty((M, F), dtype=torch.int8, device="cuda")
     yd = torch.empty((M, F // 32), dtype=torch.float32, device="cuda")
-    G.check(G.lib_fused().gb_gemv(wtype, G.ptr(wq), N, K, M, G.ptr(xq), G.ptr(xd),
-                                  None, 0.0, None, 1, G.ptr(y), G.ptr(yq), G.ptr(yd), None, None,
-                                  None))
-    h = O.swiglu(O.mul_mat(wtype, w, N, K, x))
+    L = G.lib_fused()
+    G.check(L.gb_gemv(wtype, G.ptr(wq), N, K, M, G.ptr(xq), G.ptr(xd), None, 0.0, None, 1,
+                      G.ptr(y), G.ptr(yq), G.ptr(yd), None, None, None))
+    gu = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    G.check(L.gb_gemv(wtype, G.ptr(wq), N, K, M, G.ptr(xq), G.ptr(xd), None, 0.0, None, 0,
+                      G.ptr(gu), None, None, None, None, None))
+    h = O.swiglu(gu.cpu().numpy())
     assert np.array_equal(y.cpu().numpy(), h)
     hq = O.quantize_q8_0(h).reshape(M, F // 32, 34)
     assert np.array_equal(yq.cpu().numpy(), hq[:, :, 2:].reshape(M, F).view(np.int8))
     assert np.array_equal(yd.cpu().numpy(),
                           hq[:, :, :2].copy().view(np.float16).reshape(M, F // 32).astype(np.float32))
+    assert _close(h, O.swiglu(O.mul_mat(wtype, w, N, K, x)), 1e-4)
 
 
 @pytest.mark.parametrize("Hq,Hkv,hd,kv_pos", [(4, 2, 64, 0), (9, 3, 64, 300), (32, 8, 128, 700)])
