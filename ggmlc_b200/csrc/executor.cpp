@@ -446,7 +446,9 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                 needs(out, nf, nq);
                 const int64_t D = x.ne[0], M = x.nrows();
                 const bool rms_op = op.opcode == OP_RMS_NORM_C || op.opcode == OP_RMS_NORM;
-                if (rms_op && !nf && nq && M <= 8 && gemv_fused_fits(D, (int)M)) {
+                const bool fits = M >= 1 && gemv_fits(T_Q8_0, D, (int)M, true, gamma) &&
+                                  gemv_fits(T_Q4_0, D, (int)M, true, gamma);
+                if (rms_op && !nf && nq && M <= 8 && fits) {
                     // decode: every consumer is a quantized GEMV that normalizes in its prologue
                     o.has_f = false;
                     o.virt_rms = true;

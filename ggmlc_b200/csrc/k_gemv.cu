@@ -39,7 +39,7 @@ namespace {
 
 constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
-constexpr size_t kSmemMax = 200 * 1024;
+constexpr size_t kSmemMax = 224 * 1024;  // dynamic; static shared memory needs the rest of 227 KB
 
 __device__ __forceinline__ uint4 ldg_stream(const void* p) {
     uint4 v;
@@ -456,17 +456,24 @@ void launch_m(const GemvArgs& a, cudaStream_t st) {
 
 }  // namespace
 
-bool gemv_fused_fits(int64_t K, int M) {
+static int maxm_of(int M) { return M == 1 ? 1 : (M == 2 ? 2 : (M <= 4 ? 4 : 8)); }
+
+bool gemv_fits(int type, int64_t K, int M, bool staged, bool gamma) {
     if (M < 1 || M > 8 || K % QK != 0) return false;
-    const int maxm = M == 1 ? 1 : (M == 2 ? 2 : (M <= 4 ? 4 : 8));
-    return std::max(smem_bytes<T_Q8_0>(maxm, K, true, true),
-                    smem_bytes<T_Q4_0>(maxm, K, true, true)) <= kSmemMax;
+    const size_t b = type == T_Q8_0 ? smem_bytes<T_Q8_0>(maxm_of(M), K, staged, gamma)
+                                    : smem_bytes<T_Q4_0>(maxm_of(M), K, staged, gamma);
+    return b <= kSmemMax;
+}
+
+bool gemv_fused_fits(int64_t K, int M) {
+    return gemv_fits(T_Q8_0, K, M, false, false) && gemv_fits(T_Q4_0, K, M, false, false);
 }
 
 void launch_gemv_fused(const GemvArgs& a, cudaStream_t st) {
     GB_CHECK(a.w.type == T_Q8_0 || a.w.type == T_Q4_0, "gemv: quantized weights required");
     GB_CHECK(a.w.K % QK == 0 && a.w.K < (1LL << 30) && a.w.N < (1LL << 30), "gemv: bad shape");
-    GB_CHECK(gemv_fused_fits(a.w.K, a.M), "gemv: M or K too large for the shared-memory stage");
+    GB_CHECK(gemv_fits(a.w.type, a.w.K, a.M, a.xf != nullptr, a.gamma != nullptr),
+             "gemv: M or K too large for the shared-memory stage");
     GB_CHECK(!a.swiglu || (a.w.N == 2 * a.F && a.F % 32 == 0),
              "gemv: SwiGLU needs N == 2F, F % 32 == 0");
     GB_CHECK(a.swiglu || (!a.yq && !a.yd), "gemv: Q8_0 output only with SwiGLU");

@@ -102,6 +102,9 @@ struct GemvArgs {
     float* yd = nullptr;
 };
 void launch_gemv_fused(const GemvArgs& a, cudaStream_t st);
+// whether the GEMV's shared-memory stage fits: gemv_fits for one configuration (staged = f32
+// input, gamma = with gamma), gemv_fused_fits for Q8_0 input with either weight type
+bool gemv_fits(int type, int64_t K, int M, bool staged, bool gamma);
 bool gemv_fused_fits(int64_t K, int M);
 
 // Float-weight matmul (F32/F16 W, f32 X), used for non-quantized linears.
