@@ -46,6 +46,21 @@ def peaks() -> tuple[float, str]:
     return FALLBACK_HBM_GBS, "fallback"
 
 
+def profiled_traffic(kernel: str) -> float | None:
+    """DRAM bytes (read + write) per launch of `kernel` from the committed ncu summary
+    profiles/<kernel>_l8_decode.md (line `dram_bytes_per_launch: N`), or None."""
+    p = ROOT / "profiles" / f"{kernel}_l8_decode.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("dram_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1])
+            except ValueError:
+                return None
+    return None
+
+
 def model_path(model: str, quant: str) -> Path:
     return BENCH_DIR / f"{model}_{quant}.gguf"
 
@@ -305,11 +320,17 @@ def run_ours(args) -> None:
     kt_pp = ex.kernel_times()
     ex.set_kernel_timing(False)
     peak, peak_kind = peaks()
-    mm = kt.get("matmul_q", [0, 1, 0])
+    # dominant decode kernel by device time; its algorithmic bytes per launch (weights + Q8_0
+    # activations + outputs) over its mean launch duration
+    dom = max(kt.items(), key=lambda x: x[1][0])[0] if kt else "gemv_rms_swiglu"
+    mm = kt.get(dom, [0, 1, 0])
     achieved = mm[2] / (mm[0] / 1e3) / 1e9 if mm[0] > 0 else 0.0
+    gemv_all = [v for k, v in kt.items() if k.startswith("gemv")]
+    gemv_gbs = (sum(v[2] for v in gemv_all) / (sum(v[0] for v in gemv_all) / 1e3) / 1e9
+                if gemv_all else 0.0)
     dec_total = sum(v[0] for v in kt.values())
     shares = {k: round(v[0] / dec_total, 4) for k, v in sorted(kt.items(), key=lambda x: -x[1][0])}
-    pp_mm = kt_pp.get("matmul_q", [0, 1, 0])
+    pp_mm = kt_pp.get("gemm_q", [0, 1, 0])
 
     if rank == 0:
         cb = cpu_baseline(gguf) if (world == 1 and not args.no_cpu_baseline) else None
@@ -335,12 +356,13 @@ def run_ours(args) -> None:
             "e2e": {"value": round(e2e_tg, 2), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h,
                     "pp512_tokens_per_s": round(world * args.steps * P / (e2e_pp_ms / 1e3), 1)},
-            "roofline": {"bound": "hbm", "kernel": "matmul_q (decode GEMV, Q4_0 x Q8_0)",
+            "roofline": {"bound": "hbm", "kernel": dom,
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                         "traffic": None,
+                         "traffic": profiled_traffic(dom),
                          "bytes_per_launch": round(mm[2] / max(mm[1], 1)),
                          "launch_ms": round(mm[0] / max(mm[1], 1), 5),
+                         "all_decode_gemv_gbs": round(gemv_gbs, 1),
                          "decode_share": shares},
             "cpu_baseline": cb,
             "clocks": clk,
@@ -366,6 +388,95 @@ def pp_flops(model: str, P: int) -> float:
     return 2.0 * P * c.n_layers * per_layer + 2.0 * c.vocab * c.d_model
 
 
+# single-kernel cases at the L8 decode shapes, for ncu captures of one launch (--case NAME)
+CASES = {
+    "gemv_rms_swiglu": dict(N=28672, K=4096, mode="rms_swiglu"),  # gate_up + RMSNorm + SwiGLU
+    "gemv_rms": dict(N=6144, K=4096, mode="rms"),                 # qkv + RMSNorm prologue
+    "gemv_res": dict(N=4096, K=14336, mode="res"),                # down + residual
+    "attn_decode": dict(Hq=32, Hkv=8, hd=128, ctx=1024, pos=640),
+}
+
+
+def run_case(name: str, reps: int) -> None:
+    """Launch one decode kernel of the Llama-3-8B shapes `reps` times through the C ABI."""
+    import ctypes
+
+    import torch
+
+    from ggmlc_b200 import _runtime as R
+
+    L = R.lib()
+    P, I, I64, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
+    c = CASES[name]
+    rng = np.random.default_rng(0)
+    dev = torch.device("cuda", 0)
+    ptr = lambda t: 0 if t is None else int(t.data_ptr())  # noqa: E731
+
+    def check(rc):
+        if rc != 0:
+            raise RuntimeError(L.gb_last_error().decode())
+
+    if name.startswith("gemv"):
+        N, K = c["N"], c["K"]
+        nb = K // 32
+        blocks = rng.integers(0, 256, size=(N, nb, 18), dtype=np.uint8)
+        blocks[:, :, 0:2] = (rng.standard_normal((N, nb)) * 0.001).astype(np.float16) \
+            .view(np.uint8).reshape(N, nb, 2)
+        L.gb_weight_row_bytes.argtypes = [I, I64]
+        L.gb_weight_row_bytes.restype = I64
+        src = torch.from_numpy(blocks.reshape(-1)).to(dev)
+        wq = torch.empty(N * L.gb_weight_row_bytes(2, K), dtype=torch.uint8, device=dev)
+        L.gb_repack_blocks.argtypes = [P, I, I64, I64, P, P]
+        check(L.gb_repack_blocks(ptr(src), 2, N, K, ptr(wq), None))
+        x = torch.from_numpy(rng.standard_normal(K).astype(np.float32)).to(dev)
+        xq = torch.empty(K, dtype=torch.int8, device=dev)
+        xd = torch.empty(K // 32, dtype=torch.float32, device=dev)
+        L.gb_quantize_q8_0.argtypes = [P, I64, I64, I64, P, P, P]
+        check(L.gb_quantize_q8_0(ptr(x), K, 1, K, ptr(xq), ptr(xd), None))
+        res = torch.zeros(N, dtype=torch.float32, device=dev)
+        y = torch.empty(N, dtype=torch.float32, device=dev)
+        yq = torch.empty(N // 2, dtype=torch.int8, device=dev)
+        yd = torch.empty(N // 64, dtype=torch.float32, device=dev)
+        L.gb_gemv.argtypes = [I, P, I64, I64, I64, P, P, P, F, P, I, P, P, P, P, P, P]
+        mode = c["mode"]
+        for _ in range(reps):
+            if mode == "rms_swiglu":
+                rc = L.gb_gemv(2, ptr(wq), N, K, 1, None, None, ptr(x), 1e-5, None, 1, None,
+                               ptr(yq), ptr(yd), None, None, None)
+            elif mode == "rms":
+                rc = L.gb_gemv(2, ptr(wq), N, K, 1, None, None, ptr(x), 1e-5, None, 0, ptr(y),
+                               None, None, None, None, None)
+            else:
+                rc = L.gb_gemv(2, ptr(wq), N, K, 1, ptr(xq), ptr(xd), None, 0.0, None, 0, ptr(y),
+                               None, None, None, ptr(res), None)
+            check(rc)
+    else:
+        Hq, Hkv, hd, ctx, pos = c["Hq"], c["Hkv"], c["hd"], c["ctx"], c["pos"]
+        n_pos = 4096
+        tab = np.empty((n_pos, hd // 2, 2), np.float32)
+        L.gb_rope_table_fill.argtypes = [P, I64, I, F]
+        L.gb_rope_table_fill.restype = F
+        L.gb_rope_table_fill(tab.ctypes.data, n_pos, hd, 500000.0)
+        t_d = torch.from_numpy(tab).to(dev)
+        qkv = torch.from_numpy(rng.standard_normal((Hq + 2 * Hkv) * hd).astype(np.float32)).to(dev)
+        k = torch.randn(Hkv, ctx, hd, device=dev).half()
+        v = torch.randn(Hkv, ctx, hd, device=dev).half()
+        L.gb_attn_decode_workspace_bytes.argtypes = [I64, I64, I64, I64]
+        L.gb_attn_decode_workspace_bytes.restype = ctypes.c_size_t
+        work = torch.empty(int(L.gb_attn_decode_workspace_bytes(Hq, Hkv, hd, ctx)),
+                           dtype=torch.uint8, device=dev)
+        oq = torch.empty(Hq * hd, dtype=torch.int8, device=dev)
+        od = torch.empty(Hq * hd // 32, dtype=torch.float32, device=dev)
+        L.gb_attn_decode.argtypes = [P, I64, I64, I64, P, P, I64, I64, I, F, P, I64, F, P, P, P,
+                                     P, P]
+        for _ in range(reps):
+            check(L.gb_attn_decode(ptr(qkv), Hq, Hkv, hd, ptr(k), ptr(v), ctx, pos, hd, 500000.0,
+                                   ptr(t_d), n_pos, float(hd) ** -0.5, None, ptr(oq), ptr(od),
+                                   ptr(work), None))
+    torch.cuda.synchronize()
+    print(json.dumps({"case": name, "launches": reps, **c}))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -378,8 +489,13 @@ def main():
     ap.add_argument("--gen", type=int, default=128)
     ap.add_argument("--ref-gen", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--case", choices=sorted(CASES), help="launch one decode kernel of the L8 "
+                    "shapes (a small case for ncu) instead of the benchmark")
+    ap.add_argument("--reps", type=int, default=5)
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.case:
+        run_case(args.case, args.reps)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

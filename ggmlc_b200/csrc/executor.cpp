@@ -571,7 +571,7 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         }
                         const BufRef hr = h.ref, hq = h.q, hqd = h.qd;
                         const bool hf = h.has_f, hhq = h.has_q;
-                        add("matmul_q", [=](Program& p, cudaStream_t st) {
+                        add(virt ? "gemv_rms_swiglu" : "gemv_swiglu", [=](Program& p, cudaStream_t st) {
                             GemvArgs a = ga;
                             if (virt) {
                                 a.xf = (const float*)p.ptr(xr);
@@ -611,7 +611,7 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         pg.use(res.ref, add_op);
                     }
                     const BufRef yr = y.ref;
-                    add("matmul_q", [=](Program& p, cudaStream_t st) {
+                    add(virt ? "gemv_rms" : (add_op >= 0 ? "gemv_res" : "gemv"), [=](Program& p, cudaStream_t st) {
                         GemvArgs a = ga;
                         if (virt) {
                             a.xf = (const float*)p.ptr(xr);
@@ -668,7 +668,7 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         xl.has_q = false;
                         ensure_q(xl, oi);
                         const BufRef qb = xl.q, qdb = xl.qd;
-                        add("matmul_q", [=](Program& p, cudaStream_t st) {
+                        add("gemm_q", [=](Program& p, cudaStream_t st) {
                             MatmulEpilogue e = ep;
                             launch_matmul_q(*qw, (const int8_t*)p.ptr(qb),
                                                   (const float*)p.ptr(qdb), 1, (float*)p.ptr(yr),
@@ -677,7 +677,7 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                     } else {
                         ensure_q(xin, oi);
                         const BufRef qb = xin.q, qdb = xin.qd;
-                        add("matmul_q", [=](Program& p, cudaStream_t st) {
+                        add("gemm_q", [=](Program& p, cudaStream_t st) {
                             MatmulEpilogue e = ep;
                             if (rref.fixed || rref.buf >= 0) e.residual = (const float*)p.ptr(rref);
                             launch_matmul_q(*qw, (const int8_t*)p.ptr(qb),
@@ -1014,7 +1014,7 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         const BufRef yr = y.ref, yq = y.q, yqd = y.qd;
                         const bool hf = y.has_f, hq = y.has_q;
                         const double kvb = (double)Hkv * hd * 2 * 2;  // K+V bytes per position
-                        add("attention", [=](Program& p, cudaStream_t st) {
+                        add("attn_decode", [=](Program& p, cudaStream_t st) {
                             AttnDecArgs a = da;
                             a.qkv = (const float*)p.ptr(base);
                             a.part = (float*)p.ptr(wref);
