@@ -351,6 +351,8 @@ def run_ours(args) -> None:
             "pp512": {"value": round(pp_tps, 1), "unit": "tokens/s",
                       "ms": round(pp_ms / args.steps, 3),
                       "matmul_ms": round(pp_mm[0], 3),
+                      "kernel_ms": {k: round(v[0], 3) for k, v in
+                                    sorted(kt_pp.items(), key=lambda x: -x[1][0])},
                       "matmul_int8_tops": round(pp_flops(args.model, P) / (pp_mm[0] / 1e3) / 1e12, 1)
                       if pp_mm[0] else None},
             "e2e": {"value": round(e2e_tg, 2), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
@@ -394,6 +396,7 @@ CASES = {
     "gemv_rms": dict(N=6144, K=4096, mode="rms"),                 # qkv + RMSNorm prologue
     "gemv_res": dict(N=4096, K=14336, mode="res"),                # down + residual
     "attn_decode": dict(Hq=32, Hkv=8, hd=128, ctx=1024, pos=640),
+    "gemm_prefill": dict(N=28672, K=4096, M=512, mode="gemm"),    # gate_up at pp512
 }
 
 
@@ -416,7 +419,7 @@ def run_case(name: str, reps: int) -> None:
         if rc != 0:
             raise RuntimeError(L.gb_last_error().decode())
 
-    if name.startswith("gemv"):
+    if name.startswith("gemv") or name.startswith("gemm"):
         N, K = c["N"], c["K"]
         nb = K // 32
         blocks = rng.integers(0, 256, size=(N, nb, 18), dtype=np.uint8)
@@ -439,8 +442,19 @@ def run_case(name: str, reps: int) -> None:
         yd = torch.empty(N // 64, dtype=torch.float32, device=dev)
         L.gb_gemv.argtypes = [I, P, I64, I64, I64, P, P, P, F, P, I, P, P, P, P, P, P]
         mode = c["mode"]
+        if mode == "gemm":
+            M = c["M"]
+            xm = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).to(dev)
+            xq = torch.empty((M, K), dtype=torch.int8, device=dev)
+            xd = torch.empty((M, K // 32), dtype=torch.float32, device=dev)
+            check(L.gb_quantize_q8_0(ptr(xm), K, M, K, ptr(xq), ptr(xd), None))
+            ym = torch.empty((M, N), dtype=torch.float32, device=dev)
+            L.gb_mul_mat_q.argtypes = [I, P, I64, I64, P, P, I64, P, P, P, P]
         for _ in range(reps):
-            if mode == "rms_swiglu":
+            if mode == "gemm":
+                rc = L.gb_mul_mat_q(2, ptr(wq), N, K, ptr(xq), ptr(xd), M, ptr(ym), None, None,
+                                    None)
+            elif mode == "rms_swiglu":
                 rc = L.gb_gemv(2, ptr(wq), N, K, 1, None, None, ptr(x), 1e-5, None, 1, None,
                                ptr(yq), ptr(yd), None, None, None)
             elif mode == "rms":

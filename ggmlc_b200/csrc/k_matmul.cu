@@ -2,11 +2,13 @@
 //
 // M <= 8 (the decode path) goes to the GEMV in k_gemv.cu.
 //
-// gemm_block (M > 8, prefill): int8 tensor-core tiles (mma m16n8k32, one instruction per
+// k_gemm_q (M > 8, prefill): int8 tensor-core tiles (mma m16n8k32, one instruction per
 // 32-K block) give the exact int32 block dot; the block scale product is applied in fp32 right
 // after each block.  Integer block sums are exact; the fp32 summation order differs from the
-// CPU's lane order (within 1e-5 relative in tests/test_ops_gpu.py).
+// CPU's lane order.
 #include <cuda_fp16.h>
+
+#include <mutex>
 
 #include "common.h"
 #include "kernels.h"
@@ -16,112 +18,216 @@ namespace gb {
 
 namespace {
 
-// exact int -> float for |p| < 2^22 with one integer add and one fp32 add
-__device__ __forceinline__ float i2f_exact(int p) {
-    return __fsub_rn(__int_as_float(0x4B400000 + p), 12582912.0f);
-}
+// ---- block GEMM on int8 tensor cores (prefill, M > 8) -------------------------------------
+// CTA tile 128 activation rows (m) x 128 weight rows (n), 8 warps as 2 (m) x 4 (n), warp tile
+// 64 x 32.  K advances in stages of 4 blocks, streamed by cp.async through a 4-stage shared-memory
+// ring; fragments come from swizzled shared memory with ldmatrix.  Each 32-element block is one
+// mma.sync m16n8k32 (s8 x s8 -> exact s32 block dot) per 16x8 sub-tile, started from the
+// 1.5*2^23 bias so the int -> float conversion is one add; the block term is then scaled by
+// d_w * d_x and accumulated in fp32 registers.
+//
+// K order: a stage takes blocks {64g+2j, 64g+2j+1, 64g+32+2j, 64g+32+2j+1}, the order in which
+// the weight scale region stores them, so one 8-byte copy brings a row's four scales.
+constexpr int kBM = 128, kBN = 128, kGThreads = 256, kGStages = 4;
 
-// ---- block GEMM on int8 tensor cores (prefill) ----------------------------------------------
-// CTA tile 64 (activation rows m) x 64 (weight rows n), 4 warps each 32 x 32, one mma.sync
-// m16n8k32.s8 per 32-K block per 16x8 sub-tile; int32 block sums scaled into fp32 accumulators.
-__device__ __forceinline__ void mma_s8(int (&c)[4], const int (&a)[4], const int (&b)[2]) {
+template <int WT>
+struct GStage {
+    static constexpr int kRowB = WT == T_Q8_0 ? 128 : 64;  // weight bytes per row and stage
+    static constexpr int kA = kBM * 128;                    // activations: 4 blocks x 32 B per row
+    static constexpr int kB = kBN * kRowB;
+    static constexpr int kWs = kBN * 8;                     // 4 fp16 weight scales per row
+    static constexpr int kXs = kBM * 16;                    // 4 fp32 activation scales per row
+    static constexpr int kBytes = kA + kB + kWs + kXs;
+};
+
+__device__ __forceinline__ unsigned s_addr(const void* p) {
+    return (unsigned)__cvta_generic_to_shared(p);
+}
+// cp.async of `bytes` (4, 8 or 16) with zero fill when !valid
+template <int BYTES>
+__device__ __forceinline__ void cp_zfill(void* dst, const void* src, bool valid) {
+    const int n = valid ? BYTES : 0;
+    if (BYTES == 16)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s_addr(dst)), "l"(src),
+                     "r"(n)
+                     : "memory");
+    else
+        asm volatile("cp.async.ca.shared.global [%0], [%1], %2, %3;" ::"r"(s_addr(dst)), "l"(src),
+                     "n"(BYTES), "r"(n)
+                     : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(unsigned (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(s_addr(p)));
+}
+__device__ __forceinline__ void mma_s8(int (&d)[4], const unsigned (&a)[4], unsigned b0,
+                                       unsigned b1) {
     asm volatile(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
-        "{%8,%9}, {%0,%1,%2,%3};\n"
-        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
-        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+        "{%8,%9}, {%10,%10,%10,%10};\n"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0x4B400000));
 }
 
 template <int WT>
-__global__ void __launch_bounds__(128) k_gemm_block(const uint8_t* __restrict__ qs,
-                                                    int64_t N,
-                                                    int64_t K, const int8_t* __restrict__ xq,
-                                                    const float* __restrict__ xd, int64_t M,
-                                                    float* __restrict__ y, int64_t y_stride,
-                                                    MatmulEpilogue ep) {
-    const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+__global__ void __launch_bounds__(kGThreads, 1)
+    k_gemm_q(const uint8_t* __restrict__ qs, int N, int K, const int8_t* __restrict__ xq,
+             const float* __restrict__ xd, int M, float* __restrict__ y, int64_t y_stride,
+             MatmulEpilogue ep) {
+    extern __shared__ __align__(128) uint8_t gsm[];
+    using S = GStage<WT>;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, tg = lane & 3;
-    const int64_t m0 = (int64_t)blockIdx.y * 64 + (warp >> 1) * 32;
-    const int64_t n0 = (int64_t)blockIdx.x * 64 + (warp & 1) * 32;
-    const int64_t nb = K / QK;
-    const int64_t wrow_bytes = qrow_bytes(WT, K);
-    float acc[2][4][4];
-#pragma unroll
-    for (int a = 0; a < 2; ++a)
-#pragma unroll
-        for (int b = 0; b < 4; ++b)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) acc[a][b][c] = 0.0f;
-    int64_t arow[2][2];
-#pragma unroll
-    for (int mt = 0; mt < 2; ++mt) {
-        arow[mt][0] = min(m0 + mt * 16 + g, M - 1);
-        arow[mt][1] = min(m0 + mt * 16 + g + 8, M - 1);
-    }
-    int64_t brow[4];
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt) brow[nt] = min(n0 + nt * 8 + g, N - 1);
+    const int wm = warp >> 2, wn = warp & 3;
+    const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * kBN;
+    const int nb = K / QK;
+    const int ng = (nb + 63) / 64;
+    const int ns = 16 * (ng - 1) + min(16, (nb - 64 * (ng - 1) + 1) / 2);  // stages with a valid block
+    const int64_t rb = qrow_bytes(WT, K);
+    const int64_t scale_base = (int64_t)nb * quant_bytes(WT);
 
-    for (int64_t kb = 0; kb < nb; ++kb) {
-        int af[2][4];
-#pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-            const int8_t* r0 = xq + arow[mt][0] * K + kb * 32;
-            const int8_t* r1 = xq + arow[mt][1] * K + kb * 32;
-            af[mt][0] = __ldg((const int*)(r0 + 4 * tg));
-            af[mt][1] = __ldg((const int*)(r1 + 4 * tg));
-            af[mt][2] = __ldg((const int*)(r0 + 16 + 4 * tg));
-            af[mt][3] = __ldg((const int*)(r1 + 16 + 4 * tg));
+    // stage t: g = t / 16, j = t % 16; local block lb -> global block gblk(lb)
+    auto gblk = [&](int t, int lb) { return 64 * (t >> 4) + 2 * (t & 15) + (lb & 1) + 32 * (lb >> 1); };
+
+    auto load = [&](int t, int buf) {
+        uint8_t* st = gsm + buf * S::kBytes;
+        uint8_t* sA = st;
+        uint8_t* sB = sA + S::kA;
+        uint8_t* sW = sB + S::kB;
+        float* sX = (float*)(sW + S::kWs);
+        // activations: 128 rows x 8 chunks of 16 B (chunk c: local block c/2, half c%2)
+        for (int e = tid; e < kBM * 8; e += kGThreads) {
+            const int r = e >> 3, c = e & 7;
+            const int gb = gblk(t, c >> 1);
+            const int m = min(m0 + r, M - 1);
+            cp_zfill<16>(sA + r * 128 + ((c ^ (r & 7)) << 4),
+                         xq + (int64_t)m * K + (int64_t)gb * 32 + (c & 1) * 16, gb < nb);
         }
-        int bf[4][2];
-        float dwv[4][2];
+        for (int e = tid; e < kBM * 4; e += kGThreads) {
+            const int r = e >> 2, lb = e & 3;
+            const int gb = gblk(t, lb);
+            const int m = min(m0 + r, M - 1);
+            cp_zfill<4>(sX + r * 4 + lb, xd + (int64_t)m * nb + gb, gb < nb);
+        }
+        // weights: Q4_0 rows of 4 chunks (one per local block), Q8_0 rows of 8 (4 low, 4 high)
+        constexpr int CH = WT == T_Q8_0 ? 8 : 4;
+        for (int e = tid; e < kBN * CH; e += kGThreads) {
+            const int r = e / CH, c = e % CH;
+            const int lb = c & 3;
+            const int gb = gblk(t, lb);
+            const int n = min(n0 + r, N - 1);
+            const uint8_t* src = qs + (int64_t)n * rb + (int64_t)((c >> 2) * nb + gb) * 16;
+            const int phys = WT == T_Q8_0 ? (c ^ (r & 7)) : (c ^ ((r >> 1) & 3));
+            cp_zfill<16>(sB + r * S::kRowB + phys * 16, src, gb < nb);
+        }
+        for (int r = tid; r < kBN; r += kGThreads) {
+            const int n = min(n0 + r, N - 1);
+            cp_zfill<8>(sW + r * 8, qs + (int64_t)n * rb + scale_base + (t >> 4) * 128 + (t & 15) * 8,
+                        true);
+        }
+    };
+
+    float2 acc[4][4][2];  // [m16][n8][row g / g+8] x (col 2tg, 2tg+1)
 #pragma unroll
-        for (int nt = 0; nt < 4; ++nt) {
-            const uint8_t* wr = qs + brow[nt] * wrow_bytes;
-            if (WT == T_Q8_0) {
-                bf[nt][0] = __ldg((const int*)(wr + w_word_off(T_Q8_0, nb, kb, tg)));      // k = 4tg..
-                bf[nt][1] = __ldg((const int*)(wr + w_word_off(T_Q8_0, nb, kb, tg + 4)));  // k = 16+4tg..
-            } else {
-                const unsigned w = (unsigned)__ldg((const int*)(wr + w_word_off(T_Q4_0, nb, kb, tg)));
-                bf[nt][0] = (int)__vsub4(w & 0x0F0F0F0Fu, 0x08080808u);
-                bf[nt][1] = (int)__vsub4((w >> 4) & 0x0F0F0F0Fu, 0x08080808u);
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j][0] = acc[i][j][1] = make_float2(0.0f, 0.0f);
+
+#pragma unroll
+    for (int s = 0; s < kGStages - 1; ++s) {
+        if (s < ns) load(s, s);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    const float wsc = WT == T_Q4_0 ? 0.0625f : 1.0f;  // Q4_0 fragments hold 16 * (q - 8)
+    for (int t = 0; t < ns; ++t) {
+        asm volatile("cp.async.wait_group %0;" ::"n"(kGStages - 2) : "memory");
+        __syncthreads();
+        if (t + kGStages - 1 < ns) load(t + kGStages - 1, (t + kGStages - 1) % kGStages);
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        const uint8_t* st = gsm + (t % kGStages) * S::kBytes;
+        const uint8_t* sA = st;
+        const uint8_t* sB = sA + S::kA;
+        const __half* sW = (const __half*)(sB + S::kB);
+        const float* sX = (const float*)((const uint8_t*)sW + S::kWs);
+#pragma unroll
+        for (int lb = 0; lb < 4; ++lb) {
+            unsigned af[4][4];
+#pragma unroll
+            for (int mt = 0; mt < 4; ++mt) {
+                const int q = lane >> 3;
+                const int r = wm * 64 + mt * 16 + (lane & 7) + ((q & 1) << 3);
+                const int c = lb * 2 + (q >> 1);
+                ldsm_x4(af[mt], sA + r * 128 + ((c ^ (r & 7)) << 4));
             }
-            const int64_t c0 = min(n0 + nt * 8 + 2 * tg, N - 1);
-            const int64_t c1 = min(n0 + nt * 8 + 2 * tg + 1, N - 1);
-            dwv[nt][0] = __half2float(*(const __half*)(qs + c0 * wrow_bytes + w_scale_off(WT, nb, kb)));
-            dwv[nt][1] = __half2float(*(const __half*)(qs + c1 * wrow_bytes + w_scale_off(WT, nb, kb)));
-        }
-        float dxv[2][2];
+            unsigned blo[4], bhi[4];
+            {
+                const int r = wn * 32 + lane;
+                if (WT == T_Q8_0) {
+                    unsigned t0[4], t1[4];
+                    ldsm_x4(t0, sB + r * 128 + ((lb ^ (r & 7)) << 4));
+                    ldsm_x4(t1, sB + r * 128 + (((4 + lb) ^ (r & 7)) << 4));
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt) {
-            dxv[mt][0] = xd[arow[mt][0] * nb + kb];
-            dxv[mt][1] = xd[arow[mt][1] * nb + kb];
-        }
+                    for (int nt = 0; nt < 4; ++nt) {
+                        blo[nt] = t0[nt];
+                        bhi[nt] = t1[nt];
+                    }
+                } else {
+                    unsigned w4[4];
+                    ldsm_x4(w4, sB + r * 64 + ((lb ^ ((r >> 1) & 3)) << 4));
 #pragma unroll
-        for (int mt = 0; mt < 2; ++mt)
+                    for (int nt = 0; nt < 4; ++nt) {
+                        blo[nt] = ((w4[nt] << 4) & 0xF0F0F0F0u) ^ 0x80808080u;
+                        bhi[nt] = (w4[nt] & 0xF0F0F0F0u) ^ 0x80808080u;
+                    }
+                }
+            }
+            // scales of this block: sW/sX hold local blocks in the order [0, 2, 1, 3]
+            const int si = ((lb & 1) << 1) | (lb >> 1);
+            float2 dxv[4][2], dwv[4];
+#pragma unroll
+            for (int mt = 0; mt < 4; ++mt) {
+                const float a0 = sX[(wm * 64 + mt * 16 + g) * 4 + lb];
+                const float a1 = sX[(wm * 64 + mt * 16 + g + 8) * 4 + lb];
+                dxv[mt][0] = make_float2(a0, a0);
+                dxv[mt][1] = make_float2(a1, a1);
+            }
 #pragma unroll
             for (int nt = 0; nt < 4; ++nt) {
-                int c[4] = {0, 0, 0, 0};
-                mma_s8(c, af[mt], bf[nt]);
-                acc[mt][nt][0] = __fmaf_rn(__fmul_rn(dwv[nt][0], dxv[mt][0]), i2f_exact(c[0]), acc[mt][nt][0]);
-                acc[mt][nt][1] = __fmaf_rn(__fmul_rn(dwv[nt][1], dxv[mt][0]), i2f_exact(c[1]), acc[mt][nt][1]);
-                acc[mt][nt][2] = __fmaf_rn(__fmul_rn(dwv[nt][0], dxv[mt][1]), i2f_exact(c[2]), acc[mt][nt][2]);
-                acc[mt][nt][3] = __fmaf_rn(__fmul_rn(dwv[nt][1], dxv[mt][1]), i2f_exact(c[3]), acc[mt][nt][3]);
+                const int n = wn * 32 + nt * 8 + 2 * tg;
+                dwv[nt] = make_float2(__fmul_rn(__half2float(sW[n * 4 + si]), wsc),
+                                      __fmul_rn(__half2float(sW[(n + 1) * 4 + si]), wsc));
             }
-    }
+            const float2 bias2 = make_float2(12582912.0f, 12582912.0f);
 #pragma unroll
-    for (int mt = 0; mt < 2; ++mt)
+            for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+                for (int nt = 0; nt < 4; ++nt) {
+                    int d[4];
+                    mma_s8(d, af[mt], blo[nt], bhi[nt]);
+                    // (dot * d_w) * d_x + acc, two outputs per packed instruction
+                    const float2 v0 = sub2(make_float2(__int_as_float(d[0]), __int_as_float(d[1])), bias2);
+                    const float2 v1 = sub2(make_float2(__int_as_float(d[2]), __int_as_float(d[3])), bias2);
+                    acc[mt][nt][0] = fma2(mul2(v0, dwv[nt]), dxv[mt][0], acc[mt][nt][0]);
+                    acc[mt][nt][1] = fma2(mul2(v1, dwv[nt]), dxv[mt][1], acc[mt][nt][1]);
+                }
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+#pragma unroll
+    for (int mt = 0; mt < 4; ++mt)
 #pragma unroll
         for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
-                const int64_t m = m0 + mt * 16 + g + (e >= 2 ? 8 : 0);
-                const int64_t n = n0 + nt * 8 + 2 * tg + (e & 1);
+                const int m = m0 + wm * 64 + mt * 16 + g + ((e >> 1) << 3);
+                const int n = n0 + wn * 32 + nt * 8 + 2 * tg + (e & 1);
                 if (m < M && n < N) {
-                    float r = acc[mt][nt][e];
+                    const float2 p = acc[mt][nt][e >> 1];
+                    float r = (e & 1) ? p.y : p.x;
                     if (ep.bias) r = __fadd_rn(r, ep.bias[n]);
-                    if (ep.residual) r = __fadd_rn(ep.residual[m * ep.res_stride + n], r);
-                    y[m * y_stride + n] = r;
+                    if (ep.residual) r = __fadd_rn(ep.residual[(int64_t)m * ep.res_stride + n], r);
+                    y[(int64_t)m * y_stride + n] = r;
                 }
             }
 }
@@ -168,13 +274,29 @@ void launch_matmul_q(const QWeight& w, const int8_t* xq, const float* xd, int64_
         launch_gemv_fused(a, st);
         return;
     }
-    dim3 grid((unsigned)((w.N + 63) / 64), (unsigned)((M + 63) / 64));
+    GB_CHECK(w.N < (1LL << 31) && w.K < (1LL << 31) && M < (1LL << 31), "matmul: shape too large");
+    GB_CHECK(((uintptr_t)xq & 15) == 0, "matmul: xq must be 16-byte aligned");
+    dim3 grid((unsigned)((w.N + kBN - 1) / kBN), (unsigned)((M + kBM - 1) / kBM));
+    int dev = 0;
+    GB_CUDA(cudaGetDevice(&dev));
+    static std::mutex mu;
+    static bool configured[64] = {};
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!configured[dev & 63]) {
+            GB_CUDA(cudaFuncSetAttribute(k_gemm_q<T_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kGStages * GStage<T_Q8_0>::kBytes));
+            GB_CUDA(cudaFuncSetAttribute(k_gemm_q<T_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kGStages * GStage<T_Q4_0>::kBytes));
+            configured[dev & 63] = true;
+        }
+    }
     if (q8)
-        k_gemm_block<T_Q8_0><<<grid, 128, 0, st>>>((const uint8_t*)w.qs, w.N, w.K, xq, xd,
-                                                   M, y, y_stride, ep);
+        k_gemm_q<T_Q8_0><<<grid, kGThreads, kGStages * GStage<T_Q8_0>::kBytes, st>>>(
+            (const uint8_t*)w.qs, (int)w.N, (int)w.K, xq, xd, (int)M, y, y_stride, ep);
     else
-        k_gemm_block<T_Q4_0><<<grid, 128, 0, st>>>((const uint8_t*)w.qs, w.N, w.K, xq, xd,
-                                                   M, y, y_stride, ep);
+        k_gemm_q<T_Q4_0><<<grid, kGThreads, kGStages * GStage<T_Q4_0>::kBytes, st>>>(
+            (const uint8_t*)w.qs, (int)w.N, (int)w.K, xq, xd, (int)M, y, y_stride, ep);
     GB_CUDA(cudaGetLastError());
 }
 
