@@ -228,6 +228,225 @@ __global__ void k_attn_combine(AttnArgs a) {
     }
 }
 
+// ---- tensor-core flash attention for prefill (s >= 16, head_dim 64 or 128) ------------------
+// One warp owns 16 query rows of one q head; a CTA's 4 warps share one KV head (GQA), so each
+// K/V tile of 64 cache rows is staged once (cp.async, double-buffered, XOR-swizzled rows) for all
+// of them.  S = Q K^T and O += P V run on mma.sync m16n8k16 with fp16 inputs and fp32
+// accumulators: Q is rounded to fp16 as the CPU kernel does (q_to_vec_dot), the probabilities P
+// are rounded to fp16 for the second product (the CPU rounds its whole V accumulator to fp16
+// after every position, a larger error).  Online softmax in fp32 per row; causal limit per
+// query at absolute positions (query t sees cache rows 0 .. kv_base + t).
+constexpr int kFaKeys = 64;
+constexpr int kFaWarps = 4;
+
+__device__ __forceinline__ unsigned fa_saddr(const void* p) {
+    return (unsigned)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void fa_cp16(void* dst, const void* src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(fa_saddr(dst)), "l"(src),
+                 "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void fa_ldsm4(unsigned (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(fa_saddr(p)));
+}
+__device__ __forceinline__ void fa_ldsm4t(unsigned (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(fa_saddr(p)));
+}
+__device__ __forceinline__ void fa_mma(float (&d)[4], const unsigned (&a)[4], unsigned b0,
+                                       unsigned b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ unsigned pack_h2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *(const unsigned*)&h;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kFaWarps * 32) k_fa(AttnArgs a) {
+    constexpr int CH = HD / 8;  // 16-byte chunks per K/V row
+    extern __shared__ __align__(16) uint8_t smem[];
+    __half* sK = (__half*)smem;                      // [2][kFaKeys][HD]
+    __half* sV = sK + 2 * kFaKeys * HD;              // [2][kFaKeys][HD]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, tg = lane & 3;
+    const int rk = (int)(a.Hq / a.Hkv);
+    const int hk = blockIdx.y;
+    const int nqb = (int)((a.s + 15) / 16);
+    // work items of this KV head: (query block, head in group); 4 per CTA
+    const int item = blockIdx.x * kFaWarps + warp;
+    const bool active = item < nqb * rk;
+    const int qb = active ? item / rk : 0;
+    const int h = hk * rk + (active ? item % rk : 0);
+    const int64_t kv_base = (a.use_step ? a.step->pos : 0) + a.kv_off;
+    // rows this CTA must see: up to the last query of its last item
+    const int last_item = min((int)(blockIdx.x + 1) * kFaWarps, nqb * rk) - 1;
+    const int64_t last_q = min((int64_t)(last_item / rk) * 16 + 15, a.s - 1);
+    const int64_t nkv = kv_base + last_q + 1;
+    const int ntile = (int)((nkv + kFaKeys - 1) / kFaKeys);
+    const __half* kb = a.kc + (int64_t)hk * a.ctx * HD;
+    const __half* vb = a.vc + (int64_t)hk * a.ctx * HD;
+
+    auto stage = [&](int tile, int buf) {
+        __half* dk = sK + buf * kFaKeys * HD;
+        __half* dv = sV + buf * kFaKeys * HD;
+        for (int e = threadIdx.x; e < kFaKeys * CH; e += kFaWarps * 32) {
+            const int r = e / CH, c = e % CH;
+            const int64_t key = (int64_t)tile * kFaKeys + r;
+            const bool ok = key < nkv;
+            const int64_t kk = ok ? key : 0;
+            const int sw = (c ^ (r & 7)) * 8;
+            fa_cp16(dk + r * HD + sw, kb + kk * HD + c * 8, ok);
+            fa_cp16(dv + r * HD + sw, vb + kk * HD + c * 8, ok);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    stage(0, 0);
+
+    // Q fragments (fp16) of this warp's 16 rows: [k16 step][a0..a3]
+    unsigned qf[HD / 16][4];
+    const int64_t t0 = (int64_t)qb * 16;
+#pragma unroll
+    for (int ks = 0; ks < HD / 16; ++ks) {
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int64_t t = t0 + g + ((r & 1) << 3);
+            const int d = ks * 16 + 2 * tg + ((r >> 1) << 3);
+            float2 v = make_float2(0.0f, 0.0f);
+            if (active && t < a.s) {
+                const char* p = a.q.data + d * a.q.nb[0] + t * a.q.nb[1] + h * a.q.nb[2];
+                v = *(const float2*)p;
+            }
+            qf[ks][r] = pack_h2(v.x, v.y);
+        }
+    }
+    float o[HD / 8][4];
+#pragma unroll
+    for (int i = 0; i < HD / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+    float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.0f, 0.0f};
+    const int64_t lim0 = kv_base + t0 + g, lim1 = lim0 + 8;  // last visible row per owned row
+
+    for (int tile = 0; tile < ntile; ++tile) {
+        const int buf = tile & 1;
+        if (tile + 1 < ntile) {
+            stage(tile + 1, buf ^ 1);
+            asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        __syncthreads();
+        const __half* cK = sK + buf * kFaKeys * HD;
+        const __half* cV = sV + buf * kFaKeys * HD;
+        const int64_t key0 = (int64_t)tile * kFaKeys;
+        if (active && key0 <= kv_base + t0 + 15) {
+            // S = Q K^T: 8 key tiles of 8
+            float sc[kFaKeys / 8][4];
+#pragma unroll
+            for (int nt = 0; nt < kFaKeys / 8; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
+#pragma unroll
+            for (int ks = 0; ks < HD / 16; ++ks) {
+#pragma unroll
+                for (int np = 0; np < kFaKeys / 16; ++np) {
+                    // keys np*16 .. +15, dims ks*16 .. +15: matrices (k0-7,d0-7) (k0-7,d8-15)
+                    // (k8-15,d0-7) (k8-15,d8-15)
+                    const int q4 = lane >> 3;
+                    const int r = np * 16 + (lane & 7) + ((q4 >> 1) << 3);
+                    const int c = ks * 2 + (q4 & 1);
+                    unsigned bk[4];
+                    fa_ldsm4(bk, cK + r * HD + ((c ^ (r & 7)) << 3));
+                    fa_mma(sc[2 * np], qf[ks], bk[0], bk[1]);
+                    fa_mma(sc[2 * np + 1], qf[ks], bk[2], bk[3]);
+                }
+            }
+            // scale, causal mask, online softmax (rows g and g+8 of the warp's block)
+            float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+            for (int nt = 0; nt < kFaKeys / 8; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int64_t key = key0 + nt * 8 + 2 * tg + (e & 1);
+                    const int64_t lim = (e >> 1) ? lim1 : lim0;
+                    const float v = key <= lim ? __fmul_rn(sc[nt][e], a.scale) : -INFINITY;
+                    sc[nt][e] = v;
+                    mx[e >> 1] = fmaxf(mx[e >> 1], v);
+                }
+            float corr[2], mnew[2];
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+                mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+                mnew[r] = fmaxf(mrow[r], mx[r]);
+                corr[r] = mnew[r] == -INFINITY ? 1.0f : expf(mrow[r] - mnew[r]);
+                mrow[r] = mnew[r];
+            }
+            float ls[2] = {0.0f, 0.0f};
+            unsigned pf[kFaKeys / 16][4];
+#pragma unroll
+            for (int nt = 0; nt < kFaKeys / 8; ++nt) {
+                float p[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float mr = mnew[e >> 1];
+                    p[e] = sc[nt][e] == -INFINITY ? 0.0f : expf(sc[nt][e] - mr);
+                    ls[e >> 1] += p[e];
+                }
+                // C layout of key tile nt -> A layout of the PV product (k16 step nt/2)
+                pf[nt >> 1][(nt & 1) * 2 + 0] = pack_h2(p[0], p[1]);
+                pf[nt >> 1][(nt & 1) * 2 + 1] = pack_h2(p[2], p[3]);
+            }
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+                ls[r] += __shfl_xor_sync(0xffffffffu, ls[r], 1);
+                ls[r] += __shfl_xor_sync(0xffffffffu, ls[r], 2);
+                lrow[r] = lrow[r] * corr[r] + ls[r];
+            }
+#pragma unroll
+            for (int i = 0; i < HD / 8; ++i) {
+                o[i][0] *= corr[0];
+                o[i][1] *= corr[0];
+                o[i][2] *= corr[1];
+                o[i][3] *= corr[1];
+            }
+            // O += P V: for each 16-key step, V^T fragments with ldmatrix.trans
+#pragma unroll
+            for (int ks = 0; ks < kFaKeys / 16; ++ks) {
+#pragma unroll
+                for (int dp = 0; dp < HD / 16; ++dp) {
+                    const int q4 = lane >> 3;
+                    const int r = ks * 16 + (lane & 7) + ((q4 & 1) << 3);
+                    const int c = dp * 2 + (q4 >> 1);
+                    unsigned bv[4];
+                    fa_ldsm4t(bv, cV + r * HD + ((c ^ (r & 7)) << 3));
+                    fa_mma(o[2 * dp], pf[ks], bv[0], bv[1]);
+                    fa_mma(o[2 * dp + 1], pf[ks], bv[2], bv[3]);
+                }
+            }
+        }
+        __syncthreads();  // the buffer is restaged next
+    }
+    if (!active) return;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const int64_t t = t0 + g + r * 8;
+        if (t >= a.s) continue;
+        const float inv = lrow[r] == 0.0f ? 0.0f : 1.0f / lrow[r];
+        float* orow = a.o + (t * a.Hq + h) * HD;
+#pragma unroll
+        for (int i = 0; i < HD / 8; ++i) {
+            const int d = i * 8 + 2 * tg;
+            *(float2*)(orow + d) = make_float2(o[i][r * 2] * inv, o[i][r * 2 + 1] * inv);
+        }
+    }
+}
+
 int64_t attn_splits(int64_t s, int64_t max_kv) {
     if (s > 4) return 1;
     int64_t sp = (max_kv + kSplitLen - 1) / kSplitLen;
@@ -288,6 +507,30 @@ void launch_attention(const TView& q, const __half* kc, const __half* vc, int64_
     GB_CHECK(a.hd <= kMaxHd && a.hd % 2 == 0, "attention: head_dim must be even and <= 256");
     GB_CHECK(a.Hq % Hkv == 0, "attention: Hq must be a multiple of Hkv");
     if (!a.s) return;
+    if (a.s >= 16 && (a.hd == 64 || a.hd == 128) && q.nb[0] == 4 &&
+        ((uintptr_t)kc & 15) == 0 && ((uintptr_t)vc & 15) == 0) {
+        // tensor-core flash attention; one KV split (every query block walks its own rows)
+        a.splits = 1;
+        const int64_t rk = a.Hq / Hkv;
+        const int64_t items = ((a.s + 15) / 16) * rk;
+        dim3 grid((unsigned)((items + kFaWarps - 1) / kFaWarps), (unsigned)Hkv);
+        const size_t smem = (size_t)4 * kFaKeys * a.hd * 2;
+        if (a.hd == 64) {
+            k_fa<64><<<grid, kFaWarps * 32, smem, st>>>(a);
+        } else {
+            static bool configured[64] = {};
+            int dev = 0;
+            GB_CUDA(cudaGetDevice(&dev));
+            if (!configured[dev & 63]) {
+                GB_CUDA(cudaFuncSetAttribute(k_fa<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)smem));
+                configured[dev & 63] = true;
+            }
+            k_fa<128><<<grid, kFaWarps * 32, smem, st>>>(a);
+        }
+        GB_CUDA(cudaGetLastError());
+        return;
+    }
     a.splits = attn_splits(a.s, max_kv);
     const int64_t rk = a.Hq / Hkv;
     const int nq = (int)(rk * a.s < 8 ? rk * a.s : 8);

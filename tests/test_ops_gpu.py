@@ -233,10 +233,14 @@ def _attention_exact(q, k, v, kv_pos, scale):
 
 
 @pytest.mark.parametrize("s,kv_pos,Hq,Hkv,hd", [(1, 40, 4, 2, 64), (1, 700, 32, 8, 128),
-                                                (5, 100, 9, 3, 64), (70, 0, 4, 4, 64)])
+                                                (5, 100, 9, 3, 64), (70, 0, 4, 4, 64),
+                                                (128, 300, 32, 8, 128), (33, 17, 9, 3, 64),
+                                                (16, 0, 12, 12, 64)])
 def test_attention_close(G, s, kv_pos, Hq, Hkv, hd):
-    """fp32-accumulated attention: within 1e-5 of an exact float64 evaluation, and no further
-    from the exact result than the CPU's fp16-accumulator kernel (the oracle) is."""
+    """Attention against an exact float64 evaluation: never further from it than the CPU's
+    fp16-accumulator kernel (the oracle) is, and within 1e-5 of the output range for the
+    fp32-accumulating CUDA-core kernel (s < 16) or 1e-3 for the tensor-core kernel (s >= 16,
+    whose probabilities enter the second product as fp16)."""
     torch = G.torch_dev()
     rng = np.random.default_rng(s + kv_pos)
     ctx = 1024
@@ -258,7 +262,7 @@ def test_attention_close(G, s, kv_pos, Hq, Hkv, hd):
                        np.ascontiguousarray(v[:, :n_kv]).view(np.uint16), mask, np.float32(scale))
     err_gpu = np.max(np.abs(got - exact))
     err_cpu = np.max(np.abs(cpu - exact))
-    assert err_gpu <= 1e-5 * np.max(np.abs(exact))
+    assert err_gpu <= (1e-5 if s < 16 else 1e-3) * np.max(np.abs(exact))
     assert err_gpu <= err_cpu + 1e-6
 
 
