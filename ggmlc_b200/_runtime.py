@@ -79,6 +79,28 @@ def _load() -> ctypes.CDLL:
         "gb_executor_reset_kernel_times": ([P], I),
         "gb_executor_kernel_times": ([P], CP),
         "gb_executor_stream": ([P], P),
+        "gb_executor_init_paged_kv_cache": ([P, I64, I64], I),
+        "gb_executor_is_paged_kv_cache_enabled": ([P], I),
+        "gb_executor_paged_kv_alloc_slot": ([P, I64], I),
+        "gb_executor_paged_kv_free_slot": ([P, I64], I),
+        "gb_executor_paged_kv_ensure_tokens": ([P, I64, I64], I),
+        "gb_executor_paged_active_vram_bytes": ([P], I64),
+        "gb_executor_tokens_per_page": ([P], I64),
+        "gb_executor_set_tokens_per_page": ([P, I64], I),
+        "gb_executor_prepare_batch": ([P, I, P, P], I),
+        "gb_scheduler_create": ([P, I, I, PP], I),
+        "gb_scheduler_free": ([P], None),
+        "gb_scheduler_add_request": ([P, P, I64, I, ctypes.c_float, I,
+                                      ctypes.POINTER(ctypes.c_uint64)], I),
+        "gb_scheduler_step": ([P, P, P, I, ctypes.POINTER(I), P, I, ctypes.POINTER(I)], I),
+        "gb_scheduler_has_work": ([P], I),
+        "gb_scheduler_active_count": ([P], I64),
+        "gb_scheduler_pending_count": ([P], I64),
+        "gb_scheduler_max_batch_size": ([P], I),
+        "gb_scheduler_enable_prefix_caching": ([P, I], I),
+        "gb_scheduler_is_prefix_caching_enabled": ([P], I),
+        "gb_scheduler_get_request": ([P, ctypes.c_uint64, P], I),
+        "gb_scheduler_request_tokens": ([P, ctypes.c_uint64, I, P, I64, ctypes.POINTER(I64)], I),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(L, name)
@@ -374,8 +396,163 @@ class ModelExecutor:
     def ggml_cuda_graphs_compiled() -> bool:
         return True
 
+    # ---- paged KV cache (python_bindings.cpp:196-204) ----------------------------------------
+    def init_paged_kv_cache(self, max_batch: int = 8, max_ctx: int = 2048) -> None:
+        _check(_lib.gb_executor_init_paged_kv_cache(self._h, int(max_batch), int(max_ctx)))
+
+    def is_paged_kv_cache_enabled(self) -> bool:
+        return bool(_lib.gb_executor_is_paged_kv_cache_enabled(self._h))
+
+    def paged_kv_alloc_slot(self, slot_id: int, prefix_hash: str = "") -> None:
+        _check(_lib.gb_executor_paged_kv_alloc_slot(self._h, int(slot_id)))
+
+    def paged_kv_free_slot(self, slot_id: int) -> None:
+        _check(_lib.gb_executor_paged_kv_free_slot(self._h, int(slot_id)))
+
+    def paged_kv_ensure_tokens(self, slot_id: int, total_tokens: int) -> None:
+        _check(_lib.gb_executor_paged_kv_ensure_tokens(self._h, int(slot_id), int(total_tokens)))
+
+    def get_paged_active_vram_bytes(self) -> int:
+        return int(_lib.gb_executor_paged_active_vram_bytes(self._h))
+
+    def configure_vmm_pool(self, max_warm_pages: int = 64, prealloc_pages: int = 0) -> None:
+        """Accepted for compatibility: slots are windows of one allocation, no VMM page pool."""
+
+    @property
+    def tokens_per_page(self) -> int:
+        return int(_lib.gb_executor_tokens_per_page(self._h))
+
+    def set_tokens_per_page(self, tokens_per_page: int) -> None:
+        _check(_lib.gb_executor_set_tokens_per_page(self._h, int(tokens_per_page)))
+
+    def prepare_batch(self, pos: np.ndarray, slot: np.ndarray) -> None:
+        """One decode token for each of len(pos) sequences (row r at pos[r] in slot slot[r])."""
+        p = np.ascontiguousarray(pos, np.int32)
+        s = np.ascontiguousarray(slot, np.int32)
+        if p.shape != s.shape or p.ndim != 1:
+            raise ValueError("pos and slot must be 1-D arrays of equal length")
+        _check(_lib.gb_executor_prepare_batch(self._h, len(p), p.ctypes.data, s.ctypes.data))
+
     def __del__(self):
         h = getattr(self, "_h", None)
         if h is not None and h.value:
             _lib.gb_executor_free(h)
+            self._h = ctypes.c_void_p()
+
+
+# ---- continuous batching (batch_scheduler.h:35-77; python_bindings.cpp:261-295) -------------
+class _RequestInfo(ctypes.Structure):
+    _fields_ = [("request_id", ctypes.c_uint64), ("slot_id", ctypes.c_int),
+                ("current_pos", ctypes.c_int64), ("max_new_tokens", ctypes.c_int),
+                ("temperature", ctypes.c_float), ("eos_token_id", ctypes.c_int),
+                ("finished", ctypes.c_int), ("finish_reason", ctypes.c_char_p),
+                ("n_prompt_tokens", ctypes.c_int64), ("n_generated_tokens", ctypes.c_int64),
+                ("prefix_tokens_matched", ctypes.c_int64)]
+
+
+class GenerationRequest:
+    """Read-only snapshot of a request (python_bindings.cpp:261-272)."""
+
+    def __init__(self, info: _RequestInfo, prompt: list[int], generated: list[int]):
+        self.request_id = int(info.request_id)
+        self.prompt_tokens = prompt
+        self.generated_tokens = generated
+        self.slot_id = int(info.slot_id)
+        self.current_pos = int(info.current_pos)
+        self.max_new_tokens = int(info.max_new_tokens)
+        self.temperature = float(info.temperature)
+        self.eos_token_id = int(info.eos_token_id)
+        self.finished = bool(info.finished)
+        self.finish_reason = (info.finish_reason or b"").decode()
+        self.prefix_tokens_matched = int(info.prefix_tokens_matched)
+
+
+class StepResult:
+    """new_tokens: [(request_id, token_id)], completed_request_ids (python_bindings.cpp:274-276)."""
+
+    def __init__(self, new_tokens: list[tuple[int, int]], completed: list[int]):
+        self.new_tokens = new_tokens
+        self.completed_request_ids = completed
+
+
+class ContinuousBatchScheduler:
+    """Iteration-level continuous batching over the executor's paged KV cache.
+
+    Same interface as the reference scheduler (python_bindings.cpp:278-294).  Each step admits
+    one pending request (prefill in a free slot) or decodes one token of every active sequence,
+    each at its own position.  Prefix caching is not implemented (the toggle is accepted and
+    the hit counters stay 0).
+    """
+
+    def __init__(self, executor: ModelExecutor, max_batch_size: int = 8, eos_token_id: int = 0):
+        h = ctypes.c_void_p()
+        _check(_lib.gb_scheduler_create(executor._h, int(max_batch_size), int(eos_token_id),
+                                        ctypes.byref(h)))
+        self._h = h
+        self._executor = executor  # the scheduler drives this executor
+
+    def add_request(self, prompt_tokens, max_new_tokens: int = 32, temperature: float = 0.0,
+                    eos_token_id: int = -1) -> int:
+        p = np.ascontiguousarray(prompt_tokens, np.int32).reshape(-1)
+        rid = ctypes.c_uint64()
+        _check(_lib.gb_scheduler_add_request(self._h, p.ctypes.data, len(p), int(max_new_tokens),
+                                             float(temperature), int(eos_token_id),
+                                             ctypes.byref(rid)))
+        return int(rid.value)
+
+    def step(self) -> StepResult:
+        cap = 64
+        ids = (ctypes.c_uint64 * cap)()
+        toks = (ctypes.c_int32 * cap)()
+        done = (ctypes.c_uint64 * cap)()
+        n_new, n_done = ctypes.c_int(), ctypes.c_int()
+        _check(_lib.gb_scheduler_step(self._h, ids, toks, cap, ctypes.byref(n_new), done, cap,
+                                      ctypes.byref(n_done)))
+        return StepResult([(int(ids[i]), int(toks[i])) for i in range(n_new.value)],
+                          [int(done[i]) for i in range(n_done.value)])
+
+    def has_work(self) -> bool:
+        return bool(_lib.gb_scheduler_has_work(self._h))
+
+    def active_count(self) -> int:
+        return int(_lib.gb_scheduler_active_count(self._h))
+
+    def pending_count(self) -> int:
+        return int(_lib.gb_scheduler_pending_count(self._h))
+
+    def max_batch_size(self) -> int:
+        return int(_lib.gb_scheduler_max_batch_size(self._h))
+
+    def enable_prefix_caching(self, enable: bool) -> None:
+        _check(_lib.gb_scheduler_enable_prefix_caching(self._h, int(bool(enable))))
+
+    def is_prefix_caching_enabled(self) -> bool:
+        return bool(_lib.gb_scheduler_is_prefix_caching_enabled(self._h))
+
+    @property
+    def total_prefix_cache_hits(self) -> int:
+        return 0
+
+    @property
+    def total_prefix_tokens_saved(self) -> int:
+        return 0
+
+    def _tokens(self, rid: int, which: int) -> list[int]:
+        n = ctypes.c_int64()
+        _check(_lib.gb_scheduler_request_tokens(self._h, rid, which, None, 0, ctypes.byref(n)))
+        buf = np.empty(n.value, np.int32)
+        _check(_lib.gb_scheduler_request_tokens(self._h, rid, which, buf.ctypes.data, n.value,
+                                                ctypes.byref(n)))
+        return [int(t) for t in buf]
+
+    def get_request(self, request_id: int) -> GenerationRequest:
+        info = _RequestInfo()
+        _check(_lib.gb_scheduler_get_request(self._h, int(request_id), ctypes.byref(info)))
+        return GenerationRequest(info, self._tokens(int(request_id), 0),
+                                 self._tokens(int(request_id), 1))
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value and _lib is not None:
+            _lib.gb_scheduler_free(h)
             self._h = ctypes.c_void_p()

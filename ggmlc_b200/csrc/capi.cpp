@@ -10,6 +10,7 @@
 
 #include "executor.h"
 #include "graph.h"
+#include "scheduler.h"
 #include "kernels.h"
 #include "kutil.cuh"
 
@@ -21,6 +22,10 @@ struct gb_graph {
 struct gb_executor {
     std::unique_ptr<gb::Executor> e;
     std::string summary, mm_summary, ktimes;
+};
+
+struct gb_scheduler {
+    std::unique_ptr<gb::Scheduler> s;
 };
 
 namespace {
@@ -202,6 +207,107 @@ int gb_executor_reset_kv_cache(gb_executor* e) {
     return guard([&] { e->e->reset_kv_cache(); });
 }
 int gb_executor_has_kv_cache(const gb_executor* e) { return e->e->has_kv_cache() ? 1 : 0; }
+int gb_executor_init_paged_kv_cache(gb_executor* e, int64_t max_batch, int64_t max_ctx) {
+    return guard([&] { e->e->init_paged_kv_cache(max_batch, max_ctx); });
+}
+int gb_executor_is_paged_kv_cache_enabled(const gb_executor* e) {
+    return e->e->paged_kv_enabled() ? 1 : 0;
+}
+int gb_executor_paged_kv_alloc_slot(gb_executor* e, int64_t slot) {
+    return guard([&] { e->e->paged_kv_alloc_slot(slot); });
+}
+int gb_executor_paged_kv_free_slot(gb_executor* e, int64_t slot) {
+    return guard([&] { e->e->paged_kv_free_slot(slot); });
+}
+int gb_executor_paged_kv_ensure_tokens(gb_executor* e, int64_t slot, int64_t total_tokens) {
+    return guard([&] { e->e->paged_kv_ensure_tokens(slot, total_tokens); });
+}
+int64_t gb_executor_paged_active_vram_bytes(const gb_executor* e) {
+    return e->e->paged_active_vram_bytes();
+}
+int64_t gb_executor_tokens_per_page(const gb_executor* e) { return e->e->tokens_per_page(); }
+int gb_executor_set_tokens_per_page(gb_executor* e, int64_t n) {
+    return guard([&] { e->e->set_tokens_per_page(n); });
+}
+int gb_executor_prepare_batch(gb_executor* e, int rows, const int32_t* pos, const int32_t* slot) {
+    return guard([&] { e->e->prepare_batch(rows, pos, slot); });
+}
+
+int gb_scheduler_create(gb_executor* e, int max_batch_size, int eos_token_id, gb_scheduler** out) {
+    return guard([&] {
+        auto* h = new gb_scheduler();
+        try {
+            h->s.reset(new gb::Scheduler(*e->e, max_batch_size, eos_token_id));
+        } catch (...) {
+            delete h;
+            throw;
+        }
+        *out = h;
+    });
+}
+void gb_scheduler_free(gb_scheduler* s) { delete s; }
+int gb_scheduler_add_request(gb_scheduler* s, const int32_t* prompt, int64_t n, int max_new_tokens,
+                             float temperature, int eos_token_id, uint64_t* request_id) {
+    return guard([&] {
+        GB_CHECK(n > 0 && prompt, "add_request: empty prompt");
+        *request_id = s->s->add_request(std::vector<int32_t>(prompt, prompt + n), max_new_tokens,
+                                        temperature, eos_token_id);
+    });
+}
+int gb_scheduler_step(gb_scheduler* s, uint64_t* ids, int32_t* tokens, int cap, int* n_new,
+                      uint64_t* done, int cap_done, int* n_done) {
+    return guard([&] {
+        const gb::StepOut r = s->s->step();
+        GB_CHECK((int)r.new_tokens.size() <= cap && (int)r.completed.size() <= cap_done,
+                 "scheduler step: result buffers too small");
+        for (size_t i = 0; i < r.new_tokens.size(); ++i) {
+            ids[i] = r.new_tokens[i].first;
+            tokens[i] = r.new_tokens[i].second;
+        }
+        for (size_t i = 0; i < r.completed.size(); ++i) done[i] = r.completed[i];
+        *n_new = (int)r.new_tokens.size();
+        *n_done = (int)r.completed.size();
+    });
+}
+int gb_scheduler_has_work(const gb_scheduler* s) { return s->s->has_work() ? 1 : 0; }
+int64_t gb_scheduler_active_count(const gb_scheduler* s) { return (int64_t)s->s->active_count(); }
+int64_t gb_scheduler_pending_count(const gb_scheduler* s) { return (int64_t)s->s->pending_count(); }
+int gb_scheduler_max_batch_size(const gb_scheduler* s) { return s->s->max_batch(); }
+int gb_scheduler_enable_prefix_caching(gb_scheduler* s, int enable) {
+    s->s->enable_prefix_caching(enable != 0);
+    return 0;
+}
+int gb_scheduler_is_prefix_caching_enabled(const gb_scheduler* s) {
+    return s->s->prefix_caching() ? 1 : 0;
+}
+int gb_scheduler_get_request(gb_scheduler* s, uint64_t request_id, gb_request_info* info) {
+    return guard([&] {
+        auto r = s->s->get(request_id);
+        GB_CHECK(r != nullptr, "unknown request id " + std::to_string(request_id));
+        info->request_id = r->id;
+        info->slot_id = r->slot;
+        info->current_pos = r->pos;
+        info->max_new_tokens = r->max_new;
+        info->temperature = r->temperature;
+        info->eos_token_id = r->eos;
+        info->finished = r->finished ? 1 : 0;
+        info->finish_reason = r->finish_reason.c_str();
+        info->n_prompt_tokens = (int64_t)r->prompt.size();
+        info->n_generated_tokens = (int64_t)r->generated.size();
+        info->prefix_tokens_matched = 0;
+    });
+}
+int gb_scheduler_request_tokens(gb_scheduler* s, uint64_t request_id, int which, int32_t* buf,
+                                int64_t cap, int64_t* n) {
+    return guard([&] {
+        auto r = s->s->get(request_id);
+        GB_CHECK(r != nullptr, "unknown request id " + std::to_string(request_id));
+        const std::vector<int32_t>& v = which == 0 ? r->prompt : r->generated;
+        *n = (int64_t)v.size();
+        const int64_t k = std::min<int64_t>(cap, (int64_t)v.size());
+        if (k > 0 && buf) std::memcpy(buf, v.data(), (size_t)k * 4);
+    });
+}
 int gb_executor_set_logits_last_only(gb_executor* e, int enable) {
     return guard([&] { e->e->set_logits_last_only(enable != 0); });
 }

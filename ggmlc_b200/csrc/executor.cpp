@@ -118,6 +118,7 @@ Executor::~Executor() {
     if (h_step_) cudaFreeHost(h_step_);
     if (d_step_) cudaFree(d_step_);
     if (pinned_out_) cudaFreeHost(pinned_out_);
+    if (arena_) cudaFree(arena_);
     if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -126,8 +127,23 @@ void Executor::free_program(Program& p) {
     p.graph_exec = nullptr;
     for (void* q : p.owned) cudaFree(q);
     p.owned.clear();
-    if (p.arena) cudaFree(p.arena);
-    p.arena = nullptr;
+}
+
+// One activation arena for all programs (they run one at a time on the executor's stream).  It
+// grows to the largest program's need; growing moves it, so captured graphs are dropped.
+void Executor::ensure_arena(size_t bytes) {
+    if (bytes <= arena_cap_) return;
+    GB_CUDA(cudaStreamSynchronize(stream_));
+    for (auto& [k, p] : programs_)
+        if (p->graph_exec) {
+            cudaGraphExecDestroy(p->graph_exec);
+            p->graph_exec = nullptr;
+        }
+    if (arena_) GB_CUDA(cudaFree(arena_));
+    arena_ = nullptr;
+    const size_t cap = bytes + bytes / 4;
+    GB_CUDA(cudaMalloc(&arena_, cap));
+    arena_cap_ = cap;
 }
 
 // Upload every tensor with a GGUF payload: quantized matrices are repacked into the SoA layout
@@ -182,6 +198,10 @@ void Executor::upload_weights() {
 
 void Executor::init_kv_cache(int64_t max_ctx) {
     if (kv_enabled_) return;
+    alloc_kv(1, max_ctx);
+}
+
+void Executor::alloc_kv(int64_t slots, int64_t max_ctx) {
     // enable rule of the reference (executor.cpp:505-539)
     bool has_rope = false, has_pos_sym = false, has_pos_in = false, has_arange = false;
     for (auto& op : g_->ops) has_rope |= op.opcode == OP_ROPE;
@@ -207,7 +227,9 @@ void Executor::init_kv_cache(int64_t max_ctx) {
         c.Hkv = k.ne[2]->eval(env);
         c.batch = k.ne[3]->eval(env);
         c.ctx = max_ctx;
-        const size_t bytes = (size_t)(c.hd * c.Hkv * c.batch * max_ctx) * 2;
+        c.slots = slots;
+        GB_CHECK(c.batch == 1, "KV caches with a graph batch dimension are not supported");
+        const size_t bytes = (size_t)(c.hd * c.Hkv * slots * max_ctx) * 2;
         GB_CUDA(cudaMalloc(&c.k, bytes));
         GB_CUDA(cudaMalloc(&c.v, bytes));
         GB_CUDA(cudaMemset(c.k, 0, bytes));
@@ -220,9 +242,94 @@ void Executor::init_kv_cache(int64_t max_ctx) {
     kv_enabled_ = true;
 }
 
+void Executor::free_kv() {
+    GB_CUDA(cudaStreamSynchronize(stream_));
+    for (auto& [k, p] : programs_) free_program(*p);
+    programs_.clear();
+    active_.reset();
+    for (auto& [id, c] : kv_) {
+        cudaFree(c.k);
+        cudaFree(c.v);
+    }
+    kv_.clear();
+    kv_enabled_ = false;
+    paged_ = false;
+    slot_tokens_.clear();
+}
+
+void Executor::init_paged_kv_cache(int64_t max_batch, int64_t max_ctx) {
+    GB_CHECK(max_batch >= 1 && max_batch <= kMaxRows, "paged KV: max_batch must be 1..16");
+    GB_CHECK(max_ctx >= 1, "paged KV: max_ctx must be positive");
+    if (kv_enabled_) free_kv();
+    alloc_kv(max_batch + 1, max_ctx);  // + the scratch slot of padding rows
+    GB_CHECK(kv_enabled_, "paged KV: the graph has no attention over a KV cache");
+    paged_ = true;
+    paged_max_batch_ = max_batch;
+    slot_tokens_.assign((size_t)max_batch, -1);
+}
+
+void Executor::paged_kv_alloc_slot(int64_t slot) {
+    GB_CHECK(paged_, "paged KV cache not initialised");
+    GB_CHECK(slot >= 0 && slot < paged_max_batch_, "paged KV: slot out of range");
+    GB_CHECK(slot_tokens_[(size_t)slot] < 0, "paged KV: slot already allocated");
+    slot_tokens_[(size_t)slot] = 0;
+}
+
+void Executor::paged_kv_free_slot(int64_t slot) {
+    GB_CHECK(paged_, "paged KV cache not initialised");
+    GB_CHECK(slot >= 0 && slot < paged_max_batch_, "paged KV: slot out of range");
+    slot_tokens_[(size_t)slot] = -1;
+}
+
+void Executor::paged_kv_ensure_tokens(int64_t slot, int64_t total) {
+    GB_CHECK(paged_, "paged KV cache not initialised");
+    GB_CHECK(slot >= 0 && slot < paged_max_batch_ && slot_tokens_[(size_t)slot] >= 0,
+             "paged KV: slot not allocated");
+    GB_CHECK(total >= 0 && total <= kv_max_ctx_,
+             "paged KV: " + std::to_string(total) + " tokens exceed max_ctx " +
+                 std::to_string(kv_max_ctx_));
+    const int64_t pages = (total + tokens_per_page_ - 1) / tokens_per_page_;
+    slot_tokens_[(size_t)slot] = std::max(slot_tokens_[(size_t)slot], pages * tokens_per_page_);
+}
+
+int64_t Executor::paged_active_vram_bytes() const {
+    if (!paged_) return 0;
+    int64_t per_token = 0;
+    for (auto& [id, c] : kv_) per_token += c.Hkv * c.hd * 2 * 2;
+    int64_t total = 0;
+    for (int64_t t : slot_tokens_)
+        if (t > 0) total += std::min(t, kv_max_ctx_) * per_token;
+    return total;
+}
+
+void Executor::set_tokens_per_page(int64_t n) {
+    GB_CHECK(n >= 1, "tokens_per_page must be positive");
+    tokens_per_page_ = n;
+}
+
+void Executor::prepare_batch(int rows, const int32_t* pos, const int32_t* slot) {
+    GB_CHECK(paged_, "batched decode needs init_paged_kv_cache");
+    GB_CHECK(rows >= 1 && rows <= kMaxRows, "batched decode: 1..16 rows");
+    for (int r = 0; r < rows; ++r) {
+        GB_CHECK(slot[r] >= 0 && slot[r] <= paged_max_batch_, "batched decode: bad slot");
+        GB_CHECK(pos[r] >= 0 && pos[r] < kv_max_ctx_, "batched decode: position outside the cache");
+    }
+    SymEnv env;
+    env["s"] = rows;
+    env["__rows"] = rows;
+    env["pos"] = 0;
+    for (auto& s : g_->symbol_table)
+        if (!env.count(s)) env[s] = rows;  // the sequence symbol(s) of the graph
+    prepare(env, true);
+    for (int r = 0; r < rows; ++r) {
+        h_step_->row_pos[r] = pos[r];
+        h_step_->row_slot[r] = slot[r];
+    }
+}
+
 void Executor::reset_kv_cache() {
     for (auto& [id, c] : kv_) {
-        const size_t bytes = (size_t)(c.hd * c.Hkv * c.batch * c.ctx) * 2;
+        const size_t bytes = (size_t)(c.hd * c.Hkv * c.slots * c.ctx) * 2;
         GB_CUDA(cudaMemsetAsync(c.k, 0, bytes, stream_));
         GB_CUDA(cudaMemsetAsync(c.v, 0, bytes, stream_));
     }
@@ -268,6 +375,7 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
     Program& pg = *P;
     pg.env = env;
     pg.kv = kv;
+    pg.batch = env.count("__rows") != 0;
     const Graph& G = *g_;
     const int nops = (int)G.ops.size();
 
@@ -493,7 +601,7 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                                              std::to_string(K) + ")");
                 int64_t M = xin.nrows();
                 int64_t row0 = 0;
-                const bool last_only = logits_last_only_ && outputs.count(out) && M > 1;
+                const bool last_only = logits_last_only_ && outputs.count(out) && M > 1 && !pg.batch;
                 if (last_only) {
                     row0 = M - 1;
                     o.ne[1] = 1;
@@ -902,12 +1010,16 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                 __half* vc;
                 int64_t ctx;
                 BufRef kref, vref;
+                int64_t slot_elems = 0;
+                int64_t sb = 0;  // bytes per slot window: single-sequence launches add kv_slot * sb
                 if (use_cache) {
                     const KVCache& c = kv_.at(op.id);
                     GB_CHECK(c.hd == hd && c.Hkv == Hkv, "KV cache shape mismatch");
                     kc = c.k;
                     vc = c.v;
                     ctx = c.ctx;
+                    slot_elems = c.slot_elems();
+                    sb = pg.batch ? 0 : slot_elems * 2;
                     kref.fixed = (char*)kc;
                     vref.fixed = (char*)vc;
                 } else {
@@ -954,6 +1066,8 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                 };
                 Src sq = src_of(q), sk = src_of(k), sv = src_of(v);
                 if (s == 1) sq.row_nb = sk.row_nb = sv.row_nb = 0;  // one row: stride unused
+                GB_CHECK(!pg.batch || (use_cache && sq.ok && sk.ok && sv.ok),
+                         "batched decode needs the fused attention path over the KV cache");
                 bool fuse = sq.ok && sk.ok && sv.ok && !sv.rot && sq.rot == sk.rot &&
                             sq.ref.buf == sk.ref.buf && sk.ref.buf == sv.ref.buf &&
                             sq.ref.fixed == sk.ref.fixed && sk.ref.fixed == sv.ref.fixed &&
@@ -975,7 +1089,7 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                     y.ne[1] = Hq;
                     y.ne[2] = s;
                     y.ne[3] = 1;
-                    if (use_cache && s == 1) {
+                    if (use_cache && (s == 1 || pg.batch)) {
                         // which outputs the consumer chain needs (through a RESHAPE)
                         uint32_t look = out;
                         if (!outputs.count(out) && consumers[out].size() == 1 &&
@@ -990,11 +1104,15 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                             y.has_f = false;
                         }
                         if (nq) {
-                            y.q.buf = pg.new_buf(Hq * hd, oi);
-                            y.qd.buf = pg.new_buf(Hq * hd / QK * 4, oi);
+                            y.q.buf = pg.new_buf(s * Hq * hd, oi);
+                            y.qd.buf = pg.new_buf(s * Hq * hd / QK * 4, oi);
                             y.has_q = true;
                         }
                         AttnDecArgs da;
+                        da.rows = (int)s;
+                        da.batched = pg.batch;
+                        da.qkv_stride = sq.row_nb / 4;
+                        da.slot_elems = slot_elems;
                         da.q_off = q_off;
                         da.k_off = k_off;
                         da.v_off = v_off;
@@ -1010,12 +1128,14 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         da.max_kv = kv_max_ctx_;
                         da.splits = attn_decode_splits(Hkv, kv_max_ctx_);
                         BufRef wref;
-                        wref.buf = pg.new_buf((int64_t)attn_decode_workspace(Hq, hd, da.splits), oi);
+                        wref.buf = pg.new_buf((int64_t)attn_decode_workspace(Hq, hd, da.splits) * s, oi);
                         const BufRef yr = y.ref, yq = y.q, yqd = y.qd;
                         const bool hf = y.has_f, hq = y.has_q;
                         const double kvb = (double)Hkv * hd * 2 * 2;  // K+V bytes per position
                         add("attn_decode", [=](Program& p, cudaStream_t st) {
                             AttnDecArgs a = da;
+                            a.kc = (__half*)((char*)da.kc + p.kv_slot * sb);
+                            a.vc = (__half*)((char*)da.vc + p.kv_slot * sb);
                             a.qkv = (const float*)p.ptr(base);
                             a.part = (float*)p.ptr(wref);
                             if (hf) a.o = (float*)p.ptr(yr);
@@ -1051,8 +1171,8 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                             QkvRopeArgs a = ra;
                             a.qkv = (const float*)p.ptr(base);
                             a.q_out = (float*)p.ptr(qtr);
-                            a.kc = (__half*)p.ptr(kref);
-                            a.vc = (__half*)p.ptr(vref);
+                            a.kc = (__half*)(p.ptr(kref) + p.kv_slot * sb);
+                            a.vc = (__half*)(p.ptr(vref) + p.kv_slot * sb);
                             launch_rope_qkv(a, st);
                         });
                         Val qv = qt;  // view [hd, s, Hq] of the [s][Hq][hd] buffer
@@ -1069,8 +1189,8 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         const bool step_on = use_cache;
                         pg.use(qt.ref, oi);
                         add("attention", [=](Program& p, cudaStream_t st) {
-                            launch_attention(p.view(qv), (const __half*)p.ptr(kref),
-                                             (const __half*)p.ptr(vref), ctx, Hkv, dstep, step_on, 0,
+                            launch_attention(p.view(qv), (const __half*)(p.ptr(kref) + p.kv_slot * sb),
+                                             (const __half*)(p.ptr(vref) + p.kv_slot * sb), ctx, Hkv, dstep, step_on, 0,
                                              scale, (float*)p.ptr(yr),
                                              wbytes ? p.ptr(wref) : nullptr, max_kv, st);
                         });
@@ -1117,8 +1237,8 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                 materialize(k);
                 const Val ks = heads_then_rows(k), vs = heads_then_rows(v), qs = q;
                 add("kv_write", [=](Program& p, cudaStream_t st) {
-                    KVDst kd{(__half*)p.ptr(kref), ctx};
-                    KVDst vd{(__half*)p.ptr(vref), ctx};
+                    KVDst kd{(__half*)(p.ptr(kref) + p.kv_slot * sb), ctx};
+                    KVDst vd{(__half*)(p.ptr(vref) + p.kv_slot * sb), ctx};
                     launch_kv_write(p.view(ks), dstep, kd, st);
                     launch_kv_write(p.view(vs), dstep, vd, st);
                 });
@@ -1136,7 +1256,8 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                 const BufRef yr = y.ref;
                 const bool step_on = use_cache;
                 add("attention", [=](Program& p, cudaStream_t st) {
-                    launch_attention(p.view(qs), (const __half*)p.ptr(kref), (const __half*)p.ptr(vref),
+                    launch_attention(p.view(qs), (const __half*)(p.ptr(kref) + p.kv_slot * sb),
+                                     (const __half*)(p.ptr(vref) + p.kv_slot * sb),
                                      ctx, Hkv, dstep, step_on, 0, scale, (float*)p.ptr(yr),
                                      wbytes ? p.ptr(wref) : nullptr, max_kv, st);
                 });
@@ -1251,7 +1372,8 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
         placed.push_back(b);
     }
     pg.arena_bytes = (size_t)total;
-    if (total) GB_CUDA(cudaMalloc(&pg.arena, (size_t)total));
+    ensure_arena((size_t)total);
+    pg.arena = &arena_;
     return P;
 }
 
@@ -1268,16 +1390,21 @@ void Executor::prepare(const SymEnv& env_in, bool /*arena_reuse*/) {
     if (logits_last_only_) key += "/last";
     SymEnv shape_env;
     for (auto& [k, v] : env)
-        if (k != "pos") shape_env[k] = v;
+        if (k != "pos" && k != "slot") shape_env[k] = v;
     std::vector<std::pair<std::string, int64_t>> items(shape_env.begin(), shape_env.end());
     std::sort(items.begin(), items.end());
     for (auto& [k, v] : items) key += "/" + k + "=" + std::to_string(v);
-    if (kv) {
+    const bool batch = env.count("__rows") != 0;
+    if (kv && !batch) {
         int64_t s = env.count("s") ? env.at("s") : 1;
         GB_CHECK(pos >= 0 && pos + s <= kv_max_ctx_,
                  "KV cache overflow: pos " + std::to_string(pos) + " + s " + std::to_string(s) +
                      " > max_ctx " + std::to_string(kv_max_ctx_));
+        const int64_t slot = env.count("slot") ? env.at("slot") : 0;
+        const int64_t slots = kv_.empty() ? 1 : kv_.begin()->second.slots;
+        GB_CHECK(slot >= 0 && slot < slots, "KV slot " + std::to_string(slot) + " out of range");
     }
+    GB_CHECK(!batch || kv, "batched decode needs the KV cache");
     auto it = programs_.find(key);
     if (it == programs_.end()) {
         SymEnv benv = shape_env;
@@ -1285,13 +1412,14 @@ void Executor::prepare(const SymEnv& env_in, bool /*arena_reuse*/) {
         auto p = build(benv, kv);
         p->key = key;
         p->s = env.count("s") ? env.at("s") : 0;
-        p->decode = kv && p->s == 1;
+        p->decode = kv && (p->s == 1 || batch);
         programs_[key] = p;
         active_ = p;
     } else {
         active_ = it->second;
     }
     h_step_->pos = pos;
+    active_->kv_slot = env.count("slot") ? env.at("slot") : 0;
     if (profile_on_) {
         profile_.prepare_ms += now_ms() - t0;
         profile_.n_prepare++;
@@ -1342,7 +1470,12 @@ void Executor::run() {
             k.bytes += p.launch_bytes[i];
         }
     } else if (cuda_graph_ && p.decode) {
+        if (p.graph_exec && p.graph_slot != p.kv_slot) {
+            cudaGraphExecDestroy(p.graph_exec);
+            p.graph_exec = nullptr;
+        }
         if (!p.graph_exec) {
+            p.graph_slot = p.kv_slot;
             cudaGraph_t graph;
             GB_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
             try {

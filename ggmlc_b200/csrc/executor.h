@@ -68,9 +68,12 @@ struct Program {
     SymEnv env;
     bool kv = false;
     bool decode = false;
+    bool batch = false;  // batched decode: row r is the next token of the sequence in a slot
     std::vector<int64_t> buf_size, buf_first, buf_last, buf_off;
-    char* arena = nullptr;
+    char* const* arena = nullptr;  // the executor's shared activation arena (grows on demand)
     size_t arena_bytes = 0;
+    int64_t kv_slot = 0;           // KV slot of a single-sequence program (set by prepare)
+    int64_t graph_slot = -1;       // kv_slot the captured graph was recorded with
     std::vector<Launch> launches;
     std::vector<std::string> launch_names;
     std::vector<double> launch_bytes;  // algorithmic HBM bytes of each launch (0 if untracked)
@@ -83,7 +86,7 @@ struct Program {
     char* ptr(const BufRef& r) const {
         if (r.fixed) return r.fixed + r.off;
         if (r.buf < 0) return nullptr;
-        return arena + buf_off[r.buf] + r.off;
+        return *arena + buf_off[r.buf] + r.off;
     }
     int new_buf(int64_t bytes, int first) {
         buf_size.push_back((bytes + 255) / 256 * 256);
@@ -101,6 +104,8 @@ struct KVCache {
     __half* k = nullptr;
     __half* v = nullptr;
     int64_t hd = 0, Hkv = 0, batch = 1, ctx = 0;
+    int64_t slots = 1;  // sequence windows [slot][Hkv][ctx][hd], slot_elems apart
+    int64_t slot_elems() const { return Hkv * ctx * hd; }
 };
 
 class Executor {
@@ -128,6 +133,23 @@ public:
     void init_kv_cache(int64_t max_ctx);
     void reset_kv_cache();
     bool has_kv_cache() const { return kv_enabled_; }
+
+    // Paged KV cache (executor.h:147-161 of the reference): max_batch sequence slots of max_ctx
+    // positions each, plus one scratch slot that padding rows of a batched step write into.
+    // Slots are windows of one device allocation per layer; pages of tokens_per_page positions
+    // are accounted as sequences grow (paged_kv_ensure_tokens) and returned on free.
+    void init_paged_kv_cache(int64_t max_batch, int64_t max_ctx);
+    bool paged_kv_enabled() const { return paged_; }
+    void paged_kv_alloc_slot(int64_t slot);
+    void paged_kv_free_slot(int64_t slot);
+    void paged_kv_ensure_tokens(int64_t slot, int64_t total);
+    int64_t paged_active_vram_bytes() const;
+    int64_t tokens_per_page() const { return tokens_per_page_; }
+    void set_tokens_per_page(int64_t n);
+    int64_t paged_max_batch() const { return paged_ ? paged_max_batch_ : 0; }
+    // Batched decode step over `rows` sequences: row r decodes the token at position pos[r] of
+    // the sequence in slot slot[r] (rows padded up to a bucket use the scratch slot).
+    void prepare_batch(int rows, const int32_t* pos, const int32_t* slot);
     int64_t kv_max_ctx() const { return kv_max_ctx_; }
 
     void set_logits_last_only(bool on) { logits_last_only_ = on; }
@@ -175,6 +197,15 @@ private:
     std::map<uint32_t, KVCache> kv_;    // per FLASH_ATTN_EXT op id
     bool kv_enabled_ = false;
     int64_t kv_max_ctx_ = 0;
+    bool paged_ = false;
+    int64_t paged_max_batch_ = 0;
+    int64_t tokens_per_page_ = 256;
+    std::vector<int64_t> slot_tokens_;  // per slot: positions accounted (-1: free)
+    char* arena_ = nullptr;             // activation arena shared by every program
+    size_t arena_cap_ = 0;
+    void ensure_arena(size_t bytes);
+    void alloc_kv(int64_t slots, int64_t max_ctx);
+    void free_kv();
     bool logits_last_only_ = false;
     bool cuda_graph_ = false;
     bool profile_on_ = false;

@@ -112,14 +112,19 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(AttnDecArgs a) {
     float* sq = sstat + kMaxRk * 3;          // [kMaxRk][HD] rotated q (fp16-rounded)
     const int rk = a.Hq / a.Hkv;
     const int hk = blockIdx.y;
+    const int row = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t pos = (a.step ? a.step->pos : 0) + a.pos_off;  // position of the new token
+    // position of the new token and the KV window of its sequence
+    const int64_t pos = a.batched ? (int64_t)a.step->row_pos[row]
+                                  : (a.step ? a.step->pos : 0) + a.pos_off;
+    __half* kslot = a.kc + (a.batched ? (int64_t)a.step->row_slot[row] * a.slot_elems : 0);
+    __half* vslot = a.vc + (a.batched ? (int64_t)a.step->row_slot[row] * a.slot_elems : 0);
     const int64_t nkv = pos + 1;
     const int64_t per = (nkv + gridDim.x - 1) / gridDim.x;
     const int64_t c0 = min((int64_t)blockIdx.x * per, nkv);
     const int64_t c1 = min(c0 + per, nkv);
-    const __half* kbase = a.kc + ((int64_t)hk * a.ctx) * HD;
-    const __half* vbase = a.vc + ((int64_t)hk * a.ctx) * HD;
+    const __half* kbase = kslot + ((int64_t)hk * a.ctx) * HD;
+    const __half* vbase = vslot + ((int64_t)hk * a.ctx) * HD;
     auto stage = [&](int buf, int64_t cs, int rows) {
         __half* dk = sk + buf * kChunk * HD;
         __half* dv = sv + buf * kChunk * HD;
@@ -136,20 +141,20 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(AttnDecArgs a) {
     pdl_wait();
     pdl_launch();
 
-    const float* row = a.qkv;
+    const float* qrow = a.qkv + (int64_t)row * a.qkv_stride;
     for (int e = threadIdx.x; e < rk * HD; e += kDecThreads) {
         const int h = e / HD, d = e % HD;
-        const float* src = row + a.q_off + (int64_t)(hk * rk + h) * HD;
+        const float* src = qrow + a.q_off + (int64_t)(hk * rk + h) * HD;
         sq[e] = __half2float(__float2half_rn(rope_elem(src, d, HD, a.tab, pos)));
     }
     if (c0 <= pos && pos < c1) {
         // this split holds the new position: rotate its k, write k and v to the cache
-        const float* ks = row + a.k_off + (int64_t)hk * HD;
+        const float* ks = qrow + a.k_off + (int64_t)hk * HD;
         for (int d = threadIdx.x; d < HD; d += kDecThreads) {
             const __half kh = __float2half_rn(rope_elem(ks, d, HD, a.tab, pos));
-            const __half vh = __float2half_rn(row[a.v_off + (int64_t)hk * HD + d]);
-            a.kc[((int64_t)hk * a.ctx + pos) * HD + d] = kh;
-            a.vc[((int64_t)hk * a.ctx + pos) * HD + d] = vh;
+            const __half vh = __float2half_rn(qrow[a.v_off + (int64_t)hk * HD + d]);
+            kslot[((int64_t)hk * a.ctx + pos) * HD + d] = kh;
+            vslot[((int64_t)hk * a.ctx + pos) * HD + d] = vh;
             snew[d] = kh;
             snew[HD + d] = vh;
         }
@@ -241,7 +246,8 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(AttnDecArgs a) {
         }
     }
     __syncthreads();
-    float* part = a.part + ((int64_t)blockIdx.x * a.Hq + (int64_t)hk * rk) * (HD + 4);
+    float* part = a.part + (int64_t)row * gridDim.x * a.Hq * (HD + 4) +
+                  ((int64_t)blockIdx.x * a.Hq + (int64_t)hk * rk) * (HD + 4);
     if (threadIdx.x < rk) {
         part[threadIdx.x * (HD + 4) + 0] = c0 < c1 ? sstat[threadIdx.x * 3 + 0] : -INFINITY;
         part[threadIdx.x * (HD + 4) + 1] = c0 < c1 ? sstat[threadIdx.x * 3 + 1] : 0.0f;
@@ -263,9 +269,10 @@ __global__ void __launch_bounds__(HD) k_attn_combine(AttnDecArgs a) {
     pdl_wait();
     pdl_launch();
     const int h = blockIdx.x;  // q head
+    const int row = blockIdx.y;
     const int S = a.splits;
     const int d = threadIdx.x;
-    const float* base = a.part + (int64_t)h * (HD + 4);
+    const float* base = a.part + (int64_t)row * S * a.Hq * (HD + 4) + (int64_t)h * (HD + 4);
     const int64_t sstride = (int64_t)a.Hq * (HD + 4);
     float pv[kMaxSplits];
 #pragma unroll
@@ -294,13 +301,14 @@ __global__ void __launch_bounds__(HD) k_attn_combine(AttnDecArgs a) {
         v3 += pv[sp + 3] * sw[sp + 3];
     }
     const float v = ((v0 + v1) + (v2 + v3)) * inv;
-    if (a.o) a.o[(int64_t)h * HD + d] = v;
+    const int64_t oi = ((int64_t)row * a.Hq + h) * HD + d;
+    if (a.o) a.o[oi] = v;
     if (a.oq) {  // warp w owns elements 32w..32w+31 of the head: one Q8_0 block
         const int lane = threadIdx.x & 31;
         float d16, q;
         q8_block(v, lane, d16, q);
-        a.oq[(int64_t)h * HD + d] = (int8_t)__float2int_rn(q);
-        if (lane == 0) a.od[((int64_t)h * HD + d) / 32] = d16;
+        a.oq[oi] = (int8_t)__float2int_rn(q);
+        if (lane == 0) a.od[oi / 32] = d16;
     }
 }
 
@@ -325,8 +333,9 @@ void launch_dec(const AttnDecArgs& a, cudaStream_t st) {
             configured[dev & 63] = true;
         }
     }
-    launch_pdl(k_attn_decode<HD>, dim3((unsigned)a.splits, (unsigned)a.Hkv), kDecThreads, smem, st, a);
-    launch_pdl(k_attn_combine<HD>, dim3((unsigned)a.Hq), HD, 0, st, a);
+    launch_pdl(k_attn_decode<HD>, dim3((unsigned)a.splits, (unsigned)a.Hkv, (unsigned)a.rows),
+               kDecThreads, smem, st, a);
+    launch_pdl(k_attn_combine<HD>, dim3((unsigned)a.Hq, (unsigned)a.rows), HD, 0, st, a);
 }
 
 }  // namespace
@@ -358,6 +367,9 @@ void launch_attn_decode(const AttnDecArgs& a, cudaStream_t st) {
     GB_CHECK(a.Hkv > 0 && a.Hq % a.Hkv == 0 && a.Hq / a.Hkv <= kMaxRk,
              "attn_decode: GQA group too large");
     GB_CHECK(a.splits >= 1 && a.splits <= kMaxSplits, "attn_decode: bad split count");
+    GB_CHECK(a.rows >= 1 && a.rows <= kMaxRows && (a.rows == 1 || a.batched),
+             "attn_decode: 1..16 rows, several only in batched mode");
+    GB_CHECK(!a.batched || a.step, "attn_decode: batched mode reads positions from step params");
     switch (a.hd) {
         case 64: launch_dec<64>(a, st); break;
         case 128: launch_dec<128>(a, st); break;

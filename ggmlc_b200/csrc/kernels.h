@@ -22,8 +22,11 @@
 namespace gb {
 
 // Per-step values read by kernels inside captured graphs (decode replays change only these).
+constexpr int kMaxRows = 16;  // rows of a batched decode step (sequences decoded together)
 struct StepParams {
-    int64_t pos;  // first position of this call's tokens in the KV cache
+    int64_t pos;                  // first position of this call's tokens in the KV cache
+    int32_t row_pos[kMaxRows];    // batched decode: position of each row's token
+    int32_t row_slot[kMaxRows];   // batched decode: KV-cache slot of each row's sequence
 };
 
 __host__ __device__ inline int64_t quant_bytes(int type) { return type == 8 ? 32 : 16; }
@@ -200,9 +203,16 @@ struct AttnDecArgs {
     float* o = nullptr;
     int8_t* oq = nullptr;
     float* od = nullptr;
+    // batched decode (rows > 1 or batched): row r of qkv (qkv_stride floats apart) is the new
+    // token of a sequence at position step->row_pos[r] in KV slot step->row_slot[r]; slots are
+    // slot_elems elements apart in kc / vc; outputs and partials are per row
+    int rows = 1;
+    bool batched = false;
+    int64_t qkv_stride = 0;
+    int64_t slot_elems = 0;
 };
 int attn_decode_splits(int64_t Hkv, int64_t max_kv);
-size_t attn_decode_workspace(int64_t Hq, int64_t hd, int splits);
+size_t attn_decode_workspace(int64_t Hq, int64_t hd, int splits);  // per row
 void launch_attn_decode(const AttnDecArgs& a, cudaStream_t st);
 // Size of the per-device static split scratch behind gb_attn_decode_noalloc.
 constexpr size_t kAttnDecStaticWorkBytes = size_t(4) << 20;

@@ -1,0 +1,170 @@
+#include "scheduler.h"
+
+#include <algorithm>
+#include <cmath>
+
+#include "common.h"
+#include "kernels.h"
+
+namespace gb {
+
+Scheduler::Scheduler(Executor& ex, int max_batch, int eos, int64_t max_ctx)
+    : ex_(ex), max_batch_(max_batch), eos_(eos) {
+    GB_CHECK(max_batch >= 1 && max_batch <= kMaxRows, "scheduler: max_batch_size must be 1..16");
+    const Graph& g = ex.graph();
+    bool have_in = false;
+    for (uint32_t id : g.inputs)
+        if (g.t(id).type == T_I32) {
+            in_id_ = id;
+            have_in = true;
+            break;
+        }
+    GB_CHECK(have_in, "scheduler: the graph has no int32 token-id input");
+    GB_CHECK(!g.outputs.empty(), "scheduler: the graph has no output");
+    out_id_ = g.outputs[0];
+    ex.init_paged_kv_cache(max_batch, max_ctx);
+    ex.set_logits_last_only(true);
+    slots_.assign((size_t)max_batch, nullptr);
+}
+
+Scheduler::~Scheduler() {
+    for (size_t i = 0; i < slots_.size(); ++i)
+        if (slots_[i]) {
+            try {
+                ex_.paged_kv_free_slot((int64_t)i);
+            } catch (...) {
+            }
+        }
+}
+
+uint64_t Scheduler::add_request(const std::vector<int32_t>& prompt, int max_new, float temperature,
+                                int eos) {
+    GB_CHECK(!prompt.empty(), "scheduler: empty prompt");
+    GB_CHECK(max_new >= 1, "scheduler: max_new_tokens must be at least 1");
+    GB_CHECK((int64_t)prompt.size() + max_new <= ex_.kv_max_ctx(),
+             "scheduler: prompt + max_new_tokens exceed the KV cache length");
+    auto r = std::make_shared<GenRequest>();
+    r->id = next_id_++;
+    r->prompt = prompt;
+    r->max_new = max_new;
+    r->temperature = temperature;
+    r->eos = eos >= 0 ? eos : eos_;
+    pending_.push_back(r);
+    all_[r->id] = r;
+    return r->id;
+}
+
+bool Scheduler::has_work() const { return !pending_.empty() || active_count() > 0; }
+
+size_t Scheduler::active_count() const {
+    size_t n = 0;
+    for (auto& s : slots_) n += s ? 1 : 0;
+    return n;
+}
+
+std::shared_ptr<GenRequest> Scheduler::get(uint64_t id) const {
+    auto it = all_.find(id);
+    return it == all_.end() ? nullptr : it->second;
+}
+
+// greedy: the first maximum; otherwise a draw from softmax(logits / temperature)
+// (batch_scheduler.cpp:94-128)
+int32_t Scheduler::sample(const float* logits, int64_t vocab, float temperature) {
+    int64_t best = 0;
+    for (int64_t i = 1; i < vocab; ++i)
+        if (logits[i] > logits[best]) best = i;
+    if (temperature <= 0.0f) return (int32_t)best;
+    std::vector<float> p((size_t)vocab);
+    float total = 0.0f;
+    for (int64_t i = 0; i < vocab; ++i) {
+        p[(size_t)i] = std::exp((logits[i] - logits[best]) / temperature);
+        total += p[(size_t)i];
+    }
+    std::uniform_real_distribution<float> u(0.0f, total);
+    float r = u(rng_), run = 0.0f;
+    for (int64_t i = 0; i < vocab; ++i) {
+        run += p[(size_t)i];
+        if (run >= r) return (int32_t)i;
+    }
+    return (int32_t)(vocab - 1);
+}
+
+void Scheduler::finish(const std::shared_ptr<GenRequest>& r, int32_t tok, StepOut& out) {
+    const bool stop = r->eos >= 0 && tok == r->eos;
+    const bool length = (int)r->generated.size() >= r->max_new || r->pos >= ex_.kv_max_ctx();
+    if (!stop && !length) return;
+    r->finished = true;
+    r->finish_reason = stop ? "stop" : "length";
+    out.completed.push_back(r->id);
+    ex_.paged_kv_free_slot(r->slot);
+    slots_[(size_t)r->slot] = nullptr;
+}
+
+StepOut Scheduler::step() {
+    StepOut out;
+    // admission: one pending request per step, prefilled alone into a free slot
+    if (!pending_.empty()) {
+        int slot = -1;
+        for (size_t i = 0; i < slots_.size(); ++i)
+            if (!slots_[i]) {
+                slot = (int)i;
+                break;
+            }
+        if (slot >= 0) {
+            auto r = pending_.front();
+            pending_.pop_front();
+            r->slot = slot;
+            slots_[(size_t)slot] = r;
+            ex_.paged_kv_alloc_slot(slot);
+            const int64_t n = (int64_t)r->prompt.size();
+            ex_.paged_kv_ensure_tokens(slot, n + r->max_new);
+            SymEnv env;
+            env["s"] = n;
+            for (auto& s : ex_.graph().symbol_table) env[s] = n;
+            env["pos"] = 0;
+            env["slot"] = slot;
+            ex_.prepare(env, true);
+            ex_.set_input(in_id_, r->prompt.data(), r->prompt.size() * 4);
+            ex_.run();
+            size_t bytes = 0;
+            const float* logits = (const float*)ex_.get_output(out_id_, &bytes);
+            const int64_t vocab = (int64_t)(bytes / 4);  // last row only
+            const int32_t tok = sample(logits, vocab, r->temperature);
+            r->generated.push_back(tok);
+            r->pos = n;
+            out.new_tokens.push_back({r->id, tok});
+            finish(r, tok, out);
+            return out;
+        }
+    }
+    // one batched decode step over every active sequence, rows padded to a bucket
+    std::vector<std::shared_ptr<GenRequest>> act;
+    for (auto& s : slots_)
+        if (s) act.push_back(s);
+    if (act.empty()) return out;
+    int rows = 1;
+    while (rows < (int)act.size()) rows *= 2;
+    std::vector<int32_t> pos((size_t)rows, 0), slot((size_t)rows, max_batch_), tok((size_t)rows, 0);
+    for (size_t i = 0; i < act.size(); ++i) {
+        pos[i] = (int32_t)act[i]->pos;
+        slot[i] = act[i]->slot;
+        tok[i] = act[i]->generated.back();
+    }
+    ex_.prepare_batch(rows, pos.data(), slot.data());
+    ex_.set_input(in_id_, tok.data(), tok.size() * 4);
+    ex_.run();
+    size_t bytes = 0;
+    const float* logits = (const float*)ex_.get_output(out_id_, &bytes);
+    const int64_t vocab = (int64_t)(bytes / 4 / (size_t)rows);
+    for (size_t i = 0; i < act.size(); ++i) {
+        auto& r = act[i];
+        const int32_t t = sample(logits + (int64_t)i * vocab, vocab, r->temperature);
+        r->generated.push_back(t);
+        r->pos += 1;
+        out.new_tokens.push_back({r->id, t});
+        finish(r, t, out);
+    }
+    return out;
+}
+
+}  // namespace gb

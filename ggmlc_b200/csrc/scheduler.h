@@ -1,0 +1,79 @@
+// Continuous batching over the executor's paged KV slots: the engine-side counterpart of the
+// reference's ContinuousBatchScheduler (runtime/include/ggmlc/batch_scheduler.h:35-77,
+// runtime/src/batch_scheduler.cpp:130-403), with the same request / step / result interface.
+//
+// Differences by design: every sequence decodes at its own position in its own slot (one
+// batched step over all active sequences, rows padded to a bucket of 1/2/4/8/16 with a scratch
+// slot), where the reference runs one shared position over all slots; the graph needs no batch
+// dimension (rows of the sequence axis are the batch).  Prefix caching is not implemented:
+// enable_prefix_caching is accepted and the hit counters stay zero.
+#pragma once
+
+#include <cstdint>
+#include <deque>
+#include <map>
+#include <memory>
+#include <random>
+#include <string>
+#include <utility>
+#include <vector>
+
+#include "executor.h"
+
+namespace gb {
+
+struct GenRequest {
+    uint64_t id = 0;
+    std::vector<int32_t> prompt;
+    std::vector<int32_t> generated;
+    int slot = -1;
+    int64_t pos = 0;       // position of the next token to decode
+    int max_new = 32;
+    float temperature = 0.0f;
+    int eos = -1;
+    bool finished = false;
+    std::string finish_reason;  // "stop" (end token) or "length" (max_new reached)
+};
+
+struct StepOut {
+    std::vector<std::pair<uint64_t, int32_t>> new_tokens;  // (request id, token)
+    std::vector<uint64_t> completed;
+};
+
+class Scheduler {
+public:
+    // Initialises the executor's paged KV cache for max_batch sequences of up to max_ctx
+    // positions (the reference uses 2048) and switches logits to the last row.
+    Scheduler(Executor& ex, int max_batch, int eos, int64_t max_ctx = 2048);
+    ~Scheduler();
+
+    uint64_t add_request(const std::vector<int32_t>& prompt, int max_new, float temperature,
+                         int eos);
+    // One iteration: admit one pending request (prefill into a free slot, first token) and
+    // return, or run one batched decode step over every active sequence.
+    StepOut step();
+    bool has_work() const;
+    size_t active_count() const;
+    size_t pending_count() const { return pending_.size(); }
+    int max_batch() const { return max_batch_; }
+    std::shared_ptr<GenRequest> get(uint64_t id) const;
+    void enable_prefix_caching(bool on) { prefix_caching_ = on; }
+    bool prefix_caching() const { return prefix_caching_; }
+
+private:
+    int32_t sample(const float* logits, int64_t vocab, float temperature);
+    void finish(const std::shared_ptr<GenRequest>& r, int32_t tok, StepOut& out);
+
+    Executor& ex_;
+    int max_batch_;
+    int eos_;
+    bool prefix_caching_ = true;
+    uint64_t next_id_ = 1;
+    uint32_t in_id_ = 0, out_id_ = 0;
+    std::deque<std::shared_ptr<GenRequest>> pending_;
+    std::vector<std::shared_ptr<GenRequest>> slots_;
+    std::map<uint64_t, std::shared_ptr<GenRequest>> all_;
+    std::mt19937 rng_{1337};
+};
+
+}  // namespace gb

@@ -111,6 +111,59 @@ const char* gb_executor_kernel_times(gb_executor* e);
 /* the executor's CUDA stream (cudaStream_t), for callers that order their own work after it */
 void* gb_executor_stream(const gb_executor* e);
 
+/* ---- paged KV cache (python_bindings.cpp:196-204; executor.cpp:634-920) ---------------------
+ * init_paged_kv_cache(max_batch, max_ctx): max_batch sequence slots (1..16) of max_ctx
+ * positions.  Slots are windows of one allocation per layer (no driver-VMM mapping); pages of
+ * tokens_per_page positions are accounted as a slot grows.  prepare() with symbol "slot" runs a
+ * single sequence in that slot; gb_executor_prepare_batch runs one decode token for each of
+ * `rows` sequences (row r at position pos[r] in slot slot[r]; slot == max_batch is a scratch
+ * slot for padding rows). */
+int gb_executor_init_paged_kv_cache(gb_executor* e, int64_t max_batch, int64_t max_ctx);
+int gb_executor_is_paged_kv_cache_enabled(const gb_executor* e);
+int gb_executor_paged_kv_alloc_slot(gb_executor* e, int64_t slot);
+int gb_executor_paged_kv_free_slot(gb_executor* e, int64_t slot);
+int gb_executor_paged_kv_ensure_tokens(gb_executor* e, int64_t slot, int64_t total_tokens);
+int64_t gb_executor_paged_active_vram_bytes(const gb_executor* e);
+int64_t gb_executor_tokens_per_page(const gb_executor* e);
+int gb_executor_set_tokens_per_page(gb_executor* e, int64_t tokens_per_page);
+int gb_executor_prepare_batch(gb_executor* e, int rows, const int32_t* pos, const int32_t* slot);
+
+/* ---- ContinuousBatchScheduler (batch_scheduler.h:35-77; python_bindings.cpp:261-295) --------
+ * Iteration-level continuous batching over the paged KV cache: add_request queues a prompt;
+ * each step either admits one request (prefill into a free slot, first token) or decodes one
+ * token for every active sequence at its own position.  Greedy when temperature <= 0. */
+typedef struct gb_scheduler gb_scheduler;
+typedef struct gb_request_info {
+    uint64_t request_id;
+    int slot_id;
+    int64_t current_pos;
+    int max_new_tokens;
+    float temperature;
+    int eos_token_id;
+    int finished;
+    const char* finish_reason; /* "stop", "length" or "" (valid while the scheduler lives) */
+    int64_t n_prompt_tokens;
+    int64_t n_generated_tokens;
+    int64_t prefix_tokens_matched;
+} gb_request_info;
+int gb_scheduler_create(gb_executor* e, int max_batch_size, int eos_token_id, gb_scheduler** out);
+void gb_scheduler_free(gb_scheduler* s);
+int gb_scheduler_add_request(gb_scheduler* s, const int32_t* prompt, int64_t n, int max_new_tokens,
+                             float temperature, int eos_token_id, uint64_t* request_id);
+/* new tokens as (ids[i], tokens[i]), i < *n_new; completed request ids in done[j], j < *n_done */
+int gb_scheduler_step(gb_scheduler* s, uint64_t* ids, int32_t* tokens, int cap, int* n_new,
+                      uint64_t* done, int cap_done, int* n_done);
+int gb_scheduler_has_work(const gb_scheduler* s);
+int64_t gb_scheduler_active_count(const gb_scheduler* s);
+int64_t gb_scheduler_pending_count(const gb_scheduler* s);
+int gb_scheduler_max_batch_size(const gb_scheduler* s);
+int gb_scheduler_enable_prefix_caching(gb_scheduler* s, int enable);
+int gb_scheduler_is_prefix_caching_enabled(const gb_scheduler* s);
+int gb_scheduler_get_request(gb_scheduler* s, uint64_t request_id, gb_request_info* info);
+/* which: 0 prompt tokens, 1 generated tokens; copies min(cap, count) into buf, *n = count */
+int gb_scheduler_request_tokens(gb_scheduler* s, uint64_t request_id, int which, int32_t* buf,
+                                int64_t cap, int64_t* n);
+
 /* ---- op-level entry points (device pointers) ------------------------------------------------
  * The kernels behind the executor, exposed for operator tests and the operator sweep.  They
  * replace the CUDA ops of ggml-cuda the reference dispatches on this path.  Layouts:

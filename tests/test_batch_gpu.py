@@ -1,0 +1,140 @@
+"""Continuous batching over the paged KV cache (the reference's ContinuousBatchScheduler,
+runtime/src/batch_scheduler.cpp:130-403, and its e2e test tests/e2e/test_continuous_batching.py).
+
+Every sequence in a batched step decodes at its own position in its own slot.  Up to 8 rows run
+the decode GEMV whose per-row arithmetic does not depend on the row count, so a request's tokens
+must equal the same prompt decoded alone; 16 rows run the tensor-core GEMM and are compared at
+the logits level."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, cuda_available
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not cuda_available(), reason="needs a CUDA device")]
+
+MAX_CTX = 256
+
+
+def cos(a, b):
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    return float(a @ b / np.linalg.norm(a) / np.linalg.norm(b))
+
+
+def _executor(fixture):
+    from ggmlc_b200 import _runtime as R
+
+    g = R.ModelLoader.load_from_file(str(GOLDEN / f"{fixture}.gguf"))
+    return g, R.ModelExecutor(g, "cuda")
+
+
+def _single(fixture, prompt, n_new):
+    """Greedy tokens and per-step logits of one sequence decoded alone (paged slot 0)."""
+    g, ex = _executor(fixture)
+    ex.init_paged_kv_cache(1, MAX_CTX)
+    ex.set_logits_last_only(True)
+    sym = g.symbol_table
+    in_id, out_id = g.inputs[0], g.outputs[0]
+    env = {"s": len(prompt), "pos": 0, "slot": 0, **{s: len(prompt) for s in sym}}
+    ex.prepare(env)
+    ex.set_input_by_id(in_id, np.asarray(prompt, np.int32))
+    ex.run()
+    lg = [ex.get_output_array(out_id).reshape(-1)]
+    toks = [int(np.argmax(lg[-1]))]
+    pos = len(prompt)
+    while len(toks) < n_new:
+        ex.prepare_batch(np.array([pos], np.int32), np.array([0], np.int32))
+        ex.set_input_by_id(in_id, np.array([toks[-1]], np.int32))
+        ex.run()
+        lg.append(ex.get_output_array(out_id).reshape(-1))
+        toks.append(int(np.argmax(lg[-1])))
+        pos += 1
+    return toks, lg
+
+
+def _prompts(rng, lengths, vocab):
+    return [rng.integers(1, vocab, size=n).astype(np.int32) for n in lengths]
+
+
+@pytest.mark.parametrize("fixture", ["tiny_llama_q8_0", "tiny_llama_q4_0"])
+def test_scheduler_tokens_match_single_sequence_decode(fixture):
+    from ggmlc_b200 import _runtime as R
+
+    rng = np.random.default_rng(11)
+    lengths = [5, 17, 33, 9, 40, 3]
+    n_new = 10
+    g, ex = _executor(fixture)
+    vocab = int(np.load(GOLDEN / f"{fixture}.npz")["full_logits"].shape[1])
+    prompts = _prompts(rng, lengths, vocab)
+    sched = R.ContinuousBatchScheduler(ex, max_batch_size=4, eos_token_id=-1)
+    ex.init_paged_kv_cache(4, MAX_CTX)  # same cache length as the single-sequence runs
+    ids = [sched.add_request(p, max_new_tokens=n_new, temperature=0.0) for p in prompts]
+    assert sched.pending_count() == len(prompts)
+    streamed = {i: [] for i in ids}
+    steps = 0
+    peak_active = 0
+    while sched.has_work():
+        res = sched.step()
+        for rid, tok in res.new_tokens:
+            streamed[rid].append(tok)
+        peak_active = max(peak_active, sched.active_count())
+        steps += 1
+        assert steps < 500
+    assert peak_active == 4  # the slots were shared, more requests than slots
+    assert ex.get_paged_active_vram_bytes() == 0  # every slot returned
+    for rid, p in zip(ids, prompts):
+        req = sched.get_request(rid)
+        assert req.finished and req.finish_reason == "length"
+        assert req.generated_tokens == streamed[rid]
+        ref, _ = _single(fixture, p, n_new)
+        assert req.generated_tokens == ref, f"request {rid} (prompt {len(p)})"
+
+
+def test_batched_step_of_16_matches_single_sequences():
+    fixture = "tiny_llama_q8_0"
+    rng = np.random.default_rng(5)
+    g, ex = _executor(fixture)
+    vocab = int(np.load(GOLDEN / f"{fixture}.npz")["full_logits"].shape[1])
+    lengths = list(rng.integers(3, 60, size=16))
+    prompts = _prompts(rng, lengths, vocab)
+    ex.init_paged_kv_cache(16, MAX_CTX)
+    ex.set_logits_last_only(True)
+    sym = g.symbol_table
+    in_id, out_id = g.inputs[0], g.outputs[0]
+    first = []
+    for slot, p in enumerate(prompts):
+        ex.paged_kv_alloc_slot(slot)
+        ex.paged_kv_ensure_tokens(slot, len(p) + 1)
+        ex.prepare({"s": len(p), "pos": 0, "slot": slot, **{s: len(p) for s in sym}})
+        ex.set_input_by_id(in_id, p)
+        ex.run()
+        first.append(int(np.argmax(ex.get_output_array(out_id))))
+    assert ex.get_paged_active_vram_bytes() > 0
+    pos = np.array([len(p) for p in prompts], np.int32)
+    ex.prepare_batch(pos, np.arange(16, dtype=np.int32))
+    ex.set_input_by_id(in_id, np.array(first, np.int32))
+    ex.run()
+    out = ex.get_output_array(out_id).reshape(16, -1)
+    for r, p in enumerate(prompts):
+        _, lg = _single(fixture, p, 2)
+        assert cos(out[r], lg[1]) >= 0.9999, f"row {r}"
+    for slot in range(16):
+        ex.paged_kv_free_slot(slot)
+    assert ex.get_paged_active_vram_bytes() == 0
+
+
+def test_scheduler_rejects_bad_requests():
+    from ggmlc_b200 import _runtime as R
+
+    g, ex = _executor("tiny_llama_q8_0")
+    sched = R.ContinuousBatchScheduler(ex, max_batch_size=2, eos_token_id=0)
+    with pytest.raises(RuntimeError):
+        sched.add_request([], max_new_tokens=4)
+    with pytest.raises(RuntimeError):
+        sched.add_request([1, 2, 3], max_new_tokens=4096)  # beyond the 2048-position cache
+    with pytest.raises(RuntimeError):
+        ex.prepare_batch(np.array([0], np.int32), np.array([7], np.int32))  # no such slot
