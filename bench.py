@@ -332,6 +332,13 @@ def run_ours(args) -> None:
     shares = {k: round(v[0] / dec_total, 4) for k, v in sorted(kt.items(), key=lambda x: -x[1][0])}
     pp_mm = kt_pp.get("gemm_q", [0, 1, 0])
 
+    cb_line = None
+    if not args.no_cb:
+        del ex  # free the single-sequence caches before the batched runs
+        try:
+            cb_line = run_cb(g, gguf, local)
+        except Exception as e:  # noqa: BLE001 - reported in the line, the main metric stands
+            cb_line = {"error": str(e)[:300]}
     if rank == 0:
         cb = cpu_baseline(gguf) if (world == 1 and not args.no_cpu_baseline) else None
         weights_gb = ex_weight_gb(g)
@@ -367,6 +374,7 @@ def run_ours(args) -> None:
                          "all_decode_gemv_gbs": round(gemv_gbs, 1),
                          "decode_share": shares},
             "cpu_baseline": cb,
+            "continuous_batching": cb_line,
             "clocks": clk,
             "gpu_launches": int(args.steps * (launches_pp + G * launches_tg)),
         }
@@ -374,6 +382,46 @@ def run_ours(args) -> None:
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_cb(g, gguf, local: int, steps: int = 256, buckets=(1, 2, 4, 8, 16)) -> dict:
+    """BASELINE configs[3] continuous batching: B sequences with prompt lengths uniform in
+    [64, 1024] (seeded) and `steps` greedy decode tokens each, through the scheduler on the
+    paged KV cache.  Per B: decode tokens/s (all sequences decoding together) and overall
+    tokens/s including the one-at-a-time admissions (prefill)."""
+    import time
+
+    from ggmlc_b200 import _runtime as R
+
+    out = {}
+    ex = R.ModelExecutor(g, f"cuda:{local}")
+    ex.set_enable_cuda_graph(True)
+    for B in buckets:
+        sched = R.ContinuousBatchScheduler(ex, max_batch_size=B, eos_token_id=-1)
+        rng = np.random.default_rng(100 + B)
+        lens = rng.integers(64, 1025, size=B)
+        for n in lens:
+            sched.add_request(rng.integers(0, 128256, size=int(n)).astype(np.int32),
+                              max_new_tokens=steps, temperature=0.0)
+        t_admit = t_dec = 0.0
+        n_dec_tokens = 0
+        while sched.has_work():
+            admitting = sched.pending_count() > 0
+            t0 = time.perf_counter()
+            res = sched.step()
+            dt = time.perf_counter() - t0
+            if admitting:
+                t_admit += dt
+            else:
+                t_dec += dt
+                n_dec_tokens += len(res.new_tokens)
+        total = B * steps
+        out[f"B{B}"] = {"decode_tokens_per_s": round(n_dec_tokens / t_dec, 1) if t_dec else None,
+                        "tokens_per_s": round(total / (t_admit + t_dec), 1),
+                        "prompt_tokens": int(lens.sum()), "admit_s": round(t_admit, 3),
+                        "decode_s": round(t_dec, 3)}
+        del sched
+    return out
 
 
 def ex_weight_gb(g) -> float:
@@ -503,6 +551,7 @@ def main():
     ap.add_argument("--gen", type=int, default=128)
     ap.add_argument("--ref-gen", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-cb", action="store_true", help="skip the continuous-batching leg")
     ap.add_argument("--case", choices=sorted(CASES), help="launch one decode kernel of the L8 "
                     "shapes (a small case for ncu) instead of the benchmark")
     ap.add_argument("--reps", type=int, default=5)

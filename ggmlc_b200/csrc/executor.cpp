@@ -118,6 +118,8 @@ Executor::~Executor() {
     if (h_step_) cudaFreeHost(h_step_);
     if (d_step_) cudaFree(d_step_);
     if (pinned_out_) cudaFreeHost(pinned_out_);
+    if (d_argmax_) cudaFree(d_argmax_);
+    if (h_argmax_) cudaFreeHost(h_argmax_);
     if (arena_) cudaFree(arena_);
     if (stream_) cudaStreamDestroy(stream_);
 }
@@ -1528,6 +1530,26 @@ const void* Executor::get_output(uint32_t tid, size_t* bytes) {
     std::memcpy(host.data(), pinned_out_, n);
     *bytes = n;
     return host.data();
+}
+
+void Executor::output_argmax(uint32_t tid, int rows, int32_t* out) {
+    GB_CHECK(active_, "output_argmax before prepare");
+    GB_CHECK(rows >= 1 && rows <= kMaxRows, "output_argmax: 1..16 rows");
+    auto it = active_->vals.find(tid);
+    GB_CHECK(it != active_->vals.end(), "unknown output tensor " + std::to_string(tid));
+    const Val& v = it->second;
+    GB_CHECK(v.has_f && v.type == T_F32 && v.contiguous(), "output_argmax: needs a contiguous f32 output");
+    const int64_t total = nelem(v.ne);
+    GB_CHECK(total % rows == 0, "output_argmax: output does not split into the rows");
+    if (!d_argmax_) {
+        GB_CUDA(cudaMalloc(&d_argmax_, kMaxRows * sizeof(int32_t)));
+        GB_CUDA(cudaMallocHost(&h_argmax_, kMaxRows * sizeof(int32_t)));
+    }
+    launch_argmax_rows((const float*)active_->ptr(v.ref), rows, total / rows, d_argmax_, stream_);
+    GB_CUDA(cudaMemcpyAsync(h_argmax_, d_argmax_, rows * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                            stream_));
+    synchronize();
+    std::memcpy(out, h_argmax_, rows * sizeof(int32_t));
 }
 
 std::array<int64_t, 4> Executor::tensor_shape(uint32_t tid) const {

@@ -122,6 +122,9 @@ public:
     void run();
     void synchronize();
     const void* get_output(uint32_t tid, size_t* bytes);
+    // greedy token of each of `rows` rows of an f32 output [rows][n] (first maximum), computed on
+    // the device; only the indices cross to the host
+    void output_argmax(uint32_t tid, int rows, int32_t* out);
     std::array<int64_t, 4> tensor_shape(uint32_t tid) const;
     size_t tensor_size_bytes(uint32_t tid) const;
 
@@ -218,6 +221,8 @@ private:
     std::map<uint32_t, char*> state_dev_;
     std::map<std::string, std::pair<float2*, std::pair<int64_t, float>>> rope_tabs_;
     void* pinned_out_ = nullptr;
+    int32_t* d_argmax_ = nullptr;   // kMaxRows device indices
+    int32_t* h_argmax_ = nullptr;   // pinned copy
     size_t pinned_out_bytes_ = 0;
     bool ktiming_ = false;
     struct KTime {

@@ -102,6 +102,51 @@ __global__ void k_get_rows(QWeight w, const int32_t* __restrict__ ids, int64_t n
     }
 }
 
+// Greedy token per row: the index of the first maximum (the reference's sample_next_token with
+// temperature 0, batch_scheduler.cpp:94-106).  One CTA per row; ties keep the lowest index.
+__global__ void k_argmax_rows(const float* __restrict__ x, int64_t n, int32_t* __restrict__ out) {
+    __shared__ float sv[32];
+    __shared__ int64_t si[32];
+    const float* row = x + (int64_t)blockIdx.x * n;
+    float best = -INFINITY;
+    int64_t bi = n;
+    for (int64_t i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = row[i];
+        if (v > best || (v == best && i < bi)) {
+            best = v;
+            bi = i;
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        const float v = __shfl_xor_sync(0xffffffffu, best, o);
+        const int64_t j = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (v > best || (v == best && j < bi)) {
+            best = v;
+            bi = j;
+        }
+    }
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) {
+        sv[w] = best;
+        si[w] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int k = 1; k < (int)(blockDim.x >> 5); ++k)
+            if (sv[k] > best || (sv[k] == best && si[k] < bi)) {
+                best = sv[k];
+                bi = si[k];
+            }
+        out[blockIdx.x] = (int32_t)(bi < n ? bi : 0);
+    }
+}
+
+void launch_argmax_rows(const float* x, int64_t rows, int64_t n, int32_t* out, cudaStream_t st) {
+    if (!rows) return;
+    k_argmax_rows<<<(unsigned)rows, 1024, 0, st>>>(x, n, out);
+    GB_CUDA(cudaGetLastError());
+}
+
 void launch_get_rows(const QWeight& w, const int32_t* ids, int64_t n, float* out,
                      int64_t out_stride, cudaStream_t st) {
     if (!n) return;

@@ -61,6 +61,9 @@ void launch_quantize_q8_0(const float* x, int64_t x_stride, int64_t M, int64_t K
 void launch_repack_blocks(const uint8_t* gguf, int type, int64_t N, int64_t K, void* qs,
                           cudaStream_t st);
 
+// Index of the first maximum of each of `rows` f32 rows of length n (greedy sampling).
+void launch_argmax_rows(const float* x, int64_t rows, int64_t n, int32_t* out, cudaStream_t st);
+
 // GET_ROWS: rows ids[i] of a quantized / f16 / f32 table [V][K] dequantized to f32 out[i][K].
 void launch_get_rows(const QWeight& w, const int32_t* ids, int64_t n, float* out,
                      int64_t out_stride, cudaStream_t st);

@@ -126,10 +126,14 @@ StepOut Scheduler::step() {
             ex_.prepare(env, true);
             ex_.set_input(in_id_, r->prompt.data(), r->prompt.size() * 4);
             ex_.run();
-            size_t bytes = 0;
-            const float* logits = (const float*)ex_.get_output(out_id_, &bytes);
-            const int64_t vocab = (int64_t)(bytes / 4);  // last row only
-            const int32_t tok = sample(logits, vocab, r->temperature);
+            int32_t tok = 0;
+            if (r->temperature <= 0.0f) {
+                ex_.output_argmax(out_id_, 1, &tok);  // last row only
+            } else {
+                size_t bytes = 0;
+                const float* logits = (const float*)ex_.get_output(out_id_, &bytes);
+                tok = sample(logits, (int64_t)(bytes / 4), r->temperature);
+            }
             r->generated.push_back(tok);
             r->pos = n;
             out.new_tokens.push_back({r->id, tok});
@@ -153,12 +157,23 @@ StepOut Scheduler::step() {
     ex_.prepare_batch(rows, pos.data(), slot.data());
     ex_.set_input(in_id_, tok.data(), tok.size() * 4);
     ex_.run();
-    size_t bytes = 0;
-    const float* logits = (const float*)ex_.get_output(out_id_, &bytes);
-    const int64_t vocab = (int64_t)(bytes / 4 / (size_t)rows);
+    // greedy rows take the device argmax; logits cross to the host only for sampled rows
+    bool any_sampled = false;
+    for (auto& r : act) any_sampled |= r->temperature > 0.0f;
+    std::vector<int32_t> greedy((size_t)rows);
+    ex_.output_argmax(out_id_, rows, greedy.data());
+    const float* logits = nullptr;
+    int64_t vocab = 0;
+    if (any_sampled) {
+        size_t bytes = 0;
+        logits = (const float*)ex_.get_output(out_id_, &bytes);
+        vocab = (int64_t)(bytes / 4 / (size_t)rows);
+    }
     for (size_t i = 0; i < act.size(); ++i) {
         auto& r = act[i];
-        const int32_t t = sample(logits + (int64_t)i * vocab, vocab, r->temperature);
+        const int32_t t = r->temperature > 0.0f
+                              ? sample(logits + (int64_t)i * vocab, vocab, r->temperature)
+                              : greedy[i];
         r->generated.push_back(t);
         r->pos += 1;
         out.new_tokens.push_back({r->id, t});
