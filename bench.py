@@ -325,7 +325,7 @@ def run_ours(args) -> None:
     dom = max(kt.items(), key=lambda x: x[1][0])[0] if kt else "gemv_rms_swiglu"
     mm = kt.get(dom, [0, 1, 0])
     achieved = mm[2] / (mm[0] / 1e3) / 1e9 if mm[0] > 0 else 0.0
-    gemv_all = [v for k, v in kt.items() if k.startswith("gemv")]
+    gemv_all = [v for k, v in kt.items() if k.startswith(("gemv", "mmv"))]
     gemv_gbs = (sum(v[2] for v in gemv_all) / (sum(v[0] for v in gemv_all) / 1e3) / 1e9
                 if gemv_all else 0.0)
     dec_total = sum(v[0] for v in kt.values())

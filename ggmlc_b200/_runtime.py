@@ -47,6 +47,11 @@ def _load() -> ctypes.CDLL:
         "gb_graph_op_info": ([P, I, ctypes.POINTER(U32), ctypes.POINTER(I), ctypes.POINTER(CP)], I),
         "gb_graph_metadata_str": ([P, CP], CP),
         "gb_executor_create": ([P, CP, PP], I),
+        "gb_executor_create_tp": ([P, CP, I, I, P, PP], I),
+        "gb_nccl_unique_id": ([P], I),
+        "gb_tp_plan": ([P, I, I], CP),
+        "gb_executor_tp_size": ([P], I),
+        "gb_executor_tp_rank": ([P], I),
         "gb_executor_free": ([P], None),
         "gb_executor_device": ([P], CP),
         "gb_executor_prepare": ([P, ctypes.POINTER(CP), ctypes.POINTER(I64), I, I], I),
@@ -235,6 +240,23 @@ def _as_c(array: Any) -> np.ndarray:
     return a
 
 
+def nccl_unique_id() -> bytes:
+    """128-byte NCCL unique id for a tensor-parallel group (made once, by rank 0)."""
+    buf = ctypes.create_string_buffer(128)
+    _check(_lib.gb_nccl_unique_id(buf))
+    return buf.raw
+
+
+def tensor_parallel_plan(graph: SerializedModelGraph, tp_rank: int, tp_size: int) -> dict:
+    """One rank's tensor-parallel plan (weight slices, partial sums, rewritten shapes); host only."""
+    import json
+
+    out = _lib.gb_tp_plan(graph._h, int(tp_rank), int(tp_size))
+    if not out:
+        raise RuntimeError(_lib.gb_last_error().decode())
+    return json.loads(out.decode())
+
+
 class ModelExecutor:
     """CUDA executor with the reference ModelExecutor's interface (python_bindings.cpp:136-217).
 
@@ -242,9 +264,20 @@ class ModelExecutor:
     on the executor's stream and ``get_output_bytes`` waits for them.
     """
 
-    def __init__(self, graph: SerializedModelGraph, device: str = "cpu"):
+    def __init__(self, graph: SerializedModelGraph, device: str = "cpu", tp_rank: int = 0,
+                 tp_size: int = 1, nccl_id: bytes | None = None):
+        """``tp_size > 1``: rank ``tp_rank`` of a tensor-parallel group (no counterpart in the
+        reference).  ``nccl_id`` is the group's ``nccl_unique_id()`` made by rank 0 and shared
+        by the caller; every rank constructs its executor at the same time (collective)."""
         h = ctypes.c_void_p()
-        _check(_lib.gb_executor_create(graph._h, str(device).encode(), ctypes.byref(h)))
+        if int(tp_size) > 1:
+            if nccl_id is None or len(nccl_id) != 128:
+                raise ValueError("tensor parallelism needs the group's 128-byte nccl_unique_id()")
+            idbuf = ctypes.create_string_buffer(bytes(nccl_id), 128)
+            _check(_lib.gb_executor_create_tp(graph._h, str(device).encode(), int(tp_rank),
+                                              int(tp_size), idbuf, ctypes.byref(h)))
+        else:
+            _check(_lib.gb_executor_create(graph._h, str(device).encode(), ctypes.byref(h)))
         self._h = h
         self._graph = graph  # keeps the mmap'd GGUF alive
         self._names = {t.name: tid for tid, t in graph.tensors.items()}
@@ -252,6 +285,14 @@ class ModelExecutor:
     @property
     def device(self) -> str:
         return _lib.gb_executor_device(self._h).decode()
+
+    @property
+    def tp_size(self) -> int:
+        return int(_lib.gb_executor_tp_size(self._h))
+
+    @property
+    def tp_rank(self) -> int:
+        return int(_lib.gb_executor_tp_rank(self._h))
 
     def prepare(self, symbols: dict[str, int] | None = None, enable_arena_reuse: bool = True):
         symbols = dict(symbols or {})

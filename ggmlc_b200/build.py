@@ -69,7 +69,7 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     if force or todo or not LIB.exists() or LIB.stat().st_mtime < max(o.stat().st_mtime for o in objs):
         tmp = LIB.with_suffix(".so.tmp")
         cmd = [nvcc(), "-shared", "-o", str(tmp)] + [str(o) for o in objs] + ARCH + [
-            "-Xlinker", "--no-undefined", "-lcuda"]
+            "-Xlinker", "--no-undefined", "-lcuda", "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

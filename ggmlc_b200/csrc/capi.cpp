@@ -9,6 +9,7 @@
 #include <string>
 
 #include "executor.h"
+#include "tp.h"
 #include "graph.h"
 #include "scheduler.h"
 #include "kernels.h"
@@ -155,6 +156,34 @@ int gb_executor_create(const gb_graph* g, const char* device, gb_executor** out)
         *out = h;
     });
 }
+int gb_nccl_unique_id(void* out128) {
+    return guard([&] { gb::Executor::nccl_unique_id(out128); });
+}
+int gb_executor_create_tp(const gb_graph* g, const char* device, int tp_rank, int tp_size,
+                          const void* nccl_id, gb_executor** out) {
+    return guard([&] {
+        auto* h = new gb_executor();
+        try {
+            h->e.reset(new gb::Executor(g->g, device ? device : "cuda", tp_rank, tp_size, nccl_id));
+        } catch (...) {
+            delete h;
+            throw;
+        }
+        *out = h;
+    });
+}
+const char* gb_tp_plan(const gb_graph* g, int tp_rank, int tp_size) {
+    static thread_local std::string buf;
+    buf.clear();
+    const int rc = guard([&] {
+        gb::Graph copy = *g->g;
+        const gb::TpPlan p = gb::plan_tensor_parallel(copy, tp_rank, tp_size);
+        buf = gb::tp_plan_json(p, copy);
+    });
+    return rc == 0 ? buf.c_str() : nullptr;
+}
+int gb_executor_tp_size(const gb_executor* e) { return e->e->tp_size(); }
+int gb_executor_tp_rank(const gb_executor* e) { return e->e->tp_rank(); }
 void gb_executor_free(gb_executor* e) { delete e; }
 const char* gb_executor_device(const gb_executor* e) { return e->e->device().c_str(); }
 

@@ -3,7 +3,11 @@
 // :2362-2447, RESHAPE/PERMUTE/VIEW :2448-2560, custom ops 200-203 :2703-2757).
 #include "executor.h"
 
+#include <dlfcn.h>
+#include <nccl.h>
+
 #include <algorithm>
+#include <mutex>
 #include <chrono>
 #include <cmath>
 #include <cstring>
@@ -77,7 +81,58 @@ std::vector<std::string> Executor::available_devices() {
     return out;
 }
 
-Executor::Executor(std::shared_ptr<Graph> g, const std::string& device) : g_(std::move(g)) {
+// NCCL is opened on first use (tensor parallelism only), preferring the libnccl.so.2 that the
+// process has already loaded (PyTorch's), so the library carries no link-time NCCL dependency
+// and never loads a second NCCL next to PyTorch's.
+namespace {
+struct NcclApi {
+    ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+    ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+    ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+    ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t,
+                               ncclComm_t, cudaStream_t) = nullptr;
+    ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t,
+                               cudaStream_t) = nullptr;
+    const char* (*error_string)(ncclResult_t) = nullptr;
+};
+const NcclApi& nccl() {
+    static NcclApi api;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return;
+        api.get_unique_id = (decltype(api.get_unique_id))dlsym(h, "ncclGetUniqueId");
+        api.comm_init_rank = (decltype(api.comm_init_rank))dlsym(h, "ncclCommInitRank");
+        api.comm_destroy = (decltype(api.comm_destroy))dlsym(h, "ncclCommDestroy");
+        api.all_reduce = (decltype(api.all_reduce))dlsym(h, "ncclAllReduce");
+        api.all_gather = (decltype(api.all_gather))dlsym(h, "ncclAllGather");
+        api.error_string = (decltype(api.error_string))dlsym(h, "ncclGetErrorString");
+    });
+    GB_CHECK(api.get_unique_id && api.comm_init_rank && api.comm_destroy && api.all_reduce &&
+                 api.all_gather && api.error_string,
+             "tensor parallelism needs NCCL (libnccl.so.2), which could not be loaded");
+    return api;
+}
+}  // namespace
+
+#define GB_NCCL(call)                                                                     \
+    do {                                                                                  \
+        const ncclResult_t r_ = nccl().call;                                              \
+        GB_CHECK(r_ == ncclSuccess,                                                       \
+                 std::string("NCCL: ") + nccl().error_string(r_) + " (" #call ")");       \
+    } while (0)
+
+void Executor::nccl_unique_id(void* out128) {
+    static_assert(sizeof(ncclUniqueId) == 128, "ncclUniqueId is 128 bytes");
+    ncclUniqueId id;
+    GB_NCCL(get_unique_id(&id));
+    std::memcpy(out128, &id, sizeof(id));
+}
+
+Executor::Executor(std::shared_ptr<Graph> g, const std::string& device, int tp_rank, int tp_size,
+                   const void* nccl_id)
+    : g_(std::move(g)) {
     std::string d = device;
     for (auto& c : d) c = (char)std::tolower((unsigned char)c);
     int n = 0;
@@ -100,6 +155,16 @@ Executor::Executor(std::shared_ptr<Graph> g, const std::string& device) : g_(std
     GB_CUDA(cudaMalloc(&d_step_, sizeof(StepParams)));
     h_step_->pos = 0;
     GB_CUDA(cudaMemcpy(d_step_, h_step_, sizeof(StepParams), cudaMemcpyHostToDevice));
+    if (tp_size > 1) {
+        GB_CHECK(nccl_id != nullptr, "tensor parallelism needs the group's NCCL unique id");
+        g_ = std::make_shared<Graph>(*g_);  // this rank's shapes are rewritten in a copy
+        tp_ = plan_tensor_parallel(*g_, tp_rank, tp_size);
+        ncclUniqueId id;
+        std::memcpy(&id, nccl_id, sizeof(id));
+        ncclComm_t comm = nullptr;
+        GB_NCCL(comm_init_rank(&comm, tp_size, id, tp_rank));
+        nccl_ = comm;
+    }
     upload_weights();
 }
 
@@ -121,6 +186,7 @@ Executor::~Executor() {
     if (d_argmax_) cudaFree(d_argmax_);
     if (h_argmax_) cudaFreeHost(h_argmax_);
     if (arena_) cudaFree(arena_);
+    if (nccl_) nccl().comm_destroy((ncclComm_t)nccl_);  // after the graphs that captured its calls
     if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -148,16 +214,64 @@ void Executor::ensure_arena(size_t bytes) {
     arena_cap_ = cap;
 }
 
+namespace {
+
+// This rank's part of a GGUF tensor [N0 rows][K0 elements]: concatenated row ranges, or one
+// column range of every row (whole 32-element blocks for quantized types).
+std::vector<uint8_t> slice_payload(const GTensor& t, const TpSlice& s, int64_t* N, int64_t* K) {
+    const int64_t K0 = t.file_ne[0], N0 = t.file_ne[1] * t.file_ne[2] * t.file_ne[3];
+    const int64_t rb = row_bytes(t.type, K0);
+    GB_CHECK((uint64_t)(rb * N0) <= t.data_size, "tensor '" + t.name + "': payload too short");
+    std::vector<uint8_t> out;
+    if (!s.cols) {
+        // a 1-D tensor (bias) is sliced by elements
+        const bool vec = N0 == 1;
+        const int64_t eb = vec ? row_bytes(t.type, 1) : rb;
+        int64_t n = 0;
+        for (auto& [a, b] : s.rows) {
+            GB_CHECK(a >= 0 && b <= (vec ? K0 : N0) && a <= b, "tensor '" + t.name + "': bad slice");
+            out.insert(out.end(), t.data + a * eb, t.data + b * eb);
+            n += b - a;
+        }
+        *N = vec ? 1 : n;
+        *K = vec ? n : K0;
+        return out;
+    }
+    GB_CHECK(s.c0 >= 0 && s.c1 <= K0 && s.c0 < s.c1, "tensor '" + t.name + "': bad column slice");
+    const int64_t b0 = row_bytes(t.type, s.c0), b1 = row_bytes(t.type, s.c1);
+    out.resize((size_t)((b1 - b0) * N0));
+    for (int64_t r = 0; r < N0; ++r)
+        std::memcpy(out.data() + r * (b1 - b0), t.data + r * rb + b0, (size_t)(b1 - b0));
+    *N = N0;
+    *K = s.c1 - s.c0;
+    return out;
+}
+
+}  // namespace
+
 // Upload every tensor with a GGUF payload: quantized matrices are repacked into the SoA layout
-// (aligned quants + fp16 scale rows), everything else is copied as is.
+// (aligned quants + fp16 scale rows), everything else is copied as is.  Under tensor
+// parallelism each rank uploads only its slices.
 void Executor::upload_weights() {
     size_t staging_bytes = 0;
     for (auto& [id, t] : g_->tensors)
         if (t.data && is_quant(t.type)) staging_bytes = std::max<size_t>(staging_bytes, t.data_size);
     uint8_t* staging = nullptr;
     if (staging_bytes) GB_CUDA(cudaMalloc(&staging, staging_bytes));
-    for (auto& [id, t] : g_->tensors) {
-        if (!t.data || t.data_size == 0) continue;
+    for (auto& [id, t0] : g_->tensors) {
+        if (!t0.data || t0.data_size == 0) continue;
+        GTensor t = t0;
+        std::vector<uint8_t> part;
+        auto sl = tp_.slices.find(id);
+        if (sl != tp_.slices.end()) {
+            int64_t n = 0, k = 0;
+            part = slice_payload(t0, sl->second, &n, &k);
+            t.data = part.data();
+            t.data_size = part.size();
+            t.file_ne[0] = k;
+            t.file_ne[1] = n;
+            t.file_ne[2] = t.file_ne[3] = 1;
+        }
         if (is_quant(t.type)) {
             const int64_t K = t.file_ne[0];
             const int64_t N = t.file_ne[1] * t.file_ne[2] * t.file_ne[3];
@@ -194,6 +308,12 @@ void Executor::upload_weights() {
         }
     }
     if (staging) cudaFree(staging);
+    if (tp_.vocab_w != UINT32_MAX) {
+        const QWeight& w = qweights_.at(tp_.vocab_w);
+        tp_vocab_view_ = w;
+        tp_vocab_view_.N = tp_.vocab_rows;
+        tp_vocab_view_.qs = (const char*)w.qs + tp_.rank * tp_.vocab_rows * qrow_bytes(w.type, w.K);
+    }
 }
 
 // ------------------------------------------------------------------------------ KV cache
@@ -502,6 +622,49 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
         if (!need_f && !need_q) need_f = true;
     };
 
+    // tensor-parallel exchanges (NCCL on the executor's stream; captured with the program)
+    ncclComm_t comm = (ncclComm_t)nccl_;
+    auto tp_allreduce = [&](const Val& y) {
+        const BufRef r = y.ref;
+        const size_t n = (size_t)nelem(y.ne);
+        add("allreduce", [=](Program& p, cudaStream_t st) {
+            float* d = (float*)p.ptr(r);
+            GB_NCCL(all_reduce(d, d, n, ncclFloat32, ncclSum, comm, st));
+        }, 8.0 * (double)n);
+    };
+    const int tp_n = tp_.size;
+    auto tp_gather = [&](const Val& yl, int op) -> Val {
+        Val yf = yl;
+        yf.ne[0] = yl.ne[0] * tp_n;
+        alloc(yf, op);
+        const int64_t Vr = yl.ne[0], M = yl.nrows();
+        const BufRef lr = yl.ref, fr = yf.ref;
+        BufRef gr;
+        if (M > 1) gr.buf = pg.new_buf(Vr * M * tp_n * 4, op);
+        add("allgather", [=](Program& p, cudaStream_t st) {
+            if (M == 1) {
+                GB_NCCL(all_gather(p.ptr(lr), p.ptr(fr), (size_t)Vr, ncclFloat32, comm, st));
+                return;
+            }
+            // rank-major [rank][M][Vr] -> row-major [M][rank * Vr + j]
+            GB_NCCL(all_gather(p.ptr(lr), p.ptr(gr), (size_t)(Vr * M), ncclFloat32, comm, st));
+            TView src, dst;
+            src.data = p.ptr(gr);
+            dst.data = p.ptr(fr);
+            src.type = dst.type = T_F32;
+            const int64_t ne[4] = {Vr, M, tp_n, 1};
+            const int64_t sb[4] = {4, Vr * 4, Vr * M * 4, Vr * M * tp_n * 4};
+            const int64_t db[4] = {4, Vr * tp_n * 4, Vr * 4, Vr * M * tp_n * 4};
+            for (int d = 0; d < 4; ++d) {
+                src.ne[d] = dst.ne[d] = ne[d];
+                src.nb[d] = sb[d];
+                dst.nb[d] = db[d];
+            }
+            launch_copy(src, dst, st);
+        }, 8.0 * (double)(Vr * M * tp_n));
+        return yf;
+    };
+
     std::set<int> skip;  // ops folded into an earlier launch
     for (int oi = 0; oi < nops; ++oi) {
         if (skip.count(oi)) continue;
@@ -558,7 +721,7 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                 const bool rms_op = op.opcode == OP_RMS_NORM_C || op.opcode == OP_RMS_NORM;
                 const bool fits = M >= 1 && gemv_fits(T_Q8_0, D, (int)M, true, gamma) &&
                                   gemv_fits(T_Q4_0, D, (int)M, true, gamma);
-                if (rms_op && !nf && nq && M <= 8 && fits) {
+                if (rms_op && !nf && nq && M <= kGemvMaxRows && fits) {
                     // decode: every consumer is a quantized GEMV that normalizes in its prologue
                     o.has_f = false;
                     o.virt_rms = true;
@@ -595,9 +758,16 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
             case OP_MUL_MAT: {
                 Val& wv = in(0);
                 GB_CHECK(wv.w, "MUL_MAT: first operand must be a weight matrix");
-                const QWeight* qw = wv.w;
+                // tensor parallelism: a K-split matmul yields a partial sum (all-reduced below;
+                // only rank 0 adds bias and residual); the vocabulary-split projection computes
+                // this rank's rows and all-gathers the logits
+                const bool tp_partial = tp_.size > 1 && tp_.partial.count(out) != 0;
+                const bool tp_vocab = tp_.size > 1 && out == tp_.vocab_out;
+                const bool tp_skip_add = tp_partial && tp_.rank != 0;
+                const QWeight* qw = tp_vocab ? &tp_vocab_view_ : wv.w;
                 Val& xin = in(1);
                 const int64_t K = qw->K, N = qw->N;
+                if (tp_vocab) o.ne[0] = N;
                 GB_CHECK(xin.ne[0] == K, "MUL_MAT: inner dimensions differ (" +
                                              std::to_string(xin.ne[0]) + " vs " +
                                              std::to_string(K) + ")");
@@ -614,7 +784,8 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                 // fused residual ADD: the only consumer is ADD(other, this) of equal shape
                 int add_op = -1;
                 const float* bias = nullptr;
-                if (op.inputs.size() > 2) bias = (const float*)get(op.inputs[2]).ref.fixed;
+                if (op.inputs.size() > 2 && !tp_skip_add)
+                    bias = (const float*)get(op.inputs[2]).ref.fixed;
                 Val res;
                 if (!outputs.count(out) && consumers[out].size() == 1 && !last_only) {
                     const int ci = consumers[out][0];
@@ -630,9 +801,11 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         }
                     }
                 }
-                // decode GEMV (M <= 8): RMSNorm prologue / SwiGLU epilogue fused into one launch
-                const bool dec = is_quant(qw->type) && !last_only && Mrun <= 8 &&
-                                 gemv_fused_fits(K, (int)Mrun);
+                // decode (M <= 16): SwiGLU / residual epilogue fused into the matmul launch; an
+                // unmaterialized RMSNorm input (M <= 4) is normalized in the GEMV prologue
+                const bool dec = is_quant(qw->type) && !last_only &&
+                                 (xin.virt_rms ? Mrun <= kGemvMaxRows && gemv_fused_fits(K, (int)Mrun)
+                                               : Mrun <= kMmvMaxRows);
                 GB_CHECK(!xin.virt_rms || dec, "internal: unfused RMSNorm without a decode GEMV");
                 int swi_op = -1;
                 if (dec && !bias && add_op < 0 && !outputs.count(out) && consumers[out].size() == 1) {
@@ -681,7 +854,7 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         }
                         const BufRef hr = h.ref, hq = h.q, hqd = h.qd;
                         const bool hf = h.has_f, hhq = h.has_q;
-                        add(virt ? "gemv_rms_swiglu" : "gemv_swiglu", [=](Program& p, cudaStream_t st) {
+                        add(virt ? "gemv_rms_swiglu" : (Mrun <= kGemvMaxRows ? "gemv_swiglu" : "mmv_swiglu"), [=](Program& p, cudaStream_t st) {
                             GemvArgs a = ga;
                             if (virt) {
                                 a.xf = (const float*)p.ptr(xr);
@@ -716,12 +889,12 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         for (int d = 0; d < 4; ++d) y.ne[d] = shape[out_id][d];
                     alloc(y, oi);
                     BufRef rref;
-                    if (add_op >= 0) {
+                    if (add_op >= 0 && !tp_skip_add) {
                         rref = res.ref;
                         pg.use(res.ref, add_op);
                     }
                     const BufRef yr = y.ref;
-                    add(virt ? "gemv_rms" : (add_op >= 0 ? "gemv_res" : "gemv"), [=](Program& p, cudaStream_t st) {
+                    add(virt ? "gemv_rms" : (Mrun <= kGemvMaxRows ? (add_op >= 0 ? "gemv_res" : "gemv") : (add_op >= 0 ? "mmv_res" : "mmv")), [=](Program& p, cudaStream_t st) {
                         GemvArgs a = ga;
                         if (virt) {
                             a.xf = (const float*)p.ptr(xr);
@@ -741,6 +914,8 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         }
                         launch_gemv_fused(a, st);
                     }, bytes);
+                    if (tp_partial) tp_allreduce(y);
+                    if (tp_vocab) y = tp_gather(y, oi);
                     if (add_op >= 0) {
                         vals[out_id] = y;
                         skip.insert(add_op);
@@ -757,7 +932,7 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                 MatmulEpilogue ep;
                 ep.bias = bias;
                 BufRef rref;
-                if (add_op >= 0) {
+                if (add_op >= 0 && !tp_skip_add) {
                     rref = res.ref;
                     pg.use(res.ref, add_op);
                     ep.res_stride = N;
@@ -808,6 +983,8 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                                         (float*)p.ptr(yr), ystride, e, st);
                     });
                 }
+                if (tp_partial) tp_allreduce(y);
+                if (tp_vocab) y = tp_gather(y, oi);
                 if (add_op >= 0) {
                     vals[out_id] = y;
                     skip.insert(add_op);

@@ -21,6 +21,7 @@
 #include "common.h"
 #include "graph.h"
 #include "kernels.h"
+#include "tp.h"
 
 namespace gb {
 
@@ -110,8 +111,16 @@ struct KVCache {
 
 class Executor {
 public:
-    Executor(std::shared_ptr<Graph> g, const std::string& device);
+    // tp_size > 1: this executor is rank tp_rank of a tensor-parallel group (tp.h); nccl_id is
+    // the group's 128-byte ncclUniqueId (made by rank 0 with nccl_unique_id and shared by the
+    // caller).  Construction is collective: every rank of the group must construct its executor.
+    Executor(std::shared_ptr<Graph> g, const std::string& device, int tp_rank = 0,
+             int tp_size = 1, const void* nccl_id = nullptr);
     ~Executor();
+    static void nccl_unique_id(void* out128);
+    int tp_rank() const { return tp_.rank; }
+    int tp_size() const { return tp_.size; }
+    const TpPlan& tp_plan() const { return tp_; }
 
     static std::vector<std::string> available_devices();
     const std::string& device() const { return device_; }
@@ -190,6 +199,9 @@ private:
     void free_program(Program& p);
 
     std::shared_ptr<Graph> g_;
+    TpPlan tp_;
+    void* nccl_ = nullptr;  // ncclComm_t of the tensor-parallel group
+    QWeight tp_vocab_view_;  // this rank's rows of the vocabulary-split projection
     std::string device_;
     int dev_ = 0;
     cudaStream_t stream_ = nullptr;

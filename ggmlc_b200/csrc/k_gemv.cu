@@ -1,4 +1,4 @@
-// Decode GEMV (M <= 8 activation rows) over the split-row weight layout, with an optional fused
+// Decode GEMV (M <= 4 activation rows) over the split-row weight layout, with an optional fused
 // RMSNorm + Q8_0 prologue and a bias / residual / SwiGLU epilogue.
 //
 // Arithmetic.  Per 32-element block the integer dot sumi = sum q_w * q_x is exact (dp4a chain),
@@ -450,16 +450,15 @@ template <int WT, int SWI>
 void launch_m(const GemvArgs& a, cudaStream_t st) {
     if (a.M == 1) launch_t<WT, 1, SWI>(a, st);
     else if (a.M == 2) launch_t<WT, 2, SWI>(a, st);
-    else if (a.M <= 4) launch_t<WT, 4, SWI>(a, st);
-    else launch_t<WT, 8, SWI>(a, st);
+    else launch_t<WT, 4, SWI>(a, st);
 }
 
 }  // namespace
 
-static int maxm_of(int M) { return M == 1 ? 1 : (M == 2 ? 2 : (M <= 4 ? 4 : 8)); }
+static int maxm_of(int M) { return M == 1 ? 1 : (M == 2 ? 2 : 4); }
 
 bool gemv_fits(int type, int64_t K, int M, bool staged, bool gamma) {
-    if (M < 1 || M > 8 || K % QK != 0) return false;
+    if (M < 1 || M > kGemvMaxRows || K % QK != 0) return false;
     const size_t b = type == T_Q8_0 ? smem_bytes<T_Q8_0>(maxm_of(M), K, staged, gamma)
                                     : smem_bytes<T_Q4_0>(maxm_of(M), K, staged, gamma);
     return b <= kSmemMax;
@@ -470,6 +469,10 @@ bool gemv_fused_fits(int64_t K, int M) {
 }
 
 void launch_gemv_fused(const GemvArgs& a, cudaStream_t st) {
+    if (!a.xf && (a.M > kGemvMaxRows || !gemv_fits(a.w.type, a.w.K, a.M, false, false))) {
+        launch_mmv(a, st);  // batched decode: the tensor-core kernel
+        return;
+    }
     GB_CHECK(a.w.type == T_Q8_0 || a.w.type == T_Q4_0, "gemv: quantized weights required");
     GB_CHECK(a.w.K % QK == 0 && a.w.K < (1LL << 30) && a.w.N < (1LL << 30), "gemv: bad shape");
     GB_CHECK(gemv_fits(a.w.type, a.w.K, a.M, a.xf != nullptr, a.gamma != nullptr),

@@ -1,8 +1,9 @@
 // Quantized MUL_MAT kernels over the split-row weight layout (kernels.h).
 //
-// M <= 8 (the decode path) goes to the GEMV in k_gemv.cu.
+// M <= 16 (decode and batched decode) goes to the GEMV (k_gemv.cu, M <= 4) or the tensor-core
+// decode kernel (k_mmv.cu).
 //
-// k_gemm_q (M > 8, prefill): int8 tensor-core tiles (mma m16n8k32, one instruction per
+// k_gemm_q (M > 16, prefill): int8 tensor-core tiles (mma m16n8k32, one instruction per
 // 32-K block) give the exact int32 block dot; the block scale product is applied in fp32 right
 // after each block.  Integer block sums are exact; the fp32 summation order differs from the
 // CPU's lane order.
@@ -18,7 +19,7 @@ namespace gb {
 
 namespace {
 
-// ---- block GEMM on int8 tensor cores (prefill, M > 8) -------------------------------------
+// ---- block GEMM on int8 tensor cores (prefill, M > 16) -------------------------------------
 // CTA tile 128 activation rows (m) x 128 weight rows (n), 8 warps as 2 (m) x 4 (n), warp tile
 // 64 x 32.  K advances in stages of 4 blocks, streamed by cp.async through a 4-stage shared-memory
 // ring; fragments come from swizzled shared memory with ldmatrix.  Each 32-element block is one
@@ -260,7 +261,7 @@ void launch_matmul_q(const QWeight& w, const int8_t* xq, const float* xd, int64_
     GB_CHECK(w.K % QK == 0, "matmul: K must be a multiple of 32");
     if (M == 0 || w.N == 0) return;
     const bool q8 = w.type == T_Q8_0;
-    if (M <= 8 && gemv_fused_fits(w.K, (int)M)) {
+    if (M <= kMmvMaxRows) {
         GemvArgs a;
         a.w = w;
         a.M = (int)M;

@@ -72,7 +72,7 @@ void launch_get_rows(const QWeight& w, const int32_t* ids, int64_t n, float* out
 // Y[m][n] = sum_k X[m][k] W[n][k] (+ bias[n]) (+ residual[m][n]) for Q8_0/Q4_0 W and Q8_0 X.
 // Per 32-element block the int32 dot is exact; block terms sumi * (d_w * d_x) accumulate in fp32
 // (the reference's generic block formula; the x86 lane order differs only in rounding).
-// M <= 8 runs the decode GEMV, larger M the tensor-core block GEMM.
+// M <= 4 runs the decode GEMV, M <= 16 the tensor-core decode kernel, larger M the block GEMM.
 struct MatmulEpilogue {
     const float* bias = nullptr;      // [N] or null
     const float* residual = nullptr;  // [M][res_stride] or null
@@ -80,13 +80,17 @@ struct MatmulEpilogue {
 };
 void launch_matmul_q(const QWeight& w, const int8_t* xq, const float* xd, int64_t M, float* y,
                      int64_t y_stride, const MatmulEpilogue& ep, cudaStream_t st);
-// Decode GEMV with fused prologue / epilogue (M <= 8).  Launched as a programmatic dependent
-// launch: its weight loads start before the previous kernel on the stream has finished.
+// Decode GEMV with fused prologue / epilogue (M <= kGemvMaxRows; Q8_0 input with more rows goes
+// to launch_mmv).  Lanes run along K, so each row costs a fixed number of instructions per weight
+// byte; up to 4 rows this beats the tensor-core kernel, whose 16x8 tiles are mostly idle there.
+// Launched as a programmatic dependent launch: its weight loads start before the previous kernel
+// on the stream has finished.
 //   input : Q8_0 rows (xq, xd; xq 16-byte aligned), or f32 rows xf quantized to Q8_0 in shared
 //           memory, after RMSNorm with eps and optional gamma when xf_rms (exactly as
 //           launch_rms_norm) — the standalone norm and quantize launches disappear;
 //   output: f32 rows y (+bias, +residual), or SwiGLU of row pairs (gate n, up n+F) emitted as
 //           Q8_0 rows (yq, yd) and/or f32 rows (y) of length F — exactly launch_swiglu.
+constexpr int kGemvMaxRows = 4;
 struct GemvArgs {
     QWeight w;
     int M = 1;
@@ -112,6 +116,11 @@ void launch_gemv_fused(const GemvArgs& a, cudaStream_t st);
 // input, gamma = with gamma), gemv_fused_fits for Q8_0 input with either weight type
 bool gemv_fits(int type, int64_t K, int M, bool staged, bool gamma);
 bool gemv_fused_fits(int64_t K, int M);
+// Decode / small-batch matmul on int8 tensor cores (k_mmv.cu): Q8_0 input only (xq, xd), M <= 16,
+// the GemvArgs epilogues (bias / residual, or SwiGLU to f32 and/or Q8_0).  Any K.  A row's
+// result does not depend on M (nor on the epilogue mode).  Programmatic dependent launch.
+constexpr int kMmvMaxRows = 16;
+void launch_mmv(const GemvArgs& a, cudaStream_t st);
 
 // Float-weight matmul (F32/F16 W, f32 X), used for non-quantized linears.
 void launch_matmul_f(const QWeight& w, const float* x, int64_t x_stride, int64_t M, float* y,

@@ -60,6 +60,21 @@ const char* gb_graph_metadata_str(const gb_graph* g, const char* key);
 /* ---- ModelExecutor (python_bindings.cpp:136-217; executor.h:25-287) ----------------------- */
 /* device: "cuda", "cuda:N" or "auto".  "cpu" is refused: this engine has no CPU fallback. */
 int gb_executor_create(const gb_graph* g, const char* device, gb_executor** out);
+/* Tensor parallelism (no counterpart in the reference, which runs one device per model).
+ * gb_nccl_unique_id writes the 128-byte NCCL unique id that rank 0 creates and the caller
+ * shares with every rank; gb_executor_create_tp then builds rank tp_rank of a tp_size-way
+ * group on `device` (collective: all ranks must call it).  Fused QKV is cut by heads, fused
+ * gate_up per half, O / down along K with an all-reduce of their partial sums, the output
+ * projection by vocabulary rows with an all-gather of the logits; each rank uploads only its
+ * weight slices and keeps its own KV heads.  Outputs are complete on every rank.
+ * gb_tp_plan returns, without touching a device, the plan of one rank as JSON (weight slices,
+ * partial-sum tensors, rewritten shapes) or NULL (gb_last_error) for unsupported graphs. */
+int gb_nccl_unique_id(void* out128);
+int gb_executor_create_tp(const gb_graph* g, const char* device, int tp_rank, int tp_size,
+                          const void* nccl_id, gb_executor** out);
+const char* gb_tp_plan(const gb_graph* g, int tp_rank, int tp_size);
+int gb_executor_tp_size(const gb_executor* e);
+int gb_executor_tp_rank(const gb_executor* e);
 void gb_executor_free(gb_executor* e);
 const char* gb_executor_device(const gb_executor* e);
 /* prepare(symbols, enable_arena_reuse) — executor.cpp:1453 */
