@@ -8,8 +8,10 @@ A step is one sequence: prefill of 512 prompt tokens (one ubatch, logits of the 
 (runtime/tools/ggmlc_bench.cpp:297-565).  `value` is decode tokens/s with inputs resident in HBM
 (dummy token ids as the reference harness uses, ggmlc_bench.cpp:303,431), timed with CUDA events
 on the executor's stream; `e2e` is the same decode metric through the public API with host
-buffers (token H2D, logits D2H and a host argmax every step).  N > 1 runs independent replicas
-(weak scaling), timed as the max over ranks.
+buffers (token H2D, logits D2H and a host argmax every step).  N > 1 runs the model
+tensor-parallel over the N GPUs (one sequence; strong scaling: QKV / gate_up / O / down / output
+projection sharded, two NCCL all-reduces per layer), or with --replicas N independent copies
+(weak scaling); device time is the max over ranks.
 
 --impl reference times the reference's own CPU runtime (oracle/_ref/ggmlc-bench, built from the
 reference sources) on the same synthesized GGUF, all host threads, a bounded tg sample per step.
@@ -213,7 +215,14 @@ def run_ours(args) -> None:
     from ggmlc_b200 import _runtime as R
 
     g = R.ModelLoader.load_from_file(str(gguf))
-    ex = R.ModelExecutor(g, f"cuda:{local}")
+    tp = world > 1 and not args.replicas
+    if tp:  # one tensor-parallel group over all ranks; the engine's own NCCL communicator
+        box = [R.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=0)
+        ex = R.ModelExecutor(g, f"cuda:{local}", tp_rank=rank, tp_size=world, nccl_id=box[0])
+    else:
+        ex = R.ModelExecutor(g, f"cuda:{local}")
+    seqs = 1 if tp else world  # sequences decoded per step over the whole job
     sym = g.symbol_table[0]
     in_id, out_id = g.inputs[0], g.outputs[0]
     P, G = args.prompt, args.gen
@@ -275,8 +284,8 @@ def run_ours(args) -> None:
         t = torch.tensor([pp_ms, tg_ms, tot_ms], dtype=torch.float64, device=f"cuda:{local}")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         pp_ms, tg_ms, tot_ms = [float(x) for x in t.cpu()]
-    tg_tps = world * args.steps * G / (tg_ms / 1e3)
-    pp_tps = world * args.steps * P / (pp_ms / 1e3)
+    tg_tps = seqs * args.steps * G / (tg_ms / 1e3)
+    pp_tps = seqs * args.steps * P / (pp_ms / 1e3)
 
     # e2e: public API with host buffers — prompt H2D, per-token H2D + logits D2H + host argmax
     e0 = torch.cuda.Event(enable_timing=True)
@@ -304,7 +313,7 @@ def run_ours(args) -> None:
         t = torch.tensor([e2e_pp_ms, e2e_tg_ms], dtype=torch.float64, device=f"cuda:{local}")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_pp_ms, e2e_tg_ms = [float(x) for x in t.cpu()]
-    e2e_tg = world * args.steps * G / (e2e_tg_ms / 1e3)
+    e2e_tg = seqs * args.steps * G / (e2e_tg_ms / 1e3)
 
     # roofline of the dominant decode kernel (Q4_0 GEMV): per-launch events over one sequence
     ex.set_kernel_timing(True)
@@ -333,7 +342,7 @@ def run_ours(args) -> None:
     pp_mm = kt_pp.get("gemm_q", [0, 1, 0])
 
     cb_line = None
-    if not args.no_cb:
+    if not args.no_cb and not tp:
         del ex  # free the single-sequence caches before the batched runs
         try:
             cb_line = run_cb(g, gguf, local)
@@ -346,13 +355,15 @@ def run_ours(args) -> None:
             "metric": METRIC, "value": round(tg_tps, 2), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(tot_ms / args.steps, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None,
+            "scaling": "strong" if tp else "weak", "vs_baseline": None,
             "dtype": "q4_0 x q8_0 int8 dot, fp32 accumulate",
             "data": "synthetic: seeded N(0,0.02) random-init weights (ggmlc Q4_0 quantizer), "
                     "dummy token ids for value, random prompt ids for e2e",
             "config": {"workload": f"{args.model} {args.quant} pp{P}+tg{G} B=1 (BASELINE configs[3])",
                        "model": args.model, "quant": args.quant, "prompt": P, "gen": G,
-                       "batch": 1, "parallelism": f"replicas x{world}" if world > 1 else "single",
+                       "batch": 1,
+                       "parallelism": (f"tp{world}" if tp else f"replicas x{world}") if world > 1
+                       else "single",
                        "l2": f"inputs larger than L2: {weights_gb:.2f} GB of weights streamed per "
                              "decode token", "value_is": f"tg{G} decode tokens/s"},
             "pp512": {"value": round(pp_tps, 1), "unit": "tokens/s",
@@ -364,7 +375,7 @@ def run_ours(args) -> None:
                       if pp_mm[0] else None},
             "e2e": {"value": round(e2e_tg, 2), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h,
-                    "pp512_tokens_per_s": round(world * args.steps * P / (e2e_pp_ms / 1e3), 1)},
+                    "pp512_tokens_per_s": round(seqs * args.steps * P / (e2e_pp_ms / 1e3), 1)},
             "roofline": {"bound": "hbm", "kernel": dom,
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
@@ -552,6 +563,8 @@ def main():
     ap.add_argument("--ref-gen", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cb", action="store_true", help="skip the continuous-batching leg")
+    ap.add_argument("--replicas", action="store_true",
+                    help="N > 1: independent replicas instead of one tensor-parallel group")
     ap.add_argument("--case", choices=sorted(CASES), help="launch one decode kernel of the L8 "
                     "shapes (a small case for ncu) instead of the benchmark")
     ap.add_argument("--reps", type=int, default=5)

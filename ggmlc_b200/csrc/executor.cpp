@@ -1776,7 +1776,10 @@ void Executor::reset_state() {
 }
 
 int64_t Executor::launches_per_run() const {
-    return active_ ? (int64_t)active_->launches.size() : 0;
+    if (!active_) return 0;
+    int64_t n = 0;  // the engine's kernel launches (NCCL collectives are NCCL's kernels)
+    for (auto& name : active_->launch_names) n += name != "allreduce" && name != "allgather";
+    return n;
 }
 
 std::string Executor::graph_summary() const {

@@ -187,7 +187,7 @@ public:
 
     cudaStream_t stream() const { return stream_; }
     const Graph& graph() const { return *g_; }
-    // number of kernel launches of the active program (per run)
+    // number of the engine's kernel launches of the active program per run (collectives excluded)
     int64_t launches_per_run() const;
     size_t weight_bytes() const { return weight_bytes_; }
 
