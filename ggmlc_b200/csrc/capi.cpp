@@ -422,6 +422,27 @@ int gb_mul_mat_q(int type, const void* wq, int64_t N, int64_t K,
         gb::launch_matmul_q(w, xq, xd, M, y, N, ep, (cudaStream_t)stream);
     });
 }
+int gb_gemm_tc(int type, const void* wq, int64_t N, int64_t K, const int8_t* xq, const float* xd,
+               int64_t M, float* y, const float* bias, const float* residual, void* stream) {
+    return guard([&] {
+        GB_CHECK(type == gb::T_Q8_0 || type == gb::T_Q4_0, "gb_gemm_tc: type must be Q8_0 or Q4_0");
+        gb::QWeight w;
+        w.type = type;
+        w.N = N;
+        w.K = K;
+        w.qs = wq;
+        gb::MatmulEpilogue ep;
+        ep.bias = bias;
+        ep.residual = residual;
+        ep.res_stride = N;
+        gb::launch_gemm_tc(w, xq, xd, M, y, N, ep, (cudaStream_t)stream);
+    });
+}
+int gb_gemm_tc_error(void) {
+    int v = 0;
+    const int rc = guard([&] { v = gb::gemm_tc_error(); });
+    return rc == 0 ? v : -1;
+}
 int gb_gemv(int type, const void* wq, int64_t N, int64_t K, int64_t M,
             const int8_t* xq, const float* xd, const float* xf, float eps, const float* gamma,
             int swiglu, float* y, int8_t* yq, float* yd, const float* bias,

@@ -121,6 +121,12 @@ bool gemv_fused_fits(int64_t K, int M);
 // result does not depend on M (nor on the epilogue mode).  Programmatic dependent launch.
 constexpr int kMmvMaxRows = 16;
 void launch_mmv(const GemvArgs& a, cudaStream_t st);
+// Prefill matmul on the 5th-generation tensor cores (k_gemm_tc.cu): tcgen05 int8 MMA into
+// tensor memory, per-block scales in the epilogue; any M.  gemm_tc_error() reads the kernel's
+// sticky error word (non-zero after one of its bounded waits ran out).
+void launch_gemm_tc(const QWeight& w, const int8_t* xq, const float* xd, int64_t M, float* y,
+                    int64_t y_stride, const MatmulEpilogue& ep, cudaStream_t st);
+int gemm_tc_error();
 
 // Float-weight matmul (F32/F16 W, f32 X), used for non-quantized linears.
 void launch_matmul_f(const QWeight& w, const float* x, int64_t x_stride, int64_t M, float* y,

@@ -206,6 +206,15 @@ int gb_quantize_q8_0(const float* x, int64_t x_stride, int64_t M, int64_t K, int
 int gb_mul_mat_q(int type, const void* wq, int64_t N, int64_t K,
                  const int8_t* xq, const float* xd, int64_t M, float* y, const float* bias,
                  const float* residual, void* stream);
+/* The same MUL_MAT on the 5th-generation tensor cores, any M (mul_mat_q mmq.cuh:948 is the
+ * reference's large-M kernel): one tcgen05.mma kind::i8 per 32-element block into tensor
+ * memory, the block scales applied by epilogue warps; block dots exact, block terms summed in
+ * fp32 in block order.  gb_gemm_tc_error returns its sticky error word: 0 while every bounded
+ * wait inside it completed, non-zero after one ran out (that launch left its tile unwritten),
+ * -1 if the word cannot be read. */
+int gb_gemm_tc(int type, const void* wq, int64_t N, int64_t K, const int8_t* xq, const float* xd,
+               int64_t M, float* y, const float* bias, const float* residual, void* stream);
+int gb_gemm_tc_error(void);
 /* Decode GEMV (M <= 8) with fused prologue / epilogue, same arithmetic as gb_mul_mat_q.  Input:
  * Q8_0 rows (xq, xd; xq 16-byte aligned) or, when xf != NULL, f32 rows [M][K] put through
  * RMS_NORM(eps) (* gamma)

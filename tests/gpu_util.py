@@ -35,6 +35,7 @@ def lib():
     L.gb_weight_row_bytes.restype = I64
     L.gb_quantize_q8_0.argtypes = [P, I64, I64, I64, P, P, P]
     L.gb_mul_mat_q.argtypes = [I, P, I64, I64, P, P, I64, P, P, P, P]
+    L.gb_gemm_tc.argtypes = [I, P, I64, I64, P, P, I64, P, P, P, P]
     L.gb_get_rows.argtypes = [I, P, I64, I64, P, I64, P, P]
     L.gb_rms_norm.argtypes = [P, I64, I64, F, P, P, P, P, P]
     L.gb_swiglu.argtypes = [P, I64, I64, P, P, P, P]
@@ -87,12 +88,13 @@ def quantize(x_dev, M: int, K: int):
     return xq, xd
 
 
-def mul_mat(wtype, wq, wd, N, K, x_dev, M, bias=None, residual=None):
+def mul_mat(wtype, wq, wd, N, K, x_dev, M, bias=None, residual=None, tc=False):
+    """gb_mul_mat_q (the dispatching entry), or with tc=True the tensor-core GEMM gb_gemm_tc."""
     torch = torch_dev()
     xq, xd = quantize(x_dev, M, K)
     y = torch.empty((M, N), dtype=torch.float32, device="cuda")
-    check(lib().gb_mul_mat_q(wtype, ptr(wq), N, K, ptr(xq), ptr(xd), M, ptr(y),
-                             ptr(bias), ptr(residual), None))
+    fn = lib().gb_gemm_tc if tc else lib().gb_mul_mat_q
+    check(fn(wtype, ptr(wq), N, K, ptr(xq), ptr(xd), M, ptr(y), ptr(bias), ptr(residual), None))
     torch.cuda.synchronize()
     return y.cpu().numpy()
 

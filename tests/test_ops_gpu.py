@@ -184,6 +184,37 @@ def test_prefill_matmul_close(G, wtype, M, N, K):
 
 
 @pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_0])
+@pytest.mark.parametrize("M,N,K", [(17, 40, 1024), (64, 300, 576), (130, 77, 4096),
+                                   (300, 256, 2048), (5, 128, 14336)])
+def test_tensor_core_gemm_integer_path_bit_exact(G, wtype, M, N, K):
+    """tcgen05 GEMM (gb_gemm_tc): partial row / column tiles, partial 64-block groups (K=576),
+    long K, and M below one tile, on inputs where fp32 summation is exact."""
+    rng = np.random.default_rng(11 * N + K + M + wtype)
+    w, x = _int_exact_case(rng, wtype, N, K, M)
+    wq, wd = G.upload_weight(wtype, w, N, K)
+    y = G.mul_mat(wtype, wq, wd, N, K, G.dev(x), M, tc=True)
+    assert G.lib().gb_gemm_tc_error() == 0
+    assert np.array_equal(y, O.mul_mat(wtype, w, N, K, x))
+
+
+@pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_0])
+@pytest.mark.parametrize("M,N,K", [(64, 200, 1024), (512, 384, 4096)])
+def test_tensor_core_gemm_close_with_epilogue(G, wtype, M, N, K):
+    """tcgen05 GEMM on random data, with bias and residual, within 1e-5 of the output range of
+    the oracle and equal to the dispatching entry wherever that runs the same block order."""
+    rng = np.random.default_rng(M + N + K)
+    w = G.random_blocks(rng, wtype, N, K)
+    wq, wd = G.upload_weight(wtype, w, N, K)
+    x = _x(rng, M, K)
+    bias = rng.standard_normal(N).astype(np.float32)
+    res = rng.standard_normal((M, N)).astype(np.float32)
+    y = G.mul_mat(wtype, wq, wd, N, K, G.dev(x), M, bias=G.dev(bias), residual=G.dev(res), tc=True)
+    assert G.lib().gb_gemm_tc_error() == 0
+    ref = res + (O.mul_mat(wtype, w, N, K, x) + bias[None, :]).astype(np.float32)
+    assert np.max(np.abs(y - ref)) <= 1e-5 * np.max(np.abs(ref))
+
+
+@pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_0])
 @pytest.mark.parametrize("N,K", [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)])
 def test_operator_sweep_shapes_sampled_rows(G, wtype, N, K):
     """Operator-sweep shapes at full size; the oracle checks a sample of output rows (decode M=1
