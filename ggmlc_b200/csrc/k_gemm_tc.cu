@@ -2,13 +2,13 @@
 // kind::i8 with accumulators in tensor memory, per-block fp16 scales applied by epilogue warps.
 //
 // Arithmetic.  One tcgen05.mma (M = 128 weight rows, N = 128 activation rows, K = 32) per
-// 32-element block gives every exact int32 block dot of a 128 x 128 tile.  The accumulator it
-// adds onto holds the 1.5*2^23 bias (0x4B400000), so each result reads back as a float
-// 12582912 + sumi; epilogue warps subtract the bias, multiply by d_w * d_x and accumulate the
-// block terms in fp32 registers, then restore the bias for the next block using that buffer —
-// the block formula of the reference's vec_dot (ggml-cpu/quants.c:225-256, :451-477) with the
-// integer part exact.  Q4_0 nibbles are widened in shared memory to 16 * (q - 8) (exact in
-// int8); their weight scales are divided by 16 to compensate.
+// 32-element block writes every exact int32 block dot of a 128 x 128 tile into a tensor-memory
+// accumulator.  Epilogue warps load it, add the 1.5*2^23 bias as an integer (so the bits read as
+// the float 12582912 + sumi) and subtract it in fp32, multiply by d_w * d_x and accumulate the
+// block terms in fp32 registers — the block formula of the reference's vec_dot
+// (ggml-cpu/quants.c:225-256, :451-477) with the integer part exact.  Q4_0 nibbles are widened
+// in shared memory to 16 * (q - 8) (exact in int8); their weight scales are divided by 16 to
+// compensate.
 //
 // Work split per CTA (128 weight rows x 128 activation rows, 12 warps):
 //   warps 0-2   producers: cp.async of activations / weights / scales for a stage of 4 blocks
@@ -19,7 +19,7 @@
 //               one tcgen05.mma + tcgen05.commit per block;
 //   warps 4-11  epilogue: warp w reads tensor-memory lanes 32*(w%4).. (its weight rows) and
 //               columns 64*((w-4)/4).. (activation rows) of each finished block with
-//               tcgen05.ld, restores the bias with tcgen05.st and releases the accumulator.
+//               tcgen05.ld, releases the accumulator as soon as the loads land, then scales.
 // Every wait on an mbarrier is bounded: past the limit the kernel records an error in
 // gemm_tc_error, stops issuing, waits (bounded) for its tensor-core work to drain, frees the
 // tensor memory and returns.
@@ -137,12 +137,12 @@ __device__ __forceinline__ uint64_t smem_desc(const void* p) {
 constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTN >> 3) << 17) |
                             ((uint32_t)(kTM >> 4) << 24);
 
-// D += A * B (the accumulator is never overwritten: it starts from the bias)
+// D = A * B (enable-input-d false: each block's dots overwrite the accumulator)
 __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc) {
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
         " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(1)
+        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(0)
         : "memory");
 }
 
@@ -165,18 +165,6 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
 __device__ __forceinline__ void tmem_wait_ld() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
-// the bias into 32 consecutive columns of this thread's lane
-__device__ __forceinline__ void tmem_bias32(uint32_t taddr) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
-        "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
-        "r"(kBiasBits)
-        : "memory");
-}
-__device__ __forceinline__ void tmem_wait_st() {
-    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-}
-
 // 32 block terms of one accumulator slice: acc[j] += (v - bias) * (dw * dx)
 __device__ __forceinline__ void scale_acc(const uint32_t (&v)[32], float dw, const float* dx,
                                           float2* acc) {
@@ -187,10 +175,12 @@ __device__ __forceinline__ void scale_acc(const uint32_t (&v)[32], float dw, con
         const float4 x4 = *(const float4*)(dx + 4 * j);
         const float2 p0 = mul2(dw2, make_float2(x4.x, x4.y));
         const float2 p1 = mul2(dw2, make_float2(x4.z, x4.w));
-        const float2 f0 =
-            sub2(make_float2(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1])), bias2);
-        const float2 f1 =
-            sub2(make_float2(__uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3])), bias2);
+        const float2 f0 = sub2(make_float2(__uint_as_float(v[4 * j] + kBiasBits),
+                                           __uint_as_float(v[4 * j + 1] + kBiasBits)),
+                               bias2);
+        const float2 f1 = sub2(make_float2(__uint_as_float(v[4 * j + 2] + kBiasBits),
+                                           __uint_as_float(v[4 * j + 3] + kBiasBits)),
+                               bias2);
         acc[2 * j] = fma2(f0, p0, acc[2 * j]);
         acc[2 * j + 1] = fma2(f1, p1, acc[2 * j + 1]);
     }
@@ -380,14 +370,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
         const int q = warp & 3, h = (warp - kEpiWarp0) >> 2;
         const int r = q * 32 + lane;  // weight row of the tile (tensor-memory lane)
         const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + h * 64;
-        // every accumulator starts at the bias
-        for (int buf = 0; buf < kTBufs; ++buf) {
-            tmem_bias32(lane_base + buf * kTN);
-            tmem_bias32(lane_base + buf * kTN + 32);
-        }
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
+        // every accumulator starts free
         if (lane == 0)
             for (int buf = 0; buf < kTBufs; ++buf) mbar_arrive(&bar_tempty[buf]);
         float2 acc[32];
@@ -415,16 +398,12 @@ __global__ void __launch_bounds__(kTThreads, 1)
                 const uint32_t ta = lane_base + buf * kTN;
                 uint32_t v0[32], v1[32];
                 tmem_ld32(ta, v0);
+                tmem_ld32(ta + 32, v1);
                 tmem_wait_ld();
-                tmem_ld32(ta + 32, v1);  // in flight while the first half is scaled
-                scale_acc(v0, dw, dx, acc);
-                tmem_wait_ld();
-                tmem_bias32(ta);
-                tmem_bias32(ta + 32);
-                tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&bar_tempty[buf]);
+                if (lane == 0) mbar_arrive(&bar_tempty[buf]);  // the MMA may refill it now
+                scale_acc(v0, dw, dx, acc);
                 scale_acc(v1, dw, dx + 32, acc + 16);
             }
             if (!ok) break;
