@@ -456,6 +456,7 @@ CASES = {
     "gemv_res": dict(N=4096, K=14336, mode="res"),                # down + residual
     "attn_decode": dict(Hq=32, Hkv=8, hd=128, ctx=1024, pos=640),
     "gemm_prefill": dict(N=28672, K=4096, M=512, mode="gemm"),    # gate_up at pp512
+    "gemm_prefill_tc": dict(N=28672, K=4096, M=512, mode="gemm_tc"),  # the same on tcgen05
 }
 
 
@@ -501,7 +502,7 @@ def run_case(name: str, reps: int) -> None:
         yd = torch.empty(N // 64, dtype=torch.float32, device=dev)
         L.gb_gemv.argtypes = [I, P, I64, I64, I64, P, P, P, F, P, I, P, P, P, P, P, P]
         mode = c["mode"]
-        if mode == "gemm":
+        if mode in ("gemm", "gemm_tc"):
             M = c["M"]
             xm = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).to(dev)
             xq = torch.empty((M, K), dtype=torch.int8, device=dev)
@@ -509,8 +510,13 @@ def run_case(name: str, reps: int) -> None:
             check(L.gb_quantize_q8_0(ptr(xm), K, M, K, ptr(xq), ptr(xd), None))
             ym = torch.empty((M, N), dtype=torch.float32, device=dev)
             L.gb_mul_mat_q.argtypes = [I, P, I64, I64, P, P, I64, P, P, P, P]
+            L.gb_gemm_tc.argtypes = [I, P, I64, I64, P, P, I64, P, P, P, P]
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
         for _ in range(reps):
-            if mode == "gemm":
+            if mode == "gemm_tc":
+                rc = L.gb_gemm_tc(2, ptr(wq), N, K, ptr(xq), ptr(xd), M, ptr(ym), None, None, None)
+            elif mode == "gemm":
                 rc = L.gb_mul_mat_q(2, ptr(wq), N, K, ptr(xq), ptr(xd), M, ptr(ym), None, None,
                                     None)
             elif mode == "rms_swiglu":
@@ -523,6 +529,7 @@ def run_case(name: str, reps: int) -> None:
                 rc = L.gb_gemv(2, ptr(wq), N, K, 1, ptr(xq), ptr(xd), None, 0.0, None, 0, ptr(y),
                                None, None, None, ptr(res), None)
             check(rc)
+        e1.record()
     else:
         Hq, Hkv, hd, ctx, pos = c["Hq"], c["Hkv"], c["hd"], c["ctx"], c["pos"]
         n_pos = 4096
@@ -547,7 +554,10 @@ def run_case(name: str, reps: int) -> None:
                                    ptr(t_d), n_pos, float(hd) ** -0.5, None, ptr(oq), ptr(od),
                                    ptr(work), None))
     torch.cuda.synchronize()
-    print(json.dumps({"case": name, "launches": reps, **c}))
+    extra = {}
+    if name.startswith("gemv") or name.startswith("gemm"):
+        extra["us_per_launch"] = round(e0.elapsed_time(e1) * 1e3 / reps, 2)  # includes the first
+    print(json.dumps({"case": name, "launches": reps, **c, **extra}))
 
 
 def main():
