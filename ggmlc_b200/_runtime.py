@@ -52,6 +52,7 @@ def _load() -> ctypes.CDLL:
         "gb_tp_plan": ([P, I, I], CP),
         "gb_executor_tp_size": ([P], I),
         "gb_executor_tp_rank": ([P], I),
+        "gb_executor_tp_error": ([P], I),
         "gb_executor_free": ([P], None),
         "gb_executor_device": ([P], CP),
         "gb_executor_prepare": ([P, ctypes.POINTER(CP), ctypes.POINTER(I64), I, I], I),
@@ -293,6 +294,10 @@ class ModelExecutor:
     @property
     def tp_rank(self) -> int:
         return int(_lib.gb_executor_tp_rank(self._h))
+
+    def tp_allreduce_error(self) -> int:
+        """0 while every peer all-reduce completed its waits; 1 once one gave up on a peer."""
+        return int(_lib.gb_executor_tp_error(self._h))
 
     def prepare(self, symbols: dict[str, int] | None = None, enable_arena_reuse: bool = True):
         symbols = dict(symbols or {})

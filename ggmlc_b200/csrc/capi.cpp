@@ -183,6 +183,11 @@ const char* gb_tp_plan(const gb_graph* g, int tp_rank, int tp_size) {
     return rc == 0 ? buf.c_str() : nullptr;
 }
 int gb_executor_tp_size(const gb_executor* e) { return e->e->tp_size(); }
+int gb_executor_tp_error(gb_executor* e) {
+    int v = 0;
+    const int rc = guard([&] { v = e->e->tp_allreduce_error(); });
+    return rc == 0 ? v : -1;
+}
 int gb_executor_tp_rank(const gb_executor* e) { return e->e->tp_rank(); }
 void gb_executor_free(gb_executor* e) { delete e; }
 const char* gb_executor_device(const gb_executor* e) { return e->e->device().c_str(); }

@@ -164,8 +164,63 @@ Executor::Executor(std::shared_ptr<Graph> g, const std::string& device, int tp_r
         ncclComm_t comm = nullptr;
         GB_NCCL(comm_init_rank(&comm, tp_size, id, tp_rank));
         nccl_ = comm;
+        setup_peer_allreduce();
     }
     upload_weights();
+}
+
+// Buffers of the one-shot all-reduce (k_allreduce.cu): room for 16 rows of the widest K-split
+// output, two parities, one slot per rank; handles exchanged with one NCCL all-gather.
+void Executor::setup_peer_allreduce() {
+    const int T = tp_.size, r = tp_.rank;
+    GB_CHECK(T <= kMaxTp, "tensor parallelism: at most 8 ranks");
+    SymEnv env;
+    env["s"] = 1;
+    for (auto& s : g_->symbol_table) env[s] = 1;
+    int64_t width = 0;
+    for (uint32_t id : tp_.partial) {
+        const GTensor& t = g_->t(id);
+        width = std::max<int64_t>(width, t.ne[0] ? t.ne[0]->eval(env) : 1);
+    }
+    ar_cap_ = (std::max<int64_t>(width, 1) * kMaxRows + 3) / 4 * 4;
+    const size_t recv_bytes = (size_t)(2 * T * ar_cap_) * 4;
+    const size_t flag_bytes = (size_t)(2 * T * kArCtas) * 4;
+    GB_CUDA(cudaMalloc(&ar_base_, recv_bytes + flag_bytes));
+    GB_CUDA(cudaMemset(ar_base_, 0, recv_bytes + flag_bytes));
+    GB_CUDA(cudaMalloc(&ar_epochs_, kArCtas * sizeof(uint32_t)));
+    GB_CUDA(cudaMemset(ar_epochs_, 0, kArCtas * sizeof(uint32_t)));
+    GB_CUDA(cudaMalloc(&ar_err_, sizeof(int)));
+    GB_CUDA(cudaMemset(ar_err_, 0, sizeof(int)));
+    cudaIpcMemHandle_t h;
+    GB_CUDA(cudaIpcGetMemHandle(&h, ar_base_));
+    char* dh = nullptr;
+    GB_CUDA(cudaMalloc(&dh, (size_t)T * sizeof(h)));
+    GB_CUDA(cudaMemcpy(dh + (size_t)r * sizeof(h), &h, sizeof(h), cudaMemcpyHostToDevice));
+    GB_NCCL(all_gather(dh + (size_t)r * sizeof(h), dh, sizeof(h), ncclUint8, (ncclComm_t)nccl_,
+                       stream_));
+    GB_CUDA(cudaStreamSynchronize(stream_));
+    std::vector<cudaIpcMemHandle_t> all((size_t)T);
+    GB_CUDA(cudaMemcpy(all.data(), dh, (size_t)T * sizeof(h), cudaMemcpyDeviceToHost));
+    GB_CUDA(cudaFree(dh));
+    ar_peer_.assign((size_t)T, nullptr);
+    for (int p = 0; p < T; ++p) {
+        char* base = ar_base_;
+        if (p != r) {
+            void* m = nullptr;
+            GB_CUDA(cudaIpcOpenMemHandle(&m, all[(size_t)p], cudaIpcMemLazyEnablePeerAccess));
+            base = (char*)m;
+            ar_peer_[(size_t)p] = base;
+        }
+        ar_peers_.recv[p] = (float*)base;
+        ar_peers_.flags[p] = (uint32_t*)(base + recv_bytes);
+    }
+}
+
+int Executor::tp_allreduce_error() {
+    if (!ar_err_) return 0;
+    int v = 0;
+    GB_CUDA(cudaMemcpy(&v, ar_err_, sizeof(int), cudaMemcpyDeviceToHost));
+    return v;
 }
 
 Executor::~Executor() {
@@ -186,6 +241,11 @@ Executor::~Executor() {
     if (d_argmax_) cudaFree(d_argmax_);
     if (h_argmax_) cudaFreeHost(h_argmax_);
     if (arena_) cudaFree(arena_);
+    for (char* m : ar_peer_)
+        if (m) cudaIpcCloseMemHandle(m);
+    if (ar_base_) cudaFree(ar_base_);
+    if (ar_epochs_) cudaFree(ar_epochs_);
+    if (ar_err_) cudaFree(ar_err_);
     if (nccl_) nccl().comm_destroy((ncclComm_t)nccl_);  // after the graphs that captured its calls
     if (stream_) cudaStreamDestroy(stream_);
 }
@@ -624,9 +684,24 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
 
     // tensor-parallel exchanges (NCCL on the executor's stream; captured with the program)
     ncclComm_t comm = (ncclComm_t)nccl_;
+    // partial sums that fit the peer buffers (decode) take the one-shot peer all-reduce, larger
+    // ones (prefill) NCCL's
+    const TpPeers peers = ar_peers_;
+    const int tp_rank = tp_.rank;
+    uint32_t* const ar_epochs = ar_epochs_;
+    int* const ar_err = ar_err_;
+    const int64_t ar_cap = ar_cap_;
     auto tp_allreduce = [&](const Val& y) {
         const BufRef r = y.ref;
         const size_t n = (size_t)nelem(y.ne);
+        const int T = tp_.size;
+        if ((int64_t)n <= ar_cap) {
+            add("allreduce_peer", [=](Program& p, cudaStream_t st) {
+                launch_tp_allreduce((float*)p.ptr(r), (int64_t)n, peers, tp_rank, T, ar_epochs,
+                                    ar_cap, ar_err, st);
+            }, 8.0 * (double)n);
+            return;
+        }
         add("allreduce", [=](Program& p, cudaStream_t st) {
             float* d = (float*)p.ptr(r);
             GB_NCCL(all_reduce(d, d, n, ncclFloat32, ncclSum, comm, st));

@@ -202,6 +202,22 @@ private:
     TpPlan tp_;
     void* nccl_ = nullptr;  // ncclComm_t of the tensor-parallel group
     QWeight tp_vocab_view_;  // this rank's rows of the vocabulary-split projection
+    // peer-memory all-reduce of small partial sums (decode): this rank's buffer, the peers'
+    // buffers mapped with CUDA IPC, per-CTA epochs and the error word
+    void setup_peer_allreduce();
+    char* ar_base_ = nullptr;
+    std::vector<char*> ar_peer_;  // IPC mappings to close (index = rank; own rank null)
+    TpPeers ar_peers_{};
+    uint32_t* ar_epochs_ = nullptr;
+    int* ar_err_ = nullptr;
+    int64_t ar_cap_ = 0;
+
+public:
+    // non-zero once a peer all-reduce gave up waiting for a peer (the sum of that call is not
+    // valid)
+    int tp_allreduce_error();
+
+private:
     std::string device_;
     int dev_ = 0;
     cudaStream_t stream_ = nullptr;

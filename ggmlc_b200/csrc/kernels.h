@@ -128,6 +128,19 @@ void launch_gemm_tc(const QWeight& w, const int8_t* xq, const float* xd, int64_t
                     int64_t y_stride, const MatmulEpilogue& ep, cudaStream_t st);
 int gemm_tc_error();
 
+// Tensor-parallel one-shot all-reduce (k_allreduce.cu): y[0..n) summed over T ranks through
+// peer-mapped buffers of `cap` floats per slot (n <= cap); identical bits on every rank.
+// `epochs` holds kArCtas per-rank counters (zero at set-up), `err` is set non-zero when a bounded
+// wait for a peer ran out.  Every rank must make the same sequence of calls.
+constexpr int kMaxTp = 8;
+constexpr int kArCtas = 4;
+struct TpPeers {
+    float* recv[kMaxTp];      // rank r's receive slots [2][T][cap]
+    uint32_t* flags[kMaxTp];  // rank r's flags [2][T][kArCtas]
+};
+void launch_tp_allreduce(float* y, int64_t n, const TpPeers& peers, int rank, int T,
+                         uint32_t* epochs, int64_t cap, int* err, cudaStream_t st);
+
 // Float-weight matmul (F32/F16 W, f32 X), used for non-quantized linears.
 void launch_matmul_f(const QWeight& w, const float* x, int64_t x_stride, int64_t M, float* y,
                      int64_t y_stride, const MatmulEpilogue& ep, cudaStream_t st);

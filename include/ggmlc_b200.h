@@ -74,6 +74,10 @@ int gb_executor_create_tp(const gb_graph* g, const char* device, int tp_rank, in
                           const void* nccl_id, gb_executor** out);
 const char* gb_tp_plan(const gb_graph* g, int tp_rank, int tp_size);
 int gb_executor_tp_size(const gb_executor* e);
+/* Decode-sized partial sums are summed by a one-shot all-reduce over peer memory (CUDA IPC,
+ * NVLink stores, bounded waits); gb_executor_tp_error returns 0 while every such wait
+ * completed, 1 once one gave up on a peer (that call's sum is not valid), -1 on error. */
+int gb_executor_tp_error(gb_executor* e);
 int gb_executor_tp_rank(const gb_executor* e);
 void gb_executor_free(gb_executor* e);
 const char* gb_executor_device(const gb_executor* e);

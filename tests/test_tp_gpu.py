@@ -3,7 +3,8 @@ model reproduces the reference's logits on the committed fixtures with the singl
 (tests/test_model_gpu.py): cosine >= 0.9998 and greedy tokens equal wherever the reference's
 top-2 gap exceeds 1% of the logit range; both ranks return identical complete logits.  Prefill,
 KV-cache decode (teacher-forced with the reference's tokens) and the vocabulary all-gather are
-covered; the ranks exchange only through the engine's own NCCL communicator."""
+covered; the ranks exchange only through the engine's own NCCL communicator and its one-shot
+peer-memory all-reduce (decode-sized partial sums)."""
 
 from __future__ import annotations
 
@@ -69,6 +70,7 @@ def _rank(rank, world, fixture, idq, outq):
             ex.run()
             dec.append(ex.get_output_array(out_id).reshape(-1).copy())
             pos += 1
+        assert ex.tp_allreduce_error() == 0
         outq.put((rank, full, pre, np.stack(dec), None))
     except Exception as e:  # noqa: BLE001 - reported to the parent
         outq.put((rank, None, None, None, repr(e)))
