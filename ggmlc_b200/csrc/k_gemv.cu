@@ -209,9 +209,10 @@ __device__ __noinline__ void stage_x(const StageIn a, int nb, int nbp, uint4* sx
         return;
     }
     // f32 rows: the row is copied to shared memory with coalesced 16-byte loads (sxf: 33 floats
-    // per block, so a lane walking its own block hits a different bank every step), the sum of
-    // squares taken on the way; then one lane per block applies the scale and gamma (staged in
-    // sgm the same way) and quantizes — quantize_row_q8_0's per-block steps run once per block.
+    // per block, so lanes walking their own half-blocks hit distinct banks), the sum of squares
+    // taken on the way; then two lanes per block apply the scale and gamma (staged in sgm the same
+    // way) and quantize — quantize_row_q8_0's per-block steps, each element's arithmetic
+    // unchanged.
     const bool vec4 = ((uintptr_t)a.xf & 15) == 0 && (a.xf_stride & 3) == 0;
     for (int m = 0; m < a.M; ++m) {
         const float* xr = a.xf + (int64_t)m * a.xf_stride;
@@ -242,37 +243,47 @@ __device__ __noinline__ void stage_x(const StageIn a, int nb, int nbp, uint4* sx
         } else {
             __syncthreads();
         }
-        for (int b = threadIdx.x; b < nbp; b += kThreads) {
-            uint4 qa = make_uint4(0, 0, 0, 0), qb = make_uint4(0, 0, 0, 0);
+        // two lanes per block (elements 0-15 and 16-31 = words 0-3 and 4-7); the block's amax
+        // is combined with one shuffle.  2 * nbp is a multiple of 128, so whole warps take part.
+        for (int it = threadIdx.x; it < 2 * nbp; it += kThreads) {
+            const int b = it >> 1, hh = it & 1;
+            float v[16];
+            float amax = 0.0f;
+            if (b < nb) {
+                const float* xb = sxf + b * 33 + hh * 16;
+                const float* gb_ = sgm + b * 33 + hh * 16;
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    float t = xb[i];
+                    if (a.xf_rms) t = __fmul_rn(t, scale);
+                    if (a.gamma) t = __fmul_rn(t, gb_[i]);
+                    v[i] = t;
+                    amax = fmaxf(amax, fabsf(t));
+                }
+            }
+            amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+            uint4 qw = make_uint4(0, 0, 0, 0);
             float d16 = 0.0f;
             if (b < nb) {
-                const float* xb = sxf + b * 33;
-                const float* gb_ = sgm + b * 33;
-                auto val = [&](int i) {
-                    float v = xb[i];
-                    if (a.xf_rms) v = __fmul_rn(v, scale);
-                    if (a.gamma) v = __fmul_rn(v, gb_[i]);
-                    return v;
-                };
-                float amax = 0.0f;
-#pragma unroll 8
-                for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(val(i)));
                 // quantize_row_q8_0, x86 AVX2 build (arch/x86/quants.c:302-392)
                 d16 = __half2float(__float2half_rn(__fdiv_rn(amax, 127.0f)));
                 const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
-                auto word = [&](int j) {
-                    unsigned w = 0;
+                unsigned w[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    w[j] = 0;
 #pragma unroll
                     for (int e = 0; e < 4; ++e)
-                        w |= ((unsigned)__float2int_rn(__fmul_rn(val(4 * j + e), id)) & 0xFF) << (8 * e);
-                    return w;
-                };
-                qa.x = word(0); qa.y = word(1); qa.z = word(2); qa.w = word(3);
-                qb.x = word(4); qb.y = word(5); qb.z = word(6); qb.w = word(7);
+                        w[j] |= ((unsigned)__float2int_rn(__fmul_rn(v[4 * j + e], id)) & 0xFF) << (8 * e);
+                }
+                qw = make_uint4(w[0], w[1], w[2], w[3]);
             }
-            sxa[m * nbp + b] = qa;
-            sxb[m * nbp + b] = qb;
-            sxd[m * nbp + b] = __fmul_rn(d16, dscale);
+            if (hh == 0) {
+                sxa[m * nbp + b] = qw;
+                sxd[m * nbp + b] = __fmul_rn(d16, dscale);
+            } else {
+                sxb[m * nbp + b] = qw;
+            }
         }
         __syncthreads();  // sxf is reused by the next row
     }

@@ -54,6 +54,10 @@ __global__ void k_rms_norm(const float* __restrict__ x, int64_t x_stride, int64_
     __shared__ double sh[32];
     const int64_t m = blockIdx.x;
     const float* xr = x + m * x_stride;
+    // programmatic dependent launch: wait for the producer of x, then let the consumer start
+    // (it prefetches its weights until its own wait)
+    pdl_wait();
+    pdl_launch();
     double s = 0.0;
     for (int64_t k = threadIdx.x; k < D; k += blockDim.x) {
         const float v = xr[k];
@@ -188,9 +192,8 @@ void launch_rms_norm(const float* x, int64_t x_stride, int64_t M, int64_t D, flo
     check_row_smem(D);
     GB_CHECK(!yq || D % QK == 0, "rms_norm: quantized output needs D % 32 == 0");
     set_smem(k_rms_norm);
-    k_rms_norm<<<(unsigned)M, kRowThreads, D * 4, st>>>(x, x_stride, D, eps, gamma, y, y_stride,
-                                                        yq, yd);
-    GB_CUDA(cudaGetLastError());
+    launch_pdl(k_rms_norm, dim3((unsigned)M), dim3(kRowThreads), (size_t)(D * 4), st, x, x_stride, D,
+               eps, gamma, y, y_stride, yq, yd);
 }
 
 void launch_layer_norm(const float* x, int64_t x_stride, int64_t M, int64_t D, float eps,
