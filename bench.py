@@ -339,7 +339,7 @@ def run_ours(args) -> None:
                 if gemv_all else 0.0)
     dec_total = sum(v[0] for v in kt.values())
     shares = {k: round(v[0] / dec_total, 4) for k, v in sorted(kt.items(), key=lambda x: -x[1][0])}
-    pp_mm = kt_pp.get("gemm_q", [0, 1, 0])
+    pp_mm = [sum(v[i] for k, v in kt_pp.items() if k in ("gemm_q", "gemm_swiglu")) for i in range(3)]
 
     cb_line = None
     if not args.no_cb and not tp:

@@ -878,18 +878,24 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                 }
                 // decode (M <= 16): SwiGLU / residual epilogue fused into the matmul launch; an
                 // unmaterialized RMSNorm input (M <= 4) is normalized in the GEMV prologue
-                const bool dec = is_quant(qw->type) && !last_only &&
-                                 (xin.virt_rms ? Mrun <= kGemvMaxRows && gemv_fused_fits(K, (int)Mrun)
-                                               : Mrun <= kMmvMaxRows);
+                bool dec = is_quant(qw->type) && !last_only &&
+                           (xin.virt_rms ? Mrun <= kGemvMaxRows && gemv_fused_fits(K, (int)Mrun)
+                                         : Mrun <= kMmvMaxRows);
                 GB_CHECK(!xin.virt_rms || dec, "internal: unfused RMSNorm without a decode GEMV");
+                // SwiGLU consumer folded into the matmul epilogue: decode, and prefill whose gate
+                // and up halves split into the block GEMM's 64-unit tiles
+                const bool pre = is_quant(qw->type) && !last_only && !xin.virt_rms &&
+                                 Mrun > kMmvMaxRows && N % 128 == 0;
                 int swi_op = -1;
-                if (dec && !bias && add_op < 0 && !outputs.count(out) && consumers[out].size() == 1) {
+                if ((dec || pre) && !bias && add_op < 0 && !outputs.count(out) &&
+                    consumers[out].size() == 1) {
                     const int ci = consumers[out][0];
                     const GOp& c = G.ops[ci];
                     if ((c.opcode == OP_SWIGLU || c.opcode == OP_GLU) && c.inputs.size() == 1 &&
                         c.i("swapped", 0) == 0 && N % 64 == 0 && xin.nrows() == Mrun)
                         swi_op = ci;
                 }
+                if (swi_op >= 0) dec = true;
                 if (dec) {
                     GemvArgs ga;
                     ga.w = *qw;
@@ -929,7 +935,9 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         }
                         const BufRef hr = h.ref, hq = h.q, hqd = h.qd;
                         const bool hf = h.has_f, hhq = h.has_q;
-                        add(virt ? "gemv_rms_swiglu" : (Mrun <= kGemvMaxRows ? "gemv_swiglu" : "mmv_swiglu"), [=](Program& p, cudaStream_t st) {
+                        add(virt ? "gemv_rms_swiglu"
+                                 : (Mrun <= kGemvMaxRows ? "gemv_swiglu"
+                                                         : (Mrun <= kMmvMaxRows ? "mmv_swiglu" : "gemm_swiglu")), [=](Program& p, cudaStream_t st) {
                             GemvArgs a = ga;
                             if (virt) {
                                 a.xf = (const float*)p.ptr(xr);

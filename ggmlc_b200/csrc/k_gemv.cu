@@ -480,6 +480,18 @@ bool gemv_fused_fits(int64_t K, int M) {
 }
 
 void launch_gemv_fused(const GemvArgs& a, cudaStream_t st) {
+    if (!a.xf && a.M > kMmvMaxRows) {  // prefill: the block GEMM
+        if (a.swiglu) {
+            launch_gemm_swiglu(a, st);
+        } else {
+            MatmulEpilogue ep;
+            ep.bias = a.bias;
+            ep.residual = a.residual;
+            ep.res_stride = a.res_stride;
+            launch_matmul_q(a.w, a.xq, a.xd, a.M, a.y, a.y_stride, ep, st);
+        }
+        return;
+    }
     if (!a.xf && (a.M > kGemvMaxRows || !gemv_fits(a.w.type, a.w.K, a.M, false, false))) {
         launch_mmv(a, st);  // batched decode: the tensor-core kernel
         return;

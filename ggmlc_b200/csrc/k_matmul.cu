@@ -71,17 +71,34 @@ __device__ __forceinline__ void mma_s8(int (&d)[4], const unsigned (&a)[4], unsi
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0x4B400000));
 }
 
-template <int WT>
+// SwiGLU epilogue: the tile's weight rows are gate rows p..p+63 and up rows F+p..F+p+63
+// (p = 64 * blockIdx.x); the CTA writes silu(gate) * up of its 64 units as f32 (y) and/or Q8_0
+// (yq, yd), the arithmetic of launch_swiglu on the plain GEMM's outputs.
+struct SwiOut {
+    int F = 0;
+    float* y = nullptr;
+    int64_t y_stride = 0;
+    int8_t* yq = nullptr;
+    float* yd = nullptr;
+};
+
+template <int WT, int SWI>
 __global__ void __launch_bounds__(kGThreads, 1)
     k_gemm_q(const uint8_t* __restrict__ qs, int N, int K, const int8_t* __restrict__ xq,
              const float* __restrict__ xd, int M, float* __restrict__ y, int64_t y_stride,
-             MatmulEpilogue ep) {
+             MatmulEpilogue ep, SwiOut so) {
     extern __shared__ __align__(128) uint8_t gsm[];
     using S = GStage<WT>;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, tg = lane & 3;
     const int wm = warp >> 2, wn = warp & 3;
     const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * kBN;
+    const int p0 = blockIdx.x * (kBN / 2);
+    // weight row of tile row r
+    auto wrow = [&](int r) {
+        if (SWI) return r < kBN / 2 ? p0 + r : so.F + p0 + r - kBN / 2;
+        return min(n0 + r, N - 1);
+    };
     const int nb = K / QK;
     const int ng = (nb + 63) / 64;
     const int ns = 16 * (ng - 1) + min(16, (nb - 64 * (ng - 1) + 1) / 2);  // stages with a valid block
@@ -117,13 +134,13 @@ __global__ void __launch_bounds__(kGThreads, 1)
             const int r = e / CH, c = e % CH;
             const int lb = c & 3;
             const int gb = gblk(t, lb);
-            const int n = min(n0 + r, N - 1);
+            const int n = wrow(r);
             const uint8_t* src = qs + (int64_t)n * rb + (int64_t)((c >> 2) * nb + gb) * 16;
             const int phys = WT == T_Q8_0 ? (c ^ (r & 7)) : (c ^ ((r >> 1) & 3));
             cp_zfill<16>(sB + r * S::kRowB + phys * 16, src, gb < nb);
         }
         for (int r = tid; r < kBN; r += kGThreads) {
-            const int n = min(n0 + r, N - 1);
+            const int n = wrow(r);
             cp_zfill<8>(sW + r * 8, qs + (int64_t)n * rb + scale_base + (t >> 4) * 128 + (t & 15) * 8,
                         true);
         }
@@ -215,6 +232,40 @@ __global__ void __launch_bounds__(kGThreads, 1)
         }
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
+    if (SWI) {
+        // the tile's results through shared memory (the stage ring is free now), then one warp
+        // per (activation row, 32-unit block): ggml_vec_swiglu_f32 (vec.cpp:417-426) and
+        // quantize_row_q8_0 of the block
+        constexpr int kLd = kBN + 4;
+        float* tile = (float*)gsm;
+        __syncthreads();
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int m = wm * 64 + mt * 16 + g + ((e >> 1) << 3);
+                    const int n = wn * 32 + nt * 8 + 2 * tg + (e & 1);
+                    const float2 pv = acc[mt][nt][e >> 1];
+                    tile[m * kLd + n] = (e & 1) ? pv.y : pv.x;
+                }
+        __syncthreads();
+        for (int task = warp; task < kBM * 2; task += kGThreads / 32) {
+            const int m = task >> 1, j = (task & 1) * 32 + lane;
+            if (m0 + m >= M) continue;  // warp-uniform
+            const float h = __fmul_rn(ref_v_silu(tile[m * kLd + j]), tile[m * kLd + kBN / 2 + j]);
+            const int64_t gm = m0 + m, col = p0 + j;
+            if (so.y) so.y[gm * so.y_stride + col] = h;
+            if (so.yq) {
+                float d16, q;
+                q8_block(h, lane, d16, q);
+                so.yq[gm * so.F + col] = (int8_t)__float2int_rn(q);
+                if (lane == 0) so.yd[gm * (so.F / 32) + col / 32] = d16;
+            }
+        }
+        return;
+    }
 #pragma unroll
     for (int mt = 0; mt < 4; ++mt)
 #pragma unroll
@@ -254,13 +305,74 @@ __global__ void k_matmul_f(QWeight w, const float* __restrict__ x, int64_t x_str
     }
 }
 
+template <int WT, int SWI>
+void config_gemm(int dev) {
+    static std::mutex mu;
+    static bool configured[64] = {};
+    std::lock_guard<std::mutex> lock(mu);
+    if (!configured[dev & 63]) {
+        GB_CUDA(cudaFuncSetAttribute(k_gemm_q<WT, SWI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kGStages * GStage<WT>::kBytes));
+        configured[dev & 63] = true;
+    }
+}
+
+void launch_gemm_block(const QWeight& w, const int8_t* xq, const float* xd, int64_t M, float* y,
+                       int64_t y_stride, const MatmulEpilogue& ep, const SwiOut& so,
+                       cudaStream_t st) {
+    GB_CHECK(w.N < (1LL << 31) && w.K < (1LL << 31) && M < (1LL << 31), "matmul: shape too large");
+    GB_CHECK(((uintptr_t)xq & 15) == 0, "matmul: xq must be 16-byte aligned");
+    const bool swi = so.F > 0;
+    const int64_t tiles = swi ? so.F / (kBN / 2) : (w.N + kBN - 1) / kBN;
+    dim3 grid((unsigned)tiles, (unsigned)((M + kBM - 1) / kBM));
+    int dev = 0;
+    GB_CUDA(cudaGetDevice(&dev));
+    const bool q8 = w.type == T_Q8_0;
+    const uint8_t* qs = (const uint8_t*)w.qs;
+    const int N = (int)w.N, K = (int)w.K;
+    if (q8 && !swi) {
+        config_gemm<T_Q8_0, 0>(dev);
+        k_gemm_q<T_Q8_0, 0><<<grid, kGThreads, kGStages * GStage<T_Q8_0>::kBytes, st>>>(
+            qs, N, K, xq, xd, (int)M, y, y_stride, ep, so);
+    } else if (q8) {
+        config_gemm<T_Q8_0, 1>(dev);
+        k_gemm_q<T_Q8_0, 1><<<grid, kGThreads, kGStages * GStage<T_Q8_0>::kBytes, st>>>(
+            qs, N, K, xq, xd, (int)M, y, y_stride, ep, so);
+    } else if (!swi) {
+        config_gemm<T_Q4_0, 0>(dev);
+        k_gemm_q<T_Q4_0, 0><<<grid, kGThreads, kGStages * GStage<T_Q4_0>::kBytes, st>>>(
+            qs, N, K, xq, xd, (int)M, y, y_stride, ep, so);
+    } else {
+        config_gemm<T_Q4_0, 1>(dev);
+        k_gemm_q<T_Q4_0, 1><<<grid, kGThreads, kGStages * GStage<T_Q4_0>::kBytes, st>>>(
+            qs, N, K, xq, xd, (int)M, y, y_stride, ep, so);
+    }
+    GB_CUDA(cudaGetLastError());
+}
+
 }  // namespace
+
+void launch_gemm_swiglu(const GemvArgs& a, cudaStream_t st) {
+    GB_CHECK(a.xq && a.xd && !a.xf, "gemm swiglu: Q8_0 input required");
+    GB_CHECK(a.w.type == T_Q8_0 || a.w.type == T_Q4_0, "gemm swiglu: quantized weights required");
+    GB_CHECK(a.w.N == 2 * a.F && a.F % (kBN / 2) == 0, "gemm swiglu: N == 2F with F % 64 == 0");
+    GB_CHECK(!a.bias && !a.residual, "gemm swiglu: no bias / residual");
+    GB_CHECK(a.y || a.yq, "gemm swiglu: no output");
+    GB_CHECK(!a.yq == !a.yd, "gemm swiglu: Q8_0 output needs quants and scales");
+    if (a.M == 0) return;
+    SwiOut so;
+    so.F = (int)a.F;
+    so.y = a.y;
+    so.y_stride = a.y_stride;
+    so.yq = a.yq;
+    so.yd = a.yd;
+    launch_gemm_block(a.w, a.xq, a.xd, a.M, nullptr, 0, MatmulEpilogue(), so, st);
+}
 
 void launch_matmul_q(const QWeight& w, const int8_t* xq, const float* xd, int64_t M, float* y,
                      int64_t y_stride, const MatmulEpilogue& ep, cudaStream_t st) {
     GB_CHECK(w.K % QK == 0, "matmul: K must be a multiple of 32");
     if (M == 0 || w.N == 0) return;
-    const bool q8 = w.type == T_Q8_0;
     if (M <= kMmvMaxRows) {
         GemvArgs a;
         a.w = w;
@@ -275,30 +387,7 @@ void launch_matmul_q(const QWeight& w, const int8_t* xq, const float* xd, int64_
         launch_gemv_fused(a, st);
         return;
     }
-    GB_CHECK(w.N < (1LL << 31) && w.K < (1LL << 31) && M < (1LL << 31), "matmul: shape too large");
-    GB_CHECK(((uintptr_t)xq & 15) == 0, "matmul: xq must be 16-byte aligned");
-    dim3 grid((unsigned)((w.N + kBN - 1) / kBN), (unsigned)((M + kBM - 1) / kBM));
-    int dev = 0;
-    GB_CUDA(cudaGetDevice(&dev));
-    static std::mutex mu;
-    static bool configured[64] = {};
-    {
-        std::lock_guard<std::mutex> lock(mu);
-        if (!configured[dev & 63]) {
-            GB_CUDA(cudaFuncSetAttribute(k_gemm_q<T_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kGStages * GStage<T_Q8_0>::kBytes));
-            GB_CUDA(cudaFuncSetAttribute(k_gemm_q<T_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kGStages * GStage<T_Q4_0>::kBytes));
-            configured[dev & 63] = true;
-        }
-    }
-    if (q8)
-        k_gemm_q<T_Q8_0><<<grid, kGThreads, kGStages * GStage<T_Q8_0>::kBytes, st>>>(
-            (const uint8_t*)w.qs, (int)w.N, (int)w.K, xq, xd, (int)M, y, y_stride, ep);
-    else
-        k_gemm_q<T_Q4_0><<<grid, kGThreads, kGStages * GStage<T_Q4_0>::kBytes, st>>>(
-            (const uint8_t*)w.qs, (int)w.N, (int)w.K, xq, xd, (int)M, y, y_stride, ep);
-    GB_CUDA(cudaGetLastError());
+    launch_gemm_block(w, xq, xd, M, y, y_stride, ep, SwiOut(), st);
 }
 
 void launch_matmul_f(const QWeight& w, const float* x, int64_t x_stride, int64_t M, float* y,

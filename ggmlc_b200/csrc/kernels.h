@@ -81,7 +81,7 @@ struct MatmulEpilogue {
 void launch_matmul_q(const QWeight& w, const int8_t* xq, const float* xd, int64_t M, float* y,
                      int64_t y_stride, const MatmulEpilogue& ep, cudaStream_t st);
 // Decode GEMV with fused prologue / epilogue (M <= kGemvMaxRows; Q8_0 input with more rows goes
-// to launch_mmv).  Lanes run along K, so each row costs a fixed number of instructions per weight
+// to launch_mmv, and past 16 rows to the block GEMM with the same epilogues).  Lanes run along K, so each row costs a fixed number of instructions per weight
 // byte; up to 4 rows this beats the tensor-core kernel, whose 16x8 tiles are mostly idle there.
 // Launched as a programmatic dependent launch: its weight loads start before the previous kernel
 // on the stream has finished.
@@ -121,6 +121,9 @@ bool gemv_fused_fits(int64_t K, int M);
 // result does not depend on M (nor on the epilogue mode).  Programmatic dependent launch.
 constexpr int kMmvMaxRows = 16;
 void launch_mmv(const GemvArgs& a, cudaStream_t st);
+// Prefill gate_up matmul (M > 16) with the SwiGLU epilogue of GemvArgs (k_matmul.cu): Q8_0 input,
+// N == 2F, F % 64 == 0, no bias / residual; outputs f32 y and/or Q8_0 yq, yd.
+void launch_gemm_swiglu(const GemvArgs& a, cudaStream_t st);
 // Prefill matmul on the 5th-generation tensor cores (k_gemm_tc.cu): tcgen05 int8 MMA into
 // tensor memory, per-block scales in the epilogue; any M.  gemm_tc_error() reads the kernel's
 // sticky error word (non-zero after one of its bounded waits ran out).

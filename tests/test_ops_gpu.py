@@ -116,6 +116,37 @@ def test_decode_matmul_epilogue(G, wtype):
 
 
 @pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_0])
+@pytest.mark.parametrize("M", [17, 64, 130])
+def test_prefill_gemm_swiglu_epilogue(G, wtype, M):
+    """Prefill gate_up GEMM with SwiGLU and Q8_0 quantization fused in its epilogue (a tile of
+    64 gate rows + the 64 matching up rows): bit-exact with the CPU SwiGLU and quantizer applied
+    to the plain GEMM's outputs."""
+    torch = G.torch_dev()
+    rng = np.random.default_rng(M + 100 * wtype)
+    F, K = 192, 1024
+    N = 2 * F
+    w = G.random_blocks(rng, wtype, N, K, scale=0.05)
+    wq, wd = G.upload_weight(wtype, w, N, K)
+    x = rng.standard_normal((M, K)).astype(np.float32)
+    xq, xd = G.quantize(G.dev(x), M, K)
+    y = torch.empty((M, F), dtype=torch.float32, device="cuda")
+    yq = torch.empty((M, F), dtype=torch.int8, device="cuda")
+    yd = torch.empty((M, F // 32), dtype=torch.float32, device="cuda")
+    L = G.lib_fused()
+    G.check(L.gb_gemv(wtype, G.ptr(wq), N, K, M, G.ptr(xq), G.ptr(xd), None, 0.0, None, 1,
+                      G.ptr(y), G.ptr(yq), G.ptr(yd), None, None, None))
+    gu = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    G.check(L.gb_mul_mat_q(wtype, G.ptr(wq), N, K, G.ptr(xq), G.ptr(xd), M, G.ptr(gu), None, None,
+                           None))
+    h = O.swiglu(gu.cpu().numpy())
+    assert np.array_equal(y.cpu().numpy(), h)
+    hq = O.quantize_q8_0(h).reshape(M, F // 32, 34)
+    assert np.array_equal(yq.cpu().numpy(), hq[:, :, 2:].reshape(M, F).view(np.int8))
+    assert np.array_equal(yd.cpu().numpy(),
+                          hq[:, :, :2].copy().view(np.float16).reshape(M, F // 32).astype(np.float32))
+
+
+@pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_0])
 @pytest.mark.parametrize("K", [576, 4096, 14336])
 def test_decode_rows_independent_of_batch(G, wtype, K):
     """A row's decode-matmul result is bit-identical whatever rows run with it, with the
