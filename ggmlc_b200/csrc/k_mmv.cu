@@ -14,11 +14,13 @@
 // p..p+31 and up rows F+p..F+p+31, four 16-row tiles).  Its K range is cut into steps of 8
 // blocks {j0..j0+3, j0+32..j0+35} of one 64-block group, the blocks whose weight scales share one
 // 16-byte word run of the scale region.  Plain tiles deal the steps to all 8 warps; SwiGLU tiles
-// give each warp one 16-row tile and half of the steps.  A warp streams its steps (weights,
-// weight scales, Q8_0 activations and their scales) through its own 3-slot cp.async ring and
-// reads them back with ldmatrix / 32-bit shared loads; warps meet only at the end of a tile, to
-// add their partial sums in shared memory.  CTAs are persistent over tiles, so a warp's ring runs
-// on into its next tile.
+// give each warp one 16-row tile and half of the steps.  The Q8_0 activations and their scales
+// are staged once per CTA in shared memory, a phase of whole 64-block groups at a time (one
+// phase covers K unless K is long and M large; then every tile restages its phases).  A warp
+// streams only the weights and weight scales of its steps through its own cp.async ring (6 slots
+// for Q4_0, 4 for Q8_0) and reads them back with ldmatrix / 32-bit shared loads; warps meet at
+// phase boundaries and at the end of a tile, to add their partial sums in shared memory.  CTAs
+// are persistent over tiles, so a warp's ring runs on into its next tile.
 //
 // Q4_0 nibbles become int8 with a shift and two bitwise ops: (q<<4) ^ 0x80 read as int8 is
 // 16*(q-8); activation scales are divided by 16 (exact) to compensate.
@@ -41,31 +43,30 @@ namespace {
 constexpr int kVW = 8;            // warps per CTA
 constexpr int kVT = kVW * 32;     // threads per CTA
 constexpr int kVSB = 8;           // blocks per step
-constexpr int kVD = 3;            // ring slots per warp
 constexpr size_t kVSmemMax = 227 * 1024;
+constexpr int kActBytes = 72 * 1024;  // shared-memory budget of one activation phase
 
-template <int WT, int MAXM>
-struct VSlot {
+template <int WT>
+struct WSlot {  // one ring slot: the weights of one step of one 16-row tile
     static constexpr int kQ = WT == T_Q8_0 ? 2 : 1;   // 16-byte chunks per block and weight row
     static constexpr int kW = kVSB * kQ * 16 * 16;     // [block][chunk][row 16][16 B]
     static constexpr int kWs = 16 * 16;                // [row 16][4 words of 2 fp16 scales]
-    static constexpr int kX = kVSB * 2 * MAXM * 16;    // [block][half][m][16 B]
-    static constexpr int kXs = MAXM * kVSB * 4;        // [m][block] fp32
-    static constexpr int kBytes = kW + kWs + kX + kXs;
+    static constexpr int kBytes = kW + kWs;
+    static constexpr int kDepth = WT == T_Q8_0 ? 4 : 6;  // ring slots per warp
 };
+// blocks of one activation phase: whole 64-block groups within the budget
+template <int MAXM>
+constexpr int phase_blocks_max() {
+    return 64 * ((kActBytes / (MAXM * 64 * 36)) > 0 ? (kActBytes / (MAXM * 64 * 36)) : 1);
+}
 
 __device__ __forceinline__ unsigned v_saddr(const void* p) {
     return (unsigned)__cvta_generic_to_shared(p);
 }
-// cp.async of 16 (or 4) bytes; zero fill when !valid (the source address stays in bounds)
+// cp.async of 16 bytes; zero fill when !valid (the source address stays in bounds)
 __device__ __forceinline__ void v_cp16(void* dst, const void* src, bool valid) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(v_saddr(dst)), "l"(src),
                  "r"(valid ? 16 : 0)
-                 : "memory");
-}
-__device__ __forceinline__ void v_cp4(void* dst, const void* src, bool valid) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(v_saddr(dst)), "l"(src),
-                 "r"(valid ? 4 : 0)
                  : "memory");
 }
 __device__ __forceinline__ void v_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
@@ -92,10 +93,10 @@ __device__ __forceinline__ int step_block(int s, int lb) {
 }
 
 // weights and weight scales of step s for the 16 rows starting at row0
-template <int WT, int MAXM>
+template <int WT>
 __device__ __forceinline__ void issue_w(uint8_t* slot, const uint8_t* qs, int64_t rb, int row0,
                                         int N, int nb, int s, int lane) {
-    using S = VSlot<WT, MAXM>;
+    using S = WSlot<WT>;
     constexpr int Q = S::kQ;
 #pragma unroll
     for (int it = 0; it < Q * 4; ++it) {
@@ -116,45 +117,36 @@ __device__ __forceinline__ void issue_w(uint8_t* slot, const uint8_t* qs, int64_
     }
 }
 
-// Q8_0 activations and their scales of step s (rows 0..M-1)
-template <int WT, int MAXM>
-__device__ __forceinline__ void issue_x(uint8_t* slot, const int8_t* xq, const float* xd, int M,
-                                        int K, int nb, int s, int lane, bool xd16) {
-    using S = VSlot<WT, MAXM>;
-    uint8_t* sx = slot + S::kW + S::kWs;
-    float* sxs = (float*)(sx + S::kX);
-    for (int c = lane; c < 16 * M; c += 32) {  // [m][block][half]
-        const int half = c & 1, lb = (c >> 1) & 7, m = c >> 4;
-        const int blk = step_block(s, lb);
-        v_cp16(sx + ((lb * 2 + half) * MAXM + m) * 16,
-               xq + (int64_t)m * K + (int64_t)min(blk, nb - 1) * 32 + half * 16, blk < nb);
+// Q8_0 activations and scales of blocks [pbase, pbase + KC) of rows 0..M-1, by the whole CTA:
+// sx [block][half][m][16 B], sxs [m][block]; blocks past nb are zero.  Rows run fastest so the
+// 16-byte shared stores of a warp are contiguous.
+template <int MAXM>
+__device__ __forceinline__ void stage_act(uint8_t* sx, float* sxs, const int8_t* xq,
+                                          const float* xd, int M, int K, int nb, int pbase, int KC) {
+    for (int e = threadIdx.x; e < M * KC * 2; e += kVT) {
+        const int m = e % M, rest = e / M, half = rest & 1, pb = rest >> 1;
+        const int blk = pbase + pb;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (blk < nb) v = __ldcg((const uint4*)(xq + (int64_t)m * K + (int64_t)blk * 32 + half * 16));
+        *(uint4*)(sx + ((pb * 2 + half) * MAXM + m) * 16) = v;
     }
-    if (xd16) {  // nb % 4 == 0: the 4 scales of each half-step are one aligned 16-byte run
-        for (int c = lane; c < 2 * M; c += 32) {
-            const int h = c & 1, m = c >> 1;
-            const int blk = step_block(s, 4 * h);
-            v_cp16(sxs + m * 8 + h * 4, xd + (int64_t)m * nb + min(blk, nb - 4), blk < nb);
-        }
-    } else {
-        for (int c = lane; c < 8 * M; c += 32) {
-            const int lb = c & 7, m = c >> 3;
-            const int blk = step_block(s, lb);
-            v_cp4(sxs + m * 8 + lb, xd + (int64_t)m * nb + min(blk, nb - 1), blk < nb);
-        }
+    for (int e = threadIdx.x; e < M * KC; e += kVT) {
+        const int m = e / KC, pb = e % KC;
+        const int blk = pbase + pb;
+        sxs[m * KC + pb] = blk < nb ? __ldcg(xd + (int64_t)m * nb + blk) : 0.0f;
     }
 }
 
-// accumulate the 8 blocks of a landed step
+// accumulate the 8 blocks of a landed step; pb0 = phase-local index of the step's first block
 template <int WT, int MAXM>
-__device__ __forceinline__ void consume(const uint8_t* slot, int M, int lane,
+__device__ __forceinline__ void consume(const uint8_t* slot, const uint8_t* sX, const float* sXs,
+                                        int KC, int pb0, int M, int lane,
                                         float2 (&acc)[(MAXM + 7) / 8][2]) {
-    using S = VSlot<WT, MAXM>;
+    using S = WSlot<WT>;
     constexpr int NT = (MAXM + 7) / 8;
     const int g = lane >> 2, tg = lane & 3;
     const uint8_t* sW = slot;
     const uint8_t* sWs = slot + S::kW;
-    const uint8_t* sX = sWs + S::kWs;
-    const float* sXs = (const float*)(sX + S::kX);
     const float xsc = WT == T_Q4_0 ? 0.0625f : 1.0f;  // Q4_0 fragments hold 16 * (q - 8)
     const float2 bias2 = make_float2(12582912.0f, 12582912.0f);
     // ldmatrix row address of this lane: matrix lane>>3, row lane&7
@@ -180,17 +172,18 @@ __device__ __forceinline__ void consume(const uint8_t* slot, int M, int lane,
         const float dw1 = __half2float(*(const __half*)(sWs + (g + 8) * 16 + so));
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
+            const int pb = pb0 + 32 * (lb >> 2) + (lb & 3);
             const int cb = nt * 8 + g;  // activation row feeding this lane's B fragment
             unsigned b0 = 0, b1 = 0;
             if (MAXM == 1 ? g == 0 : cb < M) {
-                b0 = *(const unsigned*)(sX + ((lb * 2) * MAXM + cb) * 16 + tg * 4);
-                b1 = *(const unsigned*)(sX + ((lb * 2 + 1) * MAXM + cb) * 16 + tg * 4);
+                b0 = *(const unsigned*)(sX + ((pb * 2) * MAXM + cb) * 16 + tg * 4);
+                b1 = *(const unsigned*)(sX + ((pb * 2 + 1) * MAXM + cb) * 16 + tg * 4);
             }
             int d[4];
             v_mma(d, af, b0, b1);
             const int c0 = nt * 8 + 2 * tg;
-            const float dx0 = c0 < M ? __fmul_rn(sXs[c0 * 8 + lb], xsc) : 0.0f;
-            const float dx1 = c0 + 1 < M ? __fmul_rn(sXs[(c0 + 1) * 8 + lb], xsc) : 0.0f;
+            const float dx0 = c0 < M ? __fmul_rn(sXs[c0 * KC + pb], xsc) : 0.0f;
+            const float dx1 = c0 + 1 < M ? __fmul_rn(sXs[(c0 + 1) * KC + pb], xsc) : 0.0f;
             const float2 p0 = make_float2(__fmul_rn(dw0, dx0), __fmul_rn(dw0, dx1));
             const float2 p1 = make_float2(__fmul_rn(dw1, dx0), __fmul_rn(dw1, dx1));
             const float2 v0 = sub2(make_float2(__int_as_float(d[0]), __int_as_float(d[1])), bias2);
@@ -202,8 +195,9 @@ __device__ __forceinline__ void consume(const uint8_t* slot, int M, int lane,
 }
 
 template <int WT, int MAXM, int SWI>
-__global__ void __launch_bounds__(kVT, (WT == T_Q4_0 && MAXM <= 2) ? 3 : 2) k_mmv(GemvArgs a, int ns, int ntiles, int xd16) {
-    using S = VSlot<WT, MAXM>;
+__global__ void __launch_bounds__(kVT, 1) k_mmv(GemvArgs a, int ns, int ntiles, int KC) {
+    using S = WSlot<WT>;
+    constexpr int D = S::kDepth;
     constexpr int NT = (MAXM + 7) / 8;
     constexpr int KW = SWI ? 2 : 8;   // K ranges per tile
     constexpr int MT = SWI ? 4 : 1;   // 16-row tiles per CTA tile
@@ -214,17 +208,21 @@ __global__ void __launch_bounds__(kVT, (WT == T_Q4_0 && MAXM <= 2) ? 3 : 2) k_mm
     const int g = lane >> 2, tg = lane & 3;
     const int kw = SWI ? warp >> 2 : warp;
     const int mt = SWI ? warp & 3 : 0;
-    uint8_t* ring = smem + warp * kVD * S::kBytes;
-    float* red = (float*)(smem + kVW * kVD * S::kBytes);  // [KW][MT*16][RC]
+    uint8_t* sx = smem;                                             // activation phase
+    float* sxs = (float*)(sx + (size_t)KC * 2 * MAXM * 16);
+    uint8_t* ring = (uint8_t*)(sxs + (size_t)MAXM * KC) + warp * D * S::kBytes;
+    float* red = (float*)((uint8_t*)(sxs + (size_t)MAXM * KC) + kVW * D * S::kBytes);
     const int N = (int)a.w.N, K = (int)a.w.K, nb = K / QK, M = a.M;
     const int F = (int)a.F;
     const int64_t rb = qrow_bytes(WT, K);
     const uint8_t* qs = (const uint8_t*)a.w.qs;
+    const int sp = KC / 8;                     // steps per phase
+    const int nphase = (ns + sp - 1) / sp;
     auto row0 = [&](int tile) {
         return SWI ? (mt < 2 ? 0 : F) + tile * 32 + (mt & 1) * 16 : tile * 16;
     };
     const bool active = kw < ns;  // a warp with no step in a tile only adds zeros
-    // issue cursor over this warp's (tile, step) sequence
+    // issue cursor over this warp's (tile, step) sequence: weights only
     int it = blockIdx.x, is = kw, islot = 0;
     auto advance = [&](int& t, int& s) {
         s += KW;
@@ -233,28 +231,20 @@ __global__ void __launch_bounds__(kVT, (WT == T_Q4_0 && MAXM <= 2) ? 3 : 2) k_mm
             t += gridDim.x;
         }
     };
-    {
-        int t = it, s = is;
 #pragma unroll
-        for (int d = 0; d < kVD - 1; ++d) {
-            if (active && t < ntiles)
-                issue_w<WT, MAXM>(ring + d * S::kBytes, qs, rb, row0(t), N, nb, s, lane);
-            advance(t, s);
-        }
-    }
-    pdl_wait();
-    pdl_launch();
-#pragma unroll
-    for (int d = 0; d < kVD - 1; ++d) {
-        if (active && it < ntiles)
-            issue_x<WT, MAXM>(ring + d * S::kBytes, a.xq, a.xd, M, K, nb, is, lane, xd16 != 0);
+    for (int d = 0; d < D - 1; ++d) {
+        if (active && it < ntiles) issue_w<WT>(ring + d * S::kBytes, qs, rb, row0(it), N, nb, is, lane);
+        v_commit();
         advance(it, is);
     }
-    v_commit();
-#pragma unroll
-    for (int d = 1; d < kVD - 1; ++d) v_commit();
-    islot = kVD - 1;
+    islot = D - 1;
     int cslot = 0;
+    pdl_wait();
+    pdl_launch();
+    if (nphase == 1) {  // one phase: staged once for every tile
+        stage_act<MAXM>(sx, sxs, a.xq, a.xd, M, K, nb, 0, KC);
+        __syncthreads();
+    }
 
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
         // acc[i] sums the steps s == kw + KW*i (mod 8): every output is built from the same eight
@@ -264,26 +254,31 @@ __global__ void __launch_bounds__(kVT, (WT == T_Q4_0 && MAXM <= 2) ? 3 : 2) k_mm
         for (int i = 0; i < KS; ++i)
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) acc[i][nt][0] = acc[i][nt][1] = make_float2(0.0f, 0.0f);
-        if (active) {
-            for (int s0 = kw; s0 < ns; s0 += 8) {
-#pragma unroll
-                for (int i = 0; i < KS; ++i) {
-                    if (s0 + KW * i < ns) {
-                        v_wait<kVD - 2>();
-                        __syncwarp();
-                        // refill the slot the previous step consumed
-                        if (it < ntiles) {
-                            uint8_t* sl = ring + islot * S::kBytes;
-                            issue_w<WT, MAXM>(sl, qs, rb, row0(it), N, nb, is, lane);
-                            issue_x<WT, MAXM>(sl, a.xq, a.xd, M, K, nb, is, lane, xd16 != 0);
-                            advance(it, is);
-                        }
-                        v_commit();
-                        islot = islot + 1 == kVD ? 0 : islot + 1;
-                        consume<WT, MAXM>(ring + cslot * S::kBytes, M, lane, acc[i]);
-                        cslot = cslot + 1 == kVD ? 0 : cslot + 1;
-                    }
+        for (int ph = 0; ph < nphase; ++ph) {
+            if (nphase > 1) {  // every warp is done with the previous phase's activations
+                __syncthreads();
+                stage_act<MAXM>(sx, sxs, a.xq, a.xd, M, K, nb, ph * KC, KC);
+                __syncthreads();
+            }
+            const int s_end = min(ns, (ph + 1) * sp);
+            int s = ph * sp + ((kw - ph * sp) % KW + KW) % KW;  // this warp's first step here
+            for (; active && s < s_end; s += KW) {
+                v_wait<D - 2>();
+                __syncwarp();
+                // refill the slot the previous step consumed
+                if (it < ntiles) {
+                    issue_w<WT>(ring + islot * S::kBytes, qs, rb, row0(it), N, nb, is, lane);
+                    advance(it, is);
                 }
+                v_commit();
+                islot = islot + 1 == D ? 0 : islot + 1;
+                const int i = ((s - kw) / KW) % KS;
+                const int pb0 = 64 * (s >> 3) + (s & 7) * 4 - ph * KC;
+#pragma unroll
+                for (int j = 0; j < KS; ++j)
+                    if (j == i)
+                        consume<WT, MAXM>(ring + cslot * S::kBytes, sx, sxs, KC, pb0, M, lane, acc[j]);
+                cslot = cslot + 1 == D ? 0 : cslot + 1;
             }
         }
         // SwiGLU warps fold their four partials: ((P_kw + P_kw+2) + P_kw+4) + P_kw+6
@@ -339,38 +334,46 @@ __global__ void __launch_bounds__(kVT, (WT == T_Q4_0 && MAXM <= 2) ? 3 : 2) k_mm
 }
 
 template <int WT, int MAXM>
-constexpr size_t v_smem() {
-    return (size_t)kVW * kVD * VSlot<WT, MAXM>::kBytes + (size_t)1024 * ((MAXM + 7) / 8) * 4;
+constexpr size_t v_fixed_smem() {  // rings and partial sums
+    return (size_t)kVW * WSlot<WT>::kDepth * WSlot<WT>::kBytes + (size_t)1024 * ((MAXM + 7) / 8) * 4;
 }
 
 template <int WT, int MAXM, int SWI>
 void launch_v(const GemvArgs& a, cudaStream_t st) {
     auto kern = k_mmv<WT, MAXM, SWI>;
-    constexpr size_t smem = v_smem<WT, MAXM>();
-    static_assert(smem <= kVSmemMax, "mmv: ring does not fit in shared memory");
+    constexpr int kPhaseMax = phase_blocks_max<MAXM>();
+    constexpr size_t smem_max = (size_t)kPhaseMax * MAXM * 36 + v_fixed_smem<WT, MAXM>();
+    static_assert(smem_max <= kVSmemMax, "mmv: stage and rings do not fit in shared memory");
     int dev = 0;
     GB_CUDA(cudaGetDevice(&dev));
     GB_CHECK(dev >= 0 && dev < 64, "mmv: device ordinal out of range");
-    static std::mutex mu;
-    static int per_sm[64] = {};
-    {
-        std::lock_guard<std::mutex> lock(mu);
-        if (!per_sm[dev]) {
-            GB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-            int n = 0;
-            GB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kVT, smem));
-            per_sm[dev] = std::max(n, 1);
-        }
-    }
     const int nb = (int)(a.w.K / QK);
     const int ng = (nb + 63) / 64;
     const int rem = nb - 64 * (ng - 1);
     const int ns = 8 * (ng - 1) + (std::min(rem, 32) + 3) / 4;
+    const int KC = std::min(64 * ng, kPhaseMax);
+    const size_t smem = (size_t)KC * MAXM * 36 + v_fixed_smem<WT, MAXM>();
+    static std::mutex mu;
+    static bool configured[64] = {};
+    static int per_sm[64][kPhaseMax / 64 + 1] = {};  // [device][KC / 64]: resident CTAs per SM
+    const int key = KC / 64;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!configured[dev]) {
+            GB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem_max));
+            configured[dev] = true;
+        }
+        if (!per_sm[dev][key]) {
+            int n = 0;
+            GB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kern, kVT, smem));
+            per_sm[dev][key] = std::max(n, 1);
+        }
+    }
     const int ntiles = SWI ? (int)(a.F / 32) : (int)((a.w.N + 15) / 16);
     if (ntiles == 0) return;
-    const int xd16 = (nb % 4 == 0 && ((uintptr_t)a.xd & 15) == 0) ? 1 : 0;
-    const int grid = (int)std::min<int64_t>(ntiles, (int64_t)sm_count(dev) * per_sm[dev]);
-    launch_pdl(kern, (unsigned)grid, kVT, smem, st, a, ns, ntiles, xd16);
+    const int grid = (int)std::min<int64_t>(ntiles, (int64_t)sm_count(dev) * per_sm[dev][key]);
+    launch_pdl(kern, (unsigned)grid, kVT, smem, st, a, ns, ntiles, KC);
 }
 
 template <int WT, int SWI>
