@@ -54,12 +54,6 @@ struct WSlot {  // one ring slot: the weights of one step of one 16-row tile
     static constexpr int kBytes = kW + kWs;
     static constexpr int kDepth = WT == T_Q8_0 ? 4 : 6;  // ring slots per warp
 };
-// blocks of one activation phase: whole 64-block groups within the budget
-template <int MAXM>
-constexpr int phase_blocks_max() {
-    return 64 * ((kActBytes / (MAXM * 64 * 36)) > 0 ? (kActBytes / (MAXM * 64 * 36)) : 1);
-}
-
 __device__ __forceinline__ unsigned v_saddr(const void* p) {
     return (unsigned)__cvta_generic_to_shared(p);
 }
@@ -117,38 +111,77 @@ __device__ __forceinline__ void issue_w(uint8_t* slot, const uint8_t* qs, int64_
     }
 }
 
-// Q8_0 activations and scales of blocks [pbase, pbase + KC) of rows 0..M-1, by the whole CTA:
-// sx [block][half][m][16 B], sxs [m][block]; blocks past nb are zero.  Rows run fastest so the
-// 16-byte shared stores of a warp are contiguous.
+// staged activation rows: ldmatrix reads B fragments as 8-row matrices
+template <int MAXM>
+constexpr int stage_rows() { return MAXM < 8 ? 8 : MAXM; }
+
+// Stage the Q8_0 activations of blocks [pbase, pbase + KC), rows 0..M-1, by the whole CTA:
+// sx [block][half][row SR][16 B] by cp.async (one commit group per thread; blocks past nb are zero
+// filled, rows M..SR-1 are left as they are), sxs [block][row SR] fp32 scales times xsc (0 for
+// rows >= M and blocks past nb, so whatever sits in those rows of sx contributes exact zeros).
 template <int MAXM>
 __device__ __forceinline__ void stage_act(uint8_t* sx, float* sxs, const int8_t* xq,
-                                          const float* xd, int M, int K, int nb, int pbase, int KC) {
-    for (int e = threadIdx.x; e < M * KC * 2; e += kVT) {
-        const int m = e % M, rest = e / M, half = rest & 1, pb = rest >> 1;
-        const int blk = pbase + pb;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (blk < nb) v = __ldcg((const uint4*)(xq + (int64_t)m * K + (int64_t)blk * 32 + half * 16));
-        *(uint4*)(sx + ((pb * 2 + half) * MAXM + m) * 16) = v;
+                                          const float* xd, int M, int K, int nb, int pbase, int KC,
+                                          float xsc) {
+    constexpr int SR = stage_rows<MAXM>();
+    for (int e = threadIdx.x; e < KC * 2 * SR; e += kVT) {
+        const int m = e % SR, hb = e / SR, half = hb & 1, pb = hb >> 1;
+        if (m < M) {
+            const int blk = pbase + pb;
+            v_cp16(sx + (size_t)e * 16,
+                   xq + (int64_t)m * K + (int64_t)min(blk, nb - 1) * 32 + half * 16, blk < nb);
+        }
     }
-    for (int e = threadIdx.x; e < M * KC; e += kVT) {
-        const int m = e / KC, pb = e % KC;
-        const int blk = pbase + pb;
-        sxs[m * KC + pb] = blk < nb ? __ldcg(xd + (int64_t)m * nb + blk) : 0.0f;
+    v_commit();
+    // scales: up to 8 independent loads in flight per thread before the stores
+    for (int e0 = threadIdx.x; e0 < KC * SR; e0 += 8 * kVT) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int e = e0 + j * kVT;
+            const int m = e % SR, blk = pbase + e / SR;
+            v[j] = (e < KC * SR && m < M && blk < nb) ? __ldcg(xd + (int64_t)m * nb + blk) : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int e = e0 + j * kVT;
+            if (e < KC * SR) sxs[e] = __fmul_rn(v[j], xsc);
+        }
     }
 }
 
-// accumulate the 8 blocks of a landed step; pb0 = phase-local index of the step's first block
+// wait until at most n of this thread's newest commit groups are pending (0 <= n <= 5)
+__device__ __forceinline__ void v_wait_dyn(int n) {
+    switch (n) {
+        case 0: v_wait<0>(); break;
+        case 1: v_wait<1>(); break;
+        case 2: v_wait<2>(); break;
+        case 3: v_wait<3>(); break;
+        case 4: v_wait<4>(); break;
+        default: v_wait<5>(); break;
+    }
+}
+
+__device__ __forceinline__ void v_ldsm2(unsigned (&r)[2], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];"
+                 : "=r"(r[0]), "=r"(r[1])
+                 : "r"(v_saddr(p)));
+}
+
+// accumulate the 8 blocks of a landed step; pb0 = stage-local index of the step's first block
 template <int WT, int MAXM>
 __device__ __forceinline__ void consume(const uint8_t* slot, const uint8_t* sX, const float* sXs,
-                                        int KC, int pb0, int M, int lane,
-                                        float2 (&acc)[(MAXM + 7) / 8][2]) {
+                                        int pb0, int lane, float2 (&acc)[(MAXM + 7) / 8][2]) {
     using S = WSlot<WT>;
     constexpr int NT = (MAXM + 7) / 8;
+    constexpr int SR = stage_rows<MAXM>();
     const int g = lane >> 2, tg = lane & 3;
     const uint8_t* sW = slot;
-    const uint8_t* sWs = slot + S::kW;
-    const float xsc = WT == T_Q4_0 ? 0.0625f : 1.0f;  // Q4_0 fragments hold 16 * (q - 8)
     const float2 bias2 = make_float2(12582912.0f, 12582912.0f);
+    // the 8 weight scales of rows g and g + 8 (fp16, block lb at half (lb & 3) * 2 + (lb >> 2))
+    const uint4 ws0 = *(const uint4*)(slot + S::kW + g * 16);
+    const uint4 ws1 = *(const uint4*)(slot + S::kW + (g + 8) * 16);
+    const unsigned wa[4] = {ws0.x, ws0.y, ws0.z, ws0.w}, wb[4] = {ws1.x, ws1.y, ws1.z, ws1.w};
     // ldmatrix row address of this lane: matrix lane>>3, row lane&7
     const int lm = lane >> 3, lr = lane & 7;
     unsigned t[4] = {0, 0, 0, 0};
@@ -167,25 +200,33 @@ __device__ __forceinline__ void consume(const uint8_t* slot, const uint8_t* sX, 
             af[2] = (w0 & 0xF0F0F0F0u) ^ 0x80808080u;         // row g, k 16+4tg..: high nibbles
             af[3] = (w1 & 0xF0F0F0F0u) ^ 0x80808080u;
         }
-        const int so = (lb & 3) * 4 + (lb >> 2) * 2;
-        const float dw0 = __half2float(*(const __half*)(sWs + g * 16 + so));
-        const float dw1 = __half2float(*(const __half*)(sWs + (g + 8) * 16 + so));
+        const int hw = (lb & 3) * 2 + (lb >> 2);
+        const unsigned sh = (hw & 1) * 16;
+        const float dw0 = __half2float(__ushort_as_half((unsigned short)(wa[hw >> 1] >> sh)));
+        const float dw1 = __half2float(__ushort_as_half((unsigned short)(wb[hw >> 1] >> sh)));
+        const int pb = pb0 + 32 * (lb >> 2) + (lb & 3);
+        // B fragments: matrices (half 0, rows 0-7), (half 1, rows 0-7), (half 0, rows 8-15), ...
+        unsigned bq[2 * NT];
+        const uint8_t* brow = sX + ((pb * 2 + (lm & 1)) * SR + (lm >> 1) * 8 + lr) * 16;
+        if (NT == 2) {
+            unsigned r4[4];
+            v_ldsm4(r4, brow);
+#pragma unroll
+            for (int i = 0; i < 2 * NT; ++i) bq[i] = r4[i];
+        } else {
+            unsigned r2[2];
+            v_ldsm2(r2, sX + ((pb * 2 + (lm & 1)) * SR + lr) * 16);
+            bq[0] = r2[0];
+            bq[1] = r2[1];
+        }
+        (void)brow;
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-            const int pb = pb0 + 32 * (lb >> 2) + (lb & 3);
-            const int cb = nt * 8 + g;  // activation row feeding this lane's B fragment
-            unsigned b0 = 0, b1 = 0;
-            if (MAXM == 1 ? g == 0 : cb < M) {
-                b0 = *(const unsigned*)(sX + ((pb * 2) * MAXM + cb) * 16 + tg * 4);
-                b1 = *(const unsigned*)(sX + ((pb * 2 + 1) * MAXM + cb) * 16 + tg * 4);
-            }
             int d[4];
-            v_mma(d, af, b0, b1);
-            const int c0 = nt * 8 + 2 * tg;
-            const float dx0 = c0 < M ? __fmul_rn(sXs[c0 * KC + pb], xsc) : 0.0f;
-            const float dx1 = c0 + 1 < M ? __fmul_rn(sXs[(c0 + 1) * KC + pb], xsc) : 0.0f;
-            const float2 p0 = make_float2(__fmul_rn(dw0, dx0), __fmul_rn(dw0, dx1));
-            const float2 p1 = make_float2(__fmul_rn(dw1, dx0), __fmul_rn(dw1, dx1));
+            v_mma(d, af, bq[2 * nt], bq[2 * nt + 1]);
+            const float2 dx = *(const float2*)(sXs + pb * SR + nt * 8 + 2 * tg);
+            const float2 p0 = mul2(make_float2(dw0, dw0), dx);
+            const float2 p1 = mul2(make_float2(dw1, dw1), dx);
             const float2 v0 = sub2(make_float2(__int_as_float(d[0]), __int_as_float(d[1])), bias2);
             const float2 v1 = sub2(make_float2(__int_as_float(d[2]), __int_as_float(d[3])), bias2);
             acc[nt][0] = fma2(v0, p0, acc[nt][0]);
@@ -194,141 +235,189 @@ __device__ __forceinline__ void consume(const uint8_t* slot, const uint8_t* sX, 
     }
 }
 
+// Work order of a CTA: its tiles (blockIdx.x + i * gridDim.x) in chunks of TM; per chunk, the
+// activation phases; per phase, each tile of the chunk; per tile, this warp's steps of the phase
+// (s = ph * sp + kw + KW * j).  Accumulators of the whole chunk stay in registers across phases,
+// so each tile still sums its steps in ascending order.  The weight issue cursor walks the same
+// order D - 1 steps ahead.
+struct VCursor {
+    int c, ph, tt, s;  // chunk (first tile index of this CTA's list), phase, tile in chunk, step
+};
+
 template <int WT, int MAXM, int SWI>
-__global__ void __launch_bounds__(kVT, 1) k_mmv(GemvArgs a, int ns, int ntiles, int KC) {
+__global__ void __launch_bounds__(kVT, 1) k_mmv(GemvArgs a, int ns, int ntiles, int KC, int nphase) {
     using S = WSlot<WT>;
     constexpr int D = S::kDepth;
     constexpr int NT = (MAXM + 7) / 8;
+    constexpr int SR = stage_rows<MAXM>();
     constexpr int KW = SWI ? 2 : 8;   // K ranges per tile
     constexpr int MT = SWI ? 4 : 1;   // 16-row tiles per CTA tile
     constexpr int RC = 8 * NT;        // partial-sum columns
     constexpr int KS = 8 / KW;        // partial sums held per warp
+    constexpr int TM = SWI ? 1 : 4;   // tiles per chunk
     extern __shared__ __align__(16) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, tg = lane & 3;
     const int kw = SWI ? warp >> 2 : warp;
     const int mt = SWI ? warp & 3 : 0;
-    uint8_t* sx = smem;                                             // activation phase
-    float* sxs = (float*)(sx + (size_t)KC * 2 * MAXM * 16);
-    uint8_t* ring = (uint8_t*)(sxs + (size_t)MAXM * KC) + warp * D * S::kBytes;
-    float* red = (float*)((uint8_t*)(sxs + (size_t)MAXM * KC) + kVW * D * S::kBytes);
+    const int nbuf = nphase > 1 ? 2 : 1;
+    const size_t stage_bytes = (size_t)KC * SR * 36;
+    uint8_t* ring = smem + nbuf * stage_bytes + warp * D * S::kBytes;
+    float* red = (float*)(smem + nbuf * stage_bytes + kVW * D * S::kBytes);
+    auto sx_of = [&](int b) { return smem + b * stage_bytes; };
+    auto sxs_of = [&](int b) { return (float*)(smem + b * stage_bytes + (size_t)KC * 2 * SR * 16); };
     const int N = (int)a.w.N, K = (int)a.w.K, nb = K / QK, M = a.M;
     const int F = (int)a.F;
     const int64_t rb = qrow_bytes(WT, K);
     const uint8_t* qs = (const uint8_t*)a.w.qs;
-    const int sp = KC / 8;                     // steps per phase
-    const int nphase = (ns + sp - 1) / sp;
+    const float xsc = WT == T_Q4_0 ? 0.0625f : 1.0f;  // Q4_0 fragments hold 16 * (q - 8)
+    const int sp = KC / 8;                             // steps per phase
+    const int ntc = (ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+    const int tmc = nphase > 1 ? TM : 1;               // tiles per chunk at run time
+    auto tile_of = [&](int i) { return (int)blockIdx.x + i * (int)gridDim.x; };
     auto row0 = [&](int tile) {
         return SWI ? (mt < 2 ? 0 : F) + tile * 32 + (mt & 1) * 16 : tile * 16;
     };
-    const bool active = kw < ns;  // a warp with no step in a tile only adds zeros
-    // issue cursor over this warp's (tile, step) sequence: weights only
-    int it = blockIdx.x, is = kw, islot = 0;
-    auto advance = [&](int& t, int& s) {
-        s += KW;
-        if (s >= ns) {
-            s = kw;
-            t += gridDim.x;
+    auto s_end = [&](int ph) { return min(ns, (ph + 1) * sp); };
+    // move a cursor to the next (tile, step) of this warp; c >= ntc once the work is done
+    auto advance = [&](VCursor& u) {
+        u.s += KW;
+        while (u.c < ntc && u.s >= s_end(u.ph)) {
+            if (++u.tt >= min(tmc, ntc - u.c)) {
+                u.tt = 0;
+                if (++u.ph >= nphase) {
+                    u.ph = 0;
+                    u.c += tmc;
+                }
+            }
+            u.s = u.ph * sp + kw;
         }
     };
+    VCursor iu{0, 0, 0, kw - KW};
+    advance(iu);  // first step of this warp (none if kw >= ns)
+    int islot = 0;
 #pragma unroll
     for (int d = 0; d < D - 1; ++d) {
-        if (active && it < ntiles) issue_w<WT>(ring + d * S::kBytes, qs, rb, row0(it), N, nb, is, lane);
+        if (iu.c < ntc)
+            issue_w<WT>(ring + d * S::kBytes, qs, rb, row0(tile_of(iu.c + iu.tt)), N, nb, iu.s, lane);
         v_commit();
-        advance(it, is);
+        if (iu.c < ntc) advance(iu);
     }
     islot = D - 1;
     int cslot = 0;
     pdl_wait();
     pdl_launch();
-    if (nphase == 1) {  // one phase: staged once for every tile
-        stage_act<MAXM>(sx, sxs, a.xq, a.xd, M, K, nb, 0, KC);
-        __syncthreads();
-    }
+    // the first phase, then (several phases) the second one ahead of use
+    stage_act<MAXM>(sx_of(0), sxs_of(0), a.xq, a.xd, M, K, nb, 0, KC, xsc);
+    v_wait<0>();
+    __syncthreads();
+    int q = 0;  // phases started so far (over all chunks); phase q uses buffer q & 1
+    const int nq = nphase > 1 ? ((ntc + tmc - 1) / tmc) * nphase : 1;
 
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-        // acc[i] sums the steps s == kw + KW*i (mod 8): every output is built from the same eight
-        // partial sums P_r (steps s == r mod 8) in plain and SwiGLU mode
-        float2 acc[KS][NT][2];
+    for (int c = 0; c < ntc; c += tmc) {
+        const int nt_c = min(tmc, ntc - c);
+        float2 acc[TM][KS][NT][2];
 #pragma unroll
-        for (int i = 0; i < KS; ++i)
+        for (int u = 0; u < TM; ++u)
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) acc[i][nt][0] = acc[i][nt][1] = make_float2(0.0f, 0.0f);
-        for (int ph = 0; ph < nphase; ++ph) {
-            if (nphase > 1) {  // every warp is done with the previous phase's activations
-                __syncthreads();
-                stage_act<MAXM>(sx, sxs, a.xq, a.xd, M, K, nb, ph * KC, KC);
-                __syncthreads();
-            }
-            const int s_end = min(ns, (ph + 1) * sp);
-            int s = ph * sp + ((kw - ph * sp) % KW + KW) % KW;  // this warp's first step here
-            for (; active && s < s_end; s += KW) {
-                v_wait<D - 2>();
-                __syncwarp();
-                // refill the slot the previous step consumed
-                if (it < ntiles) {
-                    issue_w<WT>(ring + islot * S::kBytes, qs, rb, row0(it), N, nb, is, lane);
-                    advance(it, is);
+            for (int i = 0; i < KS; ++i)
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt)
+                    acc[u][i][nt][0] = acc[u][i][nt][1] = make_float2(0.0f, 0.0f);
+        for (int ph = 0; ph < nphase; ++ph, ++q) {
+            const int buf = nphase > 1 ? (q & 1) : 0;
+            int after = 0;  // commit groups of this thread since the next phase's stage
+            if (nphase > 1) {
+                if (q > 0) __syncthreads();  // phase q - 1 done: its buffer takes phase q + 1
+                if (q + 1 < nq) {
+                    const int nph = (ph + 1) % nphase;
+                    stage_act<MAXM>(sx_of(buf ^ 1), sxs_of(buf ^ 1), a.xq, a.xd, M, K, nb,
+                                    nph * KC, KC, xsc);
                 }
-                v_commit();
-                islot = islot + 1 == D ? 0 : islot + 1;
-                const int i = ((s - kw) / KW) % KS;
-                const int pb0 = 64 * (s >> 3) + (s & 7) * 4 - ph * KC;
-#pragma unroll
-                for (int j = 0; j < KS; ++j)
-                    if (j == i)
-                        consume<WT, MAXM>(ring + cslot * S::kBytes, sx, sxs, KC, pb0, M, lane, acc[j]);
-                cslot = cslot + 1 == D ? 0 : cslot + 1;
             }
-        }
-        // SwiGLU warps fold their four partials: ((P_kw + P_kw+2) + P_kw+4) + P_kw+6
+            const uint8_t* sX = sx_of(buf);
+            const float* sXs = sxs_of(buf);
+            for (int u = 0; u < nt_c; ++u) {
+                for (int s = ph * sp + kw; s < s_end(ph); s += KW) {
+                    v_wait<D - 2>();
+                    __syncwarp();
+                    // refill the slot the previous step consumed
+                    if (iu.c < ntc) {
+                        issue_w<WT>(ring + islot * S::kBytes, qs, rb, row0(tile_of(iu.c + iu.tt)),
+                                    N, nb, iu.s, lane);
+                        advance(iu);
+                    }
+                    v_commit();
+                    ++after;
+                    islot = islot + 1 == D ? 0 : islot + 1;
+                    const int i = ((s - kw) / KW) % KS;
+                    const int pb0 = 64 * (s >> 3) + (s & 7) * 4 - ph * KC;
 #pragma unroll
-        for (int i = 1; i < KS; ++i)
+                    for (int uu = 0; uu < TM; ++uu)
+#pragma unroll
+                        for (int j = 0; j < KS; ++j)
+                            if (uu == u && j == i)
+                                consume<WT, MAXM>(ring + cslot * S::kBytes, sX, sXs, pb0, lane,
+                                                  acc[uu][j]);
+                    cslot = cslot + 1 == D ? 0 : cslot + 1;
+                }
+            }
+            // the next phase's stage has landed once D - 1 groups followed it; else wait for it
+            if (nphase > 1 && after < D - 1) v_wait_dyn(after);
+        }
+#pragma unroll
+        for (int u = 0; u < TM; ++u) {
+            if (u >= nt_c) break;
+            const int tile = tile_of(c + u);
+            // SwiGLU warps fold their four partials: ((P_kw + P_kw+2) + P_kw+4) + P_kw+6
+#pragma unroll
+            for (int i = 1; i < KS; ++i)
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    acc[u][0][nt][0] = add2(acc[u][0][nt][0], acc[u][i][nt][0]);
+                    acc[u][0][nt][1] = add2(acc[u][0][nt][1], acc[u][i][nt][1]);
+                }
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-                acc[0][nt][0] = add2(acc[0][nt][0], acc[i][nt][0]);
-                acc[0][nt][1] = add2(acc[0][nt][1], acc[i][nt][1]);
+                float* r0 = red + (kw * MT * 16 + mt * 16 + g) * RC + nt * 8 + 2 * tg;
+                *(float2*)r0 = acc[u][0][nt][0];
+                *(float2*)(r0 + 8 * RC) = acc[u][0][nt][1];
             }
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            float* r0 = red + (kw * MT * 16 + mt * 16 + g) * RC + nt * 8 + 2 * tg;
-            *(float2*)r0 = acc[0][nt][0];
-            *(float2*)(r0 + 8 * RC) = acc[0][nt][1];
-        }
-        __syncthreads();
-        if (!SWI) {
-            for (int t = tid; t < 16 * M; t += kVT) {
-                const int r = t & 15, c = t >> 4;
-                auto P = [&](int w) { return red[(w * 16 + r) * RC + c]; };
-                // (((P0 + P2) + P4) + P6) + (((P1 + P3) + P5) + P7)
-                const float ev = __fadd_rn(__fadd_rn(__fadd_rn(P(0), P(2)), P(4)), P(6));
-                const float od = __fadd_rn(__fadd_rn(__fadd_rn(P(1), P(3)), P(5)), P(7));
-                float v = __fadd_rn(ev, od);
-                const int n = tile * 16 + r;
-                if (n < N) {
-                    if (a.bias) v = __fadd_rn(v, a.bias[n]);
-                    if (a.residual) v = __fadd_rn(a.residual[(int64_t)c * a.res_stride + n], v);
-                    a.y[(int64_t)c * a.y_stride + n] = v;
+            __syncthreads();
+            if (!SWI) {
+                for (int t = tid; t < 16 * M; t += kVT) {
+                    const int r = t & 15, cc = t >> 4;
+                    auto P = [&](int w) { return red[(w * 16 + r) * RC + cc]; };
+                    // (((P0 + P2) + P4) + P6) + (((P1 + P3) + P5) + P7)
+                    const float ev = __fadd_rn(__fadd_rn(__fadd_rn(P(0), P(2)), P(4)), P(6));
+                    const float od = __fadd_rn(__fadd_rn(__fadd_rn(P(1), P(3)), P(5)), P(7));
+                    float v = __fadd_rn(ev, od);
+                    const int n = tile * 16 + r;
+                    if (n < N) {
+                        if (a.bias) v = __fadd_rn(v, a.bias[n]);
+                        if (a.residual) v = __fadd_rn(a.residual[(int64_t)cc * a.res_stride + n], v);
+                        a.y[(int64_t)cc * a.y_stride + n] = v;
+                    }
+                }
+            } else {
+                // ggml_vec_swiglu_f32 (vec.cpp:417-426) on the tile's 32 pairs, f32 and/or Q8_0
+                for (int t = tid; t < 32 * M; t += kVT) {  // one warp per activation row
+                    const int p = t & 31, cc = t >> 5;
+                    const float gs = __fadd_rn(red[p * RC + cc], red[(64 + p) * RC + cc]);
+                    const float us = __fadd_rn(red[(32 + p) * RC + cc], red[(96 + p) * RC + cc]);
+                    const float h = __fmul_rn(ref_v_silu(gs), us);
+                    const int64_t col = (int64_t)tile * 32 + p;
+                    if (a.y) a.y[(int64_t)cc * a.y_stride + col] = h;
+                    if (a.yq) {
+                        float d16, qv;
+                        q8_block(h, p, d16, qv);
+                        a.yq[(int64_t)cc * a.F + col] = (int8_t)__float2int_rn(qv);
+                        if (p == 0) a.yd[(int64_t)cc * (a.F / 32) + tile] = d16;
+                    }
                 }
             }
-        } else {
-            // ggml_vec_swiglu_f32 (vec.cpp:417-426) on the tile's 32 pairs, f32 and/or Q8_0
-            for (int t = tid; t < 32 * M; t += kVT) {  // one warp per activation row
-                const int p = t & 31, c = t >> 5;
-                const float gs = __fadd_rn(red[p * RC + c], red[(64 + p) * RC + c]);
-                const float us = __fadd_rn(red[(32 + p) * RC + c], red[(96 + p) * RC + c]);
-                const float h = __fmul_rn(ref_v_silu(gs), us);
-                const int64_t col = (int64_t)tile * 32 + p;
-                if (a.y) a.y[(int64_t)c * a.y_stride + col] = h;
-                if (a.yq) {
-                    float d16, q;
-                    q8_block(h, p, d16, q);
-                    a.yq[(int64_t)c * a.F + col] = (int8_t)__float2int_rn(q);
-                    if (p == 0) a.yd[(int64_t)c * (a.F / 32) + tile] = d16;
-                }
-            }
+            __syncthreads();
         }
-        __syncthreads();
     }
     v_wait<0>();
 }
@@ -341,8 +430,12 @@ constexpr size_t v_fixed_smem() {  // rings and partial sums
 template <int WT, int MAXM, int SWI>
 void launch_v(const GemvArgs& a, cudaStream_t st) {
     auto kern = k_mmv<WT, MAXM, SWI>;
-    constexpr int kPhaseMax = phase_blocks_max<MAXM>();
-    constexpr size_t smem_max = (size_t)kPhaseMax * MAXM * 36 + v_fixed_smem<WT, MAXM>();
+    constexpr int SR = stage_rows<MAXM>();
+    // one phase when K fits the activation budget; else two buffers of whole 64-block groups
+    constexpr int kOne = 64 * (kActBytes / (SR * 64 * 36));
+    constexpr int kTwo = 64 * std::max(kActBytes / 2 / (SR * 64 * 36), 1);
+    static_assert(kOne >= 64, "mmv: one 64-block group must fit the activation budget");
+    constexpr size_t smem_max = (size_t)std::max(kOne, 2 * kTwo) * SR * 36 + v_fixed_smem<WT, MAXM>();
     static_assert(smem_max <= kVSmemMax, "mmv: stage and rings do not fit in shared memory");
     int dev = 0;
     GB_CUDA(cudaGetDevice(&dev));
@@ -351,12 +444,14 @@ void launch_v(const GemvArgs& a, cudaStream_t st) {
     const int ng = (nb + 63) / 64;
     const int rem = nb - 64 * (ng - 1);
     const int ns = 8 * (ng - 1) + (std::min(rem, 32) + 3) / 4;
-    const int KC = std::min(64 * ng, kPhaseMax);
-    const size_t smem = (size_t)KC * MAXM * 36 + v_fixed_smem<WT, MAXM>();
+    const bool one = 64 * ng <= kOne;
+    const int KC = one ? 64 * ng : kTwo;
+    const int nphase = one ? 1 : (64 * ng + KC - 1) / KC;
+    const size_t smem = (size_t)(one ? 1 : 2) * KC * SR * 36 + v_fixed_smem<WT, MAXM>();
     static std::mutex mu;
     static bool configured[64] = {};
-    static int per_sm[64][kPhaseMax / 64 + 1] = {};  // [device][KC / 64]: resident CTAs per SM
-    const int key = KC / 64;
+    static int per_sm[64][kOne / 64 + 2] = {};  // [device][stage size]: resident CTAs per SM
+    const int key = one ? KC / 64 : kOne / 64 + 1;
     {
         std::lock_guard<std::mutex> lock(mu);
         if (!configured[dev]) {
@@ -373,7 +468,7 @@ void launch_v(const GemvArgs& a, cudaStream_t st) {
     const int ntiles = SWI ? (int)(a.F / 32) : (int)((a.w.N + 15) / 16);
     if (ntiles == 0) return;
     const int grid = (int)std::min<int64_t>(ntiles, (int64_t)sm_count(dev) * per_sm[dev][key]);
-    launch_pdl(kern, (unsigned)grid, kVT, smem, st, a, ns, ntiles, KC);
+    launch_pdl(kern, (unsigned)grid, kVT, smem, st, a, ns, ntiles, KC, nphase);
 }
 
 template <int WT, int SWI>

@@ -246,16 +246,19 @@ def test_tensor_core_gemm_close_with_epilogue(G, wtype, M, N, K):
 
 
 @pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_0])
-@pytest.mark.parametrize("N,K", [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)])
+@pytest.mark.parametrize("N,K", [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096),
+                                 (10240, 14336)])
 def test_operator_sweep_shapes_sampled_rows(G, wtype, N, K):
-    """Operator-sweep shapes at full size; the oracle checks a sample of output rows (decode M=1
-    and prefill M=64 within 1e-5 of the output range)."""
+    """Operator-sweep shapes at full size; the oracle checks a sample of output rows (decode M=1,
+    batched decode M=8 and 16, prefill M=64, within 1e-5 of the output range).  K = 14336 runs
+    the batched decode kernel in several activation phases; 10240 rows give its CTAs more than
+    one chunk of tiles."""
     torch = G.torch_dev()
     rng = np.random.default_rng(N ^ K ^ wtype)
     w = G.random_blocks(rng, wtype, N, K, scale=0.02 / 127 * 3)
     wq, wd = G.upload_weight(wtype, w, N, K)
     rows = np.sort(rng.choice(N, size=48, replace=False))
-    for M in (1, 64):
+    for M in (1, 8, 16, 64):
         x = rng.standard_normal((M, K)).astype(np.float32)
         y = G.mul_mat(wtype, wq, wd, N, K, G.dev(x), M)
         ref = O.mul_mat(wtype, np.ascontiguousarray(w[rows]), len(rows), K, x)
