@@ -1388,7 +1388,7 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         da.ctx = ctx;
                         da.scale = scale;
                         da.max_kv = kv_max_ctx_;
-                        da.splits = attn_decode_splits(Hkv, kv_max_ctx_);
+                        da.splits = attn_decode_splits(Hkv, kv_max_ctx_, (int)s);
                         BufRef wref;
                         wref.buf = pg.new_buf((int64_t)attn_decode_workspace(Hq, hd, da.splits) * s, oi);
                         const BufRef yr = y.ref, yq = y.q, yqd = y.qd;

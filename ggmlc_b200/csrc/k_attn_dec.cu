@@ -17,6 +17,7 @@
 // attention accumulates in fp32 (the CPU rounds its V accumulator to fp16 per position).
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <mutex>
 #include <string>
 
@@ -259,6 +260,248 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(AttnDecArgs a) {
     }
 }
 
+// Split-KV decode attention on tensor cores (mma.sync m16n8k16, f16 inputs, f32 accumulation),
+// head_dim 64 or 128; one CTA per (split, KV head, row), 4 warps.  The q heads of the GQA group
+// are the rows of a 16-row A tile (rows >= the group size are zero).  Each warp walks its own
+// 16-position blocks of the split (blocks warp, warp + 4, ...) through a two-slot cp.async ring
+// and keeps its own online-softmax state, so warps never wait on one another inside the loop:
+//   scores  S[16 x 16] = Q[16 x HD] K^T   (K rows by ldmatrix, scaled, masked past the split)
+//   P = expf(S - m), the running max m and sum l per head, O rescaled by expf(m_old - m_new)
+//   O[16 x HD] += P V, with P entered as hi + lo fp16 halves (two products), so the f32 result
+//   keeps the probabilities' fp32 precision (V by ldmatrix.trans).
+// At the end the four warps' (m, l, O) are merged in shared memory in warp order and written as
+// the split's partial, in the layout k_attn_combine reads.  The new position's k and v rows are
+// written to the cache by the CTA that holds it and taken from shared memory, never re-read.
+constexpr int kTcWarps = 4;
+constexpr int kTcPos = 16;    // positions per block
+constexpr int kTcDepth = 2;   // ring slots per warp
+
+template <int HD>
+struct TcAttnSmem {
+    static constexpr int kRow = HD * 2 + 16;              // bytes per staged K / V / q row
+    static constexpr int kSlot = 2 * kTcPos * kRow;       // K block, then V block
+    static constexpr int kQ = 16 * kRow;
+    static constexpr int kNew = 2 * HD * 2;               // new k, new v (fp16)
+    static constexpr int kRing = kTcWarps * kTcDepth * kSlot;
+    static constexpr int kMerge = kTcWarps * kMaxRk * (HD + 2) * 4;
+    static constexpr int kBytes = kQ + kNew + (kRing > kMerge ? kRing : kMerge);
+};
+
+__device__ __forceinline__ void cp_async16z(void* dst, const void* src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                     (unsigned)__cvta_generic_to_shared(dst)),
+                 "l"(src), "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_ldsm4(unsigned (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"((unsigned)__cvta_generic_to_shared(p)));
+}
+__device__ __forceinline__ void tc_ldsm4t(unsigned (&r)[4], const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"((unsigned)__cvta_generic_to_shared(p)));
+}
+__device__ __forceinline__ void tc_mma(float (&d)[4], const unsigned (&a)[4], unsigned b0, unsigned b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+        "{%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ unsigned pack_h2(__half2 h) { return *(unsigned*)&h; }
+
+template <int HD>
+__global__ void __launch_bounds__(kTcWarps * 32) k_attn_decode_tc(AttnDecArgs a) {
+    using SM = TcAttnSmem<HD>;
+    constexpr int KS = HD / 16;   // k-steps of the score product = 16-dim groups of the output
+    constexpr int NTO = HD / 8;   // output n-tiles
+    constexpr int R = SM::kRow;
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint8_t* sq = smem;                                  // [16][R] rotated q, fp16
+    __half* snew = (__half*)(smem + SM::kQ);             // [2][HD]
+    uint8_t* ring_all = smem + SM::kQ + SM::kNew;
+    const int rk = a.Hq / a.Hkv;
+    const int hk = blockIdx.y;
+    const int row = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, tg = lane & 3;
+    uint8_t* ring = ring_all + warp * kTcDepth * SM::kSlot;
+    const int64_t pos = a.batched ? (int64_t)a.step->row_pos[row]
+                                  : (a.step ? a.step->pos : 0) + a.pos_off;
+    __half* kslot = a.kc + (a.batched ? (int64_t)a.step->row_slot[row] * a.slot_elems : 0);
+    __half* vslot = a.vc + (a.batched ? (int64_t)a.step->row_slot[row] * a.slot_elems : 0);
+    const int64_t nkv = pos + 1;
+    const int64_t per = (nkv + gridDim.x - 1) / gridDim.x;
+    const int64_t c0 = min((int64_t)blockIdx.x * per, nkv);
+    const int64_t c1 = min(c0 + per, nkv);
+    const __half* kbase = kslot + ((int64_t)hk * a.ctx) * HD;
+    const __half* vbase = vslot + ((int64_t)hk * a.ctx) * HD;
+    const int nblk = (int)((c1 - c0 + kTcPos - 1) / kTcPos);
+    // block b of the split into a ring slot: rows past the split and the new position read as 0
+    auto stage = [&](int slot, int b) {
+        uint8_t* dk = ring + slot * SM::kSlot;
+        uint8_t* dv = dk + kTcPos * R;
+        const int64_t ps = c0 + (int64_t)b * kTcPos;
+        for (int e = lane; e < kTcPos * (HD / 8); e += 32) {
+            const int r = e / (HD / 8), pc = e % (HD / 8);
+            const bool ok = ps + r < c1 && ps + r != pos;
+            const int64_t off = ok ? (ps + r) * HD + pc * 8 : 0;
+            cp_async16z(dk + r * R + pc * 16, kbase + off, ok);
+            cp_async16z(dv + r * R + pc * 16, vbase + off, ok);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    // cached rows were written by earlier steps: the first block is requested before the wait
+    if (warp < nblk) stage(0, warp);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
+    pdl_wait();
+    pdl_launch();
+
+    const float* qrow = a.qkv + (int64_t)row * a.qkv_stride;
+    for (int e = threadIdx.x; e < 16 * HD; e += kTcWarps * 32) {
+        const int h = e / HD, d = e % HD;
+        float v = 0.0f;
+        if (h < rk) v = rope_elem(qrow + a.q_off + (int64_t)(hk * rk + h) * HD, d, HD, a.tab, pos);
+        *(__half*)(sq + h * R + d * 2) = __float2half_rn(v);
+    }
+    const bool has_new = c0 <= pos && pos < c1;
+    if (has_new) {
+        const float* ks = qrow + a.k_off + (int64_t)hk * HD;
+        for (int d = threadIdx.x; d < HD; d += kTcWarps * 32) {
+            const __half kh = __float2half_rn(rope_elem(ks, d, HD, a.tab, pos));
+            const __half vh = __float2half_rn(qrow[a.v_off + (int64_t)hk * HD + d]);
+            kslot[((int64_t)hk * a.ctx + pos) * HD + d] = kh;
+            vslot[((int64_t)hk * a.ctx + pos) * HD + d] = vh;
+            snew[d] = kh;
+            snew[HD + d] = vh;
+        }
+    }
+    __syncthreads();  // sq and snew ready
+    unsigned qf[KS][4];
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks)
+        tc_ldsm4(qf[ks], sq + ((lane & 7) + ((lane >> 3) & 1) * 8) * R + (ks * 16 + (lane >> 4) * 8) * 2);
+    float o[NTO][4];
+#pragma unroll
+    for (int n = 0; n < NTO; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+    float m_r = -INFINITY, l_r = 0.0f;  // row g: running max, this thread's share of the sum
+    int j = 0;                           // blocks of this warp done
+    for (int b = warp; b < nblk; b += kTcWarps, ++j) {
+        __syncwarp();  // every lane is done with the slot the next block goes to
+        const int bn = b + kTcWarps;
+        if (bn < nblk) stage((j + 1) & 1, bn);
+        else asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+        __syncwarp();
+        uint8_t* ck = ring + (j & 1) * SM::kSlot;
+        uint8_t* cv = ck + kTcPos * R;
+        const int64_t ps = c0 + (int64_t)b * kTcPos;
+        if (has_new && ps <= pos && pos < ps + kTcPos) {
+            const int r = (int)(pos - ps);
+            for (int d = lane; d < HD; d += 32) {
+                *(__half*)(ck + r * R + d * 2) = snew[d];
+                *(__half*)(cv + r * R + d * 2) = snew[HD + d];
+            }
+            __syncwarp();
+        }
+        float s[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+            unsigned kb[4];  // (pos 0-7, dims lo), (pos 0-7, dims hi), (pos 8-15, lo), (8-15, hi)
+            tc_ldsm4(kb, ck + ((lane & 7) + (lane >> 4) * 8) * R + (ks * 16 + ((lane >> 3) & 1) * 8) * 2);
+            tc_mma(s[0], qf[ks], kb[0], kb[1]);
+            tc_mma(s[1], qf[ks], kb[2], kb[3]);
+        }
+        float v[4];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+                const int64_t p = ps + nt * 8 + 2 * tg + e;
+                v[nt * 2 + e] = p < c1 ? __fmul_rn(s[nt][e], a.scale) : -INFINITY;
+            }
+        float mx = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float m_new = fmaxf(m_r, mx);  // finite: every block holds a position of the split
+        const float corr = expf(m_r - m_new);
+        float p[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) p[e] = expf(v[e] - m_new);
+        l_r = __fadd_rn(__fmul_rn(l_r, corr), __fadd_rn(__fadd_rn(p[0], p[1]), __fadd_rn(p[2], p[3])));
+        m_r = m_new;
+#pragma unroll
+        for (int n = 0; n < NTO; ++n) {
+            o[n][0] = __fmul_rn(o[n][0], corr);
+            o[n][1] = __fmul_rn(o[n][1], corr);
+        }
+        const __half2 h0 = __floats2half2_rn(p[0], p[1]), h1 = __floats2half2_rn(p[2], p[3]);
+        const float2 f0 = __half22float2(h0), f1 = __half22float2(h1);
+        const __half2 r0 = __floats2half2_rn(p[0] - f0.x, p[1] - f0.y);
+        const __half2 r1 = __floats2half2_rn(p[2] - f1.x, p[3] - f1.y);
+        const unsigned ahi[4] = {pack_h2(h0), 0u, pack_h2(h1), 0u};
+        const unsigned alo[4] = {pack_h2(r0), 0u, pack_h2(r1), 0u};
+#pragma unroll
+        for (int dg = 0; dg < KS; ++dg) {
+            unsigned vb[4];  // (pos 0-7, dims 16dg..), (pos 8-15, same), (0-7, +8..), (8-15, +8..)
+            tc_ldsm4t(vb, cv + ((lane & 7) + ((lane >> 3) & 1) * 8) * R + (dg * 16 + (lane >> 4) * 8) * 2);
+            tc_mma(o[2 * dg], ahi, vb[0], vb[1]);
+            tc_mma(o[2 * dg], alo, vb[0], vb[1]);
+            tc_mma(o[2 * dg + 1], ahi, vb[2], vb[3]);
+            tc_mma(o[2 * dg + 1], alo, vb[2], vb[3]);
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    l_r = __fadd_rn(l_r, __shfl_xor_sync(0xffffffffu, l_r, 1));
+    l_r = __fadd_rn(l_r, __shfl_xor_sync(0xffffffffu, l_r, 2));
+    __syncthreads();  // every warp is done with its ring: the area holds the merge
+    float* mo = (float*)ring_all;                        // [warp][kMaxRk][HD]
+    float* mm = mo + kTcWarps * kMaxRk * HD;              // [warp][kMaxRk] max
+    float* ml = mm + kTcWarps * kMaxRk;                   // [warp][kMaxRk] sum
+    if (g < rk) {
+#pragma unroll
+        for (int n = 0; n < NTO; ++n)
+            *(float2*)(mo + (warp * kMaxRk + g) * HD + n * 8 + 2 * tg) = make_float2(o[n][0], o[n][1]);
+        if (tg == 0) {
+            mm[warp * kMaxRk + g] = m_r;
+            ml[warp * kMaxRk + g] = l_r;
+        }
+    }
+    __syncthreads();
+    float* part = a.part + (int64_t)row * gridDim.x * a.Hq * (HD + 4) +
+                  ((int64_t)blockIdx.x * a.Hq + (int64_t)hk * rk) * (HD + 4);
+    for (int e = threadIdx.x; e < rk * HD; e += kTcWarps * 32) {
+        const int h = e / HD, d = e % HD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kTcWarps; ++w) M = fmaxf(M, mm[w * kMaxRk + h]);
+        float acc = 0.0f;
+        if (M != -INFINITY) {
+#pragma unroll
+            for (int w = 0; w < kTcWarps; ++w) {
+                const float mw = mm[w * kMaxRk + h];
+                if (mw != -INFINITY)
+                    acc = __fmaf_rn(mo[(w * kMaxRk + h) * HD + d], expf(mw - M), acc);
+            }
+        }
+        part[h * (HD + 4) + 4 + d] = acc;
+        if (d == 0) {
+            float L = 0.0f;
+            if (M != -INFINITY) {
+#pragma unroll
+                for (int w = 0; w < kTcWarps; ++w) {
+                    const float mw = mm[w * kMaxRk + h];
+                    if (mw != -INFINITY) L = __fmaf_rn(ml[w * kMaxRk + h], expf(mw - M), L);
+                }
+            }
+            part[h * (HD + 4) + 0] = M;
+            part[h * (HD + 4) + 1] = L;
+        }
+    }
+}
+
 // Merge the splits of each q head; one CTA per q head, one thread per dim.  Every load is issued
 // before the first dependent step: thread d reads its value of each split, warp 0 the (m, l)
 // pairs.
@@ -333,8 +576,24 @@ void launch_dec(const AttnDecArgs& a, cudaStream_t st) {
             configured[dev & 63] = true;
         }
     }
-    launch_pdl(k_attn_decode<HD>, dim3((unsigned)a.splits, (unsigned)a.Hkv, (unsigned)a.rows),
-               kDecThreads, smem, st, a);
+    if (HD <= 128) {  // tensor-core kernel
+        constexpr size_t tsm = TcAttnSmem<HD <= 128 ? HD : 128>::kBytes;
+        static bool tc_configured[64] = {};
+        {
+            std::lock_guard<std::mutex> lock(mu);
+            if (!tc_configured[dev & 63]) {
+                GB_CUDA(cudaFuncSetAttribute(k_attn_decode_tc<HD <= 128 ? HD : 128>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm));
+                tc_configured[dev & 63] = true;
+            }
+        }
+        launch_pdl(k_attn_decode_tc<HD <= 128 ? HD : 128>,
+                   dim3((unsigned)a.splits, (unsigned)a.Hkv, (unsigned)a.rows), kTcWarps * 32, tsm,
+                   st, a);
+    } else {
+        launch_pdl(k_attn_decode<HD>, dim3((unsigned)a.splits, (unsigned)a.Hkv, (unsigned)a.rows),
+                   kDecThreads, smem, st, a);
+    }
     launch_pdl(k_attn_combine<HD>, dim3((unsigned)a.Hq, (unsigned)a.rows), HD, 0, st, a);
 }
 
@@ -350,9 +609,10 @@ void launch_rope_qkv(const QkvRopeArgs& a, cudaStream_t st) {
     GB_CUDA(cudaGetLastError());
 }
 
-int attn_decode_splits(int64_t Hkv, int64_t max_kv) {
-    // about two CTAs per SM; each split then walks max_kv / splits positions
-    int64_t s = (296 + Hkv - 1) / Hkv;
+int attn_decode_splits(int64_t Hkv, int64_t max_kv, int rows) {
+    // about two CTAs per SM over the launch; each split then walks max_kv / splits positions
+    const int64_t units = Hkv * std::max(rows, 1);
+    int64_t s = (296 + units - 1) / units;
     if (s > max_kv) s = max_kv;
     if (s > kMaxSplits) s = kMaxSplits;
     return (int)(s < 1 ? 1 : s);

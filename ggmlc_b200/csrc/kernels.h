@@ -245,7 +245,8 @@ struct AttnDecArgs {
     int64_t qkv_stride = 0;
     int64_t slot_elems = 0;
 };
-int attn_decode_splits(int64_t Hkv, int64_t max_kv);
+// splits per (row, KV head): about two CTAs per SM over all rows and heads of the launch
+int attn_decode_splits(int64_t Hkv, int64_t max_kv, int rows = 1);
 size_t attn_decode_workspace(int64_t Hq, int64_t hd, int splits);  // per row
 void launch_attn_decode(const AttnDecArgs& a, cudaStream_t st);
 // Size of the per-device static split scratch behind gb_attn_decode_noalloc.
