@@ -40,8 +40,10 @@ namespace gb {
 
 namespace {
 
-constexpr int kVW = 8;            // warps per CTA
+constexpr int kVW = 16;           // warps per CTA: two teams of kTW
+constexpr int kTW = 8;            // warps per team (one tile at a time)
 constexpr int kVT = kVW * 32;     // threads per CTA
+constexpr int kTT = kTW * 32;     // threads per team
 constexpr int kVSB = 8;           // blocks per step
 constexpr size_t kVSmemMax = 227 * 1024;
 constexpr int kActBytes = 72 * 1024;  // shared-memory budget of one activation phase
@@ -52,15 +54,20 @@ struct WSlot {  // one ring slot: the weights of one step of one 16-row tile
     static constexpr int kW = kVSB * kQ * 16 * 16;     // [block][chunk][row 16][16 B]
     static constexpr int kWs = 16 * 16;                // [row 16][4 words of 2 fp16 scales]
     static constexpr int kBytes = kW + kWs;
-    static constexpr int kDepth = WT == T_Q8_0 ? 4 : 6;  // ring slots per warp
+    static constexpr int kDepth = WT == T_Q8_0 ? 2 : 3;  // ring slots per warp
 };
 __device__ __forceinline__ unsigned v_saddr(const void* p) {
     return (unsigned)__cvta_generic_to_shared(p);
 }
-// cp.async of 16 bytes; zero fill when !valid (the source address stays in bounds)
+// cp.async of 16 (or 4) bytes; zero fill when !valid (the source address stays in bounds)
 __device__ __forceinline__ void v_cp16(void* dst, const void* src, bool valid) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(v_saddr(dst)), "l"(src),
                  "r"(valid ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void v_cp4(void* dst, const void* src, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(v_saddr(dst)), "l"(src),
+                 "r"(valid ? 4 : 0)
                  : "memory");
 }
 __device__ __forceinline__ void v_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
@@ -115,14 +122,13 @@ __device__ __forceinline__ void issue_w(uint8_t* slot, const uint8_t* qs, int64_
 template <int MAXM>
 constexpr int stage_rows() { return MAXM < 8 ? 8 : MAXM; }
 
-// Stage the Q8_0 activations of blocks [pbase, pbase + KC), rows 0..M-1, by the whole CTA:
-// sx [block][half][row SR][16 B] by cp.async (one commit group per thread; blocks past nb are zero
-// filled, rows M..SR-1 are left as they are), sxs [block][row SR] fp32 scales times xsc (0 for
-// rows >= M and blocks past nb, so whatever sits in those rows of sx contributes exact zeros).
+// Stage the Q8_0 activations of blocks [pbase, pbase + KC), rows 0..M-1, by the whole CTA, all by
+// cp.async in one commit group per thread: sx [block][half][row SR][16 B] and sxs [block][row SR]
+// fp32 scales.  Blocks past nb and scale rows M..SR-1 are zero filled; quant rows M..SR-1 are
+// left as they are (their scales are zero, so they contribute exact zeros).
 template <int MAXM>
 __device__ __forceinline__ void stage_act(uint8_t* sx, float* sxs, const int8_t* xq,
-                                          const float* xd, int M, int K, int nb, int pbase, int KC,
-                                          float xsc) {
+                                          const float* xd, int M, int K, int nb, int pbase, int KC) {
     constexpr int SR = stage_rows<MAXM>();
     for (int e = threadIdx.x; e < KC * 2 * SR; e += kVT) {
         const int m = e % SR, hb = e / SR, half = hb & 1, pb = hb >> 1;
@@ -132,22 +138,12 @@ __device__ __forceinline__ void stage_act(uint8_t* sx, float* sxs, const int8_t*
                    xq + (int64_t)m * K + (int64_t)min(blk, nb - 1) * 32 + half * 16, blk < nb);
         }
     }
-    v_commit();
-    // scales: up to 8 independent loads in flight per thread before the stores
-    for (int e0 = threadIdx.x; e0 < KC * SR; e0 += 8 * kVT) {
-        float v[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int e = e0 + j * kVT;
-            const int m = e % SR, blk = pbase + e / SR;
-            v[j] = (e < KC * SR && m < M && blk < nb) ? __ldcg(xd + (int64_t)m * nb + blk) : 0.0f;
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int e = e0 + j * kVT;
-            if (e < KC * SR) sxs[e] = __fmul_rn(v[j], xsc);
-        }
+    for (int e = threadIdx.x; e < KC * SR; e += kVT) {
+        const int m = e % SR, blk = pbase + e / SR;
+        const bool ok = m < M && blk < nb;
+        v_cp4(sxs + e, xd + (ok ? (int64_t)m * nb + blk : 0), ok);
     }
+    v_commit();
 }
 
 // wait until at most n of this thread's newest commit groups are pending (0 <= n <= 5)
@@ -224,7 +220,8 @@ __device__ __forceinline__ void consume(const uint8_t* slot, const uint8_t* sX, 
         for (int nt = 0; nt < NT; ++nt) {
             int d[4];
             v_mma(d, af, bq[2 * nt], bq[2 * nt + 1]);
-            const float2 dx = *(const float2*)(sXs + pb * SR + nt * 8 + 2 * tg);
+            float2 dx = *(const float2*)(sXs + pb * SR + nt * 8 + 2 * tg);
+            if (WT == T_Q4_0) dx = mul2(dx, make_float2(0.0625f, 0.0625f));  // 16 * (q - 8)
             const float2 p0 = mul2(make_float2(dw0, dw0), dx);
             const float2 p1 = mul2(make_float2(dw1, dw1), dx);
             const float2 v0 = sub2(make_float2(__int_as_float(d[0]), __int_as_float(d[1])), bias2);
@@ -235,13 +232,14 @@ __device__ __forceinline__ void consume(const uint8_t* slot, const uint8_t* sX, 
     }
 }
 
-// Work order of a CTA: its tiles (blockIdx.x + i * gridDim.x) in chunks of TM; per chunk, the
-// activation phases; per phase, each tile of the chunk; per tile, this warp's steps of the phase
-// (s = ph * sp + kw + KW * j).  Accumulators of the whole chunk stay in registers across phases,
-// so each tile still sums its steps in ascending order.  The weight issue cursor walks the same
-// order D - 1 steps ahead.
+// Work order.  A CTA's tiles are blockIdx.x + i * gridDim.x; its two teams of 8 warps take the
+// even and the odd i, so two tiles run at once over one activation stage.  Per team: its tiles in
+// chunks of TM; per chunk, the activation phases (shared by the CTA); per phase, each tile of the
+// chunk; per tile, this warp's steps of the phase (s = ph * sp + kw + KW * j).  Accumulators of
+// the whole chunk stay in registers across phases, so each tile still sums its steps in
+// ascending order.  The weight issue cursor walks the same order D - 1 steps ahead.
 struct VCursor {
-    int c, ph, tt, s;  // chunk (first tile index of this CTA's list), phase, tile in chunk, step
+    int c, ph, tt, s;  // chunk (first team-local tile index), phase, tile in chunk, step
 };
 
 template <int WT, int MAXM, int SWI>
@@ -257,33 +255,35 @@ __global__ void __launch_bounds__(kVT, 1) k_mmv(GemvArgs a, int ns, int ntiles, 
     constexpr int TM = SWI ? 1 : 4;   // tiles per chunk
     extern __shared__ __align__(16) uint8_t smem[];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int team = warp / kTW, wt = warp % kTW, ttid = tid % kTT;
     const int g = lane >> 2, tg = lane & 3;
-    const int kw = SWI ? warp >> 2 : warp;
-    const int mt = SWI ? warp & 3 : 0;
+    const int kw = SWI ? wt >> 2 : wt;
+    const int mt = SWI ? wt & 3 : 0;
     const int nbuf = nphase > 1 ? 2 : 1;
     const size_t stage_bytes = (size_t)KC * SR * 36;
     uint8_t* ring = smem + nbuf * stage_bytes + warp * D * S::kBytes;
-    float* red = (float*)(smem + nbuf * stage_bytes + kVW * D * S::kBytes);
+    float* red = (float*)(smem + nbuf * stage_bytes + kVW * D * S::kBytes) + team * 1024 * NT;
     auto sx_of = [&](int b) { return smem + b * stage_bytes; };
     auto sxs_of = [&](int b) { return (float*)(smem + b * stage_bytes + (size_t)KC * 2 * SR * 16); };
     const int N = (int)a.w.N, K = (int)a.w.K, nb = K / QK, M = a.M;
     const int F = (int)a.F;
     const int64_t rb = qrow_bytes(WT, K);
     const uint8_t* qs = (const uint8_t*)a.w.qs;
-    const float xsc = WT == T_Q4_0 ? 0.0625f : 1.0f;  // Q4_0 fragments hold 16 * (q - 8)
     const int sp = KC / 8;                             // steps per phase
     const int ntc = (ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+    const int ntt0 = (ntc + 1) / 2;                    // tiles of team 0 (team 1 has ntc / 2)
+    const int ntt = team == 0 ? ntt0 : ntc / 2;
     const int tmc = nphase > 1 ? TM : 1;               // tiles per chunk at run time
-    auto tile_of = [&](int i) { return (int)blockIdx.x + i * (int)gridDim.x; };
+    auto tile_of = [&](int j) { return (int)blockIdx.x + (2 * j + team) * (int)gridDim.x; };
     auto row0 = [&](int tile) {
         return SWI ? (mt < 2 ? 0 : F) + tile * 32 + (mt & 1) * 16 : tile * 16;
     };
     auto s_end = [&](int ph) { return min(ns, (ph + 1) * sp); };
-    // move a cursor to the next (tile, step) of this warp; c >= ntc once the work is done
+    // move a cursor to the next (tile, step) of this warp; c >= ntt once the work is done
     auto advance = [&](VCursor& u) {
         u.s += KW;
-        while (u.c < ntc && u.s >= s_end(u.ph)) {
-            if (++u.tt >= min(tmc, ntc - u.c)) {
+        while (u.c < ntt && u.s >= s_end(u.ph)) {
+            if (++u.tt >= min(tmc, ntt - u.c)) {
                 u.tt = 0;
                 if (++u.ph >= nphase) {
                     u.ph = 0;
@@ -294,28 +294,31 @@ __global__ void __launch_bounds__(kVT, 1) k_mmv(GemvArgs a, int ns, int ntiles, 
         }
     };
     VCursor iu{0, 0, 0, kw - KW};
-    advance(iu);  // first step of this warp (none if kw >= ns)
+    advance(iu);  // first step of this warp (none if kw >= ns or the team has no tile)
     int islot = 0;
 #pragma unroll
     for (int d = 0; d < D - 1; ++d) {
-        if (iu.c < ntc)
+        if (iu.c < ntt)
             issue_w<WT>(ring + d * S::kBytes, qs, rb, row0(tile_of(iu.c + iu.tt)), N, nb, iu.s, lane);
         v_commit();
-        if (iu.c < ntc) advance(iu);
+        if (iu.c < ntt) advance(iu);
     }
     islot = D - 1;
     int cslot = 0;
     pdl_wait();
     pdl_launch();
-    // the first phase, then (several phases) the second one ahead of use
-    stage_act<MAXM>(sx_of(0), sxs_of(0), a.xq, a.xd, M, K, nb, 0, KC, xsc);
+    // the first phase, then (several phases) the next one ahead of use
+    stage_act<MAXM>(sx_of(0), sxs_of(0), a.xq, a.xd, M, K, nb, 0, KC);
     v_wait<0>();
     __syncthreads();
     int q = 0;  // phases started so far (over all chunks); phase q uses buffer q & 1
-    const int nq = nphase > 1 ? ((ntc + tmc - 1) / tmc) * nphase : 1;
+    const int nq = nphase > 1 ? ((ntt0 + tmc - 1) / tmc) * nphase : 1;
 
-    for (int c = 0; c < ntc; c += tmc) {
-        const int nt_c = min(tmc, ntc - c);
+    // chunks follow team 0 (it has at least as many tiles as team 1); both teams meet at every
+    // phase boundary and tile epilogue
+    for (int c = 0; c < ntt0; c += tmc) {
+        const int nt_c = max(0, min(tmc, ntt - c));    // this team's tiles in the chunk
+        const int nt_max = min(tmc, ntt0 - c);
         float2 acc[TM][KS][NT][2];
 #pragma unroll
         for (int u = 0; u < TM; ++u)
@@ -332,7 +335,7 @@ __global__ void __launch_bounds__(kVT, 1) k_mmv(GemvArgs a, int ns, int ntiles, 
                 if (q + 1 < nq) {
                     const int nph = (ph + 1) % nphase;
                     stage_act<MAXM>(sx_of(buf ^ 1), sxs_of(buf ^ 1), a.xq, a.xd, M, K, nb,
-                                    nph * KC, KC, xsc);
+                                    nph * KC, KC);
                 }
             }
             const uint8_t* sX = sx_of(buf);
@@ -342,7 +345,7 @@ __global__ void __launch_bounds__(kVT, 1) k_mmv(GemvArgs a, int ns, int ntiles, 
                     v_wait<D - 2>();
                     __syncwarp();
                     // refill the slot the previous step consumed
-                    if (iu.c < ntc) {
+                    if (iu.c < ntt) {
                         issue_w<WT>(ring + islot * S::kBytes, qs, rb, row0(tile_of(iu.c + iu.tt)),
                                     N, nb, iu.s, lane);
                         advance(iu);
@@ -367,8 +370,9 @@ __global__ void __launch_bounds__(kVT, 1) k_mmv(GemvArgs a, int ns, int ntiles, 
         }
 #pragma unroll
         for (int u = 0; u < TM; ++u) {
-            if (u >= nt_c) break;
-            const int tile = tile_of(c + u);
+            if (u >= nt_max) break;
+            const bool mine = u < nt_c;  // this team has a tile at this position
+            const int tile = mine ? tile_of(c + u) : 0;
             // SwiGLU warps fold their four partials: ((P_kw + P_kw+2) + P_kw+4) + P_kw+6
 #pragma unroll
             for (int i = 1; i < KS; ++i)
@@ -377,15 +381,17 @@ __global__ void __launch_bounds__(kVT, 1) k_mmv(GemvArgs a, int ns, int ntiles, 
                     acc[u][0][nt][0] = add2(acc[u][0][nt][0], acc[u][i][nt][0]);
                     acc[u][0][nt][1] = add2(acc[u][0][nt][1], acc[u][i][nt][1]);
                 }
+            if (mine) {
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) {
-                float* r0 = red + (kw * MT * 16 + mt * 16 + g) * RC + nt * 8 + 2 * tg;
-                *(float2*)r0 = acc[u][0][nt][0];
-                *(float2*)(r0 + 8 * RC) = acc[u][0][nt][1];
+                for (int nt = 0; nt < NT; ++nt) {
+                    float* r0 = red + (kw * MT * 16 + mt * 16 + g) * RC + nt * 8 + 2 * tg;
+                    *(float2*)r0 = acc[u][0][nt][0];
+                    *(float2*)(r0 + 8 * RC) = acc[u][0][nt][1];
+                }
             }
             __syncthreads();
-            if (!SWI) {
-                for (int t = tid; t < 16 * M; t += kVT) {
+            if (mine && !SWI) {
+                for (int t = ttid; t < 16 * M; t += kTT) {
                     const int r = t & 15, cc = t >> 4;
                     auto P = [&](int w) { return red[(w * 16 + r) * RC + cc]; };
                     // (((P0 + P2) + P4) + P6) + (((P1 + P3) + P5) + P7)
@@ -399,9 +405,9 @@ __global__ void __launch_bounds__(kVT, 1) k_mmv(GemvArgs a, int ns, int ntiles, 
                         a.y[(int64_t)cc * a.y_stride + n] = v;
                     }
                 }
-            } else {
+            } else if (mine) {
                 // ggml_vec_swiglu_f32 (vec.cpp:417-426) on the tile's 32 pairs, f32 and/or Q8_0
-                for (int t = tid; t < 32 * M; t += kVT) {  // one warp per activation row
+                for (int t = ttid; t < 32 * M; t += kTT) {  // one warp per activation row
                     const int p = t & 31, cc = t >> 5;
                     const float gs = __fadd_rn(red[p * RC + cc], red[(64 + p) * RC + cc]);
                     const float us = __fadd_rn(red[(32 + p) * RC + cc], red[(96 + p) * RC + cc]);
@@ -423,8 +429,9 @@ __global__ void __launch_bounds__(kVT, 1) k_mmv(GemvArgs a, int ns, int ntiles, 
 }
 
 template <int WT, int MAXM>
-constexpr size_t v_fixed_smem() {  // rings and partial sums
-    return (size_t)kVW * WSlot<WT>::kDepth * WSlot<WT>::kBytes + (size_t)1024 * ((MAXM + 7) / 8) * 4;
+constexpr size_t v_fixed_smem() {  // rings and the two teams' partial sums
+    return (size_t)kVW * WSlot<WT>::kDepth * WSlot<WT>::kBytes +
+           (size_t)2 * 1024 * ((MAXM + 7) / 8) * 4;
 }
 
 template <int WT, int MAXM, int SWI>
