@@ -457,6 +457,8 @@ CASES = {
     "attn_decode": dict(Hq=32, Hkv=8, hd=128, ctx=1024, pos=640),
     "gemm_prefill": dict(N=28672, K=4096, M=512, mode="gemm"),    # gate_up at pp512
     "gemm_prefill_tc": dict(N=28672, K=4096, M=512, mode="gemm_tc"),  # the same on tcgen05
+    "mmv_swiglu_b16": dict(N=28672, K=4096, M=16, mode="rows_swiglu"),  # gate_up, 16 sequences
+    "mmv_res_b16": dict(N=4096, K=14336, M=16, mode="rows_res"),        # down, 16 sequences
 }
 
 
@@ -479,7 +481,7 @@ def run_case(name: str, reps: int) -> None:
         if rc != 0:
             raise RuntimeError(L.gb_last_error().decode())
 
-    if name.startswith("gemv") or name.startswith("gemm"):
+    if name.startswith(("gemv", "gemm", "mmv")):
         N, K = c["N"], c["K"]
         nb = K // 32
         blocks = rng.integers(0, 256, size=(N, nb, 18), dtype=np.uint8)
@@ -502,13 +504,16 @@ def run_case(name: str, reps: int) -> None:
         yd = torch.empty(N // 64, dtype=torch.float32, device=dev)
         L.gb_gemv.argtypes = [I, P, I64, I64, I64, P, P, P, F, P, I, P, P, P, P, P, P]
         mode = c["mode"]
-        if mode in ("gemm", "gemm_tc"):
+        if mode in ("gemm", "gemm_tc", "rows_swiglu", "rows_res"):
             M = c["M"]
             xm = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).to(dev)
             xq = torch.empty((M, K), dtype=torch.int8, device=dev)
             xd = torch.empty((M, K // 32), dtype=torch.float32, device=dev)
             check(L.gb_quantize_q8_0(ptr(xm), K, M, K, ptr(xq), ptr(xd), None))
             ym = torch.empty((M, N), dtype=torch.float32, device=dev)
+            resm = torch.zeros((M, N), dtype=torch.float32, device=dev)
+            yqm = torch.empty((M, N // 2), dtype=torch.int8, device=dev)
+            ydm = torch.empty((M, N // 64), dtype=torch.float32, device=dev)
             L.gb_mul_mat_q.argtypes = [I, P, I64, I64, P, P, I64, P, P, P, P]
             L.gb_gemm_tc.argtypes = [I, P, I64, I64, P, P, I64, P, P, P, P]
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -516,6 +521,12 @@ def run_case(name: str, reps: int) -> None:
         for _ in range(reps):
             if mode == "gemm_tc":
                 rc = L.gb_gemm_tc(2, ptr(wq), N, K, ptr(xq), ptr(xd), M, ptr(ym), None, None, None)
+            elif mode == "rows_swiglu":
+                rc = L.gb_gemv(2, ptr(wq), N, K, M, ptr(xq), ptr(xd), None, 0.0, None, 1, None,
+                               ptr(yqm), ptr(ydm), None, None, None)
+            elif mode == "rows_res":
+                rc = L.gb_gemv(2, ptr(wq), N, K, M, ptr(xq), ptr(xd), None, 0.0, None, 0, ptr(ym),
+                               None, None, None, ptr(resm), None)
             elif mode == "gemm":
                 rc = L.gb_mul_mat_q(2, ptr(wq), N, K, ptr(xq), ptr(xd), M, ptr(ym), None, None,
                                     None)
@@ -555,7 +566,7 @@ def run_case(name: str, reps: int) -> None:
                                    ptr(work), None))
     torch.cuda.synchronize()
     extra = {}
-    if name.startswith("gemv") or name.startswith("gemm"):
+    if name.startswith(("gemv", "gemm", "mmv")):
         extra["us_per_launch"] = round(e0.elapsed_time(e1) * 1e3 / reps, 2)  # includes the first
     print(json.dumps({"case": name, "launches": reps, **c, **extra}))
 
