@@ -452,13 +452,15 @@ def test_gemv_swiglu_epilogue(G, wtype, M):
     assert _close(h, O.swiglu(O.mul_mat(wtype, w, N, K, x)), 1e-4)
 
 
-@pytest.mark.parametrize("Hq,Hkv,hd,kv_pos", [(4, 2, 64, 0), (9, 3, 64, 300), (32, 8, 128, 700)])
-def test_attn_decode_fused(G, Hq, Hkv, hd, kv_pos):
+@pytest.mark.parametrize("Hq,Hkv,hd,kv_pos,ctx", [(4, 2, 64, 0, 1024), (9, 3, 64, 300, 1024),
+                                                  (32, 8, 128, 700, 1024), (9, 3, 64, 1200, 2048),
+                                                  (32, 8, 128, 1500, 2048)])
+def test_attn_decode_fused(G, Hq, Hkv, hd, kv_pos, ctx):
     """Decode attention fused with RoPE and the KV write: cache row kv_pos holds fp16(rope(k)) and
-    fp16(v) bit-exactly, the output matches exact fp64 attention over the rotated q."""
+    fp16(v) bit-exactly, the output matches exact fp64 attention over the rotated q, for caches
+    of 1024 and 2048 positions (splits of about 28 and 41-55 positions)."""
     torch = G.torch_dev()
     rng = np.random.default_rng(Hq + kv_pos)
-    ctx = 1024
     base = 500000.0
     qkv = rng.standard_normal((Hq + 2 * Hkv) * hd).astype(np.float32)
     k = rng.standard_normal((Hkv, ctx, hd)).astype(np.float16)
