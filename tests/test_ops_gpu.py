@@ -458,7 +458,7 @@ def test_gemv_swiglu_epilogue(G, wtype, M):
 def test_attn_decode_fused(G, Hq, Hkv, hd, kv_pos, ctx):
     """Decode attention fused with RoPE and the KV write: cache row kv_pos holds fp16(rope(k)) and
     fp16(v) bit-exactly, the output matches exact fp64 attention over the rotated q, for caches
-    of 1024 and 2048 positions (split-KV over 37 splits per KV head, then the merge launch)."""
+    of 1024 and 2048 positions (split-KV, then the merge launch)."""
     torch = G.torch_dev()
     rng = np.random.default_rng(Hq + kv_pos)
     base = 500000.0
