@@ -82,8 +82,9 @@ struct SwiOut {
     float* yd = nullptr;
 };
 
-template <int WT, int SWI>
-__global__ void __launch_bounds__(kGThreads, 1)
+// OCC = CTAs per SM the kernel is built for: 2 keeps the block loop rolled (128 registers).
+template <int WT, int SWI, int OCC>
+__global__ void __launch_bounds__(kGThreads, OCC)
     k_gemm_q(const uint8_t* __restrict__ qs, int N, int K, const int8_t* __restrict__ xq,
              const float* __restrict__ xd, int M, float* __restrict__ y, int64_t y_stride,
              MatmulEpilogue ep, SwiOut so) {
@@ -168,7 +169,7 @@ __global__ void __launch_bounds__(kGThreads, 1)
         const uint8_t* sB = sA + S::kA;
         const __half* sW = (const __half*)(sB + S::kB);
         const float* sX = (const float*)((const uint8_t*)sW + S::kWs);
-#pragma unroll
+#pragma unroll(OCC == 2 ? 1 : 4)
         for (int lb = 0; lb < 4; ++lb) {
             unsigned af[4][4];
 #pragma unroll
@@ -305,16 +306,25 @@ __global__ void k_matmul_f(QWeight w, const float* __restrict__ x, int64_t x_str
     }
 }
 
-template <int WT, int SWI>
-void config_gemm(int dev) {
-    static std::mutex mu;
-    static bool configured[64] = {};
-    std::lock_guard<std::mutex> lock(mu);
-    if (!configured[dev & 63]) {
-        GB_CUDA(cudaFuncSetAttribute(k_gemm_q<WT, SWI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     kGStages * GStage<WT>::kBytes));
-        configured[dev & 63] = true;
+template <int WT, int SWI, int OCC>
+void run_gemm(dim3 grid, const uint8_t* qs, int N, int K, const int8_t* xq, const float* xd,
+              int M, float* y, int64_t y_stride, const MatmulEpilogue& ep, const SwiOut& so,
+              cudaStream_t st) {
+    int dev = 0;
+    GB_CUDA(cudaGetDevice(&dev));
+    {
+        static std::mutex mu;
+        static bool configured[64] = {};
+        std::lock_guard<std::mutex> lock(mu);
+        if (!configured[dev & 63]) {
+            GB_CUDA(cudaFuncSetAttribute(k_gemm_q<WT, SWI, OCC>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kGStages * GStage<WT>::kBytes));
+            configured[dev & 63] = true;
+        }
     }
+    k_gemm_q<WT, SWI, OCC><<<grid, kGThreads, kGStages * GStage<WT>::kBytes, st>>>(
+        qs, N, K, xq, xd, M, y, y_stride, ep, so);
 }
 
 void launch_gemm_block(const QWeight& w, const int8_t* xq, const float* xd, int64_t M, float* y,
@@ -327,25 +337,19 @@ void launch_gemm_block(const QWeight& w, const int8_t* xq, const float* xd, int6
     dim3 grid((unsigned)tiles, (unsigned)((M + kBM - 1) / kBM));
     int dev = 0;
     GB_CUDA(cudaGetDevice(&dev));
-    const bool q8 = w.type == T_Q8_0;
     const uint8_t* qs = (const uint8_t*)w.qs;
-    const int N = (int)w.N, K = (int)w.K;
-    if (q8 && !swi) {
-        config_gemm<T_Q8_0, 0>(dev);
-        k_gemm_q<T_Q8_0, 0><<<grid, kGThreads, kGStages * GStage<T_Q8_0>::kBytes, st>>>(
-            qs, N, K, xq, xd, (int)M, y, y_stride, ep, so);
-    } else if (q8) {
-        config_gemm<T_Q8_0, 1>(dev);
-        k_gemm_q<T_Q8_0, 1><<<grid, kGThreads, kGStages * GStage<T_Q8_0>::kBytes, st>>>(
-            qs, N, K, xq, xd, (int)M, y, y_stride, ep, so);
-    } else if (!swi) {
-        config_gemm<T_Q4_0, 0>(dev);
-        k_gemm_q<T_Q4_0, 0><<<grid, kGThreads, kGStages * GStage<T_Q4_0>::kBytes, st>>>(
-            qs, N, K, xq, xd, (int)M, y, y_stride, ep, so);
+    const int N = (int)w.N, K = (int)w.K, m = (int)M;
+    // Q4_0 stages fit two CTAs per SM: worth it once there are tiles for two per SM
+    const bool two = w.type == T_Q4_0 && tiles * grid.y >= 2 * (int64_t)sm_count(dev);
+    if (w.type == T_Q8_0) {
+        if (swi) run_gemm<T_Q8_0, 1, 1>(grid, qs, N, K, xq, xd, m, y, y_stride, ep, so, st);
+        else run_gemm<T_Q8_0, 0, 1>(grid, qs, N, K, xq, xd, m, y, y_stride, ep, so, st);
+    } else if (two) {
+        if (swi) run_gemm<T_Q4_0, 1, 2>(grid, qs, N, K, xq, xd, m, y, y_stride, ep, so, st);
+        else run_gemm<T_Q4_0, 0, 2>(grid, qs, N, K, xq, xd, m, y, y_stride, ep, so, st);
     } else {
-        config_gemm<T_Q4_0, 1>(dev);
-        k_gemm_q<T_Q4_0, 1><<<grid, kGThreads, kGStages * GStage<T_Q4_0>::kBytes, st>>>(
-            qs, N, K, xq, xd, (int)M, y, y_stride, ep, so);
+        if (swi) run_gemm<T_Q4_0, 1, 1>(grid, qs, N, K, xq, xd, m, y, y_stride, ep, so, st);
+        else run_gemm<T_Q4_0, 0, 1>(grid, qs, N, K, xq, xd, m, y, y_stride, ep, so, st);
     }
     GB_CUDA(cudaGetLastError());
 }
