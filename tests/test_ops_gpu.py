@@ -147,6 +147,37 @@ def test_prefill_gemm_swiglu_epilogue(G, wtype, M):
 
 
 @pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_0])
+@pytest.mark.parametrize("M", [200, 600])
+def test_prefill_gemm_tile_variants(G, wtype, M):
+    """Prefill shapes on both builds of the block GEMM (Q4_0 at 600 rows has tiles for two CTAs
+    per SM and runs the rolled build; 200 rows and Q8_0 run one CTA per SM): the integer path is
+    bit-exact against the oracle on sampled output columns, and the SwiGLU epilogue is bit-exact
+    against the plain GEMM's outputs."""
+    torch = G.torch_dev()
+    rng = np.random.default_rng(M + 7 * wtype)
+    F, K = 4096, 256
+    N = 2 * F
+    w, x = _int_exact_case(rng, wtype, N, K, M)
+    wq, wd = G.upload_weight(wtype, w, N, K)
+    y = G.mul_mat(wtype, wq, wd, N, K, G.dev(x), M)
+    cols = np.sort(rng.choice(N, size=64, replace=False))
+    assert np.array_equal(y[:, cols], O.mul_mat(wtype, np.ascontiguousarray(w[cols]), len(cols), K, x))
+    xq, xd = G.quantize(G.dev(x), M, K)
+    h = torch.empty((M, F), dtype=torch.float32, device="cuda")
+    hq = torch.empty((M, F), dtype=torch.int8, device="cuda")
+    hd = torch.empty((M, F // 32), dtype=torch.float32, device="cuda")
+    L = G.lib_fused()
+    G.check(L.gb_gemv(wtype, G.ptr(wq), N, K, M, G.ptr(xq), G.ptr(xd), None, 0.0, None, 1,
+                      G.ptr(h), G.ptr(hq), G.ptr(hd), None, None, None))
+    ref = O.swiglu(y)
+    assert np.array_equal(h.cpu().numpy(), ref)
+    rq = O.quantize_q8_0(ref).reshape(M, F // 32, 34)
+    assert np.array_equal(hq.cpu().numpy(), rq[:, :, 2:].reshape(M, F).view(np.int8))
+    del wq, wd
+    torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_0])
 @pytest.mark.parametrize("K", [576, 4096, 14336])
 def test_decode_rows_independent_of_batch(G, wtype, K):
     """A row's decode-matmul result is bit-identical whatever rows run with it, with the
