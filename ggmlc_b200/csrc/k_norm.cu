@@ -29,18 +29,34 @@ __device__ double block_sum_d(double v, double* sh) {
     return sh[0];
 }
 
-// Store a finished row: f32 copy and/or Q8_0 blocks (one warp per 32-element block).
+// Store a finished row: f32 copy and/or Q8_0 blocks.  A warp quantizes four 32-element blocks
+// at once (lane = element; the four amax butterflies interleaved), with q8_block's arithmetic.
 __device__ void emit_row(const float* __restrict__ row_vals, int64_t D, float* y, int8_t* yq,
                          float* yd) {
     const int lane = threadIdx.x & 31, w = threadIdx.x / 32, nw = blockDim.x / 32;
     if (y)
         for (int64_t k = threadIdx.x; k < D; k += blockDim.x) y[k] = row_vals[k];
     if (yq) {
-        for (int64_t b = w; b < D / QK; b += nw) {
-            float d16, q;
-            q8_block(row_vals[b * QK + lane], lane, d16, q);
-            yq[b * QK + lane] = (int8_t)__float2int_rn(q);
-            if (lane == 0) yd[b] = d16;
+        const int64_t nbk = D / QK;
+        for (int64_t b0 = (int64_t)w * 4; b0 < nbk; b0 += (int64_t)nw * 4) {  // warp-uniform
+            float v[4], am[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                v[j] = b0 + j < nbk ? row_vals[(b0 + j) * QK + lane] : 0.0f;
+                am[j] = fabsf(v[j]);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) am[j] = fmaxf(am[j], __shfl_xor_sync(0xffffffffu, am[j], o));
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (b0 + j >= nbk) break;
+                const float d16 = __half2float(__float2half_rn(__fdiv_rn(am[j], 127.0f)));
+                const float id = am[j] != 0.0f ? __fdiv_rn(127.0f, am[j]) : 0.0f;
+                yq[(b0 + j) * QK + lane] = (int8_t)__float2int_rn(rintf(__fmul_rn(v[j], id)));
+                if (lane == 0) yd[b0 + j] = d16;
+            }
         }
     }
 }
