@@ -107,6 +107,17 @@ def _load() -> ctypes.CDLL:
         "gb_scheduler_is_prefix_caching_enabled": ([P], I),
         "gb_scheduler_get_request": ([P, ctypes.c_uint64, P], I),
         "gb_scheduler_request_tokens": ([P, ctypes.c_uint64, I, P, I64, ctypes.POINTER(I64)], I),
+        "gb_scheduler_prefix_stats": ([P, ctypes.POINTER(I64), ctypes.POINTER(I64)], I),
+        "gb_executor_configure_prefix_pool": ([P, I64], I),
+        "gb_radix_create": ([I64, PP], I),
+        "gb_radix_free": ([P], None),
+        "gb_radix_tokens_per_page": ([P], I64),
+        "gb_radix_total_cached_pages": ([P], I64),
+        "gb_radix_total_nodes": ([P], I64),
+        "gb_radix_reset": ([P], None),
+        "gb_radix_match_prefix": ([P, P, I64, ctypes.POINTER(I64), ctypes.POINTER(I64)], I),
+        "gb_radix_insert_prefix": ([P, P, I64, ctypes.POINTER(I64)], I),
+        "gb_radix_evict_lru": ([P], I64),
     }
     for name, (args, res) in sigs.items():
         fn = getattr(L, name)
@@ -462,7 +473,10 @@ class ModelExecutor:
         return int(_lib.gb_executor_paged_active_vram_bytes(self._h))
 
     def configure_vmm_pool(self, max_warm_pages: int = 64, prealloc_pages: int = 0) -> None:
-        """Accepted for compatibility: slots are windows of one allocation, no VMM page pool."""
+        """Size of the prefix-cache page pool in pages (max_warm_pages).  Slots are windows of
+        one allocation, so there is no VMM page pool to warm; prealloc_pages is accepted and the
+        pool is allocated on the scheduler's first use."""
+        _check(_lib.gb_executor_configure_prefix_pool(self._h, int(max_warm_pages)))
 
     @property
     def tokens_per_page(self) -> int:
@@ -483,6 +497,62 @@ class ModelExecutor:
         h = getattr(self, "_h", None)
         if h is not None and h.value:
             _lib.gb_executor_free(h)
+            self._h = ctypes.c_void_p()
+
+
+# ---- prefix cache index (radix_tree.h; python_bindings.cpp:248-258) --------------------------
+class PrefixMatchResult:
+    def __init__(self, matched_pages: int, matched_tokens: int):
+        self.matched_pages = matched_pages
+        self.matched_tokens = matched_tokens
+
+
+class PagedRadixTree:
+    """Trie over whole pages of tokens_per_page tokens (FNV-1a chunk hashes checked token by
+    token, least-recently-used leaf eviction), the index the scheduler's prefix cache uses."""
+
+    def __init__(self, tokens_per_page: int = 1024):
+        h = ctypes.c_void_p()
+        _check(_lib.gb_radix_create(int(tokens_per_page), ctypes.byref(h)))
+        self._h = h
+
+    @property
+    def tokens_per_page(self) -> int:
+        return int(_lib.gb_radix_tokens_per_page(self._h))
+
+    @property
+    def total_cached_pages(self) -> int:
+        return int(_lib.gb_radix_total_cached_pages(self._h))
+
+    @property
+    def total_nodes(self) -> int:
+        return int(_lib.gb_radix_total_nodes(self._h))
+
+    def match_prefix(self, prompt_tokens) -> PrefixMatchResult:
+        t = np.ascontiguousarray(prompt_tokens, np.int32).reshape(-1)
+        pages, toks = ctypes.c_int64(), ctypes.c_int64()
+        _check(_lib.gb_radix_match_prefix(self._h, t.ctypes.data, len(t), ctypes.byref(pages),
+                                          ctypes.byref(toks)))
+        return PrefixMatchResult(int(pages.value), int(toks.value))
+
+    def insert_prefix(self, prompt_tokens) -> int:
+        """Index the whole pages of prompt_tokens not yet present; returns how many were added."""
+        t = np.ascontiguousarray(prompt_tokens, np.int32).reshape(-1)
+        added = ctypes.c_int64()
+        _check(_lib.gb_radix_insert_prefix(self._h, t.ctypes.data, len(t), ctypes.byref(added)))
+        return int(added.value)
+
+    def evict_lru(self) -> int:
+        """Drop the least recently used leaf page; its page id, or -1 when none can go."""
+        return int(_lib.gb_radix_evict_lru(self._h))
+
+    def reset(self) -> None:
+        _lib.gb_radix_reset(self._h)
+
+    def __del__(self):
+        h = getattr(self, "_h", None)
+        if h is not None and h.value and _lib is not None:
+            _lib.gb_radix_free(h)
             self._h = ctypes.c_void_p()
 
 
@@ -525,9 +595,9 @@ class ContinuousBatchScheduler:
     """Iteration-level continuous batching over the executor's paged KV cache.
 
     Same interface as the reference scheduler (python_bindings.cpp:278-294).  Each step admits
-    one pending request (prefill in a free slot) or decodes one token of every active sequence,
-    each at its own position.  Prefix caching is not implemented (the toggle is accepted and
-    the hit counters stay 0).
+    every pending request that finds a free slot (prefill in it) or decodes one token of every
+    active sequence, each at its own position.  Prefix caching (on by default) reuses the KV rows
+    of whole cached prompt pages (executor.tokens_per_page tokens each) and prefills the rest.
     """
 
     def __init__(self, executor: ModelExecutor, max_batch_size: int = 8, eos_token_id: int = 0):
@@ -575,13 +645,18 @@ class ContinuousBatchScheduler:
     def is_prefix_caching_enabled(self) -> bool:
         return bool(_lib.gb_scheduler_is_prefix_caching_enabled(self._h))
 
+    def _prefix_stats(self) -> tuple[int, int]:
+        hits, saved = ctypes.c_int64(), ctypes.c_int64()
+        _check(_lib.gb_scheduler_prefix_stats(self._h, ctypes.byref(hits), ctypes.byref(saved)))
+        return int(hits.value), int(saved.value)
+
     @property
     def total_prefix_cache_hits(self) -> int:
-        return 0
+        return self._prefix_stats()[0]
 
     @property
     def total_prefix_tokens_saved(self) -> int:
-        return 0
+        return self._prefix_stats()[1]
 
     def _tokens(self, rid: int, which: int) -> list[int]:
         n = ctypes.c_int64()

@@ -11,6 +11,7 @@
 #include "executor.h"
 #include "tp.h"
 #include "graph.h"
+#include "radix.h"
 #include "scheduler.h"
 #include "kernels.h"
 #include "kutil.cuh"
@@ -25,6 +26,10 @@ struct gb_executor {
     std::string summary, mm_summary, ktimes;
 };
 
+struct gb_radix {
+    std::unique_ptr<gb::PrefixTree> t;
+    int64_t next_page = 0;  // page ids handed out by gb_radix_insert_prefix
+};
 struct gb_scheduler {
     std::unique_ptr<gb::Scheduler> s;
 };
@@ -314,6 +319,56 @@ int gb_scheduler_enable_prefix_caching(gb_scheduler* s, int enable) {
 int gb_scheduler_is_prefix_caching_enabled(const gb_scheduler* s) {
     return s->s->prefix_caching() ? 1 : 0;
 }
+int gb_scheduler_prefix_stats(const gb_scheduler* s, int64_t* hits, int64_t* tokens_saved) {
+    return guard([&] {
+        if (hits) *hits = s->s->prefix_cache_hits();
+        if (tokens_saved) *tokens_saved = s->s->prefix_tokens_saved();
+    });
+}
+int gb_executor_configure_prefix_pool(gb_executor* e, int64_t pages) {
+    return guard([&] { e->e->configure_prefix_pool(pages); });
+}
+
+int gb_radix_create(int64_t tokens_per_page, gb_radix** out) {
+    return guard([&] {
+        auto* h = new gb_radix();
+        try {
+            h->t.reset(new gb::PrefixTree(tokens_per_page));
+        } catch (...) {
+            delete h;
+            throw;
+        }
+        *out = h;
+    });
+}
+void gb_radix_free(gb_radix* r) { delete r; }
+int64_t gb_radix_tokens_per_page(const gb_radix* r) { return r->t->tokens_per_page(); }
+int64_t gb_radix_total_cached_pages(const gb_radix* r) { return r->t->total_pages(); }
+int64_t gb_radix_total_nodes(const gb_radix* r) { return r->t->total_nodes(); }
+void gb_radix_reset(gb_radix* r) {
+    r->t->reset();
+    r->next_page = 0;
+}
+int gb_radix_match_prefix(gb_radix* r, const int32_t* tokens, int64_t n, int64_t* matched_pages,
+                          int64_t* matched_tokens) {
+    return guard([&] {
+        GB_CHECK(n >= 0 && (n == 0 || tokens), "radix: bad token array");
+        const gb::PrefixMatch m = r->t->match(std::vector<int32_t>(tokens, tokens + n));
+        *matched_pages = m.matched_pages;
+        *matched_tokens = m.matched_tokens;
+    });
+}
+int gb_radix_insert_prefix(gb_radix* r, const int32_t* tokens, int64_t n, int64_t* added) {
+    return guard([&] {
+        GB_CHECK(n >= 0 && (n == 0 || tokens), "radix: bad token array");
+        const std::vector<int32_t> v(tokens, tokens + n);
+        const int64_t T = r->t->tokens_per_page();
+        const gb::PrefixMatch m = r->t->match(v);
+        *added = r->t->insert(v, m.matched_pages, n / T - m.matched_pages,
+                              [&](int64_t) { return r->next_page++; });
+    });
+}
+int64_t gb_radix_evict_lru(gb_radix* r) { return r->t->evict_lru(); }
 int gb_scheduler_get_request(gb_scheduler* s, uint64_t request_id, gb_request_info* info) {
     return guard([&] {
         auto r = s->s->get(request_id);
@@ -328,7 +383,7 @@ int gb_scheduler_get_request(gb_scheduler* s, uint64_t request_id, gb_request_in
         info->finish_reason = r->finish_reason.c_str();
         info->n_prompt_tokens = (int64_t)r->prompt.size();
         info->n_generated_tokens = (int64_t)r->generated.size();
-        info->prefix_tokens_matched = 0;
+        info->prefix_tokens_matched = r->prefix_matched;
     });
 }
 int gb_scheduler_request_tokens(gb_scheduler* s, uint64_t request_id, int which, int32_t* buf,

@@ -237,6 +237,7 @@ Executor::~Executor() {
     for (cudaEvent_t ev : kevents_) cudaEventDestroy(ev);
     if (h_step_) cudaFreeHost(h_step_);
     if (d_step_) cudaFree(d_step_);
+    if (prefix_pool_) cudaFree(prefix_pool_);
     if (pinned_out_) cudaFreeHost(pinned_out_);
     if (d_argmax_) cudaFree(d_argmax_);
     if (h_argmax_) cudaFreeHost(h_argmax_);
@@ -482,6 +483,68 @@ int64_t Executor::paged_active_vram_bytes() const {
     for (int64_t t : slot_tokens_)
         if (t > 0) total += std::min(t, kv_max_ctx_) * per_token;
     return total;
+}
+
+int64_t Executor::kv_page_bytes() const {
+    int64_t b = 0;
+    for (auto& [id, c] : kv_) b += 2 * c.Hkv * tokens_per_page_ * c.hd * 2;
+    return b;
+}
+
+void Executor::configure_prefix_pool(int64_t pages) {
+    GB_CHECK(pages >= 0, "prefix pool: page count must not be negative");
+    prefix_pool_want_ = pages;
+}
+
+int64_t Executor::prefix_pool_reserve() {
+    GB_CHECK(paged_, "prefix pool: the paged KV cache is not initialised");
+    const int64_t pb = kv_page_bytes();
+    GB_CHECK(pb > 0, "prefix pool: no KV cache layers");
+    if (prefix_pool_ && prefix_page_bytes_ == pb) return prefix_pool_pages_;
+    if (prefix_pool_) {  // the page layout changed (tokens_per_page): start over
+        GB_CUDA(cudaStreamSynchronize(stream_));
+        cudaFree(prefix_pool_);
+        prefix_pool_ = nullptr;
+    }
+    int64_t n = prefix_pool_want_ > 0 ? prefix_pool_want_ : std::max<int64_t>(1, (2LL << 30) / pb);
+    GB_CUDA(cudaMalloc(&prefix_pool_, (size_t)(n * pb)));
+    prefix_pool_pages_ = n;
+    prefix_page_bytes_ = pb;
+    return n;
+}
+
+// positions [t0, t0 + T) of every layer's K and V rows in `slot` <-> pool page `page`: per layer
+// and K / V, Hkv rows of T * hd halves (ctx * hd apart in the slot, T * hd apart in the page)
+void Executor::kv_slot_to_page(int64_t slot, int64_t t0, int64_t page) {
+    GB_CHECK(prefix_pool_ && page >= 0 && page < prefix_pool_pages_, "prefix pool: bad page");
+    GB_CHECK(paged_ && slot >= 0 && slot < paged_max_batch_, "prefix pool: bad slot");
+    GB_CHECK(t0 >= 0 && t0 + tokens_per_page_ <= kv_max_ctx_, "prefix pool: page past the cache");
+    char* dst = (char*)prefix_pool_ + page * prefix_page_bytes_;
+    for (auto& [id, c] : kv_) {
+        const size_t w = (size_t)(tokens_per_page_ * c.hd * 2);
+        for (__half* base : {c.k, c.v}) {
+            const __half* src = base + slot * c.slot_elems() + t0 * c.hd;
+            GB_CUDA(cudaMemcpy2DAsync(dst, w, src, (size_t)(c.ctx * c.hd * 2), w, (size_t)c.Hkv,
+                                      cudaMemcpyDeviceToDevice, stream_));
+            dst += w * (size_t)c.Hkv;
+        }
+    }
+}
+
+void Executor::kv_page_to_slot(int64_t page, int64_t slot, int64_t t0) {
+    GB_CHECK(prefix_pool_ && page >= 0 && page < prefix_pool_pages_, "prefix pool: bad page");
+    GB_CHECK(paged_ && slot >= 0 && slot < paged_max_batch_, "prefix pool: bad slot");
+    GB_CHECK(t0 >= 0 && t0 + tokens_per_page_ <= kv_max_ctx_, "prefix pool: page past the cache");
+    const char* src = (const char*)prefix_pool_ + page * prefix_page_bytes_;
+    for (auto& [id, c] : kv_) {
+        const size_t w = (size_t)(tokens_per_page_ * c.hd * 2);
+        for (__half* base : {c.k, c.v}) {
+            __half* dst = base + slot * c.slot_elems() + t0 * c.hd;
+            GB_CUDA(cudaMemcpy2DAsync(dst, (size_t)(c.ctx * c.hd * 2), src, w, w, (size_t)c.Hkv,
+                                      cudaMemcpyDeviceToDevice, stream_));
+            src += w * (size_t)c.Hkv;
+        }
+    }
 }
 
 void Executor::set_tokens_per_page(int64_t n) {

@@ -159,6 +159,16 @@ public:
     int64_t tokens_per_page() const { return tokens_per_page_; }
     void set_tokens_per_page(int64_t n);
     int64_t paged_max_batch() const { return paged_ ? paged_max_batch_ : 0; }
+    // Prefix-cache page pool (the store behind the scheduler's prefix tree): pages of
+    // tokens_per_page positions of K and V of every attention layer, [layer][K, V][Hkv][T][hd]
+    // fp16.  A hit copies pages into a sequence's slot; a prefill copies its new full pages out.
+    // configure_prefix_pool sets the page count of the next allocation (configure_vmm_pool of
+    // the reference, whose max_warm_pages it takes); prefix_pool_reserve allocates on first use.
+    int64_t kv_page_bytes() const;
+    void configure_prefix_pool(int64_t pages);
+    int64_t prefix_pool_reserve();  // pages available (allocates the pool if needed)
+    void kv_slot_to_page(int64_t slot, int64_t t0, int64_t page);
+    void kv_page_to_slot(int64_t page, int64_t slot, int64_t t0);
     // Batched decode step over `rows` sequences: row r decodes the token at position pos[r] of
     // the sequence in slot slot[r] (rows padded up to a bucket use the scratch slot).
     void prepare_batch(int rows, const int32_t* pos, const int32_t* slot);
@@ -231,6 +241,10 @@ private:
     bool paged_ = false;
     int64_t paged_max_batch_ = 0;
     int64_t tokens_per_page_ = 256;
+    void* prefix_pool_ = nullptr;      // prefix_pool_pages_ x page_bytes_at_alloc_
+    int64_t prefix_pool_pages_ = 0;
+    int64_t prefix_pool_want_ = 0;     // 0: about 2 GiB of pages
+    int64_t prefix_page_bytes_ = 0;    // page size the pool was laid out for
     std::vector<int64_t> slot_tokens_;  // per slot: positions accounted (-1: free)
     char* arena_ = nullptr;             // activation arena shared by every program
     size_t arena_cap_ = 0;

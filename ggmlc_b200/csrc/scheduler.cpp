@@ -100,47 +100,109 @@ void Scheduler::finish(const std::shared_ptr<GenRequest>& r, int32_t tok, StepOu
     slots_[(size_t)r->slot] = nullptr;
 }
 
+// Pool page for a new chunk: a free one, else the least recently used leaf's.  The pool is
+// allocated when the first page is needed.
+int64_t Scheduler::take_page() {
+    if (!pool_ready_) {
+        const int64_t n = ex_.prefix_pool_reserve();
+        free_pages_.clear();
+        for (int64_t p = n - 1; p >= 0; --p) free_pages_.push_back(p);
+        pool_ready_ = true;
+    }
+    if (!free_pages_.empty()) {
+        const int64_t p = free_pages_.back();
+        free_pages_.pop_back();
+        return p;
+    }
+    return tree_ ? tree_->evict_lru() : -1;
+}
+
+void Scheduler::ensure_tree() {
+    const int64_t T = ex_.tokens_per_page();
+    if (tree_ && tree_->tokens_per_page() == T) return;
+    tree_ = std::make_unique<PrefixTree>(T);  // a new page size starts an empty cache
+    pool_ready_ = false;
+}
+
 StepOut Scheduler::step() {
     StepOut out;
-    // admission: one pending request per step, prefilled alone into a free slot
-    if (!pending_.empty()) {
+    // admission (batch_scheduler.cpp:136-277): every pending request that finds a free slot is
+    // prefilled alone into it, reusing the KV rows of the longest cached run of whole prompt
+    // pages; a step that admits returns without decoding
+    bool admitted = false;
+    while (!pending_.empty()) {
         int slot = -1;
         for (size_t i = 0; i < slots_.size(); ++i)
             if (!slots_[i]) {
                 slot = (int)i;
                 break;
             }
-        if (slot >= 0) {
-            auto r = pending_.front();
-            pending_.pop_front();
-            r->slot = slot;
-            slots_[(size_t)slot] = r;
-            ex_.paged_kv_alloc_slot(slot);
-            const int64_t n = (int64_t)r->prompt.size();
-            ex_.paged_kv_ensure_tokens(slot, n + r->max_new);
-            SymEnv env;
-            env["s"] = n;
-            for (auto& s : ex_.graph().symbol_table) env[s] = n;
-            env["pos"] = 0;
-            env["slot"] = slot;
-            ex_.prepare(env, true);
-            ex_.set_input(in_id_, r->prompt.data(), r->prompt.size() * 4);
-            ex_.run();
-            int32_t tok = 0;
-            if (r->temperature <= 0.0f) {
-                ex_.output_argmax(out_id_, 1, &tok);  // last row only
-            } else {
-                size_t bytes = 0;
-                const float* logits = (const float*)ex_.get_output(out_id_, &bytes);
-                tok = sample(logits, (int64_t)(bytes / 4), r->temperature);
+        if (slot < 0) break;
+        auto r = pending_.front();
+        pending_.pop_front();
+        r->slot = slot;
+        slots_[(size_t)slot] = r;
+        ex_.paged_kv_alloc_slot(slot);
+        const int64_t n = (int64_t)r->prompt.size();
+        ex_.paged_kv_ensure_tokens(slot, n + r->max_new);
+        int64_t matched = 0;
+        if (prefix_caching_) {
+            ensure_tree();
+            const PrefixMatch m = tree_->match(r->prompt);
+            for (int64_t p = 0; p < m.matched_pages; ++p)
+                ex_.kv_page_to_slot(m.pages[(size_t)p], slot, p * tree_->tokens_per_page());
+            matched = m.matched_tokens;
+            if (matched > 0) {
+                ++prefix_hits_;
+                prefix_saved_ += matched;
             }
-            r->generated.push_back(tok);
-            r->pos = n;
-            out.new_tokens.push_back({r->id, tok});
-            finish(r, tok, out);
-            return out;
         }
+        r->prefix_matched = matched;
+        // the uncached tail; a prompt cached whole re-evaluates its last token
+        const int64_t pos = matched < n ? matched : n - 1;
+        const int64_t s = n - pos;
+        SymEnv env;
+        env["s"] = s;
+        for (auto& sym : ex_.graph().symbol_table) env[sym] = s;
+        env["pos"] = pos;
+        env["slot"] = slot;
+        ex_.prepare(env, true);
+        ex_.set_input(in_id_, r->prompt.data() + pos, (size_t)s * 4);
+        ex_.run();
+        if (prefix_caching_) {  // index the prompt's new whole pages
+            const int64_t T = tree_->tokens_per_page();
+            const int64_t first = matched / T, full = n / T;
+            if (full > first) {
+                try {
+                    tree_->insert(r->prompt, first, full - first, [&](int64_t i) {
+                        const int64_t page = take_page();
+                        if (page >= 0) ex_.kv_slot_to_page(slot, (first + i) * T, page);
+                        return page;
+                    });
+                } catch (const Error&) {
+                    // no memory for the pool (or a failed copy): drop the cache, serve on
+                    cudaGetLastError();
+                    tree_->reset();
+                    pool_ready_ = false;
+                    prefix_caching_ = false;
+                }
+            }
+        }
+        int32_t tok = 0;
+        if (r->temperature <= 0.0f) {
+            ex_.output_argmax(out_id_, 1, &tok);  // last row only
+        } else {
+            size_t bytes = 0;
+            const float* logits = (const float*)ex_.get_output(out_id_, &bytes);
+            tok = sample(logits, (int64_t)(bytes / 4), r->temperature);
+        }
+        r->generated.push_back(tok);
+        r->pos = n;
+        out.new_tokens.push_back({r->id, tok});
+        finish(r, tok, out);
+        admitted = true;
     }
+    if (admitted) return out;
     // one batched decode step over every active sequence, rows padded to a bucket
     std::vector<std::shared_ptr<GenRequest>> act;
     for (auto& s : slots_)

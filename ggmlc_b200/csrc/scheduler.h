@@ -5,8 +5,10 @@
 // Differences by design: every sequence decodes at its own position in its own slot (one
 // batched step over all active sequences, rows padded to a bucket of 1/2/4/8/16 with a scratch
 // slot), where the reference runs one shared position over all slots; the graph needs no batch
-// dimension (rows of the sequence axis are the batch).  Prefix caching is not implemented:
-// enable_prefix_caching is accepted and the hit counters stay zero.
+// dimension (rows of the sequence axis are the batch).  Prefix caching (on by default, as in the
+// reference) indexes whole prompt pages in a PrefixTree whose pages live in the executor's
+// prefix pool: a hit copies the cached KV rows into the new slot and prefills only the rest of
+// the prompt; a prefill copies its new whole pages out.
 #pragma once
 
 #include <cstdint>
@@ -19,6 +21,7 @@
 #include <vector>
 
 #include "executor.h"
+#include "radix.h"
 
 namespace gb {
 
@@ -33,6 +36,7 @@ struct GenRequest {
     int eos = -1;
     bool finished = false;
     std::string finish_reason;  // "stop" (end token) or "length" (max_new reached)
+    int64_t prefix_matched = 0;  // prompt tokens whose KV rows came from the prefix cache
 };
 
 struct StepOut {
@@ -49,8 +53,8 @@ public:
 
     uint64_t add_request(const std::vector<int32_t>& prompt, int max_new, float temperature,
                          int eos);
-    // One iteration: admit one pending request (prefill into a free slot, first token) and
-    // return, or run one batched decode step over every active sequence.
+    // One iteration: admit every pending request that finds a free slot (prefill, first token)
+    // and return, or run one batched decode step over every active sequence.
     StepOut step();
     bool has_work() const;
     size_t active_count() const;
@@ -59,9 +63,13 @@ public:
     std::shared_ptr<GenRequest> get(uint64_t id) const;
     void enable_prefix_caching(bool on) { prefix_caching_ = on; }
     bool prefix_caching() const { return prefix_caching_; }
+    int64_t prefix_cache_hits() const { return prefix_hits_; }
+    int64_t prefix_tokens_saved() const { return prefix_saved_; }
 
 private:
     int32_t sample(const float* logits, int64_t vocab, float temperature);
+    void ensure_tree();
+    int64_t take_page();
     void finish(const std::shared_ptr<GenRequest>& r, int32_t tok, StepOut& out);
 
     Executor& ex_;
@@ -74,6 +82,10 @@ private:
     std::vector<std::shared_ptr<GenRequest>> slots_;
     std::map<uint64_t, std::shared_ptr<GenRequest>> all_;
     std::mt19937 rng_{1337};
+    std::unique_ptr<PrefixTree> tree_;
+    std::vector<int64_t> free_pages_;
+    bool pool_ready_ = false;
+    int64_t prefix_hits_ = 0, prefix_saved_ = 0;
 };
 
 }  // namespace gb

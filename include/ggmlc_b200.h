@@ -147,10 +147,36 @@ int64_t gb_executor_tokens_per_page(const gb_executor* e);
 int gb_executor_set_tokens_per_page(gb_executor* e, int64_t tokens_per_page);
 int gb_executor_prepare_batch(gb_executor* e, int rows, const int32_t* pos, const int32_t* slot);
 
+/* Prefix-cache page pool size in pages (replaces configure_vmm_pool's max_warm_pages,
+ * python_bindings.cpp:201; the reference's pages are VMM pages shared by slots, ours are copied
+ * in and out of slots).  0 (default): about 2 GiB of pages, allocated on first use. */
+int gb_executor_configure_prefix_pool(gb_executor* e, int64_t pages);
+
+/* ---- PagedRadixTree (radix_tree.h; radix_tree.cpp:7-220; python_bindings.cpp:248-258) -------
+ * Prefix index over whole pages of tokens_per_page tokens: 64-bit FNV-1a chunk hashes verified
+ * token by token, least-recently-used leaf eviction.  Standalone handle for tests and callers;
+ * the scheduler keeps its own.  insert_prefix attaches the whole pages of `tokens` not yet
+ * present (page ids 0, 1, 2, ... in insertion order); evict_lru returns the freed page id or
+ * -1. */
+typedef struct gb_radix gb_radix;
+int gb_radix_create(int64_t tokens_per_page, gb_radix** out);
+void gb_radix_free(gb_radix* r);
+int64_t gb_radix_tokens_per_page(const gb_radix* r);
+int64_t gb_radix_total_cached_pages(const gb_radix* r);
+int64_t gb_radix_total_nodes(const gb_radix* r);
+void gb_radix_reset(gb_radix* r);
+int gb_radix_match_prefix(gb_radix* r, const int32_t* tokens, int64_t n, int64_t* matched_pages,
+                          int64_t* matched_tokens);
+int gb_radix_insert_prefix(gb_radix* r, const int32_t* tokens, int64_t n, int64_t* added);
+int64_t gb_radix_evict_lru(gb_radix* r);
+
 /* ---- ContinuousBatchScheduler (batch_scheduler.h:35-77; python_bindings.cpp:261-295) --------
  * Iteration-level continuous batching over the paged KV cache: add_request queues a prompt;
- * each step either admits one request (prefill into a free slot, first token) or decodes one
- * token for every active sequence at its own position.  Greedy when temperature <= 0. */
+ * each step either admits every pending request that finds a free slot (prefill into it, first
+ * token; batch_scheduler.cpp:136-277) or decodes one token for every active sequence at its own
+ * position.  Greedy when temperature <= 0.  Prefix caching (on by default): the KV rows of the
+ * longest cached run of whole prompt pages are copied into the slot and only the rest of the
+ * prompt is prefilled (batch_scheduler.cpp:149-164, :225-238). */
 typedef struct gb_scheduler gb_scheduler;
 typedef struct gb_request_info {
     uint64_t request_id;
@@ -178,6 +204,8 @@ int64_t gb_scheduler_pending_count(const gb_scheduler* s);
 int gb_scheduler_max_batch_size(const gb_scheduler* s);
 int gb_scheduler_enable_prefix_caching(gb_scheduler* s, int enable);
 int gb_scheduler_is_prefix_caching_enabled(const gb_scheduler* s);
+/* total_prefix_cache_hits / total_prefix_tokens_saved (batch_scheduler.h:56-57) */
+int gb_scheduler_prefix_stats(const gb_scheduler* s, int64_t* hits, int64_t* tokens_saved);
 int gb_scheduler_get_request(gb_scheduler* s, uint64_t request_id, gb_request_info* info);
 /* which: 0 prompt tokens, 1 generated tokens; copies min(cap, count) into buf, *n = count */
 int gb_scheduler_request_tokens(gb_scheduler* s, uint64_t request_id, int which, int32_t* buf,

@@ -181,3 +181,57 @@ def test_scheduler_rejects_bad_requests():
         sched.add_request([1, 2, 3], max_new_tokens=4096)  # beyond the 2048-position cache
     with pytest.raises(RuntimeError):
         ex.prepare_batch(np.array([0], np.int32), np.array([7], np.int32))  # no such slot
+
+
+@pytest.mark.parametrize("fixture", ["tiny_llama_q8_0", "tiny_llama_q4_0"])
+def test_prefix_caching_reuses_prompt_pages(fixture):
+    """The reference's prefix-caching e2e flow (tests/e2e/test_prefix_caching.py:76-142) on the
+    tiny models with 16-token pages: a cold request indexes its two whole prompt pages, three
+    requests sharing them are admitted in one step with 32 prompt tokens matched each, a prompt
+    that is cached whole re-evaluates only its last token; every request finishes, the slots are
+    returned, and the tokens follow single-sequence decode wherever its top-2 gap is clear."""
+    from ggmlc_b200 import _runtime as R
+
+    rng = np.random.default_rng(21)
+    vocab = int(np.load(GOLDEN / f"{fixture}.npz")["full_logits"].shape[1])
+    g, ex = _executor(fixture)
+    ex.set_tokens_per_page(16)
+    ex.configure_vmm_pool(max_warm_pages=8)
+    sched = R.ContinuousBatchScheduler(ex, max_batch_size=4, eos_token_id=-1)
+    ex.init_paged_kv_cache(4, MAX_CTX)  # same cache length as the single-sequence runs
+    assert sched.is_prefix_caching_enabled()
+    shared = list(rng.integers(1, vocab, size=32))
+    tails = [list(rng.integers(1, vocab, size=3)) for _ in range(4)]
+    prompts = [shared + t for t in tails]
+    n_new = 6
+    ids = [sched.add_request(prompts[0], max_new_tokens=n_new, temperature=0.0)]
+    sched.step()
+    assert sched.get_request(ids[0]).current_pos == len(prompts[0])
+    assert sched.total_prefix_cache_hits == 0
+    ids += [sched.add_request(p, max_new_tokens=n_new, temperature=0.0) for p in prompts[1:]]
+    sched.step()  # admits all three
+    assert sched.pending_count() == 0 and sched.active_count() == 4
+    assert sched.total_prefix_cache_hits == 3
+    assert sched.total_prefix_tokens_saved == 3 * 32
+    for rid in ids[1:]:
+        assert sched.get_request(rid).prefix_tokens_matched == 32
+    while sched.has_work():
+        sched.step()
+    # a prompt that is two whole cached pages
+    whole = sched.add_request(shared, max_new_tokens=n_new, temperature=0.0)
+    while sched.has_work():
+        sched.step()
+    assert sched.get_request(whole).prefix_tokens_matched == 32
+    assert sched.total_prefix_cache_hits == 4
+    assert ex.get_paged_active_vram_bytes() == 0
+    n_clear = 0
+    for rid, p in zip(ids + [whole], prompts + [shared]):
+        req = sched.get_request(rid)
+        assert req.finished and len(req.generated_tokens) == n_new
+        lg = _forced(fixture, p, req.generated_tokens)
+        srt = np.sort(lg, axis=1)
+        clear = (srt[:, -1] - srt[:, -2]) > 0.01 * (srt[:, -1] - srt[:, 0])
+        same = np.argmax(lg, axis=1) == np.asarray(req.generated_tokens)
+        assert np.all(same[clear]), f"request {rid}: {np.flatnonzero(~same)}"
+        n_clear += int(clear.sum())
+    assert n_clear >= 20
