@@ -432,7 +432,44 @@ def run_cb(g, gguf, local: int, steps: int = 256, buckets=(1, 2, 4, 8, 16)) -> d
                         "prompt_tokens": int(lens.sum()), "admit_s": round(t_admit, 3),
                         "decode_s": round(t_dec, 3)}
         del sched
+    out["prefix_cache"] = run_prefix(ex)
     return out
+
+
+def run_prefix(ex, n_req: int = 8, shared_len: int = 512, tail: int = 64) -> dict:
+    """Prefix caching: n_req requests sharing a shared_len-token prompt prefix
+    (two 256-token pages) with distinct tails, admitted in one scheduler step after a first
+    request with the same prefix has been served; that admission step's time with the cache off
+    and on."""
+    import time
+
+    from ggmlc_b200 import _runtime as R
+
+    rng = np.random.default_rng(7)
+    shared = rng.integers(0, 128256, size=shared_len).astype(np.int32)
+    tails = [rng.integers(0, 128256, size=tail).astype(np.int32) for _ in range(n_req + 1)]
+    res = {"requests": n_req, "shared_tokens": shared_len, "tail_tokens": tail,
+           "tokens_per_page": int(ex.tokens_per_page)}
+    for on in (False, True):
+        sched = R.ContinuousBatchScheduler(ex, max_batch_size=n_req, eos_token_id=-1)
+        sched.enable_prefix_caching(on)
+        sched.add_request(np.concatenate([shared, tails[-1]]), max_new_tokens=1, temperature=0.0)
+        while sched.has_work():
+            sched.step()
+        for t in tails[:n_req]:
+            sched.add_request(np.concatenate([shared, t]), max_new_tokens=1, temperature=0.0)
+        t0 = time.perf_counter()
+        sched.step()  # admits all n_req (prefill + first token each)
+        dt = time.perf_counter() - t0
+        while sched.has_work():
+            sched.step()
+        res["on" if on else "off"] = {
+            "admit_s": round(dt, 4),
+            "prompt_tokens_per_s": round(n_req * (shared_len + tail) / dt, 1),
+            "hits": sched.total_prefix_cache_hits,
+            "tokens_saved": sched.total_prefix_tokens_saved}
+        del sched
+    return res
 
 
 def ex_weight_gb(g) -> float:
