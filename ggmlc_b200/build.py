@@ -74,7 +74,26 @@ def build(force: bool = False, verbose: bool = False) -> Path:
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
         os.replace(tmp, LIB)
+    build_bench_tool(force)
     return LIB
+
+
+TOOL_SRC = PKG / "tools" / "ggmlc_bench.cpp"
+TOOL = PKG / "ggmlc-bench"
+
+
+def build_bench_tool(force: bool = False) -> Path:
+    """ggmlc_b200/ggmlc-bench: the reference's benchmark CLI over the C ABI (host C++ only)."""
+    if not force and TOOL.exists() and TOOL.stat().st_mtime >= max(
+            TOOL_SRC.stat().st_mtime, LIB.stat().st_mtime):
+        return TOOL
+    cxx = shutil.which("g++") or "g++"
+    cmd = [cxx, "-O2", "-std=c++17", "-o", str(TOOL), str(TOOL_SRC), "-I",
+           str(PKG.parent / "include"), "-L", str(PKG), "-lggmlc_b200", "-Wl,-rpath,$ORIGIN"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"ggmlc-bench build failed:\n{r.stdout}\n{r.stderr}")
+    return TOOL
 
 
 if __name__ == "__main__":
