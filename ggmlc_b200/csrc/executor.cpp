@@ -21,14 +21,6 @@ namespace gb {
 
 namespace {
 
-constexpr int64_t kKvPad = 256;  // executor.h:181 kv_n_pad_
-
-int64_t pad_kv_len(int64_t n_kv, int64_t max_ctx) {
-    if (n_kv < 1) n_kv = 1;
-    int64_t padded = std::max(kKvPad, (n_kv + kKvPad - 1) / kKvPad * kKvPad);
-    return std::min(padded, max_ctx);
-}
-
 void set_contig(Val& v) {
     const int64_t eb = v.type == T_F16 ? 2 : (v.type == T_I64 ? 8 : 4);
     v.nb[0] = eb;

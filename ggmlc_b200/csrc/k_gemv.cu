@@ -41,18 +41,6 @@ constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 constexpr size_t kSmemMax = 224 * 1024;  // dynamic; static shared memory needs the rest of 227 KB
 
-__device__ __forceinline__ uint4 ldg_stream(const void* p) {
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
-}
-__device__ __forceinline__ unsigned short ldg_u16(const void* p) {
-    unsigned short v;
-    asm volatile("ld.global.nc.L1::no_allocate.u16 %0, [%1];" : "=h"(v) : "l"(p));
-    return v;
-}
 
 __device__ __forceinline__ float block_sum_f(int s) {
     return __fsub_rn(__int_as_float(s), 12582912.0f);
@@ -189,7 +177,6 @@ __device__ __noinline__ void stage_x(const StageIn a, int nb, int nbp, uint4* sx
                                      float* sxd, float* sxf, const float* sgm, double* shd) {
     const int K = a.K;
     const float dscale = WT == T_Q4_0 ? 0.0625f : 1.0f;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (!a.xf) {
         for (int idx = threadIdx.x; idx < a.M * nbp; idx += kThreads) {
             const int m = idx / nbp, b = idx % nbp;

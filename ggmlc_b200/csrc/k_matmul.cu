@@ -233,7 +233,7 @@ __global__ void __launch_bounds__(kGThreads, OCC)
         }
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
-    if (SWI) {
+    if constexpr (SWI != 0) {
         // the tile's results through shared memory (the stage ring is free now), then one warp
         // per (activation row, 32-unit block): ggml_vec_swiglu_f32 (vec.cpp:417-426) and
         // quantize_row_q8_0 of the block
@@ -265,24 +265,24 @@ __global__ void __launch_bounds__(kGThreads, OCC)
                 if (lane == 0) so.yd[gm * (so.F / 32) + col / 32] = d16;
             }
         }
-        return;
-    }
+    } else {
 #pragma unroll
-    for (int mt = 0; mt < 4; ++mt)
+        for (int mt = 0; mt < 4; ++mt)
 #pragma unroll
-        for (int nt = 0; nt < 4; ++nt)
+            for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const int m = m0 + wm * 64 + mt * 16 + g + ((e >> 1) << 3);
-                const int n = n0 + wn * 32 + nt * 8 + 2 * tg + (e & 1);
-                if (m < M && n < N) {
-                    const float2 p = acc[mt][nt][e >> 1];
-                    float r = (e & 1) ? p.y : p.x;
-                    if (ep.bias) r = __fadd_rn(r, ep.bias[n]);
-                    if (ep.residual) r = __fadd_rn(ep.residual[(int64_t)m * ep.res_stride + n], r);
-                    y[(int64_t)m * y_stride + n] = r;
+                for (int e = 0; e < 4; ++e) {
+                    const int m = m0 + wm * 64 + mt * 16 + g + ((e >> 1) << 3);
+                    const int n = n0 + wn * 32 + nt * 8 + 2 * tg + (e & 1);
+                    if (m < M && n < N) {
+                        const float2 p = acc[mt][nt][e >> 1];
+                        float r = (e & 1) ? p.y : p.x;
+                        if (ep.bias) r = __fadd_rn(r, ep.bias[n]);
+                        if (ep.residual) r = __fadd_rn(ep.residual[(int64_t)m * ep.res_stride + n], r);
+                        y[(int64_t)m * y_stride + n] = r;
+                    }
                 }
-            }
+    }
 }
 
 // float-weight fallback (F32/F16 W): one warp per (row n, activation m)

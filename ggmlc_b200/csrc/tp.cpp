@@ -29,12 +29,6 @@ struct Ctx {
         for (int k = 0; k < 4; ++k) d[k] = t.ne[k] ? t.ne[k]->eval(env) : 1;
         return d;
     }
-    const GOp& producer(uint32_t id, const char* what) const {
-        auto it = prod.find(id);
-        GB_CHECK(it != prod.end(), std::string("tensor parallelism: ") + what +
-                                       " is not produced by an op");
-        return g.ops[(size_t)it->second];
-    }
 };
 
 void fail(const std::string& m) { GB_CHECK(false, "tensor parallelism: " + m); }
