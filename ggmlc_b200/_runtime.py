@@ -70,6 +70,7 @@ def _load() -> ctypes.CDLL:
         "gb_executor_reset_kv_cache": ([P], I),
         "gb_executor_has_kv_cache": ([P], I),
         "gb_executor_set_logits_last_only": ([P, I], I),
+        "gb_executor_set_output_rows": ([P, P, I], I),
         "gb_executor_logits_last_only": ([P], I),
         "gb_executor_set_enable_cuda_graph": ([P, I], I),
         "gb_executor_is_cuda_graph_enabled": ([P], I),
@@ -387,6 +388,14 @@ class ModelExecutor:
 
     def has_kv_cache(self) -> bool:
         return bool(_lib.gb_executor_has_kv_cache(self._h))
+
+    def set_output_rows(self, rows=None) -> None:
+        """Compute the output projections of the next prefills for these rows of the call's
+        tokens only (llama's out_ids; at most 64), logits [len(rows), vocab]; None or [] turns it
+        off.  Takes precedence over set_logits_last_only."""
+        r = np.ascontiguousarray([] if rows is None else rows, np.int32).reshape(-1)
+        _check(_lib.gb_executor_set_output_rows(self._h, r.ctypes.data if len(r) else None,
+                                                len(r)))
 
     def set_logits_last_only(self, enable: bool) -> None:
         _check(_lib.gb_executor_set_logits_last_only(self._h, int(bool(enable))))

@@ -397,6 +397,12 @@ int gb_scheduler_request_tokens(gb_scheduler* s, uint64_t request_id, int which,
         if (k > 0 && buf) std::memcpy(buf, v.data(), (size_t)k * 4);
     });
 }
+int gb_executor_set_output_rows(gb_executor* e, const int32_t* rows, int n) {
+    return guard([&] {
+        GB_CHECK(n >= 0 && (n == 0 || rows), "set_output_rows: bad row array");
+        e->e->set_output_rows(std::vector<int32_t>(rows, rows + n));
+    });
+}
 int gb_executor_set_logits_last_only(gb_executor* e, int enable) {
     return guard([&] { e->e->set_logits_last_only(enable != 0); });
 }

@@ -539,6 +539,11 @@ void Executor::kv_page_to_slot(int64_t page, int64_t slot, int64_t t0) {
     }
 }
 
+void Executor::set_output_rows(const std::vector<int32_t>& rows) {
+    GB_CHECK((int)rows.size() <= kMaxOutRows, "output rows: at most 64");
+    out_rows_ = rows;
+}
+
 void Executor::set_tokens_per_page(int64_t n) {
     GB_CHECK(n >= 1, "tokens_per_page must be positive");
     tokens_per_page_ = n;
@@ -731,7 +736,8 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
             const GOp& c = G.ops[ci];
             const bool qmm = c.opcode == OP_MUL_MAT && c.inputs.size() >= 2 && c.inputs[1] == id &&
                              is_quant(G.t(c.inputs[0]).type) && c.inputs[0] != id;
-            if (qmm && !(logits_last_only_ && outputs.count(c.outputs[0]))) need_q = true;
+            if (qmm && !((logits_last_only_ || !out_rows_.empty()) && outputs.count(c.outputs[0])))
+                need_q = true;
             else need_f = true;
         }
         if (!need_f && !need_q) need_f = true;
@@ -903,21 +909,25 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                                              std::to_string(K) + ")");
                 int64_t M = xin.nrows();
                 int64_t row0 = 0;
-                const bool last_only = logits_last_only_ && outputs.count(out) && M > 1 && !pg.batch;
-                if (last_only) {
+                // output rows: the listed rows, or the last one
+                const bool sel_rows = !out_rows_.empty() && outputs.count(out) && !pg.batch;
+                const bool last_only =
+                    !sel_rows && logits_last_only_ && outputs.count(out) && M > 1 && !pg.batch;
+                const int64_t n_sel = sel_rows ? (int64_t)out_rows_.size() : 0;
+                if (last_only || sel_rows) {
                     row0 = M - 1;
-                    o.ne[1] = 1;
+                    o.ne[1] = last_only ? 1 : n_sel;
                     o.ne[2] = 1;
                     o.ne[3] = 1;
                 }
-                const int64_t Mrun = last_only ? 1 : M;
+                const int64_t Mrun = last_only ? 1 : (sel_rows ? n_sel : M);
                 // fused residual ADD: the only consumer is ADD(other, this) of equal shape
                 int add_op = -1;
                 const float* bias = nullptr;
                 if (op.inputs.size() > 2 && !tp_skip_add)
                     bias = (const float*)get(op.inputs[2]).ref.fixed;
                 Val res;
-                if (!outputs.count(out) && consumers[out].size() == 1 && !last_only) {
+                if (!outputs.count(out) && consumers[out].size() == 1 && !last_only && !sel_rows) {
                     const int ci = consumers[out][0];
                     const GOp& c = G.ops[ci];
                     if (c.opcode == OP_ADD && c.inputs.size() == 2 && c.inputs[0] != c.inputs[1]) {
@@ -933,13 +943,13 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                 }
                 // decode (M <= 16): SwiGLU / residual epilogue fused into the matmul launch; an
                 // unmaterialized RMSNorm input (M <= 4) is normalized in the GEMV prologue
-                bool dec = is_quant(qw->type) && !last_only &&
+                bool dec = is_quant(qw->type) && !last_only && !sel_rows &&
                            (xin.virt_rms ? Mrun <= kGemvMaxRows && gemv_fused_fits(K, (int)Mrun)
                                          : Mrun <= kMmvMaxRows);
                 GB_CHECK(!xin.virt_rms || dec, "internal: unfused RMSNorm without a decode GEMV");
                 // SwiGLU consumer folded into the matmul epilogue: decode, and prefill whose gate
                 // and up halves split into the block GEMM's 64-unit tiles
-                const bool pre = is_quant(qw->type) && !last_only && !xin.virt_rms &&
+                const bool pre = is_quant(qw->type) && !last_only && !sel_rows && !xin.virt_rms &&
                                  Mrun > kMmvMaxRows && N % 128 == 0;
                 int swi_op = -1;
                 if ((dec || pre) && !bias && add_op < 0 && !outputs.count(out) &&
@@ -1077,8 +1087,38 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                 }
                 const BufRef yr = y.ref;
                 const int64_t ystride = N;
+                // the selected rows gathered into a compact f32 block first
+                Val xsel;
+                if (sel_rows) {
+                    pg.out_rows_of = pg.out_rows_of ? std::min(pg.out_rows_of, M) : M;
+                    GB_CHECK(xin.has_f, "output-row matmul needs f32 input");
+                    Val x = xin;
+                    if (!(x.nb[0] == 4 && x.rows_uniform())) x = cont(x, oi);
+                    xsel.type = T_F32;
+                    xsel.ne[0] = K;
+                    xsel.ne[1] = n_sel;
+                    alloc(xsel, oi);
+                    pg.use(x.ref, oi);
+                    const BufRef src = x.ref, dst = xsel.ref;
+                    const int64_t xs = x.nb[1] / 4;
+                    const int n = (int)n_sel;
+                    StepParams* const dstep = d_step_;
+                    add("gather_rows", [=](Program& p, cudaStream_t st) {
+                        launch_gather_rows((const float*)p.ptr(src), xs, dstep, n, K,
+                                           (float*)p.ptr(dst), st);
+                    });
+                }
                 if (is_quant(qw->type)) {
-                    if (last_only) {
+                    if (sel_rows) {
+                        ensure_q(xsel, oi);
+                        const BufRef qb = xsel.q, qdb = xsel.qd;
+                        add("gemm_q", [=](Program& p, cudaStream_t st) {
+                            MatmulEpilogue e = ep;
+                            launch_matmul_q(*qw, (const int8_t*)p.ptr(qb),
+                                            (const float*)p.ptr(qdb), Mrun, (float*)p.ptr(yr),
+                                            ystride, e, st);
+                        }, mm_bytes(qw, Mrun, false));
+                    } else if (last_only) {
                         // quantize only the last row (the CPU path quantizes the gathered row)
                         GB_CHECK(xin.has_f, "last-token matmul needs f32 input");
                         Val xl = xin;
@@ -1109,11 +1149,11 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         }, mm_bytes(qw, Mrun, add_op >= 0));
                     }
                 } else {
-                    Val x = xin;
+                    Val x = sel_rows ? xsel : xin;
                     if (!(x.nb[0] == 4 && x.rows_uniform())) x = cont(x, oi);
                     const BufRef xr = x.ref;
                     const int64_t xs = x.nb[1] / 4;
-                    const int64_t off = row0 * x.nb[1];
+                    const int64_t off = last_only ? row0 * x.nb[1] : 0;
                     add("matmul_f", [=](Program& p, cudaStream_t st) {
                         MatmulEpilogue e = ep;
                         if (rref.fixed || rref.buf >= 0) e.residual = (const float*)p.ptr(rref);
@@ -1705,6 +1745,7 @@ void Executor::prepare(const SymEnv& env_in, bool /*arena_reuse*/) {
     // the program key: every symbol except pos (kernels read pos from StepParams)
     std::string key = kv ? "kv" : "plain";
     if (logits_last_only_) key += "/last";
+    if (!out_rows_.empty()) key += "/rows=" + std::to_string(out_rows_.size());
     SymEnv shape_env;
     for (auto& [k, v] : env)
         if (k != "pos" && k != "slot") shape_env[k] = v;
@@ -1736,6 +1777,15 @@ void Executor::prepare(const SymEnv& env_in, bool /*arena_reuse*/) {
         active_ = it->second;
     }
     h_step_->pos = pos;
+    if (!out_rows_.empty() && active_->out_rows_of > 0) {
+        const int64_t s = active_->out_rows_of;
+        for (size_t r = 0; r < out_rows_.size(); ++r) {
+            GB_CHECK(out_rows_[r] >= 0 && out_rows_[r] < s,
+                     "output row " + std::to_string(out_rows_[r]) + " is not among the call's " +
+                         std::to_string(s) + " tokens");
+            h_step_->out_rows[r] = out_rows_[r];
+        }
+    }
     active_->kv_slot = env.count("slot") ? env.at("slot") : 0;
     if (profile_on_) {
         profile_.prepare_ms += now_ms() - t0;

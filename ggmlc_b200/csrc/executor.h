@@ -70,6 +70,7 @@ struct Program {
     bool kv = false;
     bool decode = false;
     bool batch = false;  // batched decode: row r is the next token of the sequence in a slot
+    int64_t out_rows_of = 0;  // rows the output projections select from (out_rows), 0: none
     std::vector<int64_t> buf_size, buf_first, buf_last, buf_off;
     char* const* arena = nullptr;  // the executor's shared activation arena (grows on demand)
     size_t arena_bytes = 0;
@@ -174,6 +175,12 @@ public:
     void prepare_batch(int rows, const int32_t* pos, const int32_t* slot);
     int64_t kv_max_ctx() const { return kv_max_ctx_; }
 
+    // Output rows (llama's out_ids; the reference's set_logits_last_only generalised): when set,
+    // a prefill's output projections compute only these rows of the call's tokens, in this
+    // order (at most kMaxOutRows, each below the call's token count); empty turns it off.  Takes
+    // precedence over logits_last_only.
+    void set_output_rows(const std::vector<int32_t>& rows);
+    const std::vector<int32_t>& output_rows() const { return out_rows_; }
     void set_logits_last_only(bool on) { logits_last_only_ = on; }
     bool logits_last_only() const { return logits_last_only_; }
     void set_enable_cuda_graph(bool on) { cuda_graph_ = on; }
@@ -252,6 +259,7 @@ private:
     void alloc_kv(int64_t slots, int64_t max_ctx);
     void free_kv();
     bool logits_last_only_ = false;
+    std::vector<int32_t> out_rows_;
     bool cuda_graph_ = false;
     bool profile_on_ = false;
     Profile profile_;

@@ -66,6 +66,13 @@ __global__ void k_copy(TView s, TView d) {
     }
 }
 
+__global__ void k_gather_rows(const float* __restrict__ x, int64_t x_stride,
+                              const StepParams* __restrict__ step, int64_t K, float* __restrict__ y) {
+    const int r = blockIdx.x;
+    const float* src = x + (int64_t)step->out_rows[r] * x_stride;
+    for (int64_t k = threadIdx.x; k < K; k += blockDim.x) y[(int64_t)r * K + k] = src[k];
+}
+
 unsigned grid_for(int64_t total) {
     int64_t b = (total + 255) / 256;
     if (b > 148 * 32) b = 148 * 32;
@@ -80,6 +87,13 @@ void launch_binary(const TView& a, const TView& b, const TView& dst, int op, cud
     for (int k = 0; k < 4; ++k)
         GB_CHECK(b.ne[k] > 0 && a.ne[k] % b.ne[k] == 0, "binary op: operand cannot be broadcast");
     k_binary<<<grid_for(total), 256, 0, st>>>(a, b, dst, op);
+    GB_CUDA(cudaGetLastError());
+}
+
+void launch_gather_rows(const float* x, int64_t x_stride, const StepParams* step, int n, int64_t K,
+                        float* y, cudaStream_t st) {
+    GB_CHECK(n >= 1 && n <= kMaxOutRows, "gather rows: 1..64 rows");
+    k_gather_rows<<<(unsigned)n, 256, 0, st>>>(x, x_stride, step, K, y);
     GB_CUDA(cudaGetLastError());
 }
 

@@ -23,10 +23,12 @@ namespace gb {
 
 // Per-step values read by kernels inside captured graphs (decode replays change only these).
 constexpr int kMaxRows = 16;  // rows of a batched decode step (sequences decoded together)
+constexpr int kMaxOutRows = 64;  // rows an output projection can be restricted to (out_rows)
 struct StepParams {
     int64_t pos;                  // first position of this call's tokens in the KV cache
     int32_t row_pos[kMaxRows];    // batched decode: position of each row's token
     int32_t row_slot[kMaxRows];   // batched decode: KV-cache slot of each row's sequence
+    int32_t out_rows[kMaxOutRows];  // rows of this call whose outputs are computed (out_rows)
 };
 
 __host__ __device__ inline int64_t quant_bytes(int type) { return type == 8 ? 32 : 16; }
@@ -176,6 +178,9 @@ struct TView {
 void launch_binary(const TView& a, const TView& b, const TView& dst, int op, cudaStream_t st);
 // dst = src (any strides, f32/f16/i32 with conversion to dst type).
 void launch_copy(const TView& src, const TView& dst, cudaStream_t st);
+// y[r][:] = x[step->out_rows[r]][:] for r < n (f32 rows of K, x rows x_stride floats apart)
+void launch_gather_rows(const float* x, int64_t x_stride, const StepParams* step, int n, int64_t K,
+                        float* y, cudaStream_t st);
 
 // ---- RoPE / KV cache / attention ---------------------------------------------------------------
 // NEOX RoPE.  x: f32 view [hd, H, s] (ne0 contiguous); positions = pos_src[pos_off + i] where

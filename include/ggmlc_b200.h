@@ -106,6 +106,12 @@ int gb_executor_reset_kv_cache(gb_executor* e);
 int gb_executor_has_kv_cache(const gb_executor* e);
 /* set_logits_last_only / logits_last_only — executor.cpp:2398-2410 */
 int gb_executor_set_logits_last_only(gb_executor* e, int enable);
+/* Output rows (the per-request output indices of the reference's doc gap 3, "Multi-request
+ * outputs", docs/benchmarks/ggmlc_vs_llama_cpp.md:195; llama's out_ids): the next prefills
+ * compute their output projections for rows[0..n) of the call's tokens only, in that order
+ * (n <= 64, each below the call's token count, checked at prepare); logits come back as
+ * [n][vocab].  n = 0 turns it off.  Takes precedence over set_logits_last_only. */
+int gb_executor_set_output_rows(gb_executor* e, const int32_t* rows, int n);
 int gb_executor_logits_last_only(const gb_executor* e);
 /* set_enable_cuda_graph / is_cuda_graph_enabled / is_cuda_graph_captured — cuda_graph.cu */
 int gb_executor_set_enable_cuda_graph(gb_executor* e, int enable);

@@ -151,3 +151,34 @@ def test_errors_are_raised_not_crashing():
     r.executor.prepare({"s": 4, "s70": 4})
     with pytest.raises(RuntimeError, match="size mismatch"):
         r.executor.set_input_by_id(r.inputs[0], np.zeros(3, np.int32))
+
+
+@pytest.mark.parametrize("fixture", FIXTURES)
+def test_output_rows_select_prompt_logits(fixture):
+    """Output rows (the per-request output indices of the reference's doc gap 3; llama's
+    out_ids): a full prompt forward restricted to chosen rows returns exactly those rows of the
+    reference's logits (cosine and argmax bar), in the order asked; the last row alone is
+    bit-identical to the last-row mode, and clearing the rows restores full logits."""
+    gold = np.load(GOLDEN / f"{fixture}.npz")
+    ref = gold["full_logits"]
+    n, V = ref.shape
+    r = _runner(fixture)
+    rows = [n - 1, 0, n // 2, 3]
+    r.executor.set_output_rows(rows)
+    out = np.asarray(r(*_args(r, gold["prompt"], 0))).reshape(-1, V)
+    assert out.shape == (len(rows), V)
+    assert cos(out, ref[rows]) >= COS_MIN
+    ok, n_diff, n_clear = argmax_agrees(out, ref[rows])
+    assert ok, f"{n_diff} argmax differences among {n_clear} clear rows"
+    r.executor.set_output_rows([n - 1])
+    one = np.asarray(r(*_args(r, gold["prompt"], 0))).reshape(-1)
+    r.executor.set_output_rows(None)
+    r.executor.set_logits_last_only(True)
+    last = np.asarray(r(*_args(r, gold["prompt"], 0))).reshape(-1)
+    assert np.array_equal(one, last)
+    r.executor.set_logits_last_only(False)
+    full = np.asarray(r(*_args(r, gold["prompt"], 0))).reshape(-1, V)
+    assert full.shape == ref.shape
+    with pytest.raises(RuntimeError, match="not among"):
+        r.executor.set_output_rows([n])
+        r(*_args(r, gold["prompt"], 0))
