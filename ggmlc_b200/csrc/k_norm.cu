@@ -208,7 +208,9 @@ void launch_rms_norm(const float* x, int64_t x_stride, int64_t M, int64_t D, flo
     check_row_smem(D);
     GB_CHECK(!yq || D % QK == 0, "rms_norm: quantized output needs D % 32 == 0");
     set_smem(k_rms_norm);
-    launch_pdl(k_rms_norm, dim3((unsigned)M), dim3(kRowThreads), (size_t)(D * 4), st, x, x_stride, D,
+    // a batched decode step normalizes at most 16 rows: a wide CTA per row shortens the chain
+    const unsigned threads = M <= kMaxRows ? 1024 : kRowThreads;
+    launch_pdl(k_rms_norm, dim3((unsigned)M), dim3(threads), (size_t)(D * 4), st, x, x_stride, D,
                eps, gamma, y, y_stride, yq, yd);
 }
 
