@@ -360,11 +360,51 @@ __global__ void __launch_bounds__(kTcWarps * 32) k_attn_decode_tc(AttnDecArgs a)
     pdl_launch();
 
     const float* qrow = a.qkv + (int64_t)row * a.qkv_stride;
-    for (int e = threadIdx.x; e < 16 * HD; e += kTcWarps * 32) {
-        const int h = e / HD, d = e % HD;
-        float v = 0.0f;
-        if (h < rk) v = rope_elem(qrow + a.q_off + (int64_t)(hk * rk + h) * HD, d, HD, a.tab, pos);
-        *(__half*)(sq + h * R + d * 2) = __float2half_rn(v);
+    {
+        // rotated q heads (rope_elem's arithmetic): every load of this thread's elements is
+        // issued before the first is used, so the rotation costs one round trip; rows >= rk zero
+        constexpr int NT = kTcWarps * 32;
+        constexpr int NE = kMaxRk * HD / NT;
+        const int half = a.tab.n_dims / 2;
+        const bool tab = a.tab.cs && pos >= 0 && pos < a.tab.n_pos;
+        float x0[NE], x1[NE];
+        float2 cs[NE];
+#pragma unroll
+        for (int k = 0; k < NE; ++k) {
+            const int e = threadIdx.x + k * NT, h = e / HD, d = e % HD;
+            x0[k] = x1[k] = 0.0f;
+            cs[k] = make_float2(1.0f, 0.0f);
+            if (h < rk) {
+                const float* src = qrow + a.q_off + (int64_t)(hk * rk + h) * HD;
+                if (d >= a.tab.n_dims) {
+                    x0[k] = src[d];
+                } else {
+                    const int i = d < half ? d : d - half;
+                    x0[k] = src[i];
+                    x1[k] = src[i + half];
+                    if (tab) cs[k] = a.tab.cs[pos * half + i];
+                }
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < NE; ++k) {
+            const int e = threadIdx.x + k * NT, h = e / HD, d = e % HD;
+            float v = 0.0f;
+            if (h < rk) {
+                if (d >= a.tab.n_dims) {
+                    v = x0[k];
+                } else {
+                    const int i = d < half ? d : d - half;
+                    float c = cs[k].x, sn = cs[k].y;
+                    if (!tab) rope_cs(a.tab, pos, i, c, sn);
+                    v = d < half ? __fmaf_rn(x0[k], c, -__fmul_rn(x1[k], sn))
+                                 : __fmaf_rn(x0[k], sn, __fmul_rn(x1[k], c));
+                }
+            }
+            *(__half*)(sq + h * R + d * 2) = __float2half_rn(v);
+        }
+        for (int e = kMaxRk * HD + threadIdx.x; e < 16 * HD; e += NT)
+            *(__half*)(sq + (e / HD) * R + (e % HD) * 2) = __float2half_rn(0.0f);
     }
     const bool has_new = c0 <= pos && pos < c1;
     if (has_new) {
