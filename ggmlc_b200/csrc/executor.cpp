@@ -857,7 +857,7 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                 const bool rms_op = op.opcode == OP_RMS_NORM_C || op.opcode == OP_RMS_NORM;
                 const bool fits = M >= 1 && gemv_fits(T_Q8_0, D, (int)M, true, gamma) &&
                                   gemv_fits(T_Q4_0, D, (int)M, true, gamma);
-                if (rms_op && !nf && nq && M <= kGemvMaxRows && fits) {
+                if (rms_op && !nf && nq && M <= kGemvRouteRows && fits) {
                     // decode: every consumer is a quantized GEMV that normalizes in its prologue
                     o.has_f = false;
                     o.virt_rms = true;
@@ -944,7 +944,7 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                 // decode (M <= 16): SwiGLU / residual epilogue fused into the matmul launch; an
                 // unmaterialized RMSNorm input (M <= 4) is normalized in the GEMV prologue
                 bool dec = is_quant(qw->type) && !last_only && !sel_rows &&
-                           (xin.virt_rms ? Mrun <= kGemvMaxRows && gemv_fused_fits(K, (int)Mrun)
+                           (xin.virt_rms ? Mrun <= kGemvRouteRows && gemv_fused_fits(K, (int)Mrun)
                                          : Mrun <= kMmvMaxRows);
                 GB_CHECK(!xin.virt_rms || dec, "internal: unfused RMSNorm without a decode GEMV");
                 // SwiGLU consumer folded into the matmul epilogue: decode, and prefill whose gate
@@ -1001,7 +1001,7 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         const BufRef hr = h.ref, hq = h.q, hqd = h.qd;
                         const bool hf = h.has_f, hhq = h.has_q;
                         add(virt ? "gemv_rms_swiglu"
-                                 : (Mrun <= kGemvMaxRows ? "gemv_swiglu"
+                                 : (Mrun <= kGemvRouteRows ? "gemv_swiglu"
                                                          : (Mrun <= kMmvMaxRows ? "mmv_swiglu" : "gemm_swiglu")), [=](Program& p, cudaStream_t st) {
                             GemvArgs a = ga;
                             if (virt) {
@@ -1042,7 +1042,7 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         pg.use(res.ref, add_op);
                     }
                     const BufRef yr = y.ref;
-                    add(virt ? "gemv_rms" : (Mrun <= kGemvMaxRows ? (add_op >= 0 ? "gemv_res" : "gemv") : (add_op >= 0 ? "mmv_res" : "mmv")), [=](Program& p, cudaStream_t st) {
+                    add(virt ? "gemv_rms" : (Mrun <= kGemvRouteRows ? (add_op >= 0 ? "gemv_res" : "gemv") : (add_op >= 0 ? "mmv_res" : "mmv")), [=](Program& p, cudaStream_t st) {
                         GemvArgs a = ga;
                         if (virt) {
                             a.xf = (const float*)p.ptr(xr);

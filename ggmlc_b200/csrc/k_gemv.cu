@@ -1,4 +1,4 @@
-// Decode GEMV (M <= 4 activation rows) over the split-row weight layout, with an optional fused
+// Decode GEMV (M <= 4 activation rows; the engine sends it 1-2) over the split-row weight layout, with an optional fused
 // RMSNorm + Q8_0 prologue and a bias / residual / SwiGLU epilogue.
 //
 // Arithmetic.  Per 32-element block the integer dot sumi = sum q_w * q_x is exact (dp4a chain),
@@ -479,7 +479,7 @@ void launch_gemv_fused(const GemvArgs& a, cudaStream_t st) {
         }
         return;
     }
-    if (!a.xf && (a.M > kGemvMaxRows || !gemv_fits(a.w.type, a.w.K, a.M, false, false))) {
+    if (!a.xf && (a.M > kGemvRouteRows || !gemv_fits(a.w.type, a.w.K, a.M, false, false))) {
         launch_mmv(a, st);  // batched decode: the tensor-core kernel
         return;
     }

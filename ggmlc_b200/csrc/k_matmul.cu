@@ -1,6 +1,6 @@
 // Quantized MUL_MAT kernels over the split-row weight layout (kernels.h).
 //
-// M <= 16 (decode and batched decode) goes to the GEMV (k_gemv.cu, M <= 4) or the tensor-core
+// M <= 16 (decode and batched decode) goes to the GEMV (k_gemv.cu, M <= 2) or the tensor-core
 // decode kernel (k_mmv.cu).
 //
 // k_gemm_q (M > 16, prefill): int8 tensor-core tiles (mma m16n8k32, one instruction per

@@ -74,7 +74,7 @@ void launch_get_rows(const QWeight& w, const int32_t* ids, int64_t n, float* out
 // Y[m][n] = sum_k X[m][k] W[n][k] (+ bias[n]) (+ residual[m][n]) for Q8_0/Q4_0 W and Q8_0 X.
 // Per 32-element block the int32 dot is exact; block terms sumi * (d_w * d_x) accumulate in fp32
 // (the reference's generic block formula; the x86 lane order differs only in rounding).
-// M <= 4 runs the decode GEMV, M <= 16 the tensor-core decode kernel, larger M the block GEMM.
+// M <= 2 runs the decode GEMV, M <= 16 the tensor-core decode kernel, larger M the block GEMM.
 struct MatmulEpilogue {
     const float* bias = nullptr;      // [N] or null
     const float* residual = nullptr;  // [M][res_stride] or null
@@ -82,9 +82,11 @@ struct MatmulEpilogue {
 };
 void launch_matmul_q(const QWeight& w, const int8_t* xq, const float* xd, int64_t M, float* y,
                      int64_t y_stride, const MatmulEpilogue& ep, cudaStream_t st);
-// Decode GEMV with fused prologue / epilogue (M <= kGemvMaxRows; Q8_0 input with more rows goes
-// to launch_mmv, and past 16 rows to the block GEMM with the same epilogues).  Lanes run along K, so each row costs a fixed number of instructions per weight
-// byte; up to 4 rows this beats the tensor-core kernel, whose 16x8 tiles are mostly idle there.
+// Decode GEMV with fused prologue / epilogue (M <= kGemvMaxRows).  Q8_0 input with more than
+// kGemvRouteRows rows goes to launch_mmv, and past 16 rows to the block GEMM, with the same
+// epilogues.  Lanes run along K, so each row costs a fixed number of instructions per weight
+// byte; for 1-2 rows this beats the tensor-core kernel, whose 16x8 tiles are mostly idle there
+// (at 3-4 rows the tensor-core kernel fed by the standalone RMSNorm is the faster step).
 // Launched as a programmatic dependent launch: its weight loads start before the previous kernel
 // on the stream has finished.
 //   input : Q8_0 rows (xq, xd; xq 16-byte aligned), or f32 rows xf quantized to Q8_0 in shared
@@ -93,6 +95,7 @@ void launch_matmul_q(const QWeight& w, const int8_t* xq, const float* xd, int64_
 //   output: f32 rows y (+bias, +residual), or SwiGLU of row pairs (gate n, up n+F) emitted as
 //           Q8_0 rows (yq, yd) and/or f32 rows (y) of length F — exactly launch_swiglu.
 constexpr int kGemvMaxRows = 4;
+constexpr int kGemvRouteRows = 2;  // rows the engine sends to the GEMV (fused RMSNorm included)
 struct GemvArgs {
     QWeight w;
     int M = 1;

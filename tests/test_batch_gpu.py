@@ -1,9 +1,9 @@
 """Continuous batching over the paged KV cache (the reference's ContinuousBatchScheduler,
 runtime/src/batch_scheduler.cpp:130-403, and its e2e test tests/e2e/test_continuous_batching.py).
 
-Every sequence in a batched step decodes at its own position in its own slot.  Steps of up to 4
+Every sequence in a batched step decodes at its own position in its own slot.  Steps of up to 2
 rows run the decode GEMV, whose per-row arithmetic does not depend on the row count, so with at
-most 4 slots a request's tokens equal the same prompt decoded alone.  5-16 rows run the
+most 2 slots a request's tokens equal the same prompt decoded alone.  3-16 rows run the
 tensor-core decode kernel (its rows are batch-invariant among themselves but summed in another
 order than the GEMV's): those requests are checked teacher-forced against single-sequence decode,
 token by token wherever the single-sequence top-2 gap exceeds 1% of the logit range."""
@@ -116,7 +116,7 @@ def test_scheduler_tokens_match_single_sequence_decode(fixture):
     rng = np.random.default_rng(11)
     vocab = int(np.load(GOLDEN / f"{fixture}.npz")["full_logits"].shape[1])
     prompts = _prompts(rng, [5, 17, 33, 9, 40, 3], vocab)
-    for p, toks in zip(prompts, _serve(fixture, prompts, 10, 4)):
+    for p, toks in zip(prompts, _serve(fixture, prompts, 10, 2)):
         ref, _ = _single(fixture, p, 10)
         assert toks == ref, f"prompt {len(p)}"
 

@@ -181,8 +181,8 @@ def test_prefill_gemm_tile_variants(G, wtype, M):
 @pytest.mark.parametrize("K", [576, 4096, 14336])
 def test_decode_rows_independent_of_batch(G, wtype, K):
     """A row's decode-matmul result is bit-identical whatever rows run with it, with the
-    residual and with the SwiGLU epilogue, within each decode kernel: the GEMV (1-4 rows) and
-    the tensor-core kernel (5-16 rows).  Continuous batching thus returns a sequence's own
+    residual and with the SwiGLU epilogue, within each decode kernel: the GEMV (1-2 rows) and
+    the tensor-core kernel (3-16 rows).  Continuous batching thus returns a sequence's own
     logits whatever batch of the same kernel it joins."""
     torch = G.torch_dev()
     rng = np.random.default_rng(K + wtype)
@@ -220,13 +220,13 @@ def test_decode_rows_independent_of_batch(G, wtype, K):
                     assert torch.equal(got[i], ref), f"M={M} row {r}"
 
     alone = [tuple(t[0] for t in run([r])) for r in range(16)]
-    check(alone, (2, 3, 4))
+    check(alone, (2,))
     by8 = [None] * 16
     for b in range(2):
         outs = run(list(range(8 * b, 8 * b + 8)))
         for i in range(8):
             by8[8 * b + i] = tuple(t[i] for t in outs)
-    check(by8, (5, 11, 16))
+    check(by8, (3, 4, 5, 11, 16))
     ref = O.mul_mat(wtype, w, N, K, x)
     for base in (alone, by8):
         got = np.stack([b[0].cpu().numpy() for b in base]) - res
