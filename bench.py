@@ -437,7 +437,7 @@ def run_cb(g, gguf, local: int, steps: int = 256, buckets=(1, 2, 4, 8, 16)) -> d
 
 
 def run_prefix(ex, n_req: int = 8, shared_len: int = 512, tail: int = 64) -> dict:
-    """Prefix caching: n_req requests sharing a shared_len-token prompt prefix
+    """Prefix caching (prompt pages reused across requests): n_req requests sharing a shared_len-token prompt prefix
     (two 256-token pages) with distinct tails, admitted in one scheduler step after a first
     request with the same prefix has been served; that admission step's time with the cache off
     and on."""

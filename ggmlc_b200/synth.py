@@ -45,7 +45,7 @@ class LlamaShape:
 
 
 SHAPES = {
-    # BASELINE.json configs
+    # the shapes of the benchmark configurations: SmolLM2-135M and Llama-3-8B
     "smollm2-135m": LlamaShape(30, 576, 9, 3, 64, 1536, 49152, 10000.0),
     "llama3-8b": LlamaShape(32, 4096, 32, 8, 128, 14336, 128256, 500000.0),
     "llama3-70b": LlamaShape(80, 8192, 64, 8, 128, 28672, 128256, 500000.0),
