@@ -138,10 +138,14 @@ def _dim(v) -> dict:
 
 def rope_freq_base(theta: float, head_dim: int) -> float:
     """freq_base as the fusion pass recovers it from the wrapper's inv_freq buffer
-    (fusion.py:322: (1/inv_freq[1]) ** (n_dims/2) in float32)."""
-    inv = np.float32(1.0) / np.power(np.float32(theta),
-                                     np.arange(0, head_dim, 2, dtype=np.float32) / np.float32(head_dim))
-    inv = inv.astype(np.float32)
+    (fusion.py:322: (1/inv_freq[1]) ** (n_dims/2) in float32).  The buffer is built with torch's
+    float32 pow, as the wrapper builds it (examples/models/hub_models.py:303): numpy's float32
+    power differs from it by an ulp at theta 500000, which the recovery's power of n_dims/2
+    turns into a freq_base about 1.25 apart."""
+    import torch
+
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim))
+    inv = inv.numpy().astype(np.float32)
     return float(np.power(np.float32(1.0) / inv[1], np.float32(head_dim / 2.0)))
 
 
