@@ -14,7 +14,10 @@ projection sharded, two NCCL all-reduces per layer), or with --replicas N indepe
 (weak scaling); device time is the max over ranks.
 
 --impl reference times the reference's own CPU runtime (oracle/_ref/ggmlc-bench, built from the
-reference sources) on the same synthesized GGUF, all host threads, a bounded tg sample per step.
+reference sources) on the same synthesized GGUF with all host threads: its `-pg 512,128` test,
+prefill then 128 decode tokens at positions 512..639, the workload of this arm's `value`.  This
+arm's `cpu_baseline` is one repetition of the same, and `parity` compares this engine with that
+reference run on the same GGUF and prompt (logits cosine, greedy tokens).
 """
 
 from __future__ import annotations
@@ -36,6 +39,7 @@ METRIC = "tokens/s pp512 & tg128 (Q4_0/Q8_0) per GPU and TP; % of HBM/INT8 roofl
 FALLBACK_HBM_GBS = 6650.0
 BENCH_DIR = Path(os.environ.get("GGMLC_B200_BENCH_DIR", "/tmp/ggmlc_b200_bench"))
 REF_BENCH = ROOT / "oracle" / "_ref" / "ggmlc-bench"
+REF_BUILD = "reference CPU build: oracle/Makefile, -O3 -march=x86-64-v3 (AVX2/FMA/F16C)"
 
 
 def peaks() -> tuple[float, str]:
@@ -123,60 +127,122 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(rows)}
 
 
-def cpu_baseline(gguf: Path, n_gen: int = 8) -> dict | None:
-    """The reference CPU runtime (ggmlc-bench built from the reference sources) on a bounded
-    tg sample of the same model."""
+def ref_pg(gguf: Path, P: int, G: int, reps: int) -> dict:
+    """The reference's own harness (ggmlc-bench, built from the reference sources) on the CPU,
+    all host threads, test `-pg P,G`: prefill P tokens, then G decode tokens at positions
+    P..P+G-1 (ggmlc_bench.cpp:566-705).  Returns pp tokens/s (P / ttft), tg tokens/s (G /
+    decode time, the decode at depth P that `value` measures) and the run's wall time."""
+    cores = host_threads()
+    cmd = [str(REF_BENCH), "-m", str(gguf), "-d", "cpu", "-t", str(cores), "-p", "0", "-n", "0",
+           "-pg", f"{P},{G}", "-r", str(reps), "-o", "json"]
+    t0 = time.time()
+    r = subprocess.run(cmd, capture_output=True, text=True, timeout=1800)
+    wall = time.time() - t0
+    if r.returncode != 0:
+        raise RuntimeError(f"ggmlc-bench rc={r.returncode}: {r.stderr[-300:]}")
+    rows = json.loads(r.stdout[r.stdout.index("["):])
+    pg = [x for x in rows if x.get("n_prompt") == P and x.get("n_gen") == G][0]
+    return {"tg": G / (float(pg["decode_ms"]) / 1e3), "pp": P / (float(pg["ttft_ms"]) / 1e3),
+            "pg": float(pg["avg_ts"]), "cores": cores, "wall_s": wall, "reps": reps,
+            "cmd": " ".join(["ggmlc-bench"] + cmd[1:2] + ["<gguf>"] + cmd[3:])}
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:  # noqa: BLE001
+        return os.cpu_count() or 1
+
+
+def cpu_baseline(gguf: Path, P: int, G: int) -> dict | None:
+    """The reference CPU runtime on one bounded sample of the same workload (pp P + tg G at
+    depth P, one repetition after the harness's own warm-up)."""
     if not REF_BENCH.exists():
         return {"value": None, "unit": "tokens/s", "cores": 0, "kind": "reference",
                 "sample": f"unavailable: {REF_BENCH.name} not built"}
-    cores = os.cpu_count() or 1
-    cmd = [str(REF_BENCH), "-m", str(gguf), "-d", "cpu", "-t", str(cores), "-p", "0", "-n",
-           str(n_gen), "-r", "1", "-o", "json", "--no-warmup"]
-    t0 = time.time()
-    r = subprocess.run(cmd, capture_output=True, text=True, timeout=900)
-    wall = time.time() - t0
     try:
-        rows = json.loads(r.stdout[r.stdout.index("["):])
-        tg = [x for x in rows if x.get("n_gen", 0) > 0][0]
-        return {"value": float(tg["avg_ts"]), "unit": "tokens/s", "cores": cores,
-                "kind": "reference",
-                "sample": f"ggmlc-bench -d cpu -t {cores} tg{n_gen} after one untimed token "
-                          f"(same GGUF; {wall:.0f} s wall incl. load)"}
+        r = ref_pg(gguf, P, G, 1)
     except Exception as e:  # noqa: BLE001
-        return {"value": None, "unit": "tokens/s", "cores": cores, "kind": "reference",
-                "sample": f"failed: {e}; {r.stderr[-200:]}"}
+        return {"value": None, "unit": "tokens/s", "cores": host_threads(), "kind": "reference",
+                "sample": f"failed: {str(e)[:200]}"}
+    return {"value": round(r["tg"], 2), "unit": "tokens/s", "cores": r["cores"],
+            "kind": "reference", "pp512_tokens_per_s": round(r["pp"], 1),
+            "sample": f"{r['cmd']} (same GGUF, {REF_BUILD}; tg{G} at positions {P}..{P + G - 1}; "
+                      f"{r['wall_s']:.0f} s wall incl. load and warm-up)"}
+
+
+def reference_parity(gguf: Path, ex, in_id: int, out_id: int, sym: str, V: int, P: int,
+                     G: int = 16) -> dict:
+    """Checker: the reference CPU runtime (oracle/_ref) and this engine on the same GGUF and
+    the same seeded prompt of P tokens, then G greedy steps.  Logits cosine per row (the engine
+    teacher-forced with the reference's tokens) and whether the free-running greedy tokens are
+    identical."""
+    from oracle import refrun
+
+    if not refrun.available():
+        return {"unavailable": "oracle/_ref not built"}
+    prompt = np.random.default_rng(11).integers(0, V, size=P).astype(np.int32)
+    t0 = time.time()
+    ref = refrun.RefRunner(gguf, V, max_ctx=P + G + 256)
+    ref_toks, ref_rows = ref.greedy(prompt, G)
+    ref.close()
+    t_ref = time.time() - t0
+
+    def run(teacher):
+        ex.prepare({"s": P, sym: P, "pos": 0})
+        ex.set_input_by_id(in_id, prompt)
+        ex.run()
+        rows = [np.asarray(ex.get_output_array(out_id), np.float32).reshape(-1)[-V:].copy()]
+        toks = [int(np.argmax(rows[0]))]
+        for i in range(G):
+            feed = toks[-1] if teacher is None else int(teacher[i])
+            ex.prepare({"s": 1, sym: 1, "pos": P + i})
+            ex.set_input_by_id(in_id, np.array([feed], np.int32))
+            ex.run()
+            rows.append(np.asarray(ex.get_output_array(out_id), np.float32).reshape(-1)[-V:].copy())
+            toks.append(int(np.argmax(rows[-1])))
+        return toks, np.stack(rows)
+
+    own, _ = run(None)
+    _, tf = run(ref_toks)
+    cs = [float(a.astype(np.float64) @ b / np.linalg.norm(a) / np.linalg.norm(b))
+          for a, b in zip(tf.astype(np.float64), ref_rows.astype(np.float64))]
+    return {"cosine_min": round(min(cs), 7), "tokens_equal": own == ref_toks,
+            "prompt": P, "greedy_steps": G, "ref_threads": ref.n_threads,
+            "ref_s": round(t_ref, 1)}
 
 
 def run_reference(args) -> None:
+    """The reference's own CPU implementation of the path on this box's host cores: its
+    ggmlc-bench on the same synthesized GGUF, test -pg 512,128 (prefill, then 128 decode tokens
+    at positions 512..639: the workload of this script's own `value`)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    gguf = ensure_model(args.model, args.quant, None if not _cuda() else "cuda:0")
-    cores = os.cpu_count() or 1
-    n_gen = args.ref_gen
-    cmd = [str(REF_BENCH), "-m", str(gguf), "-d", "cpu", "-t", str(cores), "-p", "0", "-n",
-           str(n_gen), "-r", str(args.steps), "-o", "json"]
     if not REF_BENCH.exists():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/ggmlc-bench not built "
                           "(make -C oracle needs the reference sources)"}))
         return
-    t0 = time.time()
-    r = subprocess.run(cmd, capture_output=True, text=True, timeout=1800)
-    wall = time.time() - t0
-    rows = json.loads(r.stdout[r.stdout.index("["):])
-    tg = [x for x in rows if x.get("n_gen", 0) > 0][0]
-    v = float(tg["avg_ts"])
+    gguf = ensure_model(args.model, args.quant, None if not _cuda() else "cuda:0")
+    P, G = args.prompt, args.gen
+    reps = max(1, min(args.steps, args.ref_reps))
+    r = ref_pg(gguf, P, G, reps)
+    v = round(r["tg"], 2)
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": float(tg["avg_ms"]),
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round((P / r["pp"] + G / r["tg"]) * 1e3, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "q4_0 x q8_0 int8 dot, fp32 accumulate (CPU)",
+        "dtype": f"{args.quant} x q8_0 int8 dot, fp32 accumulate (CPU)",
         "data": "synthetic: seeded N(0,0.02) random-init weights, dummy token ids",
-        "config": {"workload": f"{args.model} {args.quant} tg (decode) B=1, reference CPU runtime",
-                   "model": args.model, "quant": args.quant, "gen_per_step": n_gen, "batch": 1},
-        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "reference",
-                         "sample": f"ggmlc-bench -d cpu -t {cores} -p 0 -n {n_gen} -r {args.steps} "
-                                   f"({wall:.0f} s wall)"},
+        "config": {"workload": f"{args.model} {args.quant} pp{P}+tg{G} B=1 (BASELINE configs[3])",
+                   "model": args.model, "quant": args.quant, "prompt": P, "gen": G, "batch": 1,
+                   "value_is": f"tg{G} decode tokens/s at positions {P}..{P + G - 1}"},
+        "pp512": {"value": round(r["pp"], 1), "unit": "tokens/s"},
+        "pg": {"value": round(r["pg"], 1), "unit": "tokens/s", "test": f"pp{P}+tg{G}"},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": r["cores"], "kind": "reference",
+                         "sample": f"{r['cmd']} ({REF_BUILD}; {r['wall_s']:.0f} s wall; "
+                                   f"repetitions = min(steps, {args.ref_reps}))"},
         "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
@@ -315,31 +381,30 @@ def run_ours(args) -> None:
         e2e_pp_ms, e2e_tg_ms = [float(x) for x in t.cpu()]
     e2e_tg = seqs * args.steps * G / (e2e_tg_ms / 1e3)
 
-    # roofline of the dominant decode kernel (Q4_0 GEMV): per-launch events over one sequence
+    # prefill kernels by device time: events around every launch of one prefill (launches of
+    # 0.1-1 ms, where the events cost little)
     ex.set_kernel_timing(True)
     ex.reset_kernel_times()
-    for i in range(G):
-        decode(P + i)
-    kt = ex.kernel_times()
-    ex.set_kernel_timing(False)
-    ex.reset_kernel_times()
-    prefill(False)
-    ex.set_kernel_timing(True)
     prefill(False)
     kt_pp = ex.kernel_times()
     ex.set_kernel_timing(False)
-    peak, peak_kind = peaks()
-    # dominant decode kernel by device time; its algorithmic bytes per launch (weights + Q8_0
-    # activations + outputs) over its mean launch duration
-    dom = max(kt.items(), key=lambda x: x[1][0])[0] if kt else "gemv_rms_swiglu"
-    mm = kt.get(dom, [0, 1, 0])
-    achieved = mm[2] / (mm[0] / 1e3) / 1e9 if mm[0] > 0 else 0.0
-    gemv_all = [v for k, v in kt.items() if k.startswith(("gemv", "mmv"))]
-    gemv_gbs = (sum(v[2] for v in gemv_all) / (sum(v[0] for v in gemv_all) / 1e3) / 1e9
-                if gemv_all else 0.0)
-    dec_total = sum(v[0] for v in kt.values())
-    shares = {k: round(v[0] / dec_total, 4) for k, v in sorted(kt.items(), key=lambda x: -x[1][0])}
-    pp_mm = [sum(v[i] for k, v in kt_pp.items() if k in ("gemm_q", "gemm_swiglu")) for i in range(3)]
+    pp_mm = [sum(v[i] for k, v in kt_pp.items() if k in ("gemm_q", "gemm_swiglu", "gemm_tc",
+                                                            "gemm_tc_swiglu")) for i in range(3)]
+    tp_err = ex.tp_allreduce_error() if tp else 0
+    if tp_err:
+        raise RuntimeError("tensor-parallel all-reduce reported a timed-out peer wait: the timed "
+                           "run's sums are not valid")
+    # the dominant decode kernel (the fused RMSNorm + gate_up + SwiGLU GEMV, half of a token's
+    # weight bytes) timed without per-launch events: back-to-back launches over 16 distinct
+    # weight matrices of its shape (1.06 GB, far above L2), chained by programmatic dependent
+    # launch as in the decode graph, one event pair around each pass
+    roof = gemv_roofline(local) if rank == 0 else None
+    parity = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            parity = reference_parity(gguf, ex, in_id, out_id, sym, vocab_of(g, ex, out_id), P)
+        except Exception as e:  # noqa: BLE001 - reported in the line
+            parity = {"error": str(e)[:300]}
 
     cb_line = None
     if not args.no_cb and not tp:
@@ -349,7 +414,7 @@ def run_ours(args) -> None:
         except Exception as e:  # noqa: BLE001 - reported in the line, the main metric stands
             cb_line = {"error": str(e)[:300]}
     if rank == 0:
-        cb = cpu_baseline(gguf) if (world == 1 and not args.no_cpu_baseline) else None
+        cb = cpu_baseline(gguf, P, G) if (world == 1 and not args.no_cpu_baseline) else None
         weights_gb = ex_weight_gb(g)
         line = {
             "metric": METRIC, "value": round(tg_tps, 2), "unit": "tokens/s", "n_gpus": world,
@@ -365,7 +430,8 @@ def run_ours(args) -> None:
                        "parallelism": (f"tp{world}" if tp else f"replicas x{world}") if world > 1
                        else "single",
                        "l2": f"inputs larger than L2: {weights_gb:.2f} GB of weights streamed per "
-                             "decode token", "value_is": f"tg{G} decode tokens/s"},
+                             "decode token",
+                       "value_is": f"tg{G} decode tokens/s at positions {P}..{P + G - 1}"},
             "pp512": {"value": round(pp_tps, 1), "unit": "tokens/s",
                       "ms": round(pp_ms / args.steps, 3),
                       "matmul_ms": round(pp_mm[0], 3),
@@ -373,17 +439,13 @@ def run_ours(args) -> None:
                                     sorted(kt_pp.items(), key=lambda x: -x[1][0])},
                       "matmul_int8_tops": round(pp_flops(args.model, P) / (pp_mm[0] / 1e3) / 1e12, 1)
                       if pp_mm[0] else None},
+            "pg": {"value": round(seqs * args.steps * (P + G) / (tot_ms / 1e3), 1),
+                   "unit": "tokens/s", "test": f"pp{P}+tg{G}"},
             "e2e": {"value": round(e2e_tg, 2), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h,
                     "pp512_tokens_per_s": round(seqs * args.steps * P / (e2e_pp_ms / 1e3), 1)},
-            "roofline": {"bound": "hbm", "kernel": dom,
-                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                         "traffic": profiled_traffic(dom),
-                         "bytes_per_launch": round(mm[2] / max(mm[1], 1)),
-                         "launch_ms": round(mm[0] / max(mm[1], 1), 5),
-                         "all_decode_gemv_gbs": round(gemv_gbs, 1),
-                         "decode_share": shares},
+            "roofline": roof,
+            "parity": parity,
             "cpu_baseline": cb,
             "continuous_batching": cb_line,
             "clocks": clk,
@@ -484,6 +546,90 @@ def pp_flops(model: str, P: int) -> float:
     per_layer = c.d_model * ((c.n_heads + 2 * c.n_kv_heads) * c.head_dim) + \
         c.n_heads * c.head_dim * c.d_model + c.d_model * 2 * c.ffn + c.ffn * c.d_model
     return 2.0 * P * c.n_layers * per_layer + 2.0 * c.vocab * c.d_model
+
+
+def vocab_of(g, ex, out_id) -> int:
+    return int(ex.get_tensor_shape(out_id)[0])
+
+
+def _q4_weights(L, dev, N: int, K: int, R: int, seed: int = 0):
+    """R distinct repacked Q4_0 [N, K] weight matrices of random valid blocks (device)."""
+    import ctypes
+
+    import torch
+
+    rng = np.random.default_rng(seed)
+    nb = K // 32
+    L.gb_weight_row_bytes.argtypes = [ctypes.c_int, ctypes.c_int64]
+    L.gb_weight_row_bytes.restype = ctypes.c_int64
+    L.gb_repack_blocks.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_int64,
+                                   ctypes.c_void_p, ctypes.c_void_p]
+    out = []
+    for _ in range(R):
+        blocks = torch.randint(0, 256, (N, nb, 18), dtype=torch.uint8, device=dev)
+        sc = (torch.randn((N, nb), device=dev) * 0.001).half().view(torch.uint8).reshape(N, nb, 2)
+        blocks[:, :, 0:2] = sc
+        wq = torch.empty(N * L.gb_weight_row_bytes(2, K), dtype=torch.uint8, device=dev)
+        rc = L.gb_repack_blocks(blocks.data_ptr(), 2, N, K, wq.data_ptr(), None)
+        if rc != 0:
+            raise RuntimeError(L.gb_last_error().decode())
+        out.append(wq)
+    del blocks
+    torch.cuda.synchronize()
+    return out
+
+
+def gemv_roofline(local: int, N: int = 28672, K: int = 4096, R: int = 16, reps: int = 4) -> dict:
+    """HBM roofline of the decode gate_up GEMV (Llama-3-8B shape: RMSNorm prologue, Q4_0
+    weights [2 x 14336, 4096], SwiGLU + Q8_0 epilogue) through gb_gemv.  Algorithmic bytes per
+    launch: weights N*K*18/32 + the f32 input row K*4 + the Q8_0 output (N/2 int8 + N/64 f32
+    scales).  Timed with one event pair around R launches on distinct weights (no event between
+    launches), after one untimed pass; the mean over `reps` passes."""
+    import ctypes
+
+    import torch
+
+    from ggmlc_b200 import _runtime as R_
+
+    L = R_.lib()
+    dev = torch.device("cuda", local)
+    P_, I, I64, F = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_float
+    L.gb_gemv.argtypes = [I, P_, I64, I64, I64, P_, P_, P_, F, P_, I, P_, P_, P_, P_, P_, P_]
+    ws = _q4_weights(L, dev, N, K, R)
+    x = torch.randn(K, device=dev)
+    yq = torch.empty(N // 2, dtype=torch.int8, device=dev)
+    yd = torch.empty(N // 64, dtype=torch.float32, device=dev)
+    st = torch.cuda.current_stream(dev)
+
+    def one_pass():
+        for w in ws:
+            rc = L.gb_gemv(2, w.data_ptr(), N, K, 1, None, None, x.data_ptr(), 1e-5, None, 1,
+                           None, yq.data_ptr(), yd.data_ptr(), None, None, ctypes.c_void_p(st.cuda_stream))
+            if rc != 0:
+                raise RuntimeError(L.gb_last_error().decode())
+
+    one_pass()
+    evs = []
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        one_pass()
+        e1.record(st)
+        evs.append((e0, e1))
+    torch.cuda.synchronize(dev)
+    ms = sum(a.elapsed_time(b) for a, b in evs) / (reps * R)
+    bytes_ = N * K * 18 / 32 + K * 4 + N // 2 + (N // 64) * 4
+    peak, kind = peaks()
+    achieved = bytes_ / (ms / 1e3) / 1e9
+    del ws
+    torch.cuda.empty_cache()
+    return {"bound": "hbm", "kernel": "k_gemv (RMSNorm + gate_up Q4_0 + SwiGLU/Q8_0)",
+            "shape": f"N={N} K={K} M=1", "achieved": round(achieved, 1), "peak": peak,
+            "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": kind,
+            "traffic": profiled_traffic("gemv_rms_swiglu"),
+            "bytes_per_launch": int(bytes_), "launch_us": round(ms * 1e3, 2),
+            "timing": f"{R} back-to-back launches on distinct weights per event pair, "
+                      f"mean of {reps} passes"}
 
 
 # single-kernel cases at the L8 decode shapes, for ncu captures of one launch (--case NAME)
@@ -618,7 +764,8 @@ def main():
     ap.add_argument("--quant", default="q4_0", choices=["q4_0", "q8_0"])
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--gen", type=int, default=128)
-    ap.add_argument("--ref-gen", type=int, default=8)
+    ap.add_argument("--ref-reps", type=int, default=3,
+                    help="--impl reference: repetitions of the reference's -pg test (<= steps)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cb", action="store_true", help="skip the continuous-batching leg")
     ap.add_argument("--replicas", action="store_true",

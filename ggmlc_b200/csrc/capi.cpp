@@ -540,6 +540,7 @@ int gb_gemv(int type, const void* wq, int64_t N, int64_t K, int64_t M,
     });
 }
 size_t gb_attn_decode_workspace_bytes(int64_t Hq, int64_t Hkv, int64_t hd, int64_t ctx) {
+    if (Hq <= 0 || Hkv <= 0 || hd <= 0 || ctx <= 0) return 0;
     return gb::attn_decode_workspace(Hq, hd, gb::attn_decode_splits(Hkv, ctx));
 }
 int gb_attn_decode(const float* qkv, int64_t Hq, int64_t Hkv, int64_t hd, void* k, void* v,
@@ -547,6 +548,7 @@ int gb_attn_decode(const float* qkv, int64_t Hq, int64_t Hkv, int64_t hd, void* 
                    int64_t n_pos, float scale, float* o, int8_t* oq, float* od, void* work,
                    void* stream) {
     return guard([&] {
+        GB_CHECK(Hq > 0 && Hkv > 0 && hd > 0, "gb_attn_decode: Hq, Hkv and hd must be positive");
         GB_CHECK(kv_pos >= 0 && kv_pos < ctx, "gb_attn_decode: kv_pos outside the cache");
         gb::AttnDecArgs a;
         a.qkv = qkv;

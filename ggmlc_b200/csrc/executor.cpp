@@ -181,8 +181,11 @@ void Executor::setup_peer_allreduce() {
     GB_CUDA(cudaMemset(ar_base_, 0, recv_bytes + flag_bytes));
     GB_CUDA(cudaMalloc(&ar_epochs_, kArCtas * sizeof(uint32_t)));
     GB_CUDA(cudaMemset(ar_epochs_, 0, kArCtas * sizeof(uint32_t)));
-    GB_CUDA(cudaMalloc(&ar_err_, sizeof(int)));
-    GB_CUDA(cudaMemset(ar_err_, 0, sizeof(int)));
+    // the error word lives in mapped pinned host memory: every host synchronisation reads it
+    // without a copy (check_tp_error)
+    GB_CUDA(cudaHostAlloc((void**)&ar_err_host_, sizeof(int), cudaHostAllocMapped));
+    *ar_err_host_ = 0;
+    GB_CUDA(cudaHostGetDevicePointer((void**)&ar_err_, ar_err_host_, 0));
     cudaIpcMemHandle_t h;
     GB_CUDA(cudaIpcGetMemHandle(&h, ar_base_));
     char* dh = nullptr;
@@ -209,10 +212,20 @@ void Executor::setup_peer_allreduce() {
 }
 
 int Executor::tp_allreduce_error() {
-    if (!ar_err_) return 0;
-    int v = 0;
-    GB_CUDA(cudaMemcpy(&v, ar_err_, sizeof(int), cudaMemcpyDeviceToHost));
-    return v;
+    if (!ar_err_host_) return 0;
+    GB_CUDA(cudaStreamSynchronize(stream_));
+    return *(volatile int*)ar_err_host_;
+}
+
+// A peer all-reduce whose wait ran out wrote a sum that is not valid: every output read of this
+// executor syncs through here and raises (once; the word is cleared) instead of handing it out.
+void Executor::check_tp_error() {
+    if (ar_err_host_ && *(volatile int*)ar_err_host_) {
+        *(volatile int*)ar_err_host_ = 0;
+        throw std::runtime_error(
+            "tensor-parallel all-reduce: a peer did not arrive within the wait limit (about 1 s); "
+            "the outputs of this run are not valid");
+    }
 }
 
 Executor::~Executor() {
@@ -238,7 +251,7 @@ Executor::~Executor() {
         if (m) cudaIpcCloseMemHandle(m);
     if (ar_base_) cudaFree(ar_base_);
     if (ar_epochs_) cudaFree(ar_epochs_);
-    if (ar_err_) cudaFree(ar_err_);
+    if (ar_err_host_) cudaFreeHost(ar_err_host_);
     if (nccl_) nccl().comm_destroy((ncclComm_t)nccl_);  // after the graphs that captured its calls
     if (stream_) cudaStreamDestroy(stream_);
 }
@@ -1868,6 +1881,7 @@ void Executor::run() {
 
 void Executor::synchronize() {
     GB_CUDA(cudaStreamSynchronize(stream_));
+    check_tp_error();
 }
 
 bool Executor::cuda_graph_captured() const {

@@ -226,13 +226,15 @@ private:
     std::vector<char*> ar_peer_;  // IPC mappings to close (index = rank; own rank null)
     TpPeers ar_peers_{};
     uint32_t* ar_epochs_ = nullptr;
-    int* ar_err_ = nullptr;
+    int* ar_err_ = nullptr;       // device address of ar_err_host_
+    int* ar_err_host_ = nullptr;  // mapped pinned error word of the peer all-reduce
     int64_t ar_cap_ = 0;
 
 public:
     // non-zero once a peer all-reduce gave up waiting for a peer (the sum of that call is not
     // valid)
     int tp_allreduce_error();
+    void check_tp_error();
 
 private:
     std::string device_;

@@ -12,8 +12,9 @@
 // call k+1 before every peer has contributed to call k, which each does only after finishing
 // call k-1 (the previous use of the same parity).
 //
-// A wait that runs past its limit (about 1 s) records 1 in the error word and the call goes on,
-// so the sum it writes is not valid; the host reads the word with tp_allreduce_error.
+// A wait that runs past its limit (about 1 s) records 1 in the error word (mapped pinned host
+// memory) and the call goes on, so the sum it writes is not valid; the executor raises on the
+// next host synchronisation (every output read), and tp_allreduce_error reads the word.
 #include <cuda_runtime.h>
 
 #include "common.h"
@@ -69,7 +70,8 @@ __global__ void __launch_bounds__(kArThreads)
         const long long t0 = clock64();
         while (ld_acquire_sys(f) != e) {
             if (clock64() - t0 > kArSpin) {
-                atomicExch(err, 1);
+                *(volatile int*)err = 1;  // host-mapped word: a plain store, no atomic
+                __threadfence_system();
                 break;
             }
         }

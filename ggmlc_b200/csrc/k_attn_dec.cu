@@ -652,6 +652,7 @@ void launch_rope_qkv(const QkvRopeArgs& a, cudaStream_t st) {
 int attn_decode_splits(int64_t Hkv, int64_t max_kv, int rows) {
     // about two CTAs per SM over the launch; each split then walks max_kv / splits positions
     const int64_t units = Hkv * std::max(rows, 1);
+    if (units <= 0 || max_kv <= 0) return 1;  // invalid shapes are rejected by the launch checks
     int64_t s = (296 + units - 1) / units;
     if (s > max_kv) s = max_kv;
     if (s > kMaxSplits) s = kMaxSplits;

@@ -44,11 +44,23 @@ class LlamaShape:
     max_seq: int = 2048
 
 
+@dataclass
+class GPT2Shape:
+    n_layers: int
+    d_model: int
+    n_heads: int
+    ffn: int
+    vocab: int
+    n_pos: int
+    eps: float = 1e-5
+
+
 SHAPES = {
-    # the shapes of the benchmark configurations: SmolLM2-135M and Llama-3-8B
+    # the shapes of the benchmark configurations: SmolLM2-135M, Llama-3-8B / 70B, GPT-2-small
     "smollm2-135m": LlamaShape(30, 576, 9, 3, 64, 1536, 49152, 10000.0),
     "llama3-8b": LlamaShape(32, 4096, 32, 8, 128, 14336, 128256, 500000.0),
     "llama3-70b": LlamaShape(80, 8192, 64, 8, 128, 28672, 128256, 500000.0),
+    "gpt2-small": GPT2Shape(12, 768, 12, 3072, 50257, 1024),
 }
 
 
@@ -237,6 +249,109 @@ def llama_graph(cfg: LlamaShape, qtype: int, name: str, sym: str = "s70"):
     return spec, payload
 
 
+def gpt2_graph(cfg: GPT2Shape, qtype: int, name: str, sym: str = "s70"):
+    """(spec, payload) of a GPT-2 model as the reference compiler emits it for the
+    ``examples/models/hub_models.py:load_gpt2_model`` wrapper: token + learned position
+    embeddings, per layer LAYER_NORM(201, affine baked into the next linear) -> MUL_MAT(fused
+    QKV + bias) -> SLICE x3 -> (VIEW, PERMUTE) x3 -> FLASH_ATTN_EXT -> VIEW -> MUL_MAT(out_proj +
+    bias) -> ADD -> LAYER_NORM -> MUL_MAT(mlp_fc + baked bias) -> BIAS_GELU(200, tanh) ->
+    MUL_MAT(mlp_proj + bias) -> ADD, closed by LAYER_NORM(ln_f gamma, beta) -> MUL_MAT(tied wte).
+    Random init as the config asks: matrices N(0, 0.02), biases 0, LayerNorm gamma 1 beta 0 (the
+    bake then leaves the fused biases 0)."""
+    tensors: dict[str, dict] = {}
+    nodes: list[dict] = []
+    params: list[int] = []
+    payload: list[tuple] = []
+    nid = [0]
+    tid = [0]
+
+    def tensor(tname, ne, ttype, storage, role=None, producer=None, data=None):
+        i = tid[0]
+        tid[0] += 1
+        tensors[str(i)] = {"id": i, "name": tname, "type": ttype,
+                           "ne": [_dim(v) for v in (list(ne) + [1] * (4 - len(ne)))],
+                           "storage": storage, "producer_id": producer, "role": role}
+        if data is not None:
+            payload.append((tname, [v for v in ne], ttype, data))
+            if storage == 1:
+                params.append(i)
+        return i
+
+    def node(opcode, inputs, out_name, out_ne, attrs, op_name, storage=3):
+        i = nid[0]
+        nid[0] += 1
+        out = tensor(out_name, out_ne, F32, storage, producer=i)
+        nodes.append({"id": i, "opcode": opcode, "inputs": inputs, "outputs": [out],
+                      "attributes": attrs, "name": op_name})
+        return out
+
+    d, H, F, V, L = cfg.d_model, cfg.n_heads, cfg.ffn, cfg.vocab, cfg.n_layers
+    hd = d // H
+    s = sym
+    seed = [2000]
+
+    def wmaker(rows, cols):
+        seed[0] += 1
+        sd = seed[0]
+        return lambda device: quantized_normal(rows, cols, qtype, sd, device=device)
+
+    def zeros(n):
+        return lambda device: iter([np.zeros(n, np.float32).view(np.uint8)])
+
+    wte = tensor("wte.weight", [d, V], qtype, 1, data=wmaker(V, d))
+    wpe = tensor("wpe.weight", [d, cfg.n_pos], qtype, 1, data=wmaker(cfg.n_pos, d))
+    ids = tensor("input_ids", [s], I32, 0, role="input")
+    pids = tensor("position_ids", [s], I32, 0, role="input")
+    eps = float(cfg.eps)
+    e0 = node(40, [wte, ids], "embedding", [d, s], {"source_op": "aten.embedding.default"}, "embedding")
+    e1 = node(40, [wpe, pids], "embedding_1", [d, s], {"source_op": "aten.embedding.default"}, "embedding_1")
+    x = node(2, [e0, e1], "add", [d, s], {"source_op": "aten.add.Tensor"}, "add")
+    perm = {"dim0": 1, "dim1": 2, "axis0": 0, "axis1": 2, "axis2": 1, "axis3": 3}
+    for li in range(L):
+        p = f"layers.{li}."
+        wqkv = tensor(p + "fused_qkv.weight", [d, 3 * d], qtype, 1, data=wmaker(3 * d, d))
+        bqkv = tensor(p + "fused_qkv.bias", [3 * d], F32, 1, data=zeros(3 * d))
+        wo = tensor(p + "out_proj.weight", [d, d], qtype, 1, data=wmaker(d, d))
+        bo = tensor(p + "out_proj.bias", [d], F32, 1, role="parameter", data=zeros(d))
+        wfc = tensor(p + "mlp_fc.weight", [d, F], qtype, 1, data=wmaker(F, d))
+        # the bake names the folded bias after the linear node it feeds (linear_4, linear_10, ...)
+        bfc_baked = tensor(f"linear_{6 * li + 4}_baked_bias", [F], F32, 1, role="bias",
+                           data=zeros(F))
+        bfc = tensor(p + "mlp_fc.bias", [F], F32, 1, role="parameter", data=zeros(F))
+        wpj = tensor(p + "mlp_proj.weight", [F, d], qtype, 1, data=wmaker(d, F))
+        bpj = tensor(p + "mlp_proj.bias", [d], F32, 1, role="parameter", data=zeros(d))
+        h = node(201, [x], f"l{li}_ln1", [d, s], {"eps": eps}, f"l{li}_ln1")
+        qkv = node(29, [wqkv, h, bqkv], f"l{li}_qkv", [3 * d, s],
+                   {"fused_pass": "Horizontal QKV Projection Fusion"}, f"l{li}_qkv")
+        sl = [node(37, [qkv], f"l{li}_slice{j}", [d, s],
+                   {"dim": -1, "start": j * d, "end": (j + 1) * d, "step": 1, "ggml_dim": 0},
+                   f"l{li}_slice{j}") for j in range(3)]
+        hv = []
+        for j in range(3):
+            v_ = node(36, [sl[j]], f"l{li}_view{j}", [hd, H, s, 1], {"shape": [1, s, H, hd]},
+                      f"l{li}_view{j}")
+            hv.append(node(38, [v_], f"l{li}_t{j}", [hd, s, H, 1], dict(perm), f"l{li}_t{j}"))
+        att = node(74, hv, f"l{li}_attn", [hd, H, s, 1], {"is_causal": 1, "fused_transpose": 1},
+                   f"l{li}_sdpa")
+        a2 = node(36, [att], f"l{li}_attn2d", [d, s], {"shape": [1, s, "-1"]}, f"l{li}_view_o")
+        o = node(29, [wo, a2, bo], f"l{li}_o", [d, s], {}, f"l{li}_out_proj")
+        x = node(2, [x, o], f"l{li}_res1", [d, s], {}, f"l{li}_add1")
+        h2 = node(201, [x], f"l{li}_ln2", [d, s], {"eps": eps}, f"l{li}_ln2")
+        fc = node(29, [wfc, h2, bfc_baked], f"l{li}_fc", [F, s], {}, f"l{li}_mlp_fc")
+        g = node(200, [fc, bfc], f"l{li}_gelu", [F, s], {"approximate": "tanh"}, f"l{li}_gelu")
+        pj = node(29, [wpj, g, bpj], f"l{li}_proj", [d, s], {}, f"l{li}_mlp_proj")
+        x = node(2, [x, pj], f"l{li}_res2", [d, s], {}, f"l{li}_add2")
+    gam = tensor("ln_f.weight", [d], F32, 1, role="parameter",
+                 data=lambda device: iter([np.ones(d, np.float32).view(np.uint8)]))
+    bet = tensor("ln_f.bias", [d], F32, 1, role="parameter", data=zeros(d))
+    hf = node(201, [x, gam, bet], "final_ln", [d, s], {"eps": eps}, "final_ln")
+    logits = node(29, [wte, hf], "logits", [V, s], {}, "lm_head", storage=5)
+    spec = {"name": name, "inputs": [ids, pids], "outputs": [logits],
+            "parameters": sorted(params), "symbol_table": [s], "metadata": {},
+            "tensors": tensors, "nodes": nodes}
+    return spec, payload
+
+
 # ------------------------------------------------------------------------------ GGUF writer
 
 def _kv_str(key: str, val: str) -> bytes:
@@ -311,3 +426,19 @@ def synth_llama(path: str | Path, shape: str | LlamaShape, qtype: int = Q4_0,
     spec, payload = llama_graph(cfg, qtype, name or (shape if isinstance(shape, str) else "llama"))
     write_gguf(path, spec, payload, device=device)
     return Path(path)
+
+
+def synth_gpt2(path: str | Path, shape: str | GPT2Shape = "gpt2-small", qtype: int = Q8_0,
+               device: str | None = None, name: str | None = None) -> Path:
+    cfg = SHAPES[shape] if isinstance(shape, str) else shape
+    spec, payload = gpt2_graph(cfg, qtype, name or (shape if isinstance(shape, str) else "gpt2"))
+    write_gguf(path, spec, payload, device=device)
+    return Path(path)
+
+
+def synth_model(path: str | Path, shape: str, qtype: int, device: str | None = None,
+                name: str | None = None) -> Path:
+    """Either family by its SHAPES name."""
+    if isinstance(SHAPES[shape], GPT2Shape):
+        return synth_gpt2(path, shape, qtype, device, name)
+    return synth_llama(path, shape, qtype, device, name)

@@ -76,7 +76,10 @@ const char* gb_tp_plan(const gb_graph* g, int tp_rank, int tp_size);
 int gb_executor_tp_size(const gb_executor* e);
 /* Decode-sized partial sums are summed by a one-shot all-reduce over peer memory (CUDA IPC,
  * NVLink stores, bounded waits); gb_executor_tp_error returns 0 while every such wait
- * completed, 1 once one gave up on a peer (that call's sum is not valid), -1 on error. */
+ * completed, 1 once one gave up on a peer (that call's sum is not valid), -1 on error.  The
+ * executor also checks the word at every host synchronisation (gb_executor_synchronize and
+ * every output read): a wait that gave up makes that call fail with an error naming it
+ * (gb_last_error), once, and clears the word. */
 int gb_executor_tp_error(gb_executor* e);
 int gb_executor_tp_rank(const gb_executor* e);
 void gb_executor_free(gb_executor* e);
@@ -281,7 +284,10 @@ int gb_attn_decode(const float* qkv, int64_t Hq, int64_t Hkv, int64_t hd, void* 
  * bytes; larger shapes are rejected with an error before anything runs.  Its contents need no
  * initial value (every partial is written before it is read).  The first call on a device looks
  * up the array's address with that device current (setup): make it before any stream capture on
- * that device.  All calls on one device share the array, so two calls whose kernels can overlap
+ * that device.  The looked-up address is kept for the life of the process's context on that
+ * device: after cudaDeviceReset (or anything else that ends the context) the address is stale,
+ * so a process that resets a device must not call this entry point again; start a new process
+ * instead.  All calls on one device share the array, so two calls whose kernels can overlap
  * (different streams without ordering, or different host threads) race on it; order them on one
  * stream.  Same results as gb_attn_decode. */
 size_t gb_attn_decode_noalloc_max_bytes(void);

@@ -1,7 +1,7 @@
 """The synthetic-model builder (ggmlc_b200/synth.py, used by bench.py for the Llama shapes) writes
-the same graph the reference compiler writes: a tiny Llama synthesized at the shape of the
-reference-compiled fixtures (tests/golden/make_golden.py LLAMA) is compared node by node with
-them.  Host only: the numpy quantizers build the payload, the C++ loader reads the result."""
+the same graph the reference compiler writes: a tiny Llama and a tiny GPT-2 synthesized at the
+shapes of the reference-compiled fixtures (tests/golden/make_golden.py LLAMA, GPT2) are compared
+node by node with them.  Host only: the numpy quantizers build the payload, the C++ loader reads the result."""
 
 from __future__ import annotations
 
@@ -32,11 +32,25 @@ def _synth(tmp_path, quant: str, theta: float):
     return path
 
 
-@pytest.mark.parametrize("quant,theta", [("q8_0", 10000.0), ("q4_0", 500000.0)])
+def _synth_gpt2(tmp_path):
+    from ggmlc_b200 import synth
+
+    shape = synth.GPT2Shape(2, 256, 4, 1024, 500, 512)
+    path = tmp_path / "tiny_gpt2_q8_0.gguf"
+    synth.synth_gpt2(path, shape, synth.Q8_0, name="tiny_gpt2")
+    return path
+
+
+@pytest.mark.parametrize("quant,theta", [("q8_0", 10000.0), ("q4_0", 500000.0), ("gpt2", None)])
 def test_synthesized_graph_matches_reference_compiled(tmp_path, quant, theta):
-    path = _synth(tmp_path, quant, theta)
+    if quant == "gpt2":
+        path = _synth_gpt2(tmp_path)
+        ref_path = GOLDEN / "tiny_gpt2_q8_0.gguf"
+    else:
+        path = _synth(tmp_path, quant, theta)
+        ref_path = GOLDEN / f"tiny_llama_{quant}.gguf"
     kv, _, data = O.read_gguf(path)
-    ref_kv, _, ref_data = O.read_gguf(GOLDEN / f"tiny_llama_{quant}.gguf")
+    ref_kv, _, ref_data = O.read_gguf(ref_path)
     assert sorted(kv) == sorted(ref_kv)
     spec = json.loads(kv["ggmlc.graph_spec"])
     ref = json.loads(ref_kv["ggmlc.graph_spec"])

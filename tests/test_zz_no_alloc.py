@@ -72,7 +72,6 @@ def test_noalloc_matches_workspace_entry_point(Hq, Hkv, hd, ctx, kv_pos):
     o_ref = [outs() for _ in range(2)]
     o_na = [outs() for _ in range(2)]
     torch.cuda.synchronize()
-    free_after = []
     for step in range(2):
         pos = kv_pos + step
         o, oq, od = o_ref[step]
@@ -84,14 +83,24 @@ def test_noalloc_matches_workspace_entry_point(Hq, Hkv, hd, ctx, kv_pos):
                                          ctx, pos, hd, base, G.ptr(t_d), n_pos, scale, G.ptr(o),
                                          G.ptr(oq), G.ptr(od), None))
         torch.cuda.synchronize()
-        free_after.append(torch.cuda.mem_get_info()[0])
-    # after the first (setup) call, a call leaves the device's free memory untouched
+    # after the first (setup) call, calls leave the device's free memory untouched.  The reading
+    # covers the whole device, so another process's allocation could move it: a window of eight
+    # calls is taken up to three times and one unchanged window suffices (an allocation inside
+    # the entry point would show in every window).
     o, oq, od = o_na[1]
-    G.check(L.gb_attn_decode_noalloc(G.ptr(qkvs[1]), Hq, Hkv, hd, G.ptr(k_na), G.ptr(v_na), ctx,
-                                     kv_pos + 1, hd, base, G.ptr(t_d), n_pos, scale, G.ptr(o),
-                                     G.ptr(oq), G.ptr(od), None))
-    torch.cuda.synchronize()
-    assert torch.cuda.mem_get_info()[0] == free_after[1]
+    clean = False
+    for _ in range(3):
+        torch.cuda.synchronize()
+        before = torch.cuda.mem_get_info()[0]
+        for _ in range(8):
+            G.check(L.gb_attn_decode_noalloc(G.ptr(qkvs[1]), Hq, Hkv, hd, G.ptr(k_na),
+                                             G.ptr(v_na), ctx, kv_pos + 1, hd, base, G.ptr(t_d),
+                                             n_pos, scale, G.ptr(o), G.ptr(oq), G.ptr(od), None))
+        torch.cuda.synchronize()
+        if torch.cuda.mem_get_info()[0] == before:
+            clean = True
+            break
+    assert clean, "device free memory moved in every window of noalloc calls"
 
     for step in range(2):
         for a, b in zip(o_ref[step], o_na[step]):
