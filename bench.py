@@ -38,8 +38,29 @@ sys.path.insert(0, str(ROOT))
 METRIC = "tokens/s pp512 & tg128 (Q4_0/Q8_0) per GPU and TP; % of HBM/INT8 roofline"
 FALLBACK_HBM_GBS = 6650.0
 BENCH_DIR = Path(os.environ.get("GGMLC_B200_BENCH_DIR", "/tmp/ggmlc_b200_bench"))
-REF_BENCH = ROOT / "oracle" / "_ref" / "ggmlc-bench"
-REF_BUILD = "reference CPU build: oracle/Makefile, -O3 -march=x86-64-v3 (AVX2/FMA/F16C)"
+REF_BENCH_AVX2 = ROOT / "oracle" / "_ref" / "ggmlc-bench"
+REF_BENCH_NATIVE = ROOT / "oracle" / "_ref" / "native" / "ggmlc-bench"
+# the ISA of the native build (-march=sapphirerapids); it runs only where the host has all of it
+NATIVE_FLAGS = ("avx512f", "avx512bw", "avx512vl", "avx512_vnni", "avx512_bf16", "avx512_fp16",
+                "amx_int8", "amx_tile", "avx_vnni")
+
+
+def ref_bench() -> tuple[Path, str]:
+    """The reference's ggmlc-bench for the CPU baseline: the native build (what the reference's
+    default cmake build, GGML_NATIVE, compiles on a Sapphire-Rapids-class host) when this host
+    can run it, else the portable AVX2 build."""
+    try:
+        flags = set(Path("/proc/cpuinfo").read_text().split())
+    except OSError:
+        flags = set()
+    if REF_BENCH_NATIVE.exists() and all(f in flags for f in NATIVE_FLAGS):
+        return REF_BENCH_NATIVE, ("reference CPU build: oracle/Makefile native, -O3 "
+                                  "-march=sapphirerapids (AVX-512 VNNI/BF16/FP16, AMX), the "
+                                  "reference's GGML_NATIVE build on this host")
+    return REF_BENCH_AVX2, "reference CPU build: oracle/Makefile, -O3 -march=x86-64-v3 (AVX2/FMA/F16C)"
+
+
+REF_BENCH, REF_BUILD = ref_bench()
 
 
 def peaks() -> tuple[float, str]:

@@ -176,7 +176,9 @@ __global__ void k_bias_gelu(const float* __restrict__ x, int64_t x_stride,
         const float v3 = __fmul_rn(__fmul_rn(v, v), v);
         float inner = __fmul_rn(kS, __fmaf_rn(kA, v3, v));
         inner = fmaxf(-9.0f, fminf(9.0f, inner));
-        const float e2 = expf(__fmul_rn(2.0f, inner));
+        // the CPU's libm expf is correctly rounded but for rare last-bit cases; exp in double
+        // rounded once to float is correctly rounded
+        const float e2 = (float)exp((double)__fmul_rn(2.0f, inner));
         const float th = __fdiv_rn(__fsub_rn(e2, 1.0f), __fadd_rn(e2, 1.0f));
         srow[k] = __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, th));
     }

@@ -17,21 +17,26 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF_LIB = HERE / "_ref" / "libggmlc_ref.so"
+# "avx2": the default build (-march=x86-64-v3), the checker; "native": the same sources built as
+# the reference's default cmake build does on the benchmark hosts (oracle/Makefile `native`)
+REF_LIBS = {"avx2": HERE / "_ref" / "libggmlc_ref.so",
+            "native": HERE / "_ref" / "native" / "libggmlc_ref.so"}
+REF_LIB = REF_LIBS["avx2"]
 
-_lib = None
+_libs: dict[str, ctypes.CDLL] = {}
 
 
-def available() -> bool:
-    return REF_LIB.exists()
+def available(build: str = "avx2") -> bool:
+    return REF_LIBS[build].exists()
 
 
-def lib() -> ctypes.CDLL:
-    global _lib
-    if _lib is None:
-        if not REF_LIB.exists():
-            raise RuntimeError(f"{REF_LIB} is not built (make -C oracle, needs the reference sources)")
-        L = ctypes.CDLL(str(REF_LIB))
+def lib(build: str = "avx2") -> ctypes.CDLL:
+    if build not in _libs:
+        path = REF_LIBS[build]
+        if not path.exists():
+            raise RuntimeError(f"{path} is not built (make -C oracle, needs the reference sources)")
+        # RTLD_LOCAL (the default): the two builds export the same symbols and stay apart
+        L = ctypes.CDLL(str(path))
         P, I64, I = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
         L.ref_model_open.argtypes = [ctypes.c_char_p, I]
         L.ref_model_open.restype = P
@@ -42,8 +47,8 @@ def lib() -> ctypes.CDLL:
         L.ref_model_forward.argtypes = [P, P, I64, I64, P, I64]
         L.ref_model_forward.restype = I64
         L.ref_last_error.restype = ctypes.c_char_p
-        _lib = L
-    return _lib
+        _libs[build] = L
+    return _libs[build]
 
 
 def host_threads() -> int:
@@ -57,8 +62,8 @@ class RefRunner:
     """One reference CPU executor over a GGUF, with its padded KV cache."""
 
     def __init__(self, gguf: str | Path, vocab: int, n_threads: int | None = None,
-                 max_ctx: int = 2048):
-        self.L = lib()
+                 max_ctx: int = 2048, build: str = "avx2"):
+        self.L = lib(build)
         self.V = vocab
         self.n_threads = n_threads or host_threads()
         self.h = self.L.ref_model_open(str(gguf).encode(), self.n_threads)

