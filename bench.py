@@ -601,11 +601,12 @@ def _q4_weights(L, dev, N: int, K: int, R: int, seed: int = 0):
 
 
 def gemv_roofline(local: int, N: int = 28672, K: int = 4096, R: int = 16, reps: int = 4) -> dict:
-    """HBM roofline of the decode gate_up GEMV (Llama-3-8B shape: RMSNorm prologue, Q4_0
-    weights [2 x 14336, 4096], SwiGLU + Q8_0 epilogue) through gb_gemv.  Algorithmic bytes per
-    launch: weights N*K*18/32 + the f32 input row K*4 + the Q8_0 output (N/2 int8 + N/64 f32
-    scales).  Timed with one event pair around R launches on distinct weights (no event between
-    launches), after one untimed pass; the mean over `reps` passes."""
+    """HBM roofline of the decode gate_up GEMV as the engine runs it at batch 1 (Llama-3-8B
+    shape: RMSNorm prologue, Q4_0 weights [2 x 14336, 4096], SwiGLU epilogue to f32; the down
+    GEMV quantizes that row in its own prologue) through gb_gemv.  Algorithmic bytes per launch:
+    weights N*K*18/32 + the f32 input row K*4 + the f32 output N/2*4.  Timed with one event pair
+    around R launches on distinct weights (no event between launches), after one untimed pass;
+    the mean over `reps` passes."""
     import ctypes
 
     import torch
@@ -618,14 +619,13 @@ def gemv_roofline(local: int, N: int = 28672, K: int = 4096, R: int = 16, reps: 
     L.gb_gemv.argtypes = [I, P_, I64, I64, I64, P_, P_, P_, F, P_, I, P_, P_, P_, P_, P_, P_]
     ws = _q4_weights(L, dev, N, K, R)
     x = torch.randn(K, device=dev)
-    yq = torch.empty(N // 2, dtype=torch.int8, device=dev)
-    yd = torch.empty(N // 64, dtype=torch.float32, device=dev)
+    h = torch.empty(N // 2, dtype=torch.float32, device=dev)
     st = torch.cuda.current_stream(dev)
 
     def one_pass():
         for w in ws:
             rc = L.gb_gemv(2, w.data_ptr(), N, K, 1, None, None, x.data_ptr(), 1e-5, None, 1,
-                           None, yq.data_ptr(), yd.data_ptr(), None, None, ctypes.c_void_p(st.cuda_stream))
+                           h.data_ptr(), None, None, None, None, ctypes.c_void_p(st.cuda_stream))
             if rc != 0:
                 raise RuntimeError(L.gb_last_error().decode())
 
@@ -639,12 +639,12 @@ def gemv_roofline(local: int, N: int = 28672, K: int = 4096, R: int = 16, reps: 
         evs.append((e0, e1))
     torch.cuda.synchronize(dev)
     ms = sum(a.elapsed_time(b) for a, b in evs) / (reps * R)
-    bytes_ = N * K * 18 / 32 + K * 4 + N // 2 + (N // 64) * 4
+    bytes_ = N * K * 18 / 32 + K * 4 + (N // 2) * 4
     peak, kind = peaks()
     achieved = bytes_ / (ms / 1e3) / 1e9
     del ws
     torch.cuda.empty_cache()
-    return {"bound": "hbm", "kernel": "k_gemv (RMSNorm + gate_up Q4_0 + SwiGLU/Q8_0)",
+    return {"bound": "hbm", "kernel": "k_dgemv (RMSNorm + gate_up Q4_0 + SwiGLU)",
             "shape": f"N={N} K={K} M=1", "achieved": round(achieved, 1), "peak": peak,
             "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": kind,
             "traffic": profiled_traffic("gemv_rms_swiglu"),
@@ -734,9 +734,9 @@ def run_case(name: str, reps: int) -> None:
             elif mode == "gemm":
                 rc = L.gb_mul_mat_q(2, ptr(wq), N, K, ptr(xq), ptr(xd), M, ptr(ym), None, None,
                                     None)
-            elif mode == "rms_swiglu":
-                rc = L.gb_gemv(2, ptr(wq), N, K, 1, None, None, ptr(x), 1e-5, None, 1, None,
-                               ptr(yq), ptr(yd), None, None, None)
+            elif mode == "rms_swiglu":  # as the engine runs it at batch 1: SwiGLU to f32
+                rc = L.gb_gemv(2, ptr(wq), N, K, 1, None, None, ptr(x), 1e-5, None, 1, ptr(y),
+                               None, None, None, None, None)
             elif mode == "rms":
                 rc = L.gb_gemv(2, ptr(wq), N, K, 1, None, None, ptr(x), 1e-5, None, 0, ptr(y),
                                None, None, None, None, None)

@@ -509,6 +509,11 @@ int gb_gemm_tc_error(void) {
     const int rc = guard([&] { v = gb::gemm_tc_error(); });
     return rc == 0 ? v : -1;
 }
+int gb_gemv_error(void) {
+    int v = 0;
+    const int rc = guard([&] { v = gb::dgemv_error(); });
+    return rc == 0 ? v : -1;
+}
 int gb_gemv(int type, const void* wq, int64_t N, int64_t K, int64_t M,
             const int8_t* xq, const float* xd, const float* xf, float eps, const float* gamma,
             int swiglu, float* y, int8_t* yq, float* yd, const float* bias,

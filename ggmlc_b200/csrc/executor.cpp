@@ -982,18 +982,26 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                     int64_t xs = 0;
                     const float* gamma = nullptr;
                     float eps = 0.0f;
+                    const bool qpro = !xin.virt_rms && xin.q_in_prologue && !xin.has_q &&
+                                      Mrun <= kGemvRouteRows && xin.nb[0] == 4 &&
+                                      xin.rows_uniform() && xin.nb[1] % 16 == 0;
                     if (xin.virt_rms) {
                         xr = xin.rms_x;
                         xs = xin.rms_stride;
                         gamma = xin.rms_gamma;
                         eps = xin.rms_eps;
                         pg.use(xr, oi);
+                    } else if (qpro) {
+                        xr = xin.ref;
+                        xs = xin.nb[1] / 4;
+                        pg.use(xr, oi);
                     } else {
                         ensure_q(xin, oi);
                         qb = xin.q;
                         qdb = xin.qd;
                     }
-                    const bool virt = xin.virt_rms;
+                    const bool virt = xin.virt_rms || qpro;
+                    const bool xrms = xin.virt_rms;
                     const double bytes = mm_bytes(qw, Mrun, add_op >= 0);
                     if (swi_op >= 0) {
                         const uint32_t sout = G.ops[swi_op].outputs[0];
@@ -1004,6 +1012,14 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         GB_CHECK(h.ne[0] == F, "SwiGLU output width mismatch");
                         bool nf, nq;
                         needs(sout, nf, nq);
+                        if (nq && !nf && Mrun <= kGemvRouteRows) {
+                            // 1-2 rows: the down GEMV quantizes the f32 rows in its prologue, so
+                            // the gate_up GEMV can split its rows at any pair (no Q8_0 block
+                            // of the output has to come from one CTA)
+                            nf = true;
+                            nq = false;
+                            h.q_in_prologue = true;
+                        }
                         if (nf) alloc(h, oi);
                         else h.has_f = false;
                         if (nq) {
@@ -1013,13 +1029,14 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         }
                         const BufRef hr = h.ref, hq = h.q, hqd = h.qd;
                         const bool hf = h.has_f, hhq = h.has_q;
-                        add(virt ? "gemv_rms_swiglu"
+                        add(xrms ? "gemv_rms_swiglu"
                                  : (Mrun <= kGemvRouteRows ? "gemv_swiglu"
                                                          : (Mrun <= kMmvMaxRows ? "mmv_swiglu" : "gemm_swiglu")), [=](Program& p, cudaStream_t st) {
                             GemvArgs a = ga;
                             if (virt) {
                                 a.xf = (const float*)p.ptr(xr);
                                 a.xf_stride = xs;
+                                a.xf_rms = xrms;
                                 a.eps = eps;
                                 a.gamma = gamma;
                             } else {
@@ -1055,11 +1072,12 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         pg.use(res.ref, add_op);
                     }
                     const BufRef yr = y.ref;
-                    add(virt ? "gemv_rms" : (Mrun <= kGemvRouteRows ? (add_op >= 0 ? "gemv_res" : "gemv") : (add_op >= 0 ? "mmv_res" : "mmv")), [=](Program& p, cudaStream_t st) {
+                    add(xrms ? "gemv_rms" : (Mrun <= kGemvRouteRows ? (add_op >= 0 ? "gemv_res" : "gemv") : (add_op >= 0 ? "mmv_res" : "mmv")), [=](Program& p, cudaStream_t st) {
                         GemvArgs a = ga;
                         if (virt) {
                             a.xf = (const float*)p.ptr(xr);
                             a.xf_stride = xs;
+                            a.xf_rms = xrms;
                             a.eps = eps;
                             a.gamma = gamma;
                         } else {

@@ -46,6 +46,9 @@ struct Val {
     int64_t rms_stride = 0;
     float rms_eps = 0.0f;
     const float* rms_gamma = nullptr;
+    // f32 rows whose Q8_0 form is left unmaterialized: every consumer is a decode GEMV that
+    // quantizes them in its prologue (the SwiGLU output of a 1-2-row decode step)
+    bool q_in_prologue = false;
     // RoPE output left unmaterialized: the attention lowering rotates q/k inside its kernels.
     // rsrc_* describe the un-rotated [hd, H, s] source view; rope_perm tracks a (0,2,1,3)
     // permute applied after the rotation.

@@ -1,0 +1,588 @@
+// Decode GEMV for one or two activation rows (batch-1/2 decode): y = W x over the split-row layout,
+// the weights streamed from HBM by bulk copies (cp.async.bulk, the TMA engine's linear mode).
+//
+// Work mapping.  The output units (rows, or SwiGLU row pairs gate n / up n+F) are split into
+// contiguous ranges, one per warp of the grid.  Every warp owns a ring of shared-memory slots,
+// one weight row per slot, each with an mbarrier: lane 0 issues one bulk copy per row (rows are
+// contiguous byte ranges in the split-row layout) and refills a slot as soon as the warp has
+// consumed it, so each warp keeps up to `slots` rows in flight with a handful of instructions
+// per row.  Lanes run along K: lane l takes blocks l, l+32, l+64, ... of a row, whose quants are
+// 16 consecutive bytes (Q4_0; Q8_0 in two 16-byte halves), so the lanes' shared-memory reads are
+// conflict-free, and whose fp16 scales come two to a 32-bit word.
+//
+// Activations.  The Q8_0 activation blocks a lane needs are the same for every row, so they are
+// held in registers (BPL blocks per lane, K <= 4096) or, for longer rows, in shared memory.  They
+// come quantized (xq, xd) or as f32 (xf), quantized by every CTA in its prologue after an
+// optional RMSNorm (+gamma): the same arithmetic as launch_rms_norm and the x86 activation
+// quantizer (ggml-cpu/arch/x86/quants.c:302-392).
+//
+// Arithmetic per 32-element block: the integer dot is exact.  Q4_0: the low nibbles (elements
+// 0-15) and the high nibbles (16-31) are masked out of each 32-bit word as unsigned bytes and
+// dotted with the signed activation bytes (dp4a.u32.s32); the high-nibble chain sees 16 * q, so
+// its sum is shifted right by 4 (exact), and the -8 offset of every weight is folded into the
+// chain's start value, -8 * sum(x) of the block.  The chain starts at 1.5 * 2^23, so the int sum
+// becomes a float by one subtraction (exact for |sum| < 2^22).  The block term sumi * (d_w * d_x)
+// accumulates in fp32 per lane; a row's lane sums are combined by a fixed xor-butterfly.  This is
+// the reference's block formula (ggml-cpu/quants.c:225-256 Q4_0, :451-477 Q8_0); the x86 build
+// adds the same terms in another order, so fp32 results agree to rounding.
+//
+// Epilogues: f32 rows (+bias, +residual), or SwiGLU of each pair, silu(gate) * up (the vector
+// silu of the CPU build, ggml-cpu/vec.h:1255-1262), written as f32 rows of length F.
+//
+// Launch: one CTA of 8 warps per SM (the rings take most of the shared memory), programmatic
+// dependent launch: the first ring of every warp is requested before griddepcontrol.wait, so the
+// weight stream overlaps the tail of the previous kernel; activations are read and outputs
+// written after the wait.  Every mbarrier wait is bounded (about 2 s): past the limit the kernel
+// records an error in dgemv_error (gb_gemv_error), waits (bounded) for the copies it issued and
+// returns.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.h"
+#include "kernels.h"
+#include "kutil.cuh"
+
+namespace gb {
+
+__device__ int dgemv_error_word;
+
+namespace {
+
+constexpr int kW = 8;            // warps per CTA
+constexpr int kT = kW * 32;
+constexpr int kMaxSlots = 8;     // ring slots per warp
+constexpr size_t kRingBudget = 168 * 1024;
+constexpr long long kSpin = 4000000000LL;  // about 2 s at 1.9 GHz
+constexpr int kMagic = 0x4B400000;         // 1.5 * 2^23
+
+struct DArgs {
+    const uint8_t* w;
+    int64_t rb;        // bytes per weight row
+    int nb;            // blocks per row
+    int units;         // rows, or SwiGLU pairs
+    int F;             // SwiGLU: up row of pair n is n + F
+    int slots;         // ring slots per warp
+    int M;             // activation rows (1 or 2)
+    const int8_t* xq;  // Q8_0 input [M][K], or
+    const float* xd;
+    const float* xf;   // f32 input [M][xf_stride], quantized in the prologue
+    int64_t xf_stride;
+    int rms;
+    float eps;
+    const float* gamma;
+    int swiglu;
+    float* y;          // [M][y_stride]
+    int64_t y_stride;
+    const float* bias;
+    const float* residual;  // [M][res_stride]
+    int64_t res_stride;
+};
+
+__device__ __forceinline__ uint32_t su32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, int count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)),
+                 "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(su32(b)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
+    if (mbar_test(b, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_test(b, parity))
+        if (clock64() - t0 > kSpin) return false;
+    return true;
+}
+// one weight row (bytes, a multiple of 16, 16-byte aligned) into a slot; completion on bar
+__device__ __forceinline__ void fetch_row(void* dst, const void* src, uint32_t bytes,
+                                          uint64_t* bar) {
+    mbar_expect_tx(bar, bytes);
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(su32(dst)),
+        "l"(src), "r"(bytes), "r"(su32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ int dp4a_us(unsigned a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// One activation block as a lane holds it.
+struct XBlk {
+    int4 lo, hi;  // quants of elements 0-15, 16-31
+    float d;      // scale
+    int init;     // dot-chain start: 1.5 * 2^23 (Q8_0 weights), minus 8 * sum(q) for Q4_0
+};
+
+// sum(q) of a block's 32 quants
+__device__ __forceinline__ int qsum(const int4& lo, const int4& hi) {
+    const int one = 0x01010101;
+    int s = __dp4a(lo.x, one, 0);
+    s = __dp4a(lo.y, one, s);
+    s = __dp4a(lo.z, one, s);
+    s = __dp4a(lo.w, one, s);
+    s = __dp4a(hi.x, one, s);
+    s = __dp4a(hi.y, one, s);
+    s = __dp4a(hi.z, one, s);
+    return __dp4a(hi.w, one, s);
+}
+
+template <int WT>
+__device__ __forceinline__ int chain_init(const int4& lo, const int4& hi) {
+    return WT == T_Q4_0 ? kMagic - 8 * qsum(lo, hi) : kMagic;
+}
+
+// One weight block as the lanes consume it.  Q4_0: a = low nibbles (elements 0-15) and b = high
+// nibbles times 16 (elements 16-31), both as unsigned bytes; Q8_0: a, b = quant bytes 0-15, 16-31.
+struct WBlk {
+    uint4 a, b;
+};
+
+template <int WT>
+__device__ __forceinline__ WBlk load_w(const uint8_t* slot, int nb, int b) {
+    WBlk w;
+    if (WT == T_Q4_0) {
+        const uint4 q = *(const uint4*)(slot + (size_t)b * 16);
+        w.a = make_uint4(q.x & 0x0F0F0F0Fu, q.y & 0x0F0F0F0Fu, q.z & 0x0F0F0F0Fu, q.w & 0x0F0F0F0Fu);
+        w.b = make_uint4(q.x & 0xF0F0F0F0u, q.y & 0xF0F0F0F0u, q.z & 0xF0F0F0F0u, q.w & 0xF0F0F0F0u);
+    } else {
+        w.a = *(const uint4*)(slot + (size_t)b * 16);
+        w.b = *(const uint4*)(slot + (size_t)(nb + b) * 16);
+    }
+    return w;
+}
+
+// acc += sumi * (d_w * d_x) of a weight block against one activation block
+template <int WT>
+__device__ __forceinline__ void block_term(const WBlk& w, float dw, const XBlk& x, float& acc) {
+    int s = x.init;
+    if (WT == T_Q4_0) {
+        int sh = 0;
+        s = dp4a_us(w.a.x, x.lo.x, s);
+        s = dp4a_us(w.a.y, x.lo.y, s);
+        s = dp4a_us(w.a.z, x.lo.z, s);
+        s = dp4a_us(w.a.w, x.lo.w, s);
+        sh = dp4a_us(w.b.x, x.hi.x, sh);
+        sh = dp4a_us(w.b.y, x.hi.y, sh);
+        sh = dp4a_us(w.b.z, x.hi.z, sh);
+        sh = dp4a_us(w.b.w, x.hi.w, sh);
+        s += sh >> 4;
+    } else {
+        s = __dp4a((int)w.a.x, x.lo.x, s);
+        s = __dp4a((int)w.a.y, x.lo.y, s);
+        s = __dp4a((int)w.a.z, x.lo.z, s);
+        s = __dp4a((int)w.a.w, x.lo.w, s);
+        s = __dp4a((int)w.b.x, x.hi.x, s);
+        s = __dp4a((int)w.b.y, x.hi.y, s);
+        s = __dp4a((int)w.b.z, x.hi.z, s);
+        s = __dp4a((int)w.b.w, x.hi.w, s);
+    }
+    acc = __fmaf_rn(__fsub_rn(__int_as_float(s), 12582912.0f), __fmul_rn(dw, x.d), acc);
+}
+
+__device__ __forceinline__ float half_lo(unsigned w) {
+    return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFFu)));
+}
+__device__ __forceinline__ float half_hi(unsigned w) {
+    return __half2float(__ushort_as_half((unsigned short)(w >> 16)));
+}
+
+__device__ double cta_sum_d(double v, double* sh) {
+    v = warp_sum_d(v);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) sh[w] = v;
+    __syncthreads();
+    double t = 0.0;
+    for (int i = 0; i < kW; ++i) t += sh[i];
+    return t;
+}
+
+// Quantize f32 input row m (after RMSNorm / gamma) into the shared-memory activation stage:
+// two threads per block, elements 0-15 and 16-31 (quantize_row_q8_0, x86 AVX2 build).
+template <int WT>
+__device__ void stage_f32(const DArgs& a, int m, int4* sxa, int4* sxb, float* sxd, int* sxi,
+                          double* shd) {
+    const int nb = a.nb, K = nb * 32;
+    const float* xr = a.xf + (size_t)m * a.xf_stride;
+    float scale = 1.0f;
+    if (a.rms) {
+        // RMSNorm (ggml-cpu/ops.cpp:3859-3920): fp32 squares summed in double
+        double s = 0.0;
+        const float4* x4 = (const float4*)xr;
+        for (int k4 = threadIdx.x; k4 < K / 4; k4 += kT) {
+            const float4 t = x4[k4];
+            s += (double)__fmul_rn(t.x, t.x) + (double)__fmul_rn(t.y, t.y);
+            s += (double)__fmul_rn(t.z, t.z) + (double)__fmul_rn(t.w, t.w);
+        }
+        const double tot = cta_sum_d(s, shd);
+        const float mean = (float)(tot / (double)K);
+        scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.eps)));
+    }
+    // two threads per block; whole warps take part (the pair shares its amax by a shuffle)
+    const int items = (2 * nb + 31) / 32 * 32;
+    for (int it = threadIdx.x; it < items; it += kT) {
+        const int b = it >> 1, hh = it & 1;
+        float v[16];
+        float amax = 0.0f;
+        if (b < nb) {
+            const float4* src = (const float4*)(xr + (size_t)b * 32 + hh * 16);
+            const float4* gsrc = a.gamma ? (const float4*)(a.gamma + (size_t)b * 32 + hh * 16) : nullptr;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float4 t = src[i];
+                const float e[4] = {t.x, t.y, t.z, t.w};
+                float g[4] = {1.0f, 1.0f, 1.0f, 1.0f};
+                if (gsrc) {
+                    const float4 gg = __ldg(gsrc + i);
+                    g[0] = gg.x; g[1] = gg.y; g[2] = gg.z; g[3] = gg.w;
+                }
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float u = e[j];
+                    if (a.rms) u = __fmul_rn(u, scale);
+                    if (gsrc) u = __fmul_rn(u, g[j]);
+                    v[4 * i + j] = u;
+                    amax = fmaxf(amax, fabsf(u));
+                }
+            }
+        }
+        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+        int4 qw = make_int4(0, 0, 0, 0);
+        float d16 = 0.0f;
+        if (b < nb) {
+            d16 = __half2float(__float2half_rn(__fdiv_rn(amax, 127.0f)));
+            const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+            unsigned w[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                w[j] = 0;
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                    w[j] |= ((unsigned)__float2int_rn(__fmul_rn(v[4 * j + e], id)) & 0xFF) << (8 * e);
+            }
+            qw = make_int4((int)w[0], (int)w[1], (int)w[2], (int)w[3]);
+        }
+        const int one = 0x01010101;
+        int part = __dp4a(qw.x, one, __dp4a(qw.y, one, __dp4a(qw.z, one, __dp4a(qw.w, one, 0))));
+        part += __shfl_xor_sync(0xffffffffu, part, 1);
+        if (b < nb) {
+            if (hh == 0) {
+                sxa[b] = qw;
+                sxd[b] = d16;
+                sxi[b] = WT == T_Q4_0 ? kMagic - 8 * part : kMagic;
+            } else {
+                sxb[b] = qw;
+            }
+        }
+    }
+}
+
+template <int WT>
+__device__ void stage_q8(const DArgs& a, int m, int4* sxa, int4* sxb, float* sxd, int* sxi) {
+    for (int b = threadIdx.x; b < a.nb; b += kT) {
+        const int4* src = (const int4*)(a.xq + (size_t)m * a.nb * 32 + (size_t)b * 32);
+        const int4 lo = src[0], hi = src[1];
+        sxa[b] = lo;
+        sxb[b] = hi;
+        sxd[b] = a.xd[(size_t)m * a.nb + b];
+        sxi[b] = chain_init<WT>(lo, hi);
+    }
+}
+
+// MAXM: activation rows (1 or 2; M <= MAXM at run time).  BPL > 0: activation blocks
+// b = lane + 32 j (j < BPL) in registers; BPL == 0: read from the shared-memory stage.
+template <int WT, int MAXM, int BPL>
+__global__ void __launch_bounds__(kT, 1) k_dgemv(DArgs a) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ uint64_t bars[kW][kMaxSlots];
+    __shared__ double shd[kW];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nb = a.nb, M = a.M;
+    const int64_t rb = a.rb;
+    const int D = a.slots;
+    uint8_t* ring = smem + (size_t)warp * D * rb;
+    // activation stage of row m: [sxa nb][sxb nb][sxd nb][sxi nb]
+    uint8_t* stage = smem + (size_t)kW * D * rb;
+    auto sxa = [&](int m) { return (int4*)(stage + (size_t)m * nb * 40); };
+    auto sxb = [&](int m) { return sxa(m) + nb; };
+    auto sxd = [&](int m) { return (float*)(sxb(m) + nb); };
+    auto sxi = [&](int m) { return (int*)(sxd(m) + nb); };
+
+    // this warp's units and its row sequence (SwiGLU: gate, up, gate, up, ...)
+    const int gw = blockIdx.x * kW + warp, tw = gridDim.x * kW;
+    const int u0 = (int)((int64_t)a.units * gw / tw), u1 = (int)((int64_t)a.units * (gw + 1) / tw);
+    const int per = a.swiglu ? 2 : 1;
+    const int nrows = (u1 - u0) * per;
+    auto row_of = [&](int i) -> int64_t {
+        const int u = u0 + i / per;
+        return a.swiglu ? (int64_t)u + (i & 1) * (int64_t)a.F : (int64_t)u;
+    };
+    uint64_t* bar = bars[warp];
+    if (lane == 0) {
+        for (int s = 0; s < D; ++s) mbar_init(&bar[s], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        for (int i = 0; i < D && i < nrows; ++i)
+            fetch_row(ring + (size_t)i * rb, a.w + row_of(i) * rb, (uint32_t)rb, &bar[i]);
+    }
+    __syncwarp();
+
+    pdl_wait();
+    const bool staged = a.xf || BPL == 0;
+    for (int m = 0; m < M; ++m) {
+        if (a.xf) stage_f32<WT>(a, m, sxa(m), sxb(m), sxd(m), sxi(m), shd);
+        else if (BPL == 0) stage_q8<WT>(a, m, sxa(m), sxb(m), sxd(m), sxi(m));
+        if (a.xf && a.rms) __syncthreads();  // shd is reused by the next row's reduction
+    }
+    if (staged) __syncthreads();
+    pdl_launch();
+
+    XBlk x[MAXM][BPL > 0 ? BPL : 1];
+    if (BPL > 0) {
+#pragma unroll
+        for (int m = 0; m < MAXM; ++m) {
+#pragma unroll
+            for (int j = 0; j < BPL; ++j) {
+                const int b = lane + 32 * j;
+                XBlk& xb = x[m][BPL > 0 ? j : 0];
+                xb.lo = xb.hi = make_int4(0, 0, 0, 0);
+                xb.d = 0.0f;
+                xb.init = kMagic;
+                if (m < M && b < nb) {
+                    if (a.xf) {
+                        xb.lo = sxa(m)[b];
+                        xb.hi = sxb(m)[b];
+                        xb.d = sxd(m)[b];
+                        xb.init = sxi(m)[b];
+                    } else {
+                        const int4* src = (const int4*)(a.xq + (size_t)m * nb * 32 + (size_t)b * 32);
+                        xb.lo = src[0];
+                        xb.hi = src[1];
+                        xb.d = a.xd[(size_t)m * nb + b];
+                        xb.init = chain_init<WT>(xb.lo, xb.hi);
+                    }
+                }
+            }
+        }
+    }
+
+    const int64_t qbytes = (int64_t)nb * (WT == T_Q8_0 ? 32 : 16);
+    float gate[MAXM];
+    bool ok = true;
+    int i = 0;
+    for (; i < nrows; ++i) {
+        const int s = i % D;
+        if (!__all_sync(0xffffffffu, mbar_wait(&bar[s], (uint32_t)(i / D) & 1u))) {
+            ok = false;
+            break;
+        }
+        const uint8_t* slot = ring + (size_t)s * rb;
+        const uint8_t* sc = slot + qbytes;
+        float acc[MAXM];
+#pragma unroll
+        for (int m = 0; m < MAXM; ++m) acc[m] = 0.0f;
+        if (BPL > 0) {
+#pragma unroll
+            for (int jp = 0; jp < (BPL + 1) / 2; ++jp) {
+                const unsigned sw =
+                    64 * jp + lane < nb ? *(const unsigned*)(sc + jp * 128 + lane * 4) : 0u;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int j = 2 * jp + h;
+                    const int b = lane + 32 * j;
+                    if (j < BPL && b < nb) {
+                        const WBlk wb = load_w<WT>(slot, nb, b);
+                        const float dw = h ? half_hi(sw) : half_lo(sw);
+#pragma unroll
+                        for (int m = 0; m < MAXM; ++m)
+                            if (m < M) block_term<WT>(wb, dw, x[m][BPL > 0 ? j : 0], acc[m]);
+                    }
+                }
+            }
+        } else {
+            for (int b0 = 0; b0 < nb; b0 += 64) {
+                const int b = b0 + lane;
+                const unsigned sw = b < nb ? *(const unsigned*)(sc + (b0 >> 6) * 128 + lane * 4) : 0u;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int bb = b + 32 * h;
+                    if (bb < nb) {
+                        const WBlk wb = load_w<WT>(slot, nb, bb);
+                        const float dw = h ? half_hi(sw) : half_lo(sw);
+#pragma unroll
+                        for (int m = 0; m < MAXM; ++m) {
+                            if (m < M) {
+                                XBlk xb;
+                                xb.lo = sxa(m)[bb];
+                                xb.hi = sxb(m)[bb];
+                                xb.d = sxd(m)[bb];
+                                xb.init = sxi(m)[bb];
+                                block_term<WT>(wb, dw, xb, acc[m]);
+                            }
+                        }
+                    }
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && i + D < nrows) {  // the slot is consumed: refill it
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            fetch_row(ring + (size_t)s * rb, a.w + row_of(i + D) * rb, (uint32_t)rb, &bar[s]);
+        }
+#pragma unroll
+        for (int m = 0; m < MAXM; ++m) {
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1)
+                acc[m] = __fadd_rn(acc[m], __shfl_xor_sync(0xffffffffu, acc[m], off));
+        }
+        if (a.swiglu) {
+            if (i & 1) {
+#pragma unroll
+                for (int m = 0; m < MAXM; ++m)
+                    if (m < M && lane == m)
+                        a.y[(size_t)m * a.y_stride + u0 + i / 2] = __fmul_rn(ref_v_silu(gate[m]), acc[m]);
+            } else {
+#pragma unroll
+                for (int m = 0; m < MAXM; ++m) gate[m] = acc[m];
+            }
+        } else {
+            const int64_t row = u0 + i;
+#pragma unroll
+            for (int m = 0; m < MAXM; ++m) {
+                if (m < M && lane == m) {
+                    float r = acc[m];
+                    if (a.bias) r = __fadd_rn(r, a.bias[row]);
+                    if (a.residual) r = __fadd_rn(a.residual[(size_t)m * a.res_stride + row], r);
+                    a.y[(size_t)m * a.y_stride + row] = r;
+                }
+            }
+        }
+    }
+    if (!ok) {
+        if (lane == 0) {
+            atomicExch(&dgemv_error_word, 1);
+            // the copies this warp issued and did not consume: wait for them (bounded)
+            for (int k = i; k < nrows && k < i + D; ++k) mbar_wait(&bar[k % D], (uint32_t)(k / D) & 1u);
+        }
+        __syncwarp();
+    }
+}
+
+template <int WT, int MAXM, int BPL>
+void launch_t(const DArgs& a, size_t smem, int grid, cudaStream_t st) {
+    auto kern = k_dgemv<WT, MAXM, BPL>;
+    int dev = 0;
+    GB_CUDA(cudaGetDevice(&dev));
+    GB_CHECK(dev >= 0 && dev < 64, "dgemv: device ordinal out of range");
+    static std::mutex mu;
+    static bool configured[64] = {};
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!configured[dev]) {
+            GB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         200 * 1024));
+            configured[dev] = true;
+        }
+    }
+    launch_pdl(kern, (unsigned)grid, kT, smem, st, a);
+}
+
+template <int WT, int MAXM>
+void launch_m(const DArgs& a, size_t smem, int grid, cudaStream_t st) {
+    if (a.nb <= 32) launch_t<WT, MAXM, 1>(a, smem, grid, st);
+    else if (a.nb <= 64) launch_t<WT, MAXM, 2>(a, smem, grid, st);
+    else if (a.nb <= 96) launch_t<WT, MAXM, 3>(a, smem, grid, st);
+    else if (a.nb <= 128) launch_t<WT, MAXM, 4>(a, smem, grid, st);
+    else launch_t<WT, MAXM, 0>(a, smem, grid, st);
+}
+
+template <int WT>
+void launch_w(const DArgs& a, size_t smem, int grid, cudaStream_t st) {
+    if (a.M == 1) launch_m<WT, 1>(a, smem, grid, st);
+    else launch_m<WT, 2>(a, smem, grid, st);
+}
+
+// activation stage: per row and block 16 + 16 quant bytes, the scale and the chain start
+size_t stage_bytes(int nb, int M) { return (size_t)M * nb * (16 + 16 + 4 + 4); }
+
+}  // namespace
+
+bool dgemv_eligible(const GemvArgs& a) {
+    if (a.M < 1 || a.M > 2 || (a.w.type != T_Q4_0 && a.w.type != T_Q8_0) || a.w.K % QK != 0)
+        return false;
+    if (a.w.N <= 0 || a.w.N >= (1LL << 30) || a.w.K >= (1LL << 24)) return false;
+    if (((uintptr_t)a.w.qs & 15) != 0) return false;
+    if (a.yq || a.yd) return false;  // Q8_0 output of the SwiGLU: the tiled GEMV
+    if (a.swiglu && (a.w.N != 2 * a.F || !a.y || a.y_stride != a.F)) return false;
+    if (!a.swiglu && !a.y) return false;
+    if (a.xf) {
+        if (((uintptr_t)a.xf & 15) != 0 || (a.gamma && ((uintptr_t)a.gamma & 15) != 0)) return false;
+        if (a.M > 1 && (a.xf_stride % 4) != 0) return false;
+    } else if (!a.xq || !a.xd || ((uintptr_t)a.xq & 15) != 0) {
+        return false;
+    }
+    const int64_t rb = qrow_bytes(a.w.type, a.w.K);
+    const size_t need = (size_t)kW * rb + stage_bytes((int)(a.w.K / QK), a.M);
+    return need <= 200 * 1024;
+}
+
+void launch_dgemv(const GemvArgs& a, cudaStream_t st) {
+    GB_CHECK(dgemv_eligible(a), "dgemv: arguments outside the single-row bulk-copy GEMV");
+    DArgs d;
+    d.w = (const uint8_t*)a.w.qs;
+    d.rb = qrow_bytes(a.w.type, a.w.K);
+    d.nb = (int)(a.w.K / QK);
+    d.M = a.M;
+    d.xf_stride = a.xf_stride;
+    d.y_stride = a.y_stride;
+    d.res_stride = a.res_stride;
+    d.swiglu = a.swiglu ? 1 : 0;
+    d.F = (int)a.F;
+    d.units = (int)(a.swiglu ? a.F : a.w.N);
+    d.xq = a.xq;
+    d.xd = a.xd;
+    d.xf = a.xf;
+    d.rms = a.xf && a.xf_rms ? 1 : 0;
+    d.eps = a.eps;
+    d.gamma = a.xf ? a.gamma : nullptr;
+    d.y = a.y;
+    d.bias = a.swiglu ? nullptr : a.bias;
+    d.residual = a.swiglu ? nullptr : a.residual;
+    const size_t stage = stage_bytes(d.nb, d.M);
+    int slots = (int)std::min<int64_t>(kMaxSlots, (int64_t)(kRingBudget - stage) / (kW * d.rb));
+    if (slots < 1) slots = 1;
+    d.slots = slots;
+    const size_t smem = (size_t)kW * slots * d.rb + stage;
+    int dev = 0;
+    GB_CUDA(cudaGetDevice(&dev));
+    // one CTA per SM, fewer when there are not 8 units per CTA
+    const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(sm_count(dev), (d.units + kW - 1) / kW));
+    if (a.w.type == T_Q4_0) launch_w<T_Q4_0>(d, smem, grid, st);
+    else launch_w<T_Q8_0>(d, smem, grid, st);
+}
+
+int dgemv_error() {
+    int v = 0;
+    GB_CUDA(cudaMemcpyFromSymbol(&v, dgemv_error_word, sizeof(int)));
+    return v;
+}
+
+}  // namespace gb

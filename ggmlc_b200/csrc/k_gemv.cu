@@ -479,6 +479,10 @@ void launch_gemv_fused(const GemvArgs& a, cudaStream_t st) {
         }
         return;
     }
+    if (a.M <= kGemvRouteRows && dgemv_eligible(a)) {  // 1-2 rows: the bulk-copy GEMV
+        launch_dgemv(a, st);
+        return;
+    }
     if (!a.xf && (a.M > kGemvRouteRows || !gemv_fits(a.w.type, a.w.K, a.M, false, false))) {
         launch_mmv(a, st);  // batched decode: the tensor-core kernel
         return;

@@ -126,6 +126,13 @@ bool gemv_fused_fits(int64_t K, int M);
 // result does not depend on M (nor on the epilogue mode).  Programmatic dependent launch.
 constexpr int kMmvMaxRows = 16;
 void launch_mmv(const GemvArgs& a, cudaStream_t st);
+// Single-row decode GEMV with bulk-copy weight rings (k_dgemv.cu): M == 1, Q8_0 or f32 input (the
+// GemvArgs prologues), f32 output (+bias, +residual) or SwiGLU to f32 (no Q8_0 output).
+// launch_gemv_fused sends every eligible single-row call here.  dgemv_error() reads its sticky
+// error word (non-zero after one of its bounded waits ran out).
+bool dgemv_eligible(const GemvArgs& a);
+void launch_dgemv(const GemvArgs& a, cudaStream_t st);
+int dgemv_error();
 // Prefill gate_up matmul (M > 16) with the SwiGLU epilogue of GemvArgs (k_matmul.cu): Q8_0 input,
 // N == 2F, F % 64 == 0, no bias / residual; outputs f32 y and/or Q8_0 yq, yd.
 void launch_gemm_swiglu(const GemvArgs& a, cudaStream_t st);

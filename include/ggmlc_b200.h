@@ -256,13 +256,18 @@ int gb_mul_mat_q(int type, const void* wq, int64_t N, int64_t K,
 int gb_gemm_tc(int type, const void* wq, int64_t N, int64_t K, const int8_t* xq, const float* xd,
                int64_t M, float* y, const float* bias, const float* residual, void* stream);
 int gb_gemm_tc_error(void);
+int gb_gemv_error(void);
 /* Decode matmul with fused prologue / epilogue, same arithmetic as gb_mul_mat_q.  Input: Q8_0
  * rows (xq, xd; xq 16-byte aligned; any M: the GEMV for 1-2 rows, the tensor-core decode kernel
  * for 3-16, the block GEMM above) or, when xf != NULL, f32 rows [M][K], M <= 4, put through
  * RMS_NORM(eps) (* gamma) and Q8_0 quantization first (the GEMV).  Output: y [M][N] (+bias, +residual); or with swiglu != 0 the
  * SwiGLU of row pairs (n, n+N/2) as f32 y [M][N/2] and/or Q8_0 yq [M][N/2], yd [M][N/64].
- * Replaces the ggml-cuda sequence rms_norm_f32 -> quantize_q8_1 -> mul_mat_vec_q ->
- * unary_gated_op_kernel (norm.cu:77, quantize.cu:54, mmvq.cu:508, unary.cu:263). */
+ * A single row without Q8_0 output runs on the bulk-copy GEMV (weight rows streamed into
+ * per-warp shared-memory rings).  Replaces the ggml-cuda sequence rms_norm_f32 ->
+ * quantize_q8_1 -> mul_mat_vec_q -> unary_gated_op_kernel (norm.cu:77, quantize.cu:54,
+ * mmvq.cu:508, unary.cu:263).  gb_gemv_error: the sticky error word of that single-row kernel,
+ * 0 while every bounded wait in it completed, non-zero after one ran out (that launch left its
+ * rows unwritten), -1 if the word cannot be read. */
 int gb_gemv(int type, const void* wq, int64_t N, int64_t K, int64_t M,
             const int8_t* xq, const float* xd, const float* xf, float eps, const float* gamma,
             int swiglu, float* y, int8_t* yq, float* yd, const float* bias,

@@ -8,6 +8,8 @@ the CPU's fp16 accumulator) within 2e-3 of max|y|."""
 
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import pytest
 
@@ -527,3 +529,58 @@ def test_attn_decode_fused(G, Hq, Hkv, hd, kv_pos, ctx):
     assert np.max(np.abs(got - exact)) <= 1e-5 * np.max(np.abs(exact))
     ref_q = O.quantize_q8_0(got.reshape(1, -1)).reshape(-1, 34)
     assert np.array_equal(oq.cpu().numpy(), ref_q[:, 2:].reshape(-1).view(np.int8))
+
+
+@pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_0])
+@pytest.mark.parametrize("K", [576, 4096, 14336])
+@pytest.mark.parametrize("M", [1, 2])
+def test_gemv_bulk_copy_rows(G, wtype, K, M):
+    """The 1-2-row decode GEMV (weight rows streamed by bulk copies into per-warp rings; K up to
+    4096 keeps the activations in registers, longer rows read them from shared memory):
+    bit-exact with the oracle where fp32 summation is exact, with bias and residual; its SwiGLU
+    mode equals the CPU SwiGLU of its own plain outputs; its RMSNorm prologue gives the same
+    bits as the standalone RMSNorm's Q8_0 rows fed to it; its error word stays clear."""
+    torch = G.torch_dev()
+    rng = np.random.default_rng(K * 3 + M + wtype)
+    F = 72
+    N = 2 * F
+    w, x = _int_exact_case(rng, wtype, N, K, M)
+    wq, wd = G.upload_weight(wtype, w, N, K)
+    bias = rng.integers(-4, 5, size=N).astype(np.float32)
+    res = rng.integers(-4, 5, size=(M, N)).astype(np.float32)
+    L = G.lib_fused()
+    xq, xd = G.quantize(G.dev(x), M, K)
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    G.check(L.gb_gemv(wtype, G.ptr(wq), N, K, M, G.ptr(xq), G.ptr(xd), None, 0.0, None, 0,
+                      G.ptr(y), None, None, G.ptr(G.dev(bias)), G.ptr(G.dev(res)), None))
+    ref = res + (O.mul_mat(wtype, w, N, K, x) + bias[None, :]).astype(np.float32)
+    assert np.array_equal(y.cpu().numpy(), ref.astype(np.float32))
+    # SwiGLU of row pairs (n, n + F), f32 out
+    wr = G.random_blocks(rng, wtype, N, K, scale=0.05)
+    wq2, _ = G.upload_weight(wtype, wr, N, K)
+    xr = rng.standard_normal((M, K)).astype(np.float32)
+    xq2, xd2 = G.quantize(G.dev(xr), M, K)
+    gu = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    G.check(L.gb_gemv(wtype, G.ptr(wq2), N, K, M, G.ptr(xq2), G.ptr(xd2), None, 0.0, None, 0,
+                      G.ptr(gu), None, None, None, None, None))
+    h = torch.empty((M, F), dtype=torch.float32, device="cuda")
+    G.check(L.gb_gemv(wtype, G.ptr(wq2), N, K, M, G.ptr(xq2), G.ptr(xd2), None, 0.0, None, 1,
+                      G.ptr(h), None, None, None, None, None))
+    assert np.array_equal(h.cpu().numpy(), O.swiglu(gu.cpu().numpy()))
+    assert _close(gu.cpu().numpy(), O.mul_mat(wtype, wr, N, K, xr))
+    # RMSNorm + gamma prologue: the same bits as the standalone RMSNorm's Q8_0 rows
+    gamma = rng.standard_normal(K).astype(np.float32)
+    x_d, g_d = G.dev(xr * 3), G.dev(gamma)
+    yf = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    G.check(L.gb_gemv(wtype, G.ptr(wq2), N, K, M, None, None, G.ptr(x_d), 1e-5, G.ptr(g_d), 0,
+                      G.ptr(yf), None, None, None, None, None))
+    nq = torch.empty((M, K), dtype=torch.int8, device="cuda")
+    nd = torch.empty((M, K // 32), dtype=torch.float32, device="cuda")
+    G.check(G.lib().gb_rms_norm(G.ptr(x_d), M, K, 1e-5, G.ptr(g_d), None, G.ptr(nq), G.ptr(nd),
+                                None))
+    yq_ = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    G.check(L.gb_gemv(wtype, G.ptr(wq2), N, K, M, G.ptr(nq), G.ptr(nd), None, 0.0, None, 0,
+                      G.ptr(yq_), None, None, None, None, None))
+    assert torch.equal(yf, yq_)
+    L.gb_gemv_error.restype = ctypes.c_int
+    assert L.gb_gemv_error() == 0
