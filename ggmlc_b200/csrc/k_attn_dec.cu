@@ -272,19 +272,20 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(AttnDecArgs a) {
 // At the end the four warps' (m, l, O) are merged in shared memory in warp order and written as
 // the split's partial, in the layout k_attn_combine reads.  The new position's k and v rows are
 // written to the cache by the CTA that holds it and taken from shared memory, never re-read.
-constexpr int kTcWarps = 4;
 constexpr int kTcPos = 16;    // positions per block
 constexpr int kTcDepth = 2;   // ring slots per warp
+constexpr int kMaxCluster = 8;
 
-template <int HD>
+template <int HD, int NW>
 struct TcAttnSmem {
     static constexpr int kRow = HD * 2 + 16;              // bytes per staged K / V / q row
     static constexpr int kSlot = 2 * kTcPos * kRow;       // K block, then V block
     static constexpr int kQ = 16 * kRow;
     static constexpr int kNew = 2 * HD * 2;               // new k, new v (fp16)
-    static constexpr int kRing = kTcWarps * kTcDepth * kSlot;
-    static constexpr int kMerge = kTcWarps * kMaxRk * (HD + 2) * 4;
-    static constexpr int kBytes = kQ + kNew + (kRing > kMerge ? kRing : kMerge);
+    static constexpr int kRing = NW * kTcDepth * kSlot;
+    static constexpr int kMerge = NW * kMaxRk * (HD + 2) * 4;
+    static constexpr int kCm = kMaxRk * (HD + 2) * 4;     // the CTA's merged (acc, M, L)
+    static constexpr int kBytes = kQ + kNew + (kRing > kMerge ? kRing : kMerge) + kCm;
 };
 
 __device__ __forceinline__ void cp_async16z(void* dst, const void* src, bool valid) {
@@ -311,10 +312,29 @@ __device__ __forceinline__ void tc_mma(float (&d)[4], const unsigned (&a)[4], un
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 __device__ __forceinline__ unsigned pack_h2(__half2 h) { return *(unsigned*)&h; }
+// all threads of all CTAs of the cluster; release / acquire orders the shared-memory partials
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n"
+                 "barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// float at the same shared-memory offset as p in the CTA of cluster rank `rank`
+__device__ __forceinline__ float ld_peer(const float* p, int rank) {
+    unsigned addr;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+                 : "=r"(addr)
+                 : "r"((unsigned)__cvta_generic_to_shared(p)), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+    return v;
+}
 
-template <int HD>
-__global__ void __launch_bounds__(kTcWarps * 32) k_attn_decode_tc(AttnDecArgs a) {
-    using SM = TcAttnSmem<HD>;
+// CL: the CTAs of one (KV head, row) form a thread-block cluster (gridDim.x of them) and merge
+// their partials through distributed shared memory at the end (no workspace, no merge launch);
+// otherwise each CTA writes its partial for k_attn_combine.
+template <int HD, int NW, bool CL>
+__global__ void __launch_bounds__(NW * 32) k_attn_decode_tc(AttnDecArgs a) {
+    constexpr int kTcWarps = NW;
+    using SM = TcAttnSmem<HD, NW>;
     constexpr int KS = HD / 16;   // k-steps of the score product = 16-dim groups of the output
     constexpr int NTO = HD / 8;   // output n-tiles
     constexpr int R = SM::kRow;
@@ -510,8 +530,12 @@ __global__ void __launch_bounds__(kTcWarps * 32) k_attn_decode_tc(AttnDecArgs a)
         }
     }
     __syncthreads();
-    float* part = a.part + (int64_t)row * gridDim.x * a.Hq * (HD + 4) +
-                  ((int64_t)blockIdx.x * a.Hq + (int64_t)hk * rk) * (HD + 4);
+    // this CTA's merged partial: to the workspace (split path) or to its own shared memory
+    // (cluster path: [kMaxRk][HD] acc, then [kMaxRk] M, [kMaxRk] L)
+    float* cm = (float*)(ring_all + (SM::kRing > SM::kMerge ? SM::kRing : SM::kMerge));
+    float* part = CL ? nullptr
+                     : a.part + (int64_t)row * gridDim.x * a.Hq * (HD + 4) +
+                           ((int64_t)blockIdx.x * a.Hq + (int64_t)hk * rk) * (HD + 4);
     for (int e = threadIdx.x; e < rk * HD; e += kTcWarps * 32) {
         const int h = e / HD, d = e % HD;
         float M = -INFINITY;
@@ -526,7 +550,8 @@ __global__ void __launch_bounds__(kTcWarps * 32) k_attn_decode_tc(AttnDecArgs a)
                     acc = __fmaf_rn(mo[(w * kMaxRk + h) * HD + d], expf(mw - M), acc);
             }
         }
-        part[h * (HD + 4) + 4 + d] = acc;
+        if (CL) cm[h * HD + d] = acc;
+        else part[h * (HD + 4) + 4 + d] = acc;
         if (d == 0) {
             float L = 0.0f;
             if (M != -INFINITY) {
@@ -536,9 +561,57 @@ __global__ void __launch_bounds__(kTcWarps * 32) k_attn_decode_tc(AttnDecArgs a)
                     if (mw != -INFINITY) L = __fmaf_rn(ml[w * kMaxRk + h], expf(mw - M), L);
                 }
             }
-            part[h * (HD + 4) + 0] = M;
-            part[h * (HD + 4) + 1] = L;
+            if (CL) {
+                cm[kMaxRk * HD + h] = M;
+                cm[kMaxRk * HD + kMaxRk + h] = L;
+            } else {
+                part[h * (HD + 4) + 0] = M;
+                part[h * (HD + 4) + 1] = L;
+            }
         }
+    }
+    if (CL) {
+        // every CTA of the cluster has its partial in shared memory; the rk * HD outputs, in
+        // 32-element blocks (one Q8_0 block each), are dealt to the warps of the cluster, and
+        // each lane merges one element over the cluster's CTAs in rank order (the weights and
+        // the order of k_attn_combine)
+        cluster_sync_all();
+        const int C = (int)gridDim.x, me = (int)blockIdx.x;
+        const int nob = rk * HD / 32;
+        for (int ob = me + C * warp; ob < nob; ob += C * kTcWarps) {
+            const int e = ob * 32 + lane, h = e / HD, d = e % HD;
+            float Mc[kMaxCluster], Lc[kMaxCluster], Ac[kMaxCluster];
+#pragma unroll
+            for (int c = 0; c < kMaxCluster; ++c) {
+                Mc[c] = -INFINITY;
+                Lc[c] = Ac[c] = 0.0f;
+                if (c < C) {
+                    Ac[c] = ld_peer(cm + h * HD + d, c);
+                    Mc[c] = ld_peer(cm + kMaxRk * HD + h, c);
+                    Lc[c] = ld_peer(cm + kMaxRk * HD + kMaxRk + h, c);
+                }
+            }
+            float M = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < kMaxCluster; ++c) M = fmaxf(M, Mc[c]);
+            float L = 0.0f, v = 0.0f;
+#pragma unroll
+            for (int c = 0; c < kMaxCluster; ++c) {
+                const float w = Mc[c] == -INFINITY ? 0.0f : expf(Mc[c] - M);
+                L += Lc[c] * w;
+                v += Ac[c] * w;
+            }
+            v = v * (L == 0.0f ? 0.0f : 1.0f / L);
+            const int64_t oi = ((int64_t)row * a.Hq + (int64_t)hk * rk + h) * HD + d;
+            if (a.o) a.o[oi] = v;
+            if (a.oq) {  // the warp holds one 32-element block of one head
+                float d16, q;
+                q8_block(v, lane, d16, q);
+                a.oq[oi] = (int8_t)__float2int_rn(q);
+                if (lane == 0) a.od[oi / 32] = d16;
+            }
+        }
+        cluster_sync_all();  // no CTA leaves while a peer may still read its shared memory
     }
 }
 
@@ -601,39 +674,70 @@ size_t dec_smem() {
            kMaxRk * 12 + (size_t)kMaxRk * HD * 4;
 }
 
-template <int HD>
-void launch_dec(const AttnDecArgs& a, cudaStream_t st) {
-    const size_t smem = dec_smem<HD>();
+// cudaFuncAttributeMaxDynamicSharedMemorySize of one kernel, set once per device
+template <auto KERN>
+void set_max_smem(size_t bytes) {
     int dev = 0;
     GB_CUDA(cudaGetDevice(&dev));
     static std::mutex mu;
-    static bool configured[64] = {};
-    {
-        std::lock_guard<std::mutex> lock(mu);
-        if (!configured[dev & 63]) {
-            GB_CUDA(cudaFuncSetAttribute(k_attn_decode<HD>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-            configured[dev & 63] = true;
-        }
+    static bool done[64] = {};
+    std::lock_guard<std::mutex> lock(mu);
+    if (!done[dev & 63]) {
+        GB_CUDA(cudaFuncSetAttribute(KERN, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+        done[dev & 63] = true;
     }
-    if (HD <= 128) {  // tensor-core kernel
-        constexpr size_t tsm = TcAttnSmem<HD <= 128 ? HD : 128>::kBytes;
-        static bool tc_configured[64] = {};
-        {
-            std::lock_guard<std::mutex> lock(mu);
-            if (!tc_configured[dev & 63]) {
-                GB_CUDA(cudaFuncSetAttribute(k_attn_decode_tc<HD <= 128 ? HD : 128>,
-                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)tsm));
-                tc_configured[dev & 63] = true;
-            }
+}
+
+// programmatic dependent launch of a cluster kernel: clusters of cx CTAs along x
+template <typename... P>
+void launch_cluster_pdl(void (*kern)(P...), dim3 grid, dim3 block, size_t smem, unsigned cx,
+                        cudaStream_t st, const AttnDecArgs& a) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cx;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    GB_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
+}
+
+template <int HD, int NW>
+void launch_cluster(const AttnDecArgs& a, int C, cudaStream_t st) {
+    constexpr size_t tsm = TcAttnSmem<HD, NW>::kBytes;
+    set_max_smem<k_attn_decode_tc<HD, NW, true>>(tsm);
+    launch_cluster_pdl(k_attn_decode_tc<HD, NW, true>,
+                       dim3((unsigned)C, (unsigned)a.Hkv, (unsigned)a.rows), NW * 32, tsm,
+                       (unsigned)C, st, a);
+}
+
+template <int HD>
+void launch_dec(const AttnDecArgs& a, cudaStream_t st) {
+    if (HD <= 128) {
+        constexpr int H = HD <= 128 ? HD : 128;
+        const int C = attn_decode_cluster(a.Hkv, HD, a.ctx, a.rows);
+        if (C > 0) {  // one launch: the cluster merges its CTAs' partials
+            launch_cluster<H, 4>(a, C, st);
+            return;
         }
-        launch_pdl(k_attn_decode_tc<HD <= 128 ? HD : 128>,
-                   dim3((unsigned)a.splits, (unsigned)a.Hkv, (unsigned)a.rows), kTcWarps * 32, tsm,
-                   st, a);
+        constexpr size_t tsm = TcAttnSmem<H, 4>::kBytes;
+        set_max_smem<k_attn_decode_tc<H, 4, false>>(tsm);
+        launch_pdl(k_attn_decode_tc<H, 4, false>,
+                   dim3((unsigned)a.splits, (unsigned)a.Hkv, (unsigned)a.rows), 4 * 32, tsm, st, a);
     } else {
+        const size_t smem = dec_smem<HD>();
+        set_max_smem<k_attn_decode<HD>>(smem);
         launch_pdl(k_attn_decode<HD>, dim3((unsigned)a.splits, (unsigned)a.Hkv, (unsigned)a.rows),
                    kDecThreads, smem, st, a);
     }
+    GB_CHECK(a.part != nullptr, "attn_decode: this shape needs the split workspace");
     launch_pdl(k_attn_combine<HD>, dim3((unsigned)a.Hq, (unsigned)a.rows), HD, 0, st, a);
 }
 
@@ -657,6 +761,19 @@ int attn_decode_splits(int64_t Hkv, int64_t max_kv, int rows) {
     if (s > max_kv) s = max_kv;
     if (s > kMaxSplits) s = kMaxSplits;
     return (int)(s < 1 ? 1 : s);
+}
+
+int attn_decode_cluster(int64_t Hkv, int64_t hd, int64_t ctx, int rows) {
+    if ((hd != 64 && hd != 128) || Hkv <= 0 || ctx <= 0) return 0;
+    // about one CTA per SM over the launch, at most kMaxCluster per (row, KV head)
+    const int64_t units = Hkv * std::max(rows, 1);
+    int64_t C = (148 + units - 1) / units;
+    C = std::max<int64_t>(1, std::min<int64_t>(C, kMaxCluster));
+    // each of a CTA's 4 warps walks at most 4 blocks of 16 positions (a CTA stays under 80 KB of
+    // shared memory, so the GEMVs before and after it share the SM); longer caches take the
+    // wider split with the merge launch
+    if ((ctx + C * kTcPos - 1) / (C * kTcPos) > 16) return 0;
+    return (int)C;
 }
 
 size_t attn_decode_workspace(int64_t Hq, int64_t hd, int splits) {

@@ -1,20 +1,22 @@
-// Decode GEMV for one or two activation rows (batch-1/2 decode): y = W x over the split-row layout,
-// the weights streamed from HBM by bulk copies (cp.async.bulk, the TMA engine's linear mode).
+// Decode GEMV for one or two activation rows (batch-1/2 decode): y = W x over the split-row
+// layout, the weights streamed from HBM by bulk copies (cp.async.bulk, the TMA engine's linear
+// mode).
 //
-// Work mapping.  The output units (rows, or SwiGLU row pairs gate n / up n+F) are split into
-// contiguous ranges, one per warp of the grid.  Every warp owns a ring of shared-memory slots,
-// one weight row per slot, each with an mbarrier: lane 0 issues one bulk copy per row (rows are
-// contiguous byte ranges in the split-row layout) and refills a slot as soon as the warp has
-// consumed it, so each warp keeps up to `slots` rows in flight with a handful of instructions
-// per row.  Lanes run along K: lane l takes blocks l, l+32, l+64, ... of a row, whose quants are
-// 16 consecutive bytes (Q4_0; Q8_0 in two 16-byte halves), so the lanes' shared-memory reads are
-// conflict-free, and whose fp16 scales come two to a 32-bit word.
+// Work mapping.  Each CTA owns a contiguous range of output units (rows, or SwiGLU row pairs
+// gate n / up n+F).  A row is cut into chunks of up to 128 blocks (K = 4096); a chunk is a few
+// contiguous byte ranges of the split-row layout (quants, Q8_0 second halves, scales), fetched
+// by one bulk copy each into a slot of a per-warp ring with its own mbarrier.  Every warp works
+// on one fixed chunk index of the rows (rows of up to 128 blocks: every warp takes whole rows;
+// longer rows: the warps split into one group per chunk), so its activation blocks stay in
+// registers; lane 0 refills a slot as soon as the warp has consumed it.  Lanes run along K: lane l
+// takes blocks l, l+32, l+64, l+96 of the chunk, whose quants are 16 consecutive bytes (Q4_0;
+// Q8_0 two 16-byte halves), so the lanes' shared-memory reads are conflict-free, and whose fp16
+// scales come two to a 32-bit word.  A chunk's lane sums are combined by a fixed xor-butterfly;
+// the chunks of a row are added in chunk order at the end of the CTA.
 //
-// Activations.  The Q8_0 activation blocks a lane needs are the same for every row, so they are
-// held in registers (BPL blocks per lane, K <= 4096) or, for longer rows, in shared memory.  They
-// come quantized (xq, xd) or as f32 (xf), quantized by every CTA in its prologue after an
-// optional RMSNorm (+gamma): the same arithmetic as launch_rms_norm and the x86 activation
-// quantizer (ggml-cpu/arch/x86/quants.c:302-392).
+// Activations come quantized (xq, xd) or as f32 (xf), quantized by every CTA in its prologue
+// after an optional RMSNorm (+gamma): the same arithmetic as launch_rms_norm and the x86
+// activation quantizer (ggml-cpu/arch/x86/quants.c:302-392).
 //
 // Arithmetic per 32-element block: the integer dot is exact.  Q4_0: the low nibbles (elements
 // 0-15) and the high nibbles (16-31) are masked out of each 32-bit word as unsigned bytes and
@@ -22,22 +24,23 @@
 // its sum is shifted right by 4 (exact), and the -8 offset of every weight is folded into the
 // chain's start value, -8 * sum(x) of the block.  The chain starts at 1.5 * 2^23, so the int sum
 // becomes a float by one subtraction (exact for |sum| < 2^22).  The block term sumi * (d_w * d_x)
-// accumulates in fp32 per lane; a row's lane sums are combined by a fixed xor-butterfly.  This is
-// the reference's block formula (ggml-cpu/quants.c:225-256 Q4_0, :451-477 Q8_0); the x86 build
-// adds the same terms in another order, so fp32 results agree to rounding.
+// accumulates in fp32 per lane.  This is the reference's block formula (ggml-cpu/quants.c:225-256
+// Q4_0, :451-477 Q8_0); the x86 build adds the same terms in another order, so fp32 results agree
+// to rounding.
 //
 // Epilogues: f32 rows (+bias, +residual), or SwiGLU of each pair, silu(gate) * up (the vector
 // silu of the CPU build, ggml-cpu/vec.h:1255-1262), written as f32 rows of length F.
 //
-// Launch: one CTA of 8 warps per SM (the rings take most of the shared memory), programmatic
-// dependent launch: the first ring of every warp is requested before griddepcontrol.wait, so the
-// weight stream overlaps the tail of the previous kernel; activations are read and outputs
-// written after the wait.  Every mbarrier wait is bounded (about 2 s): past the limit the kernel
-// records an error in dgemv_error (gb_gemv_error), waits (bounded) for the copies it issued and
-// returns.
+// Launch: one CTA of 8 warps per SM, programmatic dependent launch.  The rings stay under half of
+// the shared memory, so the next kernel's CTAs start on an SM while this one finishes; every
+// warp requests its first ring of chunks before griddepcontrol.wait, so the weight stream
+// overlaps the previous kernel; activations are read and outputs written after the wait.  Every
+// mbarrier wait is bounded (about 2 s): past the limit the kernel records an error in
+// dgemv_error (gb_gemv_error), waits (bounded) for the copies it issued and returns.
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.h"
@@ -53,7 +56,9 @@ namespace {
 constexpr int kW = 8;            // warps per CTA
 constexpr int kT = kW * 32;
 constexpr int kMaxSlots = 8;     // ring slots per warp
-constexpr size_t kRingBudget = 168 * 1024;
+constexpr int kCB = 128;         // blocks per chunk
+constexpr int kMaxChunks = 8;    // K up to 32768
+constexpr size_t kRingBudget = 96 * 1024;
 constexpr long long kSpin = 4000000000LL;  // about 2 s at 1.9 GHz
 constexpr int kMagic = 0x4B400000;         // 1.5 * 2^23
 
@@ -61,6 +66,8 @@ struct DArgs {
     const uint8_t* w;
     int64_t rb;        // bytes per weight row
     int nb;            // blocks per row
+    int nc;            // chunks per row (kCB blocks each, the last one shorter)
+    int rows_cta;      // most rows one CTA owns (sizes the chunk partials)
     int units;         // rows, or SwiGLU pairs
     int F;             // SwiGLU: up row of pair n is n + F
     int slots;         // ring slots per warp
@@ -108,17 +115,6 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
         if (clock64() - t0 > kSpin) return false;
     return true;
 }
-// one weight row (bytes, a multiple of 16, 16-byte aligned) into a slot; completion on bar
-__device__ __forceinline__ void fetch_row(void* dst, const void* src, uint32_t bytes,
-                                          uint64_t* bar) {
-    mbar_expect_tx(bar, bytes);
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
-            "r"(su32(dst)),
-        "l"(src), "r"(bytes), "r"(su32(bar))
-        : "memory");
-}
-
 __device__ __forceinline__ int dp4a_us(unsigned a, int b, int c) {
     int d;
     asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
@@ -155,20 +151,6 @@ __device__ __forceinline__ int chain_init(const int4& lo, const int4& hi) {
 struct WBlk {
     uint4 a, b;
 };
-
-template <int WT>
-__device__ __forceinline__ WBlk load_w(const uint8_t* slot, int nb, int b) {
-    WBlk w;
-    if (WT == T_Q4_0) {
-        const uint4 q = *(const uint4*)(slot + (size_t)b * 16);
-        w.a = make_uint4(q.x & 0x0F0F0F0Fu, q.y & 0x0F0F0F0Fu, q.z & 0x0F0F0F0Fu, q.w & 0x0F0F0F0Fu);
-        w.b = make_uint4(q.x & 0xF0F0F0F0u, q.y & 0xF0F0F0F0u, q.z & 0xF0F0F0F0u, q.w & 0xF0F0F0F0u);
-    } else {
-        w.a = *(const uint4*)(slot + (size_t)b * 16);
-        w.b = *(const uint4*)(slot + (size_t)(nb + b) * 16);
-    }
-    return w;
-}
 
 // acc += sumi * (d_w * d_x) of a weight block against one activation block
 template <int WT>
@@ -295,163 +277,167 @@ __device__ void stage_f32(const DArgs& a, int m, int4* sxa, int4* sxb, float* sx
     }
 }
 
+// bytes of one chunk slot: quants (Q8_0: first halves, then second halves), then scales
 template <int WT>
-__device__ void stage_q8(const DArgs& a, int m, int4* sxa, int4* sxb, float* sxd, int* sxi) {
-    for (int b = threadIdx.x; b < a.nb; b += kT) {
-        const int4* src = (const int4*)(a.xq + (size_t)m * a.nb * 32 + (size_t)b * 32);
-        const int4 lo = src[0], hi = src[1];
-        sxa[b] = lo;
-        sxb[b] = hi;
-        sxd[b] = a.xd[(size_t)m * a.nb + b];
-        sxi[b] = chain_init<WT>(lo, hi);
-    }
+constexpr int slot_bytes() {
+    return kCB * (WT == T_Q8_0 ? 32 : 16) + (kCB / 64) * 128;
 }
 
-// MAXM: activation rows (1 or 2; M <= MAXM at run time).  BPL > 0: activation blocks
-// b = lane + 32 j (j < BPL) in registers; BPL == 0: read from the shared-memory stage.
-template <int WT, int MAXM, int BPL>
+// bulk copies of chunk c (kCB blocks from block 128c) of weight row `row` into a slot
+template <int WT>
+__device__ __forceinline__ void fetch_chunk(uint8_t* slot, const DArgs& a, int64_t row, int c,
+                                            uint64_t* bar) {
+    const int c0 = c * kCB, cb = min(kCB, a.nb - c0);
+    const uint8_t* src = a.w + row * a.rb;
+    const uint32_t qb = (uint32_t)cb * 16, sb = (uint32_t)((cb + 63) / 64) * 128;
+    const int qsz = WT == T_Q8_0 ? 32 : 16;
+    mbar_expect_tx(bar, qb * (WT == T_Q8_0 ? 2 : 1) + sb);
+    auto copy = [&](void* dst, const void* from, uint32_t bytes) {
+        asm volatile(
+            "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, "
+            "[%3];" ::"r"(su32(dst)),
+            "l"(from), "r"(bytes), "r"(su32(bar))
+            : "memory");
+    };
+    copy(slot, src + (size_t)c0 * 16, qb);
+    if (WT == T_Q8_0) copy(slot + kCB * 16, src + (size_t)(a.nb + c0) * 16, qb);
+    copy(slot + kCB * qsz, src + (size_t)a.nb * qsz + (size_t)(c0 / 64) * 128, sb);
+}
+
+// MAXM: activation rows (1 or 2; M <= MAXM at run time).
+template <int WT, int MAXM>
 __global__ void __launch_bounds__(kT, 1) k_dgemv(DArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t bars[kW][kMaxSlots];
     __shared__ double shd[kW];
+    constexpr int SB = slot_bytes<WT>();
+    constexpr int QS = WT == T_Q8_0 ? 32 : 16;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int nb = a.nb, M = a.M;
-    const int64_t rb = a.rb;
-    const int D = a.slots;
-    uint8_t* ring = smem + (size_t)warp * D * rb;
-    // activation stage of row m: [sxa nb][sxb nb][sxd nb][sxi nb]
-    uint8_t* stage = smem + (size_t)kW * D * rb;
+    const int nb = a.nb, M = a.M, nc = a.nc, D = a.slots;
+    uint8_t* ring = smem + (size_t)warp * D * SB;
+    // activation stage of row m: [sxa nb][sxb nb][sxd nb][sxi nb]; then the chunk partials
+    uint8_t* stage = smem + (size_t)kW * D * SB;
     auto sxa = [&](int m) { return (int4*)(stage + (size_t)m * nb * 40); };
     auto sxb = [&](int m) { return sxa(m) + nb; };
     auto sxd = [&](int m) { return (float*)(sxb(m) + nb); };
     auto sxi = [&](int m) { return (int*)(sxd(m) + nb); };
+    float* part = (float*)(stage + (size_t)(a.xf ? M : 0) * nb * 40);  // [row][chunk][m]
 
-    // this warp's units and its row sequence (SwiGLU: gate, up, gate, up, ...)
-    const int gw = blockIdx.x * kW + warp, tw = gridDim.x * kW;
-    const int u0 = (int)((int64_t)a.units * gw / tw), u1 = (int)((int64_t)a.units * (gw + 1) / tw);
+    // this CTA's units and rows (SwiGLU: local row 2k is gate k, 2k+1 is up k)
+    const int u0 = (int)((int64_t)a.units * blockIdx.x / gridDim.x);
+    const int u1 = (int)((int64_t)a.units * (blockIdx.x + 1) / gridDim.x);
     const int per = a.swiglu ? 2 : 1;
-    const int nrows = (u1 - u0) * per;
+    const int rows = (u1 - u0) * per;
     auto row_of = [&](int i) -> int64_t {
         const int u = u0 + i / per;
         return a.swiglu ? (int64_t)u + (i & 1) * (int64_t)a.F : (int64_t)u;
     };
+    // this warp: chunk `ch` of rows g, g + G, g + 2G, ... (nc <= kW: every warp has a chunk)
+    const int ch = warp % nc, g = warp / nc, G = (kW - ch + nc - 1) / nc;
+    const int nmine = rows > g ? (rows - g + G - 1) / G : 0;
+    __shared__ int s_fail;
+    if (threadIdx.x == 0) s_fail = 0;
     uint64_t* bar = bars[warp];
     if (lane == 0) {
         for (int s = 0; s < D; ++s) mbar_init(&bar[s], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        for (int i = 0; i < D && i < nrows; ++i)
-            fetch_row(ring + (size_t)i * rb, a.w + row_of(i) * rb, (uint32_t)rb, &bar[i]);
+        for (int k = 0; k < D && k < nmine; ++k)
+            fetch_chunk<WT>(ring + (size_t)k * SB, a, row_of(g + k * G), ch, &bar[k]);
     }
     __syncwarp();
 
     pdl_wait();
-    const bool staged = a.xf || BPL == 0;
-    for (int m = 0; m < M; ++m) {
-        if (a.xf) stage_f32<WT>(a, m, sxa(m), sxb(m), sxd(m), sxi(m), shd);
-        else if (BPL == 0) stage_q8<WT>(a, m, sxa(m), sxb(m), sxd(m), sxi(m));
-        if (a.xf && a.rms) __syncthreads();  // shd is reused by the next row's reduction
+    for (int m = 0; m < M && a.xf; ++m) {
+        stage_f32<WT>(a, m, sxa(m), sxb(m), sxd(m), sxi(m), shd);
+        if (a.rms) __syncthreads();  // shd is reused by the next row's reduction
     }
-    if (staged) __syncthreads();
+    if (a.xf) __syncthreads();
     pdl_launch();
 
-    XBlk x[MAXM][BPL > 0 ? BPL : 1];
-    if (BPL > 0) {
+    // the activation blocks of this warp's chunk: b = 128 ch + lane + 32 j
+    XBlk x[MAXM][4];
+    const int c0 = ch * kCB, cb = min(kCB, nb - c0);
 #pragma unroll
-        for (int m = 0; m < MAXM; ++m) {
+    for (int m = 0; m < MAXM; ++m) {
 #pragma unroll
-            for (int j = 0; j < BPL; ++j) {
-                const int b = lane + 32 * j;
-                XBlk& xb = x[m][BPL > 0 ? j : 0];
-                xb.lo = xb.hi = make_int4(0, 0, 0, 0);
-                xb.d = 0.0f;
-                xb.init = kMagic;
-                if (m < M && b < nb) {
-                    if (a.xf) {
-                        xb.lo = sxa(m)[b];
-                        xb.hi = sxb(m)[b];
-                        xb.d = sxd(m)[b];
-                        xb.init = sxi(m)[b];
-                    } else {
-                        const int4* src = (const int4*)(a.xq + (size_t)m * nb * 32 + (size_t)b * 32);
-                        xb.lo = src[0];
-                        xb.hi = src[1];
-                        xb.d = a.xd[(size_t)m * nb + b];
-                        xb.init = chain_init<WT>(xb.lo, xb.hi);
-                    }
+        for (int j = 0; j < 4; ++j) {
+            const int bl = lane + 32 * j, b = c0 + bl;
+            XBlk& xb = x[m][j];
+            xb.lo = xb.hi = make_int4(0, 0, 0, 0);
+            xb.d = 0.0f;
+            xb.init = kMagic;
+            if (m < M && bl < cb) {
+                if (a.xf) {
+                    xb.lo = sxa(m)[b];
+                    xb.hi = sxb(m)[b];
+                    xb.d = sxd(m)[b];
+                    xb.init = sxi(m)[b];
+                } else {
+                    const int4* src = (const int4*)(a.xq + (size_t)m * nb * 32 + (size_t)b * 32);
+                    xb.lo = src[0];
+                    xb.hi = src[1];
+                    xb.d = a.xd[(size_t)m * nb + b];
+                    xb.init = chain_init<WT>(xb.lo, xb.hi);
                 }
             }
         }
     }
 
-    const int64_t qbytes = (int64_t)nb * (WT == T_Q8_0 ? 32 : 16);
     float gate[MAXM];
+#pragma unroll
+    for (int m = 0; m < MAXM; ++m) gate[m] = 0.0f;
     bool ok = true;
-    int i = 0;
-    for (; i < nrows; ++i) {
-        const int s = i % D;
-        if (!__all_sync(0xffffffffu, mbar_wait(&bar[s], (uint32_t)(i / D) & 1u))) {
+    int k = 0;
+    for (; k < nmine; ++k) {
+        const int s = k % D;
+        if (!__all_sync(0xffffffffu, mbar_wait(&bar[s], (uint32_t)(k / D) & 1u))) {
             ok = false;
             break;
         }
-        const uint8_t* slot = ring + (size_t)s * rb;
-        const uint8_t* sc = slot + qbytes;
+        const uint8_t* slot = ring + (size_t)s * SB;
+        const uint8_t* sc = slot + kCB * QS;
         float acc[MAXM];
 #pragma unroll
         for (int m = 0; m < MAXM; ++m) acc[m] = 0.0f;
-        if (BPL > 0) {
 #pragma unroll
-            for (int jp = 0; jp < (BPL + 1) / 2; ++jp) {
-                const unsigned sw =
-                    64 * jp + lane < nb ? *(const unsigned*)(sc + jp * 128 + lane * 4) : 0u;
+        for (int jp = 0; jp < 2; ++jp) {
+            const unsigned sw = 64 * jp + lane < cb ? *(const unsigned*)(sc + jp * 128 + lane * 4) : 0u;
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int j = 2 * jp + h;
-                    const int b = lane + 32 * j;
-                    if (j < BPL && b < nb) {
-                        const WBlk wb = load_w<WT>(slot, nb, b);
-                        const float dw = h ? half_hi(sw) : half_lo(sw);
-#pragma unroll
-                        for (int m = 0; m < MAXM; ++m)
-                            if (m < M) block_term<WT>(wb, dw, x[m][BPL > 0 ? j : 0], acc[m]);
+            for (int h = 0; h < 2; ++h) {
+                const int j = 2 * jp + h, bl = lane + 32 * j;
+                if (bl < cb) {
+                    WBlk wb;
+                    if (WT == T_Q4_0) {
+                        const uint4 q = *(const uint4*)(slot + (size_t)bl * 16);
+                        wb.a = make_uint4(q.x & 0x0F0F0F0Fu, q.y & 0x0F0F0F0Fu, q.z & 0x0F0F0F0Fu, q.w & 0x0F0F0F0Fu);
+                        wb.b = make_uint4(q.x & 0xF0F0F0F0u, q.y & 0xF0F0F0F0u, q.z & 0xF0F0F0F0u, q.w & 0xF0F0F0F0u);
+                    } else {
+                        wb.a = *(const uint4*)(slot + (size_t)bl * 16);
+                        wb.b = *(const uint4*)(slot + (size_t)(kCB + bl) * 16);
                     }
-                }
-            }
-        } else {
-            for (int b0 = 0; b0 < nb; b0 += 64) {
-                const int b = b0 + lane;
-                const unsigned sw = b < nb ? *(const unsigned*)(sc + (b0 >> 6) * 128 + lane * 4) : 0u;
+                    const float dw = h ? half_hi(sw) : half_lo(sw);
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int bb = b + 32 * h;
-                    if (bb < nb) {
-                        const WBlk wb = load_w<WT>(slot, nb, bb);
-                        const float dw = h ? half_hi(sw) : half_lo(sw);
-#pragma unroll
-                        for (int m = 0; m < MAXM; ++m) {
-                            if (m < M) {
-                                XBlk xb;
-                                xb.lo = sxa(m)[bb];
-                                xb.hi = sxb(m)[bb];
-                                xb.d = sxd(m)[bb];
-                                xb.init = sxi(m)[bb];
-                                block_term<WT>(wb, dw, xb, acc[m]);
-                            }
-                        }
-                    }
+                    for (int m = 0; m < MAXM; ++m)
+                        if (m < M) block_term<WT>(wb, dw, x[m][j], acc[m]);
                 }
             }
         }
         __syncwarp();
-        if (lane == 0 && i + D < nrows) {  // the slot is consumed: refill it
+        if (lane == 0 && k + D < nmine) {  // the slot is consumed: refill it
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            fetch_row(ring + (size_t)s * rb, a.w + row_of(i + D) * rb, (uint32_t)rb, &bar[s]);
+            fetch_chunk<WT>(ring + (size_t)s * SB, a, row_of(g + (k + D) * G), ch, &bar[s]);
         }
 #pragma unroll
         for (int m = 0; m < MAXM; ++m) {
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1)
                 acc[m] = __fadd_rn(acc[m], __shfl_xor_sync(0xffffffffu, acc[m], off));
+        }
+        const int i = g + k * G;  // local row
+        if (nc > 1) {             // chunk partial: rows are finished below
+            if (lane < M) part[((size_t)i * nc + ch) * MAXM + lane] = lane == 0 ? acc[0] : acc[MAXM - 1];
+            continue;
         }
         if (a.swiglu) {
             if (i & 1) {
@@ -479,16 +465,41 @@ __global__ void __launch_bounds__(kT, 1) k_dgemv(DArgs a) {
     if (!ok) {
         if (lane == 0) {
             atomicExch(&dgemv_error_word, 1);
+            s_fail = 1;
             // the copies this warp issued and did not consume: wait for them (bounded)
-            for (int k = i; k < nrows && k < i + D; ++k) mbar_wait(&bar[k % D], (uint32_t)(k / D) & 1u);
+            for (int q = k; q < nmine && q < k + D; ++q) mbar_wait(&bar[q % D], (uint32_t)(q / D) & 1u);
         }
         __syncwarp();
     }
+    if (nc > 1) {
+        // rows cut into chunks: every row's chunk sums in chunk order, then the epilogue
+        __syncthreads();
+        if (s_fail) return;  // a wait ran out in this CTA: its partials are incomplete
+        for (int t = threadIdx.x; t < (u1 - u0) * M; t += kT) {
+            const int uu = t / M, m = t % M;
+            float r[2];
+            for (int hh = 0; hh < per; ++hh) {
+                const int i = uu * per + hh;
+                float v = part[((size_t)i * nc) * MAXM + m];
+                for (int c = 1; c < nc; ++c) v = __fadd_rn(v, part[((size_t)i * nc + c) * MAXM + m]);
+                r[hh] = v;
+            }
+            if (a.swiglu) {
+                a.y[(size_t)m * a.y_stride + u0 + uu] = __fmul_rn(ref_v_silu(r[0]), r[1]);
+            } else {
+                const int64_t row = u0 + uu;
+                float v = r[0];
+                if (a.bias) v = __fadd_rn(v, a.bias[row]);
+                if (a.residual) v = __fadd_rn(a.residual[(size_t)m * a.res_stride + row], v);
+                a.y[(size_t)m * a.y_stride + row] = v;
+            }
+        }
+    }
 }
 
-template <int WT, int MAXM, int BPL>
+template <int WT, int MAXM>
 void launch_t(const DArgs& a, size_t smem, int grid, cudaStream_t st) {
-    auto kern = k_dgemv<WT, MAXM, BPL>;
+    auto kern = k_dgemv<WT, MAXM>;
     int dev = 0;
     GB_CUDA(cudaGetDevice(&dev));
     GB_CHECK(dev >= 0 && dev < 64, "dgemv: device ordinal out of range");
@@ -505,30 +516,30 @@ void launch_t(const DArgs& a, size_t smem, int grid, cudaStream_t st) {
     launch_pdl(kern, (unsigned)grid, kT, smem, st, a);
 }
 
-template <int WT, int MAXM>
-void launch_m(const DArgs& a, size_t smem, int grid, cudaStream_t st) {
-    if (a.nb <= 32) launch_t<WT, MAXM, 1>(a, smem, grid, st);
-    else if (a.nb <= 64) launch_t<WT, MAXM, 2>(a, smem, grid, st);
-    else if (a.nb <= 96) launch_t<WT, MAXM, 3>(a, smem, grid, st);
-    else if (a.nb <= 128) launch_t<WT, MAXM, 4>(a, smem, grid, st);
-    else launch_t<WT, MAXM, 0>(a, smem, grid, st);
-}
-
 template <int WT>
 void launch_w(const DArgs& a, size_t smem, int grid, cudaStream_t st) {
-    if (a.M == 1) launch_m<WT, 1>(a, smem, grid, st);
-    else launch_m<WT, 2>(a, smem, grid, st);
+    if (a.M == 1) launch_t<WT, 1>(a, smem, grid, st);
+    else launch_t<WT, 2>(a, smem, grid, st);
 }
 
 // activation stage: per row and block 16 + 16 quant bytes, the scale and the chain start
 size_t stage_bytes(int nb, int M) { return (size_t)M * nb * (16 + 16 + 4 + 4); }
+
+size_t ring_budget() {
+    static const size_t v = [] {
+        const char* e = getenv("GGMLC_B200_DGEMV_RING");  // tuning: ring bytes per CTA
+        const long long b = e ? atoll(e) : 0;
+        return b > 0 ? (size_t)b : kRingBudget;
+    }();
+    return v;
+}
 
 }  // namespace
 
 bool dgemv_eligible(const GemvArgs& a) {
     if (a.M < 1 || a.M > 2 || (a.w.type != T_Q4_0 && a.w.type != T_Q8_0) || a.w.K % QK != 0)
         return false;
-    if (a.w.N <= 0 || a.w.N >= (1LL << 30) || a.w.K >= (1LL << 24)) return false;
+    if (a.w.N <= 0 || a.w.N >= (1LL << 30) || a.w.K > (int64_t)kCB * QK * kMaxChunks) return false;
     if (((uintptr_t)a.w.qs & 15) != 0) return false;
     if (a.yq || a.yd) return false;  // Q8_0 output of the SwiGLU: the tiled GEMV
     if (a.swiglu && (a.w.N != 2 * a.F || !a.y || a.y_stride != a.F)) return false;
@@ -539,9 +550,7 @@ bool dgemv_eligible(const GemvArgs& a) {
     } else if (!a.xq || !a.xd || ((uintptr_t)a.xq & 15) != 0) {
         return false;
     }
-    const int64_t rb = qrow_bytes(a.w.type, a.w.K);
-    const size_t need = (size_t)kW * rb + stage_bytes((int)(a.w.K / QK), a.M);
-    return need <= 200 * 1024;
+    return true;
 }
 
 void launch_dgemv(const GemvArgs& a, cudaStream_t st) {
@@ -550,6 +559,7 @@ void launch_dgemv(const GemvArgs& a, cudaStream_t st) {
     d.w = (const uint8_t*)a.w.qs;
     d.rb = qrow_bytes(a.w.type, a.w.K);
     d.nb = (int)(a.w.K / QK);
+    d.nc = (d.nb + kCB - 1) / kCB;
     d.M = a.M;
     d.xf_stride = a.xf_stride;
     d.y_stride = a.y_stride;
@@ -566,15 +576,16 @@ void launch_dgemv(const GemvArgs& a, cudaStream_t st) {
     d.y = a.y;
     d.bias = a.swiglu ? nullptr : a.bias;
     d.residual = a.swiglu ? nullptr : a.residual;
-    const size_t stage = stage_bytes(d.nb, d.M);
-    int slots = (int)std::min<int64_t>(kMaxSlots, (int64_t)(kRingBudget - stage) / (kW * d.rb));
-    if (slots < 1) slots = 1;
-    d.slots = slots;
-    const size_t smem = (size_t)kW * slots * d.rb + stage;
     int dev = 0;
     GB_CUDA(cudaGetDevice(&dev));
     // one CTA per SM, fewer when there are not 8 units per CTA
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(sm_count(dev), (d.units + kW - 1) / kW));
+    d.rows_cta = (int)((d.units + grid - 1) / grid + 1) * (d.swiglu ? 2 : 1);
+    const size_t sb = a.w.type == T_Q8_0 ? slot_bytes<T_Q8_0>() : slot_bytes<T_Q4_0>();
+    d.slots = (int)std::max<int64_t>(1, std::min<int64_t>(kMaxSlots, (int64_t)(ring_budget() / (kW * sb))));
+    const size_t smem = (size_t)kW * d.slots * sb + (a.xf ? stage_bytes(d.nb, d.M) : 0) +
+                        (d.nc > 1 ? (size_t)d.rows_cta * d.nc * 2 * sizeof(float) : 0);
+    GB_CHECK(smem <= 200 * 1024, "dgemv: shared memory plan too large");
     if (a.w.type == T_Q4_0) launch_w<T_Q4_0>(d, smem, grid, st);
     else launch_w<T_Q8_0>(d, smem, grid, st);
 }

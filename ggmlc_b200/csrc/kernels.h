@@ -263,6 +263,11 @@ struct AttnDecArgs {
 // splits per (row, KV head): about two CTAs per SM over all rows and heads of the launch
 int attn_decode_splits(int64_t Hkv, int64_t max_kv, int rows = 1);
 size_t attn_decode_workspace(int64_t Hq, int64_t hd, int splits);  // per row
+// CTAs per (row, KV head) when decode attention runs as one launch whose thread-block clusters
+// merge their partials in distributed shared memory (head_dim 64 / 128, caches up to a few
+// thousand positions); 0 when it takes the split workspace and the merge launch.  The workspace
+// argument is not read in the first case.
+int attn_decode_cluster(int64_t Hkv, int64_t hd, int64_t ctx, int rows = 1);
 void launch_attn_decode(const AttnDecArgs& a, cudaStream_t st);
 // Size of the per-device static split scratch behind gb_attn_decode_noalloc.
 constexpr size_t kAttnDecStaticWorkBytes = size_t(4) << 20;

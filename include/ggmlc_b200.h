@@ -275,8 +275,11 @@ int gb_gemv(int type, const void* wq, int64_t N, int64_t K, int64_t M,
 /* Decode attention for one new token, fused with its RoPE and KV-cache write: qkv is the f32
  * projection row [(Hq + 2 Hkv) * hd] (q heads, then k, then v); the new k (rotated) and v rows go
  * to cache row kv_pos; o [Hq][hd] f32 and/or oq/od Q8_0.  table / n_pos / n_dims as
- * gb_rope_neox (n_dims 0: no rotation).  work: gb_attn_decode_workspace_bytes().  Replaces
- * rope_neox + k_set_rows + flash_attn_ext_vec (rope.cu:116, set-rows.cu:114, fattn-vec.cuh:21). */
+ * gb_rope_neox (n_dims 0: no rotation).  work: gb_attn_decode_workspace_bytes() of device
+ * scratch for the split partials; with head_dim 64 / 128 and caches up to a few thousand
+ * positions the kernel runs as one launch whose thread-block clusters merge their partials in
+ * distributed shared memory and does not read it.  Replaces rope_neox + k_set_rows +
+ * flash_attn_ext_vec (rope.cu:116, set-rows.cu:114, fattn-vec.cuh:21). */
 size_t gb_attn_decode_workspace_bytes(int64_t Hq, int64_t Hkv, int64_t hd, int64_t ctx);
 int gb_attn_decode(const float* qkv, int64_t Hq, int64_t Hkv, int64_t hd, void* k, void* v,
                    int64_t ctx, int64_t kv_pos, int n_dims, float freq_base, const void* table,

@@ -487,18 +487,21 @@ def test_gemv_swiglu_epilogue(G, wtype, M):
 
 @pytest.mark.parametrize("Hq,Hkv,hd,kv_pos,ctx", [(4, 2, 64, 0, 1024), (9, 3, 64, 300, 1024),
                                                   (32, 8, 128, 700, 1024), (9, 3, 64, 1200, 2048),
-                                                  (32, 8, 128, 1500, 2048)])
+                                                  (32, 8, 128, 1500, 2048),
+                                                  (32, 8, 128, 6000, 8192)])
 def test_attn_decode_fused(G, Hq, Hkv, hd, kv_pos, ctx):
     """Decode attention fused with RoPE and the KV write: cache row kv_pos holds fp16(rope(k)) and
-    fp16(v) bit-exactly, the output matches exact fp64 attention over the rotated q, for caches
-    of 1024 and 2048 positions (split-KV, then the merge launch)."""
+    fp16(v) bit-exactly, the output matches exact fp64 attention over the rotated q.  Caches of
+    1024-2048 positions run as one launch whose thread-block clusters merge their CTAs' partials
+    in distributed shared memory; the 8192-position cache takes the wider split and the merge
+    launch."""
     torch = G.torch_dev()
     rng = np.random.default_rng(Hq + kv_pos)
     base = 500000.0
     qkv = rng.standard_normal((Hq + 2 * Hkv) * hd).astype(np.float32)
     k = rng.standard_normal((Hkv, ctx, hd)).astype(np.float16)
     v = rng.standard_normal((Hkv, ctx, hd)).astype(np.float16)
-    n_pos = 4096
+    n_pos = max(4096, ctx)
     tab = np.empty((n_pos, hd // 2, 2), np.float32)
     L = G.lib_fused()
     G.lib().gb_rope_table_fill(tab.ctypes.data, n_pos, hd, base)
@@ -551,8 +554,9 @@ def test_gemv_bulk_copy_rows(G, wtype, K, M):
     L = G.lib_fused()
     xq, xd = G.quantize(G.dev(x), M, K)
     y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    bias_d, res_d = G.dev(bias), G.dev(res)  # held: the launch reads them asynchronously
     G.check(L.gb_gemv(wtype, G.ptr(wq), N, K, M, G.ptr(xq), G.ptr(xd), None, 0.0, None, 0,
-                      G.ptr(y), None, None, G.ptr(G.dev(bias)), G.ptr(G.dev(res)), None))
+                      G.ptr(y), None, None, G.ptr(bias_d), G.ptr(res_d), None))
     ref = res + (O.mul_mat(wtype, w, N, K, x) + bias[None, :]).astype(np.float32)
     assert np.array_equal(y.cpu().numpy(), ref.astype(np.float32))
     # SwiGLU of row pairs (n, n + F), f32 out

@@ -2,7 +2,9 @@
 
 The GPU test calls it through the C ABI twice in a row (new tokens at kv_pos and kv_pos + 1) and
 checks each call bit-for-bit against gb_attn_decode with a caller-allocated workspace, on
-separate copies of the KV cache.  The file name sorts last so the test also runs after every
+separate copies of the KV cache.  Caches of up to a few thousand positions run without split
+scratch (thread-block clusters merge in distributed shared memory); the 8192-position case takes
+the split path and so reads and writes the static array.  The file name sorts last so the test also runs after every
 other test of a full session; it needs no state from them."""
 
 from __future__ import annotations
@@ -43,13 +45,14 @@ def test_noalloc_rejects_oversized_scratch():
 @pytest.mark.gpu
 @pytest.mark.skipif(not cuda_available(), reason="needs a CUDA device")
 @pytest.mark.parametrize("Hq,Hkv,hd,ctx,kv_pos", [(32, 8, 128, 1024, 700), (4, 2, 64, 512, 0),
-                                                   (64, 8, 128, 4096, 3000)])
+                                                   (64, 8, 128, 4096, 3000),
+                                                   (32, 8, 128, 8192, 6000)])
 def test_noalloc_matches_workspace_entry_point(Hq, Hkv, hd, ctx, kv_pos):
     torch = G.torch_dev()
     L = _lib()
     rng = np.random.default_rng(1000 + Hq + kv_pos)
     base = 500000.0
-    n_pos = 4096
+    n_pos = max(4096, ctx)
     tab = np.empty((n_pos, hd // 2, 2), np.float32)
     G.lib().gb_rope_table_fill(tab.ctypes.data, n_pos, hd, base)
     scale = float(np.float32(1.0) / np.sqrt(np.float32(hd)))
