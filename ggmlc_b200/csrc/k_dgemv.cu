@@ -327,14 +327,17 @@ __global__ void __launch_bounds__(kT, 1) k_dgemv(DArgs a) {
     const int u0 = (int)((int64_t)a.units * blockIdx.x / gridDim.x);
     const int u1 = (int)((int64_t)a.units * (blockIdx.x + 1) / gridDim.x);
     const int per = a.swiglu ? 2 : 1;
-    const int rows = (u1 - u0) * per;
     auto row_of = [&](int i) -> int64_t {
         const int u = u0 + i / per;
         return a.swiglu ? (int64_t)u + (i & 1) * (int64_t)a.F : (int64_t)u;
     };
-    // this warp: chunk `ch` of rows g, g + G, g + 2G, ... (nc <= kW: every warp has a chunk)
+    // this warp: chunk `ch` of units g, g + G, g + 2G, ... (nc <= kW: every warp has a chunk);
+    // item k is row `per * unit + k % per` of unit g + (k / per) * G, so a SwiGLU pair's gate
+    // and up rows go through the same warp, one after the other
     const int ch = warp % nc, g = warp / nc, G = (kW - ch + nc - 1) / nc;
-    const int nmine = rows > g ? (rows - g + G - 1) / G : 0;
+    const int nu = u1 - u0;
+    const int nmine = (nu > g ? (nu - g + G - 1) / G : 0) * per;
+    auto item_row = [&](int k) { return (g + (k / per) * G) * per + k % per; };  // local row
     __shared__ int s_fail;
     if (threadIdx.x == 0) s_fail = 0;
     uint64_t* bar = bars[warp];
@@ -343,7 +346,7 @@ __global__ void __launch_bounds__(kT, 1) k_dgemv(DArgs a) {
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         for (int k = 0; k < D && k < nmine; ++k)
-            fetch_chunk<WT>(ring + (size_t)k * SB, a, row_of(g + k * G), ch, &bar[k]);
+            fetch_chunk<WT>(ring + (size_t)k * SB, a, row_of(item_row(k)), ch, &bar[k]);
     }
     __syncwarp();
 
@@ -426,7 +429,7 @@ __global__ void __launch_bounds__(kT, 1) k_dgemv(DArgs a) {
         __syncwarp();
         if (lane == 0 && k + D < nmine) {  // the slot is consumed: refill it
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            fetch_chunk<WT>(ring + (size_t)s * SB, a, row_of(g + (k + D) * G), ch, &bar[s]);
+            fetch_chunk<WT>(ring + (size_t)s * SB, a, row_of(item_row(k + D)), ch, &bar[s]);
         }
 #pragma unroll
         for (int m = 0; m < MAXM; ++m) {
@@ -434,7 +437,7 @@ __global__ void __launch_bounds__(kT, 1) k_dgemv(DArgs a) {
             for (int off = 16; off > 0; off >>= 1)
                 acc[m] = __fadd_rn(acc[m], __shfl_xor_sync(0xffffffffu, acc[m], off));
         }
-        const int i = g + k * G;  // local row
+        const int i = item_row(k);  // local row
         if (nc > 1) {             // chunk partial: rows are finished below
             if (lane < M) part[((size_t)i * nc + ch) * MAXM + lane] = lane == 0 ? acc[0] : acc[MAXM - 1];
             continue;
