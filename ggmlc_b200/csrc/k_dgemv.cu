@@ -53,12 +53,14 @@ __device__ int dgemv_error_word;
 
 namespace {
 
-constexpr int kW = 8;            // warps per CTA
+constexpr int kW = 16;           // warps per CTA
 constexpr int kT = kW * 32;
 constexpr int kMaxSlots = 8;     // ring slots per warp
-constexpr int kCB = 128;         // blocks per chunk
-constexpr int kMaxChunks = 8;    // K up to 32768
-constexpr size_t kRingBudget = 96 * 1024;
+// blocks per chunk: 128 for Q4_0 (2304-byte slots), 64 for Q8_0 (2176-byte slots)
+template <int WT>
+constexpr int chunk_blocks() { return WT == T_Q8_0 ? 64 : 128; }
+constexpr int kMaxChunks = 16;   // chunks per row at most (a warp group per chunk)
+constexpr size_t kRingBudget = 112 * 1024;
 constexpr long long kSpin = 4000000000LL;  // about 2 s at 1.9 GHz
 constexpr int kMagic = 0x4B400000;         // 1.5 * 2^23
 
@@ -66,7 +68,7 @@ struct DArgs {
     const uint8_t* w;
     int64_t rb;        // bytes per weight row
     int nb;            // blocks per row
-    int nc;            // chunks per row (kCB blocks each, the last one shorter)
+    int nc;            // chunks per row (chunk_blocks each, the last one shorter)
     int rows_cta;      // most rows one CTA owns (sizes the chunk partials)
     int units;         // rows, or SwiGLU pairs
     int F;             // SwiGLU: up row of pair n is n + F
@@ -101,7 +103,7 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
 __device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 20000;\n"
         " selp.u32 %0, 1, 0, p;\n}"
         : "=r"(ok)
         : "r"(su32(b)), "r"(parity)
@@ -280,13 +282,14 @@ __device__ void stage_f32(const DArgs& a, int m, int4* sxa, int4* sxb, float* sx
 // bytes of one chunk slot: quants (Q8_0: first halves, then second halves), then scales
 template <int WT>
 constexpr int slot_bytes() {
-    return kCB * (WT == T_Q8_0 ? 32 : 16) + (kCB / 64) * 128;
+    return chunk_blocks<WT>() * (WT == T_Q8_0 ? 32 : 16) + (chunk_blocks<WT>() / 64) * 128;
 }
 
-// bulk copies of chunk c (kCB blocks from block 128c) of weight row `row` into a slot
+// bulk copies of chunk c (blocks from c * chunk_blocks) of weight row `row` into a slot
 template <int WT>
 __device__ __forceinline__ void fetch_chunk(uint8_t* slot, const DArgs& a, int64_t row, int c,
                                             uint64_t* bar) {
+    constexpr int kCB = chunk_blocks<WT>();
     const int c0 = c * kCB, cb = min(kCB, a.nb - c0);
     const uint8_t* src = a.w + row * a.rb;
     const uint32_t qb = (uint32_t)cb * 16, sb = (uint32_t)((cb + 63) / 64) * 128;
@@ -307,6 +310,8 @@ __device__ __forceinline__ void fetch_chunk(uint8_t* slot, const DArgs& a, int64
 // MAXM: activation rows (1 or 2; M <= MAXM at run time).
 template <int WT, int MAXM>
 __global__ void __launch_bounds__(kT, 1) k_dgemv(DArgs a) {
+    constexpr int kCB = chunk_blocks<WT>();
+    constexpr int BPL = kCB / 32;  // activation blocks per lane
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ uint64_t bars[kW][kMaxSlots];
     __shared__ double shd[kW];
@@ -359,12 +364,12 @@ __global__ void __launch_bounds__(kT, 1) k_dgemv(DArgs a) {
     pdl_launch();
 
     // the activation blocks of this warp's chunk: b = 128 ch + lane + 32 j
-    XBlk x[MAXM][4];
+    XBlk x[MAXM][BPL];
     const int c0 = ch * kCB, cb = min(kCB, nb - c0);
 #pragma unroll
     for (int m = 0; m < MAXM; ++m) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
+        for (int j = 0; j < BPL; ++j) {
             const int bl = lane + 32 * j, b = c0 + bl;
             XBlk& xb = x[m][j];
             xb.lo = xb.hi = make_int4(0, 0, 0, 0);
@@ -404,7 +409,7 @@ __global__ void __launch_bounds__(kT, 1) k_dgemv(DArgs a) {
 #pragma unroll
         for (int m = 0; m < MAXM; ++m) acc[m] = 0.0f;
 #pragma unroll
-        for (int jp = 0; jp < 2; ++jp) {
+        for (int jp = 0; jp < BPL / 2; ++jp) {
             const unsigned sw = 64 * jp + lane < cb ? *(const unsigned*)(sc + jp * 128 + lane * 4) : 0u;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
@@ -542,7 +547,8 @@ size_t ring_budget() {
 bool dgemv_eligible(const GemvArgs& a) {
     if (a.M < 1 || a.M > 2 || (a.w.type != T_Q4_0 && a.w.type != T_Q8_0) || a.w.K % QK != 0)
         return false;
-    if (a.w.N <= 0 || a.w.N >= (1LL << 30) || a.w.K > (int64_t)kCB * QK * kMaxChunks) return false;
+    const int64_t cbk = a.w.type == T_Q8_0 ? chunk_blocks<T_Q8_0>() : chunk_blocks<T_Q4_0>();
+    if (a.w.N <= 0 || a.w.N >= (1LL << 30) || a.w.K > cbk * QK * kMaxChunks) return false;
     if (((uintptr_t)a.w.qs & 15) != 0) return false;
     if (a.yq || a.yd) return false;  // Q8_0 output of the SwiGLU: the tiled GEMV
     if (a.swiglu && (a.w.N != 2 * a.F || !a.y || a.y_stride != a.F)) return false;
@@ -562,7 +568,8 @@ void launch_dgemv(const GemvArgs& a, cudaStream_t st) {
     d.w = (const uint8_t*)a.w.qs;
     d.rb = qrow_bytes(a.w.type, a.w.K);
     d.nb = (int)(a.w.K / QK);
-    d.nc = (d.nb + kCB - 1) / kCB;
+    const int64_t cbk = a.w.type == T_Q8_0 ? chunk_blocks<T_Q8_0>() : chunk_blocks<T_Q4_0>();
+    d.nc = (d.nb + (int)cbk - 1) / (int)cbk;
     d.M = a.M;
     d.xf_stride = a.xf_stride;
     d.y_stride = a.y_stride;

@@ -1,34 +1,42 @@
 // Prefill MUL_MAT (M > 16 activation rows) on the 5th-generation tensor cores: tcgen05.mma
-// kind::i8 with accumulators in tensor memory, per-block fp16 scales applied by epilogue warps.
+// kind::i8 with accumulators in tensor memory, operands brought in by the TMA engine, per-block
+// fp16 scales applied by epilogue warps.
 //
 // Arithmetic.  One tcgen05.mma (M = 128 weight rows, N = 128 activation rows, K = 32) per
-// 32-element block writes every exact int32 block dot of a 128 x 128 tile into a tensor-memory
-// accumulator.  Epilogue warps load it, add the 1.5*2^23 bias as an integer (so the bits read as
-// the float 12582912 + sumi) and subtract it in fp32, multiply by d_w * d_x and accumulate the
-// block terms in fp32 registers — the block formula of the reference's vec_dot
-// (ggml-cpu/quants.c:225-256, :451-477) with the integer part exact.  Q4_0 nibbles are widened
-// in shared memory to 16 * (q - 8) (exact in int8); their weight scales are divided by 16 to
-// compensate.
+// 32-element block adds every exact int32 block dot of a 128 x 128 tile onto a tensor-memory
+// accumulator that holds 1.5 * 2^23 (0x4B400000): the epilogue reads the bits as the float
+// 12582912 + sumi, subtracts 12582912 (exact), multiplies by d_w * d_x and accumulates the block
+// terms in fp32 registers, then writes 0x4B400000 back for the next block — the block formula of
+// the reference's vec_dot (ggml-cpu/quants.c:225-256, :451-477) with the integer part exact.
+// Q4_0 nibbles are widened in shared memory to 16 * (q - 8) (exact in int8); their weight scales
+// are divided by 16 to compensate.
 //
-// Work split per CTA (128 weight rows x 128 activation rows, 12 warps):
-//   warps 0-2   producers: cp.async of activations / weights / scales for a stage of 4 blocks
-//               into the canonical no-swizzle K-major layout (8-row x 16-byte core matrices,
-//               K-adjacent core matrices 2048 B apart, row groups 128 B apart), Q4_0 nibble
-//               widening and scale conversion, then mbarrier "full";
+// A K stage is 4 consecutive blocks.  Per stage the TMA engine loads (tile mode, no swizzle, no
+// multicast) 16-byte-wide boxes of 128 rows straight into the canonical K-major layout of the
+// MMA (8-row x 16-byte core matrices; the two 16-byte halves of a block 2048 B apart): the weight
+// quants (Q8_0 both halves; Q4_0 the packed nibbles), the activation quants, the 16-byte scale
+// word of every weight row (4 fp16 scales of the stage) and the 4 fp32 activation scales of every
+// activation row.
+//
+// Warps (20, one CTA per SM):
+//   warp 0      TMA producer (one thread), stage ring of kTS stages;
+//   warps 1-2   Q4_0 nibble widening, activation scales transposed to [block][row], then mbarrier
+//               "ready" (the MMA and the epilogue wait on it);
 //   warp 3      MMA issuer (one thread) and tensor-memory owner: 4 accumulators of 128 columns,
-//               one tcgen05.mma + tcgen05.commit per block;
-//   warps 4-11  epilogue: warp w reads tensor-memory lanes 32*(w%4).. (its weight rows) and
-//               columns 64*((w-4)/4).. (activation rows) of each finished block with
-//               tcgen05.ld, releases the accumulator as soon as the loads land, then scales.
+//               one per block of a stage, one tcgen05.mma + tcgen05.commit per block;
+//   warps 4-19  epilogue: warp w reads tensor-memory lanes 32*(w%4).. (its weight rows) and 32
+//               columns (activation rows) 32*((w-4)/4).. of each finished block with tcgen05.ld,
+//               writes the bias word back with tcgen05.st, releases the accumulator, scales.
 // Every wait on an mbarrier is bounded: past the limit the kernel records an error in
 // gemm_tc_error, stops issuing, waits (bounded) for its tensor-core work to drain, frees the
 // tensor memory and returns.
-//
-// K order: a stage takes blocks {64g+2j, 64g+2j+1, 64g+32+2j, 64g+32+2j+1}, the order in which
-// the weight scale region stores them, so one 8-byte copy brings a row's four scales.
+#include <cuda.h>
 #include <cuda_fp16.h>
 
+#include <cstring>
+#include <map>
 #include <mutex>
+#include <tuple>
 
 #include "common.h"
 #include "kernels.h"
@@ -40,27 +48,40 @@ namespace {
 
 constexpr int kTM = 128;            // weight rows per tile (MMA M, tensor-memory lanes)
 constexpr int kTN = 128;            // activation rows per tile (MMA N, tensor-memory columns)
-constexpr int kTB = 4;              // blocks per stage
+constexpr int kTB = 4;              // blocks per stage = tensor-memory accumulators
 constexpr int kTS = 4;              // stages in the ring
-constexpr int kTBufs = 4;           // tensor-memory accumulators (128 columns each)
-constexpr int kProd = 96;           // producer threads (warps 0-2)
+constexpr int kHelpWarp0 = 1, kHelpWarps = 2;
 constexpr int kMmaWarp = 3;
-constexpr int kEpiWarp0 = 4, kEpiWarps = 8;
+constexpr int kEpiWarp0 = 4, kEpiWarps = 16;
 constexpr int kTThreads = (kEpiWarp0 + kEpiWarps) * 32;
-constexpr int kTmemCols = 512;
+constexpr int kTmemCols = kTB * kTN;
 constexpr uint32_t kBiasBits = 0x4B400000u;      // 1.5 * 2^23
 constexpr long long kSpinCycles = 4000000000LL;  // about 2 s at 1.9 GHz
 
+// one stage in shared memory
 template <int WT>
 struct TcStage {
-    static constexpr int kA = kTB * 4096;                           // weights, widened to int8
-    static constexpr int kB = kTB * 4096;                           // activations
+    static constexpr int kA = kTB * 4096;                           // weights as int8, MMA layout
+    static constexpr int kB = kTB * 4096;                           // activations, MMA layout
     static constexpr int kRaw = WT == T_Q4_0 ? kTB * kTM * 16 : 0;  // packed Q4_0 nibbles
-    static constexpr int kWsr = kTM * 8;                            // 4 fp16 weight scales per row
-    static constexpr int kWs = kTB * kTM * 4;                       // fp32 weight scales [block][row]
-    static constexpr int kXs = kTB * kTN * 4;                       // fp32 activation scales
-    static constexpr int kBytes = kA + kB + kRaw + kWsr + kWs + kXs;
+    static constexpr int kWs = kTM * 16;                            // a row's scale word
+    static constexpr int kXr = kTN * 16;                            // 4 fp32 scales per act. row
+    static constexpr int kXt = kTB * kTN * 4;                       // the same, [block][row]
+    static constexpr int kBytes = kA + kB + kRaw + kWs + kXr + kXt;
+    static constexpr uint32_t kTx = (WT == T_Q4_0 ? kRaw : kA) + kB + kWs + kXr;  // TMA bytes
     static_assert(kBytes % 128 == 0, "stage alignment");
+};
+
+struct TcArgs {
+    int N, K, M;        // weight rows (SwiGLU: 2F), K, activation rows
+    int swi_F;          // > 0: SwiGLU tiles of 64 pairs (gate p, up F + p)
+    float* y;           // plain output [M][y_stride], or SwiGLU f32 output [M][F]
+    int64_t y_stride;
+    const float* bias;
+    const float* residual;
+    int64_t res_stride;
+    int8_t* yq;         // SwiGLU Q8_0 output [M][F], yd [M][F / 32]
+    float* yd;
 };
 
 __device__ int gemm_tc_error_word;
@@ -68,27 +89,16 @@ __device__ int gemm_tc_error_word;
 __device__ __forceinline__ uint32_t su32(const void* p) {
     return (uint32_t)__cvta_generic_to_shared(p);
 }
-__device__ __forceinline__ void cp16z(void* dst, const void* src, bool valid) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(su32(dst)), "l"(src),
-                 "r"(valid ? 16 : 0)
-                 : "memory");
-}
-__device__ __forceinline__ void cp8z(void* dst, const void* src, bool valid) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(su32(dst)), "l"(src),
-                 "r"(valid ? 8 : 0)
-                 : "memory");
-}
-__device__ __forceinline__ void cp4z(void* dst, const void* src, bool valid) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(su32(dst)), "l"(src),
-                 "r"(valid ? 4 : 0)
-                 : "memory");
-}
-
 __device__ __forceinline__ void mbar_init(uint64_t* b, int count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(count) : "memory");
 }
 __device__ __forceinline__ void mbar_arrive(uint64_t* b) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(b)) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)),
+                 "r"(bytes)
+                 : "memory");
 }
 __device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
     uint32_t done;
@@ -114,6 +124,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile
         }
     }
 }
+// TMA tile load of box (x, y) of a 2-D tensor map into shared memory, completion on bar
+__device__ __forceinline__ void tma_load(void* dst, const CUtensorMap* map, int x, int y,
+                                         uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+        "[%0], [%1, {%2, %3}], [%4];" ::"r"(su32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(su32(bar))
+        : "memory");
+}
 
 __device__ __forceinline__ void tc_fence_before() {
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -137,12 +156,12 @@ __device__ __forceinline__ uint64_t smem_desc(const void* p) {
 constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTN >> 3) << 17) |
                             ((uint32_t)(kTM >> 4) << 24);
 
-// D = A * B (enable-input-d false: each block's dots overwrite the accumulator)
+// D += A * B (the accumulator holds the bias word when the block starts)
 __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc) {
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
         " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(0)
+        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(1)
         : "memory");
 }
 
@@ -153,7 +172,7 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t
         "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),        \
         "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
 
-// issue a load of 32 consecutive columns of this thread's tensor-memory lane (no wait)
+// 32 consecutive columns of this thread's tensor-memory lane
 __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
@@ -162,65 +181,60 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
         : "r"(taddr)
         : "memory");
 }
+// the bias word into 32 consecutive columns of this thread's lane
+__device__ __forceinline__ void tmem_st_bias32(uint32_t taddr) {
+    const uint32_t b = kBiasBits;
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
+        "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
+        "r"(b)
+        : "memory");
+}
 __device__ __forceinline__ void tmem_wait_ld() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
-// 32 block terms of one accumulator slice: acc[j] += (v - bias) * (dw * dx)
-__device__ __forceinline__ void scale_acc(const uint32_t (&v)[32], float dw, const float* dx,
-                                          float2* acc) {
-    const float2 bias2 = make_float2(12582912.0f, 12582912.0f);
-    const float2 dw2 = make_float2(dw, dw);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const float4 x4 = *(const float4*)(dx + 4 * j);
-        const float2 p0 = mul2(dw2, make_float2(x4.x, x4.y));
-        const float2 p1 = mul2(dw2, make_float2(x4.z, x4.w));
-        const float2 f0 = sub2(make_float2(__uint_as_float(v[4 * j] + kBiasBits),
-                                           __uint_as_float(v[4 * j + 1] + kBiasBits)),
-                               bias2);
-        const float2 f1 = sub2(make_float2(__uint_as_float(v[4 * j + 2] + kBiasBits),
-                                           __uint_as_float(v[4 * j + 3] + kBiasBits)),
-                               bias2);
-        acc[2 * j] = fma2(f0, p0, acc[2 * j]);
-        acc[2 * j + 1] = fma2(f1, p1, acc[2 * j + 1]);
-    }
+__device__ __forceinline__ void tmem_wait_st() {
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+// the epilogue warps only (named barrier 1)
+__device__ __forceinline__ void epi_sync() {
+    asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
 }
 
 template <int WT>
 __global__ void __launch_bounds__(kTThreads, 1)
-    k_gemm_tc(const uint8_t* __restrict__ qs, int N, int K, const int8_t* __restrict__ xq,
-              const float* __restrict__ xd, int M, float* __restrict__ y, int64_t y_stride,
-              MatmulEpilogue ep) {
+    k_gemm_tc(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
+              const __grid_constant__ CUtensorMap tms, TcArgs a) {
     using S = TcStage<WT>;
-    extern __shared__ __align__(128) uint8_t tsm[];
-    __shared__ __align__(8) uint64_t bar_full[kTS], bar_empty[kTS], bar_tfull[kTBufs],
-        bar_tempty[kTBufs], bar_done;
+    extern __shared__ __align__(1024) uint8_t tsm[];
+    __shared__ __align__(8) uint64_t bar_full[kTS], bar_ready[kTS], bar_empty[kTS],
+        bar_tfull[kTB], bar_tempty[kTB], bar_done;
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
     volatile int* abort = &s_abort;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n0 = blockIdx.x * kTM, m0 = blockIdx.y * kTN;
-    const int nb = K / QK;
-    const int ng = (nb + 63) / 64;
-    const int ns = 16 * (ng - 1) + min(16, (nb - 64 * (ng - 1) + 1) / 2);
-    const int64_t rb = qrow_bytes(WT, K);
-    const int64_t scale_base = (int64_t)nb * quant_bytes(WT);
-    auto gblk = [](int t, int lb) { return 64 * (t >> 4) + 2 * (t & 15) + (lb & 1) + 32 * (lb >> 1); };
+    const bool swi = a.swi_F > 0;
+    const int n0 = blockIdx.x * (swi ? kTM / 2 : kTM), m0 = blockIdx.y * kTN;
+    const int nb = a.K / QK;
+    const int ns = nb / kTB;  // stages (K % 128 == 0)
+    const int qsz = WT == T_Q8_0 ? 32 : 16;
     auto stage = [&](int s) { return tsm + s * S::kBytes; };
 
     if (tid == 0) {
         s_abort = 0;
         for (int s = 0; s < kTS; ++s) {
-            mbar_init(&bar_full[s], kProd);
+            mbar_init(&bar_full[s], 1);
+            mbar_init(&bar_ready[s], kHelpWarps);
             mbar_init(&bar_empty[s], 1 + kEpiWarps);
         }
-        for (int b = 0; b < kTBufs; ++b) {
+        for (int b = 0; b < kTB; ++b) {
             mbar_init(&bar_tfull[b], 1);
             mbar_init(&bar_tempty[b], kEpiWarps);
         }
         mbar_init(&bar_done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     }
     if (warp == kMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
@@ -234,123 +248,103 @@ __global__ void __launch_bounds__(kTThreads, 1)
     tc_fence_after();
     const uint32_t tmem = s_tmem;
 
-    if (warp < kMmaWarp) {
-        // ---------------------------------------------------------------- producers
-        // Copies run rows-fastest (consecutive threads fill consecutive 16-byte slots of a core
-        // matrix column); a thread widens and converts only what it copied itself, so its own
-        // cp.async.wait_group is all the ordering a hand-off needs.
-        const int p = tid;
-        constexpr int L = 2;  // stages between issue and hand-off
-        for (int t = 0; t < ns + L && !*abort; ++t) {
-            if (t < ns) {
+    if (warp == 0) {
+        // ---------------------------------------------------------------- TMA producer
+        if (lane == 0) {
+            for (int t = 0; t < ns && !*abort; ++t) {
                 const int s = t % kTS;
                 if (t >= kTS && !mbar_wait(&bar_empty[s], ((t / kTS) - 1) & 1, abort)) break;
                 uint8_t* st = stage(s);
                 uint8_t* sA = st;
                 uint8_t* sB = st + S::kA;
                 uint8_t* sRaw = sB + S::kB;
-                uint8_t* sWsr = sRaw + S::kRaw;
-                float* sXs = (float*)(sWsr + S::kWsr + S::kWs);
-                // activations: [block][half][row]
-                for (int c = p; c < kTB * 2 * kTN; c += kProd) {
-                    const int r = c & (kTN - 1), lh = c >> 7, lb = lh >> 1, half = lh & 1;
-                    const int gb = gblk(t, lb);
-                    const int m = min(m0 + r, M - 1);
-                    cp16z(sB + lb * 4096 + half * 2048 + r * 16,
-                          xq + (int64_t)m * K + (int64_t)min(gb, nb - 1) * 32 + half * 16,
-                          gb < nb && m0 + r < M);
-                }
-                if (WT == T_Q8_0) {
-                    for (int c = p; c < kTB * 2 * kTM; c += kProd) {
-                        const int r = c & (kTM - 1), lh = c >> 7, lb = lh >> 1, half = lh & 1;
-                        const int gb = gblk(t, lb);
-                        const int n = min(n0 + r, N - 1);
-                        cp16z(sA + lb * 4096 + half * 2048 + r * 16,
-                              qs + (int64_t)n * rb + ((int64_t)half * nb + min(gb, nb - 1)) * 16,
-                              gb < nb);
-                    }
-                } else {
-                    for (int c = p; c < kTB * kTM; c += kProd) {
-                        const int r = c & (kTM - 1), lb = c >> 7;
-                        const int gb = gblk(t, lb);
-                        const int n = min(n0 + r, N - 1);
-                        cp16z(sRaw + (lb * kTM + r) * 16,
-                              qs + (int64_t)n * rb + (int64_t)min(gb, nb - 1) * 16, gb < nb);
-                    }
-                }
-                for (int r = p; r < kTM; r += kProd) {  // weight scales: one 8-byte run per row
-                    const int n = min(n0 + r, N - 1);
-                    cp8z(sWsr + r * 8,
-                         qs + (int64_t)n * rb + scale_base + (t >> 4) * 128 + (t & 15) * 8, true);
-                }
-                for (int c = p; c < kTB * kTN; c += kProd) {  // activation scales [block][row]
-                    const int r = c & (kTN - 1), lb = c >> 7;
-                    const int gb = gblk(t, lb);
-                    const int m = min(m0 + r, M - 1);
-                    cp4z(sXs + lb * kTN + r, xd + (int64_t)m * nb + min(gb, nb - 1),
-                         gb < nb && m0 + r < M);
-                }
-            }
-            asm volatile("cp.async.commit_group;" ::: "memory");
-            if (t >= L) {
-                const int tl = t - L, s = tl % kTS;
-                asm volatile("cp.async.wait_group %0;" ::"n"(L) : "memory");
-                uint8_t* st = stage(s);
-                uint8_t* sA = st;
-                uint8_t* sRaw = st + S::kA + S::kB;
-                uint8_t* sWsr = sRaw + S::kRaw;
-                float* sWs = (float*)(sWsr + S::kWsr);
-                if (WT == T_Q4_0) {  // widen nibbles to int8 16*(q-8): low -> k 0..15, high -> 16..31
-                    for (int c = p; c < kTB * kTM; c += kProd) {
-                        const int r = c & (kTM - 1), lb = c >> 7;
-                        const uint4 w = *(const uint4*)(sRaw + (lb * kTM + r) * 16);
-                        uint4 lo, hi;
-                        lo.x = ((w.x << 4) & 0xF0F0F0F0u) ^ 0x80808080u;
-                        lo.y = ((w.y << 4) & 0xF0F0F0F0u) ^ 0x80808080u;
-                        lo.z = ((w.z << 4) & 0xF0F0F0F0u) ^ 0x80808080u;
-                        lo.w = ((w.w << 4) & 0xF0F0F0F0u) ^ 0x80808080u;
-                        hi.x = (w.x & 0xF0F0F0F0u) ^ 0x80808080u;
-                        hi.y = (w.y & 0xF0F0F0F0u) ^ 0x80808080u;
-                        hi.z = (w.z & 0xF0F0F0F0u) ^ 0x80808080u;
-                        hi.w = (w.w & 0xF0F0F0F0u) ^ 0x80808080u;
-                        uint8_t* d = sA + lb * 4096 + r * 16;
-                        *(uint4*)d = lo;
-                        *(uint4*)(d + 2048) = hi;
-                    }
-                }
-                const float wsc = WT == T_Q4_0 ? 0.0625f : 1.0f;
-                for (int r = p; r < kTM; r += kProd) {  // a row's scales to fp32, local block order
-                    const __half* hs = (const __half*)(sWsr + r * 8);
-#pragma unroll
+                uint8_t* sWs = sRaw + S::kRaw;
+                uint8_t* sXr = sWs + S::kWs;
+                const int b0 = t * kTB;
+                mbar_expect_tx(&bar_full[s], S::kTx);
+                // weight rows of the tile: 128 rows, or gate rows then up rows (64 each)
+                for (int part = 0; part < (swi ? 2 : 1); ++part) {
+                    const int wy = swi ? n0 + part * a.swi_F : n0;
+                    const int ro = part * 64 * 16;  // byte offset of these rows in a 2 KB box
                     for (int lb = 0; lb < kTB; ++lb) {
-                        const int si = ((lb & 1) << 1) | (lb >> 1);
-                        sWs[lb * kTM + r] = __fmul_rn(__half2float(hs[si]), wsc);
+                        if (WT == T_Q8_0) {
+                            tma_load(sA + lb * 4096 + ro, &tmw, (b0 + lb) * 16, wy, &bar_full[s]);
+                            tma_load(sA + lb * 4096 + 2048 + ro, &tmw, (nb + b0 + lb) * 16, wy,
+                                     &bar_full[s]);
+                        } else {
+                            tma_load(sRaw + lb * 2048 + ro, &tmw, (b0 + lb) * 16, wy, &bar_full[s]);
+                        }
                     }
+                    tma_load(sWs + ro, &tmw, nb * qsz + (b0 >> 6) * 128 + (b0 & 31) * 4, wy,
+                             &bar_full[s]);
                 }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                mbar_arrive(&bar_full[s]);
+                for (int lb = 0; lb < kTB; ++lb) {
+                    tma_load(sB + lb * 4096, &tmx, (b0 + lb) * 32, m0, &bar_full[s]);
+                    tma_load(sB + lb * 4096 + 2048, &tmx, (b0 + lb) * 32 + 16, m0, &bar_full[s]);
+                }
+                tma_load(sXr, &tms, b0, m0, &bar_full[s]);
             }
         }
-        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        __syncwarp();
+    } else if (warp < kHelpWarp0 + kHelpWarps) {
+        // ---------------------------------------------------------------- helpers
+        const int p = tid - kHelpWarp0 * 32;  // 0..63
+        for (int t = 0; t < ns && !*abort; ++t) {
+            const int s = t % kTS;
+            if (!__all_sync(0xffffffffu, mbar_wait(&bar_full[s], (t / kTS) & 1, abort))) break;
+            uint8_t* st = stage(s);
+            uint8_t* sA = st;
+            uint8_t* sRaw = st + S::kA + S::kB;
+            const float* sXr = (const float*)(sRaw + S::kRaw + S::kWs);
+            float* sXt = (float*)(sRaw + S::kRaw + S::kWs + S::kXr);
+            if (WT == T_Q4_0) {  // nibbles to int8 16*(q-8): low -> k 0..15, high -> 16..31
+                for (int c = p; c < kTB * kTM; c += 32 * kHelpWarps) {
+                    const int r = c & (kTM - 1), lb = c >> 7;
+                    const uint4 w = *(const uint4*)(sRaw + lb * 2048 + r * 16);
+                    uint4 lo, hi;
+                    lo.x = ((w.x << 4) & 0xF0F0F0F0u) ^ 0x80808080u;
+                    lo.y = ((w.y << 4) & 0xF0F0F0F0u) ^ 0x80808080u;
+                    lo.z = ((w.z << 4) & 0xF0F0F0F0u) ^ 0x80808080u;
+                    lo.w = ((w.w << 4) & 0xF0F0F0F0u) ^ 0x80808080u;
+                    hi.x = (w.x & 0xF0F0F0F0u) ^ 0x80808080u;
+                    hi.y = (w.y & 0xF0F0F0F0u) ^ 0x80808080u;
+                    hi.z = (w.z & 0xF0F0F0F0u) ^ 0x80808080u;
+                    hi.w = (w.w & 0xF0F0F0F0u) ^ 0x80808080u;
+                    uint8_t* d = sA + lb * 4096 + r * 16;
+                    *(uint4*)d = lo;
+                    *(uint4*)(d + 2048) = hi;
+                }
+            }
+            // activation scales [row][block] -> [block][row]
+            for (int r = p; r < kTN; r += 32 * kHelpWarps) {
+                const float4 v = *(const float4*)(sXr + r * 4);
+                sXt[0 * kTN + r] = v.x;
+                sXt[1 * kTN + r] = v.y;
+                sXt[2 * kTN + r] = v.z;
+                sXt[3 * kTN + r] = v.w;
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // widened A -> MMA
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar_ready[s]);
+        }
     } else if (warp == kMmaWarp) {
         // ---------------------------------------------------------------- MMA issuer
         if (lane == 0) {
             bool ok = true;
             for (int t = 0; t < ns && ok; ++t) {
                 const int s = t % kTS;
-                if (!mbar_wait(&bar_full[s], (t / kTS) & 1, abort)) break;
+                if (!mbar_wait(&bar_ready[s], (t / kTS) & 1, abort)) break;
                 tc_fence_after();
                 const uint8_t* st = stage(s);
                 for (int lb = 0; lb < kTB; ++lb) {
-                    const int b = t * kTB + lb, buf = b & (kTBufs - 1);
-                    if (!mbar_wait(&bar_tempty[buf], (b >> 2) & 1, abort)) {
+                    if (!mbar_wait(&bar_tempty[lb], t & 1, abort)) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    tc_mma(tmem + buf * kTN, smem_desc(st + lb * 4096),
+                    tc_mma(tmem + lb * kTN, smem_desc(st + lb * 4096),
                            smem_desc(st + S::kA + lb * 4096));
-                    tc_commit(&bar_tfull[buf]);
+                    tc_commit(&bar_tfull[lb]);
                 }
                 if (ok) tc_commit(&bar_empty[s]);
             }
@@ -367,64 +361,124 @@ __global__ void __launch_bounds__(kTThreads, 1)
         __syncwarp();
     } else {
         // ---------------------------------------------------------------- epilogue
-        const int q = warp & 3, h = (warp - kEpiWarp0) >> 2;
+        const int q = warp & 3, cg = (warp - kEpiWarp0) >> 2;
         const int r = q * 32 + lane;  // weight row of the tile (tensor-memory lane)
-        const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + h * 64;
-        // every accumulator starts free
-        if (lane == 0)
-            for (int buf = 0; buf < kTBufs; ++buf) mbar_arrive(&bar_tempty[buf]);
-        float2 acc[32];
+        const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + cg * 32;
+        // every accumulator starts with the bias word
 #pragma unroll
-        for (int j = 0; j < 32; ++j) acc[j] = make_float2(0.0f, 0.0f);
+        for (int b = 0; b < kTB; ++b) tmem_st_bias32(lane_base + b * kTN);
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0)
+            for (int b = 0; b < kTB; ++b) mbar_arrive(&bar_tempty[b]);
+        float2 acc[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[j] = make_float2(0.0f, 0.0f);
+        const float wsc = WT == T_Q4_0 ? 0.0625f : 1.0f;
+        const float2 bias2 = make_float2(12582912.0f, 12582912.0f);
         // waits are made warp-uniform by a vote: tensor-memory loads and stores need the whole
         // warp converged
         for (int t = 0; t < ns && !*abort; ++t) {
             const int s = t % kTS;
-            if (!__all_sync(0xffffffffu, mbar_wait(&bar_full[s], (t / kTS) & 1, abort))) break;
+            if (!__all_sync(0xffffffffu, mbar_wait(&bar_ready[s], (t / kTS) & 1, abort))) break;
             const uint8_t* st = stage(s);
-            const float* sWs = (const float*)(st + S::kA + S::kB + S::kRaw + S::kWsr);
-            const float* sXs = sWs + kTB * kTM;
+            const uint4 sw = *(const uint4*)(st + S::kA + S::kB + S::kRaw + r * 16);
+            const float* sXt = (const float*)(st + S::kA + S::kB + S::kRaw + S::kWs + S::kXr);
+            // this row's 4 scales: low halves for the first 32 blocks of a 64-block group; the
+            // next block's scale moves to dw0 after each block (the block loop is not unrolled)
+            const int sh = (((t * kTB) >> 5) & 1) * 16;
+            float dw0 = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(sw.x >> sh))), wsc);
+            float dw1 = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(sw.y >> sh))), wsc);
+            float dw2 = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(sw.z >> sh))), wsc);
+            float dw3 = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(sw.w >> sh))), wsc);
             bool ok = true;
 #pragma unroll 1
             for (int lb = 0; lb < kTB; ++lb) {
-                const int b = t * kTB + lb, buf = b & (kTBufs - 1);
-                if (!__all_sync(0xffffffffu, mbar_wait(&bar_tfull[buf], (b >> 2) & 1, abort))) {
+                if (!__all_sync(0xffffffffu, mbar_wait(&bar_tfull[lb], t & 1, abort))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const float dw = sWs[lb * kTM + r];
-                const float* dx = sXs + lb * kTN + h * 64;
-                const uint32_t ta = lane_base + buf * kTN;
-                uint32_t v0[32], v1[32];
-                tmem_ld32(ta, v0);
-                tmem_ld32(ta + 32, v1);
+                uint32_t v[32];
+                tmem_ld32(lane_base + lb * kTN, v);
                 tmem_wait_ld();
+                tmem_st_bias32(lane_base + lb * kTN);
+                tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&bar_tempty[buf]);  // the MMA may refill it now
-                scale_acc(v0, dw, dx, acc);
-                scale_acc(v1, dw, dx + 32, acc + 16);
+                if (lane == 0) mbar_arrive(&bar_tempty[lb]);  // the MMA may use it again
+                const float2 dwv = make_float2(dw0, dw0);
+                dw0 = dw1;
+                dw1 = dw2;
+                dw2 = dw3;
+                const float* dx = sXt + lb * kTN + cg * 32;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const float4 x4 = *(const float4*)(dx + 4 * j);
+                    const float2 p0 = mul2(dwv, make_float2(x4.x, x4.y));
+                    const float2 p1 = mul2(dwv, make_float2(x4.z, x4.w));
+                    const float2 f0 = sub2(make_float2(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1])), bias2);
+                    const float2 f1 = sub2(make_float2(__uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3])), bias2);
+                    acc[2 * j] = fma2(f0, p0, acc[2 * j]);
+                    acc[2 * j + 1] = fma2(f1, p1, acc[2 * j + 1]);
+                }
             }
             if (!ok) break;
             __syncwarp();
-            if (lane == 0) mbar_arrive(&bar_empty[s]);
+            if (lane == 0) mbar_arrive(&bar_empty[s]);  // this stage's scales are read
         }
         if (!*abort) {
-            const int n = n0 + r;
-            if (n < N) {
-                const float bn = ep.bias ? ep.bias[n] : 0.0f;
+            if (!swi) {
+                const int n = n0 + r;
+                if (n < a.N) {
+                    const float bn = a.bias ? a.bias[n] : 0.0f;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
+                    for (int j = 0; j < 16; ++j) {
+#pragma unroll
+                        for (int e = 0; e < 2; ++e) {
+                            const int m = m0 + cg * 32 + 2 * j + e;
+                            if (m < a.M) {
+                                float o = e ? acc[j].y : acc[j].x;
+                                if (a.bias) o = __fadd_rn(o, bn);
+                                if (a.residual)
+                                    o = __fadd_rn(a.residual[(int64_t)m * a.res_stride + n], o);
+                                a.y[(int64_t)m * a.y_stride + n] = o;
+                            }
+                        }
+                    }
+                }
+            }
+        }
+        if (swi) {
+            // SwiGLU: lanes 0-63 hold gate rows n0.., lanes 64-127 the up rows of the same pairs.
+            // The up warps hand their sums over in shared memory (the stage ring is free now:
+            // every MMA and every TMA load has completed before the last stage's "ready").
+            float* xch = (float*)tsm;  // [64 pairs][128 columns]
+            epi_sync();
+            if (q >= 2 && !*abort) {
+#pragma unroll
+                for (int j = 0; j < 16; ++j)
+                    *(float2*)(xch + (r - 64) * kTN + cg * 32 + 2 * j) = acc[j];
+            }
+            epi_sync();
+            if (q < 2 && !*abort) {
+                const int pr = n0 + r;  // pair index
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
 #pragma unroll
                     for (int e = 0; e < 2; ++e) {
-                        const int m = m0 + h * 64 + 2 * j + e;
-                        if (m < M) {
-                            float o = e ? acc[j].y : acc[j].x;
-                            if (ep.bias) o = __fadd_rn(o, bn);
-                            if (ep.residual)
-                                o = __fadd_rn(ep.residual[(int64_t)m * ep.res_stride + n], o);
-                            y[(int64_t)m * y_stride + n] = o;
+                        const int col = cg * 32 + 2 * j + e, m = m0 + col;
+                        const float up = xch[r * kTN + col];
+                        const float h = __fmul_rn(ref_v_silu(e ? acc[j].y : acc[j].x), up);
+                        if (m < a.M) {  // warp-uniform
+                            if (a.y) a.y[(int64_t)m * a.y_stride + pr] = h;
+                            if (a.yq) {  // the warp's 32 lanes: one Q8_0 block of this row m
+                                float d16, qv;
+                                q8_block(h, lane, d16, qv);
+                                a.yq[(int64_t)m * a.swi_F + pr] = (int8_t)__float2int_rn(qv);
+                                if (lane == 0) a.yd[(int64_t)m * (a.swi_F / 32) + pr / 32] = d16;
+                            }
                         }
                     }
                 }
@@ -441,16 +495,51 @@ __global__ void __launch_bounds__(kTThreads, 1)
     }
 }
 
-}  // namespace
+// ---- tensor maps (host) -------------------------------------------------------------------------
 
-void launch_gemm_tc(const QWeight& w, const int8_t* xq, const float* xd, int64_t M, float* y,
-                    int64_t y_stride, const MatmulEpilogue& ep, cudaStream_t st) {
-    GB_CHECK(w.type == T_Q8_0 || w.type == T_Q4_0, "gemm_tc: quantized weights required");
-    GB_CHECK(w.K % QK == 0 && w.K > 0, "gemm_tc: K must be a positive multiple of 32");
-    GB_CHECK(w.N < (1LL << 31) && w.K < (1LL << 31) && M < (1LL << 31), "gemm_tc: shape too large");
-    GB_CHECK(((uintptr_t)xq & 15) == 0 && ((uintptr_t)w.qs & 15) == 0,
-             "gemm_tc: xq and weights must be 16-byte aligned");
-    if (M == 0 || w.N == 0) return;
+// 2-D tiled tensor map of `dtype` elements: dims {d0, d1}, row pitch `pitch` bytes, box {b0, b1};
+// no swizzle, out-of-range elements read as zero.  Cached per argument set.
+CUtensorMap tensor_map(const void* base, CUtensorMapDataType dtype, uint64_t d0, uint64_t d1,
+                       uint64_t pitch, uint32_t b0, uint32_t b1) {
+    using Key = std::tuple<const void*, int, uint64_t, uint64_t, uint64_t, uint32_t, uint32_t>;
+    static std::mutex mu;
+    static std::map<Key, CUtensorMap> cache;
+    const Key key{base, (int)dtype, d0, d1, pitch, b0, b1};
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    if (cache.size() > 4096) cache.clear();
+    CUtensorMap m;
+    std::memset(&m, 0, sizeof(m));
+    const cuuint64_t dims[2] = {d0, d1};
+    const cuuint64_t strides[1] = {pitch};
+    const cuuint32_t box[2] = {b0, b1};
+    const cuuint32_t es[2] = {1, 1};
+    // the driver entry point, looked up through the runtime: the library does not link libcuda
+    using Encode = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+    static Encode encode = nullptr;
+    if (!encode) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        GB_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+        GB_CHECK(fn != nullptr && q == cudaDriverEntryPointSuccess,
+                 "gemm_tc: cuTensorMapEncodeTiled is not available from the driver");
+        encode = (Encode)fn;
+    }
+    const CUresult rc = encode(
+        &m, dtype, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    GB_CHECK(rc == CUDA_SUCCESS, "gemm_tc: cuTensorMapEncodeTiled failed (" + std::to_string((int)rc) + ")");
+    cache.emplace(key, m);
+    return m;
+}
+
+template <int WT>
+void run_tc(const QWeight& w, const int8_t* xq, const float* xd, const TcArgs& a, cudaStream_t st) {
     int dev = 0;
     GB_CUDA(cudaGetDevice(&dev));
     static std::mutex mu;
@@ -459,21 +548,74 @@ void launch_gemm_tc(const QWeight& w, const int8_t* xq, const float* xd, int64_t
         std::lock_guard<std::mutex> lock(mu);
         GB_CHECK(dev >= 0 && dev < 64, "gemm_tc: device ordinal out of range");
         if (!configured[dev]) {
-            GB_CUDA(cudaFuncSetAttribute(k_gemm_tc<T_Q8_0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kTS * TcStage<T_Q8_0>::kBytes));
-            GB_CUDA(cudaFuncSetAttribute(k_gemm_tc<T_Q4_0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kTS * TcStage<T_Q4_0>::kBytes));
+            GB_CUDA(cudaFuncSetAttribute(k_gemm_tc<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         kTS * TcStage<WT>::kBytes));
             configured[dev] = true;
         }
     }
-    dim3 grid((unsigned)((w.N + kTM - 1) / kTM), (unsigned)((M + kTN - 1) / kTN));
-    if (w.type == T_Q8_0)
-        k_gemm_tc<T_Q8_0><<<grid, kTThreads, kTS * TcStage<T_Q8_0>::kBytes, st>>>(
-            (const uint8_t*)w.qs, (int)w.N, (int)w.K, xq, xd, (int)M, y, y_stride, ep);
-    else
-        k_gemm_tc<T_Q4_0><<<grid, kTThreads, kTS * TcStage<T_Q4_0>::kBytes, st>>>(
-            (const uint8_t*)w.qs, (int)w.N, (int)w.K, xq, xd, (int)M, y, y_stride, ep);
+    const int64_t rb = qrow_bytes(WT, w.K);
+    const bool swi = a.swi_F > 0;
+    const CUtensorMap mw = tensor_map(w.qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)rb,
+                                       (uint64_t)w.N, (uint64_t)rb, 16, swi ? kTM / 2 : kTM);
+    const CUtensorMap mx = tensor_map(xq, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)w.K,
+                                       (uint64_t)a.M, (uint64_t)w.K, 16, kTN);
+    const CUtensorMap ms = tensor_map(xd, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (uint64_t)(w.K / QK),
+                                       (uint64_t)a.M, (uint64_t)(w.K / QK) * 4, kTB, kTN);
+    const int64_t ntiles = swi ? a.swi_F / (kTM / 2) : (w.N + kTM - 1) / kTM;
+    dim3 grid((unsigned)ntiles, (unsigned)((a.M + kTN - 1) / kTN));
+    k_gemm_tc<WT><<<grid, kTThreads, kTS * TcStage<WT>::kBytes, st>>>(mw, mx, ms, a);
     GB_CUDA(cudaGetLastError());
+}
+
+void check_tc(const QWeight& w, const int8_t* xq, const float* xd) {
+    GB_CHECK(w.type == T_Q8_0 || w.type == T_Q4_0, "gemm_tc: quantized weights required");
+    GB_CHECK(gemm_tc_fits(w.K), "gemm_tc: K must be a positive multiple of 128");
+    GB_CHECK(w.N < (1LL << 31) && w.K < (1LL << 31), "gemm_tc: shape too large");
+    GB_CHECK(((uintptr_t)xq & 15) == 0 && ((uintptr_t)w.qs & 15) == 0 && ((uintptr_t)xd & 15) == 0,
+             "gemm_tc: xq, xd and weights must be 16-byte aligned");
+}
+
+}  // namespace
+
+bool gemm_tc_fits(int64_t K) { return K > 0 && K % (QK * kTB) == 0; }
+
+void launch_gemm_tc(const QWeight& w, const int8_t* xq, const float* xd, int64_t M, float* y,
+                    int64_t y_stride, const MatmulEpilogue& ep, cudaStream_t st) {
+    check_tc(w, xq, xd);
+    GB_CHECK(M < (1LL << 31), "gemm_tc: shape too large");
+    if (M == 0 || w.N == 0) return;
+    TcArgs a{};
+    a.N = (int)w.N;
+    a.K = (int)w.K;
+    a.M = (int)M;
+    a.swi_F = 0;
+    a.y = y;
+    a.y_stride = y_stride;
+    a.bias = ep.bias;
+    a.residual = ep.residual;
+    a.res_stride = ep.res_stride;
+    if (w.type == T_Q8_0) run_tc<T_Q8_0>(w, xq, xd, a, st);
+    else run_tc<T_Q4_0>(w, xq, xd, a, st);
+}
+
+void launch_gemm_tc_swiglu(const GemvArgs& g, cudaStream_t st) {
+    check_tc(g.w, g.xq, g.xd);
+    GB_CHECK(g.w.N == 2 * g.F && g.F % (kTM / 2) == 0, "gemm_tc swiglu: N == 2F with F % 64 == 0");
+    GB_CHECK(!g.bias && !g.residual, "gemm_tc swiglu: no bias / residual");
+    GB_CHECK(g.y || g.yq, "gemm_tc swiglu: no output");
+    GB_CHECK(!g.yq == !g.yd, "gemm_tc swiglu: Q8_0 output needs quants and scales");
+    if (g.M == 0) return;
+    TcArgs a{};
+    a.N = (int)g.w.N;
+    a.K = (int)g.w.K;
+    a.M = g.M;
+    a.swi_F = (int)g.F;
+    a.y = g.y;
+    a.y_stride = g.y_stride;
+    a.yq = g.yq;
+    a.yd = g.yd;
+    if (g.w.type == T_Q8_0) run_tc<T_Q8_0>(g.w, g.xq, g.xd, a, st);
+    else run_tc<T_Q4_0>(g.w, g.xq, g.xd, a, st);
 }
 
 int gemm_tc_error() {

@@ -3,10 +3,10 @@
 // M <= 16 (decode and batched decode) goes to the GEMV (k_gemv.cu, M <= 2) or the tensor-core
 // decode kernel (k_mmv.cu).
 //
-// k_gemm_q (M > 16, prefill): int8 tensor-core tiles (mma m16n8k32, one instruction per
-// 32-K block) give the exact int32 block dot; the block scale product is applied in fp32 right
-// after each block.  Integer block sums are exact; the fp32 summation order differs from the
-// CPU's lane order.
+// M > 16 (prefill) runs the tcgen05 GEMM (k_gemm_tc.cu) when K % 128 == 0, else k_gemm_q:
+// int8 tensor-core tiles (mma m16n8k32, one instruction per 32-K block) give the exact int32
+// block dot; the block scale product is applied in fp32 right after each block.  Integer block
+// sums are exact; the fp32 summation order differs from the CPU's lane order.
 #include <cuda_fp16.h>
 
 #include <mutex>
@@ -364,6 +364,10 @@ void launch_gemm_swiglu(const GemvArgs& a, cudaStream_t st) {
     GB_CHECK(a.y || a.yq, "gemm swiglu: no output");
     GB_CHECK(!a.yq == !a.yd, "gemm swiglu: Q8_0 output needs quants and scales");
     if (a.M == 0) return;
+    if (gemm_tc_fits(a.w.K)) {  // the tcgen05 GEMM with the same epilogue
+        launch_gemm_tc_swiglu(a, st);
+        return;
+    }
     SwiOut so;
     so.F = (int)a.F;
     so.y = a.y;
@@ -389,6 +393,10 @@ void launch_matmul_q(const QWeight& w, const int8_t* xq, const float* xd, int64_
         a.residual = ep.residual;
         a.res_stride = ep.res_stride;
         launch_gemv_fused(a, st);
+        return;
+    }
+    if (gemm_tc_fits(w.K)) {  // prefill on tcgen05 (TMA stages of 4 blocks: K % 128 == 0)
+        launch_gemm_tc(w, xq, xd, M, y, y_stride, ep, st);
         return;
     }
     launch_gemm_block(w, xq, xd, M, y, y_stride, ep, SwiOut(), st);

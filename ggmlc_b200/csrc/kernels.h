@@ -141,6 +141,10 @@ void launch_gemm_swiglu(const GemvArgs& a, cudaStream_t st);
 // sticky error word (non-zero after one of its bounded waits ran out).
 void launch_gemm_tc(const QWeight& w, const int8_t* xq, const float* xd, int64_t M, float* y,
                     int64_t y_stride, const MatmulEpilogue& ep, cudaStream_t st);
+// The same with the SwiGLU epilogue of launch_gemm_swiglu (N == 2F, F % 64 == 0).
+void launch_gemm_tc_swiglu(const GemvArgs& a, cudaStream_t st);
+// whether the tcgen05 GEMM takes this K (its TMA stages are 4 blocks: K % 128 == 0)
+bool gemm_tc_fits(int64_t K);
 int gemm_tc_error();
 
 // Tensor-parallel one-shot all-reduce (k_allreduce.cu): y[0..n) summed over T ranks through

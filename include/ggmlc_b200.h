@@ -242,15 +242,17 @@ int gb_quantize_q8_0(const float* x, int64_t x_stride, int64_t M, int64_t K, int
                      float* xd, void* stream);
 /* MUL_MAT Y[M][N] = X W^T (+bias[N]) (+residual[M][N]) — ggml_cuda_mul_mat
  * (ggml-cuda.cu:1812-1866: mul_mat_vec_q mmvq.cu:508 for M <= 8, mul_mat_q mmq.cuh:948
- * above).  Block int32 dots are exact; block terms accumulate in fp32 (generic block formula of
+ * above; here M > 16 runs on tcgen05, gb_gemm_tc, when K % 128 == 0).  Block int32 dots are exact; block terms accumulate in fp32 (generic block formula of
  * ggml-cpu/quants.c:225-256, :451-477). */
 int gb_mul_mat_q(int type, const void* wq, int64_t N, int64_t K,
                  const int8_t* xq, const float* xd, int64_t M, float* y, const float* bias,
                  const float* residual, void* stream);
-/* The same MUL_MAT on the 5th-generation tensor cores, any M (mul_mat_q mmq.cuh:948 is the
- * reference's large-M kernel): one tcgen05.mma kind::i8 per 32-element block into tensor
- * memory, the block scales applied by epilogue warps; block dots exact, block terms summed in
- * fp32 in block order.  gb_gemm_tc_error returns its sticky error word: 0 while every bounded
+/* The same MUL_MAT on the 5th-generation tensor cores, any M, K a multiple of 128 (mul_mat_q
+ * mmq.cuh:948 is the reference's large-M kernel): operands brought in by the TMA engine, one
+ * tcgen05.mma kind::i8 per 32-element block into tensor memory, the block scales applied by
+ * epilogue warps; block dots exact, block terms summed in fp32 in block order.  gb_mul_mat_q
+ * runs it for M > 16 whenever K % 128 == 0; xq, xd and wq 16-byte aligned.
+ * gb_gemm_tc_error returns its sticky error word: 0 while every bounded
  * wait inside it completed, non-zero after one ran out (that launch left its tile unwritten),
  * -1 if the word cannot be read. */
 int gb_gemm_tc(int type, const void* wq, int64_t N, int64_t K, const int8_t* xq, const float* xd,

@@ -151,13 +151,14 @@ def test_prefill_gemm_swiglu_epilogue(G, wtype, M):
 @pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_0])
 @pytest.mark.parametrize("M", [200, 600])
 def test_prefill_gemm_tile_variants(G, wtype, M):
-    """Prefill shapes on both builds of the block GEMM (Q4_0 at 600 rows has tiles for two CTAs
-    per SM and runs the rolled build; 200 rows and Q8_0 run one CTA per SM): the integer path is
+    """Prefill shapes on both builds of the mma.sync block GEMM, which serves K % 128 != 0 (Q4_0
+    at 600 rows has tiles for two CTAs per SM and runs the rolled build; 200 rows and Q8_0 run
+    one CTA per SM): the integer path is
     bit-exact against the oracle on sampled output columns, and the SwiGLU epilogue is bit-exact
     against the plain GEMM's outputs."""
     torch = G.torch_dev()
     rng = np.random.default_rng(M + 7 * wtype)
-    F, K = 4096, 256
+    F, K = 4096, 288  # K % 128 != 0: the mma.sync block GEMM (the tcgen05 GEMM takes the rest)
     N = 2 * F
     w, x = _int_exact_case(rng, wtype, N, K, M)
     wq, wd = G.upload_weight(wtype, w, N, K)
@@ -248,11 +249,12 @@ def test_prefill_matmul_close(G, wtype, M, N, K):
 
 
 @pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_0])
-@pytest.mark.parametrize("M,N,K", [(17, 40, 1024), (64, 300, 576), (130, 77, 4096),
-                                   (300, 256, 2048), (5, 128, 14336)])
+@pytest.mark.parametrize("M,N,K", [(17, 40, 1024), (64, 300, 640), (130, 77, 4096),
+                                   (300, 256, 2048), (5, 128, 14336), (600, 1000, 4096)])
 def test_tensor_core_gemm_integer_path_bit_exact(G, wtype, M, N, K):
-    """tcgen05 GEMM (gb_gemm_tc): partial row / column tiles, partial 64-block groups (K=576),
-    long K, and M below one tile, on inputs where fp32 summation is exact."""
+    """tcgen05 GEMM (gb_gemm_tc): partial row / column tiles, a partial 64-block scale group
+    (K = 640), long K, M below one tile and several activation tiles, on inputs where fp32
+    summation is exact."""
     rng = np.random.default_rng(11 * N + K + M + wtype)
     w, x = _int_exact_case(rng, wtype, N, K, M)
     wq, wd = G.upload_weight(wtype, w, N, K)
