@@ -427,6 +427,13 @@ def run_ours(args) -> None:
         except Exception as e:  # noqa: BLE001 - reported in the line
             parity = {"error": str(e)[:300]}
 
+    sweep = None
+    if rank == 0 and world == 1 and not args.no_sweep:
+        try:
+            sweep = operator_sweep(local)
+        except Exception as e:  # noqa: BLE001 - reported in the line
+            sweep = {"error": str(e)[:300]}
+
     cb_line = None
     if not args.no_cb and not tp:
         del ex  # free the single-sequence caches before the batched runs
@@ -469,6 +476,7 @@ def run_ours(args) -> None:
             "parity": parity,
             "cpu_baseline": cb,
             "continuous_batching": cb_line,
+            "operator_sweep": sweep,
             "clocks": clk,
             "gpu_launches": int(args.steps * (launches_pp + G * launches_tg)),
         }
@@ -653,6 +661,110 @@ def gemv_roofline(local: int, N: int = 28672, K: int = 4096, R: int = 16, reps: 
                       f"mean of {reps} passes"}
 
 
+SWEEP_SHAPES = [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]
+SWEEP_M = [1, 8, 64, 512]
+
+
+def measured_int8_tops() -> tuple[float, str]:
+    """Dense INT8 tensor peak: twice the measured dense bf16 GEMM rate (the B200's int8 and
+    bf16 tensor paths differ by 2x in dense throughput), else the nominal 4500 TOP/s."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return 2.0 * float(json.loads(p.read_text())["bf16_tflops"]), "2 x measured bf16"
+        except Exception:
+            pass
+    return 4500.0, "nominal"
+
+
+def operator_sweep(local: int, reps: int = 5) -> dict:
+    """Q8_0 / Q4_0 weights N x K in {4096x4096, 14336x4096, 4096x14336,
+    128256x4096} times fp32 activations N(0,1) with M in {1, 8, 64, 512}, the activations
+    quantized to Q8_0 (gb_quantize_q8_0) and multiplied (gb_mul_mat_q, the dispatching entry).
+    Per cell: microseconds per call (quantize + matmul, and the matmul alone), algorithmic
+    TOP/s (2 M N K) and GB/s (weights + Q8_0 activations + f32 output), and the fraction of the
+    cell's own bound: max(bytes / HBM peak, ops / INT8 peak) over the measured time.  Weights
+    rotate over copies totalling more than L2 (126 MB), so every call streams them from HBM."""
+    import ctypes
+
+    import torch
+
+    from ggmlc_b200 import _runtime as R_
+
+    L = R_.lib()
+    dev = torch.device("cuda", local)
+    P_, I, I64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
+    L.gb_quantize_q8_0.argtypes = [P_, I64, I64, I64, P_, P_, P_]
+    L.gb_mul_mat_q.argtypes = [I, P_, I64, I64, P_, P_, I64, P_, P_, P_, P_]
+    hbm, _ = peaks()
+    tops, tops_kind = measured_int8_tops()
+    st = torch.cuda.current_stream(dev)
+    sp = ctypes.c_void_p(st.cuda_stream)
+    out = {"peaks": {"hbm_gbs": hbm, "int8_tops": tops, "int8_kind": tops_kind}, "cells": {}}
+    for qt, name, bpb in ((8, "q8_0", 34), (2, "q4_0", 18)):
+        for (N, K) in SWEEP_SHAPES:
+            wbytes = N * K // 32 * bpb
+            copies = max(1, min(16, -(-(256 << 20) // wbytes)))
+            nb = K // 32
+            g = torch.Generator(device=dev)
+            g.manual_seed(N + K + qt)
+            ws = []
+            for _ in range(copies):
+                blocks = torch.randint(0, 256, (N, nb, bpb), dtype=torch.uint8, device=dev,
+                                       generator=g)
+                blocks[:, :, 0:2] = (torch.randn((N, nb), device=dev, generator=g) * 1e-3).half() \
+                    .view(torch.uint8).reshape(N, nb, 2)
+                L.gb_weight_row_bytes.argtypes = [I, I64]
+                L.gb_weight_row_bytes.restype = I64
+                wq = torch.empty(N * L.gb_weight_row_bytes(qt, K), dtype=torch.uint8, device=dev)
+                L.gb_repack_blocks.argtypes = [P_, I, I64, I64, P_, P_]
+                if L.gb_repack_blocks(blocks.data_ptr(), qt, N, K, wq.data_ptr(), None) != 0:
+                    raise RuntimeError(L.gb_last_error().decode())
+                ws.append(wq)
+                del blocks
+            for M in SWEEP_M:
+                x = torch.randn((M, K), device=dev, generator=g)
+                xq = torch.empty((M, K), dtype=torch.int8, device=dev)
+                xd = torch.empty((M, nb), dtype=torch.float32, device=dev)
+                y = torch.empty((M, N), dtype=torch.float32, device=dev)
+
+                def call(w, quant=True):
+                    if quant and L.gb_quantize_q8_0(x.data_ptr(), K, M, K, xq.data_ptr(),
+                                                    xd.data_ptr(), sp) != 0:
+                        raise RuntimeError(L.gb_last_error().decode())
+                    if L.gb_mul_mat_q(qt, w.data_ptr(), N, K, xq.data_ptr(), xd.data_ptr(), M,
+                                      y.data_ptr(), None, None, sp) != 0:
+                        raise RuntimeError(L.gb_last_error().decode())
+
+                n = max(reps, copies)
+                for w in ws:
+                    call(w)
+                times = {}
+                for quant in (True, False):
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record(st)
+                    for i in range(n):
+                        call(ws[i % copies], quant)
+                    e1.record(st)
+                    e1.synchronize()
+                    times[quant] = e0.elapsed_time(e1) * 1e3 / n
+                ops = 2.0 * M * N * K
+                byts = wbytes + M * K * 34 / 32 + M * N * 4
+                bound_us = max(byts / (hbm * 1e9), ops / (tops * 1e12)) * 1e6
+                us = times[True]
+                out["cells"][f"{name} {N}x{K} M={M}"] = {
+                    "us": round(us, 2), "matmul_us": round(times[False], 2),
+                    "tops": round(ops / (us * 1e-6) / 1e12, 1),
+                    "gbs": round(byts / (us * 1e-6) / 1e9, 1),
+                    "bound": "hbm" if byts / (hbm * 1e9) >= ops / (tops * 1e12) else "int8",
+                    "frac": round(bound_us / us, 3)}
+                del x, xq, xd, y
+            del ws
+            torch.cuda.empty_cache()
+    return out
+
+
 # single-kernel cases at the L8 decode shapes, for ncu captures of one launch (--case NAME)
 CASES = {
     "gemv_rms_swiglu": dict(N=28672, K=4096, mode="rms_swiglu"),  # gate_up + RMSNorm + SwiGLU
@@ -789,6 +901,7 @@ def main():
                     help="--impl reference: repetitions of the reference's -pg test (<= steps)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-cb", action="store_true", help="skip the continuous-batching leg")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the operator-sweep leg")
     ap.add_argument("--replicas", action="store_true",
                     help="N > 1: independent replicas instead of one tensor-parallel group")
     ap.add_argument("--case", choices=sorted(CASES), help="launch one decode kernel of the L8 "

@@ -5,9 +5,10 @@
 // Arithmetic.  One tcgen05.mma (M = 128 weight rows, N = 128 activation rows, K = 32) per
 // 32-element block adds every exact int32 block dot of a 128 x 128 tile onto a tensor-memory
 // accumulator that holds 1.5 * 2^23 (0x4B400000): the epilogue reads the bits as the float
-// 12582912 + sumi, subtracts 12582912 (exact), multiplies by d_w * d_x and accumulates the block
-// terms in fp32 registers, then writes 0x4B400000 back for the next block — the block formula of
-// the reference's vec_dot (ggml-cpu/quants.c:225-256, :451-477) with the integer part exact.
+// 12582912 + sumi, forms sumi * d_x with one fma against the exact constant -12582912 * d_x,
+// multiplies by d_w and accumulates the block terms in fp32 registers, then writes 0x4B400000
+// back for the next block — the block formula of the reference's vec_dot
+// (ggml-cpu/quants.c:225-256, :451-477) with the integer part exact.
 // Q4_0 nibbles are widened in shared memory to 16 * (q - 8) (exact in int8); their weight scales
 // are divided by 16 to compensate.
 //
@@ -66,7 +67,7 @@ struct TcStage {
     static constexpr int kRaw = WT == T_Q4_0 ? kTB * kTM * 16 : 0;  // packed Q4_0 nibbles
     static constexpr int kWs = kTM * 16;                            // a row's scale word
     static constexpr int kXr = kTN * 16;                            // 4 fp32 scales per act. row
-    static constexpr int kXt = kTB * kTN * 4;                       // the same, [block][row]
+    static constexpr int kXt = kTB * kTN * 8;  // (d_x, -1.5*2^23*d_x) pairs [block][row]
     static constexpr int kBytes = kA + kB + kRaw + kWs + kXr + kXt;
     static constexpr uint32_t kTx = (WT == T_Q4_0 ? kRaw : kA) + kB + kWs + kXr;  // TMA bytes
     static_assert(kBytes % 128 == 0, "stage alignment");
@@ -165,22 +166,6 @@ __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t
         : "memory");
 }
 
-#define GB_TC_R32(v)                                                                          \
-    "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),      \
-        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]),           \
-        "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]),        \
-        "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),        \
-        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-
-// 32 consecutive columns of this thread's tensor-memory lane
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
-        "%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : GB_TC_R32(v)
-        : "r"(taddr)
-        : "memory");
-}
 // the bias word into 32 consecutive columns of this thread's lane
 __device__ __forceinline__ void tmem_st_bias32(uint32_t taddr) {
     const uint32_t b = kBiasBits;
@@ -188,6 +173,17 @@ __device__ __forceinline__ void tmem_st_bias32(uint32_t taddr) {
         "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
         "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
         "r"(b)
+        : "memory");
+}
+// 16 consecutive columns of this thread's tensor-memory lane
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+        "%14,%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+          "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+          "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr)
         : "memory");
 }
 __device__ __forceinline__ void tmem_wait_ld() {
@@ -315,13 +311,14 @@ __global__ void __launch_bounds__(kTThreads, 1)
                     *(uint4*)(d + 2048) = hi;
                 }
             }
-            // activation scales [row][block] -> [block][row]
+            // activation scales [row][block] -> [block][row], each with -1.5*2^23 * d_x (exact:
+            // d_x carries the 11 significant bits of an fp16 scale)
             for (int r = p; r < kTN; r += 32 * kHelpWarps) {
                 const float4 v = *(const float4*)(sXr + r * 4);
-                sXt[0 * kTN + r] = v.x;
-                sXt[1 * kTN + r] = v.y;
-                sXt[2 * kTN + r] = v.z;
-                sXt[3 * kTN + r] = v.w;
+                const float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int lb = 0; lb < kTB; ++lb)
+                    *(float2*)(sXt + 2 * (lb * kTN + r)) = make_float2(e[lb], __fmul_rn(e[lb], -12582912.0f));
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // widened A -> MMA
             __syncwarp();
@@ -376,7 +373,6 @@ __global__ void __launch_bounds__(kTThreads, 1)
 #pragma unroll
         for (int j = 0; j < 16; ++j) acc[j] = make_float2(0.0f, 0.0f);
         const float wsc = WT == T_Q4_0 ? 0.0625f : 1.0f;
-        const float2 bias2 = make_float2(12582912.0f, 12582912.0f);
         // waits are made warp-uniform by a vote: tensor-memory loads and stores need the whole
         // warp converged
         for (int t = 0; t < ns && !*abort; ++t) {
@@ -400,28 +396,39 @@ __global__ void __launch_bounds__(kTThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                uint32_t v[32];
-                tmem_ld32(lane_base + lb * kTN, v);
-                tmem_wait_ld();
-                tmem_st_bias32(lane_base + lb * kTN);
-                tmem_wait_st();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&bar_tempty[lb]);  // the MMA may use it again
                 const float2 dwv = make_float2(dw0, dw0);
                 dw0 = dw1;
                 dw1 = dw2;
                 dw2 = dw3;
-                const float* dx = sXt + lb * kTN + cg * 32;
+                const float* dx = sXt + 2 * (lb * kTN + cg * 32);  // (d_x, c) per column
+                // two halves of 16 columns (fewer live registers); the accumulator gets its bias
+                // word back once both are read, then the MMA may use it again
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const float4 x4 = *(const float4*)(dx + 4 * j);
-                    const float2 p0 = mul2(dwv, make_float2(x4.x, x4.y));
-                    const float2 p1 = mul2(dwv, make_float2(x4.z, x4.w));
-                    const float2 f0 = sub2(make_float2(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1])), bias2);
-                    const float2 f1 = sub2(make_float2(__uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3])), bias2);
-                    acc[2 * j] = fma2(f0, p0, acc[2 * j]);
-                    acc[2 * j + 1] = fma2(f1, p1, acc[2 * j + 1]);
+                for (int hf = 0; hf < 2; ++hf) {
+                    uint32_t v[16];
+                    tmem_ld16(lane_base + lb * kTN + hf * 16, v);
+                    tmem_wait_ld();
+                    if (hf == 1) {
+                        tmem_st_bias32(lane_base + lb * kTN);
+                        tmem_wait_st();
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&bar_tempty[lb]);
+                    }
+                    // per column: t = fma(bits as float, d_x, c) = sumi * d_x (one rounding: the
+                    // float is 12582912 + sumi exactly and c = -12582912 * d_x exactly), then
+                    // acc = fma(t, d_w, acc)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float4 a4 = *(const float4*)(dx + 2 * (hf * 16 + 4 * j));
+                        const float4 b4 = *(const float4*)(dx + 2 * (hf * 16 + 4 * j) + 4);
+                        const float2 t0 = fma2(make_float2(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1])),
+                                               make_float2(a4.x, a4.z), make_float2(a4.y, a4.w));
+                        const float2 t1 = fma2(make_float2(__uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3])),
+                                               make_float2(b4.x, b4.z), make_float2(b4.y, b4.w));
+                        acc[hf * 8 + 2 * j] = fma2(t0, dwv, acc[hf * 8 + 2 * j]);
+                        acc[hf * 8 + 2 * j + 1] = fma2(t1, dwv, acc[hf * 8 + 2 * j + 1]);
+                    }
                 }
             }
             if (!ok) break;
