@@ -12,16 +12,19 @@
 // Q4_0 nibbles are widened in shared memory to 16 * (q - 8) (exact in int8); their weight scales
 // are divided by 16 to compensate.
 //
-// A K stage is 4 consecutive blocks.  Per stage the TMA engine loads (tile mode, no swizzle, no
-// multicast) 16-byte-wide boxes of 128 rows straight into the canonical K-major layout of the
-// MMA (8-row x 16-byte core matrices; the two 16-byte halves of a block 2048 B apart): the weight
-// quants (Q8_0 both halves; Q4_0 the packed nibbles), the activation quants, the 16-byte scale
-// word of every weight row (4 fp16 scales of the stage) and the 4 fp32 activation scales of every
-// activation row.
+// A K stage is 4 consecutive blocks.  Per stage the TMA engine loads (tile mode, no multicast)
+// the activation quants, 128 contiguous bytes per row, with the 128-byte swizzle the MMA reads
+// directly (a block's 32 bytes selected by the descriptor's start address); the weight quants,
+// 64 contiguous bytes per row (Q4_0 nibbles; Q8_0 first and second halves in two boxes), which
+// helper warps widen (Q4_0) or copy (Q8_0) into the canonical no-swizzle K-major layout
+// (8-row x 16-byte core matrices, the two 16-byte halves of a block 2048 B apart); the 16-byte
+// scale word of every weight row (4 fp16 scales of the stage) and the 4 fp32 activation scales
+// of every activation row.
 //
 // Warps (20, one CTA per SM):
-//   warp 0      TMA producer (one thread), stage ring of kTS stages;
-//   warps 1-2   Q4_0 nibble widening, activation scales transposed to [block][row], then mbarrier
+//   warp 0      TMA producer (one thread), stage ring of 3-4 stages;
+//   warps 1-2   weight quants into the MMA layout (Q4_0 widened), activation scales transposed
+//               to [block][row], then mbarrier
 //               "ready" (the MMA and the epilogue wait on it);
 //   warp 3      MMA issuer (one thread) and tensor-memory owner: 4 accumulators of 128 columns,
 //               one per block of a stage, one tcgen05.mma + tcgen05.commit per block;
@@ -50,7 +53,9 @@ namespace {
 constexpr int kTM = 128;            // weight rows per tile (MMA M, tensor-memory lanes)
 constexpr int kTN = 128;            // activation rows per tile (MMA N, tensor-memory columns)
 constexpr int kTB = 4;              // blocks per stage = tensor-memory accumulators
-constexpr int kTS = 4;              // stages in the ring
+// stages in the ring: 4 (Q4_0) or 3 (Q8_0, whose raw halves take more room)
+template <int WT>
+constexpr int stages() { return WT == T_Q8_0 ? 3 : 4; }
 constexpr int kHelpWarp0 = 1, kHelpWarps = 2;
 constexpr int kMmaWarp = 3;
 constexpr int kEpiWarp0 = 4, kEpiWarps = 16;
@@ -59,19 +64,21 @@ constexpr int kTmemCols = kTB * kTN;
 constexpr uint32_t kBiasBits = 0x4B400000u;      // 1.5 * 2^23
 constexpr long long kSpinCycles = 4000000000LL;  // about 2 s at 1.9 GHz
 
-// one stage in shared memory
+// one stage in shared memory (1024-byte aligned: the activation tile is 128-byte swizzled)
 template <int WT>
 struct TcStage {
-    static constexpr int kA = kTB * 4096;                           // weights as int8, MMA layout
-    static constexpr int kB = kTB * 4096;                           // activations, MMA layout
-    static constexpr int kRaw = WT == T_Q4_0 ? kTB * kTM * 16 : 0;  // packed Q4_0 nibbles
-    static constexpr int kWs = kTM * 16;                            // a row's scale word
-    static constexpr int kXr = kTN * 16;                            // 4 fp32 scales per act. row
+    static constexpr int kA = kTB * 4096;   // weights as int8, canonical no-swizzle MMA layout
+    static constexpr int kB = kTN * 128;    // activations [row][4 blocks x 32 B], 128 B swizzle
+    static constexpr int kRaw = kTM * 64 * (WT == T_Q8_0 ? 2 : 1);  // TMA rows: [row][4 x 16 B]
+    static constexpr int kWs = kTM * 16;    // a row's scale word
+    static constexpr int kXr = kTN * 16;    // 4 fp32 scales per activation row
     static constexpr int kXt = kTB * kTN * 8;  // (d_x, -1.5*2^23*d_x) pairs [block][row]
     static constexpr int kBytes = kA + kB + kRaw + kWs + kXr + kXt;
-    static constexpr uint32_t kTx = (WT == T_Q4_0 ? kRaw : kA) + kB + kWs + kXr;  // TMA bytes
-    static_assert(kBytes % 128 == 0, "stage alignment");
+    static constexpr uint32_t kTx = kRaw + kB + kWs + kXr;  // TMA bytes
+    static_assert(kBytes % 1024 == 0, "stage alignment");
 };
+template <int WT>
+constexpr int tc_smem() { return stages<WT>() * TcStage<WT>::kBytes + 1024; }
 
 struct TcArgs {
     int N, K, M;        // weight rows (SwiGLU: 2F), K, activation rows
@@ -153,6 +160,13 @@ __device__ __forceinline__ uint64_t smem_desc(const void* p) {
     return (uint64_t)((a & 0x3FFFF) >> 4) | ((uint64_t)(2048 >> 4) << 16) |
            ((uint64_t)(128 >> 4) << 32) | ((uint64_t)1 << 46);
 }
+// K-major, 128-byte swizzle (the TMA's CU_TENSOR_MAP_SWIZZLE_128B pattern): rows of 128 B, 8-row
+// groups 1024 B apart; a block's 32 bytes are selected by advancing the start address by 32 B
+__device__ __forceinline__ uint64_t smem_desc_sw128(const void* p) {
+    const uint32_t a = su32(p);
+    return (uint64_t)((a & 0x3FFFF) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
 // kind::i8, D s32, A / B signed 8-bit, both K-major, M = 128, N = 128
 constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTN >> 3) << 17) |
                             ((uint32_t)(kTM >> 4) << 24);
@@ -199,12 +213,16 @@ __device__ __forceinline__ void epi_sync() {
 
 template <int WT>
 __global__ void __launch_bounds__(kTThreads, 1)
-    k_gemm_tc(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmx,
-              const __grid_constant__ CUtensorMap tms, TcArgs a) {
+    k_gemm_tc(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmws,
+              const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tms,
+              TcArgs a) {
     using S = TcStage<WT>;
-    extern __shared__ __align__(1024) uint8_t tsm[];
-    __shared__ __align__(8) uint64_t bar_full[kTS], bar_ready[kTS], bar_empty[kTS],
-        bar_tfull[kTB], bar_tempty[kTB], bar_done;
+    constexpr int kTS = stages<WT>();
+    extern __shared__ __align__(1024) uint8_t tsm_raw[];
+    // the stages start on a 1024-byte boundary (the launch adds 1024 bytes of room)
+    uint8_t* tsm = tsm_raw + ((1024 - (su32(tsm_raw) & 1023)) & 1023);
+    __shared__ __align__(8) uint64_t bar_full[4], bar_ready[4], bar_empty[4], bar_tfull[kTB],
+        bar_tempty[kTB], bar_done;
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
     volatile int* abort = &s_abort;
@@ -251,7 +269,6 @@ __global__ void __launch_bounds__(kTThreads, 1)
                 const int s = t % kTS;
                 if (t >= kTS && !mbar_wait(&bar_empty[s], ((t / kTS) - 1) & 1, abort)) break;
                 uint8_t* st = stage(s);
-                uint8_t* sA = st;
                 uint8_t* sB = st + S::kA;
                 uint8_t* sRaw = sB + S::kB;
                 uint8_t* sWs = sRaw + S::kRaw;
@@ -259,25 +276,19 @@ __global__ void __launch_bounds__(kTThreads, 1)
                 const int b0 = t * kTB;
                 mbar_expect_tx(&bar_full[s], S::kTx);
                 // weight rows of the tile: 128 rows, or gate rows then up rows (64 each)
+                // weight rows of the tile: 128 rows, or gate rows then up rows (64 each); per row
+                // the stage's 4 blocks of quants are 64 contiguous bytes (Q8_0: first halves,
+                // then second halves in a second box)
                 for (int part = 0; part < (swi ? 2 : 1); ++part) {
                     const int wy = swi ? n0 + part * a.swi_F : n0;
-                    const int ro = part * 64 * 16;  // byte offset of these rows in a 2 KB box
-                    for (int lb = 0; lb < kTB; ++lb) {
-                        if (WT == T_Q8_0) {
-                            tma_load(sA + lb * 4096 + ro, &tmw, (b0 + lb) * 16, wy, &bar_full[s]);
-                            tma_load(sA + lb * 4096 + 2048 + ro, &tmw, (nb + b0 + lb) * 16, wy,
-                                     &bar_full[s]);
-                        } else {
-                            tma_load(sRaw + lb * 2048 + ro, &tmw, (b0 + lb) * 16, wy, &bar_full[s]);
-                        }
-                    }
-                    tma_load(sWs + ro, &tmw, nb * qsz + (b0 >> 6) * 128 + (b0 & 31) * 4, wy,
-                             &bar_full[s]);
+                    tma_load(sRaw + part * 64 * 64, &tmw, b0 * 16, wy, &bar_full[s]);
+                    if (WT == T_Q8_0)
+                        tma_load(sRaw + kTM * 64 + part * 64 * 64, &tmw, (nb + b0) * 16, wy,
+                                 &bar_full[s]);
+                    tma_load(sWs + part * 64 * 16, &tmws, nb * qsz + (b0 >> 6) * 128 + (b0 & 31) * 4,
+                             wy, &bar_full[s]);
                 }
-                for (int lb = 0; lb < kTB; ++lb) {
-                    tma_load(sB + lb * 4096, &tmx, (b0 + lb) * 32, m0, &bar_full[s]);
-                    tma_load(sB + lb * 4096 + 2048, &tmx, (b0 + lb) * 32 + 16, m0, &bar_full[s]);
-                }
+                tma_load(sB, &tmx, b0 * 32, m0, &bar_full[s]);  // 128 B per row, swizzled
                 tma_load(sXr, &tms, b0, m0, &bar_full[s]);
             }
         }
@@ -293,10 +304,18 @@ __global__ void __launch_bounds__(kTThreads, 1)
             uint8_t* sRaw = st + S::kA + S::kB;
             const float* sXr = (const float*)(sRaw + S::kRaw + S::kWs);
             float* sXt = (float*)(sRaw + S::kRaw + S::kWs + S::kXr);
+            if (WT == T_Q8_0) {  // both halves into the MMA layout
+                for (int c = p; c < kTB * kTM; c += 32 * kHelpWarps) {
+                    const int r = c & (kTM - 1), lb = c >> 7;
+                    uint8_t* d = sA + lb * 4096 + r * 16;
+                    *(uint4*)d = *(const uint4*)(sRaw + r * 64 + lb * 16);
+                    *(uint4*)(d + 2048) = *(const uint4*)(sRaw + kTM * 64 + r * 64 + lb * 16);
+                }
+            }
             if (WT == T_Q4_0) {  // nibbles to int8 16*(q-8): low -> k 0..15, high -> 16..31
                 for (int c = p; c < kTB * kTM; c += 32 * kHelpWarps) {
                     const int r = c & (kTM - 1), lb = c >> 7;
-                    const uint4 w = *(const uint4*)(sRaw + lb * 2048 + r * 16);
+                    const uint4 w = *(const uint4*)(sRaw + r * 64 + lb * 16);
                     uint4 lo, hi;
                     lo.x = ((w.x << 4) & 0xF0F0F0F0u) ^ 0x80808080u;
                     lo.y = ((w.y << 4) & 0xF0F0F0F0u) ^ 0x80808080u;
@@ -320,7 +339,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
                 for (int lb = 0; lb < kTB; ++lb)
                     *(float2*)(sXt + 2 * (lb * kTN + r)) = make_float2(e[lb], __fmul_rn(e[lb], -12582912.0f));
             }
-            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // widened A -> MMA
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // A -> MMA
             __syncwarp();
             if (lane == 0) mbar_arrive(&bar_ready[s]);
         }
@@ -340,7 +359,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
                     }
                     tc_fence_after();
                     tc_mma(tmem + lb * kTN, smem_desc(st + lb * 4096),
-                           smem_desc(st + S::kA + lb * 4096));
+                           smem_desc_sw128(st + S::kA + lb * 32));
                     tc_commit(&bar_tfull[lb]);
                 }
                 if (ok) tc_commit(&bar_empty[s]);
@@ -505,13 +524,14 @@ __global__ void __launch_bounds__(kTThreads, 1)
 // ---- tensor maps (host) -------------------------------------------------------------------------
 
 // 2-D tiled tensor map of `dtype` elements: dims {d0, d1}, row pitch `pitch` bytes, box {b0, b1};
-// no swizzle, out-of-range elements read as zero.  Cached per argument set.
+// no swizzle or the 128-byte swizzle, out-of-range elements read as zero.  Cached per argument
+// set.
 CUtensorMap tensor_map(const void* base, CUtensorMapDataType dtype, uint64_t d0, uint64_t d1,
-                       uint64_t pitch, uint32_t b0, uint32_t b1) {
-    using Key = std::tuple<const void*, int, uint64_t, uint64_t, uint64_t, uint32_t, uint32_t>;
+                       uint64_t pitch, uint32_t b0, uint32_t b1, bool sw128) {
+    using Key = std::tuple<const void*, int, uint64_t, uint64_t, uint64_t, uint32_t, uint32_t, bool>;
     static std::mutex mu;
     static std::map<Key, CUtensorMap> cache;
-    const Key key{base, (int)dtype, d0, d1, pitch, b0, b1};
+    const Key key{base, (int)dtype, d0, d1, pitch, b0, b1, sw128};
     std::lock_guard<std::mutex> lock(mu);
     auto it = cache.find(key);
     if (it != cache.end()) return it->second;
@@ -538,7 +558,8 @@ CUtensorMap tensor_map(const void* base, CUtensorMapDataType dtype, uint64_t d0,
     }
     const CUresult rc = encode(
         &m, dtype, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+        sw128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+        CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     GB_CHECK(rc == CUDA_SUCCESS, "gemm_tc: cuTensorMapEncodeTiled failed (" + std::to_string((int)rc) + ")");
     cache.emplace(key, m);
@@ -556,21 +577,24 @@ void run_tc(const QWeight& w, const int8_t* xq, const float* xd, const TcArgs& a
         GB_CHECK(dev >= 0 && dev < 64, "gemm_tc: device ordinal out of range");
         if (!configured[dev]) {
             GB_CUDA(cudaFuncSetAttribute(k_gemm_tc<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kTS * TcStage<WT>::kBytes));
+                                         tc_smem<WT>()));
             configured[dev] = true;
         }
     }
     const int64_t rb = qrow_bytes(WT, w.K);
     const bool swi = a.swi_F > 0;
+    const uint32_t rows = swi ? kTM / 2 : kTM;
     const CUtensorMap mw = tensor_map(w.qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)rb,
-                                       (uint64_t)w.N, (uint64_t)rb, 16, swi ? kTM / 2 : kTM);
+                                      (uint64_t)w.N, (uint64_t)rb, 64, rows, false);
+    const CUtensorMap mws = tensor_map(w.qs, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)rb,
+                                       (uint64_t)w.N, (uint64_t)rb, 16, rows, false);
     const CUtensorMap mx = tensor_map(xq, CU_TENSOR_MAP_DATA_TYPE_UINT8, (uint64_t)w.K,
-                                       (uint64_t)a.M, (uint64_t)w.K, 16, kTN);
+                                      (uint64_t)a.M, (uint64_t)w.K, 128, kTN, true);
     const CUtensorMap ms = tensor_map(xd, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (uint64_t)(w.K / QK),
-                                       (uint64_t)a.M, (uint64_t)(w.K / QK) * 4, kTB, kTN);
+                                      (uint64_t)a.M, (uint64_t)(w.K / QK) * 4, kTB, kTN, false);
     const int64_t ntiles = swi ? a.swi_F / (kTM / 2) : (w.N + kTM - 1) / kTM;
     dim3 grid((unsigned)ntiles, (unsigned)((a.M + kTN - 1) / kTN));
-    k_gemm_tc<WT><<<grid, kTThreads, kTS * TcStage<WT>::kBytes, st>>>(mw, mx, ms, a);
+    k_gemm_tc<WT><<<grid, kTThreads, tc_smem<WT>(), st>>>(mw, mws, mx, ms, a);
     GB_CUDA(cudaGetLastError());
 }
 
