@@ -111,7 +111,7 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
 __device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
     uint32_t done;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 1000000;\n"
         " selp.u32 %0, 1, 0, p;\n}"
         : "=r"(done)
         : "r"(su32(b)), "r"(parity)
@@ -420,20 +420,15 @@ __global__ void __launch_bounds__(kTThreads, 1)
                 dw1 = dw2;
                 dw2 = dw3;
                 const float* dx = sXt + 2 * (lb * kTN + cg * 32);  // (d_x, c) per column
-                // two halves of 16 columns (fewer live registers); the accumulator gets its bias
-                // word back once both are read, then the MMA may use it again
+                // two halves of 16 columns (fewer live registers); after the second read the
+                // bias word goes back (its latency overlaps the scaling), then the accumulator
+                // is released
 #pragma unroll
                 for (int hf = 0; hf < 2; ++hf) {
                     uint32_t v[16];
                     tmem_ld16(lane_base + lb * kTN + hf * 16, v);
                     tmem_wait_ld();
-                    if (hf == 1) {
-                        tmem_st_bias32(lane_base + lb * kTN);
-                        tmem_wait_st();
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&bar_tempty[lb]);
-                    }
+                    if (hf == 1) tmem_st_bias32(lane_base + lb * kTN);
                     // per column: t = fma(bits as float, d_x, c) = sumi * d_x (one rounding: the
                     // float is 12582912 + sumi exactly and c = -12582912 * d_x exactly), then
                     // acc = fma(t, d_w, acc)
@@ -449,6 +444,10 @@ __global__ void __launch_bounds__(kTThreads, 1)
                         acc[hf * 8 + 2 * j + 1] = fma2(t1, dwv, acc[hf * 8 + 2 * j + 1]);
                     }
                 }
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bar_tempty[lb]);  // the MMA may use it again
             }
             if (!ok) break;
             __syncwarp();
