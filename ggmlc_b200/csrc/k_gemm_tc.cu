@@ -330,14 +330,18 @@ __global__ void __launch_bounds__(kTThreads, 1)
                     *(uint4*)(d + 2048) = hi;
                 }
             }
-            // activation scales [row][block] -> [block][row], each with -1.5*2^23 * d_x (exact:
-            // d_x carries the 11 significant bits of an fp16 scale)
-            for (int r = p; r < kTN; r += 32 * kHelpWarps) {
-                const float4 v = *(const float4*)(sXr + r * 4);
-                const float e[4] = {v.x, v.y, v.z, v.w};
+            // activation scales [row][block] -> [block][row pair]: (d_x, d_x', c, c') for rows
+            // 2k, 2k+1 with c = -1.5*2^23 * d_x (exact: d_x carries the 11 significant bits of an
+            // fp16 scale), so the epilogue's packed pairs load as they are
+            for (int k = p; k < kTN / 2; k += 32 * kHelpWarps) {
+                const float4 v0 = *(const float4*)(sXr + (2 * k) * 4);
+                const float4 v1 = *(const float4*)(sXr + (2 * k + 1) * 4);
+                const float e0[4] = {v0.x, v0.y, v0.z, v0.w}, e1[4] = {v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
                 for (int lb = 0; lb < kTB; ++lb)
-                    *(float2*)(sXt + 2 * (lb * kTN + r)) = make_float2(e[lb], __fmul_rn(e[lb], -12582912.0f));
+                    *(float4*)(sXt + 4 * (lb * (kTN / 2) + k)) =
+                        make_float4(e0[lb], e1[lb], __fmul_rn(e0[lb], -12582912.0f),
+                                    __fmul_rn(e1[lb], -12582912.0f));
             }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // A -> MMA
             __syncwarp();
@@ -419,7 +423,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
                 dw0 = dw1;
                 dw1 = dw2;
                 dw2 = dw3;
-                const float* dx = sXt + 2 * (lb * kTN + cg * 32);  // (d_x, c) per column
+                const float* dx = sXt + 4 * (lb * (kTN / 2) + cg * 16);  // per column pair
                 // two halves of 16 columns (fewer live registers); after the second read the
                 // bias word goes back (its latency overlaps the scaling), then the accumulator
                 // is released
@@ -433,15 +437,11 @@ __global__ void __launch_bounds__(kTThreads, 1)
                     // float is 12582912 + sumi exactly and c = -12582912 * d_x exactly), then
                     // acc = fma(t, d_w, acc)
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) {
-                        const float4 a4 = *(const float4*)(dx + 2 * (hf * 16 + 4 * j));
-                        const float4 b4 = *(const float4*)(dx + 2 * (hf * 16 + 4 * j) + 4);
-                        const float2 t0 = fma2(make_float2(__uint_as_float(v[4 * j]), __uint_as_float(v[4 * j + 1])),
-                                               make_float2(a4.x, a4.z), make_float2(a4.y, a4.w));
-                        const float2 t1 = fma2(make_float2(__uint_as_float(v[4 * j + 2]), __uint_as_float(v[4 * j + 3])),
-                                               make_float2(b4.x, b4.z), make_float2(b4.y, b4.w));
-                        acc[hf * 8 + 2 * j] = fma2(t0, dwv, acc[hf * 8 + 2 * j]);
-                        acc[hf * 8 + 2 * j + 1] = fma2(t1, dwv, acc[hf * 8 + 2 * j + 1]);
+                    for (int j = 0; j < 8; ++j) {
+                        const float4 a4 = *(const float4*)(dx + 4 * (hf * 8 + j));
+                        const float2 t = fma2(make_float2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1])),
+                                              make_float2(a4.x, a4.y), make_float2(a4.z, a4.w));
+                        acc[hf * 8 + j] = fma2(t, dwv, acc[hf * 8 + j]);
                     }
                 }
                 tmem_wait_st();

@@ -76,39 +76,13 @@ __device__ __forceinline__ float ref_v_silu(float x) {
     return __fdiv_rn(x, __fadd_rn(1.0f, e));
 }
 
-// Packed fp32 pairs (sm_100 f32x2 instructions): elementwise IEEE round-to-nearest, the same
-// results as two scalar operations in half the instructions.
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
-    float2 d;
-    asm("{\n .reg .b64 ra, rb, rc, rd;\n mov.b64 ra, {%2,%3};\n mov.b64 rb, {%4,%5};\n"
-        " mov.b64 rc, {%6,%7};\n fma.rn.f32x2 rd, ra, rb, rc;\n mov.b64 {%0,%1}, rd;\n}"
-        : "=f"(d.x), "=f"(d.y)
-        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-    return d;
-}
+// Packed fp32 pairs (sm_100 f32x2 instructions, the CUDA builtins): elementwise IEEE
+// round-to-nearest, the same results as two scalar operations in half the instructions.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
 __device__ __forceinline__ float2 sub2(float2 a, float2 b) {
-    float2 d;
-    asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2,%3};\n mov.b64 rb, {%4,%5};\n"
-        " sub.rn.f32x2 rd, ra, rb;\n mov.b64 {%0,%1}, rd;\n}"
-        : "=f"(d.x), "=f"(d.y)
-        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-    return d;
-}
-__device__ __forceinline__ float2 add2(float2 a, float2 b) {
-    float2 d;
-    asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2,%3};\n mov.b64 rb, {%4,%5};\n"
-        " add.rn.f32x2 rd, ra, rb;\n mov.b64 {%0,%1}, rd;\n}"
-        : "=f"(d.x), "=f"(d.y)
-        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-    return d;
-}
-__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
-    float2 d;
-    asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2,%3};\n mov.b64 rb, {%4,%5};\n"
-        " mul.rn.f32x2 rd, ra, rb;\n mov.b64 {%0,%1}, rd;\n}"
-        : "=f"(d.x), "=f"(d.y)
-        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-    return d;
+    return __fadd2_rn(a, make_float2(-b.x, -b.y));
 }
 
 // Programmatic dependent launch.  A kernel launched with launch_pdl may start while the previous
