@@ -3,12 +3,12 @@
 // fp16 scales applied by epilogue warps.
 //
 // Arithmetic.  One tcgen05.mma (M = 128 weight rows, N = 128 activation rows, K = 32) per
-// 32-element block adds every exact int32 block dot of a 128 x 128 tile onto a tensor-memory
-// accumulator that holds 1.5 * 2^23 (0x4B400000): the epilogue reads the bits as the float
-// 12582912 + sumi, forms sumi * d_x with one fma against the exact constant -12582912 * d_x,
-// multiplies by d_w and accumulates the block terms in fp32 registers, then writes 0x4B400000
-// back for the next block — the block formula of the reference's vec_dot
-// (ggml-cpu/quants.c:225-256, :451-477) with the integer part exact.
+// 32-element block writes every exact int32 block dot of a 128 x 128 tile into a tensor-memory
+// accumulator; the epilogue adds 0x4B400000 (1.5 * 2^23) to the bits, which makes them the
+// float 12582912 + sumi, forms sumi * d_x with one fma against the exact constant
+// -12582912 * d_x, multiplies by d_w and accumulates the block terms in fp32 registers — the
+// block formula of the reference's vec_dot (ggml-cpu/quants.c:225-256, :451-477) with the
+// integer part exact.
 // Q4_0 nibbles are widened in shared memory to 16 * (q - 8) (exact in int8); their weight scales
 // are divided by 16 to compensate.
 //
@@ -21,16 +21,18 @@
 // scale word of every weight row (4 fp16 scales of the stage) and the 4 fp32 activation scales
 // of every activation row.
 //
-// Warps (20, one CTA per SM):
+// Warps (12, one CTA per SM):
 //   warp 0      TMA producer (one thread), stage ring of 3-4 stages;
-//   warps 1-2   weight quants into the MMA layout (Q4_0 widened), activation scales transposed
-//               to [block][row], then mbarrier
-//               "ready" (the MMA and the epilogue wait on it);
-//   warp 3      MMA issuer (one thread) and tensor-memory owner: 4 accumulators of 128 columns,
+//   warp 1      MMA issuer (one thread) and tensor-memory owner: 4 accumulators of 128 columns,
 //               one per block of a stage, one tcgen05.mma + tcgen05.commit per block;
-//   warps 4-19  epilogue: warp w reads tensor-memory lanes 32*(w%4).. (its weight rows) and 32
-//               columns (activation rows) 32*((w-4)/4).. of each finished block with tcgen05.ld,
-//               writes the bias word back with tcgen05.st, releases the accumulator, scales.
+//   warps 2-3   weight quants into the MMA layout (Q4_0 widened), weight scales to fp32 pairs
+//               [block][row], activation scales transposed to [block][row pair], then mbarrier
+//               "ready" (the MMA and the epilogue wait on it);
+//   warps 4-11  epilogue: warp w reads tensor-memory lanes 32*(w%4).. (its weight rows) and 64
+//               columns (activation rows) 64*((w-4)/4).. of each finished block with the
+//               16x256b tcgen05.ld shape (a thread holds 4 weight rows x 16 columns, so one
+//               shared-memory read of activation scales serves 4 rows), releases the
+//               accumulator as soon as the values are in registers, scales.
 // Every wait on an mbarrier is bounded: past the limit the kernel records an error in
 // gemm_tc_error, stops issuing, waits (bounded) for its tensor-core work to drain, frees the
 // tensor memory and returns.
@@ -56,9 +58,15 @@ constexpr int kTB = 4;              // blocks per stage = tensor-memory accumula
 // stages in the ring: 4 (Q4_0) or 3 (Q8_0, whose raw halves take more room)
 template <int WT>
 constexpr int stages() { return WT == T_Q8_0 ? 3 : 4; }
-constexpr int kHelpWarp0 = 1, kHelpWarps = 2;
-constexpr int kMmaWarp = 3;
-constexpr int kEpiWarp0 = 4, kEpiWarps = 16;
+constexpr int kMmaWarp = 1;
+constexpr int kHelpWarp0 = 2, kHelpWarps = 2;
+#ifndef GB_TC_COLS
+#define GB_TC_COLS 32
+#endif
+constexpr int kCols = GB_TC_COLS;              // accumulator columns per epilogue warp
+static_assert(kCols == 32 || kCols == 64, "epilogue width");
+constexpr int kJ = kCols / 8;                  // 8-column groups per epilogue thread
+constexpr int kEpiWarp0 = 4, kEpiWarps = 4 * (128 / kCols);
 constexpr int kTThreads = (kEpiWarp0 + kEpiWarps) * 32;
 constexpr int kTmemCols = kTB * kTN;
 constexpr uint32_t kBiasBits = 0x4B400000u;      // 1.5 * 2^23
@@ -73,7 +81,8 @@ struct TcStage {
     static constexpr int kWs = kTM * 16;    // a row's scale word
     static constexpr int kXr = kTN * 16;    // 4 fp32 scales per activation row
     static constexpr int kXt = kTB * kTN * 8;  // (d_x, -1.5*2^23*d_x) pairs [block][row]
-    static constexpr int kBytes = kA + kB + kRaw + kWs + kXr + kXt;
+    static constexpr int kWf = kTB * kTM * 8;  // (d_w, d_w) fp32 pairs [block][row]
+    static constexpr int kBytes = kA + kB + kRaw + kWs + kXr + kXt + kWf;
     static constexpr uint32_t kTx = kRaw + kB + kWs + kXr;  // TMA bytes
     static_assert(kBytes % 1024 == 0, "stage alignment");
 };
@@ -111,7 +120,7 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
 __device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
     uint32_t done;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 1000000;\n"
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
         " selp.u32 %0, 1, 0, p;\n}"
         : "=r"(done)
         : "r"(su32(b)), "r"(parity)
@@ -171,28 +180,21 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(const void* p) {
 constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kTN >> 3) << 17) |
                             ((uint32_t)(kTM >> 4) << 24);
 
-// D += A * B (the accumulator holds the bias word when the block starts)
+// D = A * B (the accumulator is overwritten: one block per accumulator)
 __device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc) {
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
         " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(1)
+        "l"(adesc), "l"(bdesc), "r"(kIdesc), "r"(0)
         : "memory");
 }
 
-// the bias word into 32 consecutive columns of this thread's lane
-__device__ __forceinline__ void tmem_st_bias32(uint32_t taddr) {
-    const uint32_t b = kBiasBits;
+// 16 lanes x 32 columns from lane `taddr.lane` (16x256b shape, 4 repeats): thread t gets, for
+// each 8-column group j, rows t/4 and t/4 + 8 at columns 8j + 2(t%4) + {0, 1}:
+// v[4j + 0..1] = row t/4, v[4j + 2..3] = row t/4 + 8
+__device__ __forceinline__ void tmem_ld_16x256(uint32_t taddr, uint32_t (&v)[16]) {
     asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
-        "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
-        "r"(b)
-        : "memory");
-}
-// 16 consecutive columns of this thread's tensor-memory lane
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
+        "tcgen05.ld.sync.aligned.16x256b.x4.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,"
         "%14,%15}, [%16];"
         : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
           "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
@@ -200,11 +202,18 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
         : "r"(taddr)
         : "memory");
 }
-__device__ __forceinline__ void tmem_wait_ld() {
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_wait_st() {
-    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+// wait for this thread's tensor-memory loads; the registers the loads fill are operands, so no
+// use of them is scheduled before the wait
+__device__ __forceinline__ void tmem_wait_ld(uint32_t (&a)[16], uint32_t (&b)[16]) {
+    asm volatile(
+        "tcgen05.wait::ld.sync.aligned;"
+        : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]), "+r"(a[6]),
+          "+r"(a[7]), "+r"(a[8]), "+r"(a[9]), "+r"(a[10]), "+r"(a[11]), "+r"(a[12]), "+r"(a[13]),
+          "+r"(a[14]), "+r"(a[15]), "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]), "+r"(b[4]),
+          "+r"(b[5]), "+r"(b[6]), "+r"(b[7]), "+r"(b[8]), "+r"(b[9]), "+r"(b[10]), "+r"(b[11]),
+          "+r"(b[12]), "+r"(b[13]), "+r"(b[14]), "+r"(b[15])
+        :
+        : "memory");
 }
 // the epilogue warps only (named barrier 1)
 __device__ __forceinline__ void epi_sync() {
@@ -293,7 +302,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
             }
         }
         __syncwarp();
-    } else if (warp < kHelpWarp0 + kHelpWarps) {
+    } else if (warp >= kHelpWarp0 && warp < kHelpWarp0 + kHelpWarps) {
         // ---------------------------------------------------------------- helpers
         const int p = tid - kHelpWarp0 * 32;  // 0..63
         for (int t = 0; t < ns && !*abort; ++t) {
@@ -343,6 +352,21 @@ __global__ void __launch_bounds__(kTThreads, 1)
                         make_float4(e0[lb], e1[lb], __fmul_rn(e0[lb], -12582912.0f),
                                     __fmul_rn(e1[lb], -12582912.0f));
             }
+            // weight scales to (d_w, d_w) fp32 pairs [block][row] (Q4_0: d_w / 16, the widened
+            // quants being 16 * (q - 8)); a row's 16-byte scale word holds the stage's 4 fp16
+            // scales in its low halves for the first 32 blocks of a 64-block group, else the high
+            {
+                const int sh = (((t * kTB) >> 5) & 1) * 16;
+                const float wsc = WT == T_Q4_0 ? 0.0625f : 1.0f;
+                const uint32_t* sWs = (const uint32_t*)(sRaw + S::kRaw);
+                float2* sWf = (float2*)(sRaw + S::kRaw + S::kWs + S::kXr + S::kXt);
+                for (int c = p; c < kTB * kTM; c += 32 * kHelpWarps) {
+                    const int r = c & (kTM - 1), lb = c >> 7;
+                    const float d = __fmul_rn(
+                        __half2float(__ushort_as_half((unsigned short)(sWs[r * 4 + lb] >> sh))), wsc);
+                    sWf[lb * kTM + r] = make_float2(d, d);
+                }
+            }
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // A -> MMA
             __syncwarp();
             if (lane == 0) mbar_arrive(&bar_ready[s]);
@@ -381,90 +405,108 @@ __global__ void __launch_bounds__(kTThreads, 1)
         __syncwarp();
     } else {
         // ---------------------------------------------------------------- epilogue
-        const int q = warp & 3, cg = (warp - kEpiWarp0) >> 2;
-        const int r = q * 32 + lane;  // weight row of the tile (tensor-memory lane)
-        const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16) + cg * 32;
-        // every accumulator starts with the bias word
-#pragma unroll
-        for (int b = 0; b < kTB; ++b) tmem_st_bias32(lane_base + b * kTN);
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
+        // warp (q, ch): tensor-memory lanes 32q.. and columns kCols*ch.. of every accumulator;
+        // thread (g, cp) = (lane / 4, lane % 4) holds weight rows 32q + 8k + g (k = 0..3) at
+        // columns kCols*ch + 8j + 2cp + {0, 1} (j < kCols / 8) in acc[k][j]
+        const int q = warp & 3, ch = (warp - kEpiWarp0) >> 2;
+        const int g = lane >> 2, cp = lane & 3;
+        const uint32_t wbase = tmem + ((uint32_t)(q * 32) << 16) + ch * kCols;
+        constexpr uint32_t kHalfLanes = 16u << 16;
+        // every accumulator starts free
         if (lane == 0)
             for (int b = 0; b < kTB; ++b) mbar_arrive(&bar_tempty[b]);
-        float2 acc[16];
+        float2 acc[4][kJ];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) acc[j] = make_float2(0.0f, 0.0f);
-        const float wsc = WT == T_Q4_0 ? 0.0625f : 1.0f;
+        for (int k = 0; k < 4; ++k)
+#pragma unroll
+            for (int j = 0; j < kJ; ++j) acc[k][j] = make_float2(0.0f, 0.0f);
+        // 32 columns (j0.. j0 + 3) of the thread's 4 rows: per column the bits sumi + 0x4B400000
+        // are the float 12582912 + sumi (|sumi| < 2^22), t = fma(that, d_x, c) = sumi * d_x (one
+        // rounding: c = -12582912 * d_x exactly), then acc = fma(t, d_w, acc); one
+        // (d_x, d_x', c, c') read serves 4 rows
+        auto scale = [&](const uint32_t(&va)[16], const uint32_t(&vb)[16], const float* dx,
+                         const float2(&dw)[4], int j0) {
+            auto u = [](uint32_t bits) { return __uint_as_float(bits + kBiasBits); };
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+                const float4 a4 = *(const float4*)(dx + 4 * (4 * jj + cp));
+                const float2 x2 = make_float2(a4.x, a4.y), c2 = make_float2(a4.z, a4.w);
+                float2& a0 = acc[0][j0 + jj];
+                float2& a1 = acc[1][j0 + jj];
+                float2& a2 = acc[2][j0 + jj];
+                float2& a3 = acc[3][j0 + jj];
+                a0 = fma2(fma2(make_float2(u(va[4 * jj]), u(va[4 * jj + 1])),
+                               x2, c2), dw[0], a0);
+                a1 = fma2(fma2(make_float2(u(va[4 * jj + 2]), u(va[4 * jj + 3])),
+                               x2, c2), dw[1], a1);
+                a2 = fma2(fma2(make_float2(u(vb[4 * jj]), u(vb[4 * jj + 1])),
+                               x2, c2), dw[2], a2);
+                a3 = fma2(fma2(make_float2(u(vb[4 * jj + 2]), u(vb[4 * jj + 3])),
+                               x2, c2), dw[3], a3);
+            }
+        };
         // waits are made warp-uniform by a vote: tensor-memory loads and stores need the whole
         // warp converged
         for (int t = 0; t < ns && !*abort; ++t) {
             const int s = t % kTS;
             if (!__all_sync(0xffffffffu, mbar_wait(&bar_ready[s], (t / kTS) & 1, abort))) break;
             const uint8_t* st = stage(s);
-            const uint4 sw = *(const uint4*)(st + S::kA + S::kB + S::kRaw + r * 16);
             const float* sXt = (const float*)(st + S::kA + S::kB + S::kRaw + S::kWs + S::kXr);
-            // this row's 4 scales: low halves for the first 32 blocks of a 64-block group; the
-            // next block's scale moves to dw0 after each block (the block loop is not unrolled)
-            const int sh = (((t * kTB) >> 5) & 1) * 16;
-            float dw0 = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(sw.x >> sh))), wsc);
-            float dw1 = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(sw.y >> sh))), wsc);
-            float dw2 = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(sw.z >> sh))), wsc);
-            float dw3 = __fmul_rn(__half2float(__ushort_as_half((unsigned short)(sw.w >> sh))), wsc);
+            const float2* sWf = (const float2*)(sXt + S::kXt / 4);
             bool ok = true;
 #pragma unroll 1
             for (int lb = 0; lb < kTB; ++lb) {
+                float2 dw[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) dw[k] = sWf[lb * kTM + q * 32 + 8 * k + g];
                 if (!__all_sync(0xffffffffu, mbar_wait(&bar_tfull[lb], t & 1, abort))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const float2 dwv = make_float2(dw0, dw0);
-                dw0 = dw1;
-                dw1 = dw2;
-                dw2 = dw3;
-                const float* dx = sXt + 4 * (lb * (kTN / 2) + cg * 16);  // per column pair
-                // two halves of 16 columns (fewer live registers); after the second read the
-                // bias word goes back (its latency overlaps the scaling), then the accumulator
-                // is released
-#pragma unroll
-                for (int hf = 0; hf < 2; ++hf) {
-                    uint32_t v[16];
-                    tmem_ld16(lane_base + lb * kTN + hf * 16, v);
-                    tmem_wait_ld();
-                    if (hf == 1) tmem_st_bias32(lane_base + lb * kTN);
-                    // per column: t = fma(bits as float, d_x, c) = sumi * d_x (one rounding: the
-                    // float is 12582912 + sumi exactly and c = -12582912 * d_x exactly), then
-                    // acc = fma(t, d_w, acc)
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const float4 a4 = *(const float4*)(dx + 4 * (hf * 8 + j));
-                        const float2 t = fma2(make_float2(__uint_as_float(v[2 * j]), __uint_as_float(v[2 * j + 1])),
-                                              make_float2(a4.x, a4.y), make_float2(a4.z, a4.w));
-                        acc[hf * 8 + j] = fma2(t, dwv, acc[hf * 8 + j]);
-                    }
+                const uint32_t ta = wbase + lb * kTN;
+                const float* dx = sXt + 4 * (lb * (kTN / 2) + ch * (kCols / 2));
+                uint32_t va[16], vb[16];
+                tmem_ld_16x256(ta, va);
+                tmem_ld_16x256(ta + kHalfLanes, vb);
+                tmem_wait_ld(va, vb);
+                if constexpr (kCols == 32) {
+                    // the accumulator is released as soon as its values are in registers
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&bar_tempty[lb]);  // the MMA may use it again
+                    scale(va, vb, dx, dw, 0);
+                } else {
+                    // columns 32..63 load while 0..31 are scaled; the accumulator is released
+                    // once both reads are done, before the last scaling
+                    uint32_t wa[16], wb[16];
+                    tmem_ld_16x256(ta + 32, wa);
+                    tmem_ld_16x256(ta + kHalfLanes + 32, wb);
+                    scale(va, vb, dx, dw, 0);
+                    tmem_wait_ld(wa, wb);
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&bar_tempty[lb]);
+                    scale(wa, wb, dx + 4 * 16, dw, 4);
                 }
-                tmem_wait_st();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&bar_tempty[lb]);  // the MMA may use it again
             }
             if (!ok) break;
             __syncwarp();
             if (lane == 0) mbar_arrive(&bar_empty[s]);  // this stage's scales are read
         }
-        if (!*abort) {
-            if (!swi) {
-                const int n = n0 + r;
+        if (!*abort && !swi) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int n = n0 + q * 32 + 8 * k + g;
                 if (n < a.N) {
                     const float bn = a.bias ? a.bias[n] : 0.0f;
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
+                    for (int j = 0; j < kJ; ++j) {
 #pragma unroll
                         for (int e = 0; e < 2; ++e) {
-                            const int m = m0 + cg * 32 + 2 * j + e;
+                            const int m = m0 + ch * kCols + 8 * j + 2 * cp + e;
                             if (m < a.M) {
-                                float o = e ? acc[j].y : acc[j].x;
+                                float o = e ? acc[k][j].y : acc[k][j].x;
                                 if (a.bias) o = __fadd_rn(o, bn);
                                 if (a.residual)
                                     o = __fadd_rn(a.residual[(int64_t)m * a.res_stride + n], o);
@@ -479,30 +521,53 @@ __global__ void __launch_bounds__(kTThreads, 1)
             // SwiGLU: lanes 0-63 hold gate rows n0.., lanes 64-127 the up rows of the same pairs.
             // The up warps hand their sums over in shared memory (the stage ring is free now:
             // every MMA and every TMA load has completed before the last stage's "ready").
-            float* xch = (float*)tsm;  // [64 pairs][128 columns]
+            constexpr int kXs = kTN + 8;  // padded row stride in floats
+            float* xch = (float*)tsm;     // [64 pairs][kXs]
             epi_sync();
             if (q >= 2 && !*abort) {
 #pragma unroll
-                for (int j = 0; j < 16; ++j)
-                    *(float2*)(xch + (r - 64) * kTN + cg * 32 + 2 * j) = acc[j];
+                for (int k = 0; k < 4; ++k)
+#pragma unroll
+                    for (int j = 0; j < kJ; ++j)
+                        *(float2*)(xch + ((q - 2) * 32 + 8 * k + g) * kXs + ch * kCols + 8 * j + 2 * cp) =
+                            acc[k][j];
             }
             epi_sync();
             if (q < 2 && !*abort) {
-                const int pr = n0 + r;  // pair index
+                // pairs n0 + 32q + 8k + g: for each activation row m the warp's lanes with one cp
+                // hold the 32 pairs of one Q8_0 block (8 row groups g x 4 rows k)
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
+                for (int j = 0; j < kJ; ++j) {
 #pragma unroll
                     for (int e = 0; e < 2; ++e) {
-                        const int col = cg * 32 + 2 * j + e, m = m0 + col;
-                        const float up = xch[r * kTN + col];
-                        const float h = __fmul_rn(ref_v_silu(e ? acc[j].y : acc[j].x), up);
-                        if (m < a.M) {  // warp-uniform
-                            if (a.y) a.y[(int64_t)m * a.y_stride + pr] = h;
-                            if (a.yq) {  // the warp's 32 lanes: one Q8_0 block of this row m
-                                float d16, qv;
-                                q8_block(h, lane, d16, qv);
-                                a.yq[(int64_t)m * a.swi_F + pr] = (int8_t)__float2int_rn(qv);
-                                if (lane == 0) a.yd[(int64_t)m * (a.swi_F / 32) + pr / 32] = d16;
+                        const int col = ch * kCols + 8 * j + 2 * cp + e, m = m0 + col;
+                        float h[4];
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            const float up = xch[(q * 32 + 8 * k + g) * kXs + col];
+                            h[k] = __fmul_rn(ref_v_silu(e ? acc[k][j].y : acc[k][j].x), up);
+                        }
+                        float amax = fmaxf(fmaxf(fabsf(h[0]), fabsf(h[1])), fmaxf(fabsf(h[2]), fabsf(h[3])));
+                        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 4));
+                        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 8));
+                        amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 16));
+                        if (m < a.M) {
+                            const int pr0 = n0 + q * 32 + g;
+                            if (a.y) {
+#pragma unroll
+                                for (int k = 0; k < 4; ++k)
+                                    a.y[(int64_t)m * a.y_stride + pr0 + 8 * k] = h[k];
+                            }
+                            if (a.yq) {  // Q8_0 quantization of the block (q8_block's formula)
+                                const float d = __fdiv_rn(amax, 127.0f);
+                                const float id = amax != 0.0f ? __fdiv_rn(127.0f, amax) : 0.0f;
+#pragma unroll
+                                for (int k = 0; k < 4; ++k)
+                                    a.yq[(int64_t)m * a.swi_F + pr0 + 8 * k] =
+                                        (int8_t)__float2int_rn(rintf(__fmul_rn(h[k], id)));
+                                if (g == 0)
+                                    a.yd[(int64_t)m * (a.swi_F / 32) + (n0 + q * 32) / 32] =
+                                        __half2float(__float2half_rn(d));
                             }
                         }
                     }
