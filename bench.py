@@ -749,6 +749,27 @@ def operator_sweep(local: int, reps: int = 5) -> dict:
                     e1.record(st)
                     e1.synchronize()
                     times[quant] = e0.elapsed_time(e1) * 1e3 / n
+                # prefill rows: the matmul alone on each GEMM path (GGMLC_B200_GEMM)
+                paths = {}
+                if M > 16:
+                    saved = os.environ.get("GGMLC_B200_GEMM")
+                    try:
+                        for path in ("tc", "mma"):
+                            os.environ["GGMLC_B200_GEMM"] = path
+                            call(ws[0], False)
+                            e0 = torch.cuda.Event(enable_timing=True)
+                            e1 = torch.cuda.Event(enable_timing=True)
+                            e0.record(st)
+                            for i in range(n):
+                                call(ws[i % copies], False)
+                            e1.record(st)
+                            e1.synchronize()
+                            paths[path] = round(e0.elapsed_time(e1) * 1e3 / n, 2)
+                    finally:
+                        if saved is None:
+                            os.environ.pop("GGMLC_B200_GEMM", None)
+                        else:
+                            os.environ["GGMLC_B200_GEMM"] = saved
                 ops = 2.0 * M * N * K
                 byts = wbytes + M * K * 34 / 32 + M * N * 4
                 bound_us = max(byts / (hbm * 1e9), ops / (tops * 1e12)) * 1e6
@@ -759,6 +780,8 @@ def operator_sweep(local: int, reps: int = 5) -> dict:
                     "gbs": round(byts / (us * 1e-6) / 1e9, 1),
                     "bound": "hbm" if byts / (hbm * 1e9) >= ops / (tops * 1e12) else "int8",
                     "frac": round(bound_us / us, 3)}
+                if paths:
+                    out["cells"][f"{name} {N}x{K} M={M}"]["matmul_us_by_path"] = paths
                 del x, xq, xd, y
             del ws
             torch.cuda.empty_cache()

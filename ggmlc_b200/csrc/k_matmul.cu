@@ -9,6 +9,8 @@
 // sums are exact; the fp32 summation order differs from the CPU's lane order.
 #include <cuda_fp16.h>
 
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "common.h"
@@ -356,6 +358,20 @@ void launch_gemm_block(const QWeight& w, const int8_t* xq, const float* xd, int6
 
 }  // namespace
 
+// Prefill GEMM path (M > 16 rows), chosen by measurement on B200: Q8_0 weights go to the tcgen05
+// kernel (k_gemm_tc.cu, 10-12% faster than the mma.sync kernel at every prefill shape measured),
+// Q4_0 weights to the mma.sync block kernel (7-10% faster there: the tcgen05 path widens the
+// nibbles to int8 in shared memory first).  The tcgen05 kernel needs K % 128 == 0.  The
+// environment variable GGMLC_B200_GEMM = "mma" or "tc" forces one path; it is read at every
+// launch, so one process can time both.
+static bool use_gemm_tc(const QWeight& w) {
+    if (!gemm_tc_fits(w.K)) return false;
+    const char* e = std::getenv("GGMLC_B200_GEMM");
+    if (e && std::strcmp(e, "mma") == 0) return false;
+    if (e && std::strcmp(e, "tc") == 0) return true;
+    return w.type == T_Q8_0;
+}
+
 void launch_gemm_swiglu(const GemvArgs& a, cudaStream_t st) {
     GB_CHECK(a.xq && a.xd && !a.xf, "gemm swiglu: Q8_0 input required");
     GB_CHECK(a.w.type == T_Q8_0 || a.w.type == T_Q4_0, "gemm swiglu: quantized weights required");
@@ -364,7 +380,7 @@ void launch_gemm_swiglu(const GemvArgs& a, cudaStream_t st) {
     GB_CHECK(a.y || a.yq, "gemm swiglu: no output");
     GB_CHECK(!a.yq == !a.yd, "gemm swiglu: Q8_0 output needs quants and scales");
     if (a.M == 0) return;
-    if (gemm_tc_fits(a.w.K)) {  // the tcgen05 GEMM with the same epilogue
+    if (use_gemm_tc(a.w)) {  // the tcgen05 GEMM with the same epilogue
         launch_gemm_tc_swiglu(a, st);
         return;
     }
@@ -395,7 +411,7 @@ void launch_matmul_q(const QWeight& w, const int8_t* xq, const float* xd, int64_
         launch_gemv_fused(a, st);
         return;
     }
-    if (gemm_tc_fits(w.K)) {  // prefill on tcgen05 (TMA stages of 4 blocks: K % 128 == 0)
+    if (use_gemm_tc(w)) {  // prefill on tcgen05 (TMA stages of 4 blocks: K % 128 == 0)
         launch_gemm_tc(w, xq, xd, M, y, y_stride, ep, st);
         return;
     }

@@ -91,11 +91,17 @@ def test_decode_matmul_close(G, wtype, M, N, K):
     assert _close(y, O.mul_mat(wtype, w, N, K, x))
 
 
+@pytest.mark.parametrize("path", ["default", "mma", "tc"])
 @pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_0])
 @pytest.mark.parametrize("M,N,K", [(1, 300, 4096), (3, 77, 14336), (8, 64, 576), (16, 96, 1024),
                                    (11, 100, 576), (17, 40, 1024), (64, 40, 4096)])
-def test_matmul_integer_path_bit_exact(G, wtype, M, N, K):
-    """Decode (M <= 16) and prefill (M > 16) kernels on inputs where fp32 summation is exact."""
+def test_matmul_integer_path_bit_exact(G, wtype, M, N, K, path, monkeypatch):
+    """Decode (M <= 16) and prefill (M > 16) kernels on inputs where fp32 summation is exact;
+    prefill on the routed GEMM path and on each path forced by GGMLC_B200_GEMM."""
+    if path != "default":
+        if M <= 16:
+            pytest.skip("decode rows do not use the prefill GEMM")
+        monkeypatch.setenv("GGMLC_B200_GEMM", path)
     rng = np.random.default_rng(7 * N + K + M + wtype)
     w, x = _int_exact_case(rng, wtype, N, K, M)
     wq, wd = G.upload_weight(wtype, w, N, K)
@@ -117,12 +123,15 @@ def test_decode_matmul_epilogue(G, wtype):
     assert np.array_equal(y, ref.astype(np.float32))
 
 
+@pytest.mark.parametrize("path", ["default", "mma", "tc"])
 @pytest.mark.parametrize("wtype", [O.Q8_0, O.Q4_0])
 @pytest.mark.parametrize("M", [17, 64, 130])
-def test_prefill_gemm_swiglu_epilogue(G, wtype, M):
+def test_prefill_gemm_swiglu_epilogue(G, wtype, M, path, monkeypatch):
     """Prefill gate_up GEMM with SwiGLU and Q8_0 quantization fused in its epilogue (a tile of
     64 gate rows + the 64 matching up rows): bit-exact with the CPU SwiGLU and quantizer applied
-    to the plain GEMM's outputs."""
+    to the plain GEMM's outputs, on the routed path and on each path forced by GGMLC_B200_GEMM."""
+    if path != "default":
+        monkeypatch.setenv("GGMLC_B200_GEMM", path)
     torch = G.torch_dev()
     rng = np.random.default_rng(M + 100 * wtype)
     F, K = 192, 1024
