@@ -411,6 +411,14 @@ def run_ours(args) -> None:
     ex.set_kernel_timing(False)
     pp_mm = [sum(v[i] for k, v in kt_pp.items() if k in ("gemm_q", "gemm_swiglu", "gemm_tc",
                                                             "gemm_tc_swiglu")) for i in range(3)]
+    # decode kernels of one token by device time, events around every launch (each launch then
+    # runs alone, without the programmatic-dependent-launch overlap of the timed run: an upper
+    # bound per kernel, for the breakdown)
+    ex.set_kernel_timing(True)
+    ex.reset_kernel_times()
+    decode(P)
+    kt_tg = ex.kernel_times()
+    ex.set_kernel_timing(False)
     tp_err = ex.tp_allreduce_error() if tp else 0
     if tp_err:
         raise RuntimeError("tensor-parallel all-reduce reported a timed-out peer wait: the timed "
@@ -467,6 +475,9 @@ def run_ours(args) -> None:
                                     sorted(kt_pp.items(), key=lambda x: -x[1][0])},
                       "matmul_int8_tops": round(pp_flops(args.model, P) / (pp_mm[0] / 1e3) / 1e12, 1)
                       if pp_mm[0] else None},
+            "tg_kernels": {k: {"us": round(v[0] * 1e3, 1), "launches": int(v[1]),
+                               "gbs": round(v[2] / (v[0] * 1e6), 1) if v[0] and v[2] else None}
+                           for k, v in sorted(kt_tg.items(), key=lambda x: -x[1][0])},
             "pg": {"value": round(seqs * args.steps * (P + G) / (tot_ms / 1e3), 1),
                    "unit": "tokens/s", "test": f"pp{P}+tg{G}"},
             "e2e": {"value": round(e2e_tg, 2), "unit": "tokens/s", "h2d_bytes_per_step": h2d,

@@ -75,6 +75,8 @@ def _load() -> ctypes.CDLL:
         "gb_executor_set_enable_cuda_graph": ([P, I], I),
         "gb_executor_is_cuda_graph_enabled": ([P], I),
         "gb_executor_is_cuda_graph_captured": ([P], I),
+        "gb_executor_set_decode_chain": ([P, I], I),
+        "gb_executor_decode_chain": ([P], I),
         "gb_executor_set_enable_profile": ([P, I], I),
         "gb_executor_reset_profile": ([P], I),
         "gb_executor_get_profile": ([P, ctypes.POINTER(D), ctypes.POINTER(D),
@@ -411,6 +413,14 @@ class ModelExecutor:
 
     def is_cuda_graph_captured(self) -> bool:
         return bool(_lib.gb_executor_is_cuda_graph_captured(self._h))
+
+    def set_decode_chain(self, enable: bool) -> None:
+        """Engine switch (no reference twin): run single-sequence decode steps as one persistent
+        launch (off by default; GGMLC_B200_CHAIN=1 turns the default on)."""
+        _check(_lib.gb_executor_set_decode_chain(self._h, int(bool(enable))))
+
+    def decode_chain(self) -> bool:
+        return bool(_lib.gb_executor_decode_chain(self._h))
 
     # bucketed graphs: one decode program (and CUDA graph) per batch bucket is kept anyway
     def set_enable_cuda_graph_buckets(self, enable: bool) -> None:

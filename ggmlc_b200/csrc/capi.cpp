@@ -413,6 +413,10 @@ int gb_executor_set_enable_cuda_graph(gb_executor* e, int enable) {
 int gb_executor_is_cuda_graph_enabled(const gb_executor* e) {
     return e->e->cuda_graph_enabled() ? 1 : 0;
 }
+int gb_executor_set_decode_chain(gb_executor* e, int enable) {
+    return guard([&] { e->e->set_decode_chain(enable != 0); });
+}
+int gb_executor_decode_chain(const gb_executor* e) { return e->e->decode_chain() ? 1 : 0; }
 int gb_executor_is_cuda_graph_captured(const gb_executor* e) {
     return e->e->cuda_graph_captured() ? 1 : 0;
 }

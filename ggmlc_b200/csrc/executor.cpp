@@ -10,6 +10,7 @@
 #include <mutex>
 #include <chrono>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <set>
 #include <sstream>
@@ -144,9 +145,16 @@ Executor::Executor(std::shared_ptr<Graph> g, const std::string& device, int tp_r
     GB_CUDA(cudaSetDevice(dev_));
     GB_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
     GB_CUDA(cudaMallocHost(&h_step_, sizeof(StepParams)));
+    GB_CUDA(cudaMallocHost(&step_ring_, kStepRing * sizeof(StepParams)));
+    for (cudaEvent_t& ev : step_ev_) GB_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
     GB_CUDA(cudaMalloc(&d_step_, sizeof(StepParams)));
     h_step_->pos = 0;
     GB_CUDA(cudaMemcpy(d_step_, h_step_, sizeof(StepParams), cudaMemcpyHostToDevice));
+    if (const char* e = std::getenv("GGMLC_B200_CHAIN")) chain_enabled_ = std::string(e) == "1";
+    if (const char* e = std::getenv("GGMLC_B200_CHAIN_OPS")) chain_max_ops_ = (size_t)std::max(0, std::atoi(e));
+    int coop = 0;
+    GB_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev_));
+    if (!coop) chain_enabled_ = false;
     if (tp_size > 1) {
         GB_CHECK(nccl_id != nullptr, "tensor parallelism needs the group's NCCL unique id");
         g_ = std::make_shared<Graph>(*g_);  // this rank's shapes are rewritten in a copy
@@ -220,6 +228,12 @@ int Executor::tp_allreduce_error() {
 // A peer all-reduce whose wait ran out wrote a sum that is not valid: every output read of this
 // executor syncs through here and raises (once; the word is cleared) instead of handing it out.
 void Executor::check_tp_error() {
+    if (chain_err_host_ && *(volatile int*)chain_err_host_) {
+        *(volatile int*)chain_err_host_ = 0;
+        throw std::runtime_error(
+            "decode chain: a wait ran out (about 2 s); the outputs of this run are not valid and "
+            "later chain launches in this process do nothing");
+    }
     if (ar_err_host_ && *(volatile int*)ar_err_host_) {
         *(volatile int*)ar_err_host_ = 0;
         throw std::runtime_error(
@@ -231,6 +245,7 @@ void Executor::check_tp_error() {
 Executor::~Executor() {
     cudaSetDevice(dev_);
     if (stream_) cudaStreamSynchronize(stream_);
+    if (chain_err_host_) cudaFreeHost(chain_err_host_);
     for (auto& [k, p] : programs_) free_program(*p);
     for (void* p : weight_allocs_) cudaFree(p);
     for (auto& [id, c] : kv_) {
@@ -241,6 +256,9 @@ Executor::~Executor() {
     for (auto& [k, t] : rope_tabs_) cudaFree(t.first);
     for (cudaEvent_t ev : kevents_) cudaEventDestroy(ev);
     if (h_step_) cudaFreeHost(h_step_);
+    if (step_ring_) cudaFreeHost(step_ring_);
+    for (cudaEvent_t ev : step_ev_)
+        if (ev) cudaEventDestroy(ev);
     if (d_step_) cudaFree(d_step_);
     if (prefix_pool_) cudaFree(prefix_pool_);
     if (pinned_out_) cudaFreeHost(pinned_out_);
@@ -428,6 +446,18 @@ void Executor::alloc_kv(int64_t slots, int64_t max_ctx) {
     if (!any) return;
     kv_max_ctx_ = max_ctx;
     kv_enabled_ = true;
+}
+
+void Executor::set_decode_chain(bool on) {
+    int coop = 0;
+    GB_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev_));
+    GB_CHECK(!on || coop, "decode chains need cooperative launch, which this device lacks");
+    if (on == chain_enabled_) return;
+    GB_CUDA(cudaStreamSynchronize(stream_));
+    for (auto& [k, p] : programs_) free_program(*p);
+    programs_.clear();
+    active_.reset();
+    chain_enabled_ = on;
 }
 
 void Executor::free_kv() {
@@ -697,7 +727,15 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
         pg.launches.push_back(std::move(fn));
         pg.launch_names.push_back(name);
         pg.launch_bytes.push_back(bytes);
+        pg.chain_descs.emplace_back();
+        pg.launch_w.emplace_back();
     };
+    // the last added launch streams the quantized weight qw (F: SwiGLU half width, 0: plain)
+    auto streams = [&](const QWeight* qw, int64_t F) {
+        pg.launch_w.back() = PfNext{qw->qs, qw->type, qw->N, qw->K, F};
+    };
+    // the last added launch can also run as an op of a decode chain
+    auto chainable = [&](ChainDesc d) { pg.chain_descs.back() = std::move(d); };
     // algorithmic bytes of a quantized matmul: weight quants + scales once, Q8_0 activations,
     // f32 outputs (and residual reads)
     auto mm_bytes = [](const QWeight* w, int64_t M, bool residual) {
@@ -730,6 +768,15 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
             launch_quantize_q8_0((const float*)p.ptr(src), stride, M, K, (int8_t*)p.ptr(qb),
                                  (float*)p.ptr(qdb), st);
         });
+        if (chain_row_ok(M, K))
+            chainable([=](const Program& p, ChainOp& c) {
+                c.kind = CH_ROW;
+                c.xf = (const float*)p.ptr(src);
+                c.D = K;
+                c.yq = (int8_t*)p.ptr(qb);
+                c.yd = (float*)p.ptr(qdb);
+                return true;
+            });
     };
     auto cont = [&](Val x, int op) -> Val {
         Val y;
@@ -902,6 +949,19 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         launch_layer_norm((const float*)p.ptr(xr), xs, M, D, eps, gamma, beta, y, D,
                                           yq, yd, st);
                 });
+                if (rms && chain_row_ok(M, D))
+                    chainable([=](const Program& p, ChainOp& c) {
+                        c.kind = CH_ROW;
+                        c.xf = (const float*)p.ptr(xr);
+                        c.D = D;
+                        c.rms = 1;
+                        c.eps = eps;
+                        c.gamma = gamma;
+                        c.y = hf ? (float*)p.ptr(orf) : nullptr;
+                        c.yq = hq ? (int8_t*)p.ptr(qr) : nullptr;
+                        c.yd = hq ? (float*)p.ptr(qdr) : nullptr;
+                        return true;
+                    });
                 break;
             }
             case OP_MUL_MAT: {
@@ -1029,10 +1089,10 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         }
                         const BufRef hr = h.ref, hq = h.q, hqd = h.qd;
                         const bool hf = h.has_f, hhq = h.has_q;
-                        add(xrms ? "gemv_rms_swiglu"
-                                 : (Mrun <= kGemvRouteRows ? "gemv_swiglu"
-                                                         : (Mrun <= kMmvMaxRows ? "mmv_swiglu" : "gemm_swiglu")), [=](Program& p, cudaStream_t st) {
+                        const size_t li = pg.launches.size();  // this launch's index
+                        auto mk = [=](const Program& p) {
                             GemvArgs a = ga;
+                            if (li < p.launch_pf.size()) a.pf = p.launch_pf[li];
                             if (virt) {
                                 a.xf = (const float*)p.ptr(xr);
                                 a.xf_stride = xs;
@@ -1053,8 +1113,15 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                                 a.yq = (int8_t*)p.ptr(hq);
                                 a.yd = (float*)p.ptr(hqd);
                             }
-                            launch_gemv_fused(a, st);
+                            return a;
+                        };
+                        add(xrms ? "gemv_rms_swiglu"
+                                 : (Mrun <= kGemvRouteRows ? "gemv_swiglu"
+                                                         : (Mrun <= kMmvMaxRows ? "mmv_swiglu" : "gemm_swiglu")), [=](Program& p, cudaStream_t st) {
+                            launch_gemv_fused(mk(p), st);
                         }, bytes);
+                        streams(qw, F);
+                        chainable([=](const Program& p, ChainOp& c) { return chain_gemv_op(mk(p), c); });
                         vals[sout] = h;
                         skip.insert(swi_op);
                         vals[out] = Val();  // never materialized
@@ -1072,8 +1139,10 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         pg.use(res.ref, add_op);
                     }
                     const BufRef yr = y.ref;
-                    add(xrms ? "gemv_rms" : (Mrun <= kGemvRouteRows ? (add_op >= 0 ? "gemv_res" : "gemv") : (add_op >= 0 ? "mmv_res" : "mmv")), [=](Program& p, cudaStream_t st) {
+                    const size_t li = pg.launches.size();  // this launch's index
+                    auto mk = [=](const Program& p) {
                         GemvArgs a = ga;
+                        if (li < p.launch_pf.size()) a.pf = p.launch_pf[li];
                         if (virt) {
                             a.xf = (const float*)p.ptr(xr);
                             a.xf_stride = xs;
@@ -1091,8 +1160,13 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                             a.residual = (const float*)p.ptr(rref);
                             a.res_stride = N;
                         }
-                        launch_gemv_fused(a, st);
+                        return a;
+                    };
+                    add(xrms ? "gemv_rms" : (Mrun <= kGemvRouteRows ? (add_op >= 0 ? "gemv_res" : "gemv") : (add_op >= 0 ? "mmv_res" : "mmv")), [=](Program& p, cudaStream_t st) {
+                        launch_gemv_fused(mk(p), st);
                     }, bytes);
+                    streams(qw, 0);
+                    chainable([=](const Program& p, ChainOp& c) { return chain_gemv_op(mk(p), c); });
                     if (tp_partial) tp_allreduce(y);
                     if (tp_vocab) y = tp_gather(y, oi);
                     if (add_op >= 0) {
@@ -1520,7 +1594,7 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         const BufRef yr = y.ref, yq = y.q, yqd = y.qd;
                         const bool hf = y.has_f, hq = y.has_q;
                         const double kvb = (double)Hkv * hd * 2 * 2;  // K+V bytes per position
-                        add("attn_decode", [=](Program& p, cudaStream_t st) {
+                        auto mk = [=](const Program& p) {
                             AttnDecArgs a = da;
                             a.kc = (__half*)((char*)da.kc + p.kv_slot * sb);
                             a.vc = (__half*)((char*)da.vc + p.kv_slot * sb);
@@ -1531,8 +1605,16 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                                 a.oq = (int8_t*)p.ptr(yq);
                                 a.od = (float*)p.ptr(yqd);
                             }
-                            launch_attn_decode(a, st);
+                            return a;
+                        };
+                        add("attn_decode", [=](Program& p, cudaStream_t st) {
+                            launch_attn_decode(mk(p), st);
                         }, kvb);
+                        chainable([=](const Program& p, ChainOp& c) {
+                            c.kind = CH_ATTN;
+                            c.at = mk(p);
+                            return chain_attn_ok(c.at);
+                        });
                         (void)row_f;
                     } else {
                         // RoPE + KV write in one launch, then attention over the cache
@@ -1762,7 +1844,95 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
     pg.arena_bytes = (size_t)total;
     ensure_arena((size_t)total);
     pg.arena = &arena_;
+    // each launch's L2 prefetch: the weights of the next launch that streams any
+    pg.launch_pf.assign(pg.launches.size(), PfNext{});
+    for (size_t i = pg.launches.size(), nxt = SIZE_MAX; i-- > 0;) {
+        if (nxt != SIZE_MAX) pg.launch_pf[i] = pg.launch_w[nxt];
+        if (pg.launch_w[i].qs) nxt = i;
+    }
+    // single-sequence decode on one GPU: runs of chainable launches become decode chains
+    if (kv && !pg.batch && tp_.size == 1 && chain_enabled_) fuse_chains(pg);
+    pg.chain_descs.clear();
     return P;
+}
+
+// Replace every run of at least three consecutive chainable launches, one of them a GEMV, by one
+// chain launch (k_chain.cu).  The run's table, barrier counters and attention scratch belong to
+// the program.
+void Executor::fuse_chains(Program& pg) {
+    const size_t n = pg.launches.size();
+    std::vector<Launch> launches;
+    std::vector<std::string> names;
+    std::vector<double> bytes;
+    size_t i = 0;
+    while (i < n) {
+        size_t j = i;
+        std::vector<ChainOp> ops;
+        bool gemv = false;
+        while (j < n && pg.chain_descs[j] && (!chain_max_ops_ || j - i < chain_max_ops_)) {
+            ChainOp op;
+            if (!pg.chain_descs[j](pg, op)) break;
+            gemv = gemv || op.kind == CH_GEMV;
+            ops.push_back(op);
+            ++j;
+        }
+        // a bounded chain length takes every chainable run, single ops included
+        if (j == i || (!chain_max_ops_ && (j - i < 3 || !gemv))) {
+            launches.push_back(pg.launches[i]);
+            names.push_back(pg.launch_names[i]);
+            bytes.push_back(pg.launch_bytes[i]);
+            ++i;
+            continue;
+        }
+        auto run = std::make_shared<ChainRun>();
+        run->descs.assign(pg.chain_descs.begin() + i, pg.chain_descs.begin() + j);
+        const int64_t part = chain_prepare(ops.data(), (int)ops.size(), dev_);
+        GB_CUDA(cudaMalloc(&run->d_ops, ops.size() * sizeof(ChainOp)));
+        pg.owned.push_back(run->d_ops);
+        GB_CUDA(cudaMalloc(&run->sync, sizeof(ChainSync)));
+        pg.owned.push_back(run->sync);
+        GB_CUDA(cudaMemset(run->sync, 0, sizeof(ChainSync)));
+        GB_CUDA(cudaMalloc(&run->part, std::max<int64_t>(part, 1) * sizeof(float)));
+        pg.owned.push_back(run->part);
+        double b = 0.0;
+        for (size_t k = i; k < j; ++k) b += pg.launch_bytes[k];
+        if (!chain_err_host_) {
+            GB_CUDA(cudaHostAlloc(&chain_err_host_, sizeof(int), cudaHostAllocMapped));
+            *chain_err_host_ = 0;
+            GB_CUDA(cudaHostGetDevicePointer((void**)&chain_err_dev_, chain_err_host_, 0));
+        }
+        int* err = chain_err_dev_;
+        launches.push_back([run, err](Program&, cudaStream_t st) {
+            launch_chain(run->d_ops, run->h_ops.data(), (int)run->h_ops.size(), run->sync,
+                         run->part, err, st);
+        });
+        std::string nm = "chain";
+        if (j - i <= 4) {  // short chains by their ops (per-op timing with a bounded length)
+            nm += ":";
+            for (size_t k = i; k < j; ++k) nm += (k > i ? "+" : "") + pg.launch_names[k];
+        }
+        names.push_back(nm);
+        bytes.push_back(b);
+        pg.chains.push_back(run);
+        i = j;
+    }
+    pg.launches = std::move(launches);
+    pg.launch_names = std::move(names);
+    pg.launch_bytes = std::move(bytes);
+}
+
+// Rewrite a chain's device table when the buffers it points at moved (outside any capture).
+void Executor::refresh_chain(Program& p, ChainRun& c) {
+    if (!c.h_ops.empty() && c.key_arena == *p.arena && c.key_slot == p.kv_slot) return;
+    std::vector<ChainOp> ops(c.descs.size());
+    for (size_t k = 0; k < ops.size(); ++k)
+        GB_CHECK(c.descs[k](p, ops[k]), "chain: an op no longer fits the chain");
+    chain_prepare(ops.data(), (int)ops.size(), dev_);
+    GB_CUDA(cudaStreamSynchronize(stream_));  // no launch in flight reads the old table
+    GB_CUDA(cudaMemcpy(c.d_ops, ops.data(), ops.size() * sizeof(ChainOp), cudaMemcpyHostToDevice));
+    c.h_ops = std::move(ops);
+    c.key_arena = *p.arena;
+    c.key_slot = p.kv_slot;
 }
 
 // ------------------------------------------------------------------------------ execution
@@ -1845,7 +2015,15 @@ void Executor::run() {
     GB_CHECK(active_, "run before prepare");
     const double t0 = profile_on_ ? now_ms() : 0;
     Program& p = *active_;
-    GB_CUDA(cudaMemcpyAsync(d_step_, h_step_, sizeof(StepParams), cudaMemcpyHostToDevice, stream_));
+    for (auto& c : p.chains) refresh_chain(p, *c);
+    // this step's parameters from a ring entry no queued copy still reads (the working copy is
+    // rewritten by the next prepare while this copy may still wait in the stream)
+    StepParams* stage = step_ring_ + step_next_;
+    GB_CUDA(cudaEventSynchronize(step_ev_[step_next_]));
+    *stage = *h_step_;
+    GB_CUDA(cudaMemcpyAsync(d_step_, stage, sizeof(StepParams), cudaMemcpyHostToDevice, stream_));
+    GB_CUDA(cudaEventRecord(step_ev_[step_next_], stream_));
+    step_next_ = (step_next_ + 1) % kStepRing;
     if (ktiming_) {
         const size_t n = p.launches.size();
         while (kevents_.size() < n + 1) {

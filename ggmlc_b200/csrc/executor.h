@@ -66,6 +66,21 @@ struct Val {
 
 struct Program;
 using Launch = std::function<void(Program&, cudaStream_t)>;
+// How a launch runs as one op of a decode chain (k_chain.cu): fills the op from the program's
+// current buffers and returns whether the chain implements it.  Empty: the launch cannot join.
+using ChainDesc = std::function<bool(const Program&, ChainOp&)>;
+// A run of consecutive launches replaced by one chain launch.  The device table is rewritten
+// before a run whenever the buffers it points at moved (arena growth, another KV slot); captured
+// graphs keep the table's address.
+struct ChainRun {
+    std::vector<ChainDesc> descs;
+    ChainOp* d_ops = nullptr;
+    std::vector<ChainOp> h_ops;
+    ChainSync* sync = nullptr;
+    float* part = nullptr;
+    char* key_arena = nullptr;
+    int64_t key_slot = -1;
+};
 
 struct Program {
     std::string key;
@@ -82,6 +97,10 @@ struct Program {
     std::vector<Launch> launches;
     std::vector<std::string> launch_names;
     std::vector<double> launch_bytes;  // algorithmic HBM bytes of each launch (0 if untracked)
+    std::vector<ChainDesc> chain_descs;  // per launch while lowering (empty: not chainable)
+    std::vector<PfNext> launch_w;   // per launch: the quantized weights it streams (GEMVs)
+    std::vector<PfNext> launch_pf;  // per launch: what it prefetches into L2 (the next launch_w)
+    std::vector<std::shared_ptr<ChainRun>> chains;
     std::map<uint32_t, Val> vals;
     std::map<uint32_t, char*> input_bufs;  // graph inputs (device, persistent per program)
     std::vector<void*> owned;              // device allocations to free
@@ -187,6 +206,12 @@ public:
     void set_logits_last_only(bool on) { logits_last_only_ = on; }
     bool logits_last_only() const { return logits_last_only_; }
     void set_enable_cuda_graph(bool on) { cuda_graph_ = on; }
+    // Decode chains (k_chain.cu): single-sequence decode steps run as one persistent launch.  Off
+    // by default (measured slower than the per-op launches at the Llama-3-8B decode shape: every
+    // op waits at a grid barrier and re-reads its operands through L2); toggling drops the
+    // prepared programs (the next prepare rebuilds them).
+    void set_decode_chain(bool on);
+    bool decode_chain() const { return chain_enabled_; }
     bool cuda_graph_enabled() const { return cuda_graph_; }
     bool cuda_graph_captured() const;
 
@@ -214,6 +239,8 @@ public:
 private:
     void upload_weights();
     std::shared_ptr<Program> build(const SymEnv& env, bool kv);
+    void fuse_chains(Program& pg);
+    void refresh_chain(Program& p, ChainRun& c);
     const float2* rope_table(int n_dims, float freq_base, float freq_scale, int64_t* n_pos,
                              float* theta_scale);
     void free_program(Program& p);
@@ -265,11 +292,26 @@ private:
     void free_kv();
     bool logits_last_only_ = false;
     std::vector<int32_t> out_rows_;
+    bool chain_enabled_ = false;  // decode chains (GGMLC_B200_CHAIN=1 turns them on by default)
+    // most ops per chain launch (GGMLC_B200_CHAIN_OPS; 0: a whole run of chainable launches).  A
+    // bound also chains runs shorter than three ops, so GGMLC_B200_CHAIN_OPS=1 times every op of
+    // the chain kernel as its own launch.
+    size_t chain_max_ops_ = 0;
+    int* chain_err_host_ = nullptr;  // mapped pinned word the chain kernel sets on failure
+    int* chain_err_dev_ = nullptr;
     bool cuda_graph_ = false;
     bool profile_on_ = false;
     Profile profile_;
-    StepParams* h_step_ = nullptr;  // pinned
+    StepParams* h_step_ = nullptr;  // working copy, rewritten by every prepare
     StepParams* d_step_ = nullptr;
+    // Pinned staging ring of step parameters.  An async host-to-device copy reads its pinned
+    // source when the stream reaches it, which can be many steps after run() returned; each run
+    // copies from its own ring entry, and an entry is rewritten only after the event recorded
+    // behind its previous copy has completed.
+    static constexpr int kStepRing = 64;
+    StepParams* step_ring_ = nullptr;
+    cudaEvent_t step_ev_[kStepRing] = {};
+    int step_next_ = 0;
     std::map<std::string, std::shared_ptr<Program>> programs_;
     std::shared_ptr<Program> active_;
     std::map<uint32_t, std::vector<uint8_t>> out_host_;

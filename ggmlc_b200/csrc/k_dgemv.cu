@@ -45,6 +45,7 @@
 
 #include "common.h"
 #include "kernels.h"
+#include "kdot.cuh"
 #include "kutil.cuh"
 
 namespace gb {
@@ -61,10 +62,14 @@ template <int WT>
 constexpr int chunk_blocks() { return WT == T_Q8_0 ? 64 : 128; }
 constexpr int kMaxChunks = 16;   // chunks per row at most (a warp group per chunk)
 constexpr size_t kRingBudget = 112 * 1024;
-constexpr long long kSpin = 4000000000LL;  // about 2 s at 1.9 GHz
-constexpr int kMagic = 0x4B400000;         // 1.5 * 2^23
 
 struct DArgs {
+    // L2 prefetch of the next GEMV's weights: rows pf_rb bytes apart, split over pf_grid CTAs
+    // like this kernel splits its own (SwiGLU: a second range pf_F rows on); at most pf_cap bytes
+    // per next-launch CTA; pf null: none
+    const uint8_t* pf;
+    int64_t pf_rb, pf_units, pf_F, pf_cap;
+    int pf_grid;
     const uint8_t* w;
     int64_t rb;        // bytes per weight row
     int nb;            // blocks per row
@@ -88,106 +93,6 @@ struct DArgs {
     const float* residual;  // [M][res_stride]
     int64_t res_stride;
 };
-
-__device__ __forceinline__ uint32_t su32(const void* p) {
-    return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ void mbar_init(uint64_t* b, int count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(b)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* b, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(b)),
-                 "r"(bytes)
-                 : "memory");
-}
-__device__ __forceinline__ bool mbar_test(uint64_t* b, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 20000;\n"
-        " selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(ok)
-        : "r"(su32(b)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity) {
-    if (mbar_test(b, parity)) return true;
-    const long long t0 = clock64();
-    while (!mbar_test(b, parity))
-        if (clock64() - t0 > kSpin) return false;
-    return true;
-}
-__device__ __forceinline__ int dp4a_us(unsigned a, int b, int c) {
-    int d;
-    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-    return d;
-}
-
-// One activation block as a lane holds it.
-struct XBlk {
-    int4 lo, hi;  // quants of elements 0-15, 16-31
-    float d;      // scale
-    int init;     // dot-chain start: 1.5 * 2^23 (Q8_0 weights), minus 8 * sum(q) for Q4_0
-};
-
-// sum(q) of a block's 32 quants
-__device__ __forceinline__ int qsum(const int4& lo, const int4& hi) {
-    const int one = 0x01010101;
-    int s = __dp4a(lo.x, one, 0);
-    s = __dp4a(lo.y, one, s);
-    s = __dp4a(lo.z, one, s);
-    s = __dp4a(lo.w, one, s);
-    s = __dp4a(hi.x, one, s);
-    s = __dp4a(hi.y, one, s);
-    s = __dp4a(hi.z, one, s);
-    return __dp4a(hi.w, one, s);
-}
-
-template <int WT>
-__device__ __forceinline__ int chain_init(const int4& lo, const int4& hi) {
-    return WT == T_Q4_0 ? kMagic - 8 * qsum(lo, hi) : kMagic;
-}
-
-// One weight block as the lanes consume it.  Q4_0: a = low nibbles (elements 0-15) and b = high
-// nibbles times 16 (elements 16-31), both as unsigned bytes; Q8_0: a, b = quant bytes 0-15, 16-31.
-struct WBlk {
-    uint4 a, b;
-};
-
-// acc += sumi * (d_w * d_x) of a weight block against one activation block
-template <int WT>
-__device__ __forceinline__ void block_term(const WBlk& w, float dw, const XBlk& x, float& acc) {
-    int s = x.init;
-    if (WT == T_Q4_0) {
-        int sh = 0;
-        s = dp4a_us(w.a.x, x.lo.x, s);
-        s = dp4a_us(w.a.y, x.lo.y, s);
-        s = dp4a_us(w.a.z, x.lo.z, s);
-        s = dp4a_us(w.a.w, x.lo.w, s);
-        sh = dp4a_us(w.b.x, x.hi.x, sh);
-        sh = dp4a_us(w.b.y, x.hi.y, sh);
-        sh = dp4a_us(w.b.z, x.hi.z, sh);
-        sh = dp4a_us(w.b.w, x.hi.w, sh);
-        s += sh >> 4;
-    } else {
-        s = __dp4a((int)w.a.x, x.lo.x, s);
-        s = __dp4a((int)w.a.y, x.lo.y, s);
-        s = __dp4a((int)w.a.z, x.lo.z, s);
-        s = __dp4a((int)w.a.w, x.lo.w, s);
-        s = __dp4a((int)w.b.x, x.hi.x, s);
-        s = __dp4a((int)w.b.y, x.hi.y, s);
-        s = __dp4a((int)w.b.z, x.hi.z, s);
-        s = __dp4a((int)w.b.w, x.hi.w, s);
-    }
-    acc = __fmaf_rn(__fsub_rn(__int_as_float(s), 12582912.0f), __fmul_rn(dw, x.d), acc);
-}
-
-__device__ __forceinline__ float half_lo(unsigned w) {
-    return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFFu)));
-}
-__device__ __forceinline__ float half_hi(unsigned w) {
-    return __half2float(__ushort_as_half((unsigned short)(w >> 16)));
-}
 
 __device__ double cta_sum_d(double v, double* sh) {
     v = warp_sum_d(v);
@@ -354,6 +259,23 @@ __global__ void __launch_bounds__(kT, 1) k_dgemv(DArgs a) {
             fetch_chunk<WT>(ring + (size_t)k * SB, a, row_of(item_row(k)), ch, &bar[k]);
     }
     __syncwarp();
+    // this CTA's share of the next weights into L2, requested before the wait for the previous
+    // launch: those bytes stream while this launch's prologue and rows run
+    if (a.pf && threadIdx.x == kT - 32) {
+        for (int nb = blockIdx.x; nb < a.pf_grid; nb += gridDim.x) {
+            const int64_t v0 = a.pf_units * nb / a.pf_grid, v1 = a.pf_units * (nb + 1) / a.pf_grid;
+            const int nr = a.pf_F ? 2 : 1;
+            const int64_t len = min((v1 - v0) * a.pf_rb, a.pf_cap / nr) & ~(int64_t)15;
+            for (int r = 0; r < nr; ++r) {
+                const uint8_t* src = a.pf + (v0 + r * a.pf_F) * a.pf_rb;
+                for (int64_t o = 0; o < len; o += 32768) {
+                    const uint32_t n = (uint32_t)min((int64_t)32768, len - o);
+                    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src + o), "r"(n)
+                                 : "memory");
+                }
+            }
+        }
+    }
 
     pdl_wait();
     for (int m = 0; m < M && a.xf; ++m) {
@@ -533,6 +455,16 @@ void launch_w(const DArgs& a, size_t smem, int grid, cudaStream_t st) {
 // activation stage: per row and block 16 + 16 quant bytes, the scale and the chain start
 size_t stage_bytes(int nb, int M) { return (size_t)M * nb * (16 + 16 + 4 + 4); }
 
+// bytes of the next GEMV's weights requested into L2 ahead of it (GGMLC_B200_L2PF, MiB; default
+// 0, off: 24-96 MiB measured no faster at the Llama-3-8B decode shape)
+size_t l2_prefetch_budget() {
+    static const size_t v = [] {
+        const char* e = getenv("GGMLC_B200_L2PF");
+        return (size_t)(e ? std::max(0LL, atoll(e)) : 0LL) << 20;
+    }();
+    return v;
+}
+
 size_t ring_budget() {
     static const size_t v = [] {
         const char* e = getenv("GGMLC_B200_DGEMV_RING");  // tuning: ring bytes per CTA
@@ -565,6 +497,22 @@ bool dgemv_eligible(const GemvArgs& a) {
 void launch_dgemv(const GemvArgs& a, cudaStream_t st) {
     GB_CHECK(dgemv_eligible(a), "dgemv: arguments outside the single-row bulk-copy GEMV");
     DArgs d;
+    d.pf = nullptr;
+    d.pf_rb = d.pf_units = d.pf_F = d.pf_cap = 0;
+    d.pf_grid = 0;
+    const PfNext& nx = a.pf;
+    if (nx.qs && l2_prefetch_budget() > 0 && (nx.type == T_Q4_0 || nx.type == T_Q8_0) &&
+        ((uintptr_t)nx.qs & 15) == 0 && nx.N > 0 && nx.K % QK == 0) {
+        int dv = 0;
+        GB_CUDA(cudaGetDevice(&dv));
+        const int64_t units = nx.F ? nx.F : nx.N;
+        d.pf = (const uint8_t*)nx.qs;
+        d.pf_rb = qrow_bytes(nx.type, nx.K);
+        d.pf_units = units;
+        d.pf_F = nx.F;
+        d.pf_grid = (int)std::max<int64_t>(1, std::min<int64_t>(sm_count(dv), (units + kW - 1) / kW));
+        d.pf_cap = (int64_t)l2_prefetch_budget() / d.pf_grid;
+    }
     d.w = (const uint8_t*)a.w.qs;
     d.rb = qrow_bytes(a.w.type, a.w.K);
     d.nb = (int)(a.w.K / QK);

@@ -96,6 +96,13 @@ void launch_matmul_q(const QWeight& w, const int8_t* xq, const float* xd, int64_
 //           Q8_0 rows (yq, yd) and/or f32 rows (y) of length F — exactly launch_swiglu.
 constexpr int kGemvMaxRows = 4;
 constexpr int kGemvRouteRows = 2;  // rows the engine sends to the GEMV (fused RMSNorm included)
+// The weights a GEMV launch streams, described for the launch before it (L2 prefetch)
+struct PfNext {
+    const void* qs = nullptr;  // split-row rows; null: nothing to prefetch
+    int type = 0;
+    int64_t N = 0, K = 0;
+    int64_t F = 0;             // SwiGLU: the up rows start F rows after the gate rows (0: plain)
+};
 struct GemvArgs {
     QWeight w;
     int M = 1;
@@ -115,6 +122,9 @@ struct GemvArgs {
     int64_t res_stride = 0;
     int8_t* yq = nullptr;
     float* yd = nullptr;
+    // L2 prefetch (launch_dgemv only): the weights of the next GEMV launch; each CTA requests,
+    // at its start, the rows that the same CTA index of that launch streams first
+    PfNext pf;
 };
 void launch_gemv_fused(const GemvArgs& a, cudaStream_t st);
 // whether the GEMV's shared-memory stage fits: gemv_fits for one configuration (staged = f32
@@ -287,5 +297,65 @@ size_t attn_workspace_bytes(int64_t s, int64_t Hq, int64_t hd, int64_t max_kv);
 void launch_attention(const TView& q, const __half* kc, const __half* vc, int64_t ctx,
                       int64_t Hkv, const StepParams* step, bool use_step, int64_t kv_off,
                       float scale, float* o, void* work, int64_t max_kv, cudaStream_t st);
+
+// ---- decode chain (k_chain.cu) ---------------------------------------------------------------
+// The launches of one single-sequence decode step — quantized GEMVs with their RMSNorm / quantize
+// prologues and residual / SwiGLU epilogues, decode attention with its RoPE and K/V write, row
+// norms — run as ONE persistent launch: one CTA per SM, the ops in order with a grid-wide barrier
+// between them, and per-warp bulk-copy rings that keep requesting the weights of the next GEMVs
+// while the CTA waits at a barrier or works on attention, so HBM streams across op boundaries.
+// Results: every GEMV bit-identical to launch_dgemv on the same input (same block order, lane
+// butterfly and chunk order); attention within the attention tests' tolerance (fp32 online
+// softmax, another summation order than launch_attn_decode).
+enum ChainKind : int { CH_GEMV = 0, CH_ATTN = 1, CH_ROW = 2 };
+struct ChainOp {
+    int kind = CH_GEMV;
+    // CH_GEMV (one row): y = W x; W in the split-row layout, rb bytes per row
+    const uint8_t* w = nullptr;
+    int wtype = 0;
+    int64_t N = 0, K = 0, rb = 0;
+    int swiglu = 0;              // y[n] = silu(row n) * row n + F, n < F
+    int64_t F = 0;
+    const int8_t* xq = nullptr;  // Q8_0 input, or
+    const float* xd = nullptr;
+    const float* xf = nullptr;   // f32 input quantized in the prologue (CH_ROW: the row)
+    int rms = 0;                 // RMSNorm the f32 input first (eps, optional gamma)
+    float eps = 0.0f;
+    const float* gamma = nullptr;
+    float* y = nullptr;          // f32 output (+bias, +residual)
+    const float* bias = nullptr;
+    const float* residual = nullptr;
+    // CH_ATTN: one decode row over the KV cache (rows == 1, not batched); splits per KV head
+    AttnDecArgs at;
+    int splits = 1;
+    // CH_ROW: D elements of xf (RMSNorm when rms) to f32 y and/or Q8_0 (yq, yd)
+    int64_t D = 0;
+    int8_t* yq = nullptr;
+    float* yd = nullptr;
+};
+// grid-barrier and attention-merge counters of the chain (zero-initialised once; every launch
+// leaves them as it found them)
+constexpr int kChainMaxKvHeads = 64;
+struct ChainSync {
+    unsigned count;
+    unsigned gen;
+    unsigned attn_cnt[kChainMaxKvHeads];
+};
+// whether one op can run inside the chain (alignment, shapes, kinds the chain implements)
+bool chain_gemv_ok(const GemvArgs& a);
+bool chain_attn_ok(const AttnDecArgs& a);
+bool chain_row_ok(int64_t M, int64_t D);
+// a CH_GEMV op from the arguments of launch_gemv_fused; false when the chain does not take them
+bool chain_gemv_op(const GemvArgs& a, ChainOp& c);
+// fills the derived fields of the ops (row bytes, attention splits for this GPU) and returns the
+// f32 elements of the attention-partials scratch the chain needs; throws when an op cannot run
+int64_t chain_prepare(ChainOp* ops, int n, int dev);
+// ops: device copy of n prepared ops (host_ops: the same on the host); part: chain_prepare's
+// floats; sync: zeroed ChainSync; err: device-visible int set to 1 when the launch fails (or null)
+void launch_chain(const ChainOp* ops, const ChainOp* host_ops, int n, ChainSync* sync, float* part,
+                  int* err, cudaStream_t st);
+// sticky error word (non-zero after one of the chain's bounded waits ran out; the sync counters
+// are then not trusted and later launches return at once)
+int chain_error();
 
 }  // namespace gb

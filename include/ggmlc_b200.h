@@ -120,6 +120,14 @@ int gb_executor_logits_last_only(const gb_executor* e);
 int gb_executor_set_enable_cuda_graph(gb_executor* e, int enable);
 int gb_executor_is_cuda_graph_enabled(const gb_executor* e);
 int gb_executor_is_cuda_graph_captured(const gb_executor* e);
+/* Decode chains (engine switch, no reference twin): a single-sequence decode step on one GPU
+ * runs its GEMVs, attention and row norms as ONE persistent launch (one CTA per SM, grid
+ * barriers between ops, weight copies requested ahead across op boundaries).  Off by default
+ * (environment GGMLC_B200_CHAIN=1 turns the default on where the device supports cooperative
+ * launch); changing it drops the prepared programs.  A chain wait that runs out (about 2 s)
+ * makes the next output read raise, and later chain launches in the process do nothing. */
+int gb_executor_set_decode_chain(gb_executor* e, int enable);
+int gb_executor_decode_chain(const gb_executor* e);
 /* set_enable_profile / reset_profile / get_profile — executor.h:103-116 */
 int gb_executor_set_enable_profile(gb_executor* e, int enable);
 int gb_executor_reset_profile(gb_executor* e);

@@ -182,3 +182,39 @@ def test_output_rows_select_prompt_logits(fixture):
     with pytest.raises(RuntimeError, match="not among"):
         r.executor.set_output_rows([n])
         r(*_args(r, gold["prompt"], 0))
+
+
+@pytest.mark.parametrize("fixture", ["tiny_llama_q8_0", "tiny_gpt2_q8_0"])
+def test_queued_steps_read_their_own_positions(fixture):
+    """Steps enqueued back to back, with no host sync between them (a prefill, 40 decode steps,
+    a second prefill, 40 more), each read the step parameters (position) their own prepare set,
+    though the host runs ahead of the device and rewrites them for later steps: the final
+    logits equal those of the same steps with a sync after each one, bit for bit."""
+    from ggmlc_b200 import _runtime as R
+
+    def run(sync_each: bool):
+        g = R.ModelLoader.load_from_file(str(GOLDEN / f"{fixture}.gguf"))
+        ex = R.ModelExecutor(g, "cuda")
+        ex.init_kv_cache(256)
+        ex.set_logits_last_only(True)
+        ex.set_enable_cuda_graph(True)
+        prompt = np.arange(1, 17, dtype=np.int32)
+
+        def step(toks, pos):
+            toks = np.asarray(toks, np.int32)
+            ex.prepare({"s": len(toks), "pos": pos, **{s: len(toks) for s in g.symbol_table}})
+            ex.set_input_by_id(g.inputs[0], toks)
+            if len(g.inputs) > 1:
+                ex.set_input_by_id(g.inputs[1], np.arange(pos, pos + len(toks), dtype=np.int32))
+            ex.run()
+            if sync_each:
+                ex.synchronize()
+
+        for seed in (3, 1):
+            step(prompt, 0)
+            for i in range(40):
+                step([(7 * i + seed) % 200], len(prompt) + i)
+        ex.synchronize()
+        return ex.get_output_array(g.outputs[0]).reshape(-1).copy()
+
+    assert np.array_equal(run(True), run(False))
