@@ -112,7 +112,8 @@ __device__ __forceinline__ Plan plan_of(const ChainOp& op, int warp) {
 }
 // local row of a warp's item k: units g, g + gw, ...; a SwiGLU pair's gate and up rows in turn
 __device__ __forceinline__ int item_row(const Plan& p, int k) {
-    return (p.g + (k / p.per) * p.gw) * p.per + k % p.per;
+    const int sh = p.per - 1;  // per is 1 or 2: shifts and masks, no division in the item loop
+    return ((p.g + (k >> sh) * p.gw) << sh) + (k & sh);
 }
 
 // A warp's producer cursor (lane 0 only; kept in shared memory, off the register budget): the

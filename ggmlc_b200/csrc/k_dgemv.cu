@@ -190,16 +190,34 @@ constexpr int slot_bytes() {
     return chunk_blocks<WT>() * (WT == T_Q8_0 ? 32 : 16) + (chunk_blocks<WT>() / 64) * 128;
 }
 
-// bulk copies of chunk c (blocks from c * chunk_blocks) of weight row `row` into a slot
+// The bulk copies of one item (chunk ch of a weight row), worked out once per warp: byte offsets
+// in the row and sizes of the quants (Q8_0: two halves) and of the scale group(s).
+struct ChunkCopy {
+    uint32_t qoff, qoff2, soff, qb, sb, tx;
+};
 template <int WT>
-__device__ __forceinline__ void fetch_chunk(uint8_t* slot, const DArgs& a, int64_t row, int c,
-                                            uint64_t* bar) {
+__device__ __forceinline__ ChunkCopy chunk_copy(const DArgs& a, int c) {
     constexpr int kCB = chunk_blocks<WT>();
+    constexpr int qsz = WT == T_Q8_0 ? 32 : 16;
     const int c0 = c * kCB, cb = min(kCB, a.nb - c0);
+    ChunkCopy cc;
+    cc.qoff = (uint32_t)c0 * 16;
+    cc.qoff2 = (uint32_t)(a.nb + c0) * 16;
+    cc.soff = (uint32_t)(a.nb * qsz + (c0 / 64) * 128);
+    cc.qb = (uint32_t)cb * 16;
+    cc.sb = (uint32_t)((cb + 63) / 64) * 128;
+    cc.tx = cc.qb * (WT == T_Q8_0 ? 2u : 1u) + cc.sb;
+    return cc;
+}
+
+// bulk copies of one item (weight row `row`, the warp's chunk) into a slot
+template <int WT>
+__device__ __forceinline__ void fetch_chunk(uint8_t* slot, const DArgs& a, int64_t row,
+                                            const ChunkCopy& cc, uint64_t* bar) {
+    constexpr int kCB = chunk_blocks<WT>();
+    constexpr int qsz = WT == T_Q8_0 ? 32 : 16;
     const uint8_t* src = a.w + row * a.rb;
-    const uint32_t qb = (uint32_t)cb * 16, sb = (uint32_t)((cb + 63) / 64) * 128;
-    const int qsz = WT == T_Q8_0 ? 32 : 16;
-    mbar_expect_tx(bar, qb * (WT == T_Q8_0 ? 2 : 1) + sb);
+    mbar_expect_tx(bar, cc.tx);
     auto copy = [&](void* dst, const void* from, uint32_t bytes) {
         asm volatile(
             "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, "
@@ -207,9 +225,9 @@ __device__ __forceinline__ void fetch_chunk(uint8_t* slot, const DArgs& a, int64
             "l"(from), "r"(bytes), "r"(su32(bar))
             : "memory");
     };
-    copy(slot, src + (size_t)c0 * 16, qb);
-    if (WT == T_Q8_0) copy(slot + kCB * 16, src + (size_t)(a.nb + c0) * 16, qb);
-    copy(slot + kCB * qsz, src + (size_t)a.nb * qsz + (size_t)(c0 / 64) * 128, sb);
+    copy(slot, src + cc.qoff, cc.qb);
+    if (WT == T_Q8_0) copy(slot + kCB * 16, src + cc.qoff2, cc.qb);
+    copy(slot + kCB * qsz, src + cc.soff, cc.sb);
 }
 
 // MAXM: activation rows (1 or 2; M <= MAXM at run time).
@@ -237,17 +255,21 @@ __global__ void __launch_bounds__(kT, 1) k_dgemv(DArgs a) {
     const int u0 = (int)((int64_t)a.units * blockIdx.x / gridDim.x);
     const int u1 = (int)((int64_t)a.units * (blockIdx.x + 1) / gridDim.x);
     const int per = a.swiglu ? 2 : 1;
-    auto row_of = [&](int i) -> int64_t {
-        const int u = u0 + i / per;
-        return a.swiglu ? (int64_t)u + (i & 1) * (int64_t)a.F : (int64_t)u;
-    };
+    const int sh = a.swiglu ? 1 : 0;  // log2(per)
     // this warp: chunk `ch` of units g, g + G, g + 2G, ... (nc <= kW: every warp has a chunk);
     // item k is row `per * unit + k % per` of unit g + (k / per) * G, so a SwiGLU pair's gate
     // and up rows go through the same warp, one after the other
     const int ch = warp % nc, g = warp / nc, G = (kW - ch + nc - 1) / nc;
     const int nu = u1 - u0;
     const int nmine = (nu > g ? (nu - g + G - 1) / G : 0) * per;
-    auto item_row = [&](int k) { return (g + (k / per) * G) * per + k % per; };  // local row
+    // item q: local unit g + (q >> sh) * G; its local row (unit << sh) + (q & sh); its weight row
+    // u0 + unit, or F rows on for the up row of a SwiGLU pair (no division in the item loop)
+    auto item_row = [&](int q) { return ((g + (q >> sh) * G) << sh) + (q & sh); };
+    auto item_wrow = [&](int q) -> int64_t {
+        const int64_t r = (int64_t)u0 + g + (q >> sh) * G;
+        return (q & sh) ? r + a.F : r;
+    };
+    const ChunkCopy cc = chunk_copy<WT>(a, ch);
     __shared__ int s_fail;
     if (threadIdx.x == 0) s_fail = 0;
     uint64_t* bar = bars[warp];
@@ -256,7 +278,7 @@ __global__ void __launch_bounds__(kT, 1) k_dgemv(DArgs a) {
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         for (int k = 0; k < D && k < nmine; ++k)
-            fetch_chunk<WT>(ring + (size_t)k * SB, a, row_of(item_row(k)), ch, &bar[k]);
+            fetch_chunk<WT>(ring + (size_t)k * SB, a, item_wrow(k), cc, &bar[k]);
     }
     __syncwarp();
     // this CTA's share of the next weights into L2, requested before the wait for the previous
@@ -319,11 +341,17 @@ __global__ void __launch_bounds__(kT, 1) k_dgemv(DArgs a) {
     for (int m = 0; m < MAXM; ++m) gate[m] = 0.0f;
     bool ok = true;
     int k = 0;
+    int rs = 0;        // ring slot of item k
+    uint32_t rph = 0;  // its mbarrier phase
     for (; k < nmine; ++k) {
-        const int s = k % D;
-        if (!__all_sync(0xffffffffu, mbar_wait(&bar[s], (uint32_t)(k / D) & 1u))) {
+        const int s = rs;
+        if (!__all_sync(0xffffffffu, mbar_wait(&bar[s], rph))) {
             ok = false;
             break;
+        }
+        if (++rs == D) {
+            rs = 0;
+            rph ^= 1u;
         }
         const uint8_t* slot = ring + (size_t)s * SB;
         const uint8_t* sc = slot + kCB * QS;
@@ -356,7 +384,7 @@ __global__ void __launch_bounds__(kT, 1) k_dgemv(DArgs a) {
         __syncwarp();
         if (lane == 0 && k + D < nmine) {  // the slot is consumed: refill it
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            fetch_chunk<WT>(ring + (size_t)s * SB, a, row_of(item_row(k + D)), ch, &bar[s]);
+            fetch_chunk<WT>(ring + (size_t)s * SB, a, item_wrow(k + D), cc, &bar[s]);
         }
 #pragma unroll
         for (int m = 0; m < MAXM; ++m) {
@@ -374,7 +402,7 @@ __global__ void __launch_bounds__(kT, 1) k_dgemv(DArgs a) {
 #pragma unroll
                 for (int m = 0; m < MAXM; ++m)
                     if (m < M && lane == m)
-                        a.y[(size_t)m * a.y_stride + u0 + i / 2] = __fmul_rn(ref_v_silu(gate[m]), acc[m]);
+                        a.y[(size_t)m * a.y_stride + u0 + (i >> 1)] = __fmul_rn(ref_v_silu(gate[m]), acc[m]);
             } else {
 #pragma unroll
                 for (int m = 0; m < MAXM; ++m) gate[m] = acc[m];
