@@ -52,6 +52,30 @@ namespace gb {
 
 __device__ int dgemv_error_word;
 
+// Optional per-CTA timeline (built with -DGB_DGEMV_TRACE only; not part of the shipped library):
+// for the n-th launch CTA b reaches, %globaltimer at entry (0), after the wait for the previous
+// launch (1), after its prologue (2), when warp 0 has consumed its items (3) and at exit (4).
+#ifdef GB_DGEMV_TRACE
+constexpr int kTrLaunches = 1024, kTrCtas = 160;
+__device__ unsigned g_dgemv_tr_n[kTrCtas];
+__device__ unsigned long long g_dgemv_tr[kTrLaunches][kTrCtas][5];
+#define DGEMV_TRACE(slot)                                                                   \
+    do {                                                                                    \
+        if (threadIdx.x == 0 && blockIdx.x < kTrCtas && tr_n < kTrLaunches) {              \
+            unsigned long long t_;                                                          \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t_));                          \
+            g_dgemv_tr[tr_n][blockIdx.x][(slot)] = t_;                                      \
+        }                                                                                   \
+    } while (0)
+#define DGEMV_TRACE_BEGIN                                                                   \
+    unsigned tr_n = kTrLaunches;                                                            \
+    if (threadIdx.x == 0 && blockIdx.x < kTrCtas) tr_n = atomicAdd(&g_dgemv_tr_n[blockIdx.x], 1u); \
+    DGEMV_TRACE(0)
+#else
+#define DGEMV_TRACE(slot) ((void)0)
+#define DGEMV_TRACE_BEGIN ((void)0)
+#endif
+
 namespace {
 
 constexpr int kW = 16;           // warps per CTA
@@ -233,6 +257,7 @@ __device__ __forceinline__ void fetch_chunk(uint8_t* slot, const DArgs& a, int64
 // MAXM: activation rows (1 or 2; M <= MAXM at run time).
 template <int WT, int MAXM>
 __global__ void __launch_bounds__(kT, 1) k_dgemv(DArgs a) {
+    DGEMV_TRACE_BEGIN;
     constexpr int kCB = chunk_blocks<WT>();
     constexpr int BPL = kCB / 32;  // activation blocks per lane
     extern __shared__ __align__(128) uint8_t smem[];
@@ -300,12 +325,14 @@ __global__ void __launch_bounds__(kT, 1) k_dgemv(DArgs a) {
     }
 
     pdl_wait();
+    DGEMV_TRACE(1);
     for (int m = 0; m < M && a.xf; ++m) {
         stage_f32<WT>(a, m, sxa(m), sxb(m), sxd(m), sxi(m), shd);
         if (a.rms) __syncthreads();  // shd is reused by the next row's reduction
     }
     if (a.xf) __syncthreads();
     pdl_launch();
+    DGEMV_TRACE(2);
 
     // the activation blocks of this warp's chunk: b = 128 ch + lane + 32 j
     XBlk x[MAXM][BPL];
@@ -420,6 +447,7 @@ __global__ void __launch_bounds__(kT, 1) k_dgemv(DArgs a) {
             }
         }
     }
+    DGEMV_TRACE(3);
     if (!ok) {
         if (lane == 0) {
             atomicExch(&dgemv_error_word, 1);
@@ -453,6 +481,7 @@ __global__ void __launch_bounds__(kT, 1) k_dgemv(DArgs a) {
             }
         }
     }
+    DGEMV_TRACE(4);
 }
 
 template <int WT, int MAXM>
@@ -480,8 +509,6 @@ void launch_w(const DArgs& a, size_t smem, int grid, cudaStream_t st) {
     else launch_t<WT, 2>(a, smem, grid, st);
 }
 
-// activation stage: per row and block 16 + 16 quant bytes, the scale and the chain start
-size_t stage_bytes(int nb, int M) { return (size_t)M * nb * (16 + 16 + 4 + 4); }
 
 // bytes of the next GEMV's weights requested into L2 ahead of it (GGMLC_B200_L2PF, MiB; default
 // 0, off: 24-96 MiB measured no faster at the Llama-3-8B decode shape)
@@ -492,6 +519,9 @@ size_t l2_prefetch_budget() {
     }();
     return v;
 }
+
+// activation stage: per row and block 16 + 16 quant bytes, the scale and the chain start
+size_t stage_bytes(int nb, int M) { return (size_t)M * nb * (16 + 16 + 4 + 4); }
 
 size_t ring_budget() {
     static const size_t v = [] {
@@ -575,6 +605,17 @@ void launch_dgemv(const GemvArgs& a, cudaStream_t st) {
     if (a.w.type == T_Q4_0) launch_w<T_Q4_0>(d, smem, grid, st);
     else launch_w<T_Q8_0>(d, smem, grid, st);
 }
+
+#ifdef GB_DGEMV_TRACE
+extern "C" int gb_dgemv_trace_read(unsigned long long* out, size_t bytes) {
+    if (bytes < sizeof(g_dgemv_tr)) return -1;
+    return cudaMemcpyFromSymbol(out, g_dgemv_tr, sizeof(g_dgemv_tr)) == cudaSuccess ? 0 : -1;
+}
+extern "C" int gb_dgemv_trace_reset() {
+    static const unsigned zero[kTrCtas] = {};
+    return cudaMemcpyToSymbol(g_dgemv_tr_n, zero, sizeof(zero)) == cudaSuccess ? 0 : -1;
+}
+#endif
 
 int dgemv_error() {
     int v = 0;
