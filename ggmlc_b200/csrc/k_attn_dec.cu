@@ -349,8 +349,12 @@ __global__ void __launch_bounds__(NW * 32) k_attn_decode_tc(AttnDecArgs a) {
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    // cached rows were written by earlier steps: the first block is requested before the wait
+    // cached rows were written by earlier steps: both ring slots (the warp's first two blocks) are
+    // requested before the wait, so at batch 1 (at most two blocks a warp) every K / V byte of
+    // the CTA is in flight while the previous launch finishes
     if (warp < nblk) stage(0, warp);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
+    if (warp + kTcWarps < nblk) stage(1, warp + kTcWarps);
     else asm volatile("cp.async.commit_group;" ::: "memory");
     pdl_wait();
     pdl_launch();
@@ -425,10 +429,7 @@ __global__ void __launch_bounds__(NW * 32) k_attn_decode_tc(AttnDecArgs a) {
     float m_r = -INFINITY, l_r = 0.0f;  // row g: running max, this thread's share of the sum
     int j = 0;                           // blocks of this warp done
     for (int b = warp; b < nblk; b += kTcWarps, ++j) {
-        __syncwarp();  // every lane is done with the slot the next block goes to
-        const int bn = b + kTcWarps;
-        if (bn < nblk) stage((j + 1) & 1, bn);
-        else asm volatile("cp.async.commit_group;" ::: "memory");
+        // blocks j and j + 1 of this warp are requested (groups in order): block j has landed
         asm volatile("cp.async.wait_group 1;" ::: "memory");
         __syncwarp();
         uint8_t* ck = ring + (j & 1) * SM::kSlot;
@@ -488,6 +489,10 @@ __global__ void __launch_bounds__(NW * 32) k_attn_decode_tc(AttnDecArgs a) {
             tc_mma(o[2 * dg + 1], ahi, vb[2], vb[3]);
             tc_mma(o[2 * dg + 1], alo, vb[2], vb[3]);
         }
+        __syncwarp();  // every lane is done with slot j & 1: block j + 2 goes there
+        const int bn = b + 2 * kTcWarps;
+        if (bn < nblk) stage(j & 1, bn);
+        else asm volatile("cp.async.commit_group;" ::: "memory");
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     l_r = __fadd_rn(l_r, __shfl_xor_sync(0xffffffffu, l_r, 1));
