@@ -99,7 +99,7 @@ def ensure_model(model: str, quant: str, device: str | None) -> Path:
     if not path.exists():
         BENCH_DIR.mkdir(parents=True, exist_ok=True)
         tmp = path.with_suffix(".tmp")
-        synth.synth_llama(tmp, model, synth.Q4_0 if quant == "q4_0" else synth.Q8_0,
+        synth.synth_model(tmp, model, synth.Q4_0 if quant == "q4_0" else synth.Q8_0,
                           device=device, name=f"{model}_{quant}")
         os.replace(tmp, path)
     return path
@@ -300,6 +300,7 @@ def run_ours(args) -> None:
     gguf = model_path(args.model, args.quant)
 
     from ggmlc_b200 import _runtime as R
+    from ggmlc_b200 import synth
 
     g = R.ModelLoader.load_from_file(str(gguf))
     tp = world > 1 and not args.replicas
@@ -318,19 +319,26 @@ def run_ours(args) -> None:
     ex.set_enable_cuda_graph(True)
     stream = torch.cuda.ExternalStream(ex.stream(), device=torch.device("cuda", local))
     rng = np.random.default_rng(rank)
-    prompt = rng.integers(0, 128256, size=P).astype(np.int32)
+    n_vocab = int(synth.SHAPES[args.model].vocab) if args.model in synth.SHAPES else 128256
+    prompt = rng.integers(0, n_vocab, size=P).astype(np.int32)
     dummy = np.ones(1, np.int32)
+    # GPT-2 graphs take the token positions as a second input
+    pos_id = g.inputs[1] if len(g.inputs) > 1 else None
 
     def prefill(upload: bool):
         ex.prepare({"s": P, sym: P, "pos": 0})
         if upload:
             ex.set_input_by_id(in_id, prompt)
+        if pos_id is not None and upload:
+            ex.set_input_by_id(pos_id, np.arange(P, dtype=np.int32))
         ex.run()
 
     def decode(pos: int, upload_tok=None):
         ex.prepare({"s": 1, sym: 1, "pos": pos})
         if upload_tok is not None:
             ex.set_input_by_id(in_id, upload_tok)
+        if pos_id is not None:
+            ex.set_input_by_id(pos_id, np.array([pos], np.int32))
         ex.run()
 
     # inputs resident: prompt and decode token uploaded once
