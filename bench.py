@@ -256,7 +256,7 @@ def run_reference(args) -> None:
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": f"{args.quant} x q8_0 int8 dot, fp32 accumulate (CPU)",
         "data": "synthetic: seeded N(0,0.02) random-init weights, dummy token ids",
-        "config": {"workload": f"{args.model} {args.quant} pp{P}+tg{G} B=1 (BASELINE configs[3])",
+        "config": {"workload": f"{args.model} {args.quant} pp{P}+tg{G} B=1 (BASELINE configs[{config_index(args.model)}])",
                    "model": args.model, "quant": args.quant, "prompt": P, "gen": G, "batch": 1,
                    "value_is": f"tg{G} decode tokens/s at positions {P}..{P + G - 1}"},
         "pp512": {"value": round(r["pp"], 1), "unit": "tokens/s"},
@@ -468,7 +468,7 @@ def run_ours(args) -> None:
             "dtype": "q4_0 x q8_0 int8 dot, fp32 accumulate",
             "data": "synthetic: seeded N(0,0.02) random-init weights (ggmlc Q4_0 quantizer), "
                     "dummy token ids for value, random prompt ids for e2e",
-            "config": {"workload": f"{args.model} {args.quant} pp{P}+tg{G} B=1 (BASELINE configs[3])",
+            "config": {"workload": f"{args.model} {args.quant} pp{P}+tg{G} B=1 (BASELINE configs[{config_index(args.model)}])",
                        "model": args.model, "quant": args.quant, "prompt": P, "gen": G,
                        "batch": 1,
                        "parallelism": (f"tp{world}" if tp else f"replicas x{world}") if world > 1
@@ -591,9 +591,17 @@ def pp_flops(model: str, P: int) -> float:
     from ggmlc_b200.synth import SHAPES
 
     c = SHAPES[model]
+    if not hasattr(c, "n_kv_heads"):  # GPT-2: fused QKV d -> 3d, O, up d -> ffn, down
+        per_layer = c.d_model * 3 * c.d_model + c.d_model * c.d_model + 2 * c.d_model * c.ffn
+        return 2.0 * P * c.n_layers * per_layer + 2.0 * c.vocab * c.d_model
     per_layer = c.d_model * ((c.n_heads + 2 * c.n_kv_heads) * c.head_dim) + \
         c.n_heads * c.head_dim * c.d_model + c.d_model * 2 * c.ffn + c.ffn * c.d_model
     return 2.0 * P * c.n_layers * per_layer + 2.0 * c.vocab * c.d_model
+
+
+def config_index(model: str) -> int:
+    """BASELINE.json configs entry a model shape belongs to."""
+    return {"gpt2-small": 0, "smollm2-135m": 2, "llama3-8b": 3, "llama3-70b": 4}.get(model, 3)
 
 
 def vocab_of(g, ex, out_id) -> int:
