@@ -3,7 +3,8 @@
 Run in a container that has the reference checkout (default /root/reference, or $GGMLC_REF) and a
 built oracle/_ref (``make -C oracle``):
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py               # everything
+    python tests/golden/make_golden.py --batch-only  # the per-sequence batch goldens only
 
 1. Seeded random-init HF models (transformers, no network) wrapped with the reference's own
    wrappers (examples/models/hub_models.py: load_smollm2_model :366, load_gpt2_model :47) and
@@ -146,6 +147,38 @@ def model_golden(L, gguf: Path, V: int, prompt_len: int, n_decode: int, seed: in
                 decode_logits=np.stack(dec_logits), greedy_tokens=np.array(tokens, np.int32))
 
 
+def batch_golden(L, gguf: Path, V: int, lengths: list[int], n_decode: int, seed: int,
+                 max_ctx: int = 1024):
+    """Several independent sequences through the reference's KV path, one executor each: for
+    prompt k (lengths[k] tokens), its greedy tokens and the logits row each token was chosen
+    from (row 0: the prefill's last row; row i: after feeding token i - 1 at position
+    lengths[k] + i - 1).  The oracle of batched decode: every row of a batched step must follow
+    its own sequence's reference run."""
+    rng = np.random.default_rng(seed)
+    prompts, toks, rows = [], [], []
+    out = np.empty(V * max_ctx, np.float32)
+    for n_p in lengths:
+        prompt = rng.integers(1, V, size=n_p, dtype=np.int32)
+        h = L.ref_model_open(str(gguf).encode(), 1)
+        assert h and L.ref_model_init_kv(h, max_ctx) == 1, L.ref_last_error()
+        n = L.ref_model_forward(h, p(prompt), n_p, 0, p(out), out.size)
+        assert n > 0, L.ref_last_error()
+        r = [out[(n_p - 1) * V:n_p * V].copy()]
+        t = [int(np.argmax(r[0]))]
+        for i in range(n_decode):
+            x = np.array([t[-1]], np.int32)
+            n = L.ref_model_forward(h, p(x), 1, n_p + i, p(out), out.size)
+            assert n == V, L.ref_last_error()
+            r.append(out[:V].copy())
+            t.append(int(np.argmax(out[:V])))
+        L.ref_model_close(h)
+        prompts.append(prompt)
+        toks.append(t)
+        rows.append(np.stack(r))
+    return dict(lengths=np.array(lengths, np.int32), prompts=np.concatenate(prompts),
+                tokens=np.array(toks, np.int32), logits=np.stack(rows))
+
+
 def op_golden(L, seed=7):
     rng = np.random.default_rng(seed)
     g = {}
@@ -225,6 +258,17 @@ def op_golden(L, seed=7):
     return g
 
 
+def main_batch():
+    """Only the per-sequence batch goldens, from the committed GGUFs (no recompilation)."""
+    L = ref_lib()
+    for fname in ("tiny_llama_q8_0.gguf", "tiny_llama_q4_0.gguf"):
+        f = HERE / fname
+        V = int(np.load(HERE / fname.replace(".gguf", ".npz"))["full_logits"].shape[1])
+        gold = batch_golden(L, f, V, [5, 17, 33, 9, 40, 3], n_decode=10, seed=31)
+        np.savez_compressed(HERE / fname.replace(".gguf", "_batch.npz"), **gold)
+        print(fname, "batch tokens", gold["tokens"][:, :6].tolist())
+
+
 def main():
     L = ref_lib()
     np.savez_compressed(HERE / "ops_golden.npz", **op_golden(L))
@@ -239,7 +283,8 @@ def main():
         gold = model_golden(L, f, V, prompt_len=37, n_decode=12, seed=11)
         np.savez_compressed(HERE / fname.replace(".gguf", ".npz"), **gold)
         print(fname, f.stat().st_size, "tokens", gold["greedy_tokens"][:8])
+    main_batch()
 
 
 if __name__ == "__main__":
-    main()
+    main_batch() if "--batch-only" in sys.argv else main()

@@ -112,3 +112,24 @@ def test_model_kv_decode_bit_exact(fixture):
         toks.append(int(np.argmax(y)))
         pos += 1
     assert toks == list(gold["greedy_tokens"])
+
+
+@pytest.mark.parametrize("fixture", ["tiny_llama_q8_0", "tiny_llama_q4_0"])
+def test_batch_goldens_pinned_by_oracle(fixture):
+    """The per-sequence goldens of the batched-decode test (written by the reference build) are
+    reproduced bit for bit by the oracle's own KV decode, for the first two sequences (the rest
+    run the same code path); every golden token is the argmax of its logits row."""
+    gold = np.load(GOLDEN / f"{fixture}_batch.npz")
+    lengths = [int(n) for n in gold["lengths"]]
+    offs = np.concatenate([[0], np.cumsum(lengths)])
+    V = gold["logits"].shape[2]
+    assert np.array_equal(np.argmax(gold["logits"], axis=2), gold["tokens"])
+    for k in range(2):
+        M = O.ModelOracle(GOLDEN / f"{fixture}.gguf")
+        assert M.init_kv_cache(1024)
+        prompt = gold["prompts"][offs[k]:offs[k + 1]]
+        y = M.forward(prompt, pos=0).reshape(-1, V)
+        assert np.array_equal(y[-1], gold["logits"][k][0])
+        for i in range(gold["tokens"].shape[1] - 1):
+            y = M.forward(np.array([gold["tokens"][k][i]]), pos=lengths[k] + i).reshape(-1)
+            assert np.array_equal(y, gold["logits"][k][i + 1]), f"sequence {k} step {i}"
