@@ -682,7 +682,7 @@ def gemv_roofline(local: int, N: int = 28672, K: int = 4096, R: int = 16, reps: 
     return {"bound": "hbm", "kernel": "k_dgemv (RMSNorm + gate_up Q4_0 + SwiGLU)",
             "shape": f"N={N} K={K} M=1", "achieved": round(achieved, 1), "peak": peak,
             "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_kind": kind,
-            "traffic": profiled_traffic("gemv_rms_swiglu"),
+            "traffic": profiled_traffic("dgemv_gate_up"),
             "bytes_per_launch": int(bytes_), "launch_us": round(ms * 1e3, 2),
             "timing": f"{R} back-to-back launches on distinct weights per event pair, "
                       f"mean of {reps} passes"}
