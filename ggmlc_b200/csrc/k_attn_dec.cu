@@ -309,6 +309,7 @@ __device__ __forceinline__ float ld_peer(const float* p, int rank) {
 // otherwise each CTA writes its partial for k_attn_combine.
 template <int HD, int NW, bool CL>
 __global__ void __launch_bounds__(NW * 32) k_attn_decode_tc(AttnDecArgs a) {
+    static_assert(NW * 32 >= HD, "one thread per element of the new k / v row");
     constexpr int kTcWarps = NW;
     using SM = TcAttnSmem<HD, NW>;
     constexpr int KS = HD / 16;   // k-steps of the score product = 16-dim groups of the output
@@ -360,6 +361,23 @@ __global__ void __launch_bounds__(NW * 32) k_attn_decode_tc(AttnDecArgs a) {
     pdl_launch();
 
     const float* qrow = a.qkv + (int64_t)row * a.qkv_stride;
+    // the new position's k and v (the CTA whose range holds it): this thread's element, loaded
+    // with the q heads below, so the CTA pays one round trip for both
+    const bool has_new = c0 <= pos && pos < c1;
+    const int nd = threadIdx.x;  // its element (head_dim <= the CTA's threads)
+    float nk0 = 0.0f, nk1 = 0.0f, nv = 0.0f;
+    if (has_new && nd < HD) {
+        const float* ks = qrow + a.k_off + (int64_t)hk * HD;
+        const int half = a.tab.n_dims / 2;
+        if (nd >= a.tab.n_dims) {
+            nk0 = ks[nd];
+        } else {
+            const int i = nd < half ? nd : nd - half;
+            nk0 = ks[i];
+            nk1 = ks[i + half];
+        }
+        nv = qrow[a.v_off + (int64_t)hk * HD + nd];
+    }
     {
         // rotated q heads (rope_elem's arithmetic): every load of this thread's elements is
         // issued before the first is used, so the rotation costs one round trip; rows >= rk zero
@@ -406,17 +424,22 @@ __global__ void __launch_bounds__(NW * 32) k_attn_decode_tc(AttnDecArgs a) {
         for (int e = kMaxRk * HD + threadIdx.x; e < 16 * HD; e += NT)
             *(__half*)(sq + (e / HD) * R + (e % HD) * 2) = __float2half_rn(0.0f);
     }
-    const bool has_new = c0 <= pos && pos < c1;
-    if (has_new) {
-        const float* ks = qrow + a.k_off + (int64_t)hk * HD;
-        for (int d = threadIdx.x; d < HD; d += kTcWarps * 32) {
-            const __half kh = __float2half_rn(rope_elem(ks, d, HD, a.tab, pos));
-            const __half vh = __float2half_rn(qrow[a.v_off + (int64_t)hk * HD + d]);
-            kslot[((int64_t)hk * a.ctx + pos) * HD + d] = kh;
-            vslot[((int64_t)hk * a.ctx + pos) * HD + d] = vh;
-            snew[d] = kh;
-            snew[HD + d] = vh;
+    if (has_new && nd < HD) {
+        // rope_elem's arithmetic on the values loaded above
+        float kr = nk0;
+        if (nd < a.tab.n_dims) {
+            const int half = a.tab.n_dims / 2;
+            const int i = nd < half ? nd : nd - half;
+            float c, sn;
+            rope_cs(a.tab, pos, i, c, sn);
+            kr = nd < half ? __fmaf_rn(nk0, c, -__fmul_rn(nk1, sn)) : __fmaf_rn(nk0, sn, __fmul_rn(nk1, c));
         }
+        const __half kh = __float2half_rn(kr);
+        const __half vh = __float2half_rn(nv);
+        kslot[((int64_t)hk * a.ctx + pos) * HD + nd] = kh;
+        vslot[((int64_t)hk * a.ctx + pos) * HD + nd] = vh;
+        snew[nd] = kh;
+        snew[HD + nd] = vh;
     }
     __syncthreads();  // sq and snew ready
     unsigned qf[KS][4];
