@@ -8,10 +8,12 @@ A step is one sequence: prefill of 512 prompt tokens (one ubatch, logits of the 
 (runtime/tools/ggmlc_bench.cpp:297-565).  `value` is decode tokens/s with inputs resident in HBM
 (dummy token ids as the reference harness uses, ggmlc_bench.cpp:303,431), timed with CUDA events
 on the executor's stream; `e2e` is the same decode metric through the public API with host
-buffers (token H2D, logits D2H and a host argmax every step).  N > 1 runs the model
-tensor-parallel over the N GPUs (one sequence; strong scaling: QKV / gate_up / O / down / output
-projection sharded, two NCCL all-reduces per layer), or with --replicas N independent copies
-(weak scaling); device time is the max over ranks.
+buffers (token H2D, logits D2H and a host argmax every step).  N > 1 follows the BASELINE
+configuration of the model: the Llama-3-70B shape (configs[4], "tensor-parallel over 2/4/8 B200")
+runs tensor-parallel over the N GPUs (one sequence; strong scaling: QKV / gate_up / O / down /
+output projection sharded, two all-reduces per layer); the shapes that one GPU serves (configs[0],
+[2], [3]) run N independent replicas, one sequence each (weak scaling).  --tp / --replicas force
+either; device time is the max over ranks.
 
 --impl reference times the reference's own CPU runtime (oracle/_ref/ggmlc-bench, built from the
 reference sources) on the same synthesized GGUF with all host threads: its `-pg 512,128` test,
@@ -303,7 +305,10 @@ def run_ours(args) -> None:
     from ggmlc_b200 import synth
 
     g = R.ModelLoader.load_from_file(str(gguf))
-    tp = world > 1 and not args.replicas
+    # tensor parallelism where the model's BASELINE configuration asks for it,
+    # replicas where one GPU serves the model (at batch 1 on the 8B shape, tensor parallelism
+    # adds two cross-GPU synchronizations a layer and measured slower than one GPU)
+    tp = world > 1 and not args.replicas and (args.tp or config_index(args.model) == 4)
     if tp:  # one tensor-parallel group over all ranks; the engine's own NCCL communicator
         box = [R.nccl_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(box, src=0)
@@ -981,6 +986,8 @@ def main():
     ap.add_argument("--no-sweep", action="store_true", help="skip the operator-sweep leg")
     ap.add_argument("--replicas", action="store_true",
                     help="N > 1: independent replicas instead of one tensor-parallel group")
+    ap.add_argument("--tp", action="store_true",
+                    help="N > 1: one tensor-parallel group for any model (default: the 70B shape)")
     ap.add_argument("--case", choices=sorted(CASES), help="launch one decode kernel of the L8 "
                     "shapes (a small case for ncu) instead of the benchmark")
     ap.add_argument("--reps", type=int, default=5)
