@@ -152,6 +152,7 @@ Executor::Executor(std::shared_ptr<Graph> g, const std::string& device, int tp_r
     GB_CUDA(cudaMemcpy(d_step_, h_step_, sizeof(StepParams), cudaMemcpyHostToDevice));
     if (const char* e = std::getenv("GGMLC_B200_CHAIN")) chain_enabled_ = std::string(e) == "1";
     if (const char* e = std::getenv("GGMLC_B200_CHAIN_OPS")) chain_max_ops_ = (size_t)std::max(0, std::atoi(e));
+    if (const char* e = std::getenv("GGMLC_B200_GEMV_AR")) gemv_ar_ = std::string(e) != "0";
     int coop = 0;
     GB_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev_));
     if (!coop) chain_enabled_ = false;
@@ -185,10 +186,13 @@ void Executor::setup_peer_allreduce() {
     ar_cap_ = (std::max<int64_t>(width, 1) * kMaxRows + 3) / 4 * 4;
     const size_t recv_bytes = (size_t)(2 * T * ar_cap_) * 4;
     const size_t flag_bytes = (size_t)(2 * T * kArCtas) * 4;
-    GB_CUDA(cudaMalloc(&ar_base_, recv_bytes + flag_bytes));
-    GB_CUDA(cudaMemset(ar_base_, 0, recv_bytes + flag_bytes));
-    GB_CUDA(cudaMalloc(&ar_epochs_, kArCtas * sizeof(uint32_t)));
-    GB_CUDA(cudaMemset(ar_epochs_, 0, kArCtas * sizeof(uint32_t)));
+    // the decode GEMV's epilogue all-reduce has slots, flags and epochs of its own
+    const size_t gflag_bytes = (size_t)(2 * T * kGemvArCtas) * 4;
+    const size_t total = 2 * recv_bytes + flag_bytes + gflag_bytes;
+    GB_CUDA(cudaMalloc(&ar_base_, total));
+    GB_CUDA(cudaMemset(ar_base_, 0, total));
+    GB_CUDA(cudaMalloc(&ar_epochs_, (kArCtas + kGemvArCtas) * sizeof(uint32_t)));
+    GB_CUDA(cudaMemset(ar_epochs_, 0, (kArCtas + kGemvArCtas) * sizeof(uint32_t)));
     // the error word lives in mapped pinned host memory: every host synchronisation reads it
     // without a copy (check_tp_error)
     GB_CUDA(cudaHostAlloc((void**)&ar_err_host_, sizeof(int), cudaHostAllocMapped));
@@ -216,6 +220,8 @@ void Executor::setup_peer_allreduce() {
         }
         ar_peers_.recv[p] = (float*)base;
         ar_peers_.flags[p] = (uint32_t*)(base + recv_bytes);
+        ar_peers_.grecv[p] = (float*)(base + recv_bytes + flag_bytes);
+        ar_peers_.gflags[p] = (uint32_t*)(base + 2 * recv_bytes + flag_bytes);
     }
 }
 
@@ -1140,8 +1146,22 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                     }
                     const BufRef yr = y.ref;
                     const size_t li = pg.launches.size();  // this launch's index
+                    // one decode row of a K-split projection: the all-reduce rides in the
+                    // GEMV's epilogue (no separate launch)
+                    GemvAllReduce gar;
+                    const bool ar_fused = tp_partial && Mrun == 1 && !pg.batch && gemv_ar_ &&
+                                          N <= ar_cap && (qw->type == T_Q4_0 || qw->type == T_Q8_0);
+                    if (ar_fused) {
+                        gar.peers = peers;
+                        gar.rank = tp_rank;
+                        gar.T = tp_.size;
+                        gar.epochs = ar_epochs + kArCtas;
+                        gar.cap = ar_cap;
+                        gar.err = ar_err;
+                    }
                     auto mk = [=](const Program& p) {
                         GemvArgs a = ga;
+                        a.ar = gar;
                         if (li < p.launch_pf.size()) a.pf = p.launch_pf[li];
                         if (virt) {
                             a.xf = (const float*)p.ptr(xr);
@@ -1167,7 +1187,7 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                     }, bytes);
                     streams(qw, 0);
                     chainable([=](const Program& p, ChainOp& c) { return chain_gemv_op(mk(p), c); });
-                    if (tp_partial) tp_allreduce(y);
+                    if (tp_partial && !ar_fused) tp_allreduce(y);
                     if (tp_vocab) y = tp_gather(y, oi);
                     if (add_op >= 0) {
                         vals[out_id] = y;

@@ -297,6 +297,9 @@ private:
     // bound also chains runs shorter than three ops, so GGMLC_B200_CHAIN_OPS=1 times every op of
     // the chain kernel as its own launch.
     size_t chain_max_ops_ = 0;
+    // tensor parallelism: decode-row all-reduces folded into the GEMV epilogue
+    // (GGMLC_B200_GEMV_AR=0: the separate all-reduce launch instead)
+    bool gemv_ar_ = true;
     int* chain_err_host_ = nullptr;  // mapped pinned word the chain kernel sets on failure
     int* chain_err_dev_ = nullptr;
     bool cuda_graph_ = false;

@@ -88,6 +88,7 @@ constexpr int kMaxChunks = 16;   // chunks per row at most (a warp group per chu
 constexpr size_t kRingBudget = 112 * 1024;
 
 struct DArgs {
+    GemvAllReduce ar;  // T > 0: y summed over the tensor-parallel ranks in the epilogue
     // L2 prefetch of the next GEMV's weights: rows pf_rb bytes apart, split over pf_grid CTAs
     // like this kernel splits its own (SwiGLU: a second range pf_F rows on); at most pf_cap bytes
     // per next-launch CTA; pf null: none
@@ -252,6 +253,54 @@ __device__ __forceinline__ void fetch_chunk(uint8_t* slot, const DArgs& a, int64
     copy(slot, src + cc.qoff, cc.qb);
     if (WT == T_Q8_0) copy(slot + kCB * 16, src + cc.qoff2, cc.qb);
     copy(slot + kCB * qsz, src + cc.soff, cc.sb);
+}
+
+__device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// The all-reduce of the epilogue (GemvAllReduce, kernels.h) over this CTA's rows [u0, u1) of y
+// (one activation row): slot [parity][rank] of every rank, flags, bounded wait, rank-order sum.
+__device__ void gemv_allreduce(const GemvAllReduce& ar, float* y, int u0, int u1) {
+    __shared__ uint32_t s_e;
+    __syncthreads();  // this CTA's rows of y are written
+    if (threadIdx.x == 0) s_e = ar.epochs[blockIdx.x] + 1;
+    __syncthreads();
+    const uint32_t e = s_e;
+    const int par = (int)(e & 1u), T = ar.T, me = ar.rank;
+    for (int p = 0; p < T; ++p) {
+        float* dst = ar.peers.grecv[p] + ((int64_t)par * T + me) * ar.cap;
+        for (int i = u0 + threadIdx.x; i < u1; i += kT) dst[i] = y[i];
+    }
+    __syncthreads();
+    if (threadIdx.x < T) {  // thread p tells rank p that this CTA's rows of slot [par][me] are in
+        __threadfence_system();
+        st_release_sys_u32(ar.peers.gflags[threadIdx.x] + ((int64_t)par * T + me) * kGemvArCtas + blockIdx.x, e);
+    }
+    if (threadIdx.x < T) {  // thread r waits for rank r's rows in this rank's memory
+        const uint32_t* f = ar.peers.gflags[me] + ((int64_t)par * T + threadIdx.x) * kGemvArCtas + blockIdx.x;
+        const long long t0 = clock64();
+        while (ld_acquire_sys_u32(f) != e) {
+            if (clock64() - t0 > kSpinCycles / 2) {  // about 1 s
+                *(volatile int*)ar.err = 1;     // host-mapped word
+                __threadfence_system();
+                break;
+            }
+        }
+    }
+    __syncthreads();
+    const float* src = ar.peers.grecv[me] + (int64_t)par * T * ar.cap;
+    for (int i = u0 + threadIdx.x; i < u1; i += kT) {
+        float v = __ldcg(src + i);
+        for (int r = 1; r < T; ++r) v = __fadd_rn(v, __ldcg(src + (int64_t)r * ar.cap + i));
+        y[i] = v;
+    }
+    if (threadIdx.x == 0) ar.epochs[blockIdx.x] = e;
 }
 
 // MAXM: activation rows (1 or 2; M <= MAXM at run time).
@@ -481,6 +530,7 @@ __global__ void __launch_bounds__(kT, 1) k_dgemv(DArgs a) {
             }
         }
     }
+    if (a.ar.T > 0) gemv_allreduce(a.ar, a.y, u0, u1);
     DGEMV_TRACE(4);
 }
 
@@ -580,6 +630,13 @@ void launch_dgemv(const GemvArgs& a, cudaStream_t st) {
     d.xf_stride = a.xf_stride;
     d.y_stride = a.y_stride;
     d.res_stride = a.res_stride;
+    d.ar = a.ar;
+    if (a.ar.T > 0) {
+        GB_CHECK(a.M == 1 && !a.swiglu && a.y_stride == a.w.N,
+                 "dgemv all-reduce: one activation row, plain output");
+        GB_CHECK(a.ar.T <= kMaxTp && a.ar.rank >= 0 && a.ar.rank < a.ar.T && a.w.N <= a.ar.cap,
+                 "dgemv all-reduce: bad rank / size or vector larger than the peer slots");
+    }
     d.swiglu = a.swiglu ? 1 : 0;
     d.F = (int)a.F;
     d.units = (int)(a.swiglu ? a.F : a.w.N);
@@ -596,6 +653,7 @@ void launch_dgemv(const GemvArgs& a, cudaStream_t st) {
     GB_CUDA(cudaGetDevice(&dev));
     // one CTA per SM, fewer when there are not 8 units per CTA
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(sm_count(dev), (d.units + kW - 1) / kW));
+    GB_CHECK(a.ar.T == 0 || grid <= kGemvArCtas, "dgemv all-reduce: more CTAs than flag slots");
     d.rows_cta = (int)((d.units + grid - 1) / grid + 1) * (d.swiglu ? 2 : 1);
     const size_t sb = a.w.type == T_Q8_0 ? slot_bytes<T_Q8_0>() : slot_bytes<T_Q4_0>();
     d.slots = (int)std::max<int64_t>(1, std::min<int64_t>(kMaxSlots, (int64_t)(ring_budget() / (kW * sb))));

@@ -483,6 +483,7 @@ void launch_gemv_fused(const GemvArgs& a, cudaStream_t st) {
         launch_dgemv(a, st);
         return;
     }
+    GB_CHECK(a.ar.T == 0, "gemv: the epilogue all-reduce needs the single-row decode GEMV");
     if (!a.xf && (a.M > kGemvRouteRows || !gemv_fits(a.w.type, a.w.K, a.M, false, false))) {
         launch_mmv(a, st);  // batched decode: the tensor-core kernel
         return;

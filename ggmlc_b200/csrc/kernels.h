@@ -96,6 +96,29 @@ void launch_matmul_q(const QWeight& w, const int8_t* xq, const float* xd, int64_
 //           Q8_0 rows (yq, yd) and/or f32 rows (y) of length F — exactly launch_swiglu.
 constexpr int kGemvMaxRows = 4;
 constexpr int kGemvRouteRows = 2;  // rows the engine sends to the GEMV (fused RMSNorm included)
+// Tensor-parallel peer buffers (k_allreduce.cu, k_dgemv.cu).
+constexpr int kMaxTp = 8;
+constexpr int kArCtas = 4;
+constexpr int kGemvArCtas = 160;  // CTAs of a decode GEMV with the all-reduce in its epilogue
+struct TpPeers {
+    float* recv[kMaxTp];       // rank r's receive slots [2][T][cap]
+    uint32_t* flags[kMaxTp];   // rank r's flags [2][T][kArCtas]
+    float* grecv[kMaxTp];      // the same for the GEMV epilogue's all-reduce: [2][T][cap]
+    uint32_t* gflags[kMaxTp];  // [2][T][kGemvArCtas]
+};
+// All-reduce folded into the epilogue of the single-row decode GEMV (k_dgemv.cu): every CTA,
+// once its rows of y are final, stores them into slot [parity][rank] of every rank (NVLink
+// stores), raises its flag there (system-scope release), waits (bounded) for the same CTA of
+// every rank and sums its rows over the ranks in rank order, so every rank holds the same bits.
+// The slots, flags and per-CTA epochs are its own (not the standalone kernel's).  T == 0: none.
+struct GemvAllReduce {
+    TpPeers peers;
+    int rank = 0, T = 0;
+    uint32_t* epochs = nullptr;  // kGemvArCtas per-CTA counters of this rank
+    int64_t cap = 0;             // floats per slot
+    int* err = nullptr;          // set when a wait for a peer ran out
+};
+
 // The weights a GEMV launch streams, described for the launch before it (L2 prefetch)
 struct PfNext {
     const void* qs = nullptr;  // split-row rows; null: nothing to prefetch
@@ -125,6 +148,8 @@ struct GemvArgs {
     // L2 prefetch (launch_dgemv only): the weights of the next GEMV launch; each CTA requests,
     // at its start, the rows that the same CTA index of that launch streams first
     PfNext pf;
+    // tensor parallelism: y summed over the ranks in the epilogue (launch_dgemv, one row)
+    GemvAllReduce ar;
 };
 void launch_gemv_fused(const GemvArgs& a, cudaStream_t st);
 // whether the GEMV's shared-memory stage fits: gemv_fits for one configuration (staged = f32
@@ -161,12 +186,6 @@ int gemm_tc_error();
 // peer-mapped buffers of `cap` floats per slot (n <= cap); identical bits on every rank.
 // `epochs` holds kArCtas per-rank counters (zero at set-up), `err` is set non-zero when a bounded
 // wait for a peer ran out.  Every rank must make the same sequence of calls.
-constexpr int kMaxTp = 8;
-constexpr int kArCtas = 4;
-struct TpPeers {
-    float* recv[kMaxTp];      // rank r's receive slots [2][T][cap]
-    uint32_t* flags[kMaxTp];  // rank r's flags [2][T][kArCtas]
-};
 void launch_tp_allreduce(float* y, int64_t n, const TpPeers& peers, int rank, int T,
                          uint32_t* epochs, int64_t cap, int* err, cudaStream_t st);
 

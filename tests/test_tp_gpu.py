@@ -4,7 +4,8 @@ model reproduces the reference's logits on the committed fixtures with the singl
 top-2 gap exceeds 1% of the logit range; both ranks return identical complete logits.  Prefill,
 KV-cache decode (teacher-forced with the reference's tokens) and the vocabulary all-gather are
 covered; the ranks exchange only through the engine's own NCCL communicator and its one-shot
-peer-memory all-reduce (decode-sized partial sums)."""
+peer-memory all-reduce (decode-sized partial sums), which single decode rows run inside the
+GEMV epilogue."""
 
 from __future__ import annotations
 
@@ -34,8 +35,11 @@ def cos(a, b):
     return float(a @ b / np.linalg.norm(a) / np.linalg.norm(b))
 
 
-def _rank(rank, world, fixture, idq, outq):
+def _rank(rank, world, fixture, idq, outq, env=None):
     try:
+        import os
+
+        os.environ.update(env or {})
         from ggmlc_b200 import _runtime as R
 
         if rank == 0:
@@ -82,13 +86,12 @@ def argmax_agrees(out, ref, rel_gap=0.01):
     return bool(np.all((np.argmax(out, 1) == np.argmax(ref, 1))[clear]))
 
 
-@pytest.mark.parametrize("fixture", ["tiny_llama_q8_0", "tiny_llama_q4_0"])
-def test_two_way_tensor_parallel_matches_reference(fixture):
+def _run_two(fixture, env=None):
     import multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     idq, outq = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, 2, fixture, idq, outq)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, fixture, idq, outq, env)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
@@ -103,6 +106,12 @@ def test_two_way_tensor_parallel_matches_reference(fixture):
                 p.kill()
     for rank in (0, 1):
         assert res[rank][4] is None, f"rank {rank}: {res[rank][4]}"
+    return res
+
+
+@pytest.mark.parametrize("fixture", ["tiny_llama_q8_0", "tiny_llama_q4_0"])
+def test_two_way_tensor_parallel_matches_reference(fixture):
+    res = _run_two(fixture)
     gold = np.load(GOLDEN / f"{fixture}.npz")
     _, full, pre, dec, _ = res[0]
     for k in (1, 2, 3):  # identical complete outputs on both ranks
@@ -114,3 +123,13 @@ def test_two_way_tensor_parallel_matches_reference(fixture):
     for i, ref in enumerate(gold["decode_logits"]):
         assert cos(dec[i], ref) >= COS_MIN, f"decode step {i}"
     assert argmax_agrees(dec, np.stack(gold["decode_logits"]))
+
+
+def test_epilogue_allreduce_bit_identical_to_separate_launch():
+    """Decode rows of the K-split projections summed over the ranks inside the GEMV's epilogue
+    (each CTA stores its rows into every rank's slot, raises its flag there and sums the ranks'
+    rows in rank order) give the same bits as the separate one-shot all-reduce launch."""
+    fused = _run_two("tiny_llama_q8_0")
+    separate = _run_two("tiny_llama_q8_0", {"GGMLC_B200_GEMV_AR": "0"})
+    for k in (1, 2, 3):
+        assert np.array_equal(fused[0][k], separate[0][k])
