@@ -640,6 +640,18 @@ int gb_rms_norm(const float* x, int64_t M, int64_t D, float eps, const float* ga
         gb::launch_rms_norm(x, D, M, D, eps, gamma, y, D, yq, yd, (cudaStream_t)stream);
     });
 }
+int gb_layer_norm(const float* x, int64_t M, int64_t D, float eps, const float* gamma,
+                  const float* beta, float* y, int8_t* yq, float* yd, void* stream) {
+    return guard([&] {
+        gb::launch_layer_norm(x, D, M, D, eps, gamma, beta, y, D, yq, yd, (cudaStream_t)stream);
+    });
+}
+int gb_bias_gelu(const float* x, const float* bias, int64_t M, int64_t F, float* y, int8_t* yq,
+                 float* yd, void* stream) {
+    return guard([&] {
+        gb::launch_bias_gelu(x, F, bias, M, F, y, F, yq, yd, (cudaStream_t)stream);
+    });
+}
 int gb_swiglu(const float* x, int64_t M, int64_t F, float* y, int8_t* yq, float* yd,
               void* stream) {
     return guard([&] {

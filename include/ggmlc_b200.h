@@ -319,6 +319,16 @@ int gb_get_rows(int type, const void* wq, int64_t N, int64_t K,
 /* RMS_NORM (+gamma), optional fused Q8_0 output — rms_norm_f32 (norm.cu:77-156) */
 int gb_rms_norm(const float* x, int64_t M, int64_t D, float eps, const float* gamma, float* y,
                 int8_t* yq, float* yd, void* stream);
+/* NORM (LayerNorm, GPT-2 blocks), optional gamma / beta and fused Q8_0 output — norm_f32
+ * (ggml-cuda/norm.cu:5, norm_f32_cuda :280); arithmetic of the CPU path
+ * ggml_compute_forward_norm_f32 (ggml-cpu/ops.cpp:3762) */
+int gb_layer_norm(const float* x, int64_t M, int64_t D, float eps, const float* gamma,
+                  const float* beta, float* y, int8_t* yq, float* yd, void* stream);
+/* bias + tanh-GELU of the GPT-2 MLP, optional fused Q8_0 output — ggmlc's CPU custom op
+ * ggmlc_compute_forward_bias_gelu (runtime/src/stdlib_kernels.cpp:29, fast_gelu_f32 :9) and
+ * the ADD + GELU pair it stands for on CUDA (ggml-cuda/unary.cu:20 op_gelu) */
+int gb_bias_gelu(const float* x, const float* bias, int64_t M, int64_t F, float* y, int8_t* yq,
+                 float* yd, void* stream);
 /* SWIGLU over [gate(F) ; up(F)] rows, optional fused Q8_0 output — unary.cu:263-337 */
 int gb_swiglu(const float* x, int64_t M, int64_t F, float* y, int8_t* yq, float* yd,
               void* stream);

@@ -39,6 +39,8 @@ def lib():
     L.gb_get_rows.argtypes = [I, P, I64, I64, P, I64, P, P]
     L.gb_rms_norm.argtypes = [P, I64, I64, F, P, P, P, P, P]
     L.gb_swiglu.argtypes = [P, I64, I64, P, P, P, P]
+    L.gb_layer_norm.argtypes = [P, I64, I64, F, P, P, P, P, P, P]
+    L.gb_bias_gelu.argtypes = [P, P, I64, I64, P, P, P, P]
     L.gb_rope_table_fill.argtypes = [P, I64, I, F]
     L.gb_rope_table_fill.restype = F
     L.gb_rope_neox.argtypes = [P, I64, I64, I64, P, I, F, P, I64, P, P]

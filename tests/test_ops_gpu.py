@@ -349,6 +349,72 @@ def test_rms_norm_bit_exact(G, D):
         assert np.array_equal(yq.cpu().numpy(), refq[:, :, 2:].reshape(M, D).view(np.int8))
 
 
+def _q8_agree(yq, ref_f32):
+    """Q8_0 quants of the engine against the oracle's quantization of its f32 reference: the
+    fraction of equal quants, and the largest difference"""
+    M, D = ref_f32.shape
+    refq = O.quantize_q8_0(ref_f32).reshape(M, D // 32, 34)[:, :, 2:].reshape(M, D).view(np.int8)
+    d = np.abs(yq.astype(np.int32) - refq.astype(np.int32))
+    return float((d == 0).mean()), int(d.max())
+
+
+@pytest.mark.parametrize("D", [768, 4096])
+def test_layer_norm_matches_oracle(G, D):
+    """LayerNorm of the GPT-2 blocks (the CPU NORM op, ggml-cpu/ops.cpp:3762, restated in the
+    oracle and pinned through the GPT-2 fixture's model-level goldens) with and without gamma /
+    beta, f32 rows and the fused Q8_0 rows: fp32 rows within 2 ulp-sized relative error (the
+    mean and variance are summed in double in another order), quants equal but for rare
+    one-step flips at rounding ties (against the oracle and against the engine's own rows)."""
+    torch = G.torch_dev()
+    rng = np.random.default_rng(D + 1)
+    M = 5
+    x = (rng.standard_normal((M, D)) * 3 + 0.5).astype(np.float32)
+    gam = rng.standard_normal(D).astype(np.float32)
+    bet = rng.standard_normal(D).astype(np.float32)
+    for gamma, beta in ((None, None), (gam, bet)):
+        y = torch.empty((M, D), dtype=torch.float32, device="cuda")
+        yq = torch.empty((M, D), dtype=torch.int8, device="cuda")
+        yd = torch.empty((M, D // 32), dtype=torch.float32, device="cuda")
+        gd = None if gamma is None else G.dev(gamma)
+        bd = None if beta is None else G.dev(beta)
+        xd_ = G.dev(x)
+        G.check(G.lib().gb_layer_norm(G.ptr(xd_), M, D, 1e-5, G.ptr(gd), G.ptr(bd), G.ptr(y),
+                                      G.ptr(yq), G.ptr(yd), None))
+        ref = O.layer_norm(x, 1e-5, gamma, beta)
+        out = y.cpu().numpy()
+        np.testing.assert_allclose(out, ref, rtol=2.5e-7 * 2, atol=1e-6)
+        same, worst = _q8_agree(yq.cpu().numpy(), out)
+        assert same >= 0.999 and worst <= 1, ("fused Q8_0 against its own f32 rows", same, worst)
+        same, worst = _q8_agree(yq.cpu().numpy(), ref)
+        assert same >= 0.999 and worst <= 1, (same, worst)
+
+
+@pytest.mark.parametrize("F", [128, 3072])
+def test_bias_gelu_matches_oracle(G, F):
+    """bias + tanh-GELU of the GPT-2 MLP (ggmlc's CPU custom op, stdlib_kernels.cpp:29, restated
+    in the oracle and pinned through the GPT-2 fixture's goldens): f32 rows within 1e-6
+    relative / 5e-7 absolute error, the fused Q8_0 rows those rows' quantization but for rare
+    one-step flips."""
+    torch = G.torch_dev()
+    rng = np.random.default_rng(F + 3)
+    M = 4
+    x = (rng.standard_normal((M, F)) * 3).astype(np.float32)
+    b = rng.standard_normal(F).astype(np.float32)
+    y = torch.empty((M, F), dtype=torch.float32, device="cuda")
+    yq = torch.empty((M, F), dtype=torch.int8, device="cuda")
+    yd = torch.empty((M, F // 32), dtype=torch.float32, device="cuda")
+    xd_, bd_ = G.dev(x), G.dev(b)  # held: a freed temporary's memory could be reused
+    G.check(G.lib().gb_bias_gelu(G.ptr(xd_), G.ptr(bd_), M, F, G.ptr(y), G.ptr(yq), G.ptr(yd),
+                                 None))
+    ref = O.bias_gelu(x, b)
+    out = y.cpu().numpy()
+    # the CPU's libm expf is off by one ulp in rare cases and 1 + tanh cancels near the
+    # negative tail, so a few near-zero outputs differ by about 1e-7 absolute
+    np.testing.assert_allclose(out, ref, rtol=1e-6, atol=5e-7)
+    same, worst = _q8_agree(yq.cpu().numpy(), out)
+    assert same >= 0.999 and worst <= 1, ("fused Q8_0 against its own f32 rows", same, worst)
+
+
 @pytest.mark.parametrize("F", [96, 1536, 14336])
 def test_swiglu_bit_exact(G, F):
     torch = G.torch_dev()
