@@ -250,7 +250,7 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(AttnDecArgs a) {
 // written to the cache by the CTA that holds it and taken from shared memory, never re-read.
 constexpr int kTcPos = 16;    // positions per block
 constexpr int kTcDepth = 2;   // ring slots per warp
-constexpr int kMaxCluster = 8;
+constexpr int kMaxCluster = 16;  // 8 portable; 16 with the non-portable cluster attribute
 
 template <int HD, int NW>
 struct TcAttnSmem {
@@ -710,13 +710,42 @@ void launch_cluster_pdl(void (*kern)(P...), dim3 grid, dim3 block, size_t smem, 
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 2;
+    if (cx > 8)
+        GB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
     GB_CUDA(cudaLaunchKernelEx(&cfg, kern, a));
 }
 
 template <int HD, int NW>
 void launch_cluster(const AttnDecArgs& a, int C, cudaStream_t st) {
     constexpr size_t tsm = TcAttnSmem<HD, NW>::kBytes;
+    auto kern = k_attn_decode_tc<HD, NW, true>;
     set_max_smem<k_attn_decode_tc<HD, NW, true>>(tsm);
+    if (C > 8) {
+        // clusters beyond the portable 8 CTAs: only where this device can hold one (asked once
+        // per device), else 8
+        static int fits[64] = {};  // 0 unknown, 1 yes, -1 no
+        int dev = 0;
+        GB_CUDA(cudaGetDevice(&dev));
+        if (dev >= 0 && dev < 64 && fits[dev] == 0) {
+            GB_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3((unsigned)C, (unsigned)a.Hkv, 1);
+            cfg.blockDim = dim3(NW * 32);
+            cfg.dynamicSmemBytes = tsm;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = (unsigned)C;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            int n = 0;
+            const cudaError_t e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+            if (e != cudaSuccess) cudaGetLastError();
+            fits[dev] = e == cudaSuccess && n >= 1 ? 1 : -1;
+        }
+        if (dev < 0 || dev >= 64 || fits[dev] < 0) C = 8;
+    }
     launch_cluster_pdl(k_attn_decode_tc<HD, NW, true>,
                        dim3((unsigned)C, (unsigned)a.Hkv, (unsigned)a.rows), NW * 32, tsm,
                        (unsigned)C, st, a);
@@ -772,7 +801,15 @@ int attn_decode_cluster(int64_t Hkv, int64_t hd, int64_t ctx, int rows) {
     // about one CTA per SM over the launch, at most kMaxCluster per (row, KV head)
     const int64_t units = Hkv * std::max(rows, 1);
     int64_t C = (148 + units - 1) / units;
-    C = std::max<int64_t>(1, std::min<int64_t>(C, kMaxCluster));
+    // CTAs per cluster at most: 16 (GGMLC_B200_ATTN_CLUSTER; 16 measured 1 % faster than the
+    // portable 8 at batch 1 on the 8B shape; launch_cluster falls back to 8 where the device
+    // cannot hold a 16-CTA cluster)
+    static const int64_t cmax = [] {
+        const char* e = getenv("GGMLC_B200_ATTN_CLUSTER");
+        const int64_t v = e ? atoll(e) : 16;
+        return std::max<int64_t>(1, std::min<int64_t>(v, kMaxCluster));
+    }();
+    C = std::max<int64_t>(1, std::min<int64_t>(C, cmax));
     // each of a CTA's 4 warps walks at most 4 blocks of 16 positions (a CTA stays under 80 KB of
     // shared memory, so the GEMVs before and after it share the SM); longer caches take the
     // wider split with the merge launch
