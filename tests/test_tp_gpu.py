@@ -133,3 +133,86 @@ def test_epilogue_allreduce_bit_identical_to_separate_launch():
     separate = _run_two("tiny_llama_q8_0", {"GGMLC_B200_GEMV_AR": "0"})
     for k in (1, 2, 3):
         assert np.array_equal(fused[0][k], separate[0][k])
+
+
+def _late_rank(rank, world, idq, outq, delay_s):
+    """Rank 1 enters the first decode step `delay_s` late (a host-side delay between steps, none
+    of its work in flight); rank 0's all-reduce wait for it runs out and is reported."""
+    try:
+        import os
+        import time
+
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        from ggmlc_b200 import _runtime as R
+
+        if rank == 0:
+            nid = R.nccl_unique_id()
+            for _ in range(world - 1):
+                idq.put(nid)
+        else:
+            nid = idq.get(timeout=120)
+        fixture = "tiny_llama_q8_0"
+        g = R.ModelLoader.load_from_file(str(GOLDEN / f"{fixture}.gguf"))
+        ex = R.ModelExecutor(g, f"cuda:{rank}", tp_rank=rank, tp_size=world, nccl_id=nid)
+        gold = np.load(GOLDEN / f"{fixture}.npz")
+        sym = g.symbol_table
+        in_id = g.inputs[0]
+        prompt = gold["prompt"]
+        ex.init_kv_cache(1024)
+        ex.prepare({"s": len(prompt), "pos": 0, **{s: len(prompt) for s in sym}})
+        ex.set_input_by_id(in_id, prompt)
+        ex.run()
+        ex.synchronize()  # the prefill's collectives bring both ranks to the same point
+
+        def step(pos, tok):
+            ex.prepare({"s": 1, "pos": pos, **{s: 1 for s in sym}})
+            ex.set_input_by_id(in_id, np.array([tok], np.int32))
+            ex.run()
+            ex.synchronize()
+
+        raised = None
+        if rank == 1:
+            time.sleep(delay_s)
+        t0 = time.time()
+        try:
+            step(len(prompt), int(gold["greedy_tokens"][0]))
+        except RuntimeError as e:
+            raised = str(e)
+        first_s = time.time() - t0
+        # the counters stayed in step: the next step completes on both ranks without an error
+        step(len(prompt) + 1, int(gold["greedy_tokens"][1]))
+        outq.put((rank, raised, first_s, ex.tp_allreduce_error(), None))
+    except Exception as e:  # noqa: BLE001 - reported to the parent
+        outq.put((rank, None, 0.0, -1, repr(e)))
+
+
+def test_late_peer_all_reduce_wait_runs_out_and_is_reported():
+    """Failure detection without a GPU fault: every peer wait of the decode all-reduce is
+    bounded (about 1 s of SM clock cycles).  With rank 1 entering a decode step 2.5 s late,
+    rank 0's wait runs out, its kernel records the error word and returns, and the next host
+    synchronisation raises.  Rank 1 may find some of rank 0's flags already advanced to a later
+    call and report the same error once.  Nothing hangs, and the following step completes on
+    both ranks without an error: the per-CTA epochs stayed in step."""
+    import multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    idq, outq = ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_late_rank, args=(r, 2, idq, outq, 2.5)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in procs:
+            r = outq.get(timeout=300)
+            res[r[0]] = r
+    finally:
+        for p in procs:
+            p.join(timeout=30)
+            if p.is_alive():
+                p.kill()
+    for rank in (0, 1):
+        assert res[rank][4] is None, f"rank {rank}: {res[rank][4]}"
+    assert res[0][1] is not None and "wait limit" in res[0][1], res[0][1]
+    assert res[0][2] >= 0.9, f"rank 0 returned after {res[0][2]:.2f} s"
+    assert res[1][1] is None or "wait limit" in res[1][1], res[1][1]
+    assert res[0][3] == 0 and res[1][3] == 0  # reported once, then clear
