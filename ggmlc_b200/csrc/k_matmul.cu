@@ -9,6 +9,7 @@
 // sums are exact; the fp32 summation order differs from the CPU's lane order.
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -89,7 +90,7 @@ template <int WT, int SWI, int OCC>
 __global__ void __launch_bounds__(kGThreads, OCC)
     k_gemm_q(const uint8_t* __restrict__ qs, int N, int K, const int8_t* __restrict__ xq,
              const float* __restrict__ xd, int M, float* __restrict__ y, int64_t y_stride,
-             MatmulEpilogue ep, SwiOut so) {
+             MatmulEpilogue ep, SwiOut so, float* __restrict__ part) {
     extern __shared__ __align__(128) uint8_t gsm[];
     using S = GStage<WT>;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -155,18 +156,21 @@ __global__ void __launch_bounds__(kGThreads, OCC)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j][0] = acc[i][j][1] = make_float2(0.0f, 0.0f);
 
+    // split K (gridDim.z > 1): this CTA's stages [tb, te), its partial sums to part
+    const int tb = (int)((int64_t)ns * blockIdx.z / gridDim.z);
+    const int te = (int)((int64_t)ns * (blockIdx.z + 1) / gridDim.z);
 #pragma unroll
     for (int s = 0; s < kGStages - 1; ++s) {
-        if (s < ns) load(s, s);
+        if (tb + s < te) load(tb + s, s);
         asm volatile("cp.async.commit_group;" ::: "memory");
     }
     const float wsc = WT == T_Q4_0 ? 0.0625f : 1.0f;  // Q4_0 fragments hold 16 * (q - 8)
-    for (int t = 0; t < ns; ++t) {
+    for (int t = tb; t < te; ++t) {
         asm volatile("cp.async.wait_group %0;" ::"n"(kGStages - 2) : "memory");
         __syncthreads();
-        if (t + kGStages - 1 < ns) load(t + kGStages - 1, (t + kGStages - 1) % kGStages);
+        if (t + kGStages - 1 < te) load(t + kGStages - 1, (t - tb + kGStages - 1) % kGStages);
         asm volatile("cp.async.commit_group;" ::: "memory");
-        const uint8_t* st = gsm + (t % kGStages) * S::kBytes;
+        const uint8_t* st = gsm + ((t - tb) % kGStages) * S::kBytes;
         const uint8_t* sA = st;
         const uint8_t* sB = sA + S::kA;
         const __half* sW = (const __half*)(sB + S::kB);
@@ -267,6 +271,21 @@ __global__ void __launch_bounds__(kGThreads, OCC)
                 if (lane == 0) so.yd[gm * (so.F / 32) + col / 32] = d16;
             }
         }
+    } else if (gridDim.z > 1) {  // split K: the partial sums, finished by k_splitk_sum
+        float* pz = part + (int64_t)blockIdx.z * M * N;
+#pragma unroll
+        for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const int m = m0 + wm * 64 + mt * 16 + g + ((e >> 1) << 3);
+                    const int n = n0 + wn * 32 + nt * 8 + 2 * tg + (e & 1);
+                    if (m < M && n < N) {
+                        const float2 p = acc[mt][nt][e >> 1];
+                        pz[(int64_t)m * N + n] = (e & 1) ? p.y : p.x;
+                    }
+                }
     } else {
 #pragma unroll
         for (int mt = 0; mt < 4; ++mt)
@@ -285,6 +304,20 @@ __global__ void __launch_bounds__(kGThreads, OCC)
                     }
                 }
     }
+}
+
+// The split-K partial sums of a plain GEMM added in split order, then bias and residual as in
+// k_gemm_q's own epilogue.  One thread per output element.
+__global__ void k_splitk_sum(const float* __restrict__ part, int S, int M, int N, float* y,
+                             int64_t y_stride, MatmulEpilogue ep) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)M * N) return;
+    const int m = (int)(i / N), n = (int)(i % N);
+    float r = part[i];
+    for (int z = 1; z < S; ++z) r = __fadd_rn(r, part[(int64_t)z * M * N + i]);
+    if (ep.bias) r = __fadd_rn(r, ep.bias[n]);
+    if (ep.residual) r = __fadd_rn(ep.residual[(int64_t)m * ep.res_stride + n], r);
+    y[(int64_t)m * y_stride + n] = r;
 }
 
 // float-weight fallback (F32/F16 W): one warp per (row n, activation m)
@@ -311,7 +344,7 @@ __global__ void k_matmul_f(QWeight w, const float* __restrict__ x, int64_t x_str
 template <int WT, int SWI, int OCC>
 void run_gemm(dim3 grid, const uint8_t* qs, int N, int K, const int8_t* xq, const float* xd,
               int M, float* y, int64_t y_stride, const MatmulEpilogue& ep, const SwiOut& so,
-              cudaStream_t st) {
+              cudaStream_t st, float* part = nullptr) {
     int dev = 0;
     GB_CUDA(cudaGetDevice(&dev));
     {
@@ -326,7 +359,16 @@ void run_gemm(dim3 grid, const uint8_t* qs, int N, int K, const int8_t* xq, cons
         }
     }
     k_gemm_q<WT, SWI, OCC><<<grid, kGThreads, kGStages * GStage<WT>::kBytes, st>>>(
-        qs, N, K, xq, xd, M, y, y_stride, ep, so);
+        qs, N, K, xq, xd, M, y, y_stride, ep, so, part);
+}
+
+// split K for plain GEMMs with tiles for at most half the SMs (GGMLC_B200_SPLITK=0: off)
+bool splitk_enabled() {
+    static const bool v = [] {
+        const char* e = getenv("GGMLC_B200_SPLITK");
+        return !(e && std::strcmp(e, "0") == 0);
+    }();
+    return v;
 }
 
 void launch_gemm_block(const QWeight& w, const int8_t* xq, const float* xd, int64_t M, float* y,
@@ -341,19 +383,45 @@ void launch_gemm_block(const QWeight& w, const int8_t* xq, const float* xd, int6
     GB_CUDA(cudaGetDevice(&dev));
     const uint8_t* qs = (const uint8_t*)w.qs;
     const int N = (int)w.N, K = (int)w.K, m = (int)M;
+    const int sms = sm_count(dev);
+    // A plain GEMM with tiles for at most half the SMs (few weight rows and few activation rows,
+    // as in the operator sweep's M = 64 cells) splits K over gridDim.z: at most one wave (two
+    // CTAs per SM for Q4_0, whose stages fit two, one for Q8_0) and at least 8 stages a split;
+    // the partial sums are added in split order by k_splitk_sum.  Measured: Q4_0 4096 x 4096 at
+    // 64 rows 76 -> 38 us, 4096 x 14336 246 -> 76 us; with 112-128 tiles (the 512-row prefill's
+    // O and down projections) splitting measured slower, so those run whole.
+    const int64_t ntile = tiles * grid.y;
+    const int ns = (int)((K / QK + 3) / 4);
+    const int64_t slots = (w.type == T_Q4_0 ? 2 : 1) * (int64_t)sms;
+    int splits = 1;
+    if (!swi && 2 * ntile <= sms && splitk_enabled())
+        splits = (int)std::max<int64_t>(
+            1, std::min<int64_t>(std::min<int64_t>(slots / ntile, ns / 8), 16));
+    float* part = nullptr;
+    if (splits > 1) {
+        grid.z = (unsigned)splits;
+        GB_CUDA(cudaMallocAsync((void**)&part, (size_t)splits * M * w.N * sizeof(float), st));
+    }
     // Q4_0 stages fit two CTAs per SM: worth it once there are tiles for two per SM
-    const bool two = w.type == T_Q4_0 && tiles * grid.y >= 2 * (int64_t)sm_count(dev);
+    const bool two = w.type == T_Q4_0 && (splits > 1 || ntile >= 2 * (int64_t)sms);
     if (w.type == T_Q8_0) {
         if (swi) run_gemm<T_Q8_0, 1, 1>(grid, qs, N, K, xq, xd, m, y, y_stride, ep, so, st);
-        else run_gemm<T_Q8_0, 0, 1>(grid, qs, N, K, xq, xd, m, y, y_stride, ep, so, st);
+        else run_gemm<T_Q8_0, 0, 1>(grid, qs, N, K, xq, xd, m, y, y_stride, ep, so, st, part);
     } else if (two) {
         if (swi) run_gemm<T_Q4_0, 1, 2>(grid, qs, N, K, xq, xd, m, y, y_stride, ep, so, st);
-        else run_gemm<T_Q4_0, 0, 2>(grid, qs, N, K, xq, xd, m, y, y_stride, ep, so, st);
+        else run_gemm<T_Q4_0, 0, 2>(grid, qs, N, K, xq, xd, m, y, y_stride, ep, so, st, part);
     } else {
         if (swi) run_gemm<T_Q4_0, 1, 1>(grid, qs, N, K, xq, xd, m, y, y_stride, ep, so, st);
-        else run_gemm<T_Q4_0, 0, 1>(grid, qs, N, K, xq, xd, m, y, y_stride, ep, so, st);
+        else run_gemm<T_Q4_0, 0, 1>(grid, qs, N, K, xq, xd, m, y, y_stride, ep, so, st, part);
     }
     GB_CUDA(cudaGetLastError());
+    if (splits > 1) {
+        const int64_t n = (int64_t)M * w.N;
+        k_splitk_sum<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(part, splits, m, N, y, y_stride,
+                                                                  ep);
+        GB_CUDA(cudaGetLastError());
+        GB_CUDA(cudaFreeAsync(part, st));
+    }
 }
 
 }  // namespace
