@@ -99,6 +99,8 @@ struct TcArgs {
     int64_t res_stride;
     int8_t* yq;         // SwiGLU Q8_0 output [M][F], yd [M][F / 32]
     float* yd;
+    float* part;        // split K (gridDim.z > 1): partial sums [z][M][N], finished by
+                        // launch_splitk_sum
 };
 
 __device__ int gemm_tc_error_word;
@@ -220,7 +222,9 @@ __device__ __forceinline__ void epi_sync() {
     asm volatile("bar.sync 1, %0;" ::"n"(kEpiWarps * 32) : "memory");
 }
 
-template <int WT>
+// SPLIT: the CTA takes stages [tb, te) of K and writes partial sums (gridDim.z splits); the
+// whole-K build is compiled separately so its code is the same as without split K.
+template <int WT, bool SPLIT>
 __global__ void __launch_bounds__(kTThreads, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmw, const __grid_constant__ CUtensorMap tmws,
               const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tms,
@@ -241,6 +245,9 @@ __global__ void __launch_bounds__(kTThreads, 1)
     const int n0 = blockIdx.x * (swi ? kTM / 2 : kTM), m0 = blockIdx.y * kTN;
     const int nb = a.K / QK;
     const int ns = nb / kTB;  // stages (K % 128 == 0)
+    // split K: this CTA's stages [tb, te); stage slots and barrier phases count from tb
+    const int tb = SPLIT ? (int)((int64_t)ns * blockIdx.z / gridDim.z) : 0;
+    const int te = SPLIT ? (int)((int64_t)ns * (blockIdx.z + 1) / gridDim.z) : ns;
     const int qsz = WT == T_Q8_0 ? 32 : 16;
     auto stage = [&](int s) { return tsm + s * S::kBytes; };
 
@@ -274,9 +281,9 @@ __global__ void __launch_bounds__(kTThreads, 1)
     if (warp == 0) {
         // ---------------------------------------------------------------- TMA producer
         if (lane == 0) {
-            for (int t = 0; t < ns && !*abort; ++t) {
-                const int s = t % kTS;
-                if (t >= kTS && !mbar_wait(&bar_empty[s], ((t / kTS) - 1) & 1, abort)) break;
+            for (int t = tb; t < te && !*abort; ++t) {
+                const int i = t - tb, s = i % kTS;
+                if (i >= kTS && !mbar_wait(&bar_empty[s], ((i / kTS) - 1) & 1, abort)) break;
                 uint8_t* st = stage(s);
                 uint8_t* sB = st + S::kA;
                 uint8_t* sRaw = sB + S::kB;
@@ -305,9 +312,9 @@ __global__ void __launch_bounds__(kTThreads, 1)
     } else if (warp >= kHelpWarp0 && warp < kHelpWarp0 + kHelpWarps) {
         // ---------------------------------------------------------------- helpers
         const int p = tid - kHelpWarp0 * 32;  // 0..63
-        for (int t = 0; t < ns && !*abort; ++t) {
-            const int s = t % kTS;
-            if (!__all_sync(0xffffffffu, mbar_wait(&bar_full[s], (t / kTS) & 1, abort))) break;
+        for (int t = tb; t < te && !*abort; ++t) {
+            const int i = t - tb, s = i % kTS;
+            if (!__all_sync(0xffffffffu, mbar_wait(&bar_full[s], (i / kTS) & 1, abort))) break;
             uint8_t* st = stage(s);
             uint8_t* sA = st;
             uint8_t* sRaw = st + S::kA + S::kB;
@@ -375,13 +382,13 @@ __global__ void __launch_bounds__(kTThreads, 1)
         // ---------------------------------------------------------------- MMA issuer
         if (lane == 0) {
             bool ok = true;
-            for (int t = 0; t < ns && ok; ++t) {
-                const int s = t % kTS;
-                if (!mbar_wait(&bar_ready[s], (t / kTS) & 1, abort)) break;
+            for (int t = tb; t < te && ok; ++t) {
+                const int i = t - tb, s = i % kTS;
+                if (!mbar_wait(&bar_ready[s], (i / kTS) & 1, abort)) break;
                 tc_fence_after();
                 const uint8_t* st = stage(s);
                 for (int lb = 0; lb < kTB; ++lb) {
-                    if (!mbar_wait(&bar_tempty[lb], t & 1, abort)) {
+                    if (!mbar_wait(&bar_tempty[lb], i & 1, abort)) {
                         ok = false;
                         break;
                     }
@@ -447,9 +454,9 @@ __global__ void __launch_bounds__(kTThreads, 1)
         };
         // waits are made warp-uniform by a vote: tensor-memory loads and stores need the whole
         // warp converged
-        for (int t = 0; t < ns && !*abort; ++t) {
-            const int s = t % kTS;
-            if (!__all_sync(0xffffffffu, mbar_wait(&bar_ready[s], (t / kTS) & 1, abort))) break;
+        for (int t = tb; t < te && !*abort; ++t) {
+            const int i = t - tb, s = i % kTS;
+            if (!__all_sync(0xffffffffu, mbar_wait(&bar_ready[s], (i / kTS) & 1, abort))) break;
             const uint8_t* st = stage(s);
             const float* sXt = (const float*)(st + S::kA + S::kB + S::kRaw + S::kWs + S::kXr);
             const float2* sWf = (const float2*)(sXt + S::kXt / 4);
@@ -459,7 +466,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
                 float2 dw[4];
 #pragma unroll
                 for (int k = 0; k < 4; ++k) dw[k] = sWf[lb * kTM + q * 32 + 8 * k + g];
-                if (!__all_sync(0xffffffffu, mbar_wait(&bar_tfull[lb], t & 1, abort))) {
+                if (!__all_sync(0xffffffffu, mbar_wait(&bar_tfull[lb], i & 1, abort))) {
                     ok = false;
                     break;
                 }
@@ -505,7 +512,10 @@ __global__ void __launch_bounds__(kTThreads, 1)
 #pragma unroll
                         for (int e = 0; e < 2; ++e) {
                             const int m = m0 + ch * kCols + 8 * j + 2 * cp + e;
-                            if (m < a.M) {
+                            if (SPLIT && m < a.M) {  // split K: the partial sum
+                                a.part[((int64_t)blockIdx.z * a.M + m) * a.N + n] =
+                                    e ? acc[k][j].y : acc[k][j].x;
+                            } else if (m < a.M) {
                                 float o = e ? acc[k][j].y : acc[k][j].x;
                                 if (a.bias) o = __fadd_rn(o, bn);
                                 if (a.residual)
@@ -640,8 +650,10 @@ void run_tc(const QWeight& w, const int8_t* xq, const float* xd, const TcArgs& a
         std::lock_guard<std::mutex> lock(mu);
         GB_CHECK(dev >= 0 && dev < 64, "gemm_tc: device ordinal out of range");
         if (!configured[dev]) {
-            GB_CUDA(cudaFuncSetAttribute(k_gemm_tc<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         tc_smem<WT>()));
+            GB_CUDA(cudaFuncSetAttribute(k_gemm_tc<WT, false>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem<WT>()));
+            GB_CUDA(cudaFuncSetAttribute(k_gemm_tc<WT, true>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, tc_smem<WT>()));
             configured[dev] = true;
         }
     }
@@ -658,8 +670,29 @@ void run_tc(const QWeight& w, const int8_t* xq, const float* xd, const TcArgs& a
                                       (uint64_t)a.M, (uint64_t)(w.K / QK) * 4, kTB, kTN, false);
     const int64_t ntiles = swi ? a.swi_F / (kTM / 2) : (w.N + kTM - 1) / kTM;
     dim3 grid((unsigned)ntiles, (unsigned)((a.M + kTN - 1) / kTN));
-    k_gemm_tc<WT><<<grid, kTThreads, tc_smem<WT>(), st>>>(mw, mws, mx, ms, a);
+    // a plain GEMM with tiles for at most half the SMs splits K (one CTA per SM, at least 8
+    // stages a split); the partial sums are added in split order by launch_splitk_sum
+    const int sms = sm_count(dev), ns = (int)(w.K / QK / kTB);
+    const int64_t ntile = (int64_t)grid.x * grid.y;
+    int splits = 1;
+    if (!swi && 2 * ntile <= sms && splitk_enabled())
+        splits = (int)std::max<int64_t>(1, std::min<int64_t>(std::min<int64_t>(sms / ntile, ns / 8), 16));
+    TcArgs b = a;
+    if (splits > 1) {
+        grid.z = (unsigned)splits;
+        GB_CUDA(cudaMallocAsync((void**)&b.part, (size_t)splits * a.M * a.N * sizeof(float), st));
+    }
+    if (splits > 1) k_gemm_tc<WT, true><<<grid, kTThreads, tc_smem<WT>(), st>>>(mw, mws, mx, ms, b);
+    else k_gemm_tc<WT, false><<<grid, kTThreads, tc_smem<WT>(), st>>>(mw, mws, mx, ms, b);
     GB_CUDA(cudaGetLastError());
+    if (splits > 1) {
+        MatmulEpilogue ep;
+        ep.bias = a.bias;
+        ep.residual = a.residual;
+        ep.res_stride = a.res_stride;
+        launch_splitk_sum(b.part, splits, a.M, a.N, a.y, a.y_stride, ep, st);
+        GB_CUDA(cudaFreeAsync(b.part, st));
+    }
 }
 
 void check_tc(const QWeight& w, const int8_t* xq, const float* xd) {

@@ -362,15 +362,6 @@ void run_gemm(dim3 grid, const uint8_t* qs, int N, int K, const int8_t* xq, cons
         qs, N, K, xq, xd, M, y, y_stride, ep, so, part);
 }
 
-// split K for plain GEMMs with tiles for at most half the SMs (GGMLC_B200_SPLITK=0: off)
-bool splitk_enabled() {
-    static const bool v = [] {
-        const char* e = getenv("GGMLC_B200_SPLITK");
-        return !(e && std::strcmp(e, "0") == 0);
-    }();
-    return v;
-}
-
 void launch_gemm_block(const QWeight& w, const int8_t* xq, const float* xd, int64_t M, float* y,
                        int64_t y_stride, const MatmulEpilogue& ep, const SwiOut& so,
                        cudaStream_t st) {
@@ -416,15 +407,28 @@ void launch_gemm_block(const QWeight& w, const int8_t* xq, const float* xd, int6
     }
     GB_CUDA(cudaGetLastError());
     if (splits > 1) {
-        const int64_t n = (int64_t)M * w.N;
-        k_splitk_sum<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(part, splits, m, N, y, y_stride,
-                                                                  ep);
-        GB_CUDA(cudaGetLastError());
+        launch_splitk_sum(part, splits, m, N, y, y_stride, ep, st);
         GB_CUDA(cudaFreeAsync(part, st));
     }
 }
 
 }  // namespace
+
+bool splitk_enabled() {
+    static const bool v = [] {
+        const char* e = getenv("GGMLC_B200_SPLITK");
+        return !(e && std::strcmp(e, "0") == 0);
+    }();
+    return v;
+}
+
+void launch_splitk_sum(const float* part, int splits, int M, int N, float* y, int64_t y_stride,
+                       const MatmulEpilogue& ep, cudaStream_t st) {
+    const int64_t n = (int64_t)M * N;
+    if (n == 0) return;
+    k_splitk_sum<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(part, splits, M, N, y, y_stride, ep);
+    GB_CUDA(cudaGetLastError());
+}
 
 // Prefill GEMM path (M > 16 rows), chosen by measurement on B200: Q8_0 weights go to the tcgen05
 // kernel (k_gemm_tc.cu, 10-12% faster than the mma.sync kernel at every prefill shape measured),

@@ -180,6 +180,12 @@ void launch_gemm_tc(const QWeight& w, const int8_t* xq, const float* xd, int64_t
 void launch_gemm_tc_swiglu(const GemvArgs& a, cudaStream_t st);
 // whether the tcgen05 GEMM takes this K (its TMA stages are 4 blocks: K % 128 == 0)
 bool gemm_tc_fits(int64_t K);
+// Split K of the prefill GEMMs (k_matmul.cu, k_gemm_tc.cu): plain GEMMs whose tiles fill at most
+// half the SMs cut K into gridDim.z ranges whose partial sums [z][M][N] (stream-ordered scratch)
+// launch_splitk_sum adds in split order before bias and residual.  GGMLC_B200_SPLITK=0: off.
+bool splitk_enabled();
+void launch_splitk_sum(const float* part, int splits, int M, int N, float* y, int64_t y_stride,
+                       const MatmulEpilogue& ep, cudaStream_t st);
 int gemm_tc_error();
 
 // Tensor-parallel one-shot all-reduce (k_allreduce.cu): y[0..n) summed over T ranks through
