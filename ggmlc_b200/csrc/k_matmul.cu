@@ -34,13 +34,14 @@ namespace {
 // the weight scale region stores them, so one 8-byte copy brings a row's four scales.
 constexpr int kBM = 128, kBN = 128, kGThreads = 256, kGStages = 4;
 
-template <int WT>
+// BM: activation rows per tile (128, or 64 for launches of at most 64 rows)
+template <int WT, int BM = kBM>
 struct GStage {
     static constexpr int kRowB = WT == T_Q8_0 ? 128 : 64;  // weight bytes per row and stage
-    static constexpr int kA = kBM * 128;                    // activations: 4 blocks x 32 B per row
+    static constexpr int kA = BM * 128;                     // activations: 4 blocks x 32 B per row
     static constexpr int kB = kBN * kRowB;
     static constexpr int kWs = kBN * 8;                     // 4 fp16 weight scales per row
-    static constexpr int kXs = kBM * 16;                    // 4 fp32 activation scales per row
+    static constexpr int kXs = BM * 16;                     // 4 fp32 activation scales per row
     static constexpr int kBytes = kA + kB + kWs + kXs;
 };
 
@@ -86,17 +87,19 @@ struct SwiOut {
 };
 
 // OCC = CTAs per SM the kernel is built for: 2 keeps the block loop rolled (128 registers).
-template <int WT, int SWI, int OCC>
+// BM = 64: the warps' tiles are 32 x 32 (two m16 rows of sub-tiles instead of four).
+template <int WT, int SWI, int OCC, int BM = kBM>
 __global__ void __launch_bounds__(kGThreads, OCC)
     k_gemm_q(const uint8_t* __restrict__ qs, int N, int K, const int8_t* __restrict__ xq,
              const float* __restrict__ xd, int M, float* __restrict__ y, int64_t y_stride,
              MatmulEpilogue ep, SwiOut so, float* __restrict__ part) {
     extern __shared__ __align__(128) uint8_t gsm[];
-    using S = GStage<WT>;
+    using S = GStage<WT, BM>;
+    constexpr int WR = BM / 2, MT = WR / 16;  // activation rows per warp, m16 sub-tiles
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, tg = lane & 3;
     const int wm = warp >> 2, wn = warp & 3;
-    const int m0 = blockIdx.y * kBM, n0 = blockIdx.x * kBN;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * kBN;
     const int p0 = blockIdx.x * (kBN / 2);
     // weight row of tile row r
     auto wrow = [&](int r) {
@@ -119,14 +122,14 @@ __global__ void __launch_bounds__(kGThreads, OCC)
         uint8_t* sW = sB + S::kB;
         float* sX = (float*)(sW + S::kWs);
         // activations: 128 rows x 8 chunks of 16 B (chunk c: local block c/2, half c%2)
-        for (int e = tid; e < kBM * 8; e += kGThreads) {
+        for (int e = tid; e < BM * 8; e += kGThreads) {
             const int r = e >> 3, c = e & 7;
             const int gb = gblk(t, c >> 1);
             const int m = min(m0 + r, M - 1);
             cp_zfill<16>(sA + r * 128 + ((c ^ (r & 7)) << 4),
                          xq + (int64_t)m * K + (int64_t)gb * 32 + (c & 1) * 16, gb < nb);
         }
-        for (int e = tid; e < kBM * 4; e += kGThreads) {
+        for (int e = tid; e < BM * 4; e += kGThreads) {
             const int r = e >> 2, lb = e & 3;
             const int gb = gblk(t, lb);
             const int m = min(m0 + r, M - 1);
@@ -150,9 +153,9 @@ __global__ void __launch_bounds__(kGThreads, OCC)
         }
     };
 
-    float2 acc[4][4][2];  // [m16][n8][row g / g+8] x (col 2tg, 2tg+1)
+    float2 acc[MT][4][2];  // [m16][n8][row g / g+8] x (col 2tg, 2tg+1)
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < MT; ++i)
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[i][j][0] = acc[i][j][1] = make_float2(0.0f, 0.0f);
 
@@ -177,11 +180,11 @@ __global__ void __launch_bounds__(kGThreads, OCC)
         const float* sX = (const float*)((const uint8_t*)sW + S::kWs);
 #pragma unroll(OCC == 2 ? 1 : 4)
         for (int lb = 0; lb < 4; ++lb) {
-            unsigned af[4][4];
+            unsigned af[MT][4];
 #pragma unroll
-            for (int mt = 0; mt < 4; ++mt) {
+            for (int mt = 0; mt < MT; ++mt) {
                 const int q = lane >> 3;
-                const int r = wm * 64 + mt * 16 + (lane & 7) + ((q & 1) << 3);
+                const int r = wm * WR + mt * 16 + (lane & 7) + ((q & 1) << 3);
                 const int c = lb * 2 + (q >> 1);
                 ldsm_x4(af[mt], sA + r * 128 + ((c ^ (r & 7)) << 4));
             }
@@ -209,11 +212,11 @@ __global__ void __launch_bounds__(kGThreads, OCC)
             }
             // scales of this block: sW/sX hold local blocks in the order [0, 2, 1, 3]
             const int si = ((lb & 1) << 1) | (lb >> 1);
-            float2 dxv[4][2], dwv[4];
+            float2 dxv[MT][2], dwv[4];
 #pragma unroll
-            for (int mt = 0; mt < 4; ++mt) {
-                const float a0 = sX[(wm * 64 + mt * 16 + g) * 4 + lb];
-                const float a1 = sX[(wm * 64 + mt * 16 + g + 8) * 4 + lb];
+            for (int mt = 0; mt < MT; ++mt) {
+                const float a0 = sX[(wm * WR + mt * 16 + g) * 4 + lb];
+                const float a1 = sX[(wm * WR + mt * 16 + g + 8) * 4 + lb];
                 dxv[mt][0] = make_float2(a0, a0);
                 dxv[mt][1] = make_float2(a1, a1);
             }
@@ -225,7 +228,7 @@ __global__ void __launch_bounds__(kGThreads, OCC)
             }
             const float2 bias2 = make_float2(12582912.0f, 12582912.0f);
 #pragma unroll
-            for (int mt = 0; mt < 4; ++mt)
+            for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
                 for (int nt = 0; nt < 4; ++nt) {
                     int d[4];
@@ -247,18 +250,18 @@ __global__ void __launch_bounds__(kGThreads, OCC)
         float* tile = (float*)gsm;
         __syncthreads();
 #pragma unroll
-        for (int mt = 0; mt < 4; ++mt)
+        for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
             for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const int m = wm * 64 + mt * 16 + g + ((e >> 1) << 3);
+                    const int m = wm * WR + mt * 16 + g + ((e >> 1) << 3);
                     const int n = wn * 32 + nt * 8 + 2 * tg + (e & 1);
                     const float2 pv = acc[mt][nt][e >> 1];
                     tile[m * kLd + n] = (e & 1) ? pv.y : pv.x;
                 }
         __syncthreads();
-        for (int task = warp; task < kBM * 2; task += kGThreads / 32) {
+        for (int task = warp; task < BM * 2; task += kGThreads / 32) {
             const int m = task >> 1, j = (task & 1) * 32 + lane;
             if (m0 + m >= M) continue;  // warp-uniform
             const float h = __fmul_rn(ref_v_silu(tile[m * kLd + j]), tile[m * kLd + kBN / 2 + j]);
@@ -274,12 +277,12 @@ __global__ void __launch_bounds__(kGThreads, OCC)
     } else if (gridDim.z > 1) {  // split K: the partial sums, finished by k_splitk_sum
         float* pz = part + (int64_t)blockIdx.z * M * N;
 #pragma unroll
-        for (int mt = 0; mt < 4; ++mt)
+        for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
             for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const int m = m0 + wm * 64 + mt * 16 + g + ((e >> 1) << 3);
+                    const int m = m0 + wm * WR + mt * 16 + g + ((e >> 1) << 3);
                     const int n = n0 + wn * 32 + nt * 8 + 2 * tg + (e & 1);
                     if (m < M && n < N) {
                         const float2 p = acc[mt][nt][e >> 1];
@@ -288,12 +291,12 @@ __global__ void __launch_bounds__(kGThreads, OCC)
                 }
     } else {
 #pragma unroll
-        for (int mt = 0; mt < 4; ++mt)
+        for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
             for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) {
-                    const int m = m0 + wm * 64 + mt * 16 + g + ((e >> 1) << 3);
+                    const int m = m0 + wm * WR + mt * 16 + g + ((e >> 1) << 3);
                     const int n = n0 + wn * 32 + nt * 8 + 2 * tg + (e & 1);
                     if (m < M && n < N) {
                         const float2 p = acc[mt][nt][e >> 1];
@@ -341,7 +344,7 @@ __global__ void k_matmul_f(QWeight w, const float* __restrict__ x, int64_t x_str
     }
 }
 
-template <int WT, int SWI, int OCC>
+template <int WT, int SWI, int OCC, int BM = kBM>
 void run_gemm(dim3 grid, const uint8_t* qs, int N, int K, const int8_t* xq, const float* xd,
               int M, float* y, int64_t y_stride, const MatmulEpilogue& ep, const SwiOut& so,
               cudaStream_t st, float* part = nullptr) {
@@ -352,14 +355,23 @@ void run_gemm(dim3 grid, const uint8_t* qs, int N, int K, const int8_t* xq, cons
         static bool configured[64] = {};
         std::lock_guard<std::mutex> lock(mu);
         if (!configured[dev & 63]) {
-            GB_CUDA(cudaFuncSetAttribute(k_gemm_q<WT, SWI, OCC>,
+            GB_CUDA(cudaFuncSetAttribute(k_gemm_q<WT, SWI, OCC, BM>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         kGStages * GStage<WT>::kBytes));
+                                         kGStages * GStage<WT, BM>::kBytes));
             configured[dev & 63] = true;
         }
     }
-    k_gemm_q<WT, SWI, OCC><<<grid, kGThreads, kGStages * GStage<WT>::kBytes, st>>>(
+    k_gemm_q<WT, SWI, OCC, BM><<<grid, kGThreads, kGStages * GStage<WT, BM>::kBytes, st>>>(
         qs, N, K, xq, xd, M, y, y_stride, ep, so, part);
+}
+
+// 64-row tiles for launches of at most 64 rows (GGMLC_B200_GEMM64=0: off)
+bool gemm64_enabled() {
+    static const bool v = [] {
+        const char* e = getenv("GGMLC_B200_GEMM64");
+        return !(e && std::strcmp(e, "0") == 0);
+    }();
+    return v;
 }
 
 void launch_gemm_block(const QWeight& w, const int8_t* xq, const float* xd, int64_t M, float* y,
@@ -369,7 +381,11 @@ void launch_gemm_block(const QWeight& w, const int8_t* xq, const float* xd, int6
     GB_CHECK(((uintptr_t)xq & 15) == 0, "matmul: xq must be 16-byte aligned");
     const bool swi = so.F > 0;
     const int64_t tiles = swi ? so.F / (kBN / 2) : (w.N + kBN - 1) / kBN;
-    dim3 grid((unsigned)tiles, (unsigned)((M + kBM - 1) / kBM));
+    // launches of at most 64 activation rows take 64-row tiles (half of a 128-row tile would be
+    // padding), two CTAs per SM
+    const bool half = M <= 64 && gemm64_enabled();
+    const int bm = half ? 64 : kBM;
+    dim3 grid((unsigned)tiles, (unsigned)((M + bm - 1) / bm));
     int dev = 0;
     GB_CUDA(cudaGetDevice(&dev));
     const uint8_t* qs = (const uint8_t*)w.qs;
@@ -395,7 +411,13 @@ void launch_gemm_block(const QWeight& w, const int8_t* xq, const float* xd, int6
     }
     // Q4_0 stages fit two CTAs per SM: worth it once there are tiles for two per SM
     const bool two = w.type == T_Q4_0 && (splits > 1 || ntile >= 2 * (int64_t)sms);
-    if (w.type == T_Q8_0) {
+    if (half && w.type == T_Q8_0) {
+        if (swi) run_gemm<T_Q8_0, 1, 2, 64>(grid, qs, N, K, xq, xd, m, y, y_stride, ep, so, st);
+        else run_gemm<T_Q8_0, 0, 2, 64>(grid, qs, N, K, xq, xd, m, y, y_stride, ep, so, st, part);
+    } else if (half) {
+        if (swi) run_gemm<T_Q4_0, 1, 2, 64>(grid, qs, N, K, xq, xd, m, y, y_stride, ep, so, st);
+        else run_gemm<T_Q4_0, 0, 2, 64>(grid, qs, N, K, xq, xd, m, y, y_stride, ep, so, st, part);
+    } else if (w.type == T_Q8_0) {
         if (swi) run_gemm<T_Q8_0, 1, 1>(grid, qs, N, K, xq, xd, m, y, y_stride, ep, so, st);
         else run_gemm<T_Q8_0, 0, 1>(grid, qs, N, K, xq, xd, m, y, y_stride, ep, so, st, part);
     } else if (two) {
