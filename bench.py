@@ -8,7 +8,8 @@ A step is one sequence: prefill of 512 prompt tokens (one ubatch, logits of the 
 (runtime/tools/ggmlc_bench.cpp:297-565).  `value` is decode tokens/s with inputs resident in HBM
 (dummy token ids as the reference harness uses, ggmlc_bench.cpp:303,431), timed with CUDA events
 on the executor's stream; `e2e` is the same decode metric through the public API with host
-buffers (token H2D, logits D2H and a host argmax every step).  N > 1 follows the BASELINE
+buffers (token H2D and the greedy token D2H every step, its argmax taken on the device by
+`output_argmax`).  N > 1 follows the BASELINE
 configuration of the model: the Llama-3-70B shape (configs[4], "tensor-parallel over 2/4/8 B200")
 runs tensor-parallel over the N GPUs (one sequence; strong scaling: QKV / gate_up / O / down /
 output projection sharded, two all-reduces per layer); the shapes that one GPU serves (configs[0],
@@ -388,7 +389,7 @@ def run_ours(args) -> None:
     tg_tps = seqs * args.steps * G / (tg_ms / 1e3)
     pp_tps = seqs * args.steps * P / (pp_ms / 1e3)
 
-    # e2e: public API with host buffers — prompt H2D, per-token H2D + logits D2H + host argmax
+    # e2e: public API with host buffers — prompt H2D, per-token H2D + device argmax (token D2H)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e2 = torch.cuda.Event(enable_timing=True)
@@ -397,19 +398,17 @@ def run_ours(args) -> None:
     for _ in range(args.steps):
         e0.record(stream)
         prefill(True)
-        logits = ex.get_output_array(out_id)
+        tok = int(ex.output_argmax(out_id)[0])  # greedy token on the device, 4 bytes back
         e1.record(stream)
-        tok = int(np.argmax(logits))
         for i in range(G):
             decode(P + i, np.array([tok], np.int32))
-            logits = ex.get_output_array(out_id)
-            tok = int(np.argmax(logits))
+            tok = int(ex.output_argmax(out_id)[0])
         e2.record(stream)
         e2.synchronize()
         e2e_pp_ms += e0.elapsed_time(e1)
         e2e_tg_ms += e1.elapsed_time(e2)
-    h2d = P * 4 + G * 4
-    d2h = (G + 1) * logits.nbytes
+    h2d = P * 4 + G * 4 + (P + G) * 4 * (pos_id is not None)
+    d2h = (G + 1) * 4
     if dist:
         t = torch.tensor([e2e_pp_ms, e2e_tg_ms], dtype=torch.float64, device=f"cuda:{local}")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)

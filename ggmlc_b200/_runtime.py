@@ -61,6 +61,7 @@ def _load() -> ctypes.CDLL:
         "gb_executor_run": ([P, I], I),
         "gb_executor_synchronize": ([P], I),
         "gb_executor_get_output": ([P, U32, PP, ctypes.POINTER(SZ)], I),
+        "gb_executor_output_argmax": ([P, U32, I, ctypes.POINTER(ctypes.c_int32)], I),
         "gb_executor_get_tensor_shape": ([P, U32, ctypes.POINTER(I64)], I),
         "gb_executor_get_tensor_size_bytes": ([P, U32, ctypes.POINTER(SZ)], I),
         "gb_executor_set_state": ([P, U32, P, SZ], I),
@@ -360,6 +361,14 @@ class ModelExecutor:
                                            ctypes.byref(n)))
         buf = (ctypes.c_char * n.value).from_address(p.value)
         return np.frombuffer(buf, dtype=np.float32).copy()
+
+    def output_argmax(self, tensor_id: int, rows: int = 1) -> np.ndarray:
+        """Greedy token (first maximum) of each of `rows` rows of an f32 output, computed on the
+        device; only the indices are copied (engine extension, no reference twin)."""
+        out = np.empty(rows, np.int32)
+        _check(_lib.gb_executor_output_argmax(
+            self._h, int(tensor_id), int(rows), out.ctypes.data_as(ctypes.POINTER(ctypes.c_int32))))
+        return out
 
     def get_state_bytes(self, tensor_id: int) -> bytes:
         return self._bytes(_lib.gb_executor_get_state, tensor_id)

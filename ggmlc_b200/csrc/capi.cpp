@@ -221,6 +221,9 @@ int gb_executor_synchronize(gb_executor* e) {
 int gb_executor_get_output(gb_executor* e, uint32_t tid, const void** data, size_t* bytes) {
     return guard([&] { *data = e->e->get_output(tid, bytes); });
 }
+int gb_executor_output_argmax(gb_executor* e, uint32_t tid, int rows, int32_t* out) {
+    return guard([&] { e->e->output_argmax(tid, rows, out); });
+}
 int gb_executor_get_tensor_shape(gb_executor* e, uint32_t tid, int64_t ne[4]) {
     return guard([&] {
         auto s = e->e->tensor_shape(tid);

@@ -97,6 +97,10 @@ int gb_executor_synchronize(gb_executor* e);
 /* get_output_bytes — executor.cpp:3138-3157: device -> host copy; *data is owned by the
  * executor and valid until the next call for the same tensor */
 int gb_executor_get_output(gb_executor* e, uint32_t tid, const void** data, size_t* bytes);
+/* Engine extension, no reference twin: the greedy token (first maximum) of each of `rows` rows
+ * of an f32 output [rows][n], computed on the device; only the `rows` indices cross to the host
+ * (the reference's runner copies the logits and takes the argmax on the host). */
+int gb_executor_output_argmax(gb_executor* e, uint32_t tid, int rows, int32_t* out);
 int gb_executor_get_tensor_shape(gb_executor* e, uint32_t tid, int64_t ne[4]);
 int gb_executor_get_tensor_size_bytes(gb_executor* e, uint32_t tid, size_t* bytes);
 /* set_state_by_id / get_state_bytes / reset_state — executor.cpp:3063-3136 */

@@ -218,3 +218,35 @@ def test_queued_steps_read_their_own_positions(fixture):
         return ex.get_output_array(g.outputs[0]).reshape(-1).copy()
 
     assert np.array_equal(run(True), run(False))
+
+
+@pytest.mark.parametrize("fixture", ["tiny_llama_q8_0", "tiny_gpt2_q8_0"])
+def test_output_argmax_on_device_matches_host(fixture):
+    """output_argmax (the greedy token of each row computed on the device, first maximum) equals
+    numpy's argmax of the copied logits, for a prefill's rows and for decode steps."""
+    from ggmlc_b200 import _runtime as R
+
+    g = R.ModelLoader.load_from_file(str(GOLDEN / f"{fixture}.gguf"))
+    ex = R.ModelExecutor(g, "cuda")
+    ex.init_kv_cache(256)
+    gold = np.load(GOLDEN / f"{fixture}.npz")
+    prompt = gold["prompt"][:12]
+
+    def step(toks, pos):
+        toks = np.asarray(toks, np.int32)
+        ex.prepare({"s": len(toks), "pos": pos, **{s: len(toks) for s in g.symbol_table}})
+        ex.set_input_by_id(g.inputs[0], toks)
+        if len(g.inputs) > 1:
+            ex.set_input_by_id(g.inputs[1], np.arange(pos, pos + len(toks), dtype=np.int32))
+        ex.run()
+
+    step(prompt, 0)
+    lg = ex.get_output_array(g.outputs[0]).reshape(len(prompt), -1)
+    assert np.array_equal(ex.output_argmax(g.outputs[0], len(prompt)), np.argmax(lg, axis=1))
+    tok, pos = int(np.argmax(lg[-1])), len(prompt)
+    for _ in range(4):
+        step([tok], pos)
+        t_dev = int(ex.output_argmax(g.outputs[0])[0])
+        t_host = int(np.argmax(ex.get_output_array(g.outputs[0])))
+        assert t_dev == t_host
+        tok, pos = t_dev, pos + 1
