@@ -124,6 +124,18 @@ class Clocks:
         except Exception:
             self.proc = None
 
+    def wait_first(self, timeout_s: float = 5.0) -> None:
+        """Block until the sampler has written its first sample: nvidia-smi's start-up (NVML
+        initialisation) then falls before the timed region, not inside a short one."""
+        t0 = time.time()
+        while self.proc and time.time() - t0 < timeout_s:
+            try:
+                if self.out.read_text().strip():
+                    return
+            except OSError:
+                pass
+            time.sleep(0.02)
+
     def stop(self) -> dict | None:
         if not self.proc:
             return None
@@ -342,10 +354,12 @@ def run_ours(args) -> None:
 
     def decode(pos: int, upload_tok=None):
         ex.prepare({"s": 1, sym: 1, "pos": pos})
+        # inputs resident for `value` (dummy token and, for GPT-2, dummy position ids, as the
+        # reference harness's dummy tokens); e2e uploads the step's token and position
         if upload_tok is not None:
             ex.set_input_by_id(in_id, upload_tok)
-        if pos_id is not None:
-            ex.set_input_by_id(pos_id, np.array([pos], np.int32))
+            if pos_id is not None:
+                ex.set_input_by_id(pos_id, np.array([pos], np.int32))
         ex.run()
 
     # inputs resident: prompt and decode token uploaded once
@@ -367,13 +381,16 @@ def run_ours(args) -> None:
         ev[2].record(stream)
         return ev
 
+    # the clock sampler starts before the warm-up (samples under load from then on)
+    clocks = Clocks(local) if rank == 0 else None
+    if clocks:
+        clocks.wait_first()
     for _ in range(args.warmup):
         one_step()
     torch.cuda.synchronize(local)
     ex.synchronize()
     if dist:
         dist.barrier()
-    clocks = Clocks(local) if rank == 0 else None
     torch.cuda.synchronize(local)
     evs = [one_step() for _ in range(args.steps)]
     ex.synchronize()
