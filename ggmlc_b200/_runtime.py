@@ -113,6 +113,9 @@ def _load() -> ctypes.CDLL:
         "gb_scheduler_request_tokens": ([P, ctypes.c_uint64, I, P, I64, ctypes.POINTER(I64)], I),
         "gb_scheduler_prefix_stats": ([P, ctypes.POINTER(I64), ctypes.POINTER(I64)], I),
         "gb_executor_configure_prefix_pool": ([P, I64], I),
+        "gb_executor_configure_kv_pool_pages": ([P, I64], I),
+        "gb_executor_kv_pool_pages": ([P], I64),
+        "gb_executor_kv_free_pages": ([P], I64),
         "gb_radix_create": ([I64, PP], I),
         "gb_radix_free": ([P], None),
         "gb_radix_tokens_per_page": ([P], I64),
@@ -501,10 +504,24 @@ class ModelExecutor:
         return int(_lib.gb_executor_paged_active_vram_bytes(self._h))
 
     def configure_vmm_pool(self, max_warm_pages: int = 64, prealloc_pages: int = 0) -> None:
-        """Size of the prefix-cache page pool in pages (max_warm_pages).  Slots are windows of
-        one allocation, so there is no VMM page pool to warm; prealloc_pages is accepted and the
-        pool is allocated on the scheduler's first use."""
+        """Pages kept for the prefix cache on top of max_batch full sequences (max_warm_pages),
+        read at the next init_paged_kv_cache.  The whole pool is allocated at init, so
+        prealloc_pages is accepted and has nothing left to do."""
         _check(_lib.gb_executor_configure_prefix_pool(self._h, int(max_warm_pages)))
+
+    def configure_kv_pool_pages(self, pages: int) -> None:
+        """Exact page count of the pool at the next init_paged_kv_cache (0: max_batch full
+        sequences plus the prefix pages).  A smaller pool serves more short sequences: the
+        scheduler admits requests as their pages allow."""
+        _check(_lib.gb_executor_configure_kv_pool_pages(self._h, int(pages)))
+
+    @property
+    def kv_pool_pages(self) -> int:
+        return int(_lib.gb_executor_kv_pool_pages(self._h))
+
+    @property
+    def kv_free_pages(self) -> int:
+        return int(_lib.gb_executor_kv_free_pages(self._h))
 
     @property
     def tokens_per_page(self) -> int:

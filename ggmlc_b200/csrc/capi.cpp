@@ -331,6 +331,11 @@ int gb_scheduler_prefix_stats(const gb_scheduler* s, int64_t* hits, int64_t* tok
 int gb_executor_configure_prefix_pool(gb_executor* e, int64_t pages) {
     return guard([&] { e->e->configure_prefix_pool(pages); });
 }
+int gb_executor_configure_kv_pool_pages(gb_executor* e, int64_t pages) {
+    return guard([&] { e->e->configure_kv_pool_pages(pages); });
+}
+int64_t gb_executor_kv_pool_pages(const gb_executor* e) { return e->e->kv_pool_pages(); }
+int64_t gb_executor_kv_free_pages(const gb_executor* e) { return e->e->kv_free_pages(); }
 
 int gb_radix_create(int64_t tokens_per_page, gb_radix** out) {
     return guard([&] {

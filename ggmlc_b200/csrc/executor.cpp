@@ -266,7 +266,10 @@ Executor::~Executor() {
     for (cudaEvent_t ev : step_ev_)
         if (ev) cudaEventDestroy(ev);
     if (d_step_) cudaFree(d_step_);
-    if (prefix_pool_) cudaFree(prefix_pool_);
+    if (d_ptab_) cudaFree(d_ptab_);
+    if (ptab_ring_) cudaFreeHost(ptab_ring_);
+    for (cudaEvent_t ev : ptab_ev_)
+        if (ev) cudaEventDestroy(ev);
     if (pinned_out_) cudaFreeHost(pinned_out_);
     if (d_argmax_) cudaFree(d_argmax_);
     if (h_argmax_) cudaFreeHost(h_argmax_);
@@ -413,7 +416,7 @@ void Executor::init_kv_cache(int64_t max_ctx) {
     alloc_kv(1, max_ctx);
 }
 
-void Executor::alloc_kv(int64_t slots, int64_t max_ctx) {
+void Executor::alloc_kv(int64_t slots, int64_t max_ctx, int64_t paged) {
     // enable rule of the reference (executor.cpp:505-539)
     bool has_rope = false, has_pos_sym = false, has_pos_in = false, has_arange = false;
     for (auto& op : g_->ops) has_rope |= op.opcode == OP_ROPE;
@@ -430,7 +433,7 @@ void Executor::alloc_kv(int64_t slots, int64_t max_ctx) {
     SymEnv env;
     env["s"] = 1;
     for (auto& s : g_->symbol_table) env[s] = 1;
-    bool any = false;
+    std::map<uint32_t, KVCache> caches;
     for (auto& op : g_->ops) {
         if (op.opcode != OP_FLASH_ATTN_EXT) continue;
         const GTensor& k = g_->t(op.inputs.at(1));
@@ -441,15 +444,61 @@ void Executor::alloc_kv(int64_t slots, int64_t max_ctx) {
         c.ctx = max_ctx;
         c.slots = slots;
         GB_CHECK(c.batch == 1, "KV caches with a graph batch dimension are not supported");
-        const size_t bytes = (size_t)(c.hd * c.Hkv * slots * max_ctx) * 2;
+        caches[op.id] = c;
+    }
+    if (caches.empty()) return;
+    int64_t pages = 0;
+    if (paged) {
+        // page bytes: T positions of K and V in every layer
+        const int64_t T = tokens_per_page_;
+        int64_t pb = 0;
+        for (auto& [id, c] : caches) pb += 2 * c.Hkv * T * c.hd * 2;
+        const int64_t per_seq = (max_ctx + T - 1) / T;
+        if (kv_pool_want_ > 0) {
+            pages = kv_pool_want_;
+        } else {
+            const int64_t warm = prefix_pool_want_ > 0
+                                     ? prefix_pool_want_
+                                     : std::min(std::max<int64_t>(1, (2LL << 30) / pb), paged * per_seq);
+            pages = paged * per_seq + warm;
+        }
+        GB_CHECK(pages >= 1, "paged KV: the pool needs at least one page");
+        GB_CHECK((size_t)((paged + 1) * per_seq) * 4 <= kMaxPtabBytes,
+                 "paged KV: page table larger than " + std::to_string(kMaxPtabBytes) +
+                     " bytes; raise tokens_per_page");
+        pages += 1;  // + the scratch page 0
+    }
+    for (auto& [id, c] : caches) {
+        c.elems = paged ? pages * c.Hkv * tokens_per_page_ * c.hd : c.hd * c.Hkv * slots * max_ctx;
+        const size_t bytes = (size_t)c.elems * 2;
         GB_CUDA(cudaMalloc(&c.k, bytes));
         GB_CUDA(cudaMalloc(&c.v, bytes));
         GB_CUDA(cudaMemset(c.k, 0, bytes));
         GB_CUDA(cudaMemset(c.v, 0, bytes));
-        kv_[op.id] = c;
-        any = true;
+        kv_[id] = c;
     }
-    if (!any) return;
+    if (paged) {
+        int shift = 0;
+        while ((int64_t(1) << shift) < tokens_per_page_) ++shift;
+        page_shift_ = shift;
+        ptab_stride_ = (int32_t)((max_ctx + tokens_per_page_ - 1) / tokens_per_page_);
+        h_ptab_.assign((size_t)((paged + 1) * ptab_stride_), 0);
+        GB_CUDA(cudaMalloc(&d_ptab_, h_ptab_.size() * 4));
+        GB_CUDA(cudaMemset(d_ptab_, 0, h_ptab_.size() * 4));
+        if (!ptab_ring_) {
+            GB_CUDA(cudaMallocHost(&ptab_ring_, (size_t)kPtabRing * kMaxPtabBytes));
+            for (cudaEvent_t& ev : ptab_ev_)
+                GB_CUDA(cudaEventCreateWithFlags(&ev, cudaEventDisableTiming));
+        }
+        page_ref_.assign((size_t)pages, 0);
+        page_ref_[0] = 1;  // the scratch page is never handed out
+        free_pages_.clear();
+        for (int64_t p = pages - 1; p >= 1; --p) free_pages_.push_back((int32_t)p);
+        slot_pages_.assign((size_t)paged, {});
+        slot_live_.assign((size_t)paged, 0);
+        ptab_dirty_ = false;
+        ++pool_gen_;
+    }
     kv_max_ctx_ = max_ctx;
     kv_enabled_ = true;
 }
@@ -478,52 +527,83 @@ void Executor::free_kv() {
     kv_.clear();
     kv_enabled_ = false;
     paged_ = false;
-    slot_tokens_.clear();
+    if (d_ptab_) cudaFree(d_ptab_);
+    d_ptab_ = nullptr;
+    h_ptab_.clear();
+    page_ref_.clear();
+    free_pages_.clear();
+    slot_pages_.clear();
+    slot_live_.clear();
+    ptab_dirty_ = false;
+    ++pool_gen_;
 }
 
 void Executor::init_paged_kv_cache(int64_t max_batch, int64_t max_ctx) {
     GB_CHECK(max_batch >= 1 && max_batch <= kMaxRows, "paged KV: max_batch must be 1..16");
     GB_CHECK(max_ctx >= 1, "paged KV: max_ctx must be positive");
     if (kv_enabled_) free_kv();
-    alloc_kv(max_batch + 1, max_ctx);  // + the scratch slot of padding rows
+    alloc_kv(max_batch + 1, max_ctx, max_batch);  // + the scratch slot of padding rows
     GB_CHECK(kv_enabled_, "paged KV: the graph has no attention over a KV cache");
     paged_ = true;
     paged_max_batch_ = max_batch;
-    slot_tokens_.assign((size_t)max_batch, -1);
+    paged_max_ctx_ = max_ctx;
 }
 
 void Executor::paged_kv_alloc_slot(int64_t slot) {
     GB_CHECK(paged_, "paged KV cache not initialised");
     GB_CHECK(slot >= 0 && slot < paged_max_batch_, "paged KV: slot out of range");
-    GB_CHECK(slot_tokens_[(size_t)slot] < 0, "paged KV: slot already allocated");
-    slot_tokens_[(size_t)slot] = 0;
+    GB_CHECK(!slot_live_[(size_t)slot], "paged KV: slot already allocated");
+    slot_live_[(size_t)slot] = 1;
 }
 
 void Executor::paged_kv_free_slot(int64_t slot) {
     GB_CHECK(paged_, "paged KV cache not initialised");
     GB_CHECK(slot >= 0 && slot < paged_max_batch_, "paged KV: slot out of range");
-    slot_tokens_[(size_t)slot] = -1;
+    auto& pages = slot_pages_[(size_t)slot];
+    for (int32_t pg : pages) kv_page_release(pg);
+    pages.clear();
+    std::fill(h_ptab_.begin() + slot * ptab_stride_, h_ptab_.begin() + (slot + 1) * ptab_stride_, 0);
+    ptab_dirty_ = true;
+    slot_live_[(size_t)slot] = 0;
+}
+
+int32_t Executor::take_free_page() {
+    GB_CHECK(!free_pages_.empty(), "paged KV: the page pool is exhausted (" +
+                                       std::to_string(page_ref_.size() - 1) + " pages)");
+    const int32_t pg = free_pages_.back();
+    free_pages_.pop_back();
+    return pg;
 }
 
 void Executor::paged_kv_ensure_tokens(int64_t slot, int64_t total) {
     GB_CHECK(paged_, "paged KV cache not initialised");
-    GB_CHECK(slot >= 0 && slot < paged_max_batch_ && slot_tokens_[(size_t)slot] >= 0,
+    GB_CHECK(slot >= 0 && slot < paged_max_batch_ && slot_live_[(size_t)slot],
              "paged KV: slot not allocated");
     GB_CHECK(total >= 0 && total <= kv_max_ctx_,
              "paged KV: " + std::to_string(total) + " tokens exceed max_ctx " +
                  std::to_string(kv_max_ctx_));
-    const int64_t pages = (total + tokens_per_page_ - 1) / tokens_per_page_;
-    slot_tokens_[(size_t)slot] = std::max(slot_tokens_[(size_t)slot], pages * tokens_per_page_);
+    const int64_t need = (total + tokens_per_page_ - 1) / tokens_per_page_;
+    auto& pages = slot_pages_[(size_t)slot];
+    while ((int64_t)pages.size() < need) {
+        const int32_t pg = take_free_page();
+        page_ref_[(size_t)pg] = 1;
+        h_ptab_[(size_t)(slot * ptab_stride_) + pages.size()] = pg;
+        pages.push_back(pg);
+        ptab_dirty_ = true;
+    }
 }
 
 int64_t Executor::paged_active_vram_bytes() const {
     if (!paged_) return 0;
-    int64_t per_token = 0;
-    for (auto& [id, c] : kv_) per_token += c.Hkv * c.hd * 2 * 2;
-    int64_t total = 0;
-    for (int64_t t : slot_tokens_)
-        if (t > 0) total += std::min(t, kv_max_ctx_) * per_token;
-    return total;
+    std::vector<char> mapped(page_ref_.size(), 0);
+    int64_t n = 0;
+    for (auto& pages : slot_pages_)
+        for (int32_t pg : pages)
+            if (!mapped[(size_t)pg]) {
+                mapped[(size_t)pg] = 1;
+                ++n;
+            }
+    return n * kv_page_bytes();
 }
 
 int64_t Executor::kv_page_bytes() const {
@@ -537,55 +617,80 @@ void Executor::configure_prefix_pool(int64_t pages) {
     prefix_pool_want_ = pages;
 }
 
-int64_t Executor::prefix_pool_reserve() {
-    GB_CHECK(paged_, "prefix pool: the paged KV cache is not initialised");
-    const int64_t pb = kv_page_bytes();
-    GB_CHECK(pb > 0, "prefix pool: no KV cache layers");
-    if (prefix_pool_ && prefix_page_bytes_ == pb) return prefix_pool_pages_;
-    if (prefix_pool_) {  // the page layout changed (tokens_per_page): start over
-        GB_CUDA(cudaStreamSynchronize(stream_));
-        cudaFree(prefix_pool_);
-        prefix_pool_ = nullptr;
-    }
-    int64_t n = prefix_pool_want_ > 0 ? prefix_pool_want_ : std::max<int64_t>(1, (2LL << 30) / pb);
-    GB_CUDA(cudaMalloc(&prefix_pool_, (size_t)(n * pb)));
-    prefix_pool_pages_ = n;
-    prefix_page_bytes_ = pb;
-    return n;
+void Executor::configure_kv_pool_pages(int64_t pages) {
+    GB_CHECK(pages >= 0, "paged KV: page count must not be negative");
+    kv_pool_want_ = pages;
 }
 
-// positions [t0, t0 + T) of every layer's K and V rows in `slot` <-> pool page `page`: per layer
-// and K / V, Hkv rows of T * hd halves (ctx * hd apart in the slot, T * hd apart in the page)
-void Executor::kv_slot_to_page(int64_t slot, int64_t t0, int64_t page) {
-    GB_CHECK(prefix_pool_ && page >= 0 && page < prefix_pool_pages_, "prefix pool: bad page");
-    GB_CHECK(paged_ && slot >= 0 && slot < paged_max_batch_, "prefix pool: bad slot");
-    GB_CHECK(t0 >= 0 && t0 + tokens_per_page_ <= kv_max_ctx_, "prefix pool: page past the cache");
-    char* dst = (char*)prefix_pool_ + page * prefix_page_bytes_;
-    for (auto& [id, c] : kv_) {
-        const size_t w = (size_t)(tokens_per_page_ * c.hd * 2);
-        for (__half* base : {c.k, c.v}) {
-            const __half* src = base + slot * c.slot_elems() + t0 * c.hd;
-            GB_CUDA(cudaMemcpy2DAsync(dst, w, src, (size_t)(c.ctx * c.hd * 2), w, (size_t)c.Hkv,
-                                      cudaMemcpyDeviceToDevice, stream_));
-            dst += w * (size_t)c.Hkv;
-        }
-    }
+int64_t Executor::kv_pool_pages() const { return paged_ ? (int64_t)page_ref_.size() - 1 : 0; }
+int64_t Executor::kv_free_pages() const { return paged_ ? (int64_t)free_pages_.size() : 0; }
+
+int64_t Executor::paged_kv_slot_pages(int64_t slot) const {
+    GB_CHECK(paged_ && slot >= 0 && slot < paged_max_batch_, "paged KV: slot out of range");
+    return (int64_t)slot_pages_[(size_t)slot].size();
 }
 
-void Executor::kv_page_to_slot(int64_t page, int64_t slot, int64_t t0) {
-    GB_CHECK(prefix_pool_ && page >= 0 && page < prefix_pool_pages_, "prefix pool: bad page");
-    GB_CHECK(paged_ && slot >= 0 && slot < paged_max_batch_, "prefix pool: bad slot");
-    GB_CHECK(t0 >= 0 && t0 + tokens_per_page_ <= kv_max_ctx_, "prefix pool: page past the cache");
-    const char* src = (const char*)prefix_pool_ + page * prefix_page_bytes_;
+int64_t Executor::kv_slot_page(int64_t slot, int64_t index) const {
+    GB_CHECK(paged_ && slot >= 0 && slot < paged_max_batch_, "paged KV: slot out of range");
+    const auto& pages = slot_pages_[(size_t)slot];
+    GB_CHECK(index >= 0 && index < (int64_t)pages.size(), "paged KV: page index out of range");
+    return pages[(size_t)index];
+}
+
+void Executor::kv_page_retain(int64_t page) {
+    GB_CHECK(paged_ && page >= 1 && page < (int64_t)page_ref_.size() && page_ref_[(size_t)page] > 0,
+             "paged KV: retain of a page nobody holds");
+    ++page_ref_[(size_t)page];
+}
+
+void Executor::kv_page_release(int64_t page) {
+    GB_CHECK(paged_ && page >= 1 && page < (int64_t)page_ref_.size() && page_ref_[(size_t)page] > 0,
+             "paged KV: release of a page nobody holds");
+    if (--page_ref_[(size_t)page] == 0) free_pages_.push_back((int32_t)page);
+}
+
+void Executor::kv_map_page(int64_t slot, int64_t page) {
+    GB_CHECK(paged_ && slot >= 0 && slot < paged_max_batch_ && slot_live_[(size_t)slot],
+             "paged KV: slot not allocated");
+    auto& pages = slot_pages_[(size_t)slot];
+    GB_CHECK((int64_t)pages.size() < ptab_stride_, "paged KV: the slot's table is full");
+    kv_page_retain(page);
+    h_ptab_[(size_t)(slot * ptab_stride_) + pages.size()] = (int32_t)page;
+    pages.push_back((int32_t)page);
+    ptab_dirty_ = true;
+}
+
+// copy-on-write: page `index` of the slot is replaced by a fresh page holding the same rows of
+// every layer (one device copy per layer and K / V: pages are contiguous in each pool)
+void Executor::kv_make_private(int64_t slot, int64_t index) {
+    const int64_t old = kv_slot_page(slot, index);
+    if (page_ref_[(size_t)old] == 1) return;  // the slot is its only holder
+    const int32_t pg = take_free_page();
+    page_ref_[(size_t)pg] = 1;
     for (auto& [id, c] : kv_) {
-        const size_t w = (size_t)(tokens_per_page_ * c.hd * 2);
-        for (__half* base : {c.k, c.v}) {
-            __half* dst = base + slot * c.slot_elems() + t0 * c.hd;
-            GB_CUDA(cudaMemcpy2DAsync(dst, (size_t)(c.ctx * c.hd * 2), src, w, w, (size_t)c.Hkv,
-                                      cudaMemcpyDeviceToDevice, stream_));
-            src += w * (size_t)c.Hkv;
-        }
+        const int64_t pe = c.Hkv * tokens_per_page_ * c.hd;
+        for (__half* pool : {c.k, c.v})
+            GB_CUDA(cudaMemcpyAsync(pool + pg * pe, pool + old * pe, (size_t)pe * 2,
+                                    cudaMemcpyDeviceToDevice, stream_));
     }
+    kv_page_release(old);
+    slot_pages_[(size_t)slot][(size_t)index] = pg;
+    h_ptab_[(size_t)(slot * ptab_stride_ + index)] = pg;
+    ptab_dirty_ = true;
+}
+
+// the host table into the device table, ordered on the stream before the next launch; each
+// upload goes through its own pinned copy that no queued transfer still reads
+void Executor::sync_page_table() {
+    if (!ptab_dirty_) return;
+    const size_t bytes = h_ptab_.size() * 4;
+    int32_t* stage = ptab_ring_ + (size_t)ptab_next_ * (kMaxPtabBytes / 4);
+    GB_CUDA(cudaEventSynchronize(ptab_ev_[ptab_next_]));
+    std::memcpy(stage, h_ptab_.data(), bytes);
+    GB_CUDA(cudaMemcpyAsync(d_ptab_, stage, bytes, cudaMemcpyHostToDevice, stream_));
+    GB_CUDA(cudaEventRecord(ptab_ev_[ptab_next_], stream_));
+    ptab_next_ = (ptab_next_ + 1) % kPtabRing;
+    ptab_dirty_ = false;
 }
 
 void Executor::set_output_rows(const std::vector<int32_t>& rows) {
@@ -594,8 +699,17 @@ void Executor::set_output_rows(const std::vector<int32_t>& rows) {
 }
 
 void Executor::set_tokens_per_page(int64_t n) {
-    GB_CHECK(n >= 1, "tokens_per_page must be positive");
+    GB_CHECK(n >= 1 && n <= 65536 && (n & (n - 1)) == 0,
+             "tokens_per_page must be a power of two (1 .. 65536)");
+    if (n == tokens_per_page_) return;
+    if (!paged_) {
+        tokens_per_page_ = n;
+        return;
+    }
+    for (char live : slot_live_) GB_CHECK(!live, "tokens_per_page: a slot is in use");
+    const int64_t mb = paged_max_batch_, mc = paged_max_ctx_;
     tokens_per_page_ = n;
+    init_paged_kv_cache(mb, mc);  // the pool is laid out again (the prefix cache starts empty)
 }
 
 void Executor::prepare_batch(int rows, const int32_t* pos, const int32_t* slot) {
@@ -604,6 +718,11 @@ void Executor::prepare_batch(int rows, const int32_t* pos, const int32_t* slot) 
     for (int r = 0; r < rows; ++r) {
         GB_CHECK(slot[r] >= 0 && slot[r] <= paged_max_batch_, "batched decode: bad slot");
         GB_CHECK(pos[r] >= 0 && pos[r] < kv_max_ctx_, "batched decode: position outside the cache");
+        if (slot[r] < paged_max_batch_)  // the scratch slot's table points at the scratch page
+            GB_CHECK(slot_live_[(size_t)slot[r]] &&
+                         pos[r] < (int64_t)slot_pages_[(size_t)slot[r]].size() * tokens_per_page_,
+                     "batched decode: position " + std::to_string(pos[r]) + " of slot " +
+                         std::to_string(slot[r]) + " has no page (paged_kv_ensure_tokens)");
     }
     SymEnv env;
     env["s"] = rows;
@@ -620,7 +739,7 @@ void Executor::prepare_batch(int rows, const int32_t* pos, const int32_t* slot) 
 
 void Executor::reset_kv_cache() {
     for (auto& [id, c] : kv_) {
-        const size_t bytes = (size_t)(c.hd * c.Hkv * c.slots * c.ctx) * 2;
+        const size_t bytes = (size_t)c.elems * 2;
         GB_CUDA(cudaMemsetAsync(c.k, 0, bytes, stream_));
         GB_CUDA(cudaMemsetAsync(c.v, 0, bytes, stream_));
     }
@@ -1494,6 +1613,9 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                 BufRef kref, vref;
                 int64_t slot_elems = 0;
                 int64_t sb = 0;  // bytes per slot window: single-sequence launches add kv_slot * sb
+                const int32_t* ptab = nullptr;  // paged cache: the page table (slot 0's row)
+                int64_t pstride = 0;
+                int pshift = 0;
                 if (use_cache) {
                     const KVCache& c = kv_.at(op.id);
                     GB_CHECK(c.hd == hd && c.Hkv == Hkv, "KV cache shape mismatch");
@@ -1504,6 +1626,12 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                     sb = pg.batch ? 0 : slot_elems * 2;
                     kref.fixed = (char*)kc;
                     vref.fixed = (char*)vc;
+                    if (paged_) {  // kc / vc are page pools; the slot is chosen by its page list
+                        ptab = d_ptab_;
+                        pstride = ptab_stride_;
+                        pshift = page_shift_;
+                        sb = 0;
+                    }
                 } else {
                     ctx = k.ne[1];
                     kref.buf = pg.new_buf(Hkv * ctx * hd * 2, oi);
@@ -1614,10 +1742,16 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                         const BufRef yr = y.ref, yq = y.q, yqd = y.qd;
                         const bool hf = y.has_f, hq = y.has_q;
                         const double kvb = (double)Hkv * hd * 2 * 2;  // K+V bytes per position
+                        const bool batched = pg.batch;
                         auto mk = [=](const Program& p) {
                             AttnDecArgs a = da;
                             a.kc = (__half*)((char*)da.kc + p.kv_slot * sb);
                             a.vc = (__half*)((char*)da.vc + p.kv_slot * sb);
+                            if (ptab) {  // batched rows add row_slot * stride in the kernel
+                                a.pg.pages = ptab + (batched ? 0 : p.kv_slot * pstride);
+                                a.pg.stride = (int32_t)pstride;
+                                a.pg.shift = pshift;
+                            }
                             a.qkv = (const float*)p.ptr(base);
                             a.part = (float*)p.ptr(wref);
                             if (hf) a.o = (float*)p.ptr(yr);
@@ -1663,6 +1797,8 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                             a.q_out = (float*)p.ptr(qtr);
                             a.kc = (__half*)(p.ptr(kref) + p.kv_slot * sb);
                             a.vc = (__half*)(p.ptr(vref) + p.kv_slot * sb);
+                            a.pages = ptab ? ptab + p.kv_slot * pstride : nullptr;
+                            a.page_shift = pshift;
                             launch_rope_qkv(a, st);
                         });
                         Val qv = qt;  // view [hd, s, Hq] of the [s][Hq][hd] buffer
@@ -1682,7 +1818,8 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                             launch_attention(p.view(qv), (const __half*)(p.ptr(kref) + p.kv_slot * sb),
                                              (const __half*)(p.ptr(vref) + p.kv_slot * sb), ctx, Hkv, dstep, step_on, 0,
                                              scale, (float*)p.ptr(yr),
-                                             wbytes ? p.ptr(wref) : nullptr, max_kv, st);
+                                             wbytes ? p.ptr(wref) : nullptr, max_kv, st,
+                                             ptab ? ptab + p.kv_slot * pstride : nullptr, pshift);
                         });
                     }
                     o = y;
@@ -1727,8 +1864,9 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                 materialize(k);
                 const Val ks = heads_then_rows(k), vs = heads_then_rows(v), qs = q;
                 add("kv_write", [=](Program& p, cudaStream_t st) {
-                    KVDst kd{(__half*)(p.ptr(kref) + p.kv_slot * sb), ctx};
-                    KVDst vd{(__half*)(p.ptr(vref) + p.kv_slot * sb), ctx};
+                    const int32_t* pl = ptab ? ptab + p.kv_slot * pstride : nullptr;
+                    KVDst kd{(__half*)(p.ptr(kref) + p.kv_slot * sb), ctx, pl, pshift};
+                    KVDst vd{(__half*)(p.ptr(vref) + p.kv_slot * sb), ctx, pl, pshift};
                     launch_kv_write(p.view(ks), dstep, kd, st);
                     launch_kv_write(p.view(vs), dstep, vd, st);
                 });
@@ -1749,7 +1887,8 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
                     launch_attention(p.view(qs), (const __half*)(p.ptr(kref) + p.kv_slot * sb),
                                      (const __half*)(p.ptr(vref) + p.kv_slot * sb),
                                      ctx, Hkv, dstep, step_on, 0, scale, (float*)p.ptr(yr),
-                                     wbytes ? p.ptr(wref) : nullptr, max_kv, st);
+                                     wbytes ? p.ptr(wref) : nullptr, max_kv, st,
+                                     ptab ? ptab + p.kv_slot * pstride : nullptr, pshift);
                 });
                 (void)causal;
                 o = y;
@@ -1871,7 +2010,7 @@ std::shared_ptr<Program> Executor::build(const SymEnv& env, bool kv) {
         if (pg.launch_w[i].qs) nxt = i;
     }
     // single-sequence decode on one GPU: runs of chainable launches become decode chains
-    if (kv && !pg.batch && tp_.size == 1 && chain_enabled_) fuse_chains(pg);
+    if (kv && !pg.batch && tp_.size == 1 && chain_enabled_ && !paged_) fuse_chains(pg);
     pg.chain_descs.clear();
     return P;
 }
@@ -1982,6 +2121,11 @@ void Executor::prepare(const SymEnv& env_in, bool /*arena_reuse*/) {
         const int64_t slot = env.count("slot") ? env.at("slot") : 0;
         const int64_t slots = kv_.empty() ? 1 : kv_.begin()->second.slots;
         GB_CHECK(slot >= 0 && slot < slots, "KV slot " + std::to_string(slot) + " out of range");
+        if (paged_)
+            GB_CHECK(slot < paged_max_batch_ && slot_live_[(size_t)slot] &&
+                         pos + s <= (int64_t)slot_pages_[(size_t)slot].size() * tokens_per_page_,
+                     "paged KV: positions up to " + std::to_string(pos + s) + " of slot " +
+                         std::to_string(slot) + " have no pages (paged_kv_ensure_tokens)");
     }
     GB_CHECK(!batch || kv, "batched decode needs the KV cache");
     auto it = programs_.find(key);
@@ -2035,6 +2179,7 @@ void Executor::run() {
     GB_CHECK(active_, "run before prepare");
     const double t0 = profile_on_ ? now_ms() : 0;
     Program& p = *active_;
+    sync_page_table();
     for (auto& c : p.chains) refresh_chain(p, *c);
     // this step's parameters from a ring entry no queued copy still reads (the working copy is
     // rewritten by the next prepare while this copy may still wait in the stream)

@@ -128,7 +128,8 @@ struct KVCache {
     __half* k = nullptr;
     __half* v = nullptr;
     int64_t hd = 0, Hkv = 0, batch = 1, ctx = 0;
-    int64_t slots = 1;  // sequence windows [slot][Hkv][ctx][hd], slot_elems apart
+    int64_t slots = 1;  // contiguous cache: sequence windows [slot][Hkv][ctx][hd], slot_elems apart
+    int64_t elems = 0;  // halves allocated for k (and for v): windows, or pages [page][Hkv][T][hd]
     int64_t slot_elems() const { return Hkv * ctx * hd; }
 };
 
@@ -169,29 +170,42 @@ public:
     void reset_kv_cache();
     bool has_kv_cache() const { return kv_enabled_; }
 
-    // Paged KV cache (executor.h:147-161 of the reference): max_batch sequence slots of max_ctx
-    // positions each, plus one scratch slot that padding rows of a batched step write into.
-    // Slots are windows of one device allocation per layer; pages of tokens_per_page positions
-    // are accounted as sequences grow (paged_kv_ensure_tokens) and returned on free.
+    // Paged KV cache (executor.h:147-161 of the reference): max_batch sequence slots of up to
+    // max_ctx positions.  Every attention layer keeps its K and its V in a page pool
+    // [page][Hkv][T][hd] fp16 (T = tokens_per_page, a power of two); one page id names the same T
+    // positions in every layer.  A device page table (max_batch + 1 rows of ceil(max_ctx / T)
+    // entries) maps each slot's runs of T positions to pool pages, and the attention kernels
+    // address the cache through it.  Pages are reference-counted: a slot holds the pages
+    // assigned as it grows (paged_kv_ensure_tokens) until paged_kv_free_slot, and the prefix
+    // cache holds references to the pages it indexes, so a prefix hit maps cached pages into a
+    // new slot's table (kv_map_page) instead of copying rows.  Page 0 is the scratch page:
+    // unassigned table entries and the scratch slot of padding rows (slot max_batch) point at it.
+    // The pool holds max_batch full sequences plus the prefix pages of configure_prefix_pool,
+    // or exactly configure_kv_pool_pages pages; both take effect at the next init.
     void init_paged_kv_cache(int64_t max_batch, int64_t max_ctx);
     bool paged_kv_enabled() const { return paged_; }
     void paged_kv_alloc_slot(int64_t slot);
     void paged_kv_free_slot(int64_t slot);
-    void paged_kv_ensure_tokens(int64_t slot, int64_t total);
-    int64_t paged_active_vram_bytes() const;
+    void paged_kv_ensure_tokens(int64_t slot, int64_t total);  // assigns pages up to `total`
+    int64_t paged_active_vram_bytes() const;  // bytes of the pages mapped into slots
     int64_t tokens_per_page() const { return tokens_per_page_; }
-    void set_tokens_per_page(int64_t n);
+    void set_tokens_per_page(int64_t n);  // a power of two; re-lays an idle pool
     int64_t paged_max_batch() const { return paged_ ? paged_max_batch_ : 0; }
-    // Prefix-cache page pool (the store behind the scheduler's prefix tree): pages of
-    // tokens_per_page positions of K and V of every attention layer, [layer][K, V][Hkv][T][hd]
-    // fp16.  A hit copies pages into a sequence's slot; a prefill copies its new full pages out.
-    // configure_prefix_pool sets the page count of the next allocation (configure_vmm_pool of
-    // the reference, whose max_warm_pages it takes); prefix_pool_reserve allocates on first use.
-    int64_t kv_page_bytes() const;
-    void configure_prefix_pool(int64_t pages);
-    int64_t prefix_pool_reserve();  // pages available (allocates the pool if needed)
-    void kv_slot_to_page(int64_t slot, int64_t t0, int64_t page);
-    void kv_page_to_slot(int64_t page, int64_t slot, int64_t t0);
+    int64_t kv_page_bytes() const;   // one page: T positions of K and V in every layer
+    void configure_prefix_pool(int64_t pages);  // prefix-cache pages beyond max_batch sequences
+    void configure_kv_pool_pages(int64_t pages);  // explicit pool size (0: the default rule)
+    int64_t kv_pool_pages() const;   // pages sequences and the prefix cache can use
+    int64_t kv_free_pages() const;   // pages nobody references
+    int64_t paged_kv_slot_pages(int64_t slot) const;  // pages in the slot's table
+    int64_t kv_pool_generation() const { return pool_gen_; }  // bumps on every re-layout
+    // page sharing for the prefix cache
+    int64_t kv_slot_page(int64_t slot, int64_t index) const;  // page of the slot's index-th run
+    void kv_page_retain(int64_t page);
+    void kv_page_release(int64_t page);
+    // append `page` to the slot's table (a reference for the slot); the slot's next run
+    void kv_map_page(int64_t slot, int64_t page);
+    // give the slot its own copy of its index-th page (before writing into a shared page)
+    void kv_make_private(int64_t slot, int64_t index);
     // Batched decode step over `rows` sequences: row r decodes the token at position pos[r] of
     // the sequence in slot slot[r] (rows padded up to a bucket use the scratch slot).
     void prepare_batch(int rows, const int32_t* pos, const int32_t* slot);
@@ -280,15 +294,32 @@ private:
     bool paged_ = false;
     int64_t paged_max_batch_ = 0;
     int64_t tokens_per_page_ = 256;
-    void* prefix_pool_ = nullptr;      // prefix_pool_pages_ x page_bytes_at_alloc_
-    int64_t prefix_pool_pages_ = 0;
-    int64_t prefix_pool_want_ = 0;     // 0: about 2 GiB of pages
-    int64_t prefix_page_bytes_ = 0;    // page size the pool was laid out for
-    std::vector<int64_t> slot_tokens_;  // per slot: positions accounted (-1: free)
+    int64_t prefix_pool_want_ = 0;     // prefix pages; 0: about 2 GiB, at most max_batch seqs
+    int64_t kv_pool_want_ = 0;         // explicit pool pages (0: the default rule)
+    int64_t paged_max_ctx_ = 0;
+    int64_t pool_gen_ = 0;
+    int32_t ptab_stride_ = 0;          // page-table entries per slot
+    int page_shift_ = 0;               // log2(tokens_per_page)
+    std::vector<int32_t> h_ptab_;      // [(max_batch + 1) * ptab_stride_]
+    int32_t* d_ptab_ = nullptr;
+    bool ptab_dirty_ = false;
+    static constexpr int kPtabRing = 4;  // pinned staging copies of the table
+    static constexpr size_t kMaxPtabBytes = size_t(64) << 10;
+    int32_t* ptab_ring_ = nullptr;
+    cudaEvent_t ptab_ev_[kPtabRing] = {};
+    int ptab_next_ = 0;
+    std::vector<int32_t> page_ref_;    // references per pool page (slots + prefix cache)
+    std::vector<int32_t> free_pages_;  // unreferenced pages (page 0 is never among them)
+    std::vector<std::vector<int32_t>> slot_pages_;  // per slot: its table's pages in order
+    std::vector<char> slot_live_;      // per slot: allocated
+    void sync_page_table();            // stream-ordered upload of a changed table
+    int32_t take_free_page();
     char* arena_ = nullptr;             // activation arena shared by every program
     size_t arena_cap_ = 0;
     void ensure_arena(size_t bytes);
-    void alloc_kv(int64_t slots, int64_t max_ctx);
+    // contiguous windows for `slots` sequences, or (paged > 0) page pools sized for `paged`
+    // sequences plus the prefix pages (init_paged_kv_cache)
+    void alloc_kv(int64_t slots, int64_t max_ctx, int64_t paged = 0);
     void free_kv();
     bool logits_last_only_ = false;
     std::vector<int32_t> out_rows_;

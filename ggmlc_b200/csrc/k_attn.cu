@@ -59,7 +59,7 @@ __global__ void k_rope_neox(TView x, const int32_t* __restrict__ pos_src, int us
             o1 = load_f(x, d1, h, t);
         }
         if (to_kv) {
-            __half* row = kv.base + (h * kv.ctx + base + t) * hd;
+            __half* row = kv.base + kv_row_off(kv.pages, kv.shift, H, kv.ctx, h, base + t, hd);
             row[d0] = __float2half_rn(o0);
             row[d1] = __float2half_rn(o1);
         } else {
@@ -78,7 +78,8 @@ __global__ void k_kv_write(TView src, const StepParams* __restrict__ step, int u
     for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
          idx += (int64_t)gridDim.x * blockDim.x) {
         const int64_t d = idx % hd, h = (idx / hd) % H, t = idx / (hd * H);
-        kv.base[(h * kv.ctx + base + t) * hd + d] = __float2half_rn(load_f(src, d, h, t));
+        kv.base[kv_row_off(kv.pages, kv.shift, H, kv.ctx, h, base + t, hd) + d] =
+            __float2half_rn(load_f(src, d, h, t));
     }
 }
 
@@ -94,8 +95,10 @@ constexpr int kSplitLen = 128;
 
 struct AttnArgs {
     TView q;              // f32 [hd, s, Hq]
-    const __half* kc;     // [Hkv][ctx][hd]
+    const __half* kc;     // [Hkv][ctx][hd], or page pools (pages != nullptr, KvPages)
     const __half* vc;
+    const int32_t* pages;
+    int shift;
     int64_t ctx, Hkv, Hq, hd, s;
     const StepParams* step;
     int use_step;
@@ -146,12 +149,11 @@ __global__ void k_attn(AttnArgs a) {
     for (int64_t tile = c0; tile < c1; tile += kTile) {
         __syncthreads();
         const int64_t rows = min((int64_t)kTile, c1 - tile);
-        const __half* kb = a.kc + (hk * a.ctx + tile) * hd;
-        const __half* vb = a.vc + (hk * a.ctx + tile) * hd;
         for (int64_t e = threadIdx.x; e < rows * hd; e += blockDim.x) {
             const int64_t r = e / hd, d = e % hd;
-            sk[r * kstride + d] = kb[e];
-            sv[r * hd + d] = vb[e];
+            const int64_t off = kv_row_off(a.pages, a.shift, a.Hkv, a.ctx, hk, tile + r, hd) + d;
+            sk[r * kstride + d] = a.kc[off];
+            sv[r * hd + d] = a.vc[off];
         }
         __syncthreads();
         if (!qvalid) continue;
@@ -292,9 +294,6 @@ __global__ void __launch_bounds__(kFaWarps * 32) k_fa(AttnArgs a) {
     const int64_t last_q = min((int64_t)(last_item / rk) * 16 + 15, a.s - 1);
     const int64_t nkv = kv_base + last_q + 1;
     const int ntile = (int)((nkv + kFaKeys - 1) / kFaKeys);
-    const __half* kb = a.kc + (int64_t)hk * a.ctx * HD;
-    const __half* vb = a.vc + (int64_t)hk * a.ctx * HD;
-
     auto stage = [&](int tile, int buf) {
         __half* dk = sK + buf * kFaKeys * HD;
         __half* dv = sV + buf * kFaKeys * HD;
@@ -302,10 +301,10 @@ __global__ void __launch_bounds__(kFaWarps * 32) k_fa(AttnArgs a) {
             const int r = e / CH, c = e % CH;
             const int64_t key = (int64_t)tile * kFaKeys + r;
             const bool ok = key < nkv;
-            const int64_t kk = ok ? key : 0;
+            const int64_t off = kv_row_off(a.pages, a.shift, a.Hkv, a.ctx, hk, ok ? key : 0, HD);
             const int sw = (c ^ (r & 7)) * 8;
-            fa_cp16(dk + r * HD + sw, kb + kk * HD + c * 8, ok);
-            fa_cp16(dv + r * HD + sw, vb + kk * HD + c * 8, ok);
+            fa_cp16(dk + r * HD + sw, a.kc + off + c * 8, ok);
+            fa_cp16(dv + r * HD + sw, a.vc + off + c * 8, ok);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
@@ -488,11 +487,14 @@ size_t attn_workspace_bytes(int64_t s, int64_t Hq, int64_t hd, int64_t max_kv) {
 
 void launch_attention(const TView& q, const __half* kc, const __half* vc, int64_t ctx,
                       int64_t Hkv, const StepParams* step, bool use_step, int64_t kv_off,
-                      float scale, float* o, void* work, int64_t max_kv, cudaStream_t st) {
+                      float scale, float* o, void* work, int64_t max_kv, cudaStream_t st,
+                      const int32_t* pages, int page_shift) {
     AttnArgs a;
     a.q = q;
     a.kc = kc;
     a.vc = vc;
+    a.pages = pages;
+    a.shift = page_shift;
     a.ctx = ctx;
     a.Hkv = Hkv;
     a.hd = q.ne[0];

@@ -48,10 +48,12 @@ __global__ void k_rope_qkv(QkvRopeArgs a) {
         } else if (hh < a.Hq + a.Hkv) {
             const int64_t h = hh - a.Hq;
             const float* src = row + a.k_off + h * hd;
-            a.kc[(h * a.ctx + p) * hd + d] = __float2half_rn(rope_elem(src, d, hd, a.tab, p));
+            a.kc[kv_row_off(a.pages, a.page_shift, a.Hkv, a.ctx, h, p, hd) + d] =
+                __float2half_rn(rope_elem(src, d, hd, a.tab, p));
         } else {
             const int64_t h = hh - a.Hq - a.Hkv;
-            a.vc[(h * a.ctx + p) * hd + d] = __float2half_rn(row[a.v_off + h * hd + d]);
+            a.vc[kv_row_off(a.pages, a.page_shift, a.Hkv, a.ctx, h, p, hd) + d] =
+                __float2half_rn(row[a.v_off + h * hd + d]);
         }
     }
 }
@@ -94,22 +96,28 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(AttnDecArgs a) {
     // position of the new token and the KV window of its sequence
     const int64_t pos = a.batched ? (int64_t)a.step->row_pos[row]
                                   : (a.step ? a.step->pos : 0) + a.pos_off;
-    __half* kslot = a.kc + (a.batched ? (int64_t)a.step->row_slot[row] * a.slot_elems : 0);
-    __half* vslot = a.vc + (a.batched ? (int64_t)a.step->row_slot[row] * a.slot_elems : 0);
+    // the sequence's rows: its page list in a paged cache, else its contiguous window
+    const int32_t* plist =
+        a.pg.pages ? a.pg.pages + (a.batched ? (int64_t)a.step->row_slot[row] * a.pg.stride : 0)
+                   : nullptr;
+    const int64_t slot_off =
+        !plist && a.batched ? (int64_t)a.step->row_slot[row] * a.slot_elems : 0;
+    __half* kslot = a.kc + slot_off;
+    __half* vslot = a.vc + slot_off;
+    auto krow = [&](int64_t t) { return kv_row_off(plist, a.pg.shift, a.Hkv, a.ctx, hk, t, HD); };
     const int64_t nkv = pos + 1;
     const int64_t per = (nkv + gridDim.x - 1) / gridDim.x;
     const int64_t c0 = min((int64_t)blockIdx.x * per, nkv);
     const int64_t c1 = min(c0 + per, nkv);
-    const __half* kbase = kslot + ((int64_t)hk * a.ctx) * HD;
-    const __half* vbase = vslot + ((int64_t)hk * a.ctx) * HD;
     auto stage = [&](int buf, int64_t cs, int rows) {
         __half* dk = sk + buf * kChunk * HD;
         __half* dv = sv + buf * kChunk * HD;
         for (int e = threadIdx.x; e < rows * VEC; e += kDecThreads) {
             const int r = e / VEC, pc = e % VEC;
             if (cs + r == pos) continue;  // the new row is taken from snew
-            cp_async16(dk + r * HD + pc * 8, kbase + (cs + r) * HD + pc * 8);
-            cp_async16(dv + r * HD + pc * 8, vbase + (cs + r) * HD + pc * 8);
+            const int64_t off = krow(cs + r) + pc * 8;
+            cp_async16(dk + r * HD + pc * 8, kslot + off);
+            cp_async16(dv + r * HD + pc * 8, vslot + off);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
@@ -130,8 +138,8 @@ __global__ void __launch_bounds__(kDecThreads) k_attn_decode(AttnDecArgs a) {
         for (int d = threadIdx.x; d < HD; d += kDecThreads) {
             const __half kh = __float2half_rn(rope_elem(ks, d, HD, a.tab, pos));
             const __half vh = __float2half_rn(qrow[a.v_off + (int64_t)hk * HD + d]);
-            kslot[((int64_t)hk * a.ctx + pos) * HD + d] = kh;
-            vslot[((int64_t)hk * a.ctx + pos) * HD + d] = vh;
+            kslot[krow(pos) + d] = kh;
+            vslot[krow(pos) + d] = vh;
             snew[d] = kh;
             snew[HD + d] = vh;
         }
@@ -327,26 +335,34 @@ __global__ void __launch_bounds__(NW * 32) k_attn_decode_tc(AttnDecArgs a) {
     uint8_t* ring = ring_all + warp * kTcDepth * SM::kSlot;
     const int64_t pos = a.batched ? (int64_t)a.step->row_pos[row]
                                   : (a.step ? a.step->pos : 0) + a.pos_off;
-    __half* kslot = a.kc + (a.batched ? (int64_t)a.step->row_slot[row] * a.slot_elems : 0);
-    __half* vslot = a.vc + (a.batched ? (int64_t)a.step->row_slot[row] * a.slot_elems : 0);
+    // the sequence's rows: its page list in a paged cache, else its contiguous window
+    const int32_t* plist =
+        a.pg.pages ? a.pg.pages + (a.batched ? (int64_t)a.step->row_slot[row] * a.pg.stride : 0)
+                   : nullptr;
+    const int64_t slot_off =
+        !plist && a.batched ? (int64_t)a.step->row_slot[row] * a.slot_elems : 0;
+    __half* kslot = a.kc + slot_off;
+    __half* vslot = a.vc + slot_off;
+    auto krow = [&](int64_t t) { return kv_row_off(plist, a.pg.shift, a.Hkv, a.ctx, hk, t, HD); };
     const int64_t nkv = pos + 1;
     const int64_t per = (nkv + gridDim.x - 1) / gridDim.x;
     const int64_t c0 = min((int64_t)blockIdx.x * per, nkv);
     const int64_t c1 = min(c0 + per, nkv);
-    const __half* kbase = kslot + ((int64_t)hk * a.ctx) * HD;
-    const __half* vbase = vslot + ((int64_t)hk * a.ctx) * HD;
     const int nblk = (int)((c1 - c0 + kTcPos - 1) / kTcPos);
     // block b of the split into a ring slot: rows past the split and the new position read as 0
     auto stage = [&](int slot, int b) {
         uint8_t* dk = ring + slot * SM::kSlot;
         uint8_t* dv = dk + kTcPos * R;
         const int64_t ps = c0 + (int64_t)b * kTcPos;
-        for (int e = lane; e < kTcPos * (HD / 8); e += 32) {
+        // lane j < kTcPos finds row j's offset (one page-table read a row, not one a chunk)
+        const int64_t mine = lane < kTcPos && ps + lane < c1 ? krow(ps + lane) : 0;
+        for (int e = lane; e < kTcPos * (HD / 8); e += 32) {  // the same trip count on every lane
             const int r = e / (HD / 8), pc = e % (HD / 8);
+            const int64_t roff = __shfl_sync(0xffffffffu, mine, r);
             const bool ok = ps + r < c1 && ps + r != pos;
-            const int64_t off = ok ? (ps + r) * HD + pc * 8 : 0;
-            cp_async16z(dk + r * R + pc * 16, kbase + off, ok);
-            cp_async16z(dv + r * R + pc * 16, vbase + off, ok);
+            const int64_t off = ok ? roff + pc * 8 : 0;
+            cp_async16z(dk + r * R + pc * 16, kslot + off, ok);
+            cp_async16z(dv + r * R + pc * 16, vslot + off, ok);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
@@ -436,8 +452,8 @@ __global__ void __launch_bounds__(NW * 32) k_attn_decode_tc(AttnDecArgs a) {
         }
         const __half kh = __float2half_rn(kr);
         const __half vh = __float2half_rn(nv);
-        kslot[((int64_t)hk * a.ctx + pos) * HD + nd] = kh;
-        vslot[((int64_t)hk * a.ctx + pos) * HD + nd] = vh;
+        kslot[krow(pos) + nd] = kh;
+        vslot[krow(pos) + nd] = vh;
         snew[nd] = kh;
         snew[HD + nd] = vh;
     }

@@ -810,7 +810,8 @@ bool chain_gemv_ok(const GemvArgs& a) {
 }
 
 bool chain_attn_ok(const AttnDecArgs& a) {
-    return a.rows == 1 && !a.batched && a.step && (a.hd == 64 || a.hd == 128) && a.Hkv > 0 &&
+    return a.rows == 1 && !a.batched && !a.pg.pages && a.step && (a.hd == 64 || a.hd == 128) &&
+           a.Hkv > 0 &&
            a.Hkv <= kChainMaxKvHeads && a.Hq % a.Hkv == 0 && a.Hq / a.Hkv <= kMaxRk &&
            a.tab.n_dims <= a.hd && a.tab.n_dims % 2 == 0 && (a.o || (a.oq && a.od));
 }

@@ -242,9 +242,30 @@ struct RopeTable {
     int n_dims = 0;
     float theta_scale = 1.0f;
 };
+// Where one sequence's K (or V) rows live in a KV cache.
+//   contiguous (pages == nullptr): the sequence's window [H][ctx][hd] starts at the base pointer;
+//   paged: the base pointer is a layer's page pool [page][H][1 << shift][hd], and pages[i] names
+//     the pool page holding the sequence's positions [i << shift, (i + 1) << shift) in every
+//     layer (one page table serves all layers).  Batched launches pass slot 0's list; slot s's
+//     list starts `stride` entries further on.
+struct KvPages {
+    const int32_t* pages = nullptr;
+    int32_t stride = 0;
+    int32_t shift = 0;
+};
+// element offset of row (h, t) of a sequence whose page list is `pages` (see KvPages)
+__host__ __device__ __forceinline__ int64_t kv_row_off(const int32_t* pages, int shift, int64_t H,
+                                                       int64_t ctx, int64_t h, int64_t t,
+                                                       int64_t hd) {
+    if (!pages) return (h * ctx + t) * hd;
+    const int64_t pg = pages[t >> shift];
+    return (((pg * H + h) << shift) + (t & ((int64_t(1) << shift) - 1))) * hd;
+}
 struct KVDst {
-    __half* base = nullptr;  // [H][ctx][hd]
+    __half* base = nullptr;  // [H][ctx][hd], or a page pool (pages != nullptr)
     int64_t ctx = 0;         // rows per head
+    const int32_t* pages = nullptr;
+    int32_t shift = 0;
 };
 void launch_rope_neox(const TView& x, const int32_t* pos_src, bool use_step_pos,
                       const StepParams* step, const RopeTable& tab, const TView* y,
@@ -268,6 +289,8 @@ struct QkvRopeArgs {
     __half* kc = nullptr;
     __half* vc = nullptr;
     int64_t ctx = 0;
+    const int32_t* pages = nullptr;  // paged cache: this sequence's page list (KvPages)
+    int32_t page_shift = 0;
 };
 void launch_rope_qkv(const QkvRopeArgs& a, cudaStream_t st);
 
@@ -298,6 +321,9 @@ struct AttnDecArgs {
     bool batched = false;
     int64_t qkv_stride = 0;
     int64_t slot_elems = 0;
+    // paged cache (KvPages): kc / vc are the layer's page pools; a single sequence's page list,
+    // or for batched launches slot 0's list with row r's at pg.pages + row_slot[r] * pg.stride
+    KvPages pg;
 };
 // splits per (row, KV head): about two CTAs per SM over all rows and heads of the launch
 int attn_decode_splits(int64_t Hkv, int64_t max_kv, int rows = 1);
@@ -319,9 +345,11 @@ float* attn_decode_static_work(size_t need);
 // Output o: f32 [s][Hq][hd] contiguous (the FLASH_ATTN_EXT permuted result) .  Q is rounded to
 // fp16 like the CPU kernel.  work: scratch of attn_workspace_bytes().
 size_t attn_workspace_bytes(int64_t s, int64_t Hq, int64_t hd, int64_t max_kv);
+// A paged cache passes its page pools as kc / vc and the sequence's page list (KvPages).
 void launch_attention(const TView& q, const __half* kc, const __half* vc, int64_t ctx,
                       int64_t Hkv, const StepParams* step, bool use_step, int64_t kv_off,
-                      float scale, float* o, void* work, int64_t max_kv, cudaStream_t st);
+                      float scale, float* o, void* work, int64_t max_kv, cudaStream_t st,
+                      const int32_t* pages = nullptr, int page_shift = 0);
 
 // ---- decode chain (k_chain.cu) ---------------------------------------------------------------
 // The launches of one single-sequence decode step — quantized GEMVs with their RMSNorm / quantize

@@ -5,9 +5,9 @@
 // bytes and verified token by token, matching walks whole pages from the root, and pages are
 // reclaimed least-recently-used first, leaves only.
 //
-// The tree only indexes; the page store is the executor's prefix pool (pages are copied into a
-// sequence's KV slot on a hit, and out of it after a prefill), so a page id here is an index into
-// that pool.
+// The tree only indexes: a page id here is a page of the executor's paged KV pool, which the
+// scheduler holds a reference to for as long as the node exists and maps into a sequence's page
+// table on a hit.
 #pragma once
 
 #include <cstdint>

@@ -23,18 +23,26 @@ Scheduler::Scheduler(Executor& ex, int max_batch, int eos, int64_t max_ctx)
     GB_CHECK(!g.outputs.empty(), "scheduler: the graph has no output");
     out_id_ = g.outputs[0];
     ex.init_paged_kv_cache(max_batch, max_ctx);
+    gen_ = ex.kv_pool_generation();
     ex.set_logits_last_only(true);
     slots_.assign((size_t)max_batch, nullptr);
 }
 
 Scheduler::~Scheduler() {
+    // after another init_paged_kv_cache the slots and pages belong to the new pool's users
+    const bool same_pool = gen_ == ex_.kv_pool_generation();
     for (size_t i = 0; i < slots_.size(); ++i)
-        if (slots_[i]) {
+        if (slots_[i] && same_pool) {
             try {
                 ex_.paged_kv_free_slot((int64_t)i);
             } catch (...) {
             }
         }
+    try {  // the prefix cache's page references
+        if (tree_ && tree_gen_ == ex_.kv_pool_generation())
+            for (int64_t pg; (pg = tree_->evict_lru()) >= 0;) ex_.kv_page_release(pg);
+    } catch (...) {
+    }
 }
 
 uint64_t Scheduler::add_request(const std::vector<int32_t>& prompt, int max_new, float temperature,
@@ -43,6 +51,8 @@ uint64_t Scheduler::add_request(const std::vector<int32_t>& prompt, int max_new,
     GB_CHECK(max_new >= 1, "scheduler: max_new_tokens must be at least 1");
     GB_CHECK((int64_t)prompt.size() + max_new <= ex_.kv_max_ctx(),
              "scheduler: prompt + max_new_tokens exceed the KV cache length");
+    GB_CHECK(pages_for((int64_t)prompt.size() + max_new) <= ex_.kv_pool_pages(),
+             "scheduler: prompt + max_new_tokens need more pages than the KV pool holds");
     auto r = std::make_shared<GenRequest>();
     r->id = next_id_++;
     r->prompt = prompt;
@@ -100,28 +110,36 @@ void Scheduler::finish(const std::shared_ptr<GenRequest>& r, int32_t tok, StepOu
     slots_[(size_t)r->slot] = nullptr;
 }
 
-// Pool page for a new chunk: a free one, else the least recently used leaf's.  The pool is
-// allocated when the first page is needed.
-int64_t Scheduler::take_page() {
-    if (!pool_ready_) {
-        const int64_t n = ex_.prefix_pool_reserve();
-        free_pages_.clear();
-        for (int64_t p = n - 1; p >= 0; --p) free_pages_.push_back(p);
-        pool_ready_ = true;
+int64_t Scheduler::pages_for(int64_t tokens) const {
+    const int64_t T = ex_.tokens_per_page();
+    return (tokens + T - 1) / T;
+}
+
+int64_t Scheduler::outstanding_pages() const {
+    int64_t n = 0;
+    for (auto& r : slots_)
+        if (r)
+            n += std::max<int64_t>(0, pages_for((int64_t)r->prompt.size() + r->max_new) -
+                                          ex_.paged_kv_slot_pages(r->slot));
+    return n;
+}
+
+bool Scheduler::make_room(int64_t need) {
+    const int64_t owed = outstanding_pages();
+    while (ex_.kv_free_pages() - owed < need) {
+        const int64_t pg = tree_ ? tree_->evict_lru() : -1;  // least recently used prefix page
+        if (pg < 0) return false;
+        ex_.kv_page_release(pg);
     }
-    if (!free_pages_.empty()) {
-        const int64_t p = free_pages_.back();
-        free_pages_.pop_back();
-        return p;
-    }
-    return tree_ ? tree_->evict_lru() : -1;
+    return true;
 }
 
 void Scheduler::ensure_tree() {
     const int64_t T = ex_.tokens_per_page();
-    if (tree_ && tree_->tokens_per_page() == T) return;
-    tree_ = std::make_unique<PrefixTree>(T);  // a new page size starts an empty cache
-    pool_ready_ = false;
+    if (tree_ && tree_->tokens_per_page() == T && tree_gen_ == ex_.kv_pool_generation()) return;
+    // a new pool layout: the old tree's page ids (and their references) went with the old pool
+    tree_ = std::make_unique<PrefixTree>(T);
+    tree_gen_ = ex_.kv_pool_generation();
 }
 
 StepOut Scheduler::step() {
@@ -130,6 +148,12 @@ StepOut Scheduler::step() {
     // prefilled alone into it, reusing the KV rows of the longest cached run of whole prompt
     // pages; a step that admits returns without decoding
     bool admitted = false;
+    if (gen_ != ex_.kv_pool_generation()) {  // the pool was laid out again
+        GB_CHECK(active_count() == 0, "scheduler: the KV pool was re-initialised under running "
+                                      "requests");
+        gen_ = ex_.kv_pool_generation();
+    }
+    if (tree_ && tree_gen_ != gen_) tree_.reset();
     while (!pending_.empty()) {
         int slot = -1;
         for (size_t i = 0; i < slots_.size(); ++i)
@@ -139,23 +163,35 @@ StepOut Scheduler::step() {
             }
         if (slot < 0) break;
         auto r = pending_.front();
+        const int64_t n = (int64_t)r->prompt.size();
+        PrefixMatch m;
+        if (prefix_caching_) {
+            ensure_tree();
+            m = tree_->match(r->prompt);
+        }
+        // the cached pages become the head of the slot's page table (a reference each)
+        ex_.paged_kv_alloc_slot(slot);
+        for (int64_t p = 0; p < m.matched_pages; ++p) ex_.kv_map_page(slot, m.pages[(size_t)p]);
+        // a prompt cached whole re-evaluates its last token, which writes into its last page:
+        // that page is copied first
+        const bool whole = m.matched_pages > 0 && m.matched_tokens == n;
+        const int64_t need = pages_for(n + r->max_new) - m.matched_pages + (whole ? 1 : 0);
+        if (!make_room(need)) {
+            ex_.paged_kv_free_slot(slot);
+            GB_CHECK(active_count() > 0, "scheduler: the KV pool cannot hold request " +
+                                             std::to_string(r->id) + " (" + std::to_string(need) +
+                                             " pages) even with nothing else running");
+            break;  // it waits for running sequences to return their pages
+        }
         pending_.pop_front();
         r->slot = slot;
         slots_[(size_t)slot] = r;
-        ex_.paged_kv_alloc_slot(slot);
-        const int64_t n = (int64_t)r->prompt.size();
-        ex_.paged_kv_ensure_tokens(slot, n + r->max_new);
-        int64_t matched = 0;
-        if (prefix_caching_) {
-            ensure_tree();
-            const PrefixMatch m = tree_->match(r->prompt);
-            for (int64_t p = 0; p < m.matched_pages; ++p)
-                ex_.kv_page_to_slot(m.pages[(size_t)p], slot, p * tree_->tokens_per_page());
-            matched = m.matched_tokens;
-            if (matched > 0) {
-                ++prefix_hits_;
-                prefix_saved_ += matched;
-            }
+        if (whole) ex_.kv_make_private(slot, m.matched_pages - 1);
+        ex_.paged_kv_ensure_tokens(slot, n);
+        const int64_t matched = m.matched_tokens;
+        if (matched > 0) {
+            ++prefix_hits_;
+            prefix_saved_ += matched;
         }
         r->prefix_matched = matched;
         // the uncached tail; a prompt cached whole re-evaluates its last token
@@ -169,24 +205,15 @@ StepOut Scheduler::step() {
         ex_.prepare(env, true);
         ex_.set_input(in_id_, r->prompt.data() + pos, (size_t)s * 4);
         ex_.run();
-        if (prefix_caching_) {  // index the prompt's new whole pages
+        if (prefix_caching_) {  // the prompt's new whole pages join the tree (a reference each)
             const int64_t T = tree_->tokens_per_page();
-            const int64_t first = matched / T, full = n / T;
-            if (full > first) {
-                try {
-                    tree_->insert(r->prompt, first, full - first, [&](int64_t i) {
-                        const int64_t page = take_page();
-                        if (page >= 0) ex_.kv_slot_to_page(slot, (first + i) * T, page);
-                        return page;
-                    });
-                } catch (const Error&) {
-                    // no memory for the pool (or a failed copy): drop the cache, serve on
-                    cudaGetLastError();
-                    tree_->reset();
-                    pool_ready_ = false;
-                    prefix_caching_ = false;
-                }
-            }
+            const int64_t first = m.matched_pages, full = n / T;
+            if (full > first)
+                tree_->insert(r->prompt, first, full - first, [&](int64_t i) {
+                    const int64_t page = ex_.kv_slot_page(slot, first + i);
+                    ex_.kv_page_retain(page);
+                    return page;
+                });
         }
         int32_t tok = 0;
         if (r->temperature <= 0.0f) {
@@ -216,6 +243,8 @@ StepOut Scheduler::step() {
         slot[i] = act[i]->slot;
         tok[i] = act[i]->generated.back();
     }
+    GB_CHECK(make_room(0), "scheduler: the KV pool is overcommitted");
+    for (auto& r : act) ex_.paged_kv_ensure_tokens(r->slot, r->pos + 1);  // the new position's page
     ex_.prepare_batch(rows, pos.data(), slot.data());
     ex_.set_input(in_id_, tok.data(), tok.size() * 4);
     ex_.run();

@@ -6,9 +6,17 @@
 // batched step over all active sequences, rows padded to a bucket of 1/2/4/8/16 with a scratch
 // slot), where the reference runs one shared position over all slots; the graph needs no batch
 // dimension (rows of the sequence axis are the batch).  Prefix caching (on by default, as in the
-// reference) indexes whole prompt pages in a PrefixTree whose pages live in the executor's
-// prefix pool: a hit copies the cached KV rows into the new slot and prefills only the rest of
-// the prompt; a prefill copies its new whole pages out.
+// reference) indexes whole prompt pages in a PrefixTree whose page ids are pages of the
+// executor's paged KV pool, each held by a reference of the tree: a hit maps the cached pages
+// into the new slot's page table (no copy) and prefills only the rest of the prompt; a prefill
+// hands its new whole pages to the tree.  A prompt cached whole re-evaluates its last token,
+// so its last page is copied first (copy-on-write).
+//
+// Admission follows the pool: a request is admitted when the pages it can still claim
+// (prompt + max_new_tokens, less the pages it shares) fit next to what the running sequences
+// may still claim, after evicting least-recently-used prefix pages; otherwise it waits.  Pages
+// are assigned as sequences grow (the prompt at admission, one page per tokens_per_page decode
+// steps after), so the pool's mapped bytes follow the tokens in use.
 #pragma once
 
 #include <cstdint>
@@ -69,7 +77,9 @@ public:
 private:
     int32_t sample(const float* logits, int64_t vocab, float temperature);
     void ensure_tree();
-    int64_t take_page();
+    int64_t pages_for(int64_t tokens) const;
+    int64_t outstanding_pages() const;  // pages running sequences may still claim
+    bool make_room(int64_t need);       // evict prefix pages until `need` pages are claimable
     void finish(const std::shared_ptr<GenRequest>& r, int32_t tok, StepOut& out);
 
     Executor& ex_;
@@ -83,8 +93,8 @@ private:
     std::map<uint64_t, std::shared_ptr<GenRequest>> all_;
     std::mt19937 rng_{1337};
     std::unique_ptr<PrefixTree> tree_;
-    std::vector<int64_t> free_pages_;
-    bool pool_ready_ = false;
+    int64_t tree_gen_ = -1;  // pool layout the tree's page ids belong to
+    int64_t gen_ = -1;       // pool layout made by the constructor
     int64_t prefix_hits_ = 0, prefix_saved_ = 0;
 };
 

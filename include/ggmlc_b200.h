@@ -152,12 +152,17 @@ const char* gb_executor_kernel_times(gb_executor* e);
 void* gb_executor_stream(const gb_executor* e);
 
 /* ---- paged KV cache (python_bindings.cpp:196-204; executor.cpp:634-920) ---------------------
- * init_paged_kv_cache(max_batch, max_ctx): max_batch sequence slots (1..16) of max_ctx
- * positions.  Slots are windows of one allocation per layer (no driver-VMM mapping); pages of
- * tokens_per_page positions are accounted as a slot grows.  prepare() with symbol "slot" runs a
- * single sequence in that slot; gb_executor_prepare_batch runs one decode token for each of
- * `rows` sequences (row r at position pos[r] in slot slot[r]; slot == max_batch is a scratch
- * slot for padding rows). */
+ * init_paged_kv_cache(max_batch, max_ctx): max_batch sequence slots (1..16) of up to max_ctx
+ * positions over a pool of pages.  A page holds tokens_per_page positions (a power of two) of K
+ * and V in every attention layer; each layer's pool is [page][Hkv][tokens_per_page][head_dim]
+ * fp16 and a device page table maps each slot's runs of positions to pages (the reference maps
+ * driver-VMM pages into per-slot address windows instead; here the kernels read the table).
+ * paged_kv_ensure_tokens assigns pages as a slot grows, paged_kv_free_slot returns them, and
+ * paged_active_vram_bytes counts the pages mapped into slots.  prepare() with symbol "slot"
+ * runs a single sequence in that slot (its positions must have pages); gb_executor_prepare_batch
+ * runs one decode token for each of `rows` sequences (row r at position pos[r] in slot
+ * slot[r]; slot == max_batch is a scratch slot for padding rows).  set_tokens_per_page on an
+ * initialised cache lays the pool out again and needs every slot free. */
 int gb_executor_init_paged_kv_cache(gb_executor* e, int64_t max_batch, int64_t max_ctx);
 int gb_executor_is_paged_kv_cache_enabled(const gb_executor* e);
 int gb_executor_paged_kv_alloc_slot(gb_executor* e, int64_t slot);
@@ -168,10 +173,17 @@ int64_t gb_executor_tokens_per_page(const gb_executor* e);
 int gb_executor_set_tokens_per_page(gb_executor* e, int64_t tokens_per_page);
 int gb_executor_prepare_batch(gb_executor* e, int rows, const int32_t* pos, const int32_t* slot);
 
-/* Prefix-cache page pool size in pages (replaces configure_vmm_pool's max_warm_pages,
- * python_bindings.cpp:201; the reference's pages are VMM pages shared by slots, ours are copied
- * in and out of slots).  0 (default): about 2 GiB of pages, allocated on first use. */
+/* Pool size, read at the next init_paged_kv_cache.  configure_prefix_pool (configure_vmm_pool's
+ * max_warm_pages, python_bindings.cpp:201): pages kept for the prefix cache on top of max_batch
+ * full sequences; 0 (default): about 2 GiB of pages, at most max_batch sequences' worth.  Cached
+ * prefix pages are shared with the slots that use them (a reference each, no copy).
+ * configure_kv_pool_pages: the pool's exact page count instead (0: the rule above); a pool
+ * smaller than max_batch full sequences makes the scheduler admit requests as pages allow.
+ * kv_pool_pages / kv_free_pages: pages of the current pool / pages nobody references. */
 int gb_executor_configure_prefix_pool(gb_executor* e, int64_t pages);
+int gb_executor_configure_kv_pool_pages(gb_executor* e, int64_t pages);
+int64_t gb_executor_kv_pool_pages(const gb_executor* e);
+int64_t gb_executor_kv_free_pages(const gb_executor* e);
 
 /* ---- PagedRadixTree (radix_tree.h; radix_tree.cpp:7-220; python_bindings.cpp:248-258) -------
  * Prefix index over whole pages of tokens_per_page tokens: 64-bit FNV-1a chunk hashes verified

@@ -13,7 +13,12 @@ built oracle/_ref (``make -C oracle``):
    reference sources): op-level vectors through one-op ggml graphs and model-level logits and
    greedy tokens through ggmlc::ModelExecutor with the padded KV cache.
 
-The GGUFs and .npz files are committed; this script is only needed to regenerate them.
+The GGUFs and .npz files are committed; this script is only needed to regenerate them.  The
+committed files were written with NumPy 2.3.5: the compiler's RoPE freq_base recovery
+(python/ggmlc/transforms/fusion.py:322, ``(1.0 / arr[1]) ** (n_dims / 2.0)`` on a float32 array
+element) stays in float32 under NumPy 2's scalar promotion and would promote to float64 under
+NumPy 1.x, which can move the recorded freq_base (and every RoPE angle after it).  The script
+refuses to run under NumPy 1.x for that reason.
 """
 
 from __future__ import annotations
@@ -287,4 +292,6 @@ def main():
 
 
 if __name__ == "__main__":
+    if int(np.__version__.split(".")[0]) < 2:
+        sys.exit(f"NumPy {np.__version__}: the committed goldens follow NumPy 2 scalar promotion")
     main_batch() if "--batch-only" in sys.argv else main()

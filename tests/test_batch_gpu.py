@@ -39,6 +39,8 @@ def _single(fixture, prompt, n_new):
     g, ex = _executor(fixture)
     ex.init_paged_kv_cache(1, MAX_CTX)
     ex.set_logits_last_only(True)
+    ex.paged_kv_alloc_slot(0)
+    ex.paged_kv_ensure_tokens(0, len(prompt) + n_new)
     sym = g.symbol_table
     in_id, out_id = g.inputs[0], g.outputs[0]
     env = {"s": len(prompt), "pos": 0, "slot": 0, **{s: len(prompt) for s in sym}}
@@ -63,6 +65,8 @@ def _forced(fixture, prompt, toks):
     g, ex = _executor(fixture)
     ex.init_paged_kv_cache(1, MAX_CTX)
     ex.set_logits_last_only(True)
+    ex.paged_kv_alloc_slot(0)
+    ex.paged_kv_ensure_tokens(0, len(prompt) + len(toks))
     in_id, out_id = g.inputs[0], g.outputs[0]
     ex.prepare({"s": len(prompt), "pos": 0, "slot": 0, **{s: len(prompt) for s in g.symbol_table}})
     ex.set_input_by_id(in_id, np.asarray(prompt, np.int32))
