@@ -354,11 +354,14 @@ __global__ void __launch_bounds__(NW * 32) k_attn_decode_tc(AttnDecArgs a) {
         uint8_t* dk = ring + slot * SM::kSlot;
         uint8_t* dv = dk + kTcPos * R;
         const int64_t ps = c0 + (int64_t)b * kTcPos;
-        // lane j < kTcPos finds row j's offset (one page-table read a row, not one a chunk)
-        const int64_t mine = lane < kTcPos && ps + lane < c1 ? krow(ps + lane) : 0;
+        // paged: lane j < kTcPos finds row j's offset (one page-table read a row, not one a
+        // chunk); contiguous: rows are HD apart from the head's first row
+        const int64_t mine = plist && lane < kTcPos && ps + lane < c1 ? krow(ps + lane) : 0;
+        const int64_t head0 = (int64_t)hk * a.ctx * HD;
         for (int e = lane; e < kTcPos * (HD / 8); e += 32) {  // the same trip count on every lane
             const int r = e / (HD / 8), pc = e % (HD / 8);
-            const int64_t roff = __shfl_sync(0xffffffffu, mine, r);
+            const int64_t roff = plist ? __shfl_sync(0xffffffffu, mine, r)  // warp-uniform branch
+                                       : head0 + (ps + r) * HD;
             const bool ok = ps + r < c1 && ps + r != pos;
             const int64_t off = ok ? roff + pc * 8 : 0;
             cp_async16z(dk + r * R + pc * 16, kslot + off, ok);
