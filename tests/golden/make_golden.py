@@ -5,6 +5,7 @@ built oracle/_ref (``make -C oracle``):
 
     python tests/golden/make_golden.py               # everything
     python tests/golden/make_golden.py --batch-only  # the per-sequence batch goldens only
+    python tests/golden/make_golden.py --kv8-only    # the eight-KV-head Llama only
 
 1. Seeded random-init HF models (transformers, no network) wrapped with the reference's own
    wrappers (examples/models/hub_models.py: load_smollm2_model :366, load_gpt2_model :47) and
@@ -67,10 +68,13 @@ def p(a):
 # Tiny model shapes (head_dim 64 keeps the reference on its FLASH_ATTN_EXT path,
 # executor.cpp:2305-2308).
 LLAMA = dict(L=2, d=256, hq=4, hkv=2, hd=64, ffn=512, V=512)
+# eight KV heads, so tensor parallelism over 2, 4 and 8 ranks each keeps whole heads
+LLAMA_KV8 = dict(L=2, d=512, hq=8, hkv=8, hd=64, ffn=1024, V=512)
 GPT2 = dict(L=2, d=256, nh=4, ffn=1024, V=500, npos=512)
 
 
-def compile_llama(out: Path, quant: str, theta: float, seed: int):
+def compile_llama(out: Path, quant: str, theta: float, seed: int, shape: dict = LLAMA,
+                  name: str = "tiny_llama"):
     sys.path.insert(0, str(REF / "python"))
     sys.path.insert(0, str(REF))
     import torch
@@ -81,7 +85,7 @@ def compile_llama(out: Path, quant: str, theta: float, seed: int):
     from examples.models import hub_models
 
     torch.manual_seed(seed)
-    c = LLAMA
+    c = shape
     cfg = LlamaConfig(hidden_size=c["d"], num_hidden_layers=c["L"], num_attention_heads=c["hq"],
                       num_key_value_heads=c["hkv"], head_dim=c["hd"], intermediate_size=c["ffn"],
                       vocab_size=c["V"], rms_norm_eps=1e-5, rope_theta=theta,
@@ -91,7 +95,7 @@ def compile_llama(out: Path, quant: str, theta: float, seed: int):
                            return_value=model):
         m, dummy, _ = hub_models.load_smollm2_model(seq_len=8)
     dim_s = torch.export.Dim("s", min=1, max=2048)
-    ggmlc.compile(m, dummy, output=str(out), dynamic_shapes=({1: dim_s},), model_name="tiny_llama",
+    ggmlc.compile(m, dummy, output=str(out), dynamic_shapes=({1: dim_s},), model_name=name,
                   quantize=quant, tasks=["text-generation"])
 
 
@@ -274,6 +278,16 @@ def main_batch():
         print(fname, "batch tokens", gold["tokens"][:, :6].tolist())
 
 
+def main_kv8():
+    """Only the eight-KV-head Llama fixture (tensor parallelism over up to 8 ranks)."""
+    L = ref_lib()
+    f = HERE / "tiny_llama_kv8_q4_0.gguf"
+    compile_llama(f, "q4_0", 500000.0, 3, LLAMA_KV8, "tiny_llama_kv8")
+    gold = model_golden(L, f, LLAMA_KV8["V"], prompt_len=37, n_decode=12, seed=13)
+    np.savez_compressed(HERE / "tiny_llama_kv8_q4_0.npz", **gold)
+    print(f.name, f.stat().st_size, "tokens", gold["greedy_tokens"][:8])
+
+
 def main():
     L = ref_lib()
     np.savez_compressed(HERE / "ops_golden.npz", **op_golden(L))
@@ -294,4 +308,10 @@ def main():
 if __name__ == "__main__":
     if int(np.__version__.split(".")[0]) < 2:
         sys.exit(f"NumPy {np.__version__}: the committed goldens follow NumPy 2 scalar promotion")
-    main_batch() if "--batch-only" in sys.argv else main()
+    if "--batch-only" in sys.argv:
+        main_batch()
+    elif "--kv8-only" in sys.argv:
+        main_kv8()
+    else:
+        main()
+        main_kv8()

@@ -87,7 +87,7 @@ def test_flash_attn_bit_exact(g):
     assert np.array_equal(y, g["fa_y"])
 
 
-@pytest.mark.parametrize("fixture", FIXTURES)
+@pytest.mark.parametrize("fixture", FIXTURES + ["tiny_llama_kv8_q4_0"])
 def test_model_forward_bit_exact(fixture):
     gold = np.load(GOLDEN / f"{fixture}.npz")
     M = O.ModelOracle(GOLDEN / f"{fixture}.gguf")
@@ -96,7 +96,7 @@ def test_model_forward_bit_exact(fixture):
     assert np.array_equal(y, gold["full_logits"])
 
 
-@pytest.mark.parametrize("fixture", FIXTURES)
+@pytest.mark.parametrize("fixture", FIXTURES + ["tiny_llama_kv8_q4_0"])
 def test_model_kv_decode_bit_exact(fixture):
     gold = np.load(GOLDEN / f"{fixture}.npz")
     M = O.ModelOracle(GOLDEN / f"{fixture}.gguf")

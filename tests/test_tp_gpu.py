@@ -87,11 +87,16 @@ def argmax_agrees(out, ref, rel_gap=0.01):
 
 
 def _run_two(fixture, env=None):
+    return _run(fixture, 2, env)
+
+
+def _run(fixture, world, env=None):
     import multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     idq, outq = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, 2, fixture, idq, outq, env)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, world, fixture, idq, outq, env))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = {}
@@ -104,7 +109,7 @@ def _run_two(fixture, env=None):
             p.join(timeout=30)
             if p.is_alive():
                 p.kill()
-    for rank in (0, 1):
+    for rank in range(world):
         assert res[rank][4] is None, f"rank {rank}: {res[rank][4]}"
     return res
 
@@ -120,6 +125,27 @@ def test_two_way_tensor_parallel_matches_reference(fixture):
     assert argmax_agrees(full, gold["full_logits"])
     kv_pre = gold["kv_prefill_logits"].reshape(pre.shape)
     assert cos(pre, kv_pre) >= COS_MIN
+    for i, ref in enumerate(gold["decode_logits"]):
+        assert cos(dec[i], ref) >= COS_MIN, f"decode step {i}"
+    assert argmax_agrees(dec, np.stack(gold["decode_logits"]))
+
+
+@pytest.mark.parametrize("world", [4, 8])
+def test_four_and_eight_way_tensor_parallel_match_reference(world):
+    """The eight-KV-head fixture (whole heads on every rank) at 4 and 8 ranks against the
+    reference's golden logits, every rank holding the same complete outputs."""
+    if _gpus() < world:
+        pytest.skip(f"needs {world} CUDA devices")
+    fixture = "tiny_llama_kv8_q4_0"
+    res = _run(fixture, world)
+    gold = np.load(GOLDEN / f"{fixture}.npz")
+    _, full, pre, dec, _ = res[0]
+    for r in range(1, world):
+        for k in (1, 2, 3):
+            assert np.array_equal(res[0][k], res[r][k]), f"rank {r}"
+    assert cos(full, gold["full_logits"]) >= COS_MIN
+    assert argmax_agrees(full, gold["full_logits"])
+    assert cos(pre, gold["kv_prefill_logits"].reshape(pre.shape)) >= COS_MIN
     for i, ref in enumerate(gold["decode_logits"]):
         assert cos(dec[i], ref) >= COS_MIN, f"decode step {i}"
     assert argmax_agrees(dec, np.stack(gold["decode_logits"]))

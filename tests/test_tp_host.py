@@ -104,14 +104,17 @@ def _rank_main(rank, world, port, fixture, q):
         q.put((rank, 0, 0, 0, repr(e)))
 
 
-@pytest.mark.parametrize("fixture", ["tiny_llama_q8_0", "tiny_llama_q4_0"])
-def test_tensor_parallel_shards_recombine_over_gloo(fixture):
+@pytest.mark.parametrize("fixture,world", [("tiny_llama_q8_0", 2), ("tiny_llama_q4_0", 2),
+                                           ("tiny_llama_kv8_q4_0", 4), ("tiny_llama_kv8_q4_0", 8)])
+def test_tensor_parallel_shards_recombine_over_gloo(fixture, world):
+    """world ranks (the eight-KV-head fixture keeps whole heads on 4 and 8 ranks)."""
     import multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, fixture, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, fixture, q))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=240) for _ in procs]
@@ -146,6 +149,16 @@ def test_tensor_parallel_plan_shapes_and_partition():
     assert plans[0]["partial"] == plans[1]["partial"] and len(plans[0]["partial"]) == 4
     with pytest.raises(RuntimeError, match="do not divide"):
         R.tensor_parallel_plan(g, 0, 3)
+    with pytest.raises(RuntimeError, match="do not divide"):
+        R.tensor_parallel_plan(g, 0, 4)  # two KV heads over four ranks
+    # eight KV heads: 8 ranks each take one q head and one KV head; the FFN splits 8 ways
+    g8 = R.ModelLoader.load_from_file(str(GOLDEN / "tiny_llama_kv8_q4_0.gguf"))
+    p8 = [R.tensor_parallel_plan(g8, r, 8) for r in range(8)]
+    assert all(p["n_attention"] == 2 and p["n_mlp"] == 2 for p in p8)
+    for name, sl in p8[0]["slices"].items():
+        if "rows" in sl:  # the ranks' row ranges tile the rows
+            rows = sorted(r for p in p8 for r in p["slices"][name]["rows"])
+            assert all(a[1] == b[0] for a, b in zip(rows, rows[1:]))
     # GPT-2: attention sharded (QKV bias sliced with its rows), the bias-GELU MLP replicated
     gp = R.tensor_parallel_plan(R.ModelLoader.load_from_file(str(GOLDEN / "tiny_gpt2_q8_0.gguf")),
                                 1, 2)
