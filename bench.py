@@ -574,6 +574,7 @@ def run_cb(g, gguf, local: int, steps: int = 256, buckets=(1, 2, 4, 8, 16)) -> d
                               max_new_tokens=steps, temperature=0.0)
         t_admit = t_dec = 0.0
         n_dec_tokens = 0
+        peak_pages = peak_bytes = 0  # paged KV in use, read between steps (host-side counters)
         while sched.has_work():
             admitting = sched.pending_count() > 0
             t0 = time.perf_counter()
@@ -584,11 +585,17 @@ def run_cb(g, gguf, local: int, steps: int = 256, buckets=(1, 2, 4, 8, 16)) -> d
             else:
                 t_dec += dt
                 n_dec_tokens += len(res.new_tokens)
+            peak_pages = max(peak_pages, ex.kv_pool_pages - ex.kv_free_pages)
+            peak_bytes = max(peak_bytes, ex.get_paged_active_vram_bytes())
         total = B * steps
         out[f"B{B}"] = {"decode_tokens_per_s": round(n_dec_tokens / t_dec, 1) if t_dec else None,
                         "tokens_per_s": round(total / (t_admit + t_dec), 1),
                         "prompt_tokens": int(lens.sum()), "admit_s": round(t_admit, 3),
-                        "decode_s": round(t_dec, 3)}
+                        "decode_s": round(t_dec, 3),
+                        "kv_pages": {"pool": int(ex.kv_pool_pages),
+                                     "tokens_per_page": int(ex.tokens_per_page),
+                                     "peak_in_use": int(peak_pages),
+                                     "peak_mapped_gb": round(peak_bytes / 1e9, 3)}}
         del sched
     out["prefix_cache"] = run_prefix(ex)
     return out
