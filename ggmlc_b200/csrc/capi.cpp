@@ -474,6 +474,14 @@ int64_t gb_weight_row_bytes(int type, int64_t K) {
     }
     return gb::qrow_bytes(type, K);
 }
+int64_t gb_kv_row_offset(const int32_t* pages, int page_shift, int64_t H, int64_t ctx, int64_t h,
+                         int64_t t, int64_t hd) {
+    if (page_shift < 0 || page_shift > 16 || H < 0 || ctx < 0 || h < 0 || t < 0 || hd < 0) {
+        g_err = "gb_kv_row_offset: negative argument or page_shift outside 0..16";
+        return -1;
+    }
+    return gb::kv_row_off(pages, page_shift, H, ctx, h, t, hd);
+}
 int gb_repack_blocks(const void* gguf, int type, int64_t N, int64_t K, void* wq, void* stream) {
     return guard([&] {
         gb::launch_repack_blocks((const uint8_t*)gguf, type, N, K, wq, (cudaStream_t)stream);

@@ -256,6 +256,13 @@ int gb_scheduler_request_tokens(gb_scheduler* s, uint64_t request_id, int which,
 
 /* Bytes of one weight row in the split-row layout (Q8_0 = 8, Q4_0 = 2). */
 int64_t gb_weight_row_bytes(int type, int64_t K);
+/* Element offset of K (or V) row (h, t), head_dim hd, of one sequence in a layer's f16 cache,
+ * as every attention kernel addresses it: the contiguous window [H][ctx][hd] when pages is NULL;
+ * else the layer's page pool [page][H][1 << page_shift][hd] with `pages` the sequence's page
+ * list (pages[i] holds positions [i << page_shift, (i + 1) << page_shift)).  Host arithmetic
+ * only; -1 for negative arguments or a shift outside 0..16. */
+int64_t gb_kv_row_offset(const int32_t* pages, int page_shift, int64_t H, int64_t ctx, int64_t h,
+                         int64_t t, int64_t hd);
 /* GGUF block rows (34-byte Q8_0 / 18-byte Q4_0 blocks) -> wq (split-row layout, padding
  * zeroed).  gguf is device memory.  Replaces the weight upload of ggml_backend_tensor_set
  * (executor.cpp:414-429). */

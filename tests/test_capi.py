@@ -103,3 +103,36 @@ def test_rope_table_fill_matches_oracle():
     y = O.rope_neox(x, np.arange(n_pos, dtype=np.int32), nd, np.float32(10000.0))
     assert np.array_equal(tab[:, :, 0], y[:, 0, : nd // 2])
     assert np.array_equal(tab[:, :, 1], y[:, 0, nd // 2:])
+
+
+def test_kv_row_offsets_tile_contiguous_and_paged_caches():
+    """gb_kv_row_offset, the addressing of every attention kernel: contiguous rows at
+    (h * ctx + t) * hd; paged rows inside the listed pages only, every (h, t) of a sequence at
+    its own offset, and two sequences with disjoint page lists never on the same row."""
+    from ggmlc_b200 import _runtime
+
+    lib = _runtime.lib()
+    P, I, I64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_int64
+    lib.gb_kv_row_offset.argtypes = [P, I, I64, I64, I64, I64, I64]
+    lib.gb_kv_row_offset.restype = I64
+    H, hd, ctx = 3, 8, 40
+    for h, t in [(0, 0), (2, 39), (1, 17)]:
+        assert lib.gb_kv_row_offset(None, 0, H, ctx, h, t, hd) == (h * ctx + t) * hd
+    assert lib.gb_kv_row_offset(None, 17, H, ctx, 0, 0, hd) == -1
+    rng = np.random.default_rng(4)
+    shift = 2  # pages of 4 positions
+    T = 1 << shift
+    pool = rng.permutation(np.arange(1, 21)).astype(np.int32)  # 20 pages, scattered order
+    seqs = [pool[:10].copy(), pool[10:].copy()]  # 10 pages = 40 positions each
+    seen = {}
+    for s, pages in enumerate(seqs):
+        for h in range(H):
+            for t in range(len(pages) * T):
+                off = lib.gb_kv_row_offset(pages.ctypes.data, shift, H, ctx, h, t, hd)
+                page = off // (H * T * hd)
+                assert page == pages[t >> shift]  # inside the page the list names
+                assert off % hd == 0
+                assert off == ((int(pages[t >> shift]) * H + h) * T + (t & (T - 1))) * hd
+                assert off not in seen, (s, h, t, seen.get(off))
+                seen[off] = (s, h, t)
+    assert len(seen) == 2 * H * 10 * T
