@@ -204,12 +204,15 @@ int gb_radix_insert_prefix(gb_radix* r, const int32_t* tokens, int64_t n, int64_
 int64_t gb_radix_evict_lru(gb_radix* r);
 
 /* ---- ContinuousBatchScheduler (batch_scheduler.h:35-77; python_bindings.cpp:261-295) --------
- * Iteration-level continuous batching over the paged KV cache: add_request queues a prompt;
- * each step either admits every pending request that finds a free slot (prefill into it, first
- * token; batch_scheduler.cpp:136-277) or decodes one token for every active sequence at its own
- * position.  Greedy when temperature <= 0.  Prefix caching (on by default): the KV rows of the
- * longest cached run of whole prompt pages are copied into the slot and only the rest of the
- * prompt is prefilled (batch_scheduler.cpp:149-164, :225-238). */
+ * Iteration-level continuous batching over the paged KV cache: add_request queues a prompt
+ * (refused if prompt + max_new_tokens exceed max_ctx or the pool's pages); each step either
+ * admits, in order, every pending request that finds a free slot and whose pages fit the pool
+ * next to what the running sequences may still claim (prefill into it, first token;
+ * batch_scheduler.cpp:136-277), or decodes one token for every active sequence at its own
+ * position.  Greedy when temperature <= 0.  Prefix caching (on by default): the pages of the
+ * longest cached run of whole prompt pages are mapped into the slot's page table (shared, not
+ * copied) and only the rest of the prompt is prefilled (batch_scheduler.cpp:149-164,
+ * :225-238); least-recently-used cached pages are evicted when admission needs their room. */
 typedef struct gb_scheduler gb_scheduler;
 typedef struct gb_request_info {
     uint64_t request_id;
