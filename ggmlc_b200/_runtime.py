@@ -641,8 +641,10 @@ class ContinuousBatchScheduler:
 
     Same interface as the reference scheduler (python_bindings.cpp:278-294).  Each step admits
     every pending request that finds a free slot (prefill in it) or decodes one token of every
-    active sequence, each at its own position.  Prefix caching (on by default) reuses the KV rows
-    of whole cached prompt pages (executor.tokens_per_page tokens each) and prefills the rest.
+    active sequence, each at its own position.  Prefix caching (on by default) maps the pages of
+    whole cached prompt pages (executor.tokens_per_page tokens each) into the new sequence's page
+    table, shared rather than copied, and prefills the rest.  A request waits while the KV pool
+    lacks the pages it may claim (prompt + max_new_tokens).
     """
 
     def __init__(self, executor: ModelExecutor, max_batch_size: int = 8, eos_token_id: int = 0):
