@@ -22,13 +22,16 @@ def _tensor_sig(spec: dict, tid: int) -> tuple:
     return t["type"], json.dumps(t["ne"]), t["storage"], t["role"]
 
 
-def _synth(tmp_path, quant: str, theta: float):
+def _synth(tmp_path, quant: str, theta: float, kv8: bool = False):
     from ggmlc_b200 import synth
 
-    shape = synth.LlamaShape(2, 256, 4, 2, 64, 512, 512, theta)
+    if kv8:  # the eight-KV-head fixture (tests/golden/make_golden.py LLAMA_KV8)
+        shape = synth.LlamaShape(2, 512, 8, 8, 64, 1024, 512, theta)
+    else:
+        shape = synth.LlamaShape(2, 256, 4, 2, 64, 512, 512, theta)
     path = tmp_path / f"tiny_{quant}.gguf"
     synth.synth_llama(path, shape, synth.Q8_0 if quant == "q8_0" else synth.Q4_0,
-                      name="tiny_llama")
+                      name="tiny_llama_kv8" if kv8 else "tiny_llama")
     return path
 
 
@@ -41,11 +44,15 @@ def _synth_gpt2(tmp_path):
     return path
 
 
-@pytest.mark.parametrize("quant,theta", [("q8_0", 10000.0), ("q4_0", 500000.0), ("gpt2", None)])
+@pytest.mark.parametrize("quant,theta", [("q8_0", 10000.0), ("q4_0", 500000.0), ("gpt2", None),
+                                         ("kv8", 500000.0)])
 def test_synthesized_graph_matches_reference_compiled(tmp_path, quant, theta):
     if quant == "gpt2":
         path = _synth_gpt2(tmp_path)
         ref_path = GOLDEN / "tiny_gpt2_q8_0.gguf"
+    elif quant == "kv8":
+        path = _synth(tmp_path, "q4_0", theta, kv8=True)
+        ref_path = GOLDEN / "tiny_llama_kv8_q4_0.gguf"
     else:
         path = _synth(tmp_path, quant, theta)
         ref_path = GOLDEN / f"tiny_llama_{quant}.gguf"
